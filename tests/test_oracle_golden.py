@@ -1,0 +1,223 @@
+"""Pin the oracle (C restatement of the reference's CPU groupby) to the reference's
+own golden vectors (tests/golden/reference_vectors.json, each case cites its test).
+CPU only."""
+import json
+import math
+import struct
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+import oracle
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+sys.path.insert(0, str(GOLDEN))
+import make_golden  # noqa: E402
+
+CASES = json.loads((GOLDEN / "reference_vectors.json").read_text())["cases"]
+
+
+def dec(x):
+    if x is None:
+        return None
+    if isinstance(x, (int, float)):
+        return float(x)
+    return float(x) if x in ("nan", "inf", "-inf") else float.fromhex(x)
+
+
+def bits(x: float) -> int:
+    return struct.unpack("<Q", struct.pack("<d", x))[0]
+
+
+def same(a, b, tol=0.0, rel=False):
+    a, b = float(a), float(b)
+    if math.isnan(b):
+        return math.isnan(a)
+    if tol == 0.0:
+        return bits(a) == bits(b)
+    err = abs(a - b)
+    return err <= tol * (abs(b) if rel else 1.0)
+
+
+def ids(kind):
+    return [c for c in CASES if c["kind"] == kind]
+
+
+@pytest.mark.parametrize("case", ids("exact_sum") + ids("exact_sum_tol"), ids=lambda c: c["cite"])
+def test_exact_sum(case):
+    _, vals = make_golden.case_inputs(case)
+    got = oracle.exact_sum(np.array(vals))
+    assert same(got, dec(case["expect"]), case.get("tol", 0.0)), (got, case["expect"])
+
+
+@pytest.mark.parametrize("case", ids("scatter_phi"), ids=lambda c: c["cite"])
+def test_scatter_phi(case):
+    keys, vals = make_golden.case_inputs(case)
+    refs = None if "refs" not in case else np.array([dec(r) for r in case["refs"]])
+    got = oracle.scatter_phi(case["phi"], keys, vals, refs, case["n_groups"])
+    for g, e in zip(got, case["expect"]):
+        assert same(g, dec(e)), (list(got), case["expect"])
+
+
+@pytest.mark.parametrize("case", ids("scatter_multi_phi"), ids=lambda c: c["cite"])
+def test_scatter_multi_phi(case):
+    keys, vals = make_golden.case_inputs(case)
+    got = oracle.scatter_multi_phi(case["phis"], keys, vals, None, case["n_groups"])
+    for out, exp in zip(got, case["expect"]):
+        assert all(same(g, dec(e)) for g, e in zip(out, exp)), (got, case["expect"])
+
+
+@pytest.mark.parametrize("case", ids("scatter_phi_masked"), ids=lambda c: c["cite"])
+def test_scatter_phi_masked(case):
+    keys, vals = make_golden.case_inputs(case)
+    mask = np.array([int(w) for w in case["mask"]], dtype=np.uint64)
+    got = oracle.scatter_phi_masked(case["phi"], keys, vals, None, mask, case["n_groups"])
+    for g, e in zip(got, case["expect"]):
+        assert same(g, dec(e)), (list(got), case["expect"])
+
+
+@pytest.mark.parametrize("case", ids("extremum"), ids=lambda c: c["cite"])
+def test_extremum(case):
+    keys, vals = make_golden.case_inputs(case)
+    mn = oracle.scatter_extremum(False, keys, vals, case["n_groups"])
+    mx = oracle.scatter_extremum(True, keys, vals, case["n_groups"])
+    assert all(same(a, dec(b)) for a, b in zip(mn, case["expect_min"]))
+    assert all(same(a, dec(b)) for a, b in zip(mx, case["expect_max"]))
+
+
+def test_unsupported_phi_errors():
+    (case,) = ids("unsupported_phi")
+    with pytest.raises(oracle.OracleError):
+        oracle.scatter_phi(case["phi"], [0], [1.0], None, 1)
+
+
+def _derived_check(mom, exp, tol, rel):
+    d = oracle.derived(mom)
+    table = {"count": mom["counts"], "sum": mom["sums"], "min": mom["mins"], "max": mom["maxs"],
+             "mean": d["mean"], "var_pop": d["var_pop"], "var_samp": d["var_samp"]}
+    for field, want in exp.items():
+        for g, w in enumerate(want):
+            if w is None:
+                continue
+            assert same(table[field][g], dec(w), tol, rel), (field, g, table[field][g], w)
+
+
+@pytest.mark.parametrize("case", ids("moments_grouped"), ids=lambda c: c["cite"])
+def test_moments_grouped(case):
+    keys, vals = make_golden.case_inputs(case)
+    mom = oracle.moments_grouped(vals, keys, case["n_groups"])
+    _derived_check(mom, case["expect"], case.get("tol", 0.0), case.get("rel", False))
+
+
+def test_mean_grouped():
+    (case,) = ids("mean_grouped")
+    keys, vals = make_golden.case_inputs(case)
+    mom = oracle.moments_grouped(vals, keys, case["n_groups"])
+    means = oracle.derived(mom)["mean"]
+    assert np.allclose(means, case["expect"], atol=case["tol"], rtol=0)
+
+
+def test_grouped_higher_moments():
+    (case,) = ids("moments_grouped_m34")
+    keys, vals = make_golden.case_inputs(case)
+    mom = oracle.moments_grouped(vals, keys, case["n_groups"])
+    n, m2, m3, m4 = mom["counts"][0], mom["m2s"][0], mom["m3s"][0], mom["m4s"][0]
+    var = m2 / n
+    g1 = (m3 / n) / (var * math.sqrt(var))           # MomentStats::skewness(bias=true), descriptive.rs:135-148
+    raw = (m4 / n) / (var * var)                     # MomentStats::kurtosis(excess, bias=true), :157-175
+    assert abs(g1 - case["expect_g0"]["skew_biased"]) < case["tol"]
+    assert abs((raw - 3.0) - case["expect_g0"]["kurt_excess_biased"]) < case["tol"]
+
+
+# ---- oracle self-consistency --------------------------------------------------------
+
+def test_mt_matches_single_thread_bit_for_bit():
+    rng = np.random.default_rng(7)
+    n, G = 200_003, 37
+    keys = rng.integers(0, G, n).astype(np.int32)
+    vals = rng.standard_normal(n) * 10.0 ** rng.integers(-30, 30, n)
+    vals[rng.random(n) < 0.01] = np.nan
+    vals[rng.random(n) < 0.002] = np.inf
+    vals[rng.random(n) < 0.002] = -np.inf
+    vals[:50] = 0.0
+    vals[50:100] = -0.0
+    a = oracle.moments_grouped(vals, keys, G, m34=False)
+    for t in (1, 3, 8):
+        b = oracle.moments_grouped_mt(vals, keys, G, threads=t)
+        for f in ("counts", "sums", "mins", "maxs", "m2s"):
+            assert np.array_equal(a[f].view(np.uint64), b[f].view(np.uint64)), (t, f)
+
+
+def test_i64_factorised_path_matches_dense_path():
+    rng = np.random.default_rng(11)
+    n, G = 50_000, 101
+    ids_ = rng.integers(0, G, n)
+    salt = rng.integers(-2**62, 2**62, G)
+    keys64 = salt[ids_]
+    vals = rng.standard_normal(n)
+    vals[rng.random(n) < 0.02] = np.nan
+    r = oracle.groupby_i64(keys64, vals)
+    order = np.argsort(salt)  # dense id of each sorted key
+    d = oracle.moments_grouped(vals, ids_.astype(np.int32), G, m34=False)
+    assert np.array_equal(r["keys"], salt[order])
+    for f in ("counts", "sums", "mins", "maxs", "m2s"):
+        assert np.array_equal(r[f].view(np.uint64), d[f][order].view(np.uint64)), f
+
+
+def test_masked_moments_equal_moments_of_filtered_rows():
+    rng = np.random.default_rng(3)
+    n, G = 10_000, 13
+    keys = rng.integers(0, G, n).astype(np.int32)
+    vals = rng.standard_normal(n)
+    mask = oracle.filter_mask("gt", 0.0, rng.standard_normal(n))
+    sel = np.array([(int(mask[i // 64]) >> (i % 64)) & 1 for i in range(n)], dtype=bool)
+    a = oracle.moments_grouped_masked(vals, keys, mask, G)
+    b = oracle.moments_grouped(vals[sel], keys[sel], G, m34=False)
+    c = oracle.moments_grouped_mt(vals, keys, G, threads=4, mask=mask)
+    for f in ("counts", "sums", "mins", "maxs", "m2s"):
+        assert np.array_equal(a[f].view(np.uint64), b[f].view(np.uint64)), f
+        assert np.array_equal(a[f].view(np.uint64), c[f].view(np.uint64)), f
+
+
+def test_kulisch_matches_fsum_on_random_data():
+    rng = np.random.default_rng(5)
+    for _ in range(20):
+        n = int(rng.integers(1, 5000))
+        x = rng.standard_normal(n) * 10.0 ** rng.integers(-300, 300, n)
+        assert bits(oracle.exact_sum(x)) == bits(math.fsum(x.tolist()) + 0.0)
+
+
+def test_out_of_range_key_is_an_error():
+    with pytest.raises(IndexError):
+        oracle.moments_grouped([1.0, 2.0], [0, 5], 2)
+    with pytest.raises(IndexError):
+        oracle.moments_grouped([1.0, 2.0], [0, -1], 2)
+
+
+def test_filter_mask_layout_and_map2():
+    a = np.array([1.0, -1.0, np.nan, 0.0, 2.0] + [1.0] * 70)
+    m = oracle.filter_mask("gt", 0.0, a)
+    assert m.size == 2
+    assert int(m[0]) & 0b11111 == 0b10001  # NaN fails a > 0
+    assert int(m[1]) >> 11 == 0  # trailing bits of the last word stay 0
+    b = np.array([2.0] * a.size)
+    c = np.array([0.5] * a.size)
+    ab = oracle.map2("a * b", a, b)
+    v = oracle.map2("a + b", ab, c)
+    assert v[0] == 2.5 and v[1] == -1.5
+
+
+def test_generator_streams():
+    # SplitMix64::new(seed).next_u64() sequence (rng.rs:73-83) == counter form
+    seed = 0x1234
+    state = seed
+    seq = []
+    for _ in range(5):
+        state = (state + 0x9E3779B97F4A7C15) & oracle.M64
+        seq.append(oracle.mix64_int(state))
+    assert list(map(int, oracle.splitmix_stream(seed, 0, 5))) == seq
+    assert [int(oracle.lib().orc_splitmix_at(seed, i)) for i in range(5)] == seq
+    k = oracle.gen_keys_uniform(1000, 256, 0)
+    assert k.min() >= 0 and k.max() < 256

@@ -1,0 +1,239 @@
+"""B200 (sm_100a) groupby-aggregate path of the WinRapids/Tambear dataframe engine.
+
+Two layers:
+
+* ``Context`` -- thin wrapper over the C ABI (include/tambear_gb.h) working on
+  device tensors (torch is used only for device memory and streams);
+* the reference's operator API, same names and meaning:
+  ``DescriptiveEngine.moments_grouped`` -> ``GroupedMomentStats`` / ``MomentStats``
+  (crates/tambear/src/descriptive.rs:67-435).
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from dataclasses import dataclass
+
+import numpy as np
+
+from ._lib import (MOMENT_FIELDS, InvalidArgument, KeyOutOfRange, Moments, TambearGbError, error_for, lib)
+
+__all__ = [
+    "Context", "DescriptiveEngine", "GroupedMomentStats", "MomentStats", "TambearGbError", "KeyOutOfRange",
+    "InvalidArgument", "MOMENT_FIELDS",
+]
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _ptr(t) -> int | None:
+    return None if t is None else int(t.data_ptr())
+
+
+def _stream_handle(stream) -> int | None:
+    if stream is None:
+        torch = _torch()
+        return int(torch.cuda.current_stream().cuda_stream)
+    return int(getattr(stream, "cuda_stream", stream))
+
+
+class Context:
+    """One tbgb_ctx on one CUDA device."""
+
+    def __init__(self, device: int = 0):
+        self._L = lib()
+        h = C.c_void_p()
+        st = self._L.tbgb_create(int(device), C.byref(h))
+        if st != 0:
+            raise error_for(st, f"tbgb_create(device={device}) failed (an sm_100 device is required)")
+        self._h = h
+        self.device = int(device)
+
+    def close(self):
+        if getattr(self, "_h", None):
+            self._L.tbgb_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def name(self) -> str:
+        return self._L.tbgb_device_name(self._h).decode()
+
+    @property
+    def launches(self) -> int:
+        return int(self._L.tbgb_launch_count(self._h))
+
+    def _check(self, st: int):
+        if st != 0:
+            raise error_for(st, self._L.tbgb_last_error(self._h).decode())
+
+    def workspace_bytes(self, n: int, n_groups: int) -> int:
+        return int(self._L.tbgb_workspace_bytes(self._h, int(n), int(n_groups)))
+
+    # -- groupby ------------------------------------------------------------------
+    @staticmethod
+    def moments_struct(out: dict) -> Moments:
+        m = Moments()
+        for f in MOMENT_FIELDS:
+            t = out.get(f)
+            setattr(m, f, _ptr(t))
+        return m
+
+    def alloc_moments(self, n_groups: int, fields=MOMENT_FIELDS) -> dict:
+        torch = _torch()
+        return {f: torch.empty(n_groups, dtype=torch.float64, device=f"cuda:{self.device}") for f in fields}
+
+    def groupby_dense(self, keys, vals, n_groups: int, mask=None, out: dict | None = None, stream=None,
+                      sync: bool = True) -> dict:
+        """Grouped count/sum/min/max/mean/m2/var of device tensors keys (int32) and vals (f64)."""
+        n = int(vals.numel())
+        if int(keys.numel()) != n:
+            raise InvalidArgument(7, "keys and values must have same length")
+        if out is None:
+            out = self.alloc_moments(n_groups)
+        m = self.moments_struct(out)
+        self._check(self._L.tbgb_groupby_dense(self._h, _ptr(keys), _ptr(vals), _ptr(mask), n, int(n_groups),
+                                               C.byref(m), _stream_handle(stream)))
+        if sync:
+            self.sync(stream)
+        return out
+
+    def sync(self, stream=None):
+        self._check(self._L.tbgb_sync(self._h, _stream_handle(stream)))
+
+    def state_bytes(self, n_groups: int) -> int:
+        return int(self._L.tbgb_state_bytes(int(n_groups)))
+
+    def groupby_dense_state(self, keys, vals, n_groups: int, row_offset: int = 0, mask=None, state=None,
+                            stream=None):
+        torch = _torch()
+        n = int(vals.numel())
+        if state is None:
+            state = torch.empty(self.state_bytes(n_groups) // 8, dtype=torch.float64,
+                                device=f"cuda:{self.device}")
+        self._check(self._L.tbgb_groupby_dense_state(self._h, _ptr(keys), _ptr(vals), _ptr(mask), n,
+                                                     int(n_groups), int(row_offset), _ptr(state),
+                                                     _stream_handle(stream)))
+        return state
+
+    def merge_states(self, states, n_states: int, n_groups: int, out: dict | None = None, stream=None) -> dict:
+        if out is None:
+            out = self.alloc_moments(n_groups)
+        m = self.moments_struct(out)
+        self._check(self._L.tbgb_merge_states(self._h, _ptr(states), int(n_states), int(n_groups), C.byref(m),
+                                              _stream_handle(stream)))
+        return out
+
+    # -- kernel timing --------------------------------------------------------------
+    def profile(self, enable: bool = True):
+        self._check(self._L.tbgb_profile_enable(self._h, 1 if enable else 0))
+
+    def kernel_time_ms(self) -> tuple[float, int]:
+        ms, cnt = C.c_double(), C.c_int64()
+        self._check(self._L.tbgb_kernel_time_ms(self._h, C.byref(ms), C.byref(cnt)))
+        return float(ms.value), int(cnt.value)
+
+    # -- synthetic inputs -------------------------------------------------------------
+    def gen_keys_uniform(self, keys, n_groups: int, seed: int, first_row: int = 0, stream=None):
+        self._check(self._L.tbgb_gen_keys_uniform(self._h, _ptr(keys), int(keys.numel()), int(n_groups),
+                                                  int(seed) & (2**64 - 1), int(first_row), _stream_handle(stream)))
+
+    def gen_values_uniform(self, vals, lo: float, hi: float, seed: int, first_row: int = 0, stream=None):
+        self._check(self._L.tbgb_gen_values_uniform(self._h, _ptr(vals), int(vals.numel()), float(lo), float(hi),
+                                                    int(seed) & (2**64 - 1), int(first_row),
+                                                    _stream_handle(stream)))
+
+    def gen_values_normal(self, vals, mu: float, sigma: float, seed: int, first_row: int = 0, stream=None):
+        self._check(self._L.tbgb_gen_values_normal(self._h, _ptr(vals), int(vals.numel()), float(mu),
+                                                   float(sigma), int(seed) & (2**64 - 1), int(first_row),
+                                                   _stream_handle(stream)))
+
+    def gen_inject_nonfinite(self, vals, nan_frac: float, inf_frac: float, seed: int, first_row: int = 0,
+                             stream=None):
+        self._check(self._L.tbgb_gen_inject_nonfinite(self._h, _ptr(vals), int(vals.numel()), float(nan_frac),
+                                                      float(inf_frac), int(seed) & (2**64 - 1), int(first_row),
+                                                      _stream_handle(stream)))
+
+
+# ---------------------------------------------------------------------------------
+# The reference's operator API (descriptive.rs)
+# ---------------------------------------------------------------------------------
+
+@dataclass
+class MomentStats:
+    """Per-group sufficient statistics (descriptive.rs:67-87); m3/m4 are not computed here."""
+
+    count: float
+    sum: float
+    min: float
+    max: float
+    m2: float
+
+    def n(self) -> int:
+        return int(self.count)
+
+    def mean(self) -> float:
+        return math.nan if self.count == 0.0 else self.sum / self.count
+
+    def variance(self, ddof: int) -> float:
+        denom = self.count - float(ddof)
+        return math.nan if denom <= 0.0 else self.m2 / denom
+
+    def std(self, ddof: int) -> float:
+        return math.sqrt(self.variance(ddof)) if not math.isnan(self.variance(ddof)) else math.nan
+
+    def range(self) -> float:
+        return math.nan if self.count == 0.0 else self.max - self.min
+
+
+@dataclass
+class GroupedMomentStats:
+    """Parallel per-group arrays (descriptive.rs:295-330)."""
+
+    n_groups: int
+    counts: np.ndarray
+    sums: np.ndarray
+    mins: np.ndarray
+    maxs: np.ndarray
+    m2s: np.ndarray
+
+    def group(self, g: int) -> MomentStats:
+        return MomentStats(float(self.counts[g]), float(self.sums[g]), float(self.mins[g]), float(self.maxs[g]),
+                           float(self.m2s[g]))
+
+    def means(self) -> np.ndarray:
+        with np.errstate(invalid="ignore", divide="ignore"):
+            return np.where(self.counts > 0, self.sums / np.where(self.counts > 0, self.counts, 1), np.nan)
+
+
+class DescriptiveEngine:
+    """Grouped descriptive statistics on the B200 path (DescriptiveEngine, descriptive.rs:352-470)."""
+
+    def __init__(self, device: int = 0):
+        self.ctx = Context(device)
+
+    def moments_grouped(self, values, keys, n_groups: int) -> GroupedMomentStats:
+        torch = _torch()
+        values = np.ascontiguousarray(values, dtype=np.float64)
+        keys = np.ascontiguousarray(keys, dtype=np.int32)
+        if values.shape != keys.shape:
+            raise InvalidArgument(7, "values and keys must have same length")
+        dev = f"cuda:{self.ctx.device}"
+        dv = torch.from_numpy(values).to(dev)
+        dk = torch.from_numpy(keys).to(dev)
+        out = self.ctx.groupby_dense(dk, dv, n_groups, out=self.ctx.alloc_moments(
+            n_groups, ("count", "sum", "min", "max", "m2")))
+        h = {k: v.cpu().numpy() for k, v in out.items()}
+        return GroupedMomentStats(n_groups, h["count"], h["sum"], h["min"], h["max"], h["m2"])
+
+    def mean_grouped(self, values, keys, n_groups: int) -> np.ndarray:
+        return self.moments_grouped(values, keys, n_groups).means()

@@ -1,0 +1,105 @@
+"""ctypes binding of include/tambear_gb.h (libtambear_gb.so, built in-tree for sm_100a).
+
+There is no fallback: if the library is missing or no sm_100 device is present,
+every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from pathlib import Path
+
+LIB_PATH = Path(__file__).resolve().parent / "libtambear_gb.so"
+
+STATUS_NAMES = {
+    0: "OK",
+    1: "Backend",
+    2: "Compile",
+    3: "Alloc",
+    4: "Transfer",
+    5: "Dispatch",
+    6: "EntryNotFound",
+    7: "InvalidArgument",
+    8: "KeyOutOfRange",
+    9: "TableFull",
+    10: "Timeout",
+}
+
+
+class TambearGbError(RuntimeError):
+    """A non-OK tbgb_status; `.status` is the numeric code, `.kind` its name."""
+
+    def __init__(self, status: int, message: str):
+        self.status = status
+        self.kind = STATUS_NAMES.get(status, f"status{status}")
+        super().__init__(f"{self.kind}: {message}")
+
+
+class KeyOutOfRange(TambearGbError):
+    pass
+
+
+class InvalidArgument(TambearGbError):
+    pass
+
+
+def error_for(status: int, message: str) -> TambearGbError:
+    if status == 8:
+        return KeyOutOfRange(status, message)
+    if status == 7:
+        return InvalidArgument(status, message)
+    return TambearGbError(status, message)
+
+
+class Moments(C.Structure):
+    _fields_ = [(name, C.c_void_p) for name in
+                ("count", "sum", "min", "max", "mean", "m2", "var_pop", "var_samp")]
+
+
+MOMENT_FIELDS = tuple(f for f, _ in Moments._fields_)
+
+_lib = None
+
+
+def lib() -> C.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `python winrapids_b200/build.py`")
+    L = C.CDLL(str(LIB_PATH))
+    vp, i32, i64, u64, f64, sz = C.c_void_p, C.c_int32, C.c_int64, C.c_uint64, C.c_double, C.c_size_t
+    st = C.c_int
+    sig = {
+        "tbgb_create": (st, [C.c_int, C.POINTER(vp)]),
+        "tbgb_destroy": (None, [vp]),
+        "tbgb_last_error": (C.c_char_p, [vp]),
+        "tbgb_device_name": (C.c_char_p, [vp]),
+        "tbgb_groupby_dense": (st, [vp, vp, vp, vp, i64, i32, C.POINTER(Moments), vp]),
+        "tbgb_sync": (st, [vp, vp]),
+        "tbgb_state_bytes": (sz, [i32]),
+        "tbgb_groupby_dense_state": (st, [vp, vp, vp, vp, i64, i32, i64, vp, vp]),
+        "tbgb_merge_states": (st, [vp, vp, i32, i32, C.POINTER(Moments), vp]),
+        "tbgb_workspace_bytes": (sz, [vp, i64, i32]),
+        "tbgb_launch_count": (u64, [vp]),
+        "tbgb_profile_enable": (st, [vp, C.c_int]),
+        "tbgb_kernel_time_ms": (st, [vp, C.POINTER(f64), C.POINTER(i64)]),
+        "tbgb_gen_keys_uniform": (st, [vp, vp, i64, i32, u64, i64, vp]),
+        "tbgb_gen_values_uniform": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
+        "tbgb_gen_values_normal": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
+        "tbgb_gen_inject_nonfinite": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
+    }
+    for name, (res, args) in sig.items():
+        fn = getattr(L, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = L
+    return L
+
+
+# Every symbol include/tambear_gb.h declares (checked by the CPU test suite).
+HEADER_SYMBOLS = (
+    "tbgb_create", "tbgb_destroy", "tbgb_last_error", "tbgb_device_name", "tbgb_groupby_dense", "tbgb_sync",
+    "tbgb_state_bytes", "tbgb_groupby_dense_state", "tbgb_merge_states", "tbgb_workspace_bytes",
+    "tbgb_launch_count", "tbgb_profile_enable", "tbgb_kernel_time_ms", "tbgb_gen_keys_uniform", "tbgb_gen_values_uniform", "tbgb_gen_values_normal",
+    "tbgb_gen_inject_nonfinite",
+)

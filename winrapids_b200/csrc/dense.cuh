@@ -1,0 +1,48 @@
+// dense.cuh -- constants and host launchers of the dense-key groupby kernels.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "tambear_gb.h"
+
+namespace tbgb {
+
+constexpr int kDenseThreads = 512;  // threads per CTA (16 warps)
+constexpr int kDenseTile = 2048;    // rows per staged tile
+constexpr int kDenseStages = 4;     // depth of the TMA ring
+constexpr int kDenseMaxGroups = 1024;
+constexpr int kDenseColBudget = 12288;  // C * n_groups doubles of column buffer (96 KiB)
+
+// Mergeable per-group state, stored as structure-of-arrays with ST_COUNT rows.
+//   nn       non-NaN rows          nf       finite rows
+//   K        shift of this state   sumoff   sum(v - K) over finite rows
+//   meanoff  mean(v) - K           m2       sum((v - mean)^2) over finite rows
+//   min/max  over non-NaN rows     zfirst   (first zero row << 1 | sign), bits of a u64
+enum { ST_NN = 0, ST_NF, ST_K, ST_SUMOFF, ST_MEANOFF, ST_M2, ST_MIN, ST_MAX, ST_ZFIRST, ST_COUNT };
+
+struct DenseLaunch {
+  int grid;       // CTAs
+  int C;          // column capacity
+  int opg;        // owners per group
+  int slots;      // n_groups * opg
+  int maxslots;   // owner slots per thread (1 or 2)
+  size_t smem;    // dynamic shared memory bytes
+  size_t part_doubles;  // ST_COUNT * grid * slots
+};
+
+DenseLaunch dense_plan(int n_groups, int num_sms);
+size_t dense_smem_bytes(int G, int C);
+
+// Enqueue the dense moments pipeline.  `part` holds part_doubles, `zfirst` G u64,
+// `err` one u32.  Writes either final outputs (`out`) or, when `state_out` is not
+// NULL, the merged state table of this call (ST_COUNT * G doubles).
+cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, const double* vals, const uint64_t* mask,
+                                 long long n, long long row_offset, int G, double* part, unsigned long long* zfirst,
+                                 uint32_t* err, const tbgb_moments* out, double* state_out, cudaStream_t stream,
+                                 uint64_t* launches, cudaEvent_t ev_start = nullptr, cudaEvent_t ev_stop = nullptr);
+
+cudaError_t merge_states_launch(const double* states, int n_states, int G, const tbgb_moments* out,
+                                cudaStream_t stream, uint64_t* launches);
+
+}  // namespace tbgb
