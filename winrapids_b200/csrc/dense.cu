@@ -4,19 +4,24 @@
 // with the NaN mask of nan_mask_count (:591-603) and the extrema of
 // scatter_extremum / extremum_grouped_nan_safe (compute_engine.rs:304-322,
 // descriptive.rs:606-620).  One pass over the data instead of the reference's two:
-// per (CTA, group owner) the kernel keeps the non-NaN count, finite count, shift
-// K, S1 = sum(v-K), S2 = sum((v-K)^2), min and max; partial states are merged with
-// Chan's formula (descriptive.rs:216-253, intermediates.rs:352-377) in a fixed
-// order, so results do not depend on which CTA finishes first.
+// per (CTA, group) the kernel keeps the finite count, a shift K, S1 = sum(v-K),
+// S2 = sum((v-K)^2), min and max, plus +-inf counts; the partial states are merged
+// with Chan's formula (descriptive.rs:216-253, intermediates.rs:352-377) in a fixed
+// order, so the merge itself does not depend on which CTA finishes first.
 //
-// Data path per CTA (one persistent 512-thread CTA per SM):
-//   * TMA bulk copies (cp.async.bulk, mbarrier completion, no multicast) stage
-//     2048-row tiles of keys, values and mask words into a 4-deep shared ring;
-//   * every thread ranks its 4 rows inside their groups with a shared-memory u32
-//     atomic and stores the value into column `rank` of a [C][n_groups] buffer;
-//   * owner threads (n_groups * opg of them) sweep their group's column and update
-//     register accumulators; rows ranked >= C go through further rounds of the
-//     same buffer, so heavy key skew stays correct (only slower).
+// One persistent 512-thread CTA per SM, warp-specialised:
+//   * TMA bulk copies (cp.async.bulk + mbarrier, no multicast) stream 2048-row
+//     tiles of keys / values / mask words into a 4-deep shared-memory ring;
+//   * warps 0-7 ("scatter") rank each finite row inside its group with a shared
+//     u32 atomic and store the value into column `rank` of a [C][n_groups]
+//     buffer (two buffers, alternating per tile); +-inf rows and the rare rows
+//     ranked >= C go to a small per-CTA spill state in global memory;
+//   * warps 8-15 ("owners") sweep the other buffer's columns concurrently and keep
+//     each group's accumulators in registers (branch-free: the columns hold finite
+//     values only; two independent accumulator chains per group).
+//   Hand-offs use mbarriers (tile full / column full / column empty) and named
+//   barriers inside each warp group, so the two roles overlap instead of meeting
+//   at CTA-wide barriers.
 #include <cstdint>
 
 #include "common.cuh"
@@ -24,40 +29,71 @@
 
 namespace tbgb {
 
-constexpr int DT = kDenseThreads;
-constexpr int TILE = kDenseTile;
+constexpr int NT = kDenseThreads;   // 512
+constexpr int NSC = 256;            // scatter threads (warps 0-7)
+constexpr int NOW = 256;            // owner threads (warps 8-15)
+constexpr int TILE = kDenseTile;    // rows per staged tile
 constexpr int STAGES = kDenseStages;
-constexpr int RPT = TILE / DT;  // rows per thread per tile
-static_assert(RPT == 4, "thread -> row mapping assumes 4 rows per thread");
+constexpr int RPS = TILE / NSC;     // rows per scatter thread per tile (8)
+constexpr int CHUNK = 2 * NSC;      // rows covered by one vector access of all scatter threads
+static_assert(RPS == 8, "scatter mapping assumes 8 rows per thread");
 
 constexpr uint32_t KEY_BYTES = TILE * 4;
 constexpr uint32_t VAL_BYTES = TILE * 8;
 constexpr uint32_t MASK_BYTES = TILE / 8;
 constexpr uint32_t STAGE_BYTES = KEY_BYTES + VAL_BYTES + MASK_BYTES;
 static_assert(STAGE_BYTES % 16 == 0, "bulk copy sizes must be 16-byte multiples");
-constexpr uint32_t NO_RANK = 0xFFFFFFFFu;
 
-struct OwnerAcc {
-  unsigned long long nn;  // non-NaN rows
-  unsigned long long nf;  // finite rows
-  double K, s1, s2, mn, mx;
-  bool kset;
-  __device__ __forceinline__ void init() {
-    nn = 0; nf = 0; K = 0.0; s1 = 0.0; s2 = 0.0; mn = pos_inf(); mx = neg_inf(); kset = false;
-  }
-  __device__ __forceinline__ void add(double v) {
-    nn += 1;
-    if (is_finite(v)) {
-      if (!kset) { K = v; kset = true; }
-      const double d = v - K;
-      s1 += d;
-      s2 = fma(d, d, s2);
-      nf += 1;
+constexpr int BAR_SCATTER = 1;  // named barrier of the scatter warps
+constexpr int BAR_OWNER = 2;    // named barrier of the owner warps
+constexpr unsigned long long K_UNSET = 0x7FF8000000000001ull;  // NaN payload no finite value has
+
+// spill state, per CTA, SoA over groups (u64 words)
+enum { SP_N = 0, SP_NINFP, SP_NINFN, SP_K, SP_S1, SP_S2, SP_MN, SP_MX, SP_COUNT };
+
+__device__ __forceinline__ unsigned long long f2o(double v) {
+  const unsigned long long b = static_cast<unsigned long long>(__double_as_longlong(v));
+  return (b >> 63) ? ~b : (b | 0x8000000000000000ull);
+}
+__device__ __forceinline__ double o2f(unsigned long long o) {
+  const unsigned long long b = (o >> 63) ? (o & 0x7FFFFFFFFFFFFFFFull) : ~o;
+  return __longlong_as_double(static_cast<long long>(b));
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+// Barrier among `n` threads that also ORs a predicate across them.
+__device__ __forceinline__ bool bar_red_or(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.or.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"(static_cast<uint32_t>(pred)), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// Bounded wait that also gives up when the other warp group raised `abort`.
+__device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 255u) == 0) {
+      if (*abort) return false;
+      if (globaltimer_ns() - t0 > 2000000000ull) {
+        atomicOr(err, KERR_TIMEOUT);
+        return false;
+      }
     }
-    mn = fmin(mn, v);
-    mx = fmax(mx, v);
   }
-};
+}
 
 struct DenseArgs {
   const int32_t* keys;
@@ -66,253 +102,301 @@ struct DenseArgs {
   long long n;
   long long row_offset;  // global index of row 0 (zero-tie ordering across shards)
   int G, C, opg, slots;
-  double* part;                // [ST_COUNT][gridDim.x * slots]
+  double* part;                // owner partials [ST_COUNT][gridDim.x * slots]
+  unsigned long long* spill;   // [gridDim.x][SP_COUNT][G]
   unsigned long long* zfirst;  // [G], preset to ~0
   uint32_t* err;
 };
 
 size_t dense_smem_bytes(int G, int C) {
   const size_t gp = (static_cast<size_t>(G) + 3) & ~size_t(3);
-  return static_cast<size_t>(STAGES) * STAGE_BYTES + static_cast<size_t>(C) * G * 8 + 2 * gp * 4 + STAGES * 8;
+  return static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * static_cast<size_t>(C) * G * 8 + 2 * gp * 4 +
+         (STAGES + 4) * 8 + 16;
 }
 
 DenseLaunch dense_plan(int G, int num_sms) {
   DenseLaunch L{};
   L.grid = num_sms;
-  int C = kDenseColBudget / G;
+  int C = (kDenseColBudget / 2) / G;
   if (C > TILE) C = TILE;
   if (C < 1) C = 1;
   L.C = C;
-  L.opg = G >= DT ? 1 : DT / G;
+  L.opg = G >= NOW ? 1 : NOW / G;
   L.slots = G * L.opg;
-  L.maxslots = (L.slots + DT - 1) / DT;
+  const int ms = (L.slots + NOW - 1) / NOW;
+  L.maxslots = ms <= 1 ? 1 : (ms <= 2 ? 2 : 4);
   L.smem = dense_smem_bytes(G, C);
   L.part_doubles = static_cast<size_t>(ST_COUNT) * L.grid * L.slots;
+  L.spill_words = static_cast<size_t>(SP_COUNT) * L.grid * G;
   return L;
 }
 
-template <int MAXSLOTS>
-__device__ __forceinline__ void owner_sweep(const DenseArgs& a, const double* col, const uint32_t* cnt, int round,
-                                            OwnerAcc (&acc)[MAXSLOTS], const int (&og)[MAXSLOTS],
-                                            const int (&osub)[MAXSLOTS]) {
-#pragma unroll
-  for (int q = 0; q < MAXSLOTS; ++q) {
-    const int g = og[q];
-    if (g < 0) continue;
-    int c = static_cast<int>(cnt[g]) - round * a.C;
-    c = c < 0 ? 0 : (c > a.C ? a.C : c);
-    const double* cg = col + g;
-    int e = osub[q];
-    // two independent loads in flight per iteration
-    for (; e + a.opg < c; e += 2 * a.opg) {
-      const double x0 = cg[static_cast<size_t>(e) * a.G];
-      const double x1 = cg[static_cast<size_t>(e + a.opg) * a.G];
-      acc[q].add(x0);
-      acc[q].add(x1);
-    }
-    if (e < c) acc[q].add(cg[static_cast<size_t>(e) * a.G]);
-  }
+// Rare path: a finite row that found its column full.
+__device__ __noinline__ void spill_add(unsigned long long* sp, int G, int g, double v) {
+  const unsigned long long vb = static_cast<unsigned long long>(__double_as_longlong(v));
+  const unsigned long long kb = atomicCAS(sp + SP_K * G + g, K_UNSET, vb);
+  const double K = kb == K_UNSET ? v : __longlong_as_double(static_cast<long long>(kb));
+  const double d = v - K;
+  atomicAdd(reinterpret_cast<double*>(sp + SP_S1 * G + g), d);
+  atomicAdd(reinterpret_cast<double*>(sp + SP_S2 * G + g), d * d);
+  atomicAdd(sp + SP_N * G + g, 1ull);
+  atomicMin(sp + SP_MN * G + g, f2o(v));
+  atomicMax(sp + SP_MX * G + g, f2o(v));
 }
 
+struct OwnerAcc {
+  double K, s1a, s1b, s2a, s2b, mn, mx;
+  unsigned long long nf;
+  bool kset;
+  __device__ __forceinline__ void init() {
+    K = 0.0; s1a = s1b = s2a = s2b = 0.0; mn = pos_inf(); mx = neg_inf(); nf = 0; kset = false;
+  }
+  // Sweep entries sub, sub+opg, ... < c of one group's column (finite values only).
+  __device__ __forceinline__ void sweep(const double* cg, int c, int sub, int opg, int G) {
+    if (c <= sub) return;
+    if (!kset) { K = cg[static_cast<size_t>(sub) * G]; kset = true; }
+    int e = sub;
+    for (; e + opg < c; e += 2 * opg) {
+      const double x0 = cg[static_cast<size_t>(e) * G];
+      const double x1 = cg[static_cast<size_t>(e + opg) * G];
+      const double d0 = x0 - K, d1 = x1 - K;
+      s1a += d0;
+      s1b += d1;
+      s2a = fma(d0, d0, s2a);
+      s2b = fma(d1, d1, s2b);
+      mn = fmin(mn, fmin(x0, x1));
+      mx = fmax(mx, fmax(x0, x1));
+    }
+    if (e < c) {
+      const double x0 = cg[static_cast<size_t>(e) * G];
+      const double d0 = x0 - K;
+      s1a += d0;
+      s2a = fma(d0, d0, s2a);
+      mn = fmin(mn, x0);
+      mx = fmax(mx, x0);
+    }
+    nf += static_cast<unsigned long long>((c - sub + opg - 1) / opg);
+  }
+};
+
 template <int MAXSLOTS, bool MASKED, bool TMA>
-__global__ void __launch_bounds__(DT, 1) dense_moments_kernel(DenseArgs a) {
+__global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int tid = threadIdx.x;
-  const int G = a.G;
+  const int G = a.G, C = a.C;
   const int gp = (G + 3) & ~3;
-  double* col = reinterpret_cast<double*>(smem + STAGES * STAGE_BYTES);
-  uint32_t* cnt = reinterpret_cast<uint32_t*>(col + static_cast<size_t>(a.C) * G);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(cnt + 2 * gp);
+  double* col0 = reinterpret_cast<double*>(smem + STAGES * STAGE_BYTES);
+  double* col1 = col0 + static_cast<size_t>(C) * G;
+  uint32_t* cnt0 = reinterpret_cast<uint32_t*>(col1 + static_cast<size_t>(C) * G);
+  uint32_t* cnt1 = cnt0 + gp;
+  uint64_t* full = reinterpret_cast<uint64_t*>(cnt1 + gp);  // [STAGES]
+  uint64_t* colfull = full + STAGES;                          // [2]
+  uint64_t* colempty = colfull + 2;                           // [2]
+  volatile int* abort = reinterpret_cast<volatile int*>(colempty + 2);
 
   const long long ntiles = a.n / TILE;
   const int P = gridDim.x, b = blockIdx.x;
   const long long t_begin = ntiles * b / P, t_end = ntiles * (b + 1) / P;
   const long long mytiles = t_end - t_begin;
   const bool has_tail = (b == P - 1) && (a.n % TILE) != 0;
+  const long long nbatch = mytiles + (has_tail ? 1 : 0);
+  unsigned long long* sp = a.spill + static_cast<size_t>(b) * SP_COUNT * G;
 
-  OwnerAcc acc[MAXSLOTS];
-  int og[MAXSLOTS], osub[MAXSLOTS];
-#pragma unroll
-  for (int q = 0; q < MAXSLOTS; ++q) {
-    acc[q].init();
-    const int o = tid + q * DT;
-    if (o < a.slots) { osub[q] = o / G; og[q] = o - osub[q] * G; }
-    else { og[q] = -1; osub[q] = 0; }
+  for (int i = tid; i < 2 * gp; i += NT) cnt0[i] = 0;
+  for (int g = tid; g < G; g += NT) {
+    sp[SP_N * G + g] = 0;
+    sp[SP_NINFP * G + g] = 0;
+    sp[SP_NINFN * G + g] = 0;
+    sp[SP_K * G + g] = K_UNSET;
+    sp[SP_S1 * G + g] = 0;
+    sp[SP_S2 * G + g] = 0;
+    sp[SP_MN * G + g] = ~0ull;
+    sp[SP_MX * G + g] = 0;
   }
-  for (int i = tid; i < 2 * gp; i += DT) cnt[i] = 0;
+  if (tid == 0) {
+    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
+    for (int s = 0; s < 2; ++s) { mbar_init(&colfull[s], 1); mbar_init(&colempty[s], 1); }
+    *abort = 0;
+    mbar_fence_init();
+  }
+  __syncthreads();
 
   const uint32_t tx_bytes = KEY_BYTES + VAL_BYTES + (MASKED ? MASK_BYTES : 0);
   auto issue = [&](int s, long long tile) {
     unsigned char* st = smem + static_cast<size_t>(s) * STAGE_BYTES;
-    mbar_arrive_expect_tx(&bars[s], tx_bytes);
-    bulk_g2s(st, a.keys + tile * TILE, KEY_BYTES, &bars[s]);
-    bulk_g2s(st + KEY_BYTES, a.vals + tile * TILE, VAL_BYTES, &bars[s]);
-    if (MASKED) bulk_g2s(st + KEY_BYTES + VAL_BYTES, a.mask + tile * (TILE / 64), MASK_BYTES, &bars[s]);
+    mbar_arrive_expect_tx(&full[s], tx_bytes);
+    bulk_g2s(st, a.keys + tile * TILE, KEY_BYTES, &full[s]);
+    bulk_g2s(st + KEY_BYTES, a.vals + tile * TILE, VAL_BYTES, &full[s]);
+    if (MASKED) bulk_g2s(st + KEY_BYTES + VAL_BYTES, a.mask + tile * (TILE / 64), MASK_BYTES, &full[s]);
   };
-  if (TMA && tid == 0) {
-    for (int s = 0; s < STAGES; ++s) mbar_init(&bars[s], 1);
-    mbar_fence_init();
-  }
-  __syncthreads();
-  if (TMA && tid == 0) {
-    for (int s = 0; s < STAGES && s < mytiles; ++s) issue(s, t_begin + s);
-  }
 
-  int cb = 0;
-  bool failed = false;
-  long long li_fail = 0;
-  // One tile: rank rows into the column buffer (round 0), barrier, owner sweep,
-  // overflow rounds; ends with a barrier after which col/cnt[cb] may be reused.
-  auto run_tile = [&](const int (&k)[RPT], const double (&v)[RPT], uint32_t mbits, long long row0, bool ok_in,
-                      int stage_to_refill, long long refill_tile) -> bool {
-    uint32_t* cur = cnt + cb * gp;
-    uint32_t* nxt = cnt + (cb ^ 1) * gp;
-    uint32_t rank[RPT];
-    bool pend = false;
+  if (tid < NSC) {
+    // ------------------------------------------------------------ scatter warps
+    const int t = tid;
+    long long issued = 0;
+    if (TMA && t == 0) {
+      for (int s = 0; s < STAGES && s < mytiles; ++s) issue(s, t_begin + s);
+      issued = mytiles < STAGES ? mytiles : STAGES;
+    }
+    long long k_fail = -1;
+    for (long long k = 0; k < nbatch; ++k) {
+      const int bs = static_cast<int>(k & 1);
+      double* col = bs ? col1 : col0;
+      uint32_t* cnt = bs ? cnt1 : cnt0;
+      bool ok = true;
+      if (k >= 2) ok = wait_or_abort(&colempty[bs], static_cast<uint32_t>(((k >> 1) - 1) & 1), a.err, abort);
+      const bool tail = k >= mytiles;
+      const long long row0 = tail ? ntiles * TILE : (t_begin + k) * TILE;
+      int kk[RPS];
+      double vv[RPS];
+      uint32_t mb = 0;
+      const int s = static_cast<int>(k % STAGES);
+      if (TMA && !tail) {
+        ok = ok && wait_or_abort(&full[s], static_cast<uint32_t>((k / STAGES) & 1), a.err, abort);
+        const unsigned char* st = smem + static_cast<size_t>(s) * STAGE_BYTES;
 #pragma unroll
-    for (int j = 0; j < RPT; ++j) {
-      rank[j] = NO_RANK;
-      const int g = k[j];
-      const double x = v[j];
-      bool ok = ok_in && ((mbits >> j) & 1u) && !is_nan(x);
-      if (ok && static_cast<unsigned>(g) >= static_cast<unsigned>(G)) {
-        atomicOr(a.err, KERR_KEY_RANGE);
-        ok = false;
+        for (int c = 0; c < RPS / 2; ++c) {
+          const int2 kp = reinterpret_cast<const int2*>(st)[c * NSC + t];
+          const double2 vp = reinterpret_cast<const double2*>(st + KEY_BYTES)[c * NSC + t];
+          kk[2 * c] = kp.x; kk[2 * c + 1] = kp.y;
+          vv[2 * c] = vp.x; vv[2 * c + 1] = vp.y;
+          if (MASKED) {
+            const int r = c * CHUNK + 2 * t;
+            const uint64_t w = reinterpret_cast<const uint64_t*>(st + KEY_BYTES + VAL_BYTES)[r >> 6];
+            mb |= static_cast<uint32_t>((w >> (r & 63)) & 3ull) << (2 * c);
+          } else {
+            mb |= 3u << (2 * c);
+          }
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < RPS / 2; ++c) {
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            const long long r = row0 + c * CHUNK + 2 * t + j;
+            if (r < a.n) {
+              kk[2 * c + j] = a.keys[r];
+              vv[2 * c + j] = a.vals[r];
+              const bool m = MASKED ? ((a.mask[r >> 6] >> (r & 63)) & 1ull) != 0 : true;
+              mb |= (m ? 1u : 0u) << (2 * c + j);
+            } else {
+              kk[2 * c + j] = 0;
+              vv[2 * c + j] = 0.0;
+            }
+          }
+        }
       }
       if (ok) {
-        if (x == 0.0) atomicMin(&a.zfirst[g], zero_code(a.row_offset + row0 + j, x));
-        const uint32_t r = atomicAdd(&cur[g], 1u);
-        rank[j] = r;
-        if (r < static_cast<uint32_t>(a.C)) col[static_cast<size_t>(r) * G + g] = x;
-        else pend = true;
-      }
-    }
-    // barrier A: tile consumed from the stage; columns and counts complete
-    if (__syncthreads_or(!ok_in)) return false;
-    if (TMA && tid == 0 && stage_to_refill >= 0) {
-      fence_proxy_async_smem();
-      issue(stage_to_refill, refill_tile);
-    }
-    for (int i = tid; i < G; i += DT) nxt[i] = 0;
-    owner_sweep<MAXSLOTS>(a, col, cur, 0, acc, og, osub);
-    int round = 0;
-    // barrier B (and overflow rounds while any group exceeded C rows)
-    while (__syncthreads_or(pend)) {
-      ++round;
-      const uint32_t lo = static_cast<uint32_t>(round) * a.C, hi = lo + a.C;
-      pend = false;
 #pragma unroll
-      for (int j = 0; j < RPT; ++j) {
-        if (rank[j] == NO_RANK || rank[j] < lo) continue;
-        if (rank[j] < hi) col[static_cast<size_t>(rank[j] - lo) * G + k[j]] = v[j];
-        else pend = true;
+        for (int i = 0; i < RPS; ++i) {
+          const int g = kk[i];
+          const double x = vv[i];
+          bool valid = ((mb >> i) & 1u) && !is_nan(x);
+          if (valid && static_cast<unsigned>(g) >= static_cast<unsigned>(G)) {
+            atomicOr(a.err, KERR_KEY_RANGE);
+            valid = false;
+          }
+          if (!valid) continue;
+          if (x == 0.0) {
+            const long long r = row0 + (i >> 1) * CHUNK + 2 * t + (i & 1);
+            atomicMin(&a.zfirst[g], zero_code(a.row_offset + r, x));
+          }
+          if (!is_finite(x)) {
+            atomicAdd(sp + (x > 0 ? SP_NINFP : SP_NINFN) * G + g, 1ull);
+            continue;
+          }
+          const uint32_t rk = atomicAdd(&cnt[g], 1u);
+          if (rk < static_cast<uint32_t>(C)) col[static_cast<size_t>(rk) * G + g] = x;
+          else spill_add(sp, G, g, x);
+        }
       }
-      __syncthreads();
-      owner_sweep<MAXSLOTS>(a, col, cur, round, acc, og, osub);
-    }
-    cb ^= 1;
-    return true;
-  };
-
-  for (long long li = 0; li < mytiles && !failed; ++li) {
-    const long long tile = t_begin + li;
-    const long long row0 = tile * TILE + tid * RPT;
-    int k[RPT];
-    double v[RPT];
-    uint32_t mbits = 0xFu;
-    bool ok = true;
-    int refill = -1;
-    if (TMA) {
-      const int s = static_cast<int>(li % STAGES);
-      const uint32_t par = static_cast<uint32_t>((li / STAGES) & 1);
-      ok = mbar_wait_bounded(&bars[s], par, a.err);
-      const unsigned char* st = smem + static_cast<size_t>(s) * STAGE_BYTES;
-      const int4 kk = reinterpret_cast<const int4*>(st)[tid];
-      const double2 v0 = reinterpret_cast<const double2*>(st + KEY_BYTES)[2 * tid];
-      const double2 v1 = reinterpret_cast<const double2*>(st + KEY_BYTES)[2 * tid + 1];
-      k[0] = kk.x; k[1] = kk.y; k[2] = kk.z; k[3] = kk.w;
-      v[0] = v0.x; v[1] = v0.y; v[2] = v1.x; v[3] = v1.y;
-      if (MASKED) {
-        const uint64_t w = reinterpret_cast<const uint64_t*>(st + KEY_BYTES + VAL_BYTES)[(tid * RPT) >> 6];
-        mbits = static_cast<uint32_t>(w >> ((tid * RPT) & 63)) & 0xFu;
+      // all scatter threads are done with stage s and with column buffer bs
+      const bool fail = bar_red_or(BAR_SCATTER, NSC, !ok || *abort);
+      if (t == 0) {
+        if (fail) *abort = 1;
+        if (TMA && !fail && !tail && k + STAGES < mytiles) {
+          fence_proxy_async_smem();
+          issue(s, t_begin + k + STAGES);
+          ++issued;
+        }
+        mbar_arrive(&colfull[bs]);
       }
-      if (li + STAGES < mytiles) refill = s;
-    } else {
-#pragma unroll
-      for (int j = 0; j < RPT; ++j) { k[j] = a.keys[row0 + j]; v[j] = a.vals[row0 + j]; }
-      if (MASKED) {
-        const uint64_t w = a.mask[row0 >> 6];
-        mbits = static_cast<uint32_t>(w >> (row0 & 63)) & 0xFu;
+      if (fail) {
+        k_fail = k;
+        break;
       }
     }
-    if (!run_tile(k, v, mbits, tile * TILE + tid * RPT, ok, refill, tile + STAGES)) {
-      failed = true;
-      li_fail = li;
-    }
-  }
-
-  if (failed) {
-    // A staged copy did not complete in time: wait (bounded) for the copies this
-    // CTA may still have in flight, then leave; the host reports TBGB_ERR_TIMEOUT.
-    if (TMA && tid == 0) {
-      // tiles li_fail .. li_fail+STAGES-1 were issued and not consumed
-      for (long long t = li_fail; t < li_fail + STAGES && t < mytiles; ++t) {
-        const int s = static_cast<int>(t % STAGES);
-        const uint32_t par = static_cast<uint32_t>((t / STAGES) & 1);
+    if (TMA && t == 0 && k_fail >= 0) {
+      // leave no bulk copy in flight into this CTA's shared memory (bounded waits)
+      for (long long j = k_fail; j < issued; ++j) {
         const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&bars[s], par)) {
+        while (!mbar_try_wait(&full[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1))) {
           if (globaltimer_ns() - t0 > 500000000ull) break;
         }
       }
     }
-    __syncthreads();
-    return;
-  }
-
-  if (has_tail) {
-    const long long tail0 = ntiles * TILE;
-    const long long row0 = tail0 + tid * RPT;
-    int k[RPT];
-    double v[RPT];
-    uint32_t mbits = 0;
+  } else {
+    // ------------------------------------------------------------ owner warps
+    const int o = tid - NSC;
+    OwnerAcc acc[MAXSLOTS];
+    int og[MAXSLOTS], osub[MAXSLOTS];
 #pragma unroll
-    for (int j = 0; j < RPT; ++j) {
-      const long long r = row0 + j;
-      if (r < a.n) {
-        k[j] = a.keys[r];
-        v[j] = a.vals[r];
-        const bool m = MASKED ? ((a.mask[r >> 6] >> (r & 63)) & 1ull) != 0 : true;
-        mbits |= (m ? 1u : 0u) << j;
-      } else {
-        k[j] = 0;
-        v[j] = 0.0;
+    for (int q = 0; q < MAXSLOTS; ++q) {
+      acc[q].init();
+      const int slot = o + q * NOW;
+      if (slot < a.slots) { osub[q] = slot / G; og[q] = slot - osub[q] * G; }
+      else { og[q] = -1; osub[q] = 0; }
+    }
+    for (long long k = 0; k < nbatch; ++k) {
+      const int bs = static_cast<int>(k & 1);
+      const double* col = bs ? col1 : col0;
+      uint32_t* cnt = bs ? cnt1 : cnt0;
+      const bool ok = wait_or_abort(&colfull[bs], static_cast<uint32_t>((k >> 1) & 1), a.err, abort);
+      int c[MAXSLOTS];
+#pragma unroll
+      for (int q = 0; q < MAXSLOTS; ++q) {
+        const int g = og[q] < 0 ? 0 : og[q];
+        const int v = static_cast<int>(cnt[g]);
+        c[q] = v < C ? v : C;
       }
-    }
-    run_tile(k, v, mbits, row0, true, -1, 0);
-  }
-
-  // partial states of this CTA's owners
-  const long long stride = static_cast<long long>(P) * a.slots;
+      // every owner has read its counts (and agrees on failure)
+      if (bar_red_or(BAR_OWNER, NOW, !ok || *abort)) {
+        if (!ok) *abort = 1;
+        break;
+      }
 #pragma unroll
-  for (int q = 0; q < MAXSLOTS; ++q) {
-    if (og[q] < 0) continue;
-    const long long idx = static_cast<long long>(b) * a.slots + (tid + q * DT);
-    const OwnerAcc& A = acc[q];
-    double meanoff = 0.0, m2 = 0.0;
-    if (A.nf > 0) {
-      const double nf = static_cast<double>(A.nf);
-      meanoff = A.s1 / nf;
-      m2 = fmax(A.s2 - A.s1 * meanoff, 0.0);
+      for (int q = 0; q < MAXSLOTS; ++q)
+        if (og[q] >= 0 && osub[q] == 0) cnt[og[q]] = 0;
+#pragma unroll
+      for (int q = 0; q < MAXSLOTS; ++q)
+        if (og[q] >= 0) acc[q].sweep(col + og[q], c[q], osub[q], a.opg, G);
+      named_bar_sync(BAR_OWNER, NOW);  // column buffer bs fully read, counts reset
+      if (o == 0) mbar_arrive(&colempty[bs]);
     }
-    a.part[ST_NN * stride + idx] = static_cast<double>(A.nn);
-    a.part[ST_NF * stride + idx] = static_cast<double>(A.nf);
-    a.part[ST_K * stride + idx] = A.K;
-    a.part[ST_SUMOFF * stride + idx] = A.s1;
-    a.part[ST_MEANOFF * stride + idx] = meanoff;
-    a.part[ST_M2 * stride + idx] = m2;
-    a.part[ST_MIN * stride + idx] = A.mn;
-    a.part[ST_MAX * stride + idx] = A.mx;
+    // partial states of this CTA's owners
+    const long long stride = static_cast<long long>(P) * a.slots;
+#pragma unroll
+    for (int q = 0; q < MAXSLOTS; ++q) {
+      if (og[q] < 0) continue;
+      const long long idx = static_cast<long long>(b) * a.slots + (o + q * NOW);
+      const OwnerAcc& A = acc[q];
+      const double s1 = A.s1a + A.s1b, s2 = A.s2a + A.s2b;
+      double meanoff = 0.0, m2 = 0.0;
+      if (A.nf > 0) {
+        meanoff = s1 / static_cast<double>(A.nf);
+        m2 = fmax(s2 - s1 * meanoff, 0.0);
+      }
+      a.part[ST_NN * stride + idx] = static_cast<double>(A.nf);
+      a.part[ST_NF * stride + idx] = static_cast<double>(A.nf);
+      a.part[ST_K * stride + idx] = A.K;
+      a.part[ST_SUMOFF * stride + idx] = s1;
+      a.part[ST_MEANOFF * stride + idx] = meanoff;
+      a.part[ST_M2 * stride + idx] = m2;
+      a.part[ST_MIN * stride + idx] = A.mn;
+      a.part[ST_MAX * stride + idx] = A.mx;
+    }
   }
+  __syncthreads();
 }
 
 // ---------------------------------------------------------------------------
@@ -331,7 +415,7 @@ __device__ __forceinline__ GState gstate_empty() {
   return s;
 }
 
-// A <- A (+) B.  A holds the earlier rows.
+// A <- A (+) B.
 __device__ __forceinline__ void gstate_fold(GState& A, const GState& B) {
   A.nn += B.nn;
   if (B.mn < A.mn) A.mn = B.mn;
@@ -393,6 +477,28 @@ __device__ __forceinline__ void gstate_store(double* st, long long stride, long 
   st[ST_ZFIRST * stride + idx] = __longlong_as_double(static_cast<long long>(s.zf));
 }
 
+// The spill state of one CTA for group g as a mergeable state.
+__device__ __forceinline__ GState spill_state(const unsigned long long* sp, int G, int g) {
+  GState s = gstate_empty();
+  const unsigned long long n = sp[SP_N * G + g];
+  const unsigned long long np = sp[SP_NINFP * G + g], nm = sp[SP_NINFN * G + g];
+  s.nn = static_cast<double>(n + np + nm);
+  if (n > 0) {
+    s.nf = static_cast<double>(n);
+    s.K = __longlong_as_double(static_cast<long long>(sp[SP_K * G + g]));
+    s.sumoff = __longlong_as_double(static_cast<long long>(sp[SP_S1 * G + g]));
+    s.meanoff = s.sumoff / s.nf;
+    s.m2 = fmax(__longlong_as_double(static_cast<long long>(sp[SP_S2 * G + g])) - s.sumoff * s.meanoff, 0.0);
+    s.mn = o2f(sp[SP_MN * G + g]);
+    s.mx = o2f(sp[SP_MX * G + g]);
+  }
+  if (nm > 0) s.mn = neg_inf();
+  if (np > 0) s.mx = pos_inf();
+  if (n == 0 && nm == 0 && np > 0) s.mn = pos_inf();
+  if (n == 0 && np == 0 && nm > 0) s.mx = neg_inf();
+  return s;
+}
+
 // Outputs in the reference's semantics (descriptive.rs:97-114, 416-418).
 __device__ __forceinline__ void gstate_finalize(const GState& A, int g, const tbgb_moments& o) {
   const double nn = A.nn;
@@ -421,33 +527,40 @@ __device__ __forceinline__ void gstate_finalize(const GState& A, int g, const tb
   if (o.var_samp) o.var_samp[g] = nn - 1.0 > 0 ? m2 / (nn - 1.0) : qnan();
 }
 
-// One warp per group: lane l folds partials l, l+32, ... in order, then a fixed
-// shuffle tree folds the lanes (lane order = row order of the partials).
-__global__ void __launch_bounds__(256) dense_fold_kernel(const double* __restrict__ part, long long stride, int P,
-                                                          int G, int opg, const unsigned long long* __restrict__ zfirst,
+// One warp per group: lane l folds partials l, l+32, ... (each CTA contributes
+// opg owner partials and one spill partial), then a fixed shuffle tree folds the
+// lanes.
+__global__ void __launch_bounds__(256) dense_fold_kernel(const double* __restrict__ part,
+                                                          const unsigned long long* __restrict__ spill, int P, int G,
+                                                          int opg, const unsigned long long* __restrict__ zfirst,
                                                           tbgb_moments out, double* state_out) {
   const int lane = threadIdx.x & 31;
   const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (g >= G) return;
   const int slots = G * opg;
-  const int nparts = P * opg;
+  const long long stride = static_cast<long long>(P) * slots;
+  const int per = opg + 1;
+  const int nparts = P * per;
   GState A = gstate_empty();
   for (int i = lane; i < nparts; i += 32) {
-    const int p = i / opg, sub = i - (i / opg) * opg;
-    const long long idx = static_cast<long long>(p) * slots + static_cast<long long>(sub) * G + g;
+    const int p = i / per, j = i - p * per;
     GState B;
-    B.nn = part[ST_NN * stride + idx];
-    B.nf = part[ST_NF * stride + idx];
-    B.K = part[ST_K * stride + idx];
-    B.sumoff = part[ST_SUMOFF * stride + idx];
-    B.meanoff = part[ST_MEANOFF * stride + idx];
-    B.m2 = part[ST_M2 * stride + idx];
-    B.mn = part[ST_MIN * stride + idx];
-    B.mx = part[ST_MAX * stride + idx];
-    B.zf = ~0ull;
+    if (j < opg) {
+      const long long idx = static_cast<long long>(p) * slots + static_cast<long long>(j) * G + g;
+      B.nn = part[ST_NN * stride + idx];
+      B.nf = part[ST_NF * stride + idx];
+      B.K = part[ST_K * stride + idx];
+      B.sumoff = part[ST_SUMOFF * stride + idx];
+      B.meanoff = part[ST_MEANOFF * stride + idx];
+      B.m2 = part[ST_M2 * stride + idx];
+      B.mn = part[ST_MIN * stride + idx];
+      B.mx = part[ST_MAX * stride + idx];
+      B.zf = ~0ull;
+    } else {
+      B = spill_state(spill + static_cast<size_t>(p) * SP_COUNT * G, G, g);
+    }
     gstate_fold(A, B);
   }
-  // lanes hold interleaved partials; fold them in lane order with a fixed tree
   for (int d = 1; d < 32; d <<= 1) {
     const GState B = gstate_shfl_down(A, d);
     if ((lane & (2 * d - 1)) == 0) gstate_fold(A, B);
@@ -481,37 +594,40 @@ static cudaError_t launch_main(const DenseLaunch& L, const DenseArgs& a, cudaStr
   auto kern = dense_moments_kernel<MAXSLOTS, MASKED, TMA>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L.smem));
   if (e != cudaSuccess) return e;
-  kern<<<L.grid, DT, L.smem, stream>>>(a);
+  kern<<<L.grid, NT, L.smem, stream>>>(a);
   return cudaGetLastError();
 }
 
+template <int MAXSLOTS>
+static cudaError_t launch_slots(const DenseLaunch& L, const DenseArgs& a, bool masked, bool aligned,
+                                cudaStream_t stream) {
+  if (masked)
+    return aligned ? launch_main<MAXSLOTS, true, true>(L, a, stream) : launch_main<MAXSLOTS, true, false>(L, a, stream);
+  return aligned ? launch_main<MAXSLOTS, false, true>(L, a, stream) : launch_main<MAXSLOTS, false, false>(L, a, stream);
+}
+
 cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, const double* vals, const uint64_t* mask,
-                                 long long n, long long row_offset, int G, double* part, unsigned long long* zfirst,
-                                 uint32_t* err, const tbgb_moments* out, double* state_out, cudaStream_t stream,
-                                 uint64_t* launches, cudaEvent_t ev_start, cudaEvent_t ev_stop) {
+                                 long long n, long long row_offset, int G, double* part, unsigned long long* spill,
+                                 unsigned long long* zfirst, uint32_t* err, const tbgb_moments* out, double* state_out,
+                                 cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start, cudaEvent_t ev_stop) {
   DenseArgs a;
   a.keys = keys; a.vals = vals; a.mask = mask; a.n = n; a.row_offset = row_offset;
   a.G = G; a.C = L.C; a.opg = L.opg; a.slots = L.slots;
-  a.part = part; a.zfirst = zfirst; a.err = err;
+  a.part = part; a.spill = spill; a.zfirst = zfirst; a.err = err;
   const bool aligned = (reinterpret_cast<uintptr_t>(keys) % 16 == 0) && (reinterpret_cast<uintptr_t>(vals) % 16 == 0) &&
                        (mask == nullptr || reinterpret_cast<uintptr_t>(mask) % 16 == 0);
   const bool masked = mask != nullptr;
   cudaError_t e;
   if (ev_start) cudaEventRecord(ev_start, stream);
-  if (L.maxslots == 1) {
-    if (masked) e = aligned ? launch_main<1, true, true>(L, a, stream) : launch_main<1, true, false>(L, a, stream);
-    else e = aligned ? launch_main<1, false, true>(L, a, stream) : launch_main<1, false, false>(L, a, stream);
-  } else {
-    if (masked) e = aligned ? launch_main<2, true, true>(L, a, stream) : launch_main<2, true, false>(L, a, stream);
-    else e = aligned ? launch_main<2, false, true>(L, a, stream) : launch_main<2, false, false>(L, a, stream);
-  }
+  if (L.maxslots == 1) e = launch_slots<1>(L, a, masked, aligned, stream);
+  else if (L.maxslots == 2) e = launch_slots<2>(L, a, masked, aligned, stream);
+  else e = launch_slots<4>(L, a, masked, aligned, stream);
   if (e != cudaSuccess) return e;
   if (ev_stop) cudaEventRecord(ev_stop, stream);
   (*launches)++;
   tbgb_moments o = out ? *out : tbgb_moments{};
-  const long long stride = static_cast<long long>(L.grid) * L.slots;
   const int blocks = (G * 32 + 255) / 256;
-  dense_fold_kernel<<<blocks, 256, 0, stream>>>(part, stride, L.grid, G, L.opg, zfirst, o, state_out);
+  dense_fold_kernel<<<blocks, 256, 0, stream>>>(part, spill, L.grid, G, L.opg, zfirst, o, state_out);
   e = cudaGetLastError();
   if (e == cudaSuccess) (*launches)++;
   return e;

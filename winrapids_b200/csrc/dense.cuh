@@ -12,7 +12,7 @@ constexpr int kDenseThreads = 512;  // threads per CTA (16 warps)
 constexpr int kDenseTile = 2048;    // rows per staged tile
 constexpr int kDenseStages = 4;     // depth of the TMA ring
 constexpr int kDenseMaxGroups = 1024;
-constexpr int kDenseColBudget = 12288;  // C * n_groups doubles of column buffer (96 KiB)
+constexpr int kDenseColBudget = 12288;  // 2 * C * n_groups doubles of column buffers (96 KiB)
 
 // Mergeable per-group state, stored as structure-of-arrays with ST_COUNT rows.
 //   nn       non-NaN rows          nf       finite rows
@@ -29,18 +29,20 @@ struct DenseLaunch {
   int maxslots;   // owner slots per thread (1 or 2)
   size_t smem;    // dynamic shared memory bytes
   size_t part_doubles;  // ST_COUNT * grid * slots
+  size_t spill_words;   // per-CTA spill states (u64 words)
 };
 
 DenseLaunch dense_plan(int n_groups, int num_sms);
 size_t dense_smem_bytes(int G, int C);
 
-// Enqueue the dense moments pipeline.  `part` holds part_doubles, `zfirst` G u64,
-// `err` one u32.  Writes either final outputs (`out`) or, when `state_out` is not
+// Enqueue the dense moments pipeline.  `part` holds part_doubles, `spill`
+// spill_words u64, `zfirst` G u64, `err` one u32.  Writes either final outputs (`out`) or, when `state_out` is not
 // NULL, the merged state table of this call (ST_COUNT * G doubles).
 cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, const double* vals, const uint64_t* mask,
-                                 long long n, long long row_offset, int G, double* part, unsigned long long* zfirst,
-                                 uint32_t* err, const tbgb_moments* out, double* state_out, cudaStream_t stream,
-                                 uint64_t* launches, cudaEvent_t ev_start = nullptr, cudaEvent_t ev_stop = nullptr);
+                                 long long n, long long row_offset, int G, double* part, unsigned long long* spill,
+                                 unsigned long long* zfirst, uint32_t* err, const tbgb_moments* out, double* state_out,
+                                 cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start = nullptr,
+                                 cudaEvent_t ev_stop = nullptr);
 
 cudaError_t merge_states_launch(const double* states, int n_states, int G, const tbgb_moments* out,
                                 cudaStream_t stream, uint64_t* launches);
