@@ -47,6 +47,7 @@ static_assert(STAGE_BYTES % 16 == 0, "bulk copy sizes must be 16-byte multiples"
 constexpr int BAR_SCATTER = 1;  // named barrier of the scatter warps
 constexpr int BAR_OWNER = 2;    // named barrier of the owner warps
 constexpr unsigned long long K_UNSET = 0x7FF8000000000001ull;  // NaN payload no finite value has
+constexpr uint32_t NO_RANK = 0xFFFFFFFFu;
 
 // spill state, per CTA, SoA over groups (u64 words)
 enum { SP_N = 0, SP_NINFP, SP_NINFN, SP_K, SP_S1, SP_S2, SP_MN, SP_MX, SP_COUNT };
@@ -287,27 +288,43 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
         }
       }
       if (ok) {
+        // classify: finite rows with an in-range key take the column path; rows with
+        // an out-of-range key, +-inf or a zero value also need the slow path below
+        uint32_t fin = 0, rare = 0;
 #pragma unroll
         for (int i = 0; i < RPS; ++i) {
-          const int g = kk[i];
           const double x = vv[i];
-          bool valid = ((mb >> i) & 1u) && !is_nan(x);
-          if (valid && static_cast<unsigned>(g) >= static_cast<unsigned>(G)) {
-            atomicOr(a.err, KERR_KEY_RANGE);
-            valid = false;
+          const bool m = (mb >> i) & 1u;
+          const bool inr = static_cast<unsigned>(kk[i]) < static_cast<unsigned>(G);
+          const bool f = is_finite(x);
+          fin |= static_cast<uint32_t>(m && inr && f) << i;
+          rare |= static_cast<uint32_t>(m && !is_nan(x) && (!inr || !f || x == 0.0)) << i;
+        }
+        // all ranks requested before any is used: the atomics overlap
+        uint32_t rk[RPS];
+#pragma unroll
+        for (int i = 0; i < RPS; ++i) rk[i] = ((fin >> i) & 1u) ? atomicAdd(&cnt[kk[i]], 1u) : NO_RANK;
+        uint32_t over = 0;
+#pragma unroll
+        for (int i = 0; i < RPS; ++i) {
+          if (rk[i] < static_cast<uint32_t>(C)) col[static_cast<size_t>(rk[i]) * G + kk[i]] = vv[i];
+          else if (rk[i] != NO_RANK) over |= 1u << i;
+        }
+        if (rare | over) {
+          for (int i = 0; i < RPS; ++i) {
+            const int g = kk[i];
+            const double x = vv[i];
+            if ((over >> i) & 1u) spill_add(sp, G, g, x);
+            if (!((rare >> i) & 1u)) continue;
+            if (static_cast<unsigned>(g) >= static_cast<unsigned>(G)) {
+              atomicOr(a.err, KERR_KEY_RANGE);
+            } else if (x == 0.0) {
+              const long long r = row0 + (i >> 1) * CHUNK + 2 * t + (i & 1);
+              atomicMin(&a.zfirst[g], zero_code(a.row_offset + r, x));
+            } else {
+              atomicAdd(sp + (x > 0 ? SP_NINFP : SP_NINFN) * G + g, 1ull);
+            }
           }
-          if (!valid) continue;
-          if (x == 0.0) {
-            const long long r = row0 + (i >> 1) * CHUNK + 2 * t + (i & 1);
-            atomicMin(&a.zfirst[g], zero_code(a.row_offset + r, x));
-          }
-          if (!is_finite(x)) {
-            atomicAdd(sp + (x > 0 ? SP_NINFP : SP_NINFN) * G + g, 1ull);
-            continue;
-          }
-          const uint32_t rk = atomicAdd(&cnt[g], 1u);
-          if (rk < static_cast<uint32_t>(C)) col[static_cast<size_t>(rk) * G + g] = x;
-          else spill_add(sp, G, g, x);
         }
       }
       // all scatter threads are done with stage s and with column buffer bs
