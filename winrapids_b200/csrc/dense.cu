@@ -11,11 +11,14 @@
 //
 // One persistent 512-thread CTA per SM, warp-specialised:
 //   * TMA bulk copies (cp.async.bulk + mbarrier, no multicast) stream 2048-row
-//     tiles of keys / values / mask words into a 4-deep shared-memory ring;
+//     tiles of keys / values / mask words into a 4-deep shared-memory ring, and
+//     bulk L2 prefetches run 4 tiles further ahead so that enough bytes are in
+//     flight to cover loaded HBM latency without more shared memory;
 //   * warps 0-7 ("scatter") rank each finite row inside its group with a shared
 //     u32 atomic and store the value into column `rank` of a [C][n_groups]
-//     buffer (two buffers, alternating per tile); +-inf rows and the rare rows
-//     ranked >= C go to a small per-CTA spill state in global memory;
+//     buffer (two buffers, alternating per tile); rows ranked >= C go to a
+//     per-buffer shared spill list (and, if that fills, to a per-CTA spill state
+//     in global memory, which also counts +-inf rows);
 //   * warps 8-15 ("owners") sweep the other buffer's columns concurrently and keep
 //     each group's accumulators in registers (branch-free: the columns hold finite
 //     values only; two independent accumulator chains per group).
@@ -43,6 +46,9 @@ constexpr uint32_t VAL_BYTES = TILE * 8;
 constexpr uint32_t MASK_BYTES = TILE / 8;
 constexpr uint32_t STAGE_BYTES = KEY_BYTES + VAL_BYTES + MASK_BYTES;
 static_assert(STAGE_BYTES % 16 == 0, "bulk copy sizes must be 16-byte multiples");
+
+constexpr int PF_AHEAD = 4;     // tiles prefetched into L2 beyond the shared ring
+constexpr int SPL = 256;        // shared spill-list entries per column buffer
 
 constexpr int BAR_SCATTER = 1;  // named barrier of the scatter warps
 constexpr int BAR_OWNER = 2;    // named barrier of the owner warps
@@ -111,8 +117,8 @@ struct DenseArgs {
 
 size_t dense_smem_bytes(int G, int C) {
   const size_t gp = (static_cast<size_t>(G) + 3) & ~size_t(3);
-  return static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * static_cast<size_t>(C) * G * 8 + 2 * gp * 4 +
-         (STAGES + 4) * 8 + 16;
+  return static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * static_cast<size_t>(C) * G * 8 + 2 * SPL * 8 +
+         2 * gp * 4 + 2 * SPL * 4 + 8 + (STAGES + 4) * 8 + 16;
 }
 
 DenseLaunch dense_plan(int G, int num_sms) {
@@ -153,6 +159,8 @@ struct OwnerAcc {
     K = 0.0; s1a = s1b = s2a = s2b = 0.0; mn = pos_inf(); mx = neg_inf(); nf = 0; kset = false;
   }
   // Sweep entries sub, sub+opg, ... < c of one group's column (finite values only).
+  // Extrema by plain compares (no NaN can reach a column); +-0 ties are settled
+  // later from the first-zero tracker.
   __device__ __forceinline__ void sweep(const double* cg, int c, int sub, int opg, int G) {
     if (c <= sub) return;
     if (!kset) { K = cg[static_cast<size_t>(sub) * G]; kset = true; }
@@ -165,18 +173,22 @@ struct OwnerAcc {
       s1b += d1;
       s2a = fma(d0, d0, s2a);
       s2b = fma(d1, d1, s2b);
-      mn = fmin(mn, fmin(x0, x1));
-      mx = fmax(mx, fmax(x0, x1));
+      const bool lt = x0 < x1;
+      const double lo = lt ? x0 : x1, hi = lt ? x1 : x0;
+      mn = lo < mn ? lo : mn;
+      mx = hi > mx ? hi : mx;
     }
-    if (e < c) {
-      const double x0 = cg[static_cast<size_t>(e) * G];
-      const double d0 = x0 - K;
-      s1a += d0;
-      s2a = fma(d0, d0, s2a);
-      mn = fmin(mn, x0);
-      mx = fmax(mx, x0);
-    }
+    if (e < c) add1(cg[static_cast<size_t>(e) * G], false);
     nf += static_cast<unsigned long long>((c - sub + opg - 1) / opg);
+  }
+  __device__ __forceinline__ void add1(double x, bool count) {
+    if (!kset) { K = x; kset = true; }
+    const double d = x - K;
+    s1a += d;
+    s2a = fma(d, d, s2a);
+    mn = x < mn ? x : mn;
+    mx = x > mx ? x : mx;
+    if (count) nf += 1;
   }
 };
 
@@ -188,9 +200,12 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   const int gp = (G + 3) & ~3;
   double* col0 = reinterpret_cast<double*>(smem + STAGES * STAGE_BYTES);
   double* col1 = col0 + static_cast<size_t>(C) * G;
-  uint32_t* cnt0 = reinterpret_cast<uint32_t*>(col1 + static_cast<size_t>(C) * G);
+  double* splv0 = col1 + static_cast<size_t>(C) * G;  // spill-list values [2][SPL]
+  uint32_t* cnt0 = reinterpret_cast<uint32_t*>(splv0 + 2 * SPL);
   uint32_t* cnt1 = cnt0 + gp;
-  uint64_t* full = reinterpret_cast<uint64_t*>(cnt1 + gp);  // [STAGES]
+  int* splk0 = reinterpret_cast<int*>(cnt1 + gp);      // spill-list keys [2][SPL]
+  uint32_t* splc = reinterpret_cast<uint32_t*>(splk0 + 2 * SPL);  // spill-list counts [2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(splc + 2);  // [STAGES]
   uint64_t* colfull = full + STAGES;                          // [2]
   uint64_t* colempty = colfull + 2;                           // [2]
   volatile int* abort = reinterpret_cast<volatile int*>(colempty + 2);
@@ -204,6 +219,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   unsigned long long* sp = a.spill + static_cast<size_t>(b) * SP_COUNT * G;
 
   for (int i = tid; i < 2 * gp; i += NT) cnt0[i] = 0;
+  if (tid < 2) splc[tid] = 0;
   for (int g = tid; g < G; g += NT) {
     sp[SP_N * G + g] = 0;
     sp[SP_NINFP * G + g] = 0;
@@ -230,6 +246,11 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     bulk_g2s(st + KEY_BYTES, a.vals + tile * TILE, VAL_BYTES, &full[s]);
     if (MASKED) bulk_g2s(st + KEY_BYTES + VAL_BYTES, a.mask + tile * (TILE / 64), MASK_BYTES, &full[s]);
   };
+  auto prefetch = [&](long long tile) {
+    bulk_prefetch_l2(a.keys + tile * TILE, KEY_BYTES);
+    bulk_prefetch_l2(a.vals + tile * TILE, VAL_BYTES);
+    if (MASKED) bulk_prefetch_l2(a.mask + tile * (TILE / 64), MASK_BYTES);
+  };
 
   if (tid < NSC) {
     // ------------------------------------------------------------ scatter warps
@@ -237,6 +258,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     long long issued = 0;
     if (TMA && t == 0) {
       for (int s = 0; s < STAGES && s < mytiles; ++s) issue(s, t_begin + s);
+      for (long long j = STAGES; j < STAGES + PF_AHEAD && j < mytiles; ++j) prefetch(t_begin + j);
       issued = mytiles < STAGES ? mytiles : STAGES;
     }
     long long k_fail = -1;
@@ -244,6 +266,8 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
       const int bs = static_cast<int>(k & 1);
       double* col = bs ? col1 : col0;
       uint32_t* cnt = bs ? cnt1 : cnt0;
+      double* splv = splv0 + bs * SPL;
+      int* splk = splk0 + bs * SPL;
       bool ok = true;
       if (k >= 2) ok = wait_or_abort(&colempty[bs], static_cast<uint32_t>(((k >> 1) - 1) & 1), a.err, abort);
       const bool tail = k >= mytiles;
@@ -314,7 +338,11 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
           for (int i = 0; i < RPS; ++i) {
             const int g = kk[i];
             const double x = vv[i];
-            if ((over >> i) & 1u) spill_add(sp, G, g, x);
+            if ((over >> i) & 1u) {
+              const uint32_t slot = atomicAdd(&splc[bs], 1u);
+              if (slot < SPL) { splk[slot] = g; splv[slot] = x; }
+              else spill_add(sp, G, g, x);
+            }
             if (!((rare >> i) & 1u)) continue;
             if (static_cast<unsigned>(g) >= static_cast<unsigned>(G)) {
               atomicOr(a.err, KERR_KEY_RANGE);
@@ -335,6 +363,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
           fence_proxy_async_smem();
           issue(s, t_begin + k + STAGES);
           ++issued;
+          if (k + STAGES + PF_AHEAD < mytiles) prefetch(t_begin + k + STAGES + PF_AHEAD);
         }
         mbar_arrive(&colfull[bs]);
       }
@@ -368,6 +397,8 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
       const int bs = static_cast<int>(k & 1);
       const double* col = bs ? col1 : col0;
       uint32_t* cnt = bs ? cnt1 : cnt0;
+      const double* splv = splv0 + bs * SPL;
+      const int* splk = splk0 + bs * SPL;
       const bool ok = wait_or_abort(&colfull[bs], static_cast<uint32_t>((k >> 1) & 1), a.err, abort);
       int c[MAXSLOTS];
 #pragma unroll
@@ -376,6 +407,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
         const int v = static_cast<int>(cnt[g]);
         c[q] = v < C ? v : C;
       }
+      const int nspill = static_cast<int>(splc[bs] < SPL ? splc[bs] : SPL);
       // every owner has read its counts (and agrees on failure)
       if (bar_red_or(BAR_OWNER, NOW, !ok || *abort)) {
         if (!ok) *abort = 1;
@@ -384,9 +416,16 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
 #pragma unroll
       for (int q = 0; q < MAXSLOTS; ++q)
         if (og[q] >= 0 && osub[q] == 0) cnt[og[q]] = 0;
+      if (o == 0) splc[bs] = 0;
 #pragma unroll
       for (int q = 0; q < MAXSLOTS; ++q)
         if (og[q] >= 0) acc[q].sweep(col + og[q], c[q], osub[q], a.opg, G);
+      for (int e = 0; e < nspill; ++e) {  // rows that overflowed their column (rare)
+        const int key = splk[e];
+#pragma unroll
+        for (int q = 0; q < MAXSLOTS; ++q)
+          if (og[q] == key && osub[q] == 0) acc[q].add1(splv[e], true);
+      }
       named_bar_sync(BAR_OWNER, NOW);  // column buffer bs fully read, counts reset
       if (o == 0) mbar_arrive(&colempty[bs]);
     }
