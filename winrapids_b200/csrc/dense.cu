@@ -32,9 +32,11 @@
 
 namespace tbgb {
 
-constexpr int NT = kDenseThreads;   // 512
+constexpr int NT = kDenseThreads;   // 544: 8 scatter + 8 owner + 1 producer warp
 constexpr int NSC = 256;            // scatter threads (warps 0-7)
 constexpr int NOW = 256;            // owner threads (warps 8-15)
+constexpr int SCATTER_WARPS = NSC / 32;
+constexpr int PRODUCER_WARP = (NSC + NOW) / 32;  // warp 16
 constexpr int TILE = kDenseTile;    // rows per staged tile
 constexpr int STAGES = kDenseStages;
 constexpr int RPS = TILE / NSC;     // rows per scatter thread per tile (8)
@@ -50,7 +52,6 @@ static_assert(STAGE_BYTES % 16 == 0, "bulk copy sizes must be 16-byte multiples"
 constexpr int PF_AHEAD = 4;     // tiles prefetched into L2 beyond the shared ring
 constexpr int SPL = 256;        // shared spill-list entries per column buffer
 
-constexpr int BAR_SCATTER = 1;  // named barrier of the scatter warps
 constexpr int BAR_OWNER = 2;    // named barrier of the owner warps
 constexpr unsigned long long K_UNSET = 0x7FF8000000000001ull;  // NaN payload no finite value has
 constexpr uint32_t NO_RANK = 0xFFFFFFFFu;
@@ -118,7 +119,7 @@ struct DenseArgs {
 size_t dense_smem_bytes(int G, int C) {
   const size_t gp = (static_cast<size_t>(G) + 3) & ~size_t(3);
   return static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * static_cast<size_t>(C) * G * 8 + 2 * SPL * 8 +
-         2 * gp * 4 + 2 * SPL * 4 + 8 + (STAGES + 4) * 8 + 16;
+         2 * gp * 4 + 2 * SPL * 4 + 8 + (2 * STAGES + 4) * 8 + 16;
 }
 
 DenseLaunch dense_plan(int G, int num_sms) {
@@ -205,9 +206,10 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   uint32_t* cnt1 = cnt0 + gp;
   int* splk0 = reinterpret_cast<int*>(cnt1 + gp);      // spill-list keys [2][SPL]
   uint32_t* splc = reinterpret_cast<uint32_t*>(splk0 + 2 * SPL);  // spill-list counts [2]
-  uint64_t* full = reinterpret_cast<uint64_t*>(splc + 2);  // [STAGES]
-  uint64_t* colfull = full + STAGES;                          // [2]
-  uint64_t* colempty = colfull + 2;                           // [2]
+  uint64_t* full = reinterpret_cast<uint64_t*>(splc + 2);  // [STAGES] tile landed
+  uint64_t* empty = full + STAGES;                            // [STAGES] tile consumed
+  uint64_t* colfull = empty + STAGES;                         // [2] column buffer written
+  uint64_t* colempty = colfull + 2;                           // [2] column buffer swept
   volatile int* abort = reinterpret_cast<volatile int*>(colempty + 2);
 
   const long long ntiles = a.n / TILE;
@@ -231,8 +233,8 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     sp[SP_MX * G + g] = 0;
   }
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) mbar_init(&full[s], 1);
-    for (int s = 0; s < 2; ++s) { mbar_init(&colfull[s], 1); mbar_init(&colempty[s], 1); }
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], SCATTER_WARPS); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&colfull[s], SCATTER_WARPS); mbar_init(&colempty[s], 1); }
     *abort = 0;
     mbar_fence_init();
   }
@@ -252,16 +254,44 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     if (MASKED) bulk_prefetch_l2(a.mask + tile * (TILE / 64), MASK_BYTES);
   };
 
-  if (tid < NSC) {
-    // ------------------------------------------------------------ scatter warps
-    const int t = tid;
-    long long issued = 0;
-    if (TMA && t == 0) {
+  const int warp = tid >> 5, lane = tid & 31;
+  if (warp == PRODUCER_WARP) {
+    // ------------------------------------------------------------ producer warp
+    // Refills each stage as soon as all scatter warps released it, and keeps
+    // PF_AHEAD further tiles streaming into L2.
+    if (TMA && lane == 0) {
+      long long issued = 0;
       for (int s = 0; s < STAGES && s < mytiles; ++s) issue(s, t_begin + s);
-      for (long long j = STAGES; j < STAGES + PF_AHEAD && j < mytiles; ++j) prefetch(t_begin + j);
       issued = mytiles < STAGES ? mytiles : STAGES;
+      for (long long j = STAGES; j < STAGES + PF_AHEAD && j < mytiles; ++j) prefetch(t_begin + j);
+      bool failed = false;
+      for (long long k = 0; k + STAGES < mytiles; ++k) {
+        const int st = static_cast<int>(k % STAGES);
+        if (!wait_or_abort(&empty[st], static_cast<uint32_t>((k / STAGES) & 1), a.err, abort)) {
+          failed = true;
+          *abort = 1;
+          break;
+        }
+        fence_proxy_async_smem();
+        issue(st, t_begin + k + STAGES);
+        ++issued;
+        if (k + STAGES + PF_AHEAD < mytiles) prefetch(t_begin + k + STAGES + PF_AHEAD);
+      }
+      if (failed || *abort) {
+        // leave no bulk copy in flight into this CTA's shared memory (bounded waits)
+        for (long long j = issued - STAGES < 0 ? 0 : issued - STAGES; j < issued; ++j) {
+          const uint64_t t0 = globaltimer_ns();
+          while (!mbar_try_wait(&full[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1))) {
+            if (globaltimer_ns() - t0 > 500000000ull) break;
+          }
+        }
+      }
     }
-    long long k_fail = -1;
+  } else if (tid < NSC) {
+    // ------------------------------------------------------------ scatter warps
+    // Each warp runs independently: it signals stage release and column
+    // completion with one mbarrier arrival per warp.
+    const int t = tid;
     for (long long k = 0; k < nbatch; ++k) {
       const int bs = static_cast<int>(k & 1);
       double* col = bs ? col1 : col0;
@@ -311,79 +341,62 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
           }
         }
       }
-      if (ok) {
-        // classify: finite rows with an in-range key take the column path; rows with
-        // an out-of-range key, +-inf or a zero value also need the slow path below
-        uint32_t fin = 0, rare = 0;
+      if (__any_sync(0xffffffffu, !ok)) {
+        if (lane == 0) *abort = 1;
+        break;
+      }
+      // classify: finite rows with an in-range key take the column path; rows with
+      // an out-of-range key, +-inf or a zero value also need the slow path below
+      uint32_t fin = 0, rare = 0;
 #pragma unroll
+      for (int i = 0; i < RPS; ++i) {
+        const double x = vv[i];
+        const bool m = (mb >> i) & 1u;
+        const bool inr = static_cast<unsigned>(kk[i]) < static_cast<unsigned>(G);
+        const bool f = is_finite(x);
+        fin |= static_cast<uint32_t>(m && inr && f) << i;
+        rare |= static_cast<uint32_t>(m && !is_nan(x) && (!inr || !f || x == 0.0)) << i;
+      }
+      // the stage's rows are in registers: release it to the producer
+      __syncwarp();
+      if (TMA && !tail && lane == 0) mbar_arrive(&empty[s]);
+      // all ranks requested before any is used: the atomics overlap
+      uint32_t rk[RPS];
+#pragma unroll
+      for (int i = 0; i < RPS; ++i) rk[i] = ((fin >> i) & 1u) ? atomicAdd(&cnt[kk[i]], 1u) : NO_RANK;
+      uint32_t over = 0;
+#pragma unroll
+      for (int i = 0; i < RPS; ++i) {
+        if (rk[i] < static_cast<uint32_t>(C)) col[static_cast<size_t>(rk[i]) * G + kk[i]] = vv[i];
+        else if (rk[i] != NO_RANK) over |= 1u << i;
+      }
+      if (rare | over) {
         for (int i = 0; i < RPS; ++i) {
+          const int g = kk[i];
           const double x = vv[i];
-          const bool m = (mb >> i) & 1u;
-          const bool inr = static_cast<unsigned>(kk[i]) < static_cast<unsigned>(G);
-          const bool f = is_finite(x);
-          fin |= static_cast<uint32_t>(m && inr && f) << i;
-          rare |= static_cast<uint32_t>(m && !is_nan(x) && (!inr || !f || x == 0.0)) << i;
-        }
-        // all ranks requested before any is used: the atomics overlap
-        uint32_t rk[RPS];
-#pragma unroll
-        for (int i = 0; i < RPS; ++i) rk[i] = ((fin >> i) & 1u) ? atomicAdd(&cnt[kk[i]], 1u) : NO_RANK;
-        uint32_t over = 0;
-#pragma unroll
-        for (int i = 0; i < RPS; ++i) {
-          if (rk[i] < static_cast<uint32_t>(C)) col[static_cast<size_t>(rk[i]) * G + kk[i]] = vv[i];
-          else if (rk[i] != NO_RANK) over |= 1u << i;
-        }
-        if (rare | over) {
-          for (int i = 0; i < RPS; ++i) {
-            const int g = kk[i];
-            const double x = vv[i];
-            if ((over >> i) & 1u) {
-              const uint32_t slot = atomicAdd(&splc[bs], 1u);
-              if (slot < SPL) { splk[slot] = g; splv[slot] = x; }
-              else spill_add(sp, G, g, x);
-            }
-            if (!((rare >> i) & 1u)) continue;
-            if (static_cast<unsigned>(g) >= static_cast<unsigned>(G)) {
-              atomicOr(a.err, KERR_KEY_RANGE);
-            } else if (x == 0.0) {
-              const long long r = row0 + (i >> 1) * CHUNK + 2 * t + (i & 1);
-              atomicMin(&a.zfirst[g], zero_code(a.row_offset + r, x));
-            } else {
-              atomicAdd(sp + (x > 0 ? SP_NINFP : SP_NINFN) * G + g, 1ull);
-            }
+          if ((over >> i) & 1u) {
+            const uint32_t slot = atomicAdd(&splc[bs], 1u);
+            if (slot < SPL) { splk[slot] = g; splv[slot] = x; }
+            else spill_add(sp, G, g, x);
+          }
+          if (!((rare >> i) & 1u)) continue;
+          if (static_cast<unsigned>(g) >= static_cast<unsigned>(G)) {
+            atomicOr(a.err, KERR_KEY_RANGE);
+          } else if (x == 0.0) {
+            const long long r = row0 + (i >> 1) * CHUNK + 2 * t + (i & 1);
+            atomicMin(&a.zfirst[g], zero_code(a.row_offset + r, x));
+          } else {
+            atomicAdd(sp + (x > 0 ? SP_NINFP : SP_NINFN) * G + g, 1ull);
           }
         }
       }
-      // all scatter threads are done with stage s and with column buffer bs
-      const bool fail = bar_red_or(BAR_SCATTER, NSC, !ok || *abort);
-      if (t == 0) {
-        if (fail) *abort = 1;
-        if (TMA && !fail && !tail && k + STAGES < mytiles) {
-          fence_proxy_async_smem();
-          issue(s, t_begin + k + STAGES);
-          ++issued;
-          if (k + STAGES + PF_AHEAD < mytiles) prefetch(t_begin + k + STAGES + PF_AHEAD);
-        }
-        mbar_arrive(&colfull[bs]);
-      }
-      if (fail) {
-        k_fail = k;
-        break;
-      }
-    }
-    if (TMA && t == 0 && k_fail >= 0) {
-      // leave no bulk copy in flight into this CTA's shared memory (bounded waits)
-      for (long long j = k_fail; j < issued; ++j) {
-        const uint64_t t0 = globaltimer_ns();
-        while (!mbar_try_wait(&full[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1))) {
-          if (globaltimer_ns() - t0 > 500000000ull) break;
-        }
-      }
+      // this warp's rows of tile k are in column buffer bs
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&colfull[bs]);
     }
   } else {
     // ------------------------------------------------------------ owner warps
-    const int o = tid - NSC;
+    const int o = tid - NSC;  // owner threads: warps 8-15
     OwnerAcc acc[MAXSLOTS];
     int og[MAXSLOTS], osub[MAXSLOTS];
 #pragma unroll
