@@ -88,17 +88,16 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 // Bounded wait that also gives up when the other warp group raised `abort`.
+// Waiting threads sleep in try_wait (suspend hint) rather than spin.
 __device__ __forceinline__ bool wait_or_abort(uint64_t* bar, uint32_t parity, uint32_t* err, volatile int* abort) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
-  for (uint32_t it = 1;; ++it) {
-    if (mbar_try_wait(bar, parity)) return true;
-    if ((it & 255u) == 0) {
-      if (*abort) return false;
-      if (globaltimer_ns() - t0 > 2000000000ull) {
-        atomicOr(err, KERR_TIMEOUT);
-        return false;
-      }
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (*abort) return false;
+    if (globaltimer_ns() - t0 > 2000000000ull) {
+      atomicOr(err, KERR_TIMEOUT);
+      return false;
     }
   }
 }
@@ -166,20 +165,27 @@ struct OwnerAcc {
     if (c <= sub) return;
     if (!kset) { K = cg[static_cast<size_t>(sub) * G]; kset = true; }
     int e = sub;
-    for (; e + opg < c; e += 2 * opg) {
-      const double x0 = cg[static_cast<size_t>(e) * G];
-      const double x1 = cg[static_cast<size_t>(e + opg) * G];
-      const double d0 = x0 - K, d1 = x1 - K;
+    const size_t step = static_cast<size_t>(opg) * G;
+    const double* p = cg + static_cast<size_t>(sub) * G;
+    for (; e + 3 * opg < c; e += 4 * opg, p += 4 * step) {
+      const double x0 = p[0], x1 = p[step], x2 = p[2 * step], x3 = p[3 * step];
+      const double d0 = x0 - K, d1 = x1 - K, d2 = x2 - K, d3 = x3 - K;
       s1a += d0;
       s1b += d1;
       s2a = fma(d0, d0, s2a);
       s2b = fma(d1, d1, s2b);
-      const bool lt = x0 < x1;
-      const double lo = lt ? x0 : x1, hi = lt ? x1 : x0;
+      s1a += d2;
+      s1b += d3;
+      s2a = fma(d2, d2, s2a);
+      s2b = fma(d3, d3, s2b);
+      const bool l01 = x0 < x1, l23 = x2 < x3;
+      const double lo01 = l01 ? x0 : x1, hi01 = l01 ? x1 : x0;
+      const double lo23 = l23 ? x2 : x3, hi23 = l23 ? x3 : x2;
+      const double lo = lo01 < lo23 ? lo01 : lo23, hi = hi01 > hi23 ? hi01 : hi23;
       mn = lo < mn ? lo : mn;
       mx = hi > mx ? hi : mx;
     }
-    if (e < c) add1(cg[static_cast<size_t>(e) * G], false);
+    for (; e < c; e += opg, p += step) add1(*p, false);
     nf += static_cast<unsigned long long>((c - sub + opg - 1) / opg);
   }
   __device__ __forceinline__ void add1(double x, bool count) {
@@ -345,30 +351,50 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
         if (lane == 0) *abort = 1;
         break;
       }
-      // classify: finite rows with an in-range key take the column path; rows with
-      // an out-of-range key, +-inf or a zero value also need the slow path below
-      uint32_t fin = 0, rare = 0;
+      // Fast path: every row of the warp is unmasked with an in-range key and a
+      // finite non-zero value (one predicated compare chain per row, one vote).
+      bool good = !MASKED || mb == 0xFFu;
 #pragma unroll
-      for (int i = 0; i < RPS; ++i) {
-        const double x = vv[i];
-        const bool m = (mb >> i) & 1u;
-        const bool inr = static_cast<unsigned>(kk[i]) < static_cast<unsigned>(G);
-        const bool f = is_finite(x);
-        fin |= static_cast<uint32_t>(m && inr && f) << i;
-        rare |= static_cast<uint32_t>(m && !is_nan(x) && (!inr || !f || x == 0.0)) << i;
-      }
+      for (int i = 0; i < RPS; ++i)
+        good = good && static_cast<unsigned>(kk[i]) < static_cast<unsigned>(G) && fabs(vv[i]) > 0.0 &&
+               fabs(vv[i]) < pos_inf();
+      const bool all_good = __all_sync(0xffffffffu, good);
       // the stage's rows are in registers: release it to the producer
       __syncwarp();
       if (TMA && !tail && lane == 0) mbar_arrive(&empty[s]);
-      // all ranks requested before any is used: the atomics overlap
-      uint32_t rk[RPS];
-#pragma unroll
-      for (int i = 0; i < RPS; ++i) rk[i] = ((fin >> i) & 1u) ? atomicAdd(&cnt[kk[i]], 1u) : NO_RANK;
       uint32_t over = 0;
+      if (all_good) {
+        uint32_t rk[RPS];
 #pragma unroll
-      for (int i = 0; i < RPS; ++i) {
-        if (rk[i] < static_cast<uint32_t>(C)) col[static_cast<size_t>(rk[i]) * G + kk[i]] = vv[i];
-        else if (rk[i] != NO_RANK) over |= 1u << i;
+        for (int i = 0; i < RPS; ++i) rk[i] = atomicAdd(&cnt[kk[i]], 1u);
+#pragma unroll
+        for (int i = 0; i < RPS; ++i) {
+          if (rk[i] < static_cast<uint32_t>(C)) col[static_cast<size_t>(rk[i]) * G + kk[i]] = vv[i];
+          else over |= 1u << i;
+        }
+      }
+      uint32_t rare = 0;
+      if (!all_good) {
+        // general path: finite rows with an in-range key take the column; rows with
+        // an out-of-range key, +-inf or a zero value also need the slow path below
+        uint32_t fin = 0;
+#pragma unroll
+        for (int i = 0; i < RPS; ++i) {
+          const double x = vv[i];
+          const bool m = (mb >> i) & 1u;
+          const bool inr = static_cast<unsigned>(kk[i]) < static_cast<unsigned>(G);
+          const bool f = is_finite(x);
+          fin |= static_cast<uint32_t>(m && inr && f) << i;
+          rare |= static_cast<uint32_t>(m && !is_nan(x) && (!inr || !f || x == 0.0)) << i;
+        }
+        uint32_t rk[RPS];
+#pragma unroll
+        for (int i = 0; i < RPS; ++i) rk[i] = ((fin >> i) & 1u) ? atomicAdd(&cnt[kk[i]], 1u) : NO_RANK;
+#pragma unroll
+        for (int i = 0; i < RPS; ++i) {
+          if (rk[i] < static_cast<uint32_t>(C)) col[static_cast<size_t>(rk[i]) * G + kk[i]] = vv[i];
+          else if (rk[i] != NO_RANK) over |= 1u << i;
+        }
       }
       if (rare | over) {
         for (int i = 0; i < RPS; ++i) {
