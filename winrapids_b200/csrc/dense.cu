@@ -118,7 +118,7 @@ struct DenseArgs {
 size_t dense_smem_bytes(int G, int C) {
   const size_t gp = (static_cast<size_t>(G) + 3) & ~size_t(3);
   return static_cast<size_t>(STAGES) * STAGE_BYTES + 2 * static_cast<size_t>(C) * G * 8 + 2 * SPL * 8 +
-         2 * gp * 4 + 2 * SPL * 4 + 8 + (2 * STAGES + 4) * 8 + 16;
+         2 * gp * 4 + 2 * SPL * 4 + 16 + (2 * STAGES + 4) * 8 + 16;
 }
 
 DenseLaunch dense_plan(int G, int num_sms) {
@@ -151,51 +151,87 @@ __device__ __noinline__ void spill_add(unsigned long long* sp, int G, int g, dou
   atomicMax(sp + SP_MX * G + g, f2o(v));
 }
 
+// Register accumulators of one owner slot; NCH independent chains shorten the
+// dependency path through S1/S2.
+template <int NCH>
 struct OwnerAcc {
-  double K, s1a, s1b, s2a, s2b, mn, mx;
+  double K, s1[NCH], s2[NCH], mn, mx;
   unsigned long long nf;
   bool kset;
   __device__ __forceinline__ void init() {
-    K = 0.0; s1a = s1b = s2a = s2b = 0.0; mn = pos_inf(); mx = neg_inf(); nf = 0; kset = false;
+    K = 0.0;
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) { s1[j] = 0.0; s2[j] = 0.0; }
+    mn = pos_inf(); mx = neg_inf(); nf = 0; kset = false;
   }
-  // Sweep entries sub, sub+opg, ... < c of one group's column (finite values only).
-  // Extrema by plain compares (no NaN can reach a column); +-0 ties are settled
-  // later from the first-zero tracker.
-  __device__ __forceinline__ void sweep(const double* cg, int c, int sub, int opg, int G) {
-    if (c <= sub) return;
-    if (!kset) { K = cg[static_cast<size_t>(sub) * G]; kset = true; }
-    int e = sub;
-    const size_t step = static_cast<size_t>(opg) * G;
-    const double* p = cg + static_cast<size_t>(sub) * G;
-    for (; e + 3 * opg < c; e += 4 * opg, p += 4 * step) {
-      const double x0 = p[0], x1 = p[step], x2 = p[2 * step], x3 = p[3 * step];
-      const double d0 = x0 - K, d1 = x1 - K, d2 = x2 - K, d3 = x3 - K;
-      s1a += d0;
-      s1b += d1;
-      s2a = fma(d0, d0, s2a);
-      s2b = fma(d1, d1, s2b);
-      s1a += d2;
-      s1b += d3;
-      s2a = fma(d2, d2, s2a);
-      s2b = fma(d3, d3, s2b);
-      const bool l01 = x0 < x1, l23 = x2 < x3;
-      const double lo01 = l01 ? x0 : x1, hi01 = l01 ? x1 : x0;
-      const double lo23 = l23 ? x2 : x3, hi23 = l23 ? x3 : x2;
-      const double lo = lo01 < lo23 ? lo01 : lo23, hi = hi01 > hi23 ? hi01 : hi23;
-      mn = lo < mn ? lo : mn;
-      mx = hi > mx ? hi : mx;
-    }
-    for (; e < c; e += opg, p += step) add1(*p, false);
-    nf += static_cast<unsigned long long>((c - sub + opg - 1) / opg);
+  __device__ __forceinline__ void quad(double x0, double x1, double x2, double x3) {
+    const double d0 = x0 - K, d1 = x1 - K, d2 = x2 - K, d3 = x3 - K;
+    s1[0 % NCH] += d0;
+    s2[0 % NCH] = fma(d0, d0, s2[0 % NCH]);
+    s1[1 % NCH] += d1;
+    s2[1 % NCH] = fma(d1, d1, s2[1 % NCH]);
+    s1[2 % NCH] += d2;
+    s2[2 % NCH] = fma(d2, d2, s2[2 % NCH]);
+    s1[3 % NCH] += d3;
+    s2[3 % NCH] = fma(d3, d3, s2[3 % NCH]);
+    // extrema by plain compares (no NaN reaches a column); +-0 ties are settled
+    // later from the first-zero tracker
+    const bool l01 = x0 < x1, l23 = x2 < x3;
+    const double lo01 = l01 ? x0 : x1, hi01 = l01 ? x1 : x0;
+    const double lo23 = l23 ? x2 : x3, hi23 = l23 ? x3 : x2;
+    const double lo = lo01 < lo23 ? lo01 : lo23, hi = hi01 > hi23 ? hi01 : hi23;
+    mn = lo < mn ? lo : mn;
+    mx = hi > mx ? hi : mx;
   }
-  __device__ __forceinline__ void add1(double x, bool count) {
-    if (!kset) { K = x; kset = true; }
+  __device__ __forceinline__ void one(double x) {
     const double d = x - K;
-    s1a += d;
-    s2a = fma(d, d, s2a);
+    s1[0] += d;
+    s2[0] = fma(d, d, s2[0]);
     mn = x < mn ? x : mn;
     mx = x > mx ? x : mx;
-    if (count) nf += 1;
+  }
+  // Sweep entries sub, sub+opg, ... < c of one group's column (finite values
+  // only), keeping the next four loads in flight while the current four are added.
+  __device__ __forceinline__ void sweep(const double* cg, int c, int sub, int opg, int G) {
+    if (c <= sub) return;
+    const size_t step = static_cast<size_t>(opg) * G;
+    const double* p = cg + static_cast<size_t>(sub) * G;
+    const int m = (c - sub + opg - 1) / opg;  // values of this sub-owner
+    if (!kset) { K = p[0]; kset = true; }
+    int i = 0;
+    if (m >= 4) {
+      double y0 = p[0], y1 = p[step], y2 = p[2 * step], y3 = p[3 * step];
+      for (; i + 8 <= m; i += 4) {
+        const double x0 = y0, x1 = y1, x2 = y2, x3 = y3;
+        const double* q = p + static_cast<size_t>(i + 4) * step;
+        y0 = q[0];
+        y1 = q[step];
+        y2 = q[2 * step];
+        y3 = q[3 * step];
+        quad(x0, x1, x2, x3);
+      }
+      quad(y0, y1, y2, y3);
+      i += 4;
+    }
+    for (; i < m; ++i) one(p[static_cast<size_t>(i) * step]);
+    nf += static_cast<unsigned long long>(m);
+  }
+  __device__ __forceinline__ void add1(double x) {
+    if (!kset) { K = x; kset = true; }
+    one(x);
+    nf += 1;
+  }
+  __device__ __forceinline__ double sum_s1() const {
+    double r = 0.0;
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) r += s1[j];
+    return r;
+  }
+  __device__ __forceinline__ double sum_s2() const {
+    double r = 0.0;
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) r += s2[j];
+    return r;
   }
 };
 
@@ -211,8 +247,10 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   uint32_t* cnt0 = reinterpret_cast<uint32_t*>(splv0 + 2 * SPL);
   uint32_t* cnt1 = cnt0 + gp;
   int* splk0 = reinterpret_cast<int*>(cnt1 + gp);      // spill-list keys [2][SPL]
-  uint32_t* splc = reinterpret_cast<uint32_t*>(splk0 + 2 * SPL);  // spill-list counts [2]
-  uint64_t* full = reinterpret_cast<uint64_t*>(splc + 2);  // [STAGES] tile landed
+  // spill-list counts, one per batch modulo 4: batch k uses splc[k & 3]; the owners of
+  // batch k clear splc[(k + 2) & 3], which batch k - 2 used and batch k + 2 will use
+  uint32_t* splc = reinterpret_cast<uint32_t*>(splk0 + 2 * SPL);
+  uint64_t* full = reinterpret_cast<uint64_t*>(splc + 4);  // [STAGES] tile landed
   uint64_t* empty = full + STAGES;                            // [STAGES] tile consumed
   uint64_t* colfull = empty + STAGES;                         // [2] column buffer written
   uint64_t* colempty = colfull + 2;                           // [2] column buffer swept
@@ -227,7 +265,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   unsigned long long* sp = a.spill + static_cast<size_t>(b) * SP_COUNT * G;
 
   for (int i = tid; i < 2 * gp; i += NT) cnt0[i] = 0;
-  if (tid < 2) splc[tid] = 0;
+  if (tid < 4) splc[tid] = 0;
   for (int g = tid; g < G; g += NT) {
     sp[SP_N * G + g] = 0;
     sp[SP_NINFP * G + g] = 0;
@@ -240,7 +278,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   }
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], SCATTER_WARPS); }
-    for (int s = 0; s < 2; ++s) { mbar_init(&colfull[s], SCATTER_WARPS); mbar_init(&colempty[s], 1); }
+    for (int s = 0; s < 2; ++s) { mbar_init(&colfull[s], SCATTER_WARPS); mbar_init(&colempty[s], NOW / 32); }
     *abort = 0;
     mbar_fence_init();
   }
@@ -401,7 +439,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
           const int g = kk[i];
           const double x = vv[i];
           if ((over >> i) & 1u) {
-            const uint32_t slot = atomicAdd(&splc[bs], 1u);
+            const uint32_t slot = atomicAdd(&splc[k & 3], 1u);
             if (slot < SPL) { splk[slot] = g; splv[slot] = x; }
             else spill_add(sp, G, g, x);
           }
@@ -423,7 +461,8 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   } else {
     // ------------------------------------------------------------ owner warps
     const int o = tid - NSC;  // owner threads: warps 8-15
-    OwnerAcc acc[MAXSLOTS];
+    constexpr int NCH = MAXSLOTS == 1 ? 4 : (MAXSLOTS == 2 ? 2 : 1);
+    OwnerAcc<NCH> acc[MAXSLOTS];
     int og[MAXSLOTS], osub[MAXSLOTS];
 #pragma unroll
     for (int q = 0; q < MAXSLOTS; ++q) {
@@ -432,6 +471,10 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
       if (slot < a.slots) { osub[q] = slot / G; og[q] = slot - osub[q] * G; }
       else { og[q] = -1; osub[q] = 0; }
     }
+    // With one owner per group (n_groups >= owner threads) each count has a single
+    // reader and the owner warps run independently; otherwise the sub-owners of a
+    // group meet at a named barrier before its count is reset.
+    const bool shared_counts = a.opg > 1;
     for (long long k = 0; k < nbatch; ++k) {
       const int bs = static_cast<int>(k & 1);
       const double* col = bs ? col1 : col0;
@@ -446,16 +489,20 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
         const int v = static_cast<int>(cnt[g]);
         c[q] = v < C ? v : C;
       }
-      const int nspill = static_cast<int>(splc[bs] < SPL ? splc[bs] : SPL);
-      // every owner has read its counts (and agrees on failure)
-      if (bar_red_or(BAR_OWNER, NOW, !ok || *abort)) {
-        if (!ok) *abort = 1;
+      const uint32_t ns = splc[k & 3];
+      const int nspill = static_cast<int>(ns < SPL ? ns : SPL);
+      if (shared_counts) {
+        if (bar_red_or(BAR_OWNER, NOW, !ok || *abort)) {
+          if (!ok) *abort = 1;
+          break;
+        }
+      } else if (__any_sync(0xffffffffu, !ok)) {
+        if (lane == 0) *abort = 1;
         break;
       }
 #pragma unroll
       for (int q = 0; q < MAXSLOTS; ++q)
         if (og[q] >= 0 && osub[q] == 0) cnt[og[q]] = 0;
-      if (o == 0) splc[bs] = 0;
 #pragma unroll
       for (int q = 0; q < MAXSLOTS; ++q)
         if (og[q] >= 0) acc[q].sweep(col + og[q], c[q], osub[q], a.opg, G);
@@ -463,10 +510,13 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
         const int key = splk[e];
 #pragma unroll
         for (int q = 0; q < MAXSLOTS; ++q)
-          if (og[q] == key && osub[q] == 0) acc[q].add1(splv[e], true);
+          if (og[q] == key && osub[q] == 0) acc[q].add1(splv[e]);
       }
-      named_bar_sync(BAR_OWNER, NOW);  // column buffer bs fully read, counts reset
-      if (o == 0) mbar_arrive(&colempty[bs]);
+      if (o == 0) splc[(k + 2) & 3] = 0;
+      // this warp is done with column buffer bs (and, when counts are shared,
+      // every owner has read them before the first reset above)
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&colempty[bs]);
     }
     // partial states of this CTA's owners
     const long long stride = static_cast<long long>(P) * a.slots;
@@ -474,8 +524,8 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     for (int q = 0; q < MAXSLOTS; ++q) {
       if (og[q] < 0) continue;
       const long long idx = static_cast<long long>(b) * a.slots + (o + q * NOW);
-      const OwnerAcc& A = acc[q];
-      const double s1 = A.s1a + A.s1b, s2 = A.s2a + A.s2b;
+      const auto& A = acc[q];
+      const double s1 = A.sum_s1(), s2 = A.sum_s2();
       double meanoff = 0.0, m2 = 0.0;
       if (A.nf > 0) {
         meanoff = s1 / static_cast<double>(A.nf);
