@@ -19,9 +19,11 @@
 //     buffer (two buffers, alternating per tile); rows ranked >= C go to a
 //     per-buffer shared spill list (and, if that fills, to a per-CTA spill state
 //     in global memory, which also counts +-inf rows);
-//   * warps 8-15 ("owners") sweep the other buffer's columns concurrently and keep
-//     each group's accumulators in registers (branch-free: the columns hold finite
-//     values only; two independent accumulator chains per group).
+//   * two teams of 8 owner warps (team t owns the buffer of every other tile) sweep
+//     the columns concurrently and keep each group's accumulators in registers
+//     (branch-free: the columns hold finite values only; several accumulator
+//     chains per group, loads kept in flight);
+//   * a producer warp refills the ring.
 //   Hand-offs use mbarriers (tile full / column full / column empty) and named
 //   barriers inside each warp group, so the two roles overlap instead of meeting
 //   at CTA-wide barriers.
@@ -32,11 +34,13 @@
 
 namespace tbgb {
 
-constexpr int NT = kDenseThreads;   // 544: 8 scatter + 8 owner + 1 producer warp
+constexpr int NT = kDenseThreads;   // 800: 8 scatter + 2 x 8 owner + 1 producer warp
 constexpr int NSC = 256;            // scatter threads (warps 0-7)
-constexpr int NOW = 256;            // owner threads (warps 8-15)
+constexpr int NOW = 256;            // owner threads per team (team 0: warps 8-15, team 1: 16-23)
+constexpr int TEAMS = 2;            // team t sweeps the column buffer of batches k with k % 2 == t
 constexpr int SCATTER_WARPS = NSC / 32;
-constexpr int PRODUCER_WARP = (NSC + NOW) / 32;  // warp 16
+constexpr int PRODUCER_WARP = (NSC + TEAMS * NOW) / 32;  // warp 24
+// 25 warps put up to 7 warps on one SM sub-partition: 72 registers per thread.
 constexpr int TILE = kDenseTile;    // rows per staged tile
 constexpr int STAGES = kDenseStages;
 constexpr int RPS = TILE / NSC;     // rows per scatter thread per tile (8)
@@ -109,7 +113,7 @@ struct DenseArgs {
   long long n;
   long long row_offset;  // global index of row 0 (zero-tie ordering across shards)
   int G, C, opg, slots;
-  double* part;                // owner partials [ST_COUNT][gridDim.x * slots]
+  double* part;                // owner partials [ST_COUNT][gridDim.x * TEAMS * slots]
   unsigned long long* spill;   // [gridDim.x][SP_COUNT][G]
   unsigned long long* zfirst;  // [G], preset to ~0
   uint32_t* err;
@@ -133,13 +137,13 @@ DenseLaunch dense_plan(int G, int num_sms) {
   const int ms = (L.slots + NOW - 1) / NOW;
   L.maxslots = ms <= 1 ? 1 : (ms <= 2 ? 2 : 4);
   L.smem = dense_smem_bytes(G, C);
-  L.part_doubles = static_cast<size_t>(ST_COUNT) * L.grid * L.slots;
+  L.part_doubles = static_cast<size_t>(ST_COUNT) * L.grid * TEAMS * L.slots;
   L.spill_words = static_cast<size_t>(SP_COUNT) * L.grid * G;
   return L;
 }
 
 // Rare path: a finite row that found its column full.
-__device__ __noinline__ void spill_add(unsigned long long* sp, int G, int g, double v) {
+__device__ __forceinline__ void spill_add(unsigned long long* sp, int G, int g, double v) {
   const unsigned long long vb = static_cast<unsigned long long>(__double_as_longlong(v));
   const unsigned long long kb = atomicCAS(sp + SP_K * G + g, K_UNSET, vb);
   const double K = kb == K_UNSET ? v : __longlong_as_double(static_cast<long long>(kb));
@@ -279,6 +283,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], SCATTER_WARPS); }
     for (int s = 0; s < 2; ++s) { mbar_init(&colfull[s], SCATTER_WARPS); mbar_init(&colempty[s], NOW / 32); }
+    static_assert(TEAMS == 2, "one owner team per column buffer");
     *abort = 0;
     mbar_fence_init();
   }
@@ -331,10 +336,11 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
         }
       }
     }
-  } else if (tid < NSC) {
+  } else if (warp < SCATTER_WARPS) {
     // ------------------------------------------------------------ scatter warps
     // Each warp runs independently: it signals stage release and column
-    // completion with one mbarrier arrival per warp.
+    // completion with one mbarrier arrival per warp.  A thread's 8 rows of a tile
+    // are handled as two halves of 4 (register budget of a 25-warp CTA).
     const int t = tid;
     for (long long k = 0; k < nbatch; ++k) {
       const int bs = static_cast<int>(k & 1);
@@ -346,111 +352,117 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
       if (k >= 2) ok = wait_or_abort(&colempty[bs], static_cast<uint32_t>(((k >> 1) - 1) & 1), a.err, abort);
       const bool tail = k >= mytiles;
       const long long row0 = tail ? ntiles * TILE : (t_begin + k) * TILE;
-      int kk[RPS];
-      double vv[RPS];
-      uint32_t mb = 0;
       const int s = static_cast<int>(k % STAGES);
-      if (TMA && !tail) {
-        ok = ok && wait_or_abort(&full[s], static_cast<uint32_t>((k / STAGES) & 1), a.err, abort);
-        const unsigned char* st = smem + static_cast<size_t>(s) * STAGE_BYTES;
-#pragma unroll
-        for (int c = 0; c < RPS / 2; ++c) {
-          const int2 kp = reinterpret_cast<const int2*>(st)[c * NSC + t];
-          const double2 vp = reinterpret_cast<const double2*>(st + KEY_BYTES)[c * NSC + t];
-          kk[2 * c] = kp.x; kk[2 * c + 1] = kp.y;
-          vv[2 * c] = vp.x; vv[2 * c + 1] = vp.y;
-          if (MASKED) {
-            const int r = c * CHUNK + 2 * t;
-            const uint64_t w = reinterpret_cast<const uint64_t*>(st + KEY_BYTES + VAL_BYTES)[r >> 6];
-            mb |= static_cast<uint32_t>((w >> (r & 63)) & 3ull) << (2 * c);
-          } else {
-            mb |= 3u << (2 * c);
-          }
-        }
-      } else {
-#pragma unroll
-        for (int c = 0; c < RPS / 2; ++c) {
-#pragma unroll
-          for (int j = 0; j < 2; ++j) {
-            const long long r = row0 + c * CHUNK + 2 * t + j;
-            if (r < a.n) {
-              kk[2 * c + j] = a.keys[r];
-              vv[2 * c + j] = a.vals[r];
-              const bool m = MASKED ? ((a.mask[r >> 6] >> (r & 63)) & 1ull) != 0 : true;
-              mb |= (m ? 1u : 0u) << (2 * c + j);
-            } else {
-              kk[2 * c + j] = 0;
-              vv[2 * c + j] = 0.0;
-            }
-          }
-        }
-      }
+      const bool staged = TMA && !tail;
+      if (staged) ok = ok && wait_or_abort(&full[s], static_cast<uint32_t>((k / STAGES) & 1), a.err, abort);
       if (__any_sync(0xffffffffu, !ok)) {
         if (lane == 0) *abort = 1;
         break;
       }
-      // Fast path: every row of the warp is unmasked with an in-range key and a
-      // finite non-zero value (one predicated compare chain per row, one vote).
-      bool good = !MASKED || mb == 0xFFu;
+      const unsigned char* st = smem + static_cast<size_t>(s) * STAGE_BYTES;
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        constexpr int R = RPS / 2;
+        int kk[R];
+        double vv[R];
+        uint32_t mb = 0;
+        if (staged) {
 #pragma unroll
-      for (int i = 0; i < RPS; ++i)
-        good = good && static_cast<unsigned>(kk[i]) < static_cast<unsigned>(G) && fabs(vv[i]) > 0.0 &&
-               fabs(vv[i]) < pos_inf();
-      const bool all_good = __all_sync(0xffffffffu, good);
-      // the stage's rows are in registers: release it to the producer
-      __syncwarp();
-      if (TMA && !tail && lane == 0) mbar_arrive(&empty[s]);
-      uint32_t over = 0;
-      if (all_good) {
-        uint32_t rk[RPS];
-#pragma unroll
-        for (int i = 0; i < RPS; ++i) rk[i] = atomicAdd(&cnt[kk[i]], 1u);
-#pragma unroll
-        for (int i = 0; i < RPS; ++i) {
-          if (rk[i] < static_cast<uint32_t>(C)) col[static_cast<size_t>(rk[i]) * G + kk[i]] = vv[i];
-          else over |= 1u << i;
-        }
-      }
-      uint32_t rare = 0;
-      if (!all_good) {
-        // general path: finite rows with an in-range key take the column; rows with
-        // an out-of-range key, +-inf or a zero value also need the slow path below
-        uint32_t fin = 0;
-#pragma unroll
-        for (int i = 0; i < RPS; ++i) {
-          const double x = vv[i];
-          const bool m = (mb >> i) & 1u;
-          const bool inr = static_cast<unsigned>(kk[i]) < static_cast<unsigned>(G);
-          const bool f = is_finite(x);
-          fin |= static_cast<uint32_t>(m && inr && f) << i;
-          rare |= static_cast<uint32_t>(m && !is_nan(x) && (!inr || !f || x == 0.0)) << i;
-        }
-        uint32_t rk[RPS];
-#pragma unroll
-        for (int i = 0; i < RPS; ++i) rk[i] = ((fin >> i) & 1u) ? atomicAdd(&cnt[kk[i]], 1u) : NO_RANK;
-#pragma unroll
-        for (int i = 0; i < RPS; ++i) {
-          if (rk[i] < static_cast<uint32_t>(C)) col[static_cast<size_t>(rk[i]) * G + kk[i]] = vv[i];
-          else if (rk[i] != NO_RANK) over |= 1u << i;
-        }
-      }
-      if (rare | over) {
-        for (int i = 0; i < RPS; ++i) {
-          const int g = kk[i];
-          const double x = vv[i];
-          if ((over >> i) & 1u) {
-            const uint32_t slot = atomicAdd(&splc[k & 3], 1u);
-            if (slot < SPL) { splk[slot] = g; splv[slot] = x; }
-            else spill_add(sp, G, g, x);
+          for (int cc = 0; cc < R / 2; ++cc) {
+            const int c = 2 * h + cc;
+            const int2 kp = reinterpret_cast<const int2*>(st)[c * NSC + t];
+            const double2 vp = reinterpret_cast<const double2*>(st + KEY_BYTES)[c * NSC + t];
+            kk[2 * cc] = kp.x; kk[2 * cc + 1] = kp.y;
+            vv[2 * cc] = vp.x; vv[2 * cc + 1] = vp.y;
+            if (MASKED) {
+              const int r = c * CHUNK + 2 * t;
+              const uint64_t w = reinterpret_cast<const uint64_t*>(st + KEY_BYTES + VAL_BYTES)[r >> 6];
+              mb |= static_cast<uint32_t>((w >> (r & 63)) & 3ull) << (2 * cc);
+            } else {
+              mb |= 3u << (2 * cc);
+            }
           }
-          if (!((rare >> i) & 1u)) continue;
-          if (static_cast<unsigned>(g) >= static_cast<unsigned>(G)) {
-            atomicOr(a.err, KERR_KEY_RANGE);
-          } else if (x == 0.0) {
-            const long long r = row0 + (i >> 1) * CHUNK + 2 * t + (i & 1);
-            atomicMin(&a.zfirst[g], zero_code(a.row_offset + r, x));
-          } else {
-            atomicAdd(sp + (x > 0 ? SP_NINFP : SP_NINFN) * G + g, 1ull);
+        } else {
+#pragma unroll
+          for (int cc = 0; cc < R / 2; ++cc) {
+#pragma unroll
+            for (int j = 0; j < 2; ++j) {
+              const long long r = row0 + (2 * h + cc) * CHUNK + 2 * t + j;
+              if (r < a.n) {
+                kk[2 * cc + j] = a.keys[r];
+                vv[2 * cc + j] = a.vals[r];
+                const bool m = MASKED ? ((a.mask[r >> 6] >> (r & 63)) & 1ull) != 0 : true;
+                mb |= (m ? 1u : 0u) << (2 * cc + j);
+              } else {
+                kk[2 * cc + j] = 0;
+                vv[2 * cc + j] = 0.0;
+              }
+            }
+          }
+        }
+        // the stage's rows are in registers: release it to the producer
+        if (h == 1) {
+          __syncwarp();
+          if (staged && lane == 0) mbar_arrive(&empty[s]);
+        }
+        // Fast path: every row of the warp is unmasked with an in-range key and a
+        // finite non-zero value (one predicated compare chain per row, one vote).
+        bool good = !MASKED || mb == 0xFu;
+#pragma unroll
+        for (int i = 0; i < R; ++i)
+          good = good && static_cast<unsigned>(kk[i]) < static_cast<unsigned>(G) && fabs(vv[i]) > 0.0 &&
+                 fabs(vv[i]) < pos_inf();
+        const bool all_good = __all_sync(0xffffffffu, good);
+        uint32_t over = 0, rare = 0;
+        if (all_good) {
+          uint32_t rk[R];
+#pragma unroll
+          for (int i = 0; i < R; ++i) rk[i] = atomicAdd(&cnt[kk[i]], 1u);
+#pragma unroll
+          for (int i = 0; i < R; ++i) {
+            if (rk[i] < static_cast<uint32_t>(C)) col[static_cast<size_t>(rk[i]) * G + kk[i]] = vv[i];
+            else over |= 1u << i;
+          }
+        } else {
+          // general path: finite rows with an in-range key take the column; rows with
+          // an out-of-range key, +-inf or a zero value also need the slow path below
+          uint32_t fin = 0;
+#pragma unroll
+          for (int i = 0; i < R; ++i) {
+            const double x = vv[i];
+            const bool m = (mb >> i) & 1u;
+            const bool inr = static_cast<unsigned>(kk[i]) < static_cast<unsigned>(G);
+            const bool f = is_finite(x);
+            fin |= static_cast<uint32_t>(m && inr && f) << i;
+            rare |= static_cast<uint32_t>(m && !is_nan(x) && (!inr || !f || x == 0.0)) << i;
+          }
+          uint32_t rk[R];
+#pragma unroll
+          for (int i = 0; i < R; ++i) rk[i] = ((fin >> i) & 1u) ? atomicAdd(&cnt[kk[i]], 1u) : NO_RANK;
+#pragma unroll
+          for (int i = 0; i < R; ++i) {
+            if (rk[i] < static_cast<uint32_t>(C)) col[static_cast<size_t>(rk[i]) * G + kk[i]] = vv[i];
+            else if (rk[i] != NO_RANK) over |= 1u << i;
+          }
+        }
+        if (rare | over) {
+          for (int i = 0; i < R; ++i) {
+            const int g = kk[i];
+            const double x = vv[i];
+            if ((over >> i) & 1u) {
+              const uint32_t slot = atomicAdd(&splc[k & 3], 1u);
+              if (slot < SPL) { splk[slot] = g; splv[slot] = x; }
+              else spill_add(sp, G, g, x);
+            }
+            if (!((rare >> i) & 1u)) continue;
+            if (static_cast<unsigned>(g) >= static_cast<unsigned>(G)) {
+              atomicOr(a.err, KERR_KEY_RANGE);
+            } else if (x == 0.0) {
+              const long long r = row0 + (2 * h + (i >> 1)) * CHUNK + 2 * t + (i & 1);
+              atomicMin(&a.zfirst[g], zero_code(a.row_offset + r, x));
+            } else {
+              atomicAdd(sp + (x > 0 ? SP_NINFP : SP_NINFN) * G + g, 1ull);
+            }
           }
         }
       }
@@ -460,7 +472,8 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     }
   } else {
     // ------------------------------------------------------------ owner warps
-    const int o = tid - NSC;  // owner threads: warps 8-15
+    const int team = (tid - NSC) / NOW;
+    const int o = tid - NSC - team * NOW;  // owner index within the team
     constexpr int NCH = MAXSLOTS == 1 ? 4 : (MAXSLOTS == 2 ? 2 : 1);
     OwnerAcc<NCH> acc[MAXSLOTS];
     int og[MAXSLOTS], osub[MAXSLOTS];
@@ -475,8 +488,8 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     // reader and the owner warps run independently; otherwise the sub-owners of a
     // group meet at a named barrier before its count is reset.
     const bool shared_counts = a.opg > 1;
-    for (long long k = 0; k < nbatch; ++k) {
-      const int bs = static_cast<int>(k & 1);
+    for (long long k = team; k < nbatch; k += TEAMS) {
+      const int bs = team;
       const double* col = bs ? col1 : col0;
       uint32_t* cnt = bs ? cnt1 : cnt0;
       const double* splv = splv0 + bs * SPL;
@@ -492,7 +505,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
       const uint32_t ns = splc[k & 3];
       const int nspill = static_cast<int>(ns < SPL ? ns : SPL);
       if (shared_counts) {
-        if (bar_red_or(BAR_OWNER, NOW, !ok || *abort)) {
+        if (bar_red_or(BAR_OWNER + team, NOW, !ok || *abort)) {
           if (!ok) *abort = 1;
           break;
         }
@@ -519,11 +532,11 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
       if (lane == 0) mbar_arrive(&colempty[bs]);
     }
     // partial states of this CTA's owners
-    const long long stride = static_cast<long long>(P) * a.slots;
+    const long long stride = static_cast<long long>(P) * TEAMS * a.slots;
 #pragma unroll
     for (int q = 0; q < MAXSLOTS; ++q) {
       if (og[q] < 0) continue;
-      const long long idx = static_cast<long long>(b) * a.slots + (o + q * NOW);
+      const long long idx = (static_cast<long long>(b) * TEAMS + team) * a.slots + (o + q * NOW);
       const auto& A = acc[q];
       const double s1 = A.sum_s1(), s2 = A.sum_s2();
       double meanoff = 0.0, m2 = 0.0;
@@ -673,8 +686,8 @@ __device__ __forceinline__ void gstate_finalize(const GState& A, int g, const tb
 }
 
 // One warp per group: lane l folds partials l, l+32, ... (each CTA contributes
-// opg owner partials and one spill partial), then a fixed shuffle tree folds the
-// lanes.
+// TEAMS * opg owner partials and one spill partial), then a fixed shuffle tree
+// folds the lanes.
 __global__ void __launch_bounds__(256) dense_fold_kernel(const double* __restrict__ part,
                                                           const unsigned long long* __restrict__ spill, int P, int G,
                                                           int opg, const unsigned long long* __restrict__ zfirst,
@@ -683,15 +696,17 @@ __global__ void __launch_bounds__(256) dense_fold_kernel(const double* __restric
   const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (g >= G) return;
   const int slots = G * opg;
-  const long long stride = static_cast<long long>(P) * slots;
-  const int per = opg + 1;
+  const long long stride = static_cast<long long>(P) * TEAMS * slots;
+  const int per = TEAMS * opg + 1;
   const int nparts = P * per;
   GState A = gstate_empty();
   for (int i = lane; i < nparts; i += 32) {
     const int p = i / per, j = i - p * per;
     GState B;
-    if (j < opg) {
-      const long long idx = static_cast<long long>(p) * slots + static_cast<long long>(j) * G + g;
+    if (j < TEAMS * opg) {
+      // partial of team j / opg, sub-owner j % opg
+      const long long idx = static_cast<long long>(p) * TEAMS * slots + static_cast<long long>(j / opg) * slots +
+                            static_cast<long long>(j % opg) * G + g;
       B.nn = part[ST_NN * stride + idx];
       B.nf = part[ST_NF * stride + idx];
       B.K = part[ST_K * stride + idx];

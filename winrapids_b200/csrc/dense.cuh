@@ -8,7 +8,7 @@
 
 namespace tbgb {
 
-constexpr int kDenseThreads = 544;  // threads per CTA (17 warps)
+constexpr int kDenseThreads = 800;  // threads per CTA (25 warps)
 constexpr int kDenseTile = 2048;    // rows per staged tile
 constexpr int kDenseStages = 4;     // depth of the TMA ring
 constexpr int kDenseMaxGroups = 1024;
