@@ -360,7 +360,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
         break;
       }
       const unsigned char* st = smem + static_cast<size_t>(s) * STAGE_BYTES;
-#pragma unroll 1
+#pragma unroll
       for (int h = 0; h < 2; ++h) {
         constexpr int R = RPS / 2;
         int kk[R];
