@@ -106,6 +106,22 @@ tbgb_status tbgb_groupby_dense_state(tbgb_ctx* ctx, const int32_t* d_keys, const
 tbgb_status tbgb_merge_states(tbgb_ctx* ctx, const void* d_states, int32_t n_states, int32_t n_groups,
                               const tbgb_moments* out, void* stream);
 
+/* Dense-key groupby that allocates no device memory and needs no context: for
+ * callers that must not have the library allocate at call time (for example a host
+ * engine that has already reserved nearly all device memory for its own buffers,
+ * or a latency-critical loop that cannot accept cudaMalloc's implicit device
+ * synchronisation).  No counterpart in the reference.
+ * Same semantics and outputs as tbgb_groupby_dense, on the current device.
+ * Limits: 1 <= n_groups <= 256 (TBGB_ERR_INVALID_ARGUMENT otherwise).  Scratch is
+ * a fixed device array of about 8.5 MB inside this library, held by every GPU that
+ * loads the library until the process exits.  The first call on a device looks up
+ * that array's address (make it before any stream capture).  All calls share the
+ * array: calls that overlap on the GPU (other streams, other threads) race and
+ * must be serialised by the caller.  The call waits for `stream` and returns any
+ * device-side error (e.g. TBGB_ERR_KEY_OUT_OF_RANGE). */
+tbgb_status tbgb_groupby_dense_noalloc(const int32_t* d_keys, const double* d_vals, const uint64_t* d_mask,
+                                       int64_t n, int32_t n_groups, const tbgb_moments* out, void* stream);
+
 /* Bytes of device workspace the context holds after a call of this size. */
 size_t tbgb_workspace_bytes(const tbgb_ctx* ctx, int64_t n, int32_t n_groups);
 

@@ -76,6 +76,7 @@ def lib() -> C.CDLL:
         "tbgb_device_name": (C.c_char_p, [vp]),
         "tbgb_groupby_dense": (st, [vp, vp, vp, vp, i64, i32, C.POINTER(Moments), vp]),
         "tbgb_sync": (st, [vp, vp]),
+        "tbgb_groupby_dense_noalloc": (st, [vp, vp, vp, i64, i32, C.POINTER(Moments), vp]),
         "tbgb_state_bytes": (sz, [i32]),
         "tbgb_groupby_dense_state": (st, [vp, vp, vp, vp, i64, i32, i64, vp, vp]),
         "tbgb_merge_states": (st, [vp, vp, i32, i32, C.POINTER(Moments), vp]),
@@ -99,6 +100,7 @@ def lib() -> C.CDLL:
 # Every symbol include/tambear_gb.h declares (checked by the CPU test suite).
 HEADER_SYMBOLS = (
     "tbgb_create", "tbgb_destroy", "tbgb_last_error", "tbgb_device_name", "tbgb_groupby_dense", "tbgb_sync",
+    "tbgb_groupby_dense_noalloc",
     "tbgb_state_bytes", "tbgb_groupby_dense_state", "tbgb_merge_states", "tbgb_workspace_bytes",
     "tbgb_launch_count", "tbgb_profile_enable", "tbgb_kernel_time_ms", "tbgb_gen_keys_uniform", "tbgb_gen_values_uniform", "tbgb_gen_values_normal",
     "tbgb_gen_inject_nonfinite",
