@@ -83,7 +83,7 @@ def traffic_per_row():
         return None, None
     try:
         d = json.loads(p.read_text())["dense_moments_kernel"]
-        return float(d["dram_bytes_per_row"]), d.get("source")
+        return (float(d["dram_bytes_per_row"]), float(d.get("fixed_bytes_per_launch", 0.0))), d.get("source")
     except Exception:
         return None, None
 
@@ -378,7 +378,7 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
                            "fallback 6.65 TB/s",
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": (tpr * n_local) if tpr else None,
+            "traffic": (tpr[0] * n_local + tpr[1]) if tpr else None,
             "traffic_source": tsrc,
             "kernel": "dense_moments_kernel",
             "algorithmic_bytes_per_launch": n_local * BYTES_PER_ROW,
