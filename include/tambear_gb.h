@@ -17,6 +17,18 @@
  *   tbgb_groupby_dense_state /      MomentStats::merge / SufficientStatistics::merge
  *   tbgb_merge_states               (descriptive.rs:216-253, intermediates.rs:352-377) used
  *                                   across row shards (one partial table per GPU)
+ *   tbgb_columns (filter + expr)    FilterJit::filter_mask (crates/tambear/src/filter_jit.rs:71-121,
+ *                                   kernel :196-252) and ComputeEngine::map_phi2
+ *                                   (crates/tambear/src/compute_engine.rs:198-210, CPU :627-636),
+ *                                   fused into the groupby pass as ScatterJit::scatter_multi_phi_masked
+ *                                   fuses mask + scatter (crates/tambear/src/scatter_jit.rs:402-495)
+ *   tbgb_groupby_dense_columns      the same composition over dense int32 keys, any n_groups
+ *   tbgb_groupby_hash               GroupIndex::build (crates/tambear/src/group_index.rs:117-204) +
+ *                                   moments_grouped for int64 keys: the reference factorises keys on
+ *                                   the host and accepts i32 codes only; here an open-addressing table
+ *                                   in HBM groups arbitrary int64 keys in the same pass
+ *   tbgb_hash_partition             no counterpart in the reference (single GPU); routes rows to
+ *                                   the GPU that owns their key for the sharded high-cardinality path
  *
  * Threading: one context per device; calls on one context are serialised by the
  * caller (the context's workspace is reused by every call); different contexts
@@ -84,10 +96,70 @@ typedef struct {
  * (bit i of mask[i/64] set <=> row i participates, filter_jit.rs:202-243 layout;
  * NULL = all rows).  Enqueued on `stream` (a cudaStream_t, NULL = legacy default
  * stream); returns after the launch.  Deferred device errors (key out of range,
- * timeouts) are reported by tbgb_sync.  Requires 1 <= n_groups <= 1024 in this
- * version (TBGB_ERR_INVALID_ARGUMENT otherwise). */
+ * timeouts) are reported by tbgb_sync.  1 <= n_groups <= 2^31 - 1: up to 1024
+ * groups run the shared-memory column kernel, more groups the global-table kernel. */
 tbgb_status tbgb_groupby_dense(tbgb_ctx* ctx, const int32_t* d_keys, const double* d_vals, const uint64_t* d_mask,
                                int64_t n, int32_t n_groups, const tbgb_moments* out, void* stream);
+
+/* ---- value columns with a fused filter and expression ------------------------------
+ * The value aggregated for row i is v = expr(a[i], b[i], c[i]) computed in f64 with
+ * every operation rounded separately (no fused multiply-add), exactly as the
+ * reference's map_phi2 composes `a*b` and then `+ c`.  f32 columns are widened to
+ * f64 exactly before any arithmetic.  Row i takes part iff its mask bit is set (or
+ * mask is NULL) and pred(a[i], threshold) holds; every comparison with a NaN `a`
+ * fails, as in the reference's filter kernels.  Rows whose v is NaN are skipped by
+ * every aggregate but, in the hash entry point, still create their key's group. */
+typedef enum { TBGB_F64 = 0, TBGB_F32 = 1 } tbgb_dtype;
+typedef enum {
+  TBGB_PRED_NONE = 0,    /* every row                 */
+  TBGB_PRED_GT = 1,      /* a >  threshold            */
+  TBGB_PRED_GE = 2,      /* a >= threshold            */
+  TBGB_PRED_LT = 3,      /* a <  threshold            */
+  TBGB_PRED_LE = 4,      /* a <= threshold            */
+  TBGB_PRED_NOT_NAN = 5, /* a is not NaN              */
+  TBGB_PRED_FINITE = 6   /* a is finite               */
+} tbgb_pred;
+typedef enum {
+  TBGB_EXPR_A = 0,         /* v = a                   */
+  TBGB_EXPR_ADD = 1,       /* v = a + b               */
+  TBGB_EXPR_SUB = 2,       /* v = a - b               */
+  TBGB_EXPR_MUL = 3,       /* v = a * b               */
+  TBGB_EXPR_MUL_PLUS1 = 4, /* v = (a * b) + 1.0       */
+  TBGB_EXPR_MUL_ADD = 5    /* v = (a * b) + c         */
+} tbgb_expr;
+typedef struct {
+  const void* a;       /* device column a (n elements of dtype)                 */
+  const void* b;       /* device column b, read by ADD / SUB / MUL / MUL_PLUS1 / MUL_ADD */
+  const void* c;       /* device column c, read by MUL_ADD                       */
+  int32_t dtype;       /* tbgb_dtype of a, b and c                               */
+  int32_t expr;        /* tbgb_expr                                              */
+  int32_t pred;        /* tbgb_pred, applied to column a                         */
+  int32_t reserved;    /* 0                                                      */
+  double threshold;
+} tbgb_columns;
+
+/* Dense-key groupby of expr(a, b, c) over the rows that pass mask and pred. */
+tbgb_status tbgb_groupby_dense_columns(tbgb_ctx* ctx, const int32_t* d_keys, const tbgb_columns* cols,
+                                       const uint64_t* d_mask, int64_t n, int32_t n_groups,
+                                       const tbgb_moments* out, void* stream);
+
+/* int64-key groupby through an open-addressing table in device memory (any key
+ * value, INT64_MIN included).  Groups are the distinct keys among the rows that
+ * pass mask and pred.  Group j's key is written to d_out_keys[j] and its outputs to
+ * element j of each non-NULL pointer of `out`, j < number of groups, in an order that
+ * is not specified (sort by key for a canonical order); the number of groups is
+ * written to *d_n_groups (device memory).  At most max_groups groups fit; more
+ * distinct keys make tbgb_sync report TBGB_ERR_TABLE_FULL (the outputs are then
+ * incomplete).  When out->min, max, m2, var_pop and var_samp are all NULL the table
+ * keeps only count and sum (a 32-byte slot instead of 96). */
+tbgb_status tbgb_groupby_hash(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb_columns* cols,
+                              const uint64_t* d_mask, int64_t n, int64_t max_groups, int64_t* d_out_keys,
+                              const tbgb_moments* out, int64_t* d_n_groups, void* stream);
+
+/* How the global-table kernel treats rows: 0 = choose by size (default), 1 = always
+ * pre-aggregate in a per-CTA shared-memory table (skewed keys), 2 = always update the
+ * global table directly (uniform high-cardinality keys). */
+tbgb_status tbgb_set_table_mode(tbgb_ctx* ctx, int mode);
 
 /* Waits for `stream` and returns the first deferred device error of the calls
  * enqueued since the previous tbgb_sync (then clears it). */
@@ -152,6 +224,18 @@ tbgb_status tbgb_gen_values_normal(tbgb_ctx* ctx, double* d_vals, int64_t n, dou
  * (nan_frac <= u < nan_frac + inf_frac, sign from the low bit), u from column 2. */
 tbgb_status tbgb_gen_inject_nonfinite(tbgb_ctx* ctx, double* d_vals, int64_t n, double nan_frac, double inf_frac,
                                       uint64_t seed, int64_t first_row, void* stream);
+
+/* int64 keys through an inverse CDF: u = u01 of column 0, rank = first r with
+ * d_cdf[r] >= u (d_cdf: n_ids increasing doubles, the last one 1.0), key =
+ * mix64(rank ^ salt).  With a Zipf table this is the fused-pipeline key column. */
+tbgb_status tbgb_gen_keys_cdf(tbgb_ctx* ctx, int64_t* d_keys, int64_t n, const double* d_cdf, int64_t n_ids,
+                              uint64_t salt, uint64_t seed, int64_t first_row, void* stream);
+/* int64 keys uniform over n_ids random ids: key = mix64((x % n_ids) ^ salt), x from column 0. */
+tbgb_status tbgb_gen_keys_ids(tbgb_ctx* ctx, int64_t* d_keys, int64_t n, int64_t n_ids, uint64_t salt, uint64_t seed,
+                              int64_t first_row, void* stream);
+/* f32 LogNormal(mu, sigma): (float)exp(mu + sigma * z), z the normal stream of column 1. */
+tbgb_status tbgb_gen_values_lognormal_f32(tbgb_ctx* ctx, float* d_vals, int64_t n, double mu, double sigma,
+                                          uint64_t seed, int64_t first_row, void* stream);
 
 #ifdef __cplusplus
 }

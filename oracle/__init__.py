@@ -273,6 +273,30 @@ def gen_values_normal(n, mu, sigma, seed, start=0):
     return mu + sigma * z
 
 
+def zipf_cdf(n_ids, s):
+    """Inverse-CDF table of Zipf(s) over ranks 0..n_ids-1 (p(r) ~ (r+1)^-s); last entry exactly 1.0."""
+    w = np.arange(1, n_ids + 1, dtype=np.float64) ** (-float(s))
+    cdf = np.cumsum(w)
+    cdf /= cdf[-1]
+    cdf[-1] = 1.0
+    return cdf
+
+
+def gen_keys_cdf(n, cdf, salt, seed, start=0):
+    u = u01_np(splitmix_stream(column_seed(seed, 0), start, n))
+    rank = np.searchsorted(cdf, u, side="left").astype(np.uint64)
+    return mix64_np(rank ^ np.uint64(salt & M64)).view(np.int64)
+
+
+def gen_keys_ids(n, n_ids, salt, seed, start=0):
+    x = splitmix_stream(column_seed(seed, 0), start, n) % np.uint64(n_ids)
+    return mix64_np(x ^ np.uint64(salt & M64)).view(np.int64)
+
+
+def gen_values_lognormal_f32(n, mu, sigma, seed, start=0):
+    return np.exp(gen_values_normal(n, mu, sigma, seed, start)).astype(np.float32)
+
+
 def inject_nonfinite(vals, nan_frac, inf_frac, seed, start=0):
     x = splitmix_stream(column_seed(seed, 2), start, vals.size)
     u = u01_np(x)

@@ -16,12 +16,15 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._lib import (MOMENT_FIELDS, InvalidArgument, KeyOutOfRange, Moments, TambearGbError, error_for, lib)
+from ._lib import (DTYPES, EXPRS, MOMENT_FIELDS, PREDS, Columns, InvalidArgument, KeyOutOfRange, Moments,
+                   TableFull, TambearGbError, error_for, lib)
 
 __all__ = [
     "Context", "DescriptiveEngine", "GroupedMomentStats", "MomentStats", "TambearGbError", "KeyOutOfRange",
-    "InvalidArgument", "MOMENT_FIELDS",
+    "InvalidArgument", "TableFull", "MOMENT_FIELDS", "SUMCOUNT_FIELDS",
 ]
+
+SUMCOUNT_FIELDS = ("count", "sum", "mean")
 
 
 def _torch():
@@ -110,6 +113,68 @@ class Context:
     def sync(self, stream=None):
         self._check(self._L.tbgb_sync(self._h, _stream_handle(stream)))
 
+    def set_table_mode(self, mode: str | int):
+        """'auto' (0), 'local' (1: per-CTA shared-memory pre-aggregation) or 'direct' (2)."""
+        m = {"auto": 0, "local": 1, "direct": 2}.get(mode, mode)
+        self._check(self._L.tbgb_set_table_mode(self._h, int(m)))
+
+    @staticmethod
+    def columns(a, b=None, c=None, expr: str = "a", pred: str | None = None, threshold: float = 0.0) -> Columns:
+        torch = _torch()
+        if a.dtype == torch.float64:
+            dt = DTYPES["f64"]
+        elif a.dtype == torch.float32:
+            dt = DTYPES["f32"]
+        else:
+            raise InvalidArgument(7, f"unsupported value dtype {a.dtype}")
+        for t in (b, c):
+            if t is not None and t.dtype != a.dtype:
+                raise InvalidArgument(7, "columns a, b, c must share one dtype")
+        cols = Columns()
+        cols.a, cols.b, cols.c = _ptr(a), _ptr(b), _ptr(c)
+        cols.dtype, cols.expr, cols.pred, cols.reserved = dt, EXPRS[expr], PREDS[pred], 0
+        cols.threshold = float(threshold)
+        return cols
+
+    def groupby_dense_columns(self, keys, a, n_groups: int, b=None, c=None, expr: str = "a",
+                              pred: str | None = None, threshold: float = 0.0, mask=None,
+                              out: dict | None = None, stream=None, sync: bool = True) -> dict:
+        """Dense-key groupby of expr(a, b, c) over rows passing mask and pred(a, threshold)."""
+        n = int(keys.numel())
+        if int(a.numel()) != n:
+            raise InvalidArgument(7, "keys and columns must have same length")
+        if out is None:
+            out = self.alloc_moments(n_groups)
+        cols = self.columns(a, b, c, expr, pred, threshold)
+        m = self.moments_struct(out)
+        self._check(self._L.tbgb_groupby_dense_columns(self._h, _ptr(keys), C.byref(cols), _ptr(mask), n,
+                                                       int(n_groups), C.byref(m), _stream_handle(stream)))
+        if sync:
+            self.sync(stream)
+        return out
+
+    def groupby_hash(self, keys, a, max_groups: int, b=None, c=None, expr: str = "a", pred: str | None = None,
+                     threshold: float = 0.0, mask=None, fields=MOMENT_FIELDS, stream=None):
+        """int64-key groupby; returns (group keys, {field: tensor}) trimmed to the group count
+        (group order unspecified).  fields=SUMCOUNT_FIELDS keeps only count/sum/mean."""
+        torch = _torch()
+        n = int(keys.numel())
+        if keys.dtype != torch.int64:
+            raise InvalidArgument(7, "hash keys must be int64")
+        if int(a.numel()) != n:
+            raise InvalidArgument(7, "keys and columns must have same length")
+        dev = f"cuda:{self.device}"
+        out = self.alloc_moments(int(max_groups), fields)
+        out_keys = torch.empty(int(max_groups), dtype=torch.int64, device=dev)
+        ng = torch.zeros(1, dtype=torch.int64, device=dev)
+        cols = self.columns(a, b, c, expr, pred, threshold)
+        m = self.moments_struct(out)
+        self._check(self._L.tbgb_groupby_hash(self._h, _ptr(keys), C.byref(cols), _ptr(mask), n, int(max_groups),
+                                              _ptr(out_keys), C.byref(m), _ptr(ng), _stream_handle(stream)))
+        self.sync(stream)
+        g = int(ng.item())
+        return out_keys[:g], {k: v[:g] for k, v in out.items()}
+
     def state_bytes(self, n_groups: int) -> int:
         return int(self._L.tbgb_state_bytes(int(n_groups)))
 
@@ -156,6 +221,21 @@ class Context:
         self._check(self._L.tbgb_gen_values_normal(self._h, _ptr(vals), int(vals.numel()), float(mu),
                                                    float(sigma), int(seed) & (2**64 - 1), int(first_row),
                                                    _stream_handle(stream)))
+
+    def gen_keys_cdf(self, keys, cdf, salt: int, seed: int, first_row: int = 0, stream=None):
+        self._check(self._L.tbgb_gen_keys_cdf(self._h, _ptr(keys), int(keys.numel()), _ptr(cdf), int(cdf.numel()),
+                                              int(salt) & (2**64 - 1), int(seed) & (2**64 - 1), int(first_row),
+                                              _stream_handle(stream)))
+
+    def gen_keys_ids(self, keys, n_ids: int, salt: int, seed: int, first_row: int = 0, stream=None):
+        self._check(self._L.tbgb_gen_keys_ids(self._h, _ptr(keys), int(keys.numel()), int(n_ids),
+                                              int(salt) & (2**64 - 1), int(seed) & (2**64 - 1), int(first_row),
+                                              _stream_handle(stream)))
+
+    def gen_values_lognormal_f32(self, vals, mu: float, sigma: float, seed: int, first_row: int = 0, stream=None):
+        self._check(self._L.tbgb_gen_values_lognormal_f32(self._h, _ptr(vals), int(vals.numel()), float(mu),
+                                                          float(sigma), int(seed) & (2**64 - 1), int(first_row),
+                                                          _stream_handle(stream)))
 
     def gen_inject_nonfinite(self, vals, nan_frac: float, inf_frac: float, seed: int, first_row: int = 0,
                              stream=None):

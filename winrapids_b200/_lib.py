@@ -47,7 +47,25 @@ def error_for(status: int, message: str) -> TambearGbError:
         return KeyOutOfRange(status, message)
     if status == 7:
         return InvalidArgument(status, message)
+    if status == 9:
+        return TableFull(status, message)
     return TambearGbError(status, message)
+
+
+class TableFull(TambearGbError):
+    pass
+
+
+class Columns(C.Structure):
+    """tbgb_columns: value columns a, b, c with the fused expression and filter."""
+
+    _fields_ = [("a", C.c_void_p), ("b", C.c_void_p), ("c", C.c_void_p), ("dtype", C.c_int32),
+                ("expr", C.c_int32), ("pred", C.c_int32), ("reserved", C.c_int32), ("threshold", C.c_double)]
+
+
+DTYPES = {"f64": 0, "f32": 1}
+PREDS = {None: 0, "none": 0, ">": 1, ">=": 2, "<": 3, "<=": 4, "not_nan": 5, "finite": 6}
+EXPRS = {"a": 0, "a+b": 1, "a-b": 2, "a*b": 3, "a*b+1": 4, "a*b+c": 5}
 
 
 class Moments(C.Structure):
@@ -84,10 +102,16 @@ def lib() -> C.CDLL:
         "tbgb_launch_count": (u64, [vp]),
         "tbgb_profile_enable": (st, [vp, C.c_int]),
         "tbgb_kernel_time_ms": (st, [vp, C.POINTER(f64), C.POINTER(i64)]),
+        "tbgb_groupby_dense_columns": (st, [vp, vp, C.POINTER(Columns), vp, i64, i32, C.POINTER(Moments), vp]),
+        "tbgb_groupby_hash": (st, [vp, vp, C.POINTER(Columns), vp, i64, i64, vp, C.POINTER(Moments), vp, vp]),
+        "tbgb_set_table_mode": (st, [vp, C.c_int]),
         "tbgb_gen_keys_uniform": (st, [vp, vp, i64, i32, u64, i64, vp]),
         "tbgb_gen_values_uniform": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
         "tbgb_gen_values_normal": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
         "tbgb_gen_inject_nonfinite": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
+        "tbgb_gen_keys_cdf": (st, [vp, vp, i64, vp, i64, u64, u64, i64, vp]),
+        "tbgb_gen_keys_ids": (st, [vp, vp, i64, i64, u64, u64, i64, vp]),
+        "tbgb_gen_values_lognormal_f32": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
     }
     for name, (res, args) in sig.items():
         fn = getattr(L, name)
@@ -103,5 +127,6 @@ HEADER_SYMBOLS = (
     "tbgb_groupby_dense_noalloc",
     "tbgb_state_bytes", "tbgb_groupby_dense_state", "tbgb_merge_states", "tbgb_workspace_bytes",
     "tbgb_launch_count", "tbgb_profile_enable", "tbgb_kernel_time_ms", "tbgb_gen_keys_uniform", "tbgb_gen_values_uniform", "tbgb_gen_values_normal",
-    "tbgb_gen_inject_nonfinite",
+    "tbgb_gen_inject_nonfinite", "tbgb_groupby_dense_columns", "tbgb_groupby_hash", "tbgb_set_table_mode",
+    "tbgb_gen_keys_cdf", "tbgb_gen_keys_ids", "tbgb_gen_values_lognormal_f32",
 )

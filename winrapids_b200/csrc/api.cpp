@@ -10,6 +10,7 @@
 #include "dense.cuh"
 #include "errbits.hpp"
 #include "gen.cuh"
+#include "table.cuh"
 #include "tambear_gb.h"
 
 struct tbgb_ctx {
@@ -21,6 +22,7 @@ struct tbgb_ctx {
   size_t ws_bytes = 0;
   uint32_t* err = nullptr;  // deferred kernel error bits (persist until tbgb_sync)
   uint64_t launches = 0;
+  int table_mode = 0;    // tbgb_set_table_mode
   bool profile = false;  // record events around main kernels
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;
 };
@@ -88,8 +90,18 @@ tbgb_status check_dense_args(tbgb_ctx* ctx, const int32_t* keys, const double* v
   if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
   if (n < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n must be >= 0");
   if (G < 1 || G > tbgb::kDenseMaxGroups)
-    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_groups must be in [1, 1024] for the dense kernel");
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_groups must be in [1, 1024] for the column kernel");
   if (n > 0 && (!keys || !vals)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "keys/values pointer is NULL");
+  return TBGB_OK;
+}
+
+tbgb_status profile_events(tbgb_ctx* ctx, cudaEvent_t* e0, cudaEvent_t* e1) {
+  *e0 = nullptr;
+  *e1 = nullptr;
+  if (!ctx->profile) return TBGB_OK;
+  if (cudaEventCreate(e0) != cudaSuccess || cudaEventCreate(e1) != cudaSuccess)
+    return fail(ctx, TBGB_ERR_BACKEND, "cudaEventCreate failed");
+  ctx->events.emplace_back(*e0, *e1);
   return TBGB_OK;
 }
 
@@ -107,16 +119,86 @@ tbgb_status dense_common(tbgb_ctx* ctx, const int32_t* keys, const double* vals,
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemsetAsync(w.zfirst, 0xFF, static_cast<size_t>(G) * 8, s);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "memset", e);
-  cudaEvent_t e0 = nullptr, e1 = nullptr;
-  if (ctx->profile) {
-    if (cudaEventCreate(&e0) != cudaSuccess || cudaEventCreate(&e1) != cudaSuccess)
-      return fail(ctx, TBGB_ERR_BACKEND, "cudaEventCreate failed");
-    ctx->events.emplace_back(e0, e1);
-  }
+  cudaEvent_t e0, e1;
+  st = profile_events(ctx, &e0, &e1);
+  if (st != TBGB_OK) return st;
   e = tbgb::dense_moments_launch(L, keys, vals, mask, n, row_offset, G, w.part, w.spill, w.zfirst, ctx->err, out,
                                  state_out, s, &ctx->launches, e0, e1);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "dense groupby launch", e);
   return TBGB_OK;
+}
+
+bool wants_full(const tbgb_moments* out) {
+  return !out || out->min || out->max || out->m2 || out->var_pop || out->var_samp;
+}
+
+tbgb_status check_columns(tbgb_ctx* ctx, const tbgb_columns* c, int64_t n) {
+  if (!c) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "columns descriptor is NULL");
+  if (c->dtype != TBGB_F64 && c->dtype != TBGB_F32) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "unknown dtype");
+  if (c->expr < TBGB_EXPR_A || c->expr > TBGB_EXPR_MUL_ADD)
+    return fail(ctx, TBGB_ERR_ENTRY_NOT_FOUND, "unknown expression id");
+  if (c->pred < TBGB_PRED_NONE || c->pred > TBGB_PRED_FINITE)
+    return fail(ctx, TBGB_ERR_ENTRY_NOT_FOUND, "unknown predicate id");
+  if (n > 0) {
+    if (!c->a) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "column a is NULL");
+    if (c->expr != TBGB_EXPR_A && !c->b) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "column b is NULL");
+    if (c->expr == TBGB_EXPR_MUL_ADD && !c->c) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "column c is NULL");
+  }
+  return TBGB_OK;
+}
+
+// Global-table groupby: dense keys (hash == false, `groups` = n_groups) or int64
+// keys (`groups` = max_groups).
+tbgb_status table_common(tbgb_ctx* ctx, bool hash, const void* keys, const tbgb_columns* cols, const uint64_t* mask,
+                         int64_t n, long long groups, int64_t row_offset, int64_t* out_keys,
+                         const tbgb_moments* out, double* state_out, int64_t* d_n_groups, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (n < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (groups < 1) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "the group count must be >= 1");
+  if (n > 0 && !keys) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "keys pointer is NULL");
+  tbgb_status st = check_columns(ctx, cols, n);
+  if (st != TBGB_OK) return st;
+  if (n / (ctx->num_sms > 0 ? ctx->num_sms : 1) >= (1ll << 31))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "too many rows for one call (split the rows)");
+  const bool full = state_out != nullptr || wants_full(out);
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  const tbgb::TablePlan P = tbgb::table_plan(hash, full, ctx->table_mode, groups, ctx->num_sms);
+  st = ensure_ws(ctx, P.table_bytes);
+  if (st != TBGB_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  unsigned long long* T = static_cast<unsigned long long*>(ctx->ws);
+  cudaError_t e = tbgb::table_init(P, T, s, &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "table init", e);
+  tbgb::TableArgs a{};
+  a.keys = keys;
+  a.cols = *cols;
+  a.mask = mask;
+  a.n = n;
+  a.row_offset = row_offset;
+  a.table = T;
+  a.slots = P.slots;
+  a.ngroups = T + (P.slots + (hash ? 1 : 0)) * tbgb::table_slot_words(full);
+  a.max_groups = groups;
+  a.err = ctx->err;
+  cudaEvent_t e0, e1;
+  st = profile_events(ctx, &e0, &e1);
+  if (st != TBGB_OK) return st;
+  e = tbgb::table_accumulate(P, a, s, &ctx->launches, e0, e1);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "table groupby launch", e);
+  if (hash) e = tbgb::table_finalize_hash(P, T, groups, out_keys, out, d_n_groups, ctx->err, s, &ctx->launches);
+  else e = tbgb::table_finalize_dense(P, T, groups, out, state_out, s, &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "table finalize launch", e);
+  return TBGB_OK;
+}
+
+tbgb_columns plain_f64(const double* vals) {
+  tbgb_columns c{};
+  c.a = vals;
+  c.dtype = TBGB_F64;
+  c.expr = TBGB_EXPR_A;
+  c.pred = TBGB_PRED_NONE;
+  return c;
 }
 
 }  // namespace
@@ -196,15 +278,55 @@ tbgb_status tbgb_kernel_time_ms(tbgb_ctx* ctx, double* total_ms, int64_t* launch
 
 size_t tbgb_workspace_bytes(const tbgb_ctx* ctx, int64_t n, int32_t n_groups) {
   (void)n;
-  if (!ctx || n_groups < 1 || n_groups > tbgb::kDenseMaxGroups) return 0;
+  if (!ctx || n_groups < 1) return 0;
+  if (n_groups > tbgb::kDenseMaxGroups)
+    return tbgb::table_plan(false, true, ctx->table_mode, n_groups, ctx->num_sms).table_bytes;
   const tbgb::DenseLaunch L = tbgb::dense_plan(n_groups, ctx->num_sms);
   return dense_ws_layout(nullptr, L, n_groups).bytes;
+}
+
+tbgb_status tbgb_set_table_mode(tbgb_ctx* ctx, int mode) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (mode < 0 || mode > 2) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "table mode must be 0, 1 or 2");
+  ctx->table_mode = mode;
+  return TBGB_OK;
 }
 
 tbgb_status tbgb_groupby_dense(tbgb_ctx* ctx, const int32_t* d_keys, const double* d_vals, const uint64_t* d_mask,
                                int64_t n, int32_t n_groups, const tbgb_moments* out, void* stream) {
   if (!out) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "out is NULL");
+  if (n_groups > tbgb::kDenseMaxGroups) {
+    if (n > 0 && !d_vals) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "values pointer is NULL");
+    const tbgb_columns c = plain_f64(d_vals);
+    return table_common(ctx, false, d_keys, &c, d_mask, n, n_groups, 0, nullptr, out, nullptr, nullptr, stream);
+  }
   return dense_common(ctx, d_keys, d_vals, d_mask, n, n_groups, 0, out, nullptr, stream);
+}
+
+tbgb_status tbgb_groupby_dense_columns(tbgb_ctx* ctx, const int32_t* d_keys, const tbgb_columns* cols,
+                                       const uint64_t* d_mask, int64_t n, int32_t n_groups,
+                                       const tbgb_moments* out, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (!out) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "out is NULL");
+  tbgb_status st = check_columns(ctx, cols, n);
+  if (st != TBGB_OK) return st;
+  const bool plain = cols->dtype == TBGB_F64 && cols->expr == TBGB_EXPR_A && cols->pred == TBGB_PRED_NONE;
+  if (plain && n_groups >= 1 && n_groups <= tbgb::kDenseMaxGroups)
+    return dense_common(ctx, d_keys, static_cast<const double*>(cols->a), d_mask, n, n_groups, 0, out, nullptr,
+                        stream);
+  return table_common(ctx, false, d_keys, cols, d_mask, n, n_groups, 0, nullptr, out, nullptr, nullptr, stream);
+}
+
+tbgb_status tbgb_groupby_hash(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb_columns* cols,
+                              const uint64_t* d_mask, int64_t n, int64_t max_groups, int64_t* d_out_keys,
+                              const tbgb_moments* out, int64_t* d_n_groups, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (!out || !d_out_keys || !d_n_groups)
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "out, out_keys and n_groups must not be NULL");
+  if (max_groups < 1 || max_groups > (1ll << 40))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "max_groups must be in [1, 2^40]");
+  return table_common(ctx, true, d_keys, cols, d_mask, n, max_groups, 0, d_out_keys, out, nullptr, d_n_groups,
+                      stream);
 }
 
 size_t tbgb_state_bytes(int32_t n_groups) {
@@ -216,6 +338,12 @@ tbgb_status tbgb_groupby_dense_state(tbgb_ctx* ctx, const int32_t* d_keys, const
                                      void* d_state, void* stream) {
   if (!d_state) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "state buffer is NULL");
   if (row_offset < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "row_offset must be >= 0");
+  if (n_groups > tbgb::kDenseMaxGroups) {
+    if (n > 0 && !d_vals) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "values pointer is NULL");
+    const tbgb_columns c = plain_f64(d_vals);
+    return table_common(ctx, false, d_keys, &c, d_mask, n, n_groups, row_offset, nullptr, nullptr,
+                        static_cast<double*>(d_state), nullptr, stream);
+  }
   return dense_common(ctx, d_keys, d_vals, d_mask, n, n_groups, row_offset, nullptr, static_cast<double*>(d_state),
                       stream);
 }
@@ -279,6 +407,24 @@ tbgb_status tbgb_gen_inject_nonfinite(tbgb_ctx* ctx, double* d_vals, int64_t n, 
                                       uint64_t seed, int64_t first_row, void* stream) {
   GEN_ENTRY(tbgb::gen_inject_nonfinite(d_vals, n, nan_frac, inf_frac, seed, first_row,
                                        static_cast<cudaStream_t>(stream)))
+}
+
+tbgb_status tbgb_gen_keys_cdf(tbgb_ctx* ctx, int64_t* d_keys, int64_t n, const double* d_cdf, int64_t n_ids,
+                              uint64_t salt, uint64_t seed, int64_t first_row, void* stream) {
+  if (n_ids < 1 || (n > 0 && !d_cdf)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "bad cdf table");
+  GEN_ENTRY(tbgb::gen_keys_cdf(d_keys, n, d_cdf, n_ids, salt, seed, first_row, static_cast<cudaStream_t>(stream)))
+}
+
+tbgb_status tbgb_gen_keys_ids(tbgb_ctx* ctx, int64_t* d_keys, int64_t n, int64_t n_ids, uint64_t salt, uint64_t seed,
+                              int64_t first_row, void* stream) {
+  if (n_ids < 1) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_ids must be >= 1");
+  GEN_ENTRY(tbgb::gen_keys_ids(d_keys, n, static_cast<uint64_t>(n_ids), salt, seed, first_row,
+                               static_cast<cudaStream_t>(stream)))
+}
+
+tbgb_status tbgb_gen_values_lognormal_f32(tbgb_ctx* ctx, float* d_vals, int64_t n, double mu, double sigma,
+                                          uint64_t seed, int64_t first_row, void* stream) {
+  GEN_ENTRY(tbgb::gen_values_lognormal_f32(d_vals, n, mu, sigma, seed, first_row, static_cast<cudaStream_t>(stream)))
 }
 
 }  // extern "C"

@@ -58,7 +58,67 @@ __global__ void k_inject(double* v, long long n, double nan_frac, double inf_fra
   }
 }
 
+// int64 keys drawn through an inverse CDF: rank = first r with cdf[r] >= u (the
+// table's last entry is 1.0), key = mix64(rank ^ salt) -- random 64-bit ids with the
+// rank distribution of the table (Zipf for the fused-pipeline workload).
+__global__ void k_keys_cdf(int64_t* keys, long long n, const double* __restrict__ cdf, long long n_ids, uint64_t salt,
+                           uint64_t cs, long long first) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const double u = u01(splitmix_at(cs, static_cast<uint64_t>(first + i)));
+    long long lo = 0, hi = n_ids - 1;
+    while (lo < hi) {
+      const long long mid = (lo + hi) >> 1;
+      if (cdf[mid] >= u) hi = mid;
+      else lo = mid + 1;
+    }
+    keys[i] = static_cast<int64_t>(mix64(static_cast<uint64_t>(lo) ^ salt));
+  }
+}
+
+// int64 keys uniform over n_ids random 64-bit ids: key = mix64((x % n_ids) ^ salt).
+__global__ void k_keys_ids(int64_t* keys, long long n, uint64_t n_ids, uint64_t salt, uint64_t cs, long long first) {
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x)
+    keys[i] = static_cast<int64_t>(mix64((splitmix_at(cs, static_cast<uint64_t>(first + i)) % n_ids) ^ salt));
+}
+
+// f32 LogNormal(mu, sigma): exp of the column's normal stream, rounded to f32.
+__global__ void k_values_lognormal_f32(float* v, long long n, double mu, double sigma, uint64_t cs, long long first) {
+  const double two_pi = 6.283185307179586;
+  for (long long i = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; i < n;
+       i += static_cast<long long>(gridDim.x) * blockDim.x) {
+    const uint64_t r = static_cast<uint64_t>(first + i);
+    double u1 = u01(splitmix_at(cs, 2 * r));
+    const double u2 = u01(splitmix_at(cs, 2 * r + 1));
+    if (u1 <= 0.0) u1 = 1.0 / 9007199254740992.0;
+    const double z = __dmul_rn(sqrt(__dmul_rn(-2.0, log(u1))), cos(__dmul_rn(two_pi, u2)));
+    v[i] = static_cast<float>(exp(__dadd_rn(mu, __dmul_rn(sigma, z))));
+  }
+}
+
 }  // namespace
+
+cudaError_t gen_keys_cdf(int64_t* keys, long long n, const double* cdf, long long n_ids, uint64_t salt, uint64_t seed,
+                         long long first, cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  k_keys_cdf<<<gen_blocks(n), kGenThreads, 0, s>>>(keys, n, cdf, n_ids, salt, column_seed(seed, 0), first);
+  return cudaGetLastError();
+}
+
+cudaError_t gen_keys_ids(int64_t* keys, long long n, uint64_t n_ids, uint64_t salt, uint64_t seed, long long first,
+                         cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  k_keys_ids<<<gen_blocks(n), kGenThreads, 0, s>>>(keys, n, n_ids, salt, column_seed(seed, 0), first);
+  return cudaGetLastError();
+}
+
+cudaError_t gen_values_lognormal_f32(float* vals, long long n, double mu, double sigma, uint64_t seed, long long first,
+                                     cudaStream_t s) {
+  if (n == 0) return cudaSuccess;
+  k_values_lognormal_f32<<<gen_blocks(n), kGenThreads, 0, s>>>(vals, n, mu, sigma, column_seed(seed, 1), first);
+  return cudaGetLastError();
+}
 
 cudaError_t gen_keys_uniform(int32_t* keys, long long n, int G, uint64_t seed, long long first, cudaStream_t s) {
   if (n == 0) return cudaSuccess;

@@ -29,6 +29,12 @@ cudaError_t gen_values_uniform(double* vals, long long n, double lo, double hi, 
                                cudaStream_t s);
 cudaError_t gen_values_normal(double* vals, long long n, double mu, double sigma, uint64_t seed, long long first,
                               cudaStream_t s);
+cudaError_t gen_keys_cdf(int64_t* keys, long long n, const double* cdf, long long n_ids, uint64_t salt, uint64_t seed,
+                         long long first, cudaStream_t s);
+cudaError_t gen_keys_ids(int64_t* keys, long long n, uint64_t n_ids, uint64_t salt, uint64_t seed, long long first,
+                         cudaStream_t s);
+cudaError_t gen_values_lognormal_f32(float* vals, long long n, double mu, double sigma, uint64_t seed, long long first,
+                                     cudaStream_t s);
 cudaError_t gen_inject_nonfinite(double* vals, long long n, double nan_frac, double inf_frac, uint64_t seed,
                                  long long first, cudaStream_t s);
 

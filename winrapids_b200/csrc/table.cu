@@ -1,0 +1,598 @@
+// table.cu -- groupby through an accumulator table in device memory.
+//
+// Covers what the shared-memory column kernel (dense.cu) cannot: int64 keys of any
+// value (an open-addressing hash table in HBM; the reference factorises keys on the
+// host, group_index.rs:117-204, and accepts i32 codes only), dense keys with more
+// than 1024 groups, f32 columns, and the filter / expression fused into the pass
+// (filter_jit.rs:196-252 mask semantics, map_phi2 compute_engine.rs:198-210 and its
+// CPU arithmetic :627-636, fused like scatter_jit.rs:402-495).
+//
+// Per group the table keeps non-NaN and finite row counts, a shift K (the first
+// finite value that reached the slot), S1 = sum(v - K), S2 = sum((v - K)^2), the
+// extrema as order-preserving u64 (so integer atomicMin / atomicMax apply) and the
+// first zero row; the finaliser turns a slot into the same mergeable state and the
+// same outputs as the dense kernel (gstate.cuh), so sum, mean and m2 follow
+// descriptive.rs:383-435 and extrema the strict `<` / `>` scans of
+// compute_engine.rs:304-322.
+//
+// One persistent 1024-thread CTA per SM streams rows with coalesced evict-first
+// loads, four rows per thread per tile with their loads issued together.  Rows
+// either update the global table with atomics (the first probe of all four rows is
+// issued before any of them is resolved), or -- for skewed keys -- first go to a
+// per-CTA shared-memory table of a few thousand slots that absorbs the hot keys and
+// is merged into the global table once at the end (shifted sums re-centred on the
+// global slot's K).  Rows whose key is not admitted to the shared table (it is full)
+// take the global path, so any key distribution is handled.
+#include <cstdint>
+
+#include "common.cuh"
+#include "gstate.cuh"
+#include "table.cuh"
+
+namespace tbgb {
+
+namespace {
+
+constexpr int TNT = 1024;           // threads per CTA
+constexpr int TR = 4;               // rows per thread per tile
+constexpr int TTILE = TNT * TR;     // rows per tile
+constexpr int LS_FULL = 2048;       // shared-table slots with the FULL layout (64 B each)
+constexpr int LS_SC = 4096;         // shared-table slots with the SUMCOUNT layout (20 B each)
+constexpr int LPROBE = 8;           // shared-table probe limit
+constexpr unsigned long long K_UNSET = 0x7FF8000000000001ull;  // NaN payload no finite value has
+
+// MurmurHash3's 64-bit finaliser (public domain): spreads keys over the table.
+__device__ __forceinline__ unsigned long long fmix64(unsigned long long k) {
+  k ^= k >> 33;
+  k *= 0xff51afd7ed558ccdull;
+  k ^= k >> 33;
+  k *= 0xc4ceb9fe1a85ec53ull;
+  k ^= k >> 33;
+  return k;
+}
+
+__device__ __forceinline__ unsigned long long dbits(double v) {
+  return static_cast<unsigned long long>(__double_as_longlong(v));
+}
+__device__ __forceinline__ double bitsd(unsigned long long b) { return __longlong_as_double(static_cast<long long>(b)); }
+
+template <bool F32>
+__device__ __forceinline__ double load_val(const void* p, long long i) {
+  if constexpr (F32) return static_cast<double>(__ldcs(static_cast<const float*>(p) + i));
+  else return __ldcs(static_cast<const double*>(p) + i);
+}
+
+template <bool KEY64>
+__device__ __forceinline__ long long load_key(const void* p, long long i) {
+  if constexpr (KEY64) return __ldcs(static_cast<const long long*>(p) + i);
+  else return static_cast<long long>(__ldcs(static_cast<const int*>(p) + i));
+}
+
+// Expression of the reference's map_phi2 CPU whitelist (compute_engine.rs:627-636)
+// plus `(a*b)+c`; every operation rounded on its own, no contraction.
+__device__ __forceinline__ double eval_expr(int expr, double a, double b, double c) {
+  switch (expr) {
+    case TBGB_EXPR_ADD: return __dadd_rn(a, b);
+    case TBGB_EXPR_SUB: return __dsub_rn(a, b);
+    case TBGB_EXPR_MUL: return __dmul_rn(a, b);
+    case TBGB_EXPR_MUL_PLUS1: return __dadd_rn(__dmul_rn(a, b), 1.0);
+    case TBGB_EXPR_MUL_ADD: return __dadd_rn(__dmul_rn(a, b), c);
+    default: return a;
+  }
+}
+
+// Predicate on column a; comparisons with NaN fail (filter_jit.rs:196-243).
+__device__ __forceinline__ bool eval_pred(int pred, double a, double t) {
+  switch (pred) {
+    case TBGB_PRED_GT: return a > t;
+    case TBGB_PRED_GE: return a >= t;
+    case TBGB_PRED_LT: return a < t;
+    case TBGB_PRED_LE: return a <= t;
+    case TBGB_PRED_NOT_NAN: return !is_nan(a);
+    case TBGB_PRED_FINITE: return is_finite(a);
+    default: return true;
+  }
+}
+
+template <bool FULL>
+__host__ __device__ constexpr int slot_words() { return FULL ? FL_WORDS : SC_WORDS; }
+
+// Assigns the output row of a newly inserted hash slot.
+__device__ __forceinline__ void assign_id(const TableArgs& a, unsigned long long* p, int wid) {
+  const unsigned long long id = atomicAdd(a.ngroups, 1ull);
+  p[wid] = id;
+  if (id >= static_cast<unsigned long long>(a.max_groups)) atomicOr(a.err, KERR_TABLE_FULL);
+}
+
+// Slot of `key` in the hash table, inserting it when absent; -1 when the probe
+// limit is reached (reported as KERR_TABLE_FULL).  INT64_MIN, the free-slot
+// marker, lives in the sentinel slot after the table, claimed through its ID word.
+template <bool FULL>
+__device__ __forceinline__ long long hash_slot_from(const TableArgs& a, unsigned long long key,
+                                                    unsigned long long h, unsigned long long cur) {
+  constexpr int W = slot_words<FULL>();
+  constexpr int ID = FULL ? FL_ID : SC_ID;
+  unsigned long long* T = a.table;
+  if (key == kEmptyKey) {
+    unsigned long long* p = T + a.slots * W;
+    if (__ldcg(p + ID) == kNoId && atomicCAS(p + ID, kNoId, kNoId - 1) == kNoId) assign_id(a, p, ID);
+    return static_cast<long long>(a.slots);
+  }
+  const unsigned long long m = a.slots - 1;
+  for (int probe = 0; probe < kMaxProbe; ++probe) {
+    if (probe > 0) cur = __ldcg(T + h * W);
+    if (cur == key) return static_cast<long long>(h);
+    if (cur == kEmptyKey) {
+      const unsigned long long old = atomicCAS(T + h * W, kEmptyKey, key);
+      if (old == kEmptyKey) {
+        assign_id(a, T + h * W, ID);
+        return static_cast<long long>(h);
+      }
+      if (old == key) return static_cast<long long>(h);
+    }
+    h = (h + 1) & m;
+  }
+  atomicOr(a.err, KERR_TABLE_FULL);
+  return -1;
+}
+
+// K of a slot: the first finite value that reached it.
+__device__ __forceinline__ double slot_shift(unsigned long long* kw, double v) {
+  unsigned long long kb = __ldcg(kw);
+  if (kb == K_UNSET) {
+    kb = atomicCAS(kw, K_UNSET, dbits(v));
+    if (kb == K_UNSET) kb = dbits(v);
+  }
+  return bitsd(kb);
+}
+
+// One non-NaN row into a global slot.
+template <bool FULL>
+__device__ __forceinline__ void global_row(unsigned long long* p, double v, long long grow) {
+  if constexpr (FULL) {
+    atomicAdd(p + FL_NN, 1ull);
+    if (is_finite(v)) {
+      const double d = v - slot_shift(p + FL_K, v);
+      atomicAdd(reinterpret_cast<double*>(p + FL_S1), d);
+      atomicAdd(reinterpret_cast<double*>(p + FL_S2), d * d);
+      atomicAdd(p + FL_NF, 1ull);
+    }
+    const unsigned long long o = f2o(v);
+    if (o < __ldcg(p + FL_MN)) atomicMin(p + FL_MN, o);
+    if (o > __ldcg(p + FL_MX)) atomicMax(p + FL_MX, o);
+    if (v == 0.0) atomicMin(p + FL_ZF, zero_code(grow, v));
+  } else {
+    atomicAdd(p + SC_NN, 1ull);
+    if (is_finite(v)) atomicAdd(reinterpret_cast<double*>(p + SC_SUM), v);
+  }
+}
+
+// Per-CTA shared-memory table.
+template <bool FULL>
+struct LocalTable {
+  static constexpr int LS = FULL ? LS_FULL : LS_SC;
+  static constexpr int LIMIT = LS * 3 / 4;  // admission stops at this fill
+  unsigned long long* key;
+  unsigned long long* K;     // FULL
+  double* s1;                // FULL: sum(v - K); SUMCOUNT: sum(v)
+  double* s2;                // FULL
+  unsigned long long* mn;    // FULL
+  unsigned long long* mx;    // FULL
+  unsigned long long* zf;    // FULL
+  uint32_t* nn;
+  uint32_t* nf;              // FULL
+  uint32_t* fill;
+
+  static constexpr size_t bytes() {
+    return FULL ? static_cast<size_t>(LS) * (7 * 8 + 2 * 4) + 16 : static_cast<size_t>(LS) * (2 * 8 + 4) + 16;
+  }
+
+  __device__ __forceinline__ void carve(unsigned char* sm) {
+    unsigned char* q = sm;
+    key = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+    if constexpr (FULL) {
+      K = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+      s1 = reinterpret_cast<double*>(q); q += LS * 8;
+      s2 = reinterpret_cast<double*>(q); q += LS * 8;
+      mn = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+      mx = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+      zf = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+      nn = reinterpret_cast<uint32_t*>(q); q += LS * 4;
+      nf = reinterpret_cast<uint32_t*>(q); q += LS * 4;
+    } else {
+      s1 = reinterpret_cast<double*>(q); q += LS * 8;
+      nn = reinterpret_cast<uint32_t*>(q); q += LS * 4;
+    }
+    fill = reinterpret_cast<uint32_t*>(q);
+  }
+
+  __device__ __forceinline__ void init(int tid) {
+    for (int s = tid; s < LS; s += TNT) {
+      key[s] = kEmptyKey;
+      s1[s] = 0.0;
+      nn[s] = 0;
+      if constexpr (FULL) {
+        K[s] = K_UNSET;
+        s2[s] = 0.0;
+        mn[s] = f2o(pos_inf());
+        mx[s] = f2o(neg_inf());
+        zf[s] = ~0ull;
+        nf[s] = 0;
+      }
+    }
+    if (tid == 0) *fill = 0;
+  }
+
+  // Slot of `k` (inserted if there is room), or -1.
+  __device__ __forceinline__ int find(unsigned long long k) {
+    if (k == kEmptyKey) return -1;
+    volatile unsigned long long* vk = key;
+    unsigned int h = static_cast<unsigned int>(fmix64(k)) & (LS - 1);
+    for (int probe = 0; probe < LPROBE; ++probe) {
+      const unsigned long long cur = vk[h];
+      if (cur == k) return static_cast<int>(h);
+      if (cur == kEmptyKey) {
+        if (*reinterpret_cast<volatile uint32_t*>(fill) >= static_cast<uint32_t>(LIMIT)) return -1;
+        const unsigned long long old = atomicCAS(key + h, kEmptyKey, k);
+        if (old == kEmptyKey) {
+          atomicAdd(fill, 1u);
+          return static_cast<int>(h);
+        }
+        if (old == k) return static_cast<int>(h);
+      }
+      h = (h + 1) & (LS - 1);
+    }
+    return -1;
+  }
+
+  __device__ __forceinline__ void row(int s, double v, long long grow) {
+    atomicAdd(nn + s, 1u);
+    if constexpr (FULL) {
+      if (is_finite(v)) {
+        unsigned long long kb = *reinterpret_cast<volatile unsigned long long*>(K + s);
+        if (kb == K_UNSET) {
+          kb = atomicCAS(K + s, K_UNSET, dbits(v));
+          if (kb == K_UNSET) kb = dbits(v);
+        }
+        const double d = v - bitsd(kb);
+        atomicAdd(s1 + s, d);
+        atomicAdd(s2 + s, d * d);
+        atomicAdd(nf + s, 1u);
+      }
+      const unsigned long long o = f2o(v);
+      if (o < *reinterpret_cast<volatile unsigned long long*>(mn + s)) atomicMin(mn + s, o);
+      if (o > *reinterpret_cast<volatile unsigned long long*>(mx + s)) atomicMax(mx + s, o);
+      if (v == 0.0) atomicMin(zf + s, zero_code(grow, v));
+    } else {
+      if (is_finite(v)) atomicAdd(s1 + s, v);
+    }
+  }
+
+  // Merges local slot s into global slot p.
+  __device__ __forceinline__ void flush(int s, unsigned long long* p) {
+    if constexpr (FULL) {
+      const unsigned long long n_nn = nn[s], n_f = nf[s];
+      if (n_nn) atomicAdd(p + FL_NN, n_nn);
+      if (n_f) {
+        const double Kl = bitsd(K[s]);
+        const double Kg = slot_shift(p + FL_K, Kl);
+        const double off = Kl - Kg, a1 = s1[s], a2 = s2[s], nfd = static_cast<double>(n_f);
+        atomicAdd(reinterpret_cast<double*>(p + FL_S1), a1 + nfd * off);
+        atomicAdd(reinterpret_cast<double*>(p + FL_S2), a2 + off * (2.0 * a1 + nfd * off));
+        atomicAdd(p + FL_NF, n_f);
+      }
+      if (n_nn) {
+        if (mn[s] < __ldcg(p + FL_MN)) atomicMin(p + FL_MN, mn[s]);
+        if (mx[s] > __ldcg(p + FL_MX)) atomicMax(p + FL_MX, mx[s]);
+        if (zf[s] != ~0ull) atomicMin(p + FL_ZF, zf[s]);
+      }
+    } else {
+      if (nn[s]) {
+        atomicAdd(p + SC_NN, static_cast<unsigned long long>(nn[s]));
+        atomicAdd(reinterpret_cast<double*>(p + SC_SUM), s1[s]);
+      }
+    }
+  }
+};
+
+template <bool KEY64, bool F32, bool FULL, bool LOCAL>
+__global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  constexpr int W = slot_words<FULL>();
+  const int tid = threadIdx.x;
+  LocalTable<FULL> lt;
+  if constexpr (LOCAL) {
+    lt.carve(sm);
+    lt.init(tid);
+    __syncthreads();
+  }
+  const long long n = a.n;
+  const int expr = a.cols.expr, pred = a.cols.pred;
+  const double thr = a.cols.threshold;
+  const bool need_b = expr != TBGB_EXPR_A, need_c = expr == TBGB_EXPR_MUL_ADD;
+  const uint64_t* mask = a.mask;
+  unsigned long long* T = a.table;
+  const unsigned long long hmask = a.slots - 1;
+
+  for (long long base = static_cast<long long>(blockIdx.x) * TTILE; base < n;
+       base += static_cast<long long>(gridDim.x) * TTILE) {
+    long long kk[TR];
+    double va[TR], vb[TR], vc[TR];
+#pragma unroll
+    for (int r = 0; r < TR; ++r) {
+      const long long row = base + r * TNT + tid;
+      kk[r] = 0; va[r] = 0.0; vb[r] = 0.0; vc[r] = 0.0;
+      if (row < n) {
+        kk[r] = load_key<KEY64>(a.keys, row);
+        va[r] = load_val<F32>(a.cols.a, row);
+        if (need_b) vb[r] = load_val<F32>(a.cols.b, row);
+        if (need_c) vc[r] = load_val<F32>(a.cols.c, row);
+      }
+    }
+    // filter + expression; `live` rows have passed mask and predicate
+    bool live[TR];
+    double v[TR];
+#pragma unroll
+    for (int r = 0; r < TR; ++r) {
+      const long long row = base + r * TNT + tid;
+      bool ok = row < n;
+      if (ok && mask) ok = (__ldg(mask + (row >> 6)) >> (row & 63)) & 1ull;
+      if (ok) ok = eval_pred(pred, va[r], thr);
+      if (ok && !KEY64 && static_cast<unsigned long long>(kk[r]) >= a.slots) {
+        atomicOr(a.err, KERR_KEY_RANGE);
+        ok = false;
+      }
+      v[r] = eval_expr(expr, va[r], vb[r], vc[r]);
+      // dense keys need no slot for NaN rows; hash keys still create their group
+      if (!KEY64 && is_nan(v[r])) ok = false;
+      live[r] = ok;
+    }
+    // shared-table admission
+    int ls[TR];
+#pragma unroll
+    for (int r = 0; r < TR; ++r) {
+      ls[r] = -1;
+      if constexpr (LOCAL) {
+        if (live[r]) ls[r] = lt.find(static_cast<unsigned long long>(kk[r]));
+      }
+    }
+    // first probe of every global-path row, issued together
+    unsigned long long hh[TR], cur[TR];
+#pragma unroll
+    for (int r = 0; r < TR; ++r) {
+      hh[r] = 0; cur[r] = 0;
+      if constexpr (KEY64) {
+        if (live[r] && ls[r] < 0) {
+          hh[r] = fmix64(static_cast<unsigned long long>(kk[r])) & hmask;
+          if (static_cast<unsigned long long>(kk[r]) != kEmptyKey) cur[r] = __ldcg(T + hh[r] * W);
+        }
+      }
+    }
+#pragma unroll
+    for (int r = 0; r < TR; ++r) {
+      if (!live[r]) continue;
+      const long long grow = a.row_offset + base + r * TNT + tid;
+      if constexpr (LOCAL) {
+        if (ls[r] >= 0) {
+          if (!is_nan(v[r])) lt.row(ls[r], v[r], grow);
+          continue;
+        }
+      }
+      long long gs;
+      if constexpr (KEY64) {
+        gs = hash_slot_from<FULL>(a, static_cast<unsigned long long>(kk[r]), hh[r], cur[r]);
+        if (gs < 0) continue;
+      } else {
+        gs = kk[r];
+      }
+      if (!is_nan(v[r])) global_row<FULL>(T + static_cast<unsigned long long>(gs) * W, v[r], grow);
+    }
+  }
+
+  if constexpr (LOCAL) {
+    __syncthreads();
+    for (int s = tid; s < LocalTable<FULL>::LS; s += TNT) {
+      const unsigned long long k = lt.key[s];
+      if (k == kEmptyKey) continue;
+      long long gs;
+      if constexpr (KEY64) {
+        const unsigned long long h = fmix64(k) & hmask;
+        gs = hash_slot_from<FULL>(a, k, h, __ldcg(T + h * W));
+        if (gs < 0) continue;
+      } else {
+        gs = static_cast<long long>(k);
+      }
+      lt.flush(s, T + static_cast<unsigned long long>(gs) * W);
+    }
+  }
+}
+
+__global__ void table_init_kernel(unsigned long long* T, unsigned long long nslots, int full) {
+  const unsigned long long i0 = blockIdx.x * static_cast<unsigned long long>(blockDim.x) + threadIdx.x;
+  const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
+  if (full) {
+    const unsigned long long mn0 = f2o(pos_inf()), mx0 = f2o(neg_inf());
+    for (unsigned long long s = i0; s < nslots; s += stride) {
+      ulonglong2* p = reinterpret_cast<ulonglong2*>(T + s * FL_WORDS);
+      p[0] = make_ulonglong2(kEmptyKey, K_UNSET);  // KEY, K
+      p[1] = make_ulonglong2(0ull, 0ull);          // NN, NF
+      p[2] = make_ulonglong2(0ull, 0ull);          // S1, S2 (+0.0)
+      p[3] = make_ulonglong2(mn0, mx0);            // MN, MX
+      p[4] = make_ulonglong2(kNoId, ~0ull);        // ID, ZF
+      p[5] = make_ulonglong2(0ull, 0ull);          // S3, S4
+    }
+  } else {
+    for (unsigned long long s = i0; s < nslots; s += stride) {
+      ulonglong2* p = reinterpret_cast<ulonglong2*>(T + s * SC_WORDS);
+      p[0] = make_ulonglong2(kEmptyKey, 0ull);     // KEY, NN
+      p[1] = make_ulonglong2(0ull, kNoId);         // SUM, ID
+    }
+  }
+  if (i0 == 0) T[nslots * (full ? FL_WORDS : SC_WORDS)] = 0ull;  // distinct-key counter
+}
+
+// A FULL slot as a mergeable state.
+__device__ __forceinline__ GState slot_state(const unsigned long long* p) {
+  GState s = gstate_empty();
+  s.nn = static_cast<double>(p[FL_NN]);
+  const unsigned long long nf = p[FL_NF];
+  if (nf > 0) {
+    s.nf = static_cast<double>(nf);
+    s.K = bitsd(p[FL_K]);
+    s.sumoff = bitsd(p[FL_S1]);
+    s.meanoff = s.sumoff / s.nf;
+    s.m2 = fmax(bitsd(p[FL_S2]) - s.sumoff * s.meanoff, 0.0);
+  }
+  s.mn = o2f(p[FL_MN]);
+  s.mx = o2f(p[FL_MX]);
+  s.zf = p[FL_ZF];
+  return s;
+}
+
+__device__ __forceinline__ void sumcount_finalize(const unsigned long long* p, long long j, const tbgb_moments& o) {
+  const double nn = static_cast<double>(p[SC_NN]);
+  double sum = bitsd(p[SC_SUM]);
+  if (sum == 0.0) sum = 0.0;
+  if (o.count) o.count[j] = nn;
+  if (o.sum) o.sum[j] = sum;
+  if (o.mean) o.mean[j] = nn > 0 ? sum / nn : qnan();
+}
+
+__global__ void table_finalize_dense_kernel(const unsigned long long* __restrict__ T, long long G, int full,
+                                            tbgb_moments out, double* state_out) {
+  for (long long g = blockIdx.x * static_cast<long long>(blockDim.x) + threadIdx.x; g < G;
+       g += static_cast<long long>(gridDim.x) * blockDim.x) {
+    if (full) {
+      const GState s = slot_state(T + g * FL_WORDS);
+      if (state_out) gstate_store(state_out, G, g, s);
+      else gstate_finalize(s, g, out);
+    } else {
+      sumcount_finalize(T + g * SC_WORDS, g, out);
+    }
+  }
+}
+
+__global__ void table_finalize_hash_kernel(const unsigned long long* __restrict__ T, unsigned long long slots,
+                                           int full, long long max_groups, int64_t* out_keys, tbgb_moments out,
+                                           int64_t* n_groups) {
+  const int W = full ? FL_WORDS : SC_WORDS;
+  const int ID = full ? FL_ID : SC_ID;
+  const unsigned long long i0 = blockIdx.x * static_cast<unsigned long long>(blockDim.x) + threadIdx.x;
+  if (i0 == 0) {
+    const unsigned long long c = T[(slots + 1) * W];
+    *n_groups = static_cast<int64_t>(c < static_cast<unsigned long long>(max_groups) ? c : max_groups);
+  }
+  for (unsigned long long i = i0; i <= slots; i += static_cast<unsigned long long>(gridDim.x) * blockDim.x) {
+    const unsigned long long* p = T + i * W;
+    const unsigned long long key = p[0];
+    const bool occupied = i < slots ? key != kEmptyKey : p[ID] != kNoId;
+    if (!occupied) continue;
+    const unsigned long long id = p[ID];
+    if (id >= static_cast<unsigned long long>(max_groups)) continue;
+    out_keys[id] = static_cast<int64_t>(key);
+    if (full) gstate_finalize(slot_state(p), static_cast<long long>(id), out);
+    else sumcount_finalize(p, static_cast<long long>(id), out);
+  }
+}
+
+template <bool KEY64, bool F32, bool FULL, bool LOCAL>
+cudaError_t launch_table(const TablePlan& P, const TableArgs& a, cudaStream_t s) {
+  auto k = table_kernel<KEY64, F32, FULL, LOCAL>;
+  if (P.smem > 0) {
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(P.smem));
+    if (e != cudaSuccess) return e;
+  }
+  k<<<P.grid, P.block, P.smem, s>>>(a);
+  return cudaGetLastError();
+}
+
+template <bool KEY64, bool F32>
+cudaError_t launch_table_kf(const TablePlan& P, const TableArgs& a, cudaStream_t s) {
+  if (P.full)
+    return P.local ? launch_table<KEY64, F32, true, true>(P, a, s) : launch_table<KEY64, F32, true, false>(P, a, s);
+  return P.local ? launch_table<KEY64, F32, false, true>(P, a, s) : launch_table<KEY64, F32, false, false>(P, a, s);
+}
+
+unsigned long long next_pow2(unsigned long long x) {
+  unsigned long long p = 1;
+  while (p < x) p <<= 1;
+  return p;
+}
+
+}  // namespace
+
+size_t table_slot_words(bool full) { return full ? FL_WORDS : SC_WORDS; }
+
+TablePlan table_plan(bool hash, bool full, int mode, long long groups, int num_sms) {
+  TablePlan P{};
+  P.hash = hash;
+  P.full = full;
+  const long long limit = full ? LocalTable<true>::LIMIT : LocalTable<false>::LIMIT;
+  if (hash) {
+    const unsigned long long want = static_cast<unsigned long long>(groups) * 2;
+    P.slots = next_pow2(want < 1024 ? 1024 : want);
+  } else {
+    P.slots = static_cast<unsigned long long>(groups);
+  }
+  if (mode == 1) P.local = true;
+  else if (mode == 2) P.local = false;
+  else P.local = hash ? groups <= (1ll << 22) : groups <= limit;
+  const unsigned long long words = (P.slots + (hash ? 1 : 0)) * table_slot_words(full) + 1;
+  P.table_bytes = (words * 8 + 255) / 256 * 256;
+  P.grid = num_sms;
+  P.block = TNT;
+  P.smem = P.local ? (full ? LocalTable<true>::bytes() : LocalTable<false>::bytes()) : 0;
+  return P;
+}
+
+cudaError_t table_init(const TablePlan& P, unsigned long long* table, cudaStream_t s, uint64_t* launches) {
+  const unsigned long long nslots = P.slots + (P.hash ? 1 : 0);
+  unsigned long long blocks = (nslots + 255) / 256;
+  if (blocks > 65536ull) blocks = 65536ull;
+  if (blocks < 1) blocks = 1;
+  table_init_kernel<<<static_cast<unsigned int>(blocks), 256, 0, s>>>(table, nslots, P.full ? 1 : 0);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) (*launches)++;
+  return e;
+}
+
+cudaError_t table_accumulate(const TablePlan& P, const TableArgs& a, cudaStream_t s, uint64_t* launches,
+                             cudaEvent_t ev0, cudaEvent_t ev1) {
+  if (a.n == 0) return cudaSuccess;
+  const bool f32 = a.cols.dtype == TBGB_F32;
+  if (ev0) cudaEventRecord(ev0, s);
+  cudaError_t e;
+  if (P.hash) e = f32 ? launch_table_kf<true, true>(P, a, s) : launch_table_kf<true, false>(P, a, s);
+  else e = f32 ? launch_table_kf<false, true>(P, a, s) : launch_table_kf<false, false>(P, a, s);
+  if (e != cudaSuccess) return e;
+  if (ev1) cudaEventRecord(ev1, s);
+  (*launches)++;
+  return cudaSuccess;
+}
+
+cudaError_t table_finalize_dense(const TablePlan& P, const unsigned long long* table, long long G,
+                                 const tbgb_moments* out, double* state_out, cudaStream_t s, uint64_t* launches) {
+  long long blocks = (G + 255) / 256;
+  if (blocks > 65536) blocks = 65536;
+  tbgb_moments o = out ? *out : tbgb_moments{};
+  table_finalize_dense_kernel<<<static_cast<unsigned int>(blocks), 256, 0, s>>>(table, G, P.full ? 1 : 0, o,
+                                                                                 state_out);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) (*launches)++;
+  return e;
+}
+
+cudaError_t table_finalize_hash(const TablePlan& P, const unsigned long long* table, long long max_groups,
+                                int64_t* out_keys, const tbgb_moments* out, int64_t* d_n_groups, uint32_t* err,
+                                cudaStream_t s, uint64_t* launches) {
+  (void)err;
+  unsigned long long blocks = (P.slots + 1 + 255) / 256;
+  if (blocks > 65536ull) blocks = 65536ull;
+  table_finalize_hash_kernel<<<static_cast<unsigned int>(blocks), 256, 0, s>>>(table, P.slots, P.full ? 1 : 0,
+                                                                               max_groups, out_keys, *out, d_n_groups);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) (*launches)++;
+  return e;
+}
+
+}  // namespace tbgb

@@ -1,0 +1,68 @@
+// table.cuh -- global-memory accumulator tables: int64 keys (open addressing) and
+// dense keys beyond the shared-memory column kernel's range.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+#include "tambear_gb.h"
+
+namespace tbgb {
+
+// Slot words (u64).  FULL slot, 96 bytes: the eight words a row touches share the
+// slot's first two 32-byte sectors.
+//   KEY  the key (hash mode; EMPTY when free)    K   shift: first finite value seen (bits)
+//   NN   non-NaN rows                            NF  finite rows
+//   S1   sum(v - K) over finite rows             S2  sum((v - K)^2) over finite rows
+//   MN/MX extrema over non-NaN rows, order-preserving u64 encoding
+//   ID   output row of the group (hash mode)     ZF  first zero row code (row << 1 | sign)
+//   S3/S4 reserved
+// SUMCOUNT slot, 32 bytes (one sector): KEY, NN, SUM (finite values), ID.
+enum { FL_KEY = 0, FL_K, FL_NN, FL_NF, FL_S1, FL_S2, FL_MN, FL_MX, FL_ID, FL_ZF, FL_S3, FL_S4, FL_WORDS };
+enum { SC_KEY = 0, SC_NN, SC_SUM, SC_ID, SC_WORDS };
+
+constexpr unsigned long long kEmptyKey = 0x8000000000000000ull;  // INT64_MIN marks a free slot
+constexpr unsigned long long kNoId = ~0ull;
+constexpr int kMaxProbe = 4096;
+
+struct TableArgs {
+  const void* keys;      // int32 (dense) or int64 (hash)
+  tbgb_columns cols;
+  const uint64_t* mask;  // nullable
+  long long n;
+  long long row_offset;  // global index of row 0 (first-zero codes)
+  unsigned long long* table;
+  unsigned long long slots;   // dense: n_groups; hash: power of two (plus one sentinel slot after them)
+  unsigned long long* ngroups;  // hash: distinct-key counter
+  long long max_groups;
+  uint32_t* err;
+};
+
+struct TablePlan {
+  bool hash;       // int64 keys
+  bool full;       // FULL slot (else SUMCOUNT)
+  bool local;      // per-CTA shared-memory pre-aggregation
+  unsigned long long slots;
+  size_t table_bytes;  // including the sentinel slot and the counter word
+  int grid;
+  int block;
+  size_t smem;
+};
+
+size_t table_slot_words(bool full);
+TablePlan table_plan(bool hash, bool full, int mode, long long n_groups_or_max, int num_sms);
+
+// Fills every slot with its empty pattern and clears the counter.
+cudaError_t table_init(const TablePlan& P, unsigned long long* table, cudaStream_t s, uint64_t* launches);
+// One pass over the rows.
+cudaError_t table_accumulate(const TablePlan& P, const TableArgs& a, cudaStream_t s, uint64_t* launches,
+                             cudaEvent_t ev0 = nullptr, cudaEvent_t ev1 = nullptr);
+// Dense mode: outputs (or, when state_out != NULL, mergeable states) for groups [0, G).
+cudaError_t table_finalize_dense(const TablePlan& P, const unsigned long long* table, long long G,
+                                 const tbgb_moments* out, double* state_out, cudaStream_t s, uint64_t* launches);
+// Hash mode: group j (its ID) to out_keys[j] / element j of out; writes the group count.
+cudaError_t table_finalize_hash(const TablePlan& P, const unsigned long long* table, long long max_groups,
+                                int64_t* out_keys, const tbgb_moments* out, int64_t* d_n_groups, uint32_t* err,
+                                cudaStream_t s, uint64_t* launches);
+
+}  // namespace tbgb
