@@ -7,6 +7,13 @@ key.  Rows are split evenly over N GPUs (one process per GPU, launched by
 torch.distributed.run); each GPU reduces its shard to a mergeable per-group state
 table, the tables are all-gathered over NCCL and folded in rank order.
 
+Other workloads (--workload): `pipeline` (100,000,000 rows, int64 Zipf(1.1) keys over
+1,000,000 ids, filter a>0, v=a*b+c, sum/count/mean/var), `highcard` (2,000,000,000
+rows, int64 keys over 2^28 random ids, f32 LogNormal values, sum/count/mean; rows
+hash-partitioned to their key's owner GPU over NCCL all-to-all), `stress`
+(200,000,000 rows, 10,000 groups, 1e9 + N(0,1e-3) with NaN / +-inf), `cpu-ref`
+(1,000,000 rows, 1,000 groups) and `stress-1k`.
+
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload NAME]
 
 Rank 0 prints one JSON line.  `value` is whole-job rows/s with the inputs resident
@@ -22,6 +29,7 @@ import statistics
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 from pathlib import Path
 
@@ -30,21 +38,33 @@ sys.path.insert(0, str(ROOT))
 
 METRIC = "groupby-agg rows/s and HBM GB/s (frac of ~8 TB/s) at 1/2/4/8 B200"
 FALLBACK_HBM_GBS = 6650.0
+KEY_SALT = 0x5EED5EED12345678
 
 WORKLOADS = {
-    # name: rows, groups, value model, seed, description
-    "lowcard": dict(rows=1_000_000_000, groups=256, values=("uniform", -1.0, 1.0), nonfinite=None, seed=0,
+    "lowcard": dict(kind="dense", rows=1_000_000_000, groups=256, values=("uniform", -1.0, 1.0), nonfinite=None,
+                    seed=0,
                     desc="low-cardinality sharded: 1,000,000,000 rows; int32 key uniform in [0,256); "
                          "f64 value ~U(-1,1); sum/count/min/max/mean/var; rows split evenly over the GPUs, "
                          "partial tables all-gathered over NCCL and merged"),
-    "cpu-ref": dict(rows=1_000_000, groups=1000, values=("normal", 0.0, 1.0), nonfinite=None, seed=0,
+    "cpu-ref": dict(kind="dense", rows=1_000_000, groups=1000, values=("normal", 0.0, 1.0), nonfinite=None, seed=0,
                     desc="1,000,000 rows; int32 key uniform in [0,1000); f64 value ~N(0,1); "
                          "sum/count/min/max/mean/var; seed 0"),
-    "stress-1k": dict(rows=200_000_000, groups=1000, values=("normal", 1e9, 1e-3), nonfinite=(0.01, 0.001), seed=0,
+    "stress": dict(kind="dense", rows=200_000_000, groups=10000, values=("normal", 1e9, 1e-3),
+                   nonfinite=(0.01, 0.001), seed=0,
+                   desc="numerical stress: 200,000,000 rows; int32 key uniform in [0,10000); f64 value "
+                        "1e9 + N(0,1e-3) with 1% NaN and 0.1% +-inf; count/sum/mean/var/min/max"),
+    "stress-1k": dict(kind="dense", rows=200_000_000, groups=1000, values=("normal", 1e9, 1e-3),
+                      nonfinite=(0.01, 0.001), seed=0,
                       desc="200,000,000 rows; int32 key uniform in [0,1000); f64 value 1e9 + N(0,1e-3), 1% NaN, "
                            "0.1% +-inf; count/mean/var/min/max"),
+    "pipeline": dict(kind="pipeline", rows=100_000_000, ids=1_000_000, zipf=1.1, seed=0,
+                     desc="fused pipeline: 100,000,000 rows; int64 key Zipf(1.1) over 1,000,000 random ids; "
+                          "columns a,b,c f64 ~N(0,1); filter a>0, then v=a*b+c; sum/count/mean/var of v per key"),
+    "highcard": dict(kind="highcard", rows=2_000_000_000, ids=1 << 28, seed=0,
+                     desc="high-cardinality sharded: 2,000,000,000 rows; int64 key uniform over 2^28 random ids; "
+                          "f32 value ~LogNormal(0,1); sum/count/mean; rows hash-partitioned to the owner GPU of "
+                          "their key (NCCL all-to-all), each GPU groups the keys it owns"),
 }
-BYTES_PER_ROW = 12  # 4 B key + 8 B value, each column read once
 
 
 def parse():
@@ -58,6 +78,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU work of the baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--ids", type=int, default=None, help="override the distinct-id count of a hash workload")
+    ap.add_argument("--table-mode", default="auto", choices=["auto", "local", "direct"],
+                    help="global-table kernel: shared-memory pre-aggregation or direct atomics")
     return ap.parse_args()
 
 
@@ -76,13 +99,13 @@ def measured_peak():
     return FALLBACK_HBM_GBS, "fallback"
 
 
-def traffic_per_row():
-    """dram bytes per row of the main kernel from the committed ncu summary, if any."""
+def traffic_model(workload: str):
+    """DRAM bytes of the main kernel per row (+ fixed bytes per launch) from the committed ncu summary."""
     p = ROOT / "profiles" / "traffic.json"
     if not p.exists():
         return None, None
     try:
-        d = json.loads(p.read_text())["dense_moments_kernel"]
+        d = json.loads(p.read_text())[workload]
         return (float(d["dram_bytes_per_row"]), float(d.get("fixed_bytes_per_launch", 0.0))), d.get("source")
     except Exception:
         return None, None
@@ -138,6 +161,8 @@ class ClockSampler:
                 "sm_max_mhz": max(smax) if smax else None, "reasons": reasons, "samples": len(rows)}
 
 
+
+
 def cpu_threads() -> int:
     try:
         return len(os.sched_getaffinity(0))
@@ -145,35 +170,101 @@ def cpu_threads() -> int:
         return os.cpu_count() or 1
 
 
+def zipf_table(wl):
+    import oracle
+
+    return oracle.zipf_cdf(wl["ids"], wl["zipf"])
+
+
 def host_inputs(wl, start, count):
-    """The workload's rows [start, start+count) generated on the host (same bits as the device generator
-    for keys and uniform values)."""
+    """Rows [start, start+count) of the workload generated on the host (same recipes as the device
+    generators; integer columns bit-identical)."""
     import oracle
 
-    keys = oracle.gen_keys_uniform(count, wl["groups"], wl["seed"], start)
-    kind, a, b = wl["values"]
-    if kind == "uniform":
-        vals = oracle.gen_values_uniform(count, a, b, wl["seed"], start)
+    seed = wl["seed"]
+    if wl["kind"] == "dense":
+        keys = oracle.gen_keys_uniform(count, wl["groups"], seed, start)
+        kind, a, b = wl["values"]
+        if kind == "uniform":
+            vals = oracle.gen_values_uniform(count, a, b, seed, start)
+        else:
+            vals = oracle.gen_values_normal(count, a, b, seed, start)
+        if wl["nonfinite"]:
+            vals = oracle.inject_nonfinite(vals, wl["nonfinite"][0], wl["nonfinite"][1], seed, start)
+        return {"keys": keys, "a": vals}
+    if wl["kind"] == "pipeline":
+        return {"keys": oracle.gen_keys_cdf(count, zipf_table(wl), KEY_SALT, seed, start),
+                "a": oracle.gen_values_normal(count, 0.0, 1.0, seed + 1, start),
+                "b": oracle.gen_values_normal(count, 0.0, 1.0, seed + 2, start),
+                "c": oracle.gen_values_normal(count, 0.0, 1.0, seed + 3, start)}
+    return {"keys": oracle.gen_keys_ids(count, wl["ids"], KEY_SALT, seed, start),
+            "a": oracle.gen_values_lognormal_f32(count, 0.0, 1.0, seed, start)}
+
+
+def cpu_groupby(wl, cols, threads):
+    """The reference's CPU groupby (oracle port) over host columns, on `threads` threads."""
+    import numpy as np
+
+    import oracle
+
+    if wl["kind"] == "dense":
+        return oracle.moments_grouped_mt(cols["a"], cols["keys"], wl["groups"], threads=threads)
+    keys = cols["keys"]
+    if wl["kind"] == "pipeline":
+        mask = oracle.filter_mask("gt", 0.0, cols["a"])
+        v = oracle.map2("a + b", oracle.map2("a * b", cols["a"], cols["b"]), cols["c"])
+        live = ((mask[np.arange(keys.size) // 64] >> (np.arange(keys.size) % 64).astype(np.uint64))
+                & np.uint64(1)).astype(bool)
+        keys, v = keys[live], v[live]
     else:
-        vals = oracle.gen_values_normal(count, a, b, wl["seed"], start)
-    if wl["nonfinite"]:
-        vals = oracle.inject_nonfinite(vals, wl["nonfinite"][0], wl["nonfinite"][1], wl["seed"], start)
-    return keys, vals
+        v = cols["a"].astype(np.float64)
+    if threads <= 1:
+        return oracle.groupby_i64(keys, v)
+    # key-disjoint buckets, one per thread (the C oracle runs without the GIL)
+    bucket = (keys.view(np.uint64) * np.uint64(0x9E3779B97F4A7C15)) >> np.uint64(58)
+    bucket = (bucket % np.uint64(threads)).astype(np.int64)
+    order = np.argsort(bucket, kind="stable")
+    bounds = np.searchsorted(bucket[order], np.arange(threads + 1))
+    res = [None] * threads
+
+    def work(t):
+        idx = order[bounds[t]:bounds[t + 1]]
+        res[t] = oracle.groupby_i64(keys[idx], v[idx])
+
+    ths = [threading.Thread(target=work, args=(t,)) for t in range(threads)]
+    for th in ths:
+        th.start()
+    for th in ths:
+        th.join()
+    return res
 
 
-def cpu_sample_rows(wl, target_s, threads):
+def cpu_sample_rows(wl, target_s, threads, n_rows):
     """Rows the oracle processes in about target_s seconds on `threads` threads (calibrated)."""
-    import oracle
-
-    n0 = min(2_000_000, wl["rows"])
-    k, v = host_inputs(wl, 0, n0)
+    n0 = min(2_000_000, n_rows)
+    cols = host_inputs(wl, 0, n0)
     t0 = time.perf_counter()
-    oracle.moments_grouped_mt(v, k, wl["groups"], threads=threads)
+    cpu_groupby(wl, cols, threads)
     rate = n0 / (time.perf_counter() - t0)
-    return min(max(n0, int(rate * target_s)), wl["rows"], 200_000_000)
+    return min(max(n0, int(rate * target_s)), n_rows, 200_000_000)
+
+
+def bytes_per_row(wl) -> int:
+    """Algorithmic input bytes per row: every column read once."""
+    return {"dense": 12, "pipeline": 32, "highcard": 12}[wl["kind"]]
 
 
 def base_line(args, wl, n_rows, world):
+    bpr = bytes_per_row(wl)
+    cfg = {"workload": wl["desc"], "rows": n_rows, "bytes_per_row": bpr, "parallelism": f"row-shards x{world}",
+           "l2": "inputs far larger than the 126 MB L2; no flush needed between steps"
+           if n_rows * bpr > 1 << 30 else "inputs smaller than L2: L2 flushed between steps"}
+    if "groups" in wl:
+        cfg["n_groups"] = wl["groups"]
+    else:
+        cfg["distinct_ids"] = wl["ids"]
+    if args.table_mode != "auto":
+        cfg["table_mode"] = args.table_mode
     return {
         "metric": METRIC,
         "unit": "rows/s",
@@ -185,15 +276,7 @@ def base_line(args, wl, n_rows, world):
         "vs_baseline": None,
         "dtype": "f64",
         "data": "synthetic (counter-based SplitMix64 streams, same shapes and distributions as the configuration)",
-        "config": {
-            "workload": wl["desc"],
-            "rows": n_rows,
-            "n_groups": wl["groups"],
-            "bytes_per_row": BYTES_PER_ROW,
-            "parallelism": f"row-shards x{world}",
-            "l2": "inputs (12 B/row) far larger than the 126 MB L2; no flush needed between steps"
-            if n_rows * BYTES_PER_ROW > 1 << 30 else "inputs smaller than L2: L2 flushed between steps",
-        },
+        "config": cfg,
     }
 
 
@@ -204,27 +287,26 @@ def base_line(args, wl, n_rows, world):
 def run_reference(args, wl, n_rows, world, rank):
     if rank != 0:
         return
-    import oracle
-
     threads = cpu_threads()
     per_step_s = max(2.0, min(20.0, 150.0 / max(1, args.steps + args.warmup)))
-    sample = cpu_sample_rows(wl, per_step_s, threads)
-    k, v = host_inputs(wl, 0, sample)
+    sample = cpu_sample_rows(wl, per_step_s, threads, n_rows)
+    cols = host_inputs(wl, 0, sample)
     for _ in range(args.warmup):
-        oracle.moments_grouped_mt(v, k, wl["groups"], threads=threads)
+        cpu_groupby(wl, cols, threads)
     t0 = time.perf_counter()
     for _ in range(args.steps):
-        oracle.moments_grouped_mt(v, k, wl["groups"], threads=threads)
+        cpu_groupby(wl, cols, threads)
     dt = time.perf_counter() - t0
     value = sample * args.steps / dt
     line = base_line(args, wl, n_rows, world)
+    how = ("exact Kulisch groupby, per-thread registers merged in row-range order" if wl["kind"] == "dense" else
+           "sort-based exact groupby of int64 keys, key-disjoint buckets per thread")
     line.update({
         "impl": "reference",
         "value": value,
         "ms_per_step": dt * 1000.0 / args.steps,
         "cpu_baseline": {"value": value, "unit": "rows/s", "cores": threads, "kind": "port",
-                         "sample": f"first {sample} rows of the workload per step (exact Kulisch groupby, "
-                                   f"per-thread registers merged in row-range order)"},
+                         "sample": f"first {sample} rows of the workload per step ({how})"},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     })
     print(json.dumps(line), flush=True)
@@ -234,6 +316,135 @@ def run_reference(args, wl, n_rows, world, rank):
 # our arm
 # ---------------------------------------------------------------------------------
 
+class DenseJob:
+    """int32 keys in [0, G): the shared-memory column kernel (G <= 1024) or the global table."""
+
+    def __init__(self, ctx, wl, lo, hi, world, dist, dev):
+        import torch
+
+        self.ctx, self.wl, self.lo, self.world, self.dist = ctx, wl, lo, world, dist
+        G = self.G = wl["groups"]
+        n = self.n_local = hi - lo
+        self.kernel = "dense_moments_kernel" if G <= 1024 else "table_kernel"
+        self.bpr = 12
+        dk = torch.empty(n, dtype=torch.int32, device=dev)
+        dv = torch.empty(n, dtype=torch.float64, device=dev)
+        seed = wl["seed"]
+        ctx.gen_keys_uniform(dk, G, seed, lo)
+        kind, a, b = wl["values"]
+        if kind == "uniform":
+            ctx.gen_values_uniform(dv, a, b, seed, lo)
+        else:
+            ctx.gen_values_normal(dv, a, b, seed, lo)
+        if wl["nonfinite"]:
+            ctx.gen_inject_nonfinite(dv, wl["nonfinite"][0], wl["nonfinite"][1], seed, lo)
+        self.inputs = [dk, dv]
+        self.out = ctx.alloc_moments(G)
+        self.sharded = None
+        if world > 1:
+            from winrapids_b200.sharded import ShardedDenseGroupby
+
+            self.sharded = ShardedDenseGroupby(ctx, dist, world, G, self.out, dev)
+
+    def step(self, inputs):
+        keys, vals = inputs
+        if self.sharded is None:
+            self.ctx.groupby_dense(keys, vals, self.G, out=self.out, sync=False)
+        else:
+            self.sharded.step(keys, vals, self.lo)
+
+    def kernel_bytes(self) -> int:
+        return self.n_local * self.bpr
+
+    def read_result(self, host: dict) -> int:
+        import torch
+
+        for f, t in self.out.items():
+            if f not in host:
+                host[f] = torch.empty(t.numel(), dtype=t.dtype, pin_memory=True)
+            host[f].copy_(t, non_blocking=True)
+        return sum(t.numel() * 8 for t in self.out.values())
+
+
+class HashJob:
+    """int64 keys through the hash table: `pipeline` (filter + expression, Zipf keys) and `highcard`
+    (f32 values, sum/count/mean; owner-sharded over NCCL all-to-all when world > 1)."""
+
+    def __init__(self, ctx, wl, lo, hi, world, dist, dev):
+        import torch
+
+        import winrapids_b200 as wb
+
+        self.ctx, self.wl, self.world, self.dist = ctx, wl, world, dist
+        n = self.n_local = hi - lo
+        self.kernel = "table_kernel"
+        seed = wl["seed"]
+        keys = torch.empty(n, dtype=torch.int64, device=dev)
+        if wl["kind"] == "pipeline":
+            self.bpr = 32
+            self.fields = ("count", "sum", "mean", "m2", "var_pop", "var_samp")
+            cdf = torch.as_tensor(zipf_table(wl)).to(dev)
+            ctx.gen_keys_cdf(keys, cdf, KEY_SALT, seed, lo)
+            cols = []
+            for j in (1, 2, 3):
+                t = torch.empty(n, dtype=torch.float64, device=dev)
+                ctx.gen_values_normal(t, 0.0, 1.0, seed + j, lo)
+                cols.append(t)
+            self.inputs = [keys] + cols
+            self.op = dict(expr="a*b+c", pred=">", threshold=0.0)
+        else:
+            self.bpr = 12
+            self.fields = wb.SUMCOUNT_FIELDS
+            ctx.gen_keys_ids(keys, wl["ids"], KEY_SALT, seed, lo)
+            vals = torch.empty(n, dtype=torch.float32, device=dev)
+            ctx.gen_values_lognormal_f32(vals, 0.0, 1.0, seed, lo)
+            self.inputs = [keys, vals]
+            self.op = {}
+        ids = wl["ids"]
+        if world == 1:
+            self.max_groups = ids
+            self.out_keys = torch.empty(ids, dtype=torch.int64, device=dev)
+            self.out = {f: torch.empty(ids, dtype=torch.float64, device=dev) for f in self.fields}
+            self.ng = torch.zeros(1, dtype=torch.int64, device=dev)
+            self.sharded = None
+        else:
+            from winrapids_b200.sharded import ShardedHashGroupby
+
+            per_owner = int(ids / world * 1.05) + 4096
+            self.sharded = ShardedHashGroupby(ctx, dist, world, n, per_owner, self.fields, dev)
+            self.out_keys, self.out, self.ng = self.sharded.out_keys, self.sharded.out, self.sharded.n_groups
+
+    def _cols(self, inputs):
+        keys, a = inputs[0], inputs[1]
+        b = inputs[2] if len(inputs) > 2 else None
+        c = inputs[3] if len(inputs) > 3 else None
+        return keys, a, b, c
+
+    def step(self, inputs):
+        keys, a, b, c = self._cols(inputs)
+        if self.sharded is None:
+            self.ctx.groupby_hash_into(keys, a, self.max_groups, self.out_keys, self.out, self.ng, b=b, c=c,
+                                       **self.op)
+        else:
+            self.sharded.step(keys, a, b=b, c=c, **self.op)
+
+    def kernel_bytes(self) -> int:
+        # the table kernel reads the shard's columns (one GPU) or the received (key, f64 value) rows
+        return self.n_local * self.bpr if self.sharded is None else self.sharded.n_recv * 16
+
+    def read_result(self, host: dict) -> int:
+        import torch
+
+        g = int(self.ng.item())  # the group count decides how much to read back
+        total = 8
+        for f, t in [("keys", self.out_keys)] + list(self.out.items()):
+            if f not in host:
+                host[f] = torch.empty(t.numel(), dtype=t.dtype, pin_memory=True)
+            host[f][:g].copy_(t[:g], non_blocking=True)
+            total += g * 8
+        return total
+
+
 def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
     import torch
 
@@ -242,37 +453,15 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
     dev = torch.device(f"cuda:{local_rank}")
     torch.cuda.set_device(dev)
     ctx = wb.Context(local_rank)
-    G = wl["groups"]
+    ctx.set_table_mode(args.table_mode)
     lo, hi = n_rows * rank // world, n_rows * (rank + 1) // world
-    n_local = hi - lo
+    job = (DenseJob if wl["kind"] == "dense" else HashJob)(ctx, wl, lo, hi, world, dist, dev)
+    n_local = job.n_local
     stream = torch.cuda.current_stream()
-
-    # inputs resident in HBM, generated where they live
-    dk = torch.empty(n_local, dtype=torch.int32, device=dev)
-    dv = torch.empty(n_local, dtype=torch.float64, device=dev)
-    ctx.gen_keys_uniform(dk, G, wl["seed"], lo)
-    kind, a, b = wl["values"]
-    if kind == "uniform":
-        ctx.gen_values_uniform(dv, a, b, wl["seed"], lo)
-    else:
-        ctx.gen_values_normal(dv, a, b, wl["seed"], lo)
-    if wl["nonfinite"]:
-        ctx.gen_inject_nonfinite(dv, wl["nonfinite"][0], wl["nonfinite"][1], wl["seed"], lo)
-    out = ctx.alloc_moments(G)
-    st_local = torch.empty(ctx.state_bytes(G) // 8, dtype=torch.float64, device=dev)
-    gathered = torch.empty(world * st_local.numel(), dtype=torch.float64, device=dev)
     torch.cuda.synchronize()
 
-    small = n_local * BYTES_PER_ROW <= 256 << 20
+    small = n_local * job.bpr <= 256 << 20
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev) if small else None
-
-    def step(keys, vals):
-        if world == 1:
-            ctx.groupby_dense(keys, vals, G, out=out, sync=False)
-        else:
-            ctx.groupby_dense_state(keys, vals, G, row_offset=lo, state=st_local)
-            dist.all_gather_into_tensor(gathered, st_local)
-            ctx.merge_states(gathered, world, G, out=out)
 
     def barrier():
         if dist is not None:
@@ -281,11 +470,10 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
     for _ in range(args.warmup):
         if flush is not None:
             flush.zero_()
-        step(dk, dv)
+        job.step(job.inputs)
     ctx.sync()
     torch.cuda.synchronize()
 
-    uuid = None
     try:
         uuid = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
     except Exception:
@@ -298,37 +486,40 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
     barrier()
     torch.cuda.synchronize()
     ctx.profile(True)
+    kbytes = 0
     ev0.record(stream)
     for _ in range(args.steps):
         if flush is not None:
             flush.zero_()
-        step(dk, dv)
+        job.step(job.inputs)
+        kbytes += job.kernel_bytes()
     ev1.record(stream)
     torch.cuda.synchronize()
     barrier()
     ctx.profile(False)
     launches = ctx.launches - launches0
     kms, klaunches = ctx.kernel_time_ms()
-    ctx.sync()  # surfaces deferred device errors (e.g. a key out of range)
+    ctx.sync()  # surfaces deferred device errors (a key out of range, a full table)
     ms = ev0.elapsed_time(ev1)
 
     # ---- end to end through the public API, host buffers in pinned memory
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(3, min(args.steps, 10))
-    hk = torch.empty(n_local, dtype=torch.int32, pin_memory=True)
-    hv = torch.empty(n_local, dtype=torch.float64, pin_memory=True)
-    hk.copy_(dk)
-    hv.copy_(dv)
-    hout = {f: torch.empty(G, dtype=torch.float64, pin_memory=True) for f in out}
-    ek = torch.empty_like(dk)
-    ev = torch.empty_like(dv)
-    del dk, dv
+    host_in = []
+    for t in job.inputs:
+        h = torch.empty(t.numel(), dtype=t.dtype, pin_memory=True)
+        h.copy_(t)
+        host_in.append(h)
+    h2d = sum(h.numel() * h.element_size() for h in host_in)
+    dev_in = [torch.empty_like(t) for t in job.inputs]
+    job.inputs = None
+    host_out = {}
+    d2h = [0]
 
     def e2e_step():
-        ek.copy_(hk, non_blocking=True)
-        ev.copy_(hv, non_blocking=True)
-        step(ek, ev)
-        for f in out:
-            hout[f].copy_(out[f], non_blocking=True)
+        for d, h in zip(dev_in, host_in):
+            d.copy_(h, non_blocking=True)
+        job.step(dev_in)
+        d2h[0] = job.read_result(host_out)
 
     e2e_step()
     torch.cuda.synchronize()
@@ -345,30 +536,31 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
     clk = clocks.stop()
 
     # ---- max over ranks
-    t = torch.tensor([ms, e2e_ms, -(n_local * BYTES_PER_ROW / (kms / max(klaunches, 1) / 1e3) / 1e9 if kms > 0 else 0.0),
-                      float(launches)], dtype=torch.float64, device=dev)
+    kern_gbs = kbytes / args.steps / (kms / max(klaunches, 1) / 1e3) / 1e9 if kms > 0 else 0.0
+    t = torch.tensor([ms, e2e_ms, -kern_gbs, float(launches), float(h2d), float(d2h[0])], dtype=torch.float64,
+                     device=dev)
     if dist is not None:
         mx = t[:3].clone()
         dist.all_reduce(mx, op=dist.ReduceOp.MAX)
         sm = t[3:].clone()
         dist.all_reduce(sm, op=dist.ReduceOp.SUM)
         t = torch.cat([mx, sm])
-    ms_max, e2e_ms_max, neg_ach, launches_total = t.tolist()
+    ms_max, e2e_ms_max, neg_ach, launches_total, h2d_total, d2h_total = t.tolist()
     achieved = -neg_ach  # the slowest rank's kernel bandwidth
 
     if rank != 0:
         return
+    bpr = job.bpr
     value = n_rows * args.steps / (ms_max / 1e3)
     peak, peak_kind = measured_peak()
-    tpr, tsrc = traffic_per_row()
+    tm, tsrc = traffic_model(args.workload)
     line = base_line(args, wl, n_rows, world)
     line.update({
         "value": value,
         "ms_per_step": ms_max / args.steps,
         "impl": "ours",
         "e2e": {"value": n_rows * e2e_steps / (e2e_ms_max / 1e3), "unit": "rows/s",
-                "h2d_bytes_per_step": n_rows * BYTES_PER_ROW,
-                "d2h_bytes_per_step": world * len(out) * G * 8, "steps": e2e_steps},
+                "h2d_bytes_per_step": int(h2d_total), "d2h_bytes_per_step": int(d2h_total), "steps": e2e_steps},
         "gpu_launches": int(launches_total),
         "roofline": {
             "bound": "hbm",
@@ -378,27 +570,26 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
                            "fallback 6.65 TB/s",
             "unit": "GB/s",
             "frac": achieved / peak,
-            "traffic": (tpr[0] * n_local + tpr[1]) if tpr else None,
+            "traffic": (tm[0] * n_local + tm[1]) if tm else None,
             "traffic_source": tsrc,
-            "kernel": "dense_moments_kernel",
-            "algorithmic_bytes_per_launch": n_local * BYTES_PER_ROW,
+            "kernel": job.kernel,
+            "algorithmic_bytes_per_launch": kbytes / args.steps,
             "kernel_ms_avg": kms / max(klaunches, 1),
         },
-        "hbm_gbs_job": n_rows * BYTES_PER_ROW / (ms_max / args.steps / 1e3) / 1e9,
+        "hbm_gbs_job": n_rows * bpr / (ms_max / args.steps / 1e3) / 1e9,
         "clocks": clk,
         "device": ctx.name,
     })
     if world == 1 and not args.no_cpu_baseline:
-        import oracle
-
         threads = cpu_threads()
-        sample = cpu_sample_rows(wl, args.cpu_seconds, threads)
-        k, v = host_inputs(wl, 0, sample)
+        sample = cpu_sample_rows(wl, args.cpu_seconds, threads, n_rows)
+        cols = host_inputs(wl, 0, sample)
         t0 = time.perf_counter()
-        oracle.moments_grouped_mt(v, k, G, threads=threads)
+        cpu_groupby(wl, cols, threads)
         dt = time.perf_counter() - t0
+        how = ("exact Kulisch groupby" if wl["kind"] == "dense" else "sort-based exact groupby of int64 keys")
         line["cpu_baseline"] = {"value": sample / dt, "unit": "rows/s", "cores": threads, "kind": "port",
-                                "sample": f"first {sample} rows of the workload, exact Kulisch groupby "
+                                "sample": f"first {sample} rows of the workload, {how} "
                                           f"(oracle port of the reference's CPU path), {threads} threads"}
     print(json.dumps(line), flush=True)
 
@@ -407,6 +598,9 @@ def main():
     args = parse()
     wl = dict(WORKLOADS[args.workload])
     n_rows = args.rows or wl["rows"]
+    if args.ids is not None and "ids" in wl:
+        wl["ids"] = args.ids
+        wl["desc"] += f" (distinct ids overridden: {args.ids})"
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))

@@ -156,6 +156,19 @@ tbgb_status tbgb_groupby_hash(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb_c
                               const uint64_t* d_mask, int64_t n, int64_t max_groups, int64_t* d_out_keys,
                               const tbgb_moments* out, int64_t* d_n_groups, void* stream);
 
+/* ---- sharded int64-key groupby (one process / GPU per shard) ----------------------
+ * Routes the rows of this shard that pass mask and pred to their owner part
+ * owner(key) = (fmix64(key) >> 32) % n_parts (fmix64: MurmurHash3's 64-bit
+ * finaliser), 1 <= n_parts <= 32: the rows of part p are written to
+ * d_out_keys / d_out_vals (v = expr(a, b, c) in f64) starting at the sum of the
+ * counts of parts < p, in row order; d_part_counts[p] (device memory) receives part
+ * p's row count.  Output buffers hold up to n rows.  The caller exchanges the parts
+ * (e.g. an NCCL all-to-all, senders concatenated in rank order) and runs
+ * tbgb_groupby_hash on what it received: each shard then holds the groups it owns. */
+tbgb_status tbgb_hash_partition(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb_columns* cols,
+                                const uint64_t* d_mask, int64_t n, int32_t n_parts, int64_t* d_out_keys,
+                                double* d_out_vals, int64_t* d_part_counts, void* stream);
+
 /* How the global-table kernel treats rows: 0 = choose by size (default), 1 = always
  * pre-aggregate in a per-CTA shared-memory table (skewed keys), 2 = always update the
  * global table directly (uniform high-cardinality keys). */

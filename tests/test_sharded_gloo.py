@@ -1,0 +1,191 @@
+"""Host logic of the row-sharded paths (winrapids_b200.sharded) on world_size-2 gloo
+process groups, CPU only.  The GPU kernels are stood in for by oracle-based fakes with
+the same methods as winrapids_b200.Context, so what is tested is the collective
+choreography: split sizes, rank order of the exchanged parts, state gathering and
+folding order, and that a rank whose receive buffer is too small fails on every rank
+instead of hanging."""
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+import oracle
+
+WORLD = 2
+
+
+def free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def owner_np(keys, P):
+    k = np.asarray(keys).view(np.uint64).copy()
+    with np.errstate(over="ignore"):
+        k ^= k >> np.uint64(33)
+        k *= np.uint64(0xFF51AFD7ED558CCD)
+        k ^= k >> np.uint64(33)
+        k *= np.uint64(0xC4CEB9FE1A85EC53)
+        k ^= k >> np.uint64(33)
+    return ((k >> np.uint64(32)) % np.uint64(P)).astype(np.int64)
+
+
+class FakeCtx:
+    """CPU stand-in for winrapids_b200.Context: same method names and buffer contracts."""
+
+    # hash path ------------------------------------------------------------------------
+    def hash_partition(self, keys, a, n_parts, out_keys, out_vals, part_counts, b=None, c=None, expr="a",
+                       pred=None, threshold=0.0, mask=None):
+        k = keys.numpy()
+        v = a.numpy().astype(np.float64)
+        own = owner_np(k, n_parts)
+        order = np.argsort(own, kind="stable")
+        out_keys[:k.size] = torch.from_numpy(k[order])
+        out_vals[:k.size] = torch.from_numpy(v[order])
+        part_counts[:] = torch.from_numpy(np.bincount(own, minlength=n_parts).astype(np.int64))
+
+    def groupby_hash_into(self, keys, a, max_groups, out_keys, out, n_groups, **kw):
+        res = oracle.groupby_i64(keys.numpy(), a.numpy().astype(np.float64))
+        g = res["keys"].size
+        out_keys[:g] = torch.from_numpy(res["keys"])
+        out["count"][:g] = torch.from_numpy(res["counts"])
+        out["sum"][:g] = torch.from_numpy(res["sums"])
+        n_groups[0] = g
+
+    def sync(self):
+        pass
+
+    # dense path: state = (count, exact sum, min, max) per group, folded in rank order --
+    def state_bytes(self, G):
+        return 4 * G * 8
+
+    def groupby_dense_state(self, keys, vals, G, row_offset=0, mask=None, state=None):
+        st = oracle.moments_grouped_mt(vals.numpy(), keys.numpy(), G, threads=1)
+        s = state.view(4, G)
+        for i, f in enumerate(("counts", "sums", "mins", "maxs")):
+            s[i] = torch.from_numpy(st[f])
+
+    def merge_states(self, states, n_states, G, out=None):
+        s = states.view(n_states, 4, G).numpy()
+        out["count"][:] = torch.from_numpy(s[:, 0].sum(axis=0))
+        tot = np.zeros(G)
+        for r in range(n_states):  # rank order
+            tot = tot + s[r, 1]
+        out["sum"][:] = torch.from_numpy(tot)
+        out["min"][:] = torch.from_numpy(s[:, 2].min(axis=0))
+        out["max"][:] = torch.from_numpy(s[:, 3].max(axis=0))
+
+
+def _init(rank, port):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+
+
+def _hash_worker(rank, port, n, ids, q):
+    from winrapids_b200.sharded import ShardedHashGroupby
+
+    _init(rank, port)
+    try:
+        keys = oracle.gen_keys_ids(n, ids, 77, 3)
+        vals = oracle.gen_values_normal(n, 0.0, 1.0, 3)
+        lo, hi = n * rank // WORLD, n * (rank + 1) // WORLD
+        sh = ShardedHashGroupby(FakeCtx(), dist, WORLD, hi - lo, ids, ("count", "sum"), "cpu")
+        sh.step(torch.from_numpy(keys[lo:hi]), torch.from_numpy(vals[lo:hi]))
+        gk, out = sh.result()
+        q.put((rank, gk.numpy().copy(), out["count"].numpy().copy(), out["sum"].numpy().copy(), sh.n_recv))
+    finally:
+        dist.destroy_process_group()
+
+
+def _small_buffer_worker(rank, port, q):
+    from winrapids_b200.sharded import exchange_parts
+
+    _init(rank, port)
+    try:
+        n = 1000
+        pk = torch.arange(n, dtype=torch.int64)
+        pv = torch.zeros(n, dtype=torch.float64)
+        # rank 0 sends everything to rank 1, whose receive buffer holds 10 rows
+        pc = torch.tensor([0, n] if rank == 0 else [0, 0], dtype=torch.int64)
+        cap = 10 if rank == 1 else n
+        try:
+            exchange_parts(dist, pk, pv, pc, torch.empty(cap, dtype=torch.int64), torch.empty(cap), )
+            q.put((rank, "no error"))
+        except RuntimeError as e:
+            q.put((rank, "raised" if "too small" in str(e) else str(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def _dense_worker(rank, port, n, G, q):
+    from winrapids_b200.sharded import ShardedDenseGroupby
+
+    _init(rank, port)
+    try:
+        keys = oracle.gen_keys_uniform(n, G, 5)
+        vals = oracle.gen_values_uniform(n, -1.0, 1.0, 5)
+        lo, hi = n * rank // WORLD, n * (rank + 1) // WORLD
+        out = {f: torch.empty(G, dtype=torch.float64) for f in ("count", "sum", "min", "max")}
+        sh = ShardedDenseGroupby(FakeCtx(), dist, WORLD, G, out, "cpu")
+        sh.step(torch.from_numpy(keys[lo:hi]), torch.from_numpy(vals[lo:hi]), lo)
+        q.put((rank, {f: t.numpy().copy() for f, t in out.items()}))
+    finally:
+        dist.destroy_process_group()
+
+
+def _spawn(fn, *args):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=fn, args=(r, *args, q)) for r in range(WORLD)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(WORLD)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return sorted(res, key=lambda x: x[0])
+
+
+def test_sharded_hash_groupby_gloo():
+    n, ids = 60_000, 5_000
+    res = _spawn(_hash_worker, free_port(), n, ids)
+    keys = oracle.gen_keys_ids(n, ids, 77, 3)
+    vals = oracle.gen_values_normal(n, 0.0, 1.0, 3)
+    want = oracle.groupby_i64(keys, vals)
+    gk = np.concatenate([r[1] for r in res])
+    cnt = np.concatenate([r[2] for r in res])
+    sm = np.concatenate([r[3] for r in res])
+    assert sum(r[4] for r in res) == n
+    for rank, k, *_ in res:
+        assert np.all(owner_np(k, WORLD) == rank), "a group on a rank that does not own it"
+    order = np.argsort(gk)
+    assert np.array_equal(gk[order], want["keys"])
+    assert np.array_equal(cnt[order], want["counts"])
+    # the owner sees each key's rows in global row order, so its exact sums are the oracle's
+    assert np.array_equal(sm[order], want["sums"])
+
+
+def test_exchange_rejects_small_receive_buffer_on_all_ranks():
+    res = _spawn(_small_buffer_worker, free_port())
+    assert [r[1] for r in res] == ["raised", "raised"]
+
+
+def test_sharded_dense_gloo():
+    n, G = 50_000, 300
+    res = _spawn(_dense_worker, free_port(), n, G)
+    keys = oracle.gen_keys_uniform(n, G, 5)
+    vals = oracle.gen_values_uniform(n, -1.0, 1.0, 5)
+    want = oracle.moments_grouped_mt(vals, keys, G, threads=1)
+    for _, out in res:  # every rank holds the merged result
+        assert np.array_equal(out["count"], want["counts"])
+        assert np.array_equal(out["min"], want["mins"]) and np.array_equal(out["max"], want["maxs"])
+        absum = np.bincount(keys, weights=np.abs(vals), minlength=G)
+        assert np.all(np.abs(out["sum"] - want["sums"]) <= 1e-12 * absum)

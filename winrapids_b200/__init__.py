@@ -153,6 +153,25 @@ class Context:
             self.sync(stream)
         return out
 
+    def groupby_hash_into(self, keys, a, max_groups: int, out_keys, out: dict, n_groups, b=None, c=None,
+                          expr: str = "a", pred: str | None = None, threshold: float = 0.0, mask=None,
+                          stream=None):
+        """Enqueue an int64-key groupby into caller-owned device buffers (no host synchronisation):
+        out_keys (int64, max_groups), out {field: f64 tensor}, n_groups (int64, 1 element)."""
+        n = int(keys.numel())
+        cols = self.columns(a, b, c, expr, pred, threshold)
+        m = self.moments_struct(out)
+        self._check(self._L.tbgb_groupby_hash(self._h, _ptr(keys), C.byref(cols), _ptr(mask), n, int(max_groups),
+                                              _ptr(out_keys), C.byref(m), _ptr(n_groups), _stream_handle(stream)))
+
+    def hash_partition(self, keys, a, n_parts: int, out_keys, out_vals, part_counts, b=None, c=None,
+                       expr: str = "a", pred: str | None = None, threshold: float = 0.0, mask=None, stream=None):
+        """Enqueue the owner routing of this shard's rows (see tbgb_hash_partition)."""
+        cols = self.columns(a, b, c, expr, pred, threshold)
+        self._check(self._L.tbgb_hash_partition(self._h, _ptr(keys), C.byref(cols), _ptr(mask), int(keys.numel()),
+                                                int(n_parts), _ptr(out_keys), _ptr(out_vals), _ptr(part_counts),
+                                                _stream_handle(stream)))
+
     def groupby_hash(self, keys, a, max_groups: int, b=None, c=None, expr: str = "a", pred: str | None = None,
                      threshold: float = 0.0, mask=None, fields=MOMENT_FIELDS, stream=None):
         """int64-key groupby; returns (group keys, {field: tensor}) trimmed to the group count

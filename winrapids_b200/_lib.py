@@ -105,6 +105,7 @@ def lib() -> C.CDLL:
         "tbgb_groupby_dense_columns": (st, [vp, vp, C.POINTER(Columns), vp, i64, i32, C.POINTER(Moments), vp]),
         "tbgb_groupby_hash": (st, [vp, vp, C.POINTER(Columns), vp, i64, i64, vp, C.POINTER(Moments), vp, vp]),
         "tbgb_set_table_mode": (st, [vp, C.c_int]),
+        "tbgb_hash_partition": (st, [vp, vp, C.POINTER(Columns), vp, i64, i32, vp, vp, vp, vp]),
         "tbgb_gen_keys_uniform": (st, [vp, vp, i64, i32, u64, i64, vp]),
         "tbgb_gen_values_uniform": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
         "tbgb_gen_values_normal": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
@@ -128,5 +129,5 @@ HEADER_SYMBOLS = (
     "tbgb_state_bytes", "tbgb_groupby_dense_state", "tbgb_merge_states", "tbgb_workspace_bytes",
     "tbgb_launch_count", "tbgb_profile_enable", "tbgb_kernel_time_ms", "tbgb_gen_keys_uniform", "tbgb_gen_values_uniform", "tbgb_gen_values_normal",
     "tbgb_gen_inject_nonfinite", "tbgb_groupby_dense_columns", "tbgb_groupby_hash", "tbgb_set_table_mode",
-    "tbgb_gen_keys_cdf", "tbgb_gen_keys_ids", "tbgb_gen_values_lognormal_f32",
+    "tbgb_gen_keys_cdf", "tbgb_gen_keys_ids", "tbgb_gen_values_lognormal_f32", "tbgb_hash_partition",
 )

@@ -10,6 +10,7 @@
 #include "dense.cuh"
 #include "errbits.hpp"
 #include "gen.cuh"
+#include "partition.cuh"
 #include "table.cuh"
 #include "tambear_gb.h"
 
@@ -357,6 +358,36 @@ tbgb_status tbgb_merge_states(tbgb_ctx* ctx, const void* d_states, int32_t n_sta
   cudaError_t e = tbgb::merge_states_launch(static_cast<const double*>(d_states), n_states, n_groups, out,
                                             static_cast<cudaStream_t>(stream), &ctx->launches);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "merge_states launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_hash_partition(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb_columns* cols,
+                                const uint64_t* d_mask, int64_t n, int32_t n_parts, int64_t* d_out_keys,
+                                double* d_out_vals, int64_t* d_part_counts, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (n < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (n_parts < 1 || n_parts > tbgb::kMaxParts)
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_parts must be in [1, 32]");
+  if (!d_part_counts) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "part_counts is NULL");
+  if (n > 0 && (!d_keys || !d_out_keys || !d_out_vals))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "keys / output pointers are NULL");
+  tbgb_status st = check_columns(ctx, cols, n);
+  if (st != TBGB_OK) return st;
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  st = ensure_ws(ctx, tbgb::partition_scratch_bytes(n, n_parts));
+  if (st != TBGB_OK) return st;
+  tbgb::PartitionArgs a{};
+  a.keys = d_keys;
+  a.cols = *cols;
+  a.mask = d_mask;
+  a.n = n;
+  a.P = n_parts;
+  a.out_keys = d_out_keys;
+  a.out_vals = d_out_vals;
+  cudaError_t e = tbgb::partition_launch(a, static_cast<unsigned long long*>(ctx->ws), d_part_counts,
+                                         static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "hash partition launch", e);
   return TBGB_OK;
 }
 

@@ -1,0 +1,108 @@
+"""Row-sharded execution over one process per GPU (torch.distributed, NCCL over NVLink).
+
+Low cardinality (dense keys): every shard reduces its rows to a mergeable per-group
+state table (``Context.groupby_dense_state``), the tables are all-gathered and folded
+in rank order (``Context.merge_states``) -- a few KB per GPU, latency-bound.
+
+High cardinality (int64 keys): every shard routes its rows to the owner of their key
+(``Context.hash_partition``, a stable partition with the filter and expression applied),
+one all-to-all moves each owner's rows to it (senders concatenated in rank order, so
+every key's rows keep their global order), and the owner groups what it received
+(``Context.groupby_hash``).  The result is sharded by owner.  Raw rows are shipped
+rather than per-shard partial tables: with 2^28 distinct keys a shard's partial table
+is about as large as its rows, and the owner's table is 1/world of the full one.
+
+The collective calls take any ``torch.distributed`` group, so the same code runs on
+gloo with CPU tensors in the CPU test suite.
+"""
+from __future__ import annotations
+
+
+def exchange_parts(dist, part_keys, part_vals, part_counts, recv_keys, recv_vals, group=None) -> int:
+    """All-to-all of owner parts.  part_counts[p] rows of part p lie contiguously (in owner
+    order) in part_keys / part_vals; rows received from rank r land after those of ranks < r.
+    Returns the number of rows received; raises if they do not fit the receive buffers."""
+    import torch
+
+    send_counts = part_counts.to(torch.int64)
+    recv_counts = torch.empty_like(send_counts)
+    dist.all_to_all_single(recv_counts, send_counts, group=group)
+    s = [int(x) for x in send_counts.tolist()]
+    r = [int(x) for x in recv_counts.tolist()]
+    n_send, n_recv = sum(s), sum(r)
+    # every rank takes the same collective steps, so a rank whose buffers are too small
+    # still joins the exchange and raises afterwards
+    fits = torch.tensor([1 if n_recv <= recv_keys.numel() and n_recv <= recv_vals.numel() else 0],
+                        dtype=torch.int64, device=send_counts.device)
+    dist.all_reduce(fits, op=dist.ReduceOp.MIN, group=group)
+    if int(fits.item()) == 0:
+        raise RuntimeError(f"receive buffers too small on some rank (this rank needs {n_recv} rows)")
+    dist.all_to_all_single(recv_keys[:n_recv], part_keys[:n_send], r, s, group=group)
+    dist.all_to_all_single(recv_vals[:n_recv], part_vals[:n_send], r, s, group=group)
+    return n_recv
+
+
+class ShardedDenseGroupby:
+    """Row-sharded dense-key groupby: shard state -> all-gather -> fold in rank order.
+
+    ``ctx`` is a ``winrapids_b200.Context`` (or an object with the same ``state_bytes`` /
+    ``groupby_dense_state`` / ``merge_states`` methods); ``out`` holds the merged outputs
+    on every rank."""
+
+    def __init__(self, ctx, dist, world: int, n_groups: int, out: dict, device, group=None):
+        import torch
+
+        self.ctx, self.dist, self.world, self.G, self.group = ctx, dist, int(world), int(n_groups), group
+        words = ctx.state_bytes(n_groups) // 8
+        self.st_local = torch.empty(words, dtype=torch.float64, device=device)
+        self.gathered = torch.empty(self.world * words, dtype=torch.float64, device=device)
+        self.out = out
+
+    def step(self, keys, vals, row_offset: int, mask=None):
+        self.ctx.groupby_dense_state(keys, vals, self.G, row_offset=row_offset, mask=mask, state=self.st_local)
+        self.dist.all_gather_into_tensor(self.gathered, self.st_local, group=self.group)
+        self.ctx.merge_states(self.gathered, self.world, self.G, out=self.out)
+
+
+class ShardedHashGroupby:
+    """Owner-sharded int64-key groupby of one shard's rows (see the module docstring).
+
+    ``ctx`` is a ``winrapids_b200.Context`` (or an object with the same ``hash_partition`` /
+    ``groupby_hash_into`` methods).  Buffers are allocated once for shards of up to
+    ``max_rows`` rows, receive buffers with ``recv_slack`` headroom over an even share.
+    """
+
+    def __init__(self, ctx, dist, world: int, max_rows: int, max_groups_per_owner: int, fields, device,
+                 recv_slack: float = 1.25, group=None):
+        import torch
+
+        self.ctx, self.dist, self.world, self.group = ctx, dist, int(world), group
+        self.max_groups = int(max_groups_per_owner)
+        cap = int(max_rows * recv_slack) + 4096
+        self.part_keys = torch.empty(max_rows, dtype=torch.int64, device=device)
+        self.part_vals = torch.empty(max_rows, dtype=torch.float64, device=device)
+        self.part_counts = torch.zeros(self.world, dtype=torch.int64, device=device)
+        self.recv_keys = torch.empty(cap, dtype=torch.int64, device=device)
+        self.recv_vals = torch.empty(cap, dtype=torch.float64, device=device)
+        self.out_keys = torch.empty(self.max_groups, dtype=torch.int64, device=device)
+        self.out = {f: torch.empty(self.max_groups, dtype=torch.float64, device=device) for f in fields}
+        self.n_groups = torch.zeros(1, dtype=torch.int64, device=device)
+        self.n_recv = 0
+
+    def step(self, keys, a, b=None, c=None, expr: str = "a", pred=None, threshold: float = 0.0, mask=None):
+        """Route, exchange and group one shard; results stay in self.out_keys / self.out (the
+        first self.n_groups entries)."""
+        if keys.numel() > self.part_keys.numel():
+            raise ValueError("shard larger than the buffers")
+        self.ctx.hash_partition(keys, a, self.world, self.part_keys, self.part_vals, self.part_counts, b=b, c=c,
+                                expr=expr, pred=pred, threshold=threshold, mask=mask)
+        self.n_recv = exchange_parts(self.dist, self.part_keys, self.part_vals, self.part_counts, self.recv_keys,
+                                     self.recv_vals, group=self.group)
+        self.ctx.groupby_hash_into(self.recv_keys[:self.n_recv], self.recv_vals[:self.n_recv], self.max_groups,
+                                   self.out_keys, self.out, self.n_groups)
+
+    def result(self):
+        """(keys, {field: values}) of the groups this rank owns (host synchronisation)."""
+        self.ctx.sync()
+        g = int(self.n_groups.item())
+        return self.out_keys[:g], {f: v[:g] for f, v in self.out.items()}
