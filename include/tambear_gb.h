@@ -27,6 +27,13 @@
  *                                   moments_grouped for int64 keys: the reference factorises keys on
  *                                   the host and accepts i32 codes only; here an open-addressing table
  *                                   in HBM groups arbitrary int64 keys in the same pass
+ *   tbgb_scatter_phi /              ComputeEngine::scatter_phi / scatter_multi_phi /
+ *   tbgb_scatter_multi_phi_masked / scatter_phi_masked (crates/tambear/src/compute_engine.rs:109-154,
+ *   tbgb_scatter_extremum           CPU :252-302) and ScatterJit::scatter_multi_phi_masked
+ *                                   (scatter_jit.rs:402-495); ComputeEngine::scatter_extremum
+ *                                   (compute_engine.rs:165-178, CPU :304-322).  These are the
+ *                                   entry names the reference's TamGpu dispatches by (scatter_phi,
+ *                                   scatter_multi_phi, scatter_phi_masked, scatter_extremum)
  *   tbgb_hash_partition             no counterpart in the reference (single GPU); routes rows to
  *                                   the GPU that owns their key for the sharded high-cardinality path
  *
@@ -155,6 +162,45 @@ tbgb_status tbgb_groupby_dense_columns(tbgb_ctx* ctx, const int32_t* d_keys, con
 tbgb_status tbgb_groupby_hash(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb_columns* cols,
                               const uint64_t* d_mask, int64_t n, int64_t max_groups, int64_t* d_out_keys,
                               const tbgb_moments* out, int64_t* d_n_groups, void* stream);
+
+/* ---- scatter primitives over dense int32 keys ----------------------------------------
+ * phi expressions of the reference's phi_scatter_eval (compute_engine.rs:593-609), r =
+ * refs[key] (0.0 when refs is NULL), each operation rounded separately: */
+typedef enum {
+  TBGB_PHI_V = 0,        /* v                       */
+  TBGB_PHI_VV = 1,       /* v * v                   */
+  TBGB_PHI_ONE = 2,      /* 1.0                     */
+  TBGB_PHI_VMR = 3,      /* v - r                   */
+  TBGB_PHI_VMR2 = 4,     /* (v - r) * (v - r)       */
+  TBGB_PHI_ABS_VMR = 5,  /* fabs(v - r)             */
+  TBGB_PHI_VMR3 = 6,     /* (v - r)^3 as (d * d) * d */
+  TBGB_PHI_VMR4 = 7,     /* (v - r)^4 as d2 * d2    */
+  TBGB_PHI_VR = 8,       /* v * r                   */
+  TBGB_PHI_LOG = 9,      /* log(v)                  */
+  TBGB_PHI_RECIP = 10    /* 1.0 / v                 */
+} tbgb_phi;
+
+/* out[j * n_groups + g] = sum over rows i with keys[i] == g (and mask bit i set, when
+ * d_mask is not NULL) of phis[j](vals[i], refs[g]), over the finite nonzero terms (the
+ * reference's CPU accumulator skips +-0, NaN and +-inf terms), f64 accumulation.
+ * 1 <= n_phi <= 5.  Every row's key must lie in [0, n_groups) (masked-out rows are not
+ * checked), else tbgb_sync reports TBGB_ERR_KEY_OUT_OF_RANGE.  Unknown phi ids:
+ * TBGB_ERR_ENTRY_NOT_FOUND. */
+tbgb_status tbgb_scatter_multi_phi_masked(tbgb_ctx* ctx, const int32_t* phis, int32_t n_phi, const int32_t* d_keys,
+                                          const double* d_vals, const double* d_refs, const uint64_t* d_mask,
+                                          int64_t n, int32_t n_groups, double* d_out, void* stream);
+tbgb_status tbgb_scatter_phi(tbgb_ctx* ctx, int32_t phi, const int32_t* d_keys, const double* d_vals,
+                             const double* d_refs, int64_t n, int32_t n_groups, double* d_out, void* stream);
+tbgb_status tbgb_scatter_multi_phi(tbgb_ctx* ctx, const int32_t* phis, int32_t n_phi, const int32_t* d_keys,
+                                   const double* d_vals, const double* d_refs, int64_t n, int32_t n_groups,
+                                   double* d_out, void* stream);
+tbgb_status tbgb_scatter_phi_masked(tbgb_ctx* ctx, int32_t phi, const int32_t* d_keys, const double* d_vals,
+                                    const double* d_refs, const uint64_t* d_mask, int64_t n, int32_t n_groups,
+                                    double* d_out, void* stream);
+/* out[g] = min (is_max == 0) or max of the non-NaN values of group g by a strict scan in
+ * row order (+-0 ties: the first zero), +inf / -inf for groups without one. */
+tbgb_status tbgb_scatter_extremum(tbgb_ctx* ctx, int32_t is_max, const int32_t* d_keys, const double* d_vals,
+                                  int64_t n, int32_t n_groups, double* d_out, void* stream);
 
 /* ---- sharded int64-key groupby (one process / GPU per shard) ----------------------
  * Routes the rows of this shard that pass mask and pred to their owner part

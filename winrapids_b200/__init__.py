@@ -20,6 +20,7 @@ from ._lib import (DTYPES, EXPRS, MOMENT_FIELDS, PREDS, Columns, InvalidArgument
                    TableFull, TambearGbError, error_for, lib)
 
 __all__ = [
+    "ComputeEngine", "AccumulateEngine", "HashScatterEngine", "GroupByResult", "Grouping", "Op",
     "Context", "DescriptiveEngine", "GroupedMomentStats", "MomentStats", "TambearGbError", "KeyOutOfRange",
     "InvalidArgument", "TableFull", "MOMENT_FIELDS", "SUMCOUNT_FIELDS",
 ]
@@ -336,3 +337,6 @@ class DescriptiveEngine:
 
     def mean_grouped(self, values, keys, n_groups: int) -> np.ndarray:
         return self.moments_grouped(values, keys, n_groups).means()
+
+
+from .engines import AccumulateEngine, ComputeEngine, GroupByResult, Grouping, HashScatterEngine, Op  # noqa: E402

@@ -106,6 +106,11 @@ def lib() -> C.CDLL:
         "tbgb_groupby_hash": (st, [vp, vp, C.POINTER(Columns), vp, i64, i64, vp, C.POINTER(Moments), vp, vp]),
         "tbgb_set_table_mode": (st, [vp, C.c_int]),
         "tbgb_hash_partition": (st, [vp, vp, C.POINTER(Columns), vp, i64, i32, vp, vp, vp, vp]),
+        "tbgb_scatter_multi_phi_masked": (st, [vp, C.POINTER(i32), i32, vp, vp, vp, vp, i64, i32, vp, vp]),
+        "tbgb_scatter_phi": (st, [vp, i32, vp, vp, vp, i64, i32, vp, vp]),
+        "tbgb_scatter_multi_phi": (st, [vp, C.POINTER(i32), i32, vp, vp, vp, i64, i32, vp, vp]),
+        "tbgb_scatter_phi_masked": (st, [vp, i32, vp, vp, vp, vp, i64, i32, vp, vp]),
+        "tbgb_scatter_extremum": (st, [vp, i32, vp, vp, i64, i32, vp, vp]),
         "tbgb_gen_keys_uniform": (st, [vp, vp, i64, i32, u64, i64, vp]),
         "tbgb_gen_values_uniform": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
         "tbgb_gen_values_normal": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
@@ -130,4 +135,11 @@ HEADER_SYMBOLS = (
     "tbgb_launch_count", "tbgb_profile_enable", "tbgb_kernel_time_ms", "tbgb_gen_keys_uniform", "tbgb_gen_values_uniform", "tbgb_gen_values_normal",
     "tbgb_gen_inject_nonfinite", "tbgb_groupby_dense_columns", "tbgb_groupby_hash", "tbgb_set_table_mode",
     "tbgb_gen_keys_cdf", "tbgb_gen_keys_ids", "tbgb_gen_values_lognormal_f32", "tbgb_hash_partition",
+    "tbgb_scatter_multi_phi_masked", "tbgb_scatter_phi", "tbgb_scatter_multi_phi", "tbgb_scatter_phi_masked",
+    "tbgb_scatter_extremum",
 )
+
+# phi expressions by the reference's source spelling (phi_scatter_eval, compute_engine.rs:593-609)
+PHI_IDS = {"v": 0, "v * v": 1, "1.0": 2, "v - r": 3, "(v - r)": 3, "(v - r) * (v - r)": 4, "fabs(v - r)": 5,
+           "abs(v - r)": 5, "(v - r) * (v - r) * (v - r)": 6, "(v - r) * (v - r) * (v - r) * (v - r)": 7,
+           "v * r": 8, "log(v)": 9, "1.0 / v": 10}

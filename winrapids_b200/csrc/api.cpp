@@ -11,6 +11,7 @@
 #include "errbits.hpp"
 #include "gen.cuh"
 #include "partition.cuh"
+#include "phi.cuh"
 #include "table.cuh"
 #include "tambear_gb.h"
 
@@ -358,6 +359,62 @@ tbgb_status tbgb_merge_states(tbgb_ctx* ctx, const void* d_states, int32_t n_sta
   cudaError_t e = tbgb::merge_states_launch(static_cast<const double*>(d_states), n_states, n_groups, out,
                                             static_cast<cudaStream_t>(stream), &ctx->launches);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "merge_states launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_scatter_multi_phi_masked(tbgb_ctx* ctx, const int32_t* phis, int32_t n_phi, const int32_t* d_keys,
+                                          const double* d_vals, const double* d_refs, const uint64_t* d_mask,
+                                          int64_t n, int32_t n_groups, double* d_out, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (!phis || n_phi < 1 || n_phi > tbgb::kMaxPhi)
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "between 1 and 5 phi expressions per call");
+  for (int j = 0; j < n_phi; ++j)
+    if (phis[j] < TBGB_PHI_V || phis[j] > TBGB_PHI_RECIP)
+      return fail(ctx, TBGB_ERR_ENTRY_NOT_FOUND, "unknown phi id " + std::to_string(phis[j]));
+  if (n < 0 || n_groups < 1) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n must be >= 0 and n_groups >= 1");
+  if (!d_out || (n > 0 && (!d_keys || !d_vals)))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "keys / values / out pointer is NULL");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  cudaError_t e = tbgb::phi_scatter_launch(phis, n_phi, d_keys, d_vals, d_refs, d_mask, n, n_groups, d_out, ctx->err,
+                                           ctx->num_sms, static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "scatter launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_scatter_phi(tbgb_ctx* ctx, int32_t phi, const int32_t* d_keys, const double* d_vals,
+                             const double* d_refs, int64_t n, int32_t n_groups, double* d_out, void* stream) {
+  return tbgb_scatter_multi_phi_masked(ctx, &phi, 1, d_keys, d_vals, d_refs, nullptr, n, n_groups, d_out, stream);
+}
+
+tbgb_status tbgb_scatter_multi_phi(tbgb_ctx* ctx, const int32_t* phis, int32_t n_phi, const int32_t* d_keys,
+                                   const double* d_vals, const double* d_refs, int64_t n, int32_t n_groups,
+                                   double* d_out, void* stream) {
+  return tbgb_scatter_multi_phi_masked(ctx, phis, n_phi, d_keys, d_vals, d_refs, nullptr, n, n_groups, d_out,
+                                       stream);
+}
+
+tbgb_status tbgb_scatter_phi_masked(tbgb_ctx* ctx, int32_t phi, const int32_t* d_keys, const double* d_vals,
+                                    const double* d_refs, const uint64_t* d_mask, int64_t n, int32_t n_groups,
+                                    double* d_out, void* stream) {
+  if (ctx && n > 0 && !d_mask) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "mask is NULL");
+  return tbgb_scatter_multi_phi_masked(ctx, &phi, 1, d_keys, d_vals, d_refs, d_mask, n, n_groups, d_out, stream);
+}
+
+tbgb_status tbgb_scatter_extremum(tbgb_ctx* ctx, int32_t is_max, const int32_t* d_keys, const double* d_vals,
+                                  int64_t n, int32_t n_groups, double* d_out, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (n < 0 || n_groups < 1) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n must be >= 0 and n_groups >= 1");
+  if (!d_out || (n > 0 && (!d_keys || !d_vals)))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "keys / values / out pointer is NULL");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  tbgb_status st = ensure_ws(ctx, static_cast<size_t>(n_groups) * 16);
+  if (st != TBGB_OK) return st;
+  cudaError_t e = tbgb::extremum_launch(is_max != 0, d_keys, d_vals, n, n_groups, d_out,
+                                        static_cast<unsigned long long*>(ctx->ws), ctx->err, ctx->num_sms,
+                                        static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "extremum launch", e);
   return TBGB_OK;
 }
 
