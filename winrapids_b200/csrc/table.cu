@@ -43,7 +43,7 @@ constexpr int LPROBE = 8;           // shared-table probe limit
 constexpr unsigned long long K_UNSET = 0x7FF8000000000001ull;  // NaN payload no finite value has
 
 template <bool FULL>
-__host__ __device__ constexpr int slot_words() { return FULL ? FL_WORDS : SC_WORDS; }
+__host__ __device__ constexpr int slot_words() { return FULL ? int(FL_WORDS) : int(SC_WORDS); }
 
 // Assigns the output row of a newly inserted hash slot.
 __device__ __forceinline__ void assign_id(const TableArgs& a, unsigned long long* p, int wid) {
@@ -469,7 +469,7 @@ unsigned long long next_pow2(unsigned long long x) {
 
 }  // namespace
 
-size_t table_slot_words(bool full) { return full ? FL_WORDS : SC_WORDS; }
+size_t table_slot_words(bool full) { return full ? size_t(FL_WORDS) : size_t(SC_WORDS); }
 
 TablePlan table_plan(bool hash, bool full, int mode, long long groups, int num_sms) {
   TablePlan P{};
