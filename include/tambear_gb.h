@@ -215,9 +215,13 @@ tbgb_status tbgb_hash_partition(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb
                                 const uint64_t* d_mask, int64_t n, int32_t n_parts, int64_t* d_out_keys,
                                 double* d_out_vals, int64_t* d_part_counts, void* stream);
 
-/* How the global-table kernel treats rows: 0 = choose by size (default), 1 = always
- * pre-aggregate in a per-CTA shared-memory table (skewed keys), 2 = always update the
- * global table directly (uniform high-cardinality keys). */
+/* Strategy for groupbys the shared-memory column kernel cannot take alone (int64 keys,
+ * more than 1024 dense groups, filter / expression / f32 columns): 0 = choose by size
+ * (default); 3 = bucket first (dense keys: stable key-range partition into parts of at
+ * most 512 groups, each reduced by the column kernel, up to 16384 groups; int64 keys:
+ * stable partition by high hash bits into sub-tables of about 64 MB); 1 = global table
+ * with per-CTA shared-memory pre-aggregation (skewed keys); 2 = global table, direct
+ * updates (uniform high-cardinality keys).  Modes 1 and 2 never bucket. */
 tbgb_status tbgb_set_table_mode(tbgb_ctx* ctx, int mode);
 
 /* Waits for `stream` and returns the first deferred device error of the calls

@@ -151,6 +151,33 @@ tbgb_status check_columns(tbgb_ctx* ctx, const tbgb_columns* c, int64_t n) {
 
 // Global-table groupby: dense keys (hash == false, `groups` = n_groups) or int64
 // keys (`groups` = max_groups).
+tbgb_columns plain_f64(const double* vals) {
+  tbgb_columns c{};
+  c.a = vals;
+  c.dtype = TBGB_F64;
+  c.expr = TBGB_EXPR_A;
+  c.pred = TBGB_PRED_NONE;
+  return c;
+}
+
+// Bucket count of a hash table: sub-tables of about 64 MB keep a bucket's probes inside
+// L2 and the TLB's reach; at most kMaxParts (the partition's limit).
+int hash_buckets(tbgb_ctx* ctx, bool full, long long groups) {
+  if (ctx->table_mode == 1 || ctx->table_mode == 2) return 1;
+  const tbgb::TablePlan one = tbgb::table_plan(true, full, 0, groups, ctx->num_sms, 1);
+  const size_t target = size_t(64) << 20;
+  if (ctx->table_mode != 3 && one.table_bytes <= 4 * target) return 1;
+  int b = 1;
+  while (b < tbgb::kMaxParts && one.table_bytes / b > target) b <<= 1;
+  return b < 2 ? 2 : b;
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+// Global-table groupby: dense keys (hash == false, `groups` = n_groups) or int64
+// keys (`groups` = max_groups).  int64 keys with a large table are first routed to
+// sub-tables by their high hash bits (a stable partition that also applies the filter
+// and the expression), then each sub-table takes its rows.
 tbgb_status table_common(tbgb_ctx* ctx, bool hash, const void* keys, const tbgb_columns* cols, const uint64_t* mask,
                          int64_t n, long long groups, int64_t row_offset, int64_t* out_keys,
                          const tbgb_moments* out, double* state_out, int64_t* d_n_groups, void* stream) {
@@ -165,42 +192,152 @@ tbgb_status table_common(tbgb_ctx* ctx, bool hash, const void* keys, const tbgb_
   const bool full = state_out != nullptr || wants_full(out);
   DeviceGuard dg(ctx->device);
   if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
-  const tbgb::TablePlan P = tbgb::table_plan(hash, full, ctx->table_mode, groups, ctx->num_sms);
-  st = ensure_ws(ctx, P.table_bytes);
+  const int B = hash ? hash_buckets(ctx, full, groups) : 1;
+  const int mode = ctx->table_mode == 3 ? 0 : ctx->table_mode;
+  const tbgb::TablePlan P = tbgb::table_plan(hash, full, mode, groups, ctx->num_sms, B);
+  // workspace: table | partition scratch | part counts | part starts | routed keys | routed values
+  const size_t t_bytes = align256(P.table_bytes);
+  const size_t sc_bytes = B > 1 ? align256(tbgb::partition_scratch_bytes(n, B)) : 0;
+  const size_t pc_bytes = B > 1 ? 256 : 0;
+  const size_t rows = B > 1 ? tbgb::partition_output_rows(n, B, 1) : 0;
+  const size_t pk_bytes = align256(rows * 8), pv_bytes = align256(rows * 8);
+  const size_t fin_bytes = hash ? align256(tbgb::table_finalize_scratch_bytes(P)) : 0;
+  st = ensure_ws(ctx, t_bytes + sc_bytes + 2 * pc_bytes + pk_bytes + pv_bytes + fin_bytes);
   if (st != TBGB_OK) return st;
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  unsigned long long* T = static_cast<unsigned long long*>(ctx->ws);
-  cudaError_t e = tbgb::table_init(P, T, s, &ctx->launches);
-  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "table init", e);
-  tbgb::TableArgs a{};
-  a.keys = keys;
-  a.cols = *cols;
-  a.mask = mask;
-  a.n = n;
-  a.row_offset = row_offset;
-  a.table = T;
-  a.slots = P.slots;
-  a.ngroups = T + (P.slots + (hash ? 1 : 0)) * tbgb::table_slot_words(full);
-  a.max_groups = groups;
-  a.err = ctx->err;
+  char* w = static_cast<char*>(ctx->ws);
+  unsigned long long* T = reinterpret_cast<unsigned long long*>(w);
+  unsigned long long* scratch = reinterpret_cast<unsigned long long*>(w + t_bytes);
+  int64_t* pcounts = reinterpret_cast<int64_t*>(w + t_bytes + sc_bytes);
+  int64_t* pstarts = reinterpret_cast<int64_t*>(w + t_bytes + sc_bytes + pc_bytes);
+  int64_t* pkeys = reinterpret_cast<int64_t*>(w + t_bytes + sc_bytes + 2 * pc_bytes);
+  double* pvals = reinterpret_cast<double*>(w + t_bytes + sc_bytes + 2 * pc_bytes + pk_bytes);
+  unsigned long long* fin = reinterpret_cast<unsigned long long*>(w + t_bytes + sc_bytes + 2 * pc_bytes + pk_bytes +
+                                                                  pv_bytes);
   cudaEvent_t e0, e1;
   st = profile_events(ctx, &e0, &e1);
   if (st != TBGB_OK) return st;
-  e = tbgb::table_accumulate(P, a, s, &ctx->launches, e0, e1);
-  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "table groupby launch", e);
-  if (hash) e = tbgb::table_finalize_hash(P, T, groups, out_keys, out, d_n_groups, ctx->err, s, &ctx->launches);
+  if (e0) cudaEventRecord(e0, s);
+  cudaError_t e = tbgb::table_init(P, T, s, &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "table init", e);
+  tbgb::TableArgs a{};
+  a.row_offset = row_offset;
+  a.slots = P.slots;
+  a.ngroups = tbgb::table_counter(P, T);
+  a.max_groups = groups;
+  a.err = ctx->err;
+  if (B == 1) {
+    a.keys = keys;
+    a.cols = *cols;
+    a.mask = mask;
+    a.n = n;
+    a.table = T;
+    e = tbgb::table_accumulate(P, a, s, &ctx->launches);
+    if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "table groupby launch", e);
+  } else {
+    tbgb::PartitionArgs pa{};
+    pa.keys = keys;
+    pa.cols = *cols;
+    pa.mask = mask;
+    pa.n = n;
+    pa.P = B;
+    pa.range = false;
+    pa.align_rows = 1;
+    pa.out_keys = pkeys;
+    pa.out_vals = pvals;
+    pa.err = ctx->err;
+    e = tbgb::partition_launch(pa, scratch, pcounts, pstarts, s, &ctx->launches);
+    if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "bucket partition launch", e);
+    a.keys = pkeys;
+    a.cols = plain_f64(pvals);
+    a.mask = nullptr;
+    a.n = 0;
+    for (int b = 0; b < B; ++b) {
+      a.table = tbgb::table_bucket(P, T, b);
+      a.dev_count = pcounts + b;
+      a.dev_start = pstarts + b;
+      e = tbgb::table_accumulate(P, a, s, &ctx->launches);
+      if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "table groupby launch", e);
+    }
+  }
+  if (e1) cudaEventRecord(e1, s);
+  if (hash) e = tbgb::table_finalize_hash(P, T, groups, out_keys, out, d_n_groups, fin, s, &ctx->launches);
   else e = tbgb::table_finalize_dense(P, T, groups, out, state_out, s, &ctx->launches);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "table finalize launch", e);
   return TBGB_OK;
 }
 
-tbgb_columns plain_f64(const double* vals) {
-  tbgb_columns c{};
-  c.a = vals;
-  c.dtype = TBGB_F64;
-  c.expr = TBGB_EXPR_A;
-  c.pred = TBGB_PRED_NONE;
-  return c;
+// Groups per key-range part: the column kernel's two-slot owner variant covers up to 512.
+constexpr int kBucketGroups = 512;
+
+// Key-range bucketing serves dense groupbys of up to kMaxParts * kBucketGroups groups unless the
+// context asks for the table kernel (modes 1 and 2).
+bool use_buckets(const tbgb_ctx* ctx, long long G) {
+  return (ctx->table_mode == 0 || ctx->table_mode == 3) && G <= static_cast<long long>(tbgb::kMaxParts) * kBucketGroups;
+}
+
+// Dense keys in [0, G) with G up to kMaxParts * kBucketGroups (or any filter / expression / f32
+// columns): a stable key-range partition into parts of at most kBucketGroups groups (applying
+// mask, predicate and expression, dropping NaN rows), then the shared-memory column
+// kernel on each part, writing that part's slice of the outputs.
+tbgb_status bucketed_dense(tbgb_ctx* ctx, const int32_t* keys, const tbgb_columns* cols, const uint64_t* mask,
+                           int64_t n, int32_t G, const tbgb_moments* out, void* stream) {
+  if (n > 0 && !keys) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "keys pointer is NULL");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  const int nb = (G + kBucketGroups - 1) / kBucketGroups;
+  const int W = (G + nb - 1) / nb;
+  const tbgb::DenseLaunch L = tbgb::dense_plan(W, ctx->num_sms);
+  DenseWs dw = dense_ws_layout(nullptr, L, W);
+  const int align = 4;  // part starts on 16-byte boundaries of the int32 keys (32 of the values)
+  const size_t rows = tbgb::partition_output_rows(n, nb, align);
+  const size_t sc_bytes = align256(tbgb::partition_scratch_bytes(n, nb));
+  const size_t pk_bytes = align256(rows * 4), pv_bytes = align256(rows * 8);
+  const size_t d_bytes = align256(dw.bytes);
+  tbgb_status st = ensure_ws(ctx, d_bytes + sc_bytes + 512 + pk_bytes + pv_bytes);
+  if (st != TBGB_OK) return st;
+  char* w = static_cast<char*>(ctx->ws);
+  dw = dense_ws_layout(w, L, W);
+  unsigned long long* scratch = reinterpret_cast<unsigned long long*>(w + d_bytes);
+  int64_t* pcounts = reinterpret_cast<int64_t*>(w + d_bytes + sc_bytes);
+  int64_t* pstarts = pcounts + 32;
+  int32_t* pkeys = reinterpret_cast<int32_t*>(w + d_bytes + sc_bytes + 512);
+  double* pvals = reinterpret_cast<double*>(w + d_bytes + sc_bytes + 512 + pk_bytes);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaEvent_t e0, e1;
+  st = profile_events(ctx, &e0, &e1);
+  if (st != TBGB_OK) return st;
+  if (e0) cudaEventRecord(e0, s);
+  tbgb::PartitionArgs pa{};
+  pa.keys = keys;
+  pa.cols = *cols;
+  pa.mask = mask;
+  pa.n = n;
+  pa.P = nb;
+  pa.range = true;
+  pa.width = W;
+  pa.n_groups = G;
+  pa.align_rows = align;
+  pa.out_keys = pkeys;
+  pa.out_vals = pvals;
+  pa.err = ctx->err;
+  cudaError_t e = tbgb::partition_launch(pa, scratch, pcounts, pstarts, s, &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "key-range partition launch", e);
+  for (int b = 0; b < nb; ++b) {
+    const int Gb = (b + 1) * W <= G ? W : G - b * W;
+    const tbgb::DenseLaunch Lb = tbgb::dense_plan(Gb, ctx->num_sms);
+    tbgb_moments ob = *out;
+    double** f[] = {&ob.count, &ob.sum, &ob.min, &ob.max, &ob.mean, &ob.m2, &ob.var_pop, &ob.var_samp};
+    for (double** q : f)
+      if (*q) *q += static_cast<size_t>(b) * W;
+    e = cudaMemsetAsync(dw.zfirst, 0xFF, static_cast<size_t>(Gb) * 8, s);
+    if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "memset", e);
+    e = tbgb::dense_moments_launch(Lb, pkeys, pvals, nullptr, 0, 0, Gb, dw.part, dw.spill, dw.zfirst, ctx->err, &ob,
+                                   nullptr, s, &ctx->launches, nullptr, nullptr, pcounts + b, pstarts + b);
+    if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "dense groupby launch", e);
+  }
+  if (e1) cudaEventRecord(e1, s);
+  return TBGB_OK;
 }
 
 }  // namespace
@@ -289,7 +426,7 @@ size_t tbgb_workspace_bytes(const tbgb_ctx* ctx, int64_t n, int32_t n_groups) {
 
 tbgb_status tbgb_set_table_mode(tbgb_ctx* ctx, int mode) {
   if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
-  if (mode < 0 || mode > 2) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "table mode must be 0, 1 or 2");
+  if (mode < 0 || mode > 3) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "table mode must be 0, 1, 2 or 3");
   ctx->table_mode = mode;
   return TBGB_OK;
 }
@@ -300,6 +437,7 @@ tbgb_status tbgb_groupby_dense(tbgb_ctx* ctx, const int32_t* d_keys, const doubl
   if (n_groups > tbgb::kDenseMaxGroups) {
     if (n > 0 && !d_vals) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "values pointer is NULL");
     const tbgb_columns c = plain_f64(d_vals);
+    if (use_buckets(ctx, n_groups)) return bucketed_dense(ctx, d_keys, &c, d_mask, n, n_groups, out, stream);
     return table_common(ctx, false, d_keys, &c, d_mask, n, n_groups, 0, nullptr, out, nullptr, nullptr, stream);
   }
   return dense_common(ctx, d_keys, d_vals, d_mask, n, n_groups, 0, out, nullptr, stream);
@@ -316,6 +454,8 @@ tbgb_status tbgb_groupby_dense_columns(tbgb_ctx* ctx, const int32_t* d_keys, con
   if (plain && n_groups >= 1 && n_groups <= tbgb::kDenseMaxGroups)
     return dense_common(ctx, d_keys, static_cast<const double*>(cols->a), d_mask, n, n_groups, 0, out, nullptr,
                         stream);
+  if (n_groups >= 1 && use_buckets(ctx, n_groups))
+    return bucketed_dense(ctx, d_keys, cols, d_mask, n, n_groups, out, stream);
   return table_common(ctx, false, d_keys, cols, d_mask, n, n_groups, 0, nullptr, out, nullptr, nullptr, stream);
 }
 
@@ -432,7 +572,8 @@ tbgb_status tbgb_hash_partition(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb
   if (st != TBGB_OK) return st;
   DeviceGuard dg(ctx->device);
   if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
-  st = ensure_ws(ctx, tbgb::partition_scratch_bytes(n, n_parts));
+  const size_t sc_bytes = align256(tbgb::partition_scratch_bytes(n, n_parts));
+  st = ensure_ws(ctx, sc_bytes + 256);
   if (st != TBGB_OK) return st;
   tbgb::PartitionArgs a{};
   a.keys = d_keys;
@@ -440,10 +581,15 @@ tbgb_status tbgb_hash_partition(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb
   a.mask = d_mask;
   a.n = n;
   a.P = n_parts;
+  a.range = false;
+  a.align_rows = 1;
   a.out_keys = d_out_keys;
   a.out_vals = d_out_vals;
-  cudaError_t e = tbgb::partition_launch(a, static_cast<unsigned long long*>(ctx->ws), d_part_counts,
-                                         static_cast<cudaStream_t>(stream), &ctx->launches);
+  a.err = ctx->err;
+  char* w = static_cast<char*>(ctx->ws);
+  cudaError_t e = tbgb::partition_launch(a, reinterpret_cast<unsigned long long*>(w), d_part_counts,
+                                         reinterpret_cast<int64_t*>(w + sc_bytes), static_cast<cudaStream_t>(stream),
+                                         &ctx->launches);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "hash partition launch", e);
   return TBGB_OK;
 }

@@ -104,6 +104,8 @@ struct DenseArgs {
   const uint64_t* mask;  // nullable (MASKED template flag)
   long long n;
   long long row_offset;  // global index of row 0 (zero-tie ordering across shards)
+  const int64_t* dev_count;  // when set: n = *dev_count rows starting at row *dev_start (a partition's part)
+  const int64_t* dev_start;
   int G, C, opg, slots;
   double* part;                // owner partials [ST_COUNT][gridDim.x * TEAMS * slots]
   unsigned long long* spill;   // [gridDim.x][SP_COUNT][G]
@@ -232,8 +234,15 @@ struct OwnerAcc {
 };
 
 template <int MAXSLOTS, bool MASKED, bool TMA>
-__global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
+__global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a_in) {
   extern __shared__ __align__(128) unsigned char smem[];
+  DenseArgs a = a_in;
+  if (a.dev_count) {  // one part of a partition: the part's start keeps the 16-byte alignment of the buffers
+    const long long start = *a.dev_start;
+    a.n = *a.dev_count;
+    a.keys += start;
+    a.vals += start;
+  }
   const int tid = threadIdx.x;
   const int G = a.G, C = a.C;
   const int gp = (G + 3) & ~3;
@@ -659,9 +668,11 @@ static cudaError_t launch_slots(const DenseLaunch& L, const DenseArgs& a, bool m
 cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, const double* vals, const uint64_t* mask,
                                  long long n, long long row_offset, int G, double* part, unsigned long long* spill,
                                  unsigned long long* zfirst, uint32_t* err, const tbgb_moments* out, double* state_out,
-                                 cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start, cudaEvent_t ev_stop) {
+                                 cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start, cudaEvent_t ev_stop,
+                                 const int64_t* dev_count, const int64_t* dev_start) {
   DenseArgs a;
   a.keys = keys; a.vals = vals; a.mask = mask; a.n = n; a.row_offset = row_offset;
+  a.dev_count = dev_count; a.dev_start = dev_start;
   a.G = G; a.C = L.C; a.opg = L.opg; a.slots = L.slots;
   a.part = part; a.spill = spill; a.zfirst = zfirst; a.err = err;
   const bool aligned = (reinterpret_cast<uintptr_t>(keys) % 16 == 0) && (reinterpret_cast<uintptr_t>(vals) % 16 == 0) &&

@@ -37,12 +37,15 @@ size_t dense_smem_bytes(int G, int C);
 
 // Enqueue the dense moments pipeline.  `part` holds part_doubles, `spill`
 // spill_words u64, `zfirst` G u64, `err` one u32.  Writes either final outputs (`out`) or, when `state_out` is not
-// NULL, the merged state table of this call (ST_COUNT * G doubles).
+// NULL, the merged state table of this call (ST_COUNT * G doubles).  With dev_count / dev_start the
+// kernel reads its row count and first row from device memory (one part of a partition; `n` is
+// then ignored and the part start must keep keys and values 16-byte aligned).
 cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, const double* vals, const uint64_t* mask,
                                  long long n, long long row_offset, int G, double* part, unsigned long long* spill,
                                  unsigned long long* zfirst, uint32_t* err, const tbgb_moments* out, double* state_out,
                                  cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start = nullptr,
-                                 cudaEvent_t ev_stop = nullptr);
+                                 cudaEvent_t ev_stop = nullptr, const int64_t* dev_count = nullptr,
+                                 const int64_t* dev_start = nullptr);
 
 cudaError_t merge_states_launch(const double* states, int n_states, int G, const tbgb_moments* out,
                                 cudaStream_t stream, uint64_t* launches);

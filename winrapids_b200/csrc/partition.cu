@@ -1,17 +1,25 @@
-// partition.cu -- routes rows to the GPU that owns their key (sharded high-cardinality
-// groupby).  No counterpart in the reference, which runs on one GPU.
+// partition.cu -- stable partition of rows into parts, for two uses:
+//   * owner routing of int64 keys (sharded high-cardinality groupby; no counterpart in the
+//     reference, which runs on one GPU): part = (fmix64(key) >> 32) % P, the high hash bits,
+//     independent of the low bits a table uses inside a part.  Rows that pass the mask and
+//     the predicate are written as (key, v = expr(a, b, c) in f64); NaN rows are kept (they
+//     still create their key's group).  The same routing buckets one GPU's rows so that each
+//     bucket's table slice is small.
+//   * key-range bucketing of dense int32 keys: part = key / width, written as (key - part *
+//     width, v), so that each part is a dense groupby of at most `width` groups for the
+//     shared-memory column kernel.  NaN rows are dropped (a dense groupby ignores them and
+//     never checks their keys); a non-NaN row whose key is outside [0, n_groups) sets
+//     KERR_KEY_RANGE and is dropped.
+// Each part's rows keep their row order (a stable partition), so every key's rows keep
+// their relative order -- which keeps the +-0 tie rule of the extrema exact downstream.
+// Parts may be padded to start on a multiple of `align_rows` rows (16-byte aligned part
+// starts for the bulk copies of the column kernel).
 //
-// owner(key) = (fmix64(key) >> 32) % n_parts: the high hash bits, independent of the
-// low bits the owner's table slots use.  Rows that pass the mask and the predicate
-// are written as (key, v = expr(a, b, c) in f64) grouped by owner, each owner's rows
-// in row order (a stable partition), so that after an all-to-all that concatenates
-// the senders in rank order every key's rows keep their global order -- which keeps
-// the +-0 tie rule of the extrema exact on the owner.
-//
-// Three launches over fixed tiles of 65,536 rows: per-tile owner counts, one block
-// scanning the [owner][tile] count matrix into write offsets, and the stable scatter
-// (per 1024-row step: one ballot per owner inside each warp, a prefix over the
-// block's warps, rows written at running offset + prefix + rank in warp).
+// Three launches over fixed tiles of 65,536 rows: per-tile part counts, one block scanning
+// the [part][tile] count matrix into write offsets (plus the part counts and padded part
+// starts), and the scatter (per 1024-row step: one ballot per part inside each warp, one
+// warp per part scanning the warps' counts, rows written at running offset + prefix +
+// rank in warp).  Counting uses the same ballots, each lane keeping one part's count.
 #include <cstdint>
 
 #include "common.cuh"
@@ -31,9 +39,9 @@ __device__ __forceinline__ int owner_of(unsigned long long key, int P) {
   return static_cast<int>((fmix64(key) >> 32) % static_cast<unsigned long long>(P));
 }
 
-// Owner of row `row`, or -1 when the row is filtered out; `v` receives its value.
-template <bool F32>
-__device__ __forceinline__ int route_row(const PartitionArgs& a, long long row, unsigned long long* key, double* v) {
+// Part of row `row`, or -1 when the row is dropped; `key` / `v` receive what is written.
+template <bool RANGE, bool F32>
+__device__ __forceinline__ int route_row(const PartitionArgs& a, long long row, long long* key, double* v) {
   if (row >= a.n) return -1;
   if (a.mask && !((__ldg(a.mask + (row >> 6)) >> (row & 63)) & 1ull)) return -1;
   const double av = load_val<F32>(a.cols.a, row);
@@ -42,32 +50,51 @@ __device__ __forceinline__ int route_row(const PartitionArgs& a, long long row, 
   const double bv = expr != TBGB_EXPR_A ? load_val<F32>(a.cols.b, row) : 0.0;
   const double cv = expr == TBGB_EXPR_MUL_ADD ? load_val<F32>(a.cols.c, row) : 0.0;
   *v = eval_expr(expr, av, bv, cv);
-  *key = static_cast<unsigned long long>(__ldcs(a.keys + row));
-  return owner_of(*key, a.P);
+  if constexpr (RANGE) {
+    if (is_nan(*v)) return -1;
+    const int k = __ldcs(static_cast<const int*>(a.keys) + row);
+    if (static_cast<unsigned>(k) >= static_cast<unsigned>(a.n_groups)) {
+      atomicOr(a.err, KERR_KEY_RANGE);
+      return -1;
+    }
+    const int p = k / a.width;
+    *key = k - p * a.width;
+    return p;
+  } else {
+    *key = __ldcs(static_cast<const long long*>(a.keys) + row);
+    return owner_of(static_cast<unsigned long long>(*key), a.P);
+  }
 }
 
-template <bool F32>
+template <bool RANGE, bool F32>
 __global__ void __launch_bounds__(PNT) part_count_kernel(PartitionArgs a, long long ntiles,
                                                          unsigned long long* tile_counts) {
   __shared__ unsigned int cnt[kMaxParts];
   const long long t = blockIdx.x;
+  const int lane = threadIdx.x & 31;
   if (threadIdx.x < a.P) cnt[threadIdx.x] = 0;
   __syncthreads();
   const long long base = t * PTILE;
+  unsigned int mine = 0;  // lane p counts this warp's rows of part p
   for (int s = 0; s < PSTEPS; ++s) {
-    unsigned long long key;
+    long long key;
     double v;
-    const int d = route_row<F32>(a, base + static_cast<long long>(s) * PNT + threadIdx.x, &key, &v);
-    if (d >= 0) atomicAdd(cnt + d, 1u);
+    const int d = route_row<RANGE, F32>(a, base + static_cast<long long>(s) * PNT + threadIdx.x, &key, &v);
+    for (int p = 0; p < a.P; ++p) {
+      const unsigned bal = __ballot_sync(0xffffffffu, d == p);
+      if (lane == p) mine += __popc(bal);
+    }
   }
+  if (lane < a.P && mine) atomicAdd(cnt + lane, mine);
   __syncthreads();
   if (threadIdx.x < a.P) tile_counts[static_cast<long long>(threadIdx.x) * ntiles + t] = cnt[threadIdx.x];
 }
 
-// Exclusive scan of the [P][ntiles] count matrix (owner-major) in one block; writes
-// offsets in place and the per-owner totals.
+// Exclusive scan of the [P][ntiles] count matrix (part-major) in one block; writes the
+// offsets in place (unpadded), the per-part totals and the padded part starts.
 __global__ void __launch_bounds__(SCAN_NT) part_scan_kernel(unsigned long long* counts, long long len, int P,
-                                                            long long ntiles, int64_t* part_counts) {
+                                                            long long ntiles, int align, int64_t* part_counts,
+                                                            int64_t* part_starts) {
   __shared__ unsigned long long warp_sums[SCAN_NT / 32];
   __shared__ unsigned long long carry;
   if (threadIdx.x == 0) carry = 0;
@@ -98,51 +125,88 @@ __global__ void __launch_bounds__(SCAN_NT) part_scan_kernel(unsigned long long* 
     if (threadIdx.x == SCAN_NT - 1) carry = before + x;
     __syncthreads();
   }
-  // per-owner totals: offset of the owner's first tile to the next owner's (or the end)
-  if (threadIdx.x < P) {
-    const int p = threadIdx.x;
-    const unsigned long long start = counts[static_cast<long long>(p) * ntiles];
-    const unsigned long long end = p + 1 < P ? counts[static_cast<long long>(p + 1) * ntiles] : carry;
-    part_counts[p] = static_cast<int64_t>(end - start);
+  if (threadIdx.x == 0) {
+    unsigned long long start = 0;
+    for (int p = 0; p < P; ++p) {
+      const unsigned long long s0 = counts[static_cast<long long>(p) * ntiles];
+      const unsigned long long s1 = p + 1 < P ? counts[static_cast<long long>(p + 1) * ntiles] : carry;
+      part_counts[p] = static_cast<int64_t>(s1 - s0);
+      part_starts[p] = static_cast<int64_t>(start);
+      start += s1 - s0;
+      start = (start + align - 1) / align * align;
+    }
   }
 }
 
-template <bool F32>
+template <bool RANGE, bool F32>
 __global__ void __launch_bounds__(PNT) part_scatter_kernel(PartitionArgs a, long long ntiles,
-                                                           const unsigned long long* __restrict__ offsets) {
-  __shared__ unsigned int wcnt[PNT / 32][kMaxParts];  // per warp, per owner: rows in this step
+                                                           const unsigned long long* __restrict__ offsets,
+                                                           const int64_t* __restrict__ part_starts) {
+  constexpr int NW = PNT / 32;
+  __shared__ unsigned int wcnt[NW][kMaxParts];  // per warp, per part: rows in this step, then their prefix
+  __shared__ unsigned int total[kMaxParts];
   __shared__ unsigned long long running[kMaxParts];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const long long t = blockIdx.x;
   const int P = a.P;
-  if (threadIdx.x < P) running[threadIdx.x] = offsets[static_cast<long long>(threadIdx.x) * ntiles + t];
+  if (threadIdx.x < P) {
+    const long long d = threadIdx.x;
+    running[d] = static_cast<unsigned long long>(part_starts[d]) + offsets[d * ntiles + t] - offsets[d * ntiles];
+  }
   const unsigned lt = (1u << lane) - 1u;
   const long long base = t * PTILE;
   for (int s = 0; s < PSTEPS; ++s) {
-    unsigned long long key = 0;
+    long long key = 0;
     double v = 0.0;
-    const int d = route_row<F32>(a, base + static_cast<long long>(s) * PNT + threadIdx.x, &key, &v);
+    const int d = route_row<RANGE, F32>(a, base + static_cast<long long>(s) * PNT + threadIdx.x, &key, &v);
     unsigned int rank = 0;
     for (int p = 0; p < P; ++p) {
       const unsigned bal = __ballot_sync(0xffffffffu, d == p);
       if (d == p) rank = __popc(bal & lt);
-      if (lane == 0) wcnt[warp][p] = __popc(bal);
+      if (lane == p) wcnt[warp][p] = __popc(bal);
     }
     __syncthreads();
-    // warp w's offset for owner p: rows of warps < w in this step
+    // warp p turns column p of wcnt into exclusive prefixes over the warps (lane = warp index)
+    if (warp < P) {
+      const unsigned c = wcnt[lane][warp];
+      unsigned inc = c;
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+      }
+      wcnt[lane][warp] = inc - c;
+      if (lane == 31) total[warp] = inc;
+    }
+    __syncthreads();
     if (d >= 0) {
-      unsigned long long off = running[d];
-      for (int w = 0; w < warp; ++w) off += wcnt[w][d];
-      a.out_keys[off + rank] = static_cast<int64_t>(key);
-      a.out_vals[off + rank] = v;
+      const unsigned long long off = running[d] + wcnt[warp][d] + rank;
+      if constexpr (RANGE) static_cast<int32_t*>(a.out_keys)[off] = static_cast<int32_t>(key);
+      else static_cast<int64_t*>(a.out_keys)[off] = static_cast<int64_t>(key);
+      a.out_vals[off] = v;
     }
     __syncthreads();
-    if (threadIdx.x < P) {
-      unsigned long long tot = 0;
-      for (int w = 0; w < PNT / 32; ++w) tot += wcnt[w][threadIdx.x];
-      running[threadIdx.x] += tot;
-    }
-    __syncthreads();
+    if (threadIdx.x < P) running[threadIdx.x] += total[threadIdx.x];
+    // the next step's writes of wcnt / total and reads of running are ordered by its first barrier
+  }
+}
+
+template <bool RANGE, bool F32>
+cudaError_t launch_all(const PartitionArgs& a, long long ntiles, unsigned long long* scratch, int64_t* part_counts,
+                       int64_t* part_starts, cudaStream_t s) {
+  part_count_kernel<RANGE, F32><<<static_cast<unsigned int>(ntiles), PNT, 0, s>>>(a, ntiles, scratch);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  part_scan_kernel<<<1, SCAN_NT, 0, s>>>(scratch, ntiles * a.P, a.P, ntiles, a.align_rows, part_counts, part_starts);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  part_scatter_kernel<RANGE, F32><<<static_cast<unsigned int>(ntiles), PNT, 0, s>>>(a, ntiles, scratch, part_starts);
+  return cudaGetLastError();
+}
+
+__global__ void part_empty_kernel(int64_t* part_counts, int64_t* part_starts, int P) {
+  if (threadIdx.x < P) {
+    part_counts[threadIdx.x] = 0;
+    part_starts[threadIdx.x] = 0;
   }
 }
 
@@ -151,24 +215,29 @@ __global__ void __launch_bounds__(PNT) part_scatter_kernel(PartitionArgs a, long
 long long partition_tiles(long long n) { return (n + PTILE - 1) / PTILE; }
 
 size_t partition_scratch_bytes(long long n, int P) {
-  return static_cast<size_t>(partition_tiles(n) > 0 ? partition_tiles(n) : 1) * P * 8;
+  const long long t = partition_tiles(n);
+  return (static_cast<size_t>(t > 0 ? t : 1) * P * 8 + 255) / 256 * 256;
+}
+
+size_t partition_output_rows(long long n, int P, int align_rows) {
+  return static_cast<size_t>(n) + static_cast<size_t>(P) * (align_rows > 1 ? align_rows - 1 : 0);
 }
 
 cudaError_t partition_launch(const PartitionArgs& a, unsigned long long* scratch, int64_t* part_counts,
-                             cudaStream_t s, uint64_t* launches) {
+                             int64_t* part_starts, cudaStream_t s, uint64_t* launches) {
   const long long ntiles = partition_tiles(a.n);
-  if (ntiles == 0) return cudaMemsetAsync(part_counts, 0, static_cast<size_t>(a.P) * 8, s);
+  if (ntiles == 0) {
+    part_empty_kernel<<<1, 32, 0, s>>>(part_counts, part_starts, a.P);
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) (*launches)++;
+    return e;
+  }
   const bool f32 = a.cols.dtype == TBGB_F32;
-  if (f32) part_count_kernel<true><<<static_cast<unsigned int>(ntiles), PNT, 0, s>>>(a, ntiles, scratch);
-  else part_count_kernel<false><<<static_cast<unsigned int>(ntiles), PNT, 0, s>>>(a, ntiles, scratch);
-  cudaError_t e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  part_scan_kernel<<<1, SCAN_NT, 0, s>>>(scratch, ntiles * a.P, a.P, ntiles, part_counts);
-  e = cudaGetLastError();
-  if (e != cudaSuccess) return e;
-  if (f32) part_scatter_kernel<true><<<static_cast<unsigned int>(ntiles), PNT, 0, s>>>(a, ntiles, scratch);
-  else part_scatter_kernel<false><<<static_cast<unsigned int>(ntiles), PNT, 0, s>>>(a, ntiles, scratch);
-  e = cudaGetLastError();
+  cudaError_t e;
+  if (a.range) e = f32 ? launch_all<true, true>(a, ntiles, scratch, part_counts, part_starts, s)
+                       : launch_all<true, false>(a, ntiles, scratch, part_counts, part_starts, s);
+  else e = f32 ? launch_all<false, true>(a, ntiles, scratch, part_counts, part_starts, s)
+               : launch_all<false, false>(a, ntiles, scratch, part_counts, part_starts, s);
   if (e == cudaSuccess) *launches += 3;
   return e;
 }

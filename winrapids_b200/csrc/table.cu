@@ -246,6 +246,17 @@ struct LocalTable {
 template <bool KEY64, bool F32, bool FULL, bool LOCAL>
 __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
   extern __shared__ __align__(16) unsigned char sm[];
+  // The rows: the call's columns, or one part of a partition (plain f64 values, no mask)
+  // whose row count and first row are read from device memory.
+  long long n = a.n;
+  const char* keys = static_cast<const char*>(a.keys);
+  const char* col_a = static_cast<const char*>(a.cols.a);
+  if (a.dev_count) {
+    const long long start = *a.dev_start;
+    n = *a.dev_count;
+    keys += start * (KEY64 ? 8 : 4);
+    col_a += start * (F32 ? 4 : 8);
+  }
   constexpr int W = slot_words<FULL>();
   const int tid = threadIdx.x;
   LocalTable<FULL> lt;
@@ -254,7 +265,6 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
     lt.init(tid);
     __syncthreads();
   }
-  const long long n = a.n;
   const int expr = a.cols.expr, pred = a.cols.pred;
   const double thr = a.cols.threshold;
   const bool need_b = expr != TBGB_EXPR_A, need_c = expr == TBGB_EXPR_MUL_ADD;
@@ -271,8 +281,8 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
       const long long row = base + r * TNT + tid;
       kk[r] = 0; va[r] = 0.0; vb[r] = 0.0; vc[r] = 0.0;
       if (row < n) {
-        kk[r] = load_key<KEY64>(a.keys, row);
-        va[r] = load_val<F32>(a.cols.a, row);
+        kk[r] = load_key<KEY64>(keys, row);
+        va[r] = load_val<F32>(col_a, row);
         if (need_b) vb[r] = load_val<F32>(a.cols.b, row);
         if (need_c) vc[r] = load_val<F32>(a.cols.c, row);
       }
@@ -420,26 +430,112 @@ __global__ void table_finalize_dense_kernel(const unsigned long long* __restrict
   }
 }
 
-__global__ void table_finalize_hash_kernel(const unsigned long long* __restrict__ T, unsigned long long slots,
-                                           int full, long long max_groups, int64_t* out_keys, tbgb_moments out,
-                                           int64_t* n_groups) {
-  const int W = full ? FL_WORDS : SC_WORDS;
-  const int ID = full ? FL_ID : SC_ID;
-  const unsigned long long i0 = blockIdx.x * static_cast<unsigned long long>(blockDim.x) + threadIdx.x;
-  if (i0 == 0) {
-    const unsigned long long c = T[(slots + 1) * W];
-    *n_groups = static_cast<int64_t>(c < static_cast<unsigned long long>(max_groups) ? c : max_groups);
+// ---- compaction of a hash table's occupied slots, in slot order --------------------------
+// Sub-tables of `slots` slots each are followed by their sentinel slot; the distinct-key
+// counter follows the last.  Blocks of FIN_CHUNK slots count their occupied slots, one block
+// scans the counts, then every block writes its groups contiguously from its offset (a
+// ballot-ranked block scan per 256 slots), so the outputs are written in long runs.
+constexpr int FIN_NT = 256;
+constexpr int FIN_CHUNK = FIN_NT * 16;
+
+__device__ __forceinline__ bool slot_occupied(const unsigned long long* T, unsigned long long i,
+                                              unsigned long long slots, int W, int ID) {
+  const unsigned long long* p = T + i * W;
+  return (i % (slots + 1)) < slots ? p[0] != kEmptyKey : p[ID] != kNoId;
+}
+
+__global__ void __launch_bounds__(FIN_NT) table_occ_count_kernel(const unsigned long long* __restrict__ T,
+                                                                 unsigned long long slots, unsigned long long total,
+                                                                 int full, unsigned long long* counts) {
+  const int W = full ? FL_WORDS : SC_WORDS, ID = full ? FL_ID : SC_ID;
+  const unsigned long long i0 = static_cast<unsigned long long>(blockIdx.x) * FIN_CHUNK;
+  unsigned int c = 0;
+  for (int k = 0; k < FIN_CHUNK / FIN_NT; ++k) {
+    const unsigned long long i = i0 + static_cast<unsigned long long>(k) * FIN_NT + threadIdx.x;
+    if (i < total && slot_occupied(T, i, slots, W, ID)) ++c;
   }
-  for (unsigned long long i = i0; i <= slots; i += static_cast<unsigned long long>(gridDim.x) * blockDim.x) {
-    const unsigned long long* p = T + i * W;
-    const unsigned long long key = p[0];
-    const bool occupied = i < slots ? key != kEmptyKey : p[ID] != kNoId;
-    if (!occupied) continue;
-    const unsigned long long id = p[ID];
-    if (id >= static_cast<unsigned long long>(max_groups)) continue;
-    out_keys[id] = static_cast<int64_t>(key);
-    if (full) gstate_finalize(slot_state(p), static_cast<long long>(id), out);
-    else sumcount_finalize(p, static_cast<long long>(id), out);
+  for (int o = 16; o > 0; o >>= 1) c += __shfl_down_sync(0xffffffffu, c, o);
+  __shared__ unsigned int ws[FIN_NT / 32];
+  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = c;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    unsigned long long t = 0;
+    for (int w = 0; w < FIN_NT / 32; ++w) t += ws[w];
+    counts[blockIdx.x] = t;
+  }
+}
+
+// Exclusive scan of `len` counts in one block (in place); the total goes to *n_groups,
+// clipped to max_groups.
+__global__ void __launch_bounds__(1024) table_occ_scan_kernel(unsigned long long* counts, long long len,
+                                                             long long max_groups, int64_t* n_groups) {
+  __shared__ unsigned long long warp_sums[32];
+  __shared__ unsigned long long carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (long long base = 0; base < len; base += 1024) {
+    const long long i = base + threadIdx.x;
+    const unsigned long long x = i < len ? counts[i] : 0ull;
+    unsigned long long inc = x;
+    for (int d = 1; d < 32; d <<= 1) {
+      const unsigned long long y = __shfl_up_sync(0xffffffffu, inc, d);
+      if (lane >= d) inc += y;
+    }
+    if (lane == 31) warp_sums[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+      unsigned long long w = warp_sums[lane];
+      for (int d = 1; d < 32; d <<= 1) {
+        const unsigned long long y = __shfl_up_sync(0xffffffffu, w, d);
+        if (lane >= d) w += y;
+      }
+      warp_sums[lane] = w;
+    }
+    __syncthreads();
+    const unsigned long long before = carry + (warp > 0 ? warp_sums[warp - 1] : 0ull) + inc - x;
+    if (i < len) counts[i] = before;
+    __syncthreads();
+    if (threadIdx.x == 1023) carry = before + x;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0)
+    *n_groups = static_cast<int64_t>(carry < static_cast<unsigned long long>(max_groups) ? carry : max_groups);
+}
+
+__global__ void __launch_bounds__(FIN_NT) table_compact_kernel(const unsigned long long* __restrict__ T,
+                                                               unsigned long long slots, unsigned long long total,
+                                                               int full, const unsigned long long* __restrict__ offsets,
+                                                               long long max_groups, int64_t* out_keys,
+                                                               tbgb_moments out) {
+  const int W = full ? FL_WORDS : SC_WORDS, ID = full ? FL_ID : SC_ID;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __shared__ unsigned int wpre[FIN_NT / 32];
+  unsigned long long pos = offsets[blockIdx.x];
+  const unsigned long long i0 = static_cast<unsigned long long>(blockIdx.x) * FIN_CHUNK;
+  for (int k = 0; k < FIN_CHUNK / FIN_NT; ++k) {
+    const unsigned long long i = i0 + static_cast<unsigned long long>(k) * FIN_NT + threadIdx.x;
+    const bool occ = i < total && slot_occupied(T, i, slots, W, ID);
+    const unsigned bal = __ballot_sync(0xffffffffu, occ);
+    if (lane == 0) wpre[warp] = __popc(bal);
+    __syncthreads();
+    unsigned int before = 0, all = 0;
+    for (int w = 0; w < FIN_NT / 32; ++w) {
+      const unsigned int c = wpre[w];
+      before += w < warp ? c : 0u;
+      all += c;
+    }
+    if (occ) {
+      const unsigned long long j = pos + before + __popc(bal & ((1u << lane) - 1u));
+      if (j < static_cast<unsigned long long>(max_groups)) {
+        const unsigned long long* p = T + i * W;
+        out_keys[j] = static_cast<int64_t>(p[0]);
+        if (full) gstate_finalize(slot_state(p), static_cast<long long>(j), out);
+        else sumcount_finalize(p, static_cast<long long>(j), out);
+      }
+    }
+    pos += all;
+    __syncthreads();
   }
 }
 
@@ -471,21 +567,24 @@ unsigned long long next_pow2(unsigned long long x) {
 
 size_t table_slot_words(bool full) { return full ? size_t(FL_WORDS) : size_t(SC_WORDS); }
 
-TablePlan table_plan(bool hash, bool full, int mode, long long groups, int num_sms) {
+TablePlan table_plan(bool hash, bool full, int mode, long long groups, int num_sms, int buckets) {
   TablePlan P{};
   P.hash = hash;
   P.full = full;
+  P.buckets = hash && buckets > 1 ? buckets : 1;
   const long long limit = full ? LocalTable<true>::LIMIT : LocalTable<false>::LIMIT;
   if (hash) {
     const unsigned long long want = static_cast<unsigned long long>(groups) * 2;
-    P.slots = next_pow2(want < 1024 ? 1024 : want);
+    const unsigned long long total = next_pow2(want < 1024 ? 1024 : want);
+    P.slots = total / P.buckets >= 256 ? total / P.buckets : 256;
   } else {
     P.slots = static_cast<unsigned long long>(groups);
   }
   if (mode == 1) P.local = true;
   else if (mode == 2) P.local = false;
   else P.local = hash ? groups <= (1ll << 22) : groups <= limit;
-  const unsigned long long words = (P.slots + (hash ? 1 : 0)) * table_slot_words(full) + 1;
+  const unsigned long long words =
+      static_cast<unsigned long long>(P.buckets) * (P.slots + (hash ? 1 : 0)) * table_slot_words(full) + 1;
   P.table_bytes = (words * 8 + 255) / 256 * 256;
   P.grid = num_sms;
   P.block = TNT;
@@ -493,8 +592,16 @@ TablePlan table_plan(bool hash, bool full, int mode, long long groups, int num_s
   return P;
 }
 
+unsigned long long* table_bucket(const TablePlan& P, unsigned long long* table, int b) {
+  return table + static_cast<unsigned long long>(b) * (P.slots + (P.hash ? 1 : 0)) * table_slot_words(P.full);
+}
+
+unsigned long long* table_counter(const TablePlan& P, unsigned long long* table) {
+  return table_bucket(P, table, P.buckets);
+}
+
 cudaError_t table_init(const TablePlan& P, unsigned long long* table, cudaStream_t s, uint64_t* launches) {
-  const unsigned long long nslots = P.slots + (P.hash ? 1 : 0);
+  const unsigned long long nslots = static_cast<unsigned long long>(P.buckets) * (P.slots + (P.hash ? 1 : 0));
   unsigned long long blocks = (nslots + 255) / 256;
   if (blocks > 65536ull) blocks = 65536ull;
   if (blocks < 1) blocks = 1;
@@ -506,7 +613,7 @@ cudaError_t table_init(const TablePlan& P, unsigned long long* table, cudaStream
 
 cudaError_t table_accumulate(const TablePlan& P, const TableArgs& a, cudaStream_t s, uint64_t* launches,
                              cudaEvent_t ev0, cudaEvent_t ev1) {
-  if (a.n == 0) return cudaSuccess;
+  if (a.n == 0 && !a.dev_count) return cudaSuccess;
   const bool f32 = a.cols.dtype == TBGB_F32;
   if (ev0) cudaEventRecord(ev0, s);
   cudaError_t e;
@@ -530,16 +637,23 @@ cudaError_t table_finalize_dense(const TablePlan& P, const unsigned long long* t
   return e;
 }
 
+size_t table_finalize_scratch_bytes(const TablePlan& P) {
+  const unsigned long long total = static_cast<unsigned long long>(P.buckets) * (P.slots + 1);
+  return ((total + FIN_CHUNK - 1) / FIN_CHUNK * 8 + 255) / 256 * 256;
+}
+
 cudaError_t table_finalize_hash(const TablePlan& P, const unsigned long long* table, long long max_groups,
-                                int64_t* out_keys, const tbgb_moments* out, int64_t* d_n_groups, uint32_t* err,
-                                cudaStream_t s, uint64_t* launches) {
-  (void)err;
-  unsigned long long blocks = (P.slots + 1 + 255) / 256;
-  if (blocks > 65536ull) blocks = 65536ull;
-  table_finalize_hash_kernel<<<static_cast<unsigned int>(blocks), 256, 0, s>>>(table, P.slots, P.full ? 1 : 0,
-                                                                               max_groups, out_keys, *out, d_n_groups);
+                                int64_t* out_keys, const tbgb_moments* out, int64_t* d_n_groups,
+                                unsigned long long* scratch, cudaStream_t s, uint64_t* launches) {
+  const unsigned long long total = static_cast<unsigned long long>(P.buckets) * (P.slots + 1);
+  const unsigned long long nblk = (total + FIN_CHUNK - 1) / FIN_CHUNK;
+  const int full = P.full ? 1 : 0;
+  table_occ_count_kernel<<<static_cast<unsigned int>(nblk), FIN_NT, 0, s>>>(table, P.slots, total, full, scratch);
+  table_occ_scan_kernel<<<1, 1024, 0, s>>>(scratch, static_cast<long long>(nblk), max_groups, d_n_groups);
+  table_compact_kernel<<<static_cast<unsigned int>(nblk), FIN_NT, 0, s>>>(table, P.slots, total, full, scratch,
+                                                                          max_groups, out_keys, *out);
   cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess) (*launches)++;
+  if (e == cudaSuccess) *launches += 3;
   return e;
 }
 

@@ -31,6 +31,8 @@ struct TableArgs {
   const uint64_t* mask;  // nullable
   long long n;
   long long row_offset;  // global index of row 0 (first-zero codes)
+  const int64_t* dev_count;  // when set: n = *dev_count rows starting at row *dev_start (a partition's part)
+  const int64_t* dev_start;
   unsigned long long* table;
   unsigned long long slots;   // dense: n_groups; hash: power of two (plus one sentinel slot after them)
   unsigned long long* ngroups;  // hash: distinct-key counter
@@ -42,7 +44,8 @@ struct TablePlan {
   bool hash;       // int64 keys
   bool full;       // FULL slot (else SUMCOUNT)
   bool local;      // per-CTA shared-memory pre-aggregation
-  unsigned long long slots;
+  int buckets;     // hash: sub-tables (rows bucketed by their key's high hash bits first), 1 = one table
+  unsigned long long slots;       // dense: n_groups; hash: slots of each sub-table (a power of two)
   size_t table_bytes;  // including the sentinel slot and the counter word
   int grid;
   int block;
@@ -50,7 +53,12 @@ struct TablePlan {
 };
 
 size_t table_slot_words(bool full);
-TablePlan table_plan(bool hash, bool full, int mode, long long n_groups_or_max, int num_sms);
+// mode: 0 auto, 1 shared-memory pre-aggregation, 2 direct global updates; `buckets` > 1 splits
+// a hash table into that many sub-tables (power of two).
+TablePlan table_plan(bool hash, bool full, int mode, long long n_groups_or_max, int num_sms, int buckets = 1);
+// Sub-table b of a bucketed hash table, and where the distinct-key counter lives.
+unsigned long long* table_bucket(const TablePlan& P, unsigned long long* table, int b);
+unsigned long long* table_counter(const TablePlan& P, unsigned long long* table);
 
 // Fills every slot with its empty pattern and clears the counter.
 cudaError_t table_init(const TablePlan& P, unsigned long long* table, cudaStream_t s, uint64_t* launches);
@@ -60,9 +68,11 @@ cudaError_t table_accumulate(const TablePlan& P, const TableArgs& a, cudaStream_
 // Dense mode: outputs (or, when state_out != NULL, mergeable states) for groups [0, G).
 cudaError_t table_finalize_dense(const TablePlan& P, const unsigned long long* table, long long G,
                                  const tbgb_moments* out, double* state_out, cudaStream_t s, uint64_t* launches);
-// Hash mode: group j (its ID) to out_keys[j] / element j of out; writes the group count.
+// Hash mode: the occupied slots, in slot order, to out_keys / out (at most max_groups of
+// them); writes the group count.  `scratch` holds table_finalize_scratch_bytes(P).
+size_t table_finalize_scratch_bytes(const TablePlan& P);
 cudaError_t table_finalize_hash(const TablePlan& P, const unsigned long long* table, long long max_groups,
-                                int64_t* out_keys, const tbgb_moments* out, int64_t* d_n_groups, uint32_t* err,
-                                cudaStream_t s, uint64_t* launches);
+                                int64_t* out_keys, const tbgb_moments* out, int64_t* d_n_groups,
+                                unsigned long long* scratch, cudaStream_t s, uint64_t* launches);
 
 }  // namespace tbgb
