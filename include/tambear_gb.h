@@ -217,7 +217,8 @@ tbgb_status tbgb_hash_partition(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb
 
 /* Strategy for groupbys the shared-memory column kernel cannot take alone (int64 keys,
  * more than 1024 dense groups, filter / expression / f32 columns): 0 = choose by size
- * (default); 3 = bucket first (dense keys: stable key-range partition into parts of at
+ * (default: the global table, shared-memory pre-aggregation unless the keys are many);
+ * 3 = bucket first (dense keys: stable key-range partition into parts of at
  * most 512 groups, each reduced by the column kernel, up to 16384 groups; int64 keys:
  * stable partition by high hash bits into sub-tables of about 64 MB); 1 = global table
  * with per-CTA shared-memory pre-aggregation (skewed keys); 2 = global table, direct

@@ -163,10 +163,10 @@ tbgb_columns plain_f64(const double* vals) {
 // Bucket count of a hash table: sub-tables of about 64 MB keep a bucket's probes inside
 // L2 and the TLB's reach; at most kMaxParts (the partition's limit).
 int hash_buckets(tbgb_ctx* ctx, bool full, long long groups) {
-  if (ctx->table_mode == 1 || ctx->table_mode == 2) return 1;
+  // opt-in: with 2^28 keys, 32 sub-tables of 512 MB measured no faster than one 16 GB table
+  if (ctx->table_mode != 3) return 1;
   const tbgb::TablePlan one = tbgb::table_plan(true, full, 0, groups, ctx->num_sms, 1);
   const size_t target = size_t(64) << 20;
-  if (ctx->table_mode != 3 && one.table_bytes <= 4 * target) return 1;
   int b = 1;
   while (b < tbgb::kMaxParts && one.table_bytes / b > target) b <<= 1;
   return b < 2 ? 2 : b;
@@ -270,10 +270,12 @@ tbgb_status table_common(tbgb_ctx* ctx, bool hash, const void* keys, const tbgb_
 // Groups per key-range part: the column kernel's two-slot owner variant covers up to 512.
 constexpr int kBucketGroups = 512;
 
-// Key-range bucketing serves dense groupbys of up to kMaxParts * kBucketGroups groups unless the
-// context asks for the table kernel (modes 1 and 2).
+// Key-range bucketing serves dense groupbys of up to kMaxParts * kBucketGroups groups when the
+// context asks for it (mode 3).
 bool use_buckets(const tbgb_ctx* ctx, long long G) {
-  return (ctx->table_mode == 0 || ctx->table_mode == 3) && G <= static_cast<long long>(tbgb::kMaxParts) * kBucketGroups;
+  // opt-in: on the 10,000-group stress shape the partition pass costs more than the column
+  // kernel saves over the shared-memory table (measured)
+  return ctx->table_mode == 3 && G <= static_cast<long long>(tbgb::kMaxParts) * kBucketGroups;
 }
 
 // Dense keys in [0, G) with G up to kMaxParts * kBucketGroups (or any filter / expression / f32
