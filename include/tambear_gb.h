@@ -34,6 +34,10 @@
  *                                   (compute_engine.rs:165-178, CPU :304-322).  These are the
  *                                   entry names the reference's TamGpu dispatches by (scatter_phi,
  *                                   scatter_multi_phi, scatter_phi_masked, scatter_extremum)
+ *   tbgb_group_index_build          GroupIndex::build (crates/tambear/src/group_index.rs:117-204),
+ *                                   on the device instead of the host
+ *   tbgb_factorize_i64              Dictionary::encode (crates/tambear/src/dictionary.rs:40-75):
+ *                                   codes in first-seen order, for int64 keys
  *   tbgb_hash_partition             no counterpart in the reference (single GPU); routes rows to
  *                                   the GPU that owns their key for the sharded high-cardinality path
  *
@@ -87,7 +91,9 @@ const char* tbgb_device_name(const tbgb_ctx* ctx);
  *            sequential `v < acc` scan in row order would
  *   mean     sum / count, NaN when count == 0
  *   m2       sum over finite values of (v - r)^2 with r = sum/count (0.0 when empty)
- *   var_pop  m2 / count, NaN when count == 0;  var_samp  m2 / (count - 1), NaN when count <= 1 */
+ *   var_pop  m2 / count, NaN when count == 0;  var_samp  m2 / (count - 1), NaN when count <= 1
+ *   m3 / m4  sums over finite values of (v - r)^3 and (v - r)^4, r as for m2 (the m3s / m4s of
+ *            GroupedMomentStats, descriptive.rs:421-432); computed only when requested */
 typedef struct {
   double* count;
   double* sum;
@@ -97,6 +103,8 @@ typedef struct {
   double* m2;
   double* var_pop;
   double* var_samp;
+  double* m3;
+  double* m4;
 } tbgb_moments;
 
 /* Dense-key groupby: keys in [0, n_groups), f64 values, optional row mask
@@ -202,6 +210,24 @@ tbgb_status tbgb_scatter_phi_masked(tbgb_ctx* ctx, int32_t phi, const int32_t* d
 tbgb_status tbgb_scatter_extremum(tbgb_ctx* ctx, int32_t is_max, const int32_t* d_keys, const double* d_vals,
                                   int64_t n, int32_t n_groups, double* d_out, void* stream);
 
+/* ---- key factorisation ---------------------------------------------------------------
+ * GroupIndex::build for keys in [0, max_key]: row_to_group[i] = keys[i] (n entries),
+ * group_counts[g] (max_key + 1 entries), group_offsets[g] = sum of the counts of groups < g
+ * (max_key + 2 entries, the last = n), rows_by_group = row ids ordered by group with the row
+ * order kept inside each group (n entries), *d_n_active (device) = groups with a row.  All
+ * device memory, caller-owned; u32 like the reference.  n must be in [1, 2^32) (an empty
+ * column is TBGB_ERR_INVALID_ARGUMENT, as in the reference); a key outside [0, max_key]
+ * makes tbgb_sync report TBGB_ERR_KEY_OUT_OF_RANGE. */
+tbgb_status tbgb_group_index_build(tbgb_ctx* ctx, const int32_t* d_keys, int64_t n, int32_t max_key,
+                                   uint32_t* d_row_to_group, uint32_t* d_group_counts, uint32_t* d_group_offsets,
+                                   uint32_t* d_rows_by_group, int64_t* d_n_active, void* stream);
+/* Dictionary codes of int64 keys: distinct keys are numbered 0, 1, ... in the order they are
+ * first seen; d_codes[i] = number of keys[i] (n entries), d_uniques[j] = key j (up to
+ * max_groups entries), *d_n_uniques (device) = distinct keys (at most max_groups; more make
+ * tbgb_sync report TBGB_ERR_TABLE_FULL). */
+tbgb_status tbgb_factorize_i64(tbgb_ctx* ctx, const int64_t* d_keys, int64_t n, int64_t max_groups, int32_t* d_codes,
+                               int64_t* d_uniques, int64_t* d_n_uniques, void* stream);
+
 /* ---- sharded int64-key groupby (one process / GPU per shard) ----------------------
  * Routes the rows of this shard that pass mask and pred to their owner part
  * owner(key) = (fmix64(key) >> 32) % n_parts (fmix64: MurmurHash3's 64-bit
@@ -231,7 +257,7 @@ tbgb_status tbgb_sync(tbgb_ctx* ctx, void* stream);
 
 /* ---- row-sharded execution (one process / GPU per shard) ------------------------
  * A shard computes its mergeable per-group state table (tbgb_state_bytes(n_groups)
- * bytes, caller-owned device memory); the caller exchanges the tables (e.g. an
+ * bytes, caller-owned device memory, including m3 / m4 terms); the caller exchanges the tables (e.g. an
  * NCCL all-gather over NVLink) and folds them in rank order with
  * tbgb_merge_states.  `row_offset` is the global index of the shard's first row
  * (used only to order +-0 ties exactly as the unsharded scan would). */
@@ -249,7 +275,7 @@ tbgb_status tbgb_merge_states(tbgb_ctx* ctx, const void* d_states, int32_t n_sta
  * synchronisation).  No counterpart in the reference.
  * Same semantics and outputs as tbgb_groupby_dense, on the current device.
  * Limits: 1 <= n_groups <= 256 (TBGB_ERR_INVALID_ARGUMENT otherwise).  Scratch is
- * a fixed device array of about 8.5 MB inside this library, held by every GPU that
+ * a fixed device array of about 10.5 MB inside this library, held by every GPU that
  * loads the library until the process exits.  The first call on a device looks up
  * that array's address (make it before any stream capture).  All calls share the
  * array: calls that overlap on the GPU (other streams, other threads) race and

@@ -203,6 +203,29 @@ def groupby_i64(keys, values, mask=None, m34=False):
     return res
 
 
+def group_index_build(keys, max_key):
+    """GroupIndex::build (group_index.rs:117-204) in numpy: row_to_group, group_counts,
+    group_offsets (with the n sentinel), rows_by_group (stable by group), n_active."""
+    k = np.ascontiguousarray(keys, dtype=np.int32)
+    G = int(max_key) + 1
+    counts = np.bincount(k, minlength=G).astype(np.uint32)
+    offsets = np.zeros(G + 1, dtype=np.uint32)
+    offsets[1:] = np.cumsum(counts, dtype=np.uint64).astype(np.uint32)
+    return {"row_to_group": k.astype(np.uint32), "group_counts": counts, "group_offsets": offsets,
+            "rows_by_group": np.argsort(k, kind="stable").astype(np.uint32),
+            "n_active": int(np.count_nonzero(counts))}
+
+
+def factorize_first_seen(keys):
+    """Dictionary::encode (dictionary.rs:40-75) over a key column: codes in first-seen order."""
+    k = np.ascontiguousarray(keys, dtype=np.int64)
+    uniq, first, inv = np.unique(k, return_index=True, return_inverse=True)
+    order = np.argsort(first, kind="stable")
+    rank = np.empty_like(order)
+    rank[order] = np.arange(order.size)
+    return rank[inv].astype(np.int32), uniq[order]
+
+
 def mean(count, total):
     return float(lib().orc_mean(float(count), float(total)))
 

@@ -61,5 +61,5 @@ def test_no_oracle_in_product():
 def test_state_bytes_without_gpu(libpath):
     from winrapids_b200._lib import lib
 
-    assert lib().tbgb_state_bytes(256) == 9 * 256 * 8
+    assert lib().tbgb_state_bytes(256) == 11 * 256 * 8  # 11 state fields per group
     assert lib().tbgb_state_bytes(0) == 0

@@ -221,3 +221,21 @@ def test_generator_streams():
     assert [int(oracle.lib().orc_splitmix_at(seed, i)) for i in range(5)] == seq
     k = oracle.gen_keys_uniform(1000, 256, 0)
     assert k.min() >= 0 and k.max() < 256
+
+
+def test_group_index_oracle_hand_case():
+    """GroupIndex::build semantics (group_index.rs:117-204) on a hand-worked column: counts,
+    offsets with the n sentinel, rows_by_group in row order inside each group."""
+    gi = oracle.group_index_build([2, 0, 2, 1, 0], 3)
+    assert gi["row_to_group"].tolist() == [2, 0, 2, 1, 0]
+    assert gi["group_counts"].tolist() == [2, 1, 2, 0]
+    assert gi["group_offsets"].tolist() == [0, 2, 3, 5, 5]
+    assert gi["rows_by_group"].tolist() == [1, 4, 3, 0, 2]
+    assert gi["n_active"] == 3
+
+
+def test_factorize_oracle_first_seen_order():
+    """Dictionary::encode (dictionary.rs:40-75): codes follow the order values are first seen."""
+    codes, uniq = oracle.factorize_first_seen([5, 3, 5, -7, 3, 2**63 - 1, -(2**63)])
+    assert codes.tolist() == [0, 1, 0, 2, 1, 3, 4]
+    assert uniq.tolist() == [5, 3, -7, 2**63 - 1, -(2**63)]

@@ -16,13 +16,13 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._lib import (DTYPES, EXPRS, MOMENT_FIELDS, PREDS, Columns, InvalidArgument, KeyOutOfRange, Moments,
-                   TableFull, TambearGbError, error_for, lib)
+from ._lib import (DTYPES, EXPRS, HIGHER_FIELDS, MOMENT_FIELDS, PREDS, Columns, InvalidArgument, KeyOutOfRange,
+                   Moments, TableFull, TambearGbError, error_for, lib)
 
 __all__ = [
-    "ComputeEngine", "AccumulateEngine", "HashScatterEngine", "GroupByResult", "Grouping", "Op",
+    "ComputeEngine", "AccumulateEngine", "HashScatterEngine", "GroupByResult", "Grouping", "Op", "GroupIndex",
     "Context", "DescriptiveEngine", "GroupedMomentStats", "MomentStats", "TambearGbError", "KeyOutOfRange",
-    "InvalidArgument", "TableFull", "MOMENT_FIELDS", "SUMCOUNT_FIELDS",
+    "InvalidArgument", "TableFull", "MOMENT_FIELDS", "HIGHER_FIELDS", "SUMCOUNT_FIELDS",
 ]
 
 SUMCOUNT_FIELDS = ("count", "sum", "mean")
@@ -87,9 +87,8 @@ class Context:
     @staticmethod
     def moments_struct(out: dict) -> Moments:
         m = Moments()
-        for f in MOMENT_FIELDS:
-            t = out.get(f)
-            setattr(m, f, _ptr(t))
+        for f, _ in Moments._fields_:
+            setattr(m, f, _ptr(out.get(f)))
         return m
 
     def alloc_moments(self, n_groups: int, fields=MOMENT_FIELDS) -> dict:
@@ -154,6 +153,38 @@ class Context:
         if sync:
             self.sync(stream)
         return out
+
+    def group_index_build(self, keys, max_key: int, stream=None) -> dict:
+        """GroupIndex::build of an int32 device key column (u32 outputs as int32 tensors of the
+        same bits): row_to_group, group_counts, group_offsets, rows_by_group, n_active."""
+        torch = _torch()
+        n = int(keys.numel())
+        dev = f"cuda:{self.device}"
+        G = int(max_key) + 1
+        out = {"row_to_group": torch.empty(n, dtype=torch.int32, device=dev),
+               "group_counts": torch.empty(G, dtype=torch.int32, device=dev),
+               "group_offsets": torch.empty(G + 1, dtype=torch.int32, device=dev),
+               "rows_by_group": torch.empty(n, dtype=torch.int32, device=dev)}
+        na = torch.zeros(1, dtype=torch.int64, device=dev)
+        self._check(self._L.tbgb_group_index_build(self._h, _ptr(keys), n, int(max_key), _ptr(out["row_to_group"]),
+                                                   _ptr(out["group_counts"]), _ptr(out["group_offsets"]),
+                                                   _ptr(out["rows_by_group"]), _ptr(na), _stream_handle(stream)))
+        self.sync(stream)
+        out["n_active"] = int(na.item())
+        return out
+
+    def factorize_i64(self, keys, max_groups: int, stream=None):
+        """Dictionary codes of int64 device keys in first-seen order: (codes int32, uniques int64)."""
+        torch = _torch()
+        n = int(keys.numel())
+        dev = f"cuda:{self.device}"
+        codes = torch.empty(n, dtype=torch.int32, device=dev)
+        uniques = torch.empty(int(max_groups), dtype=torch.int64, device=dev)
+        nu = torch.zeros(1, dtype=torch.int64, device=dev)
+        self._check(self._L.tbgb_factorize_i64(self._h, _ptr(keys), n, int(max_groups), _ptr(codes), _ptr(uniques),
+                                               _ptr(nu), _stream_handle(stream)))
+        self.sync(stream)
+        return codes, uniques[:int(nu.item())]
 
     def groupby_hash_into(self, keys, a, max_groups: int, out_keys, out: dict, n_groups, b=None, c=None,
                           expr: str = "a", pred: str | None = None, threshold: float = 0.0, mask=None,
@@ -271,13 +302,20 @@ class Context:
 
 @dataclass
 class MomentStats:
-    """Per-group sufficient statistics (descriptive.rs:67-87); m3/m4 are not computed here."""
+    """Per-group sufficient statistics (descriptive.rs:67-254): count, sum, min, max and the
+    central moment sums m2, m3, m4."""
 
     count: float
     sum: float
     min: float
     max: float
     m2: float
+    m3: float = 0.0
+    m4: float = 0.0
+
+    @staticmethod
+    def empty() -> "MomentStats":
+        return MomentStats(0.0, 0.0, math.inf, -math.inf, 0.0, 0.0, 0.0)
 
     def n(self) -> int:
         return int(self.count)
@@ -295,6 +333,59 @@ class MomentStats:
     def range(self) -> float:
         return math.nan if self.count == 0.0 else self.max - self.min
 
+    def cv(self) -> float:
+        m = self.mean()
+        if m == 0.0 or self.count < 2.0:
+            return math.nan
+        return self.std(1) / abs(m)
+
+    def sem(self) -> float:
+        return math.nan if self.count < 2.0 else self.std(1) / math.sqrt(self.count)
+
+    def skewness(self, bias: bool) -> float:
+        n = self.count
+        if n < 1.0 or self.m2 == 0.0:
+            return math.nan
+        var = self.m2 / n
+        g1 = (self.m3 / n) / (var * math.sqrt(var))
+        if bias:
+            return g1
+        return math.nan if n < 3.0 else g1 * math.sqrt(n * (n - 1.0)) / (n - 2.0)
+
+    def kurtosis(self, excess: bool, bias: bool) -> float:
+        n = self.count
+        if n < 1.0 or self.m2 == 0.0:
+            return math.nan
+        var = self.m2 / n
+        raw = (self.m4 / n) / (var * var)
+        if bias:
+            return raw - 3.0 if excess else raw
+        if n < 4.0:
+            return math.nan
+        g2 = ((n - 1.0) / ((n - 2.0) * (n - 3.0))) * ((n + 1.0) * (raw - 3.0) + 6.0)
+        return g2 if excess else g2 + 3.0
+
+    @staticmethod
+    def merge(a: "MomentStats", b: "MomentStats") -> "MomentStats":
+        """Parallel merge of two partitions' moments (descriptive.rs:216-253)."""
+        na, nb = a.count, b.count
+        n = na + nb
+        if n == 0.0:
+            return MomentStats.empty()
+        if na == 0.0:
+            return b
+        if nb == 0.0:
+            return a
+        delta = b.sum / nb - a.sum / na
+        d2 = delta * delta
+        m2 = a.m2 + b.m2 + d2 * na * nb / n
+        m3 = a.m3 + b.m3 + d2 * delta * na * nb * (na - nb) / (n * n) + 3.0 * delta * (na * b.m2 - nb * a.m2) / n
+        m4 = (a.m4 + b.m4 + d2 * d2 * na * nb * (na * na - na * nb + nb * nb) / (n * n * n)
+              + 6.0 * d2 * (na * na * b.m2 + nb * nb * a.m2) / (n * n) + 4.0 * delta * (na * b.m3 - nb * a.m3) / n)
+        mn = math.nan if math.isnan(a.min) or math.isnan(b.min) else min(a.min, b.min)
+        mx = math.nan if math.isnan(a.max) or math.isnan(b.max) else max(a.max, b.max)
+        return MomentStats(n, a.sum + b.sum, mn, mx, m2, m3, m4)
+
 
 @dataclass
 class GroupedMomentStats:
@@ -306,10 +397,12 @@ class GroupedMomentStats:
     mins: np.ndarray
     maxs: np.ndarray
     m2s: np.ndarray
+    m3s: np.ndarray
+    m4s: np.ndarray
 
     def group(self, g: int) -> MomentStats:
         return MomentStats(float(self.counts[g]), float(self.sums[g]), float(self.mins[g]), float(self.maxs[g]),
-                           float(self.m2s[g]))
+                           float(self.m2s[g]), float(self.m3s[g]), float(self.m4s[g]))
 
     def means(self) -> np.ndarray:
         with np.errstate(invalid="ignore", divide="ignore"):
@@ -332,12 +425,13 @@ class DescriptiveEngine:
         dv = torch.from_numpy(values).to(dev)
         dk = torch.from_numpy(keys).to(dev)
         out = self.ctx.groupby_dense(dk, dv, n_groups, out=self.ctx.alloc_moments(
-            n_groups, ("count", "sum", "min", "max", "m2")))
+            n_groups, ("count", "sum", "min", "max", "m2", "m3", "m4")))
         h = {k: v.cpu().numpy() for k, v in out.items()}
-        return GroupedMomentStats(n_groups, h["count"], h["sum"], h["min"], h["max"], h["m2"])
+        return GroupedMomentStats(n_groups, h["count"], h["sum"], h["min"], h["max"], h["m2"], h["m3"], h["m4"])
 
     def mean_grouped(self, values, keys, n_groups: int) -> np.ndarray:
         return self.moments_grouped(values, keys, n_groups).means()
 
 
 from .engines import AccumulateEngine, ComputeEngine, GroupByResult, Grouping, HashScatterEngine, Op  # noqa: E402
+from .group_index import GroupIndex  # noqa: E402

@@ -70,10 +70,13 @@ EXPRS = {"a": 0, "a+b": 1, "a-b": 2, "a*b": 3, "a*b+1": 4, "a*b+c": 5}
 
 class Moments(C.Structure):
     _fields_ = [(name, C.c_void_p) for name in
-                ("count", "sum", "min", "max", "mean", "m2", "var_pop", "var_samp")]
+                ("count", "sum", "min", "max", "mean", "m2", "var_pop", "var_samp", "m3", "m4")]
 
 
-MOMENT_FIELDS = tuple(f for f, _ in Moments._fields_)
+# The grouped moments computed by default; m3 / m4 (HIGHER_FIELDS) cost a little more and are
+# computed only when their outputs are requested.
+MOMENT_FIELDS = ("count", "sum", "min", "max", "mean", "m2", "var_pop", "var_samp")
+HIGHER_FIELDS = ("m3", "m4")
 
 _lib = None
 
@@ -111,6 +114,8 @@ def lib() -> C.CDLL:
         "tbgb_scatter_multi_phi": (st, [vp, C.POINTER(i32), i32, vp, vp, vp, i64, i32, vp, vp]),
         "tbgb_scatter_phi_masked": (st, [vp, i32, vp, vp, vp, vp, i64, i32, vp, vp]),
         "tbgb_scatter_extremum": (st, [vp, i32, vp, vp, i64, i32, vp, vp]),
+        "tbgb_group_index_build": (st, [vp, vp, i64, i32, vp, vp, vp, vp, vp, vp]),
+        "tbgb_factorize_i64": (st, [vp, vp, i64, i64, vp, vp, vp, vp]),
         "tbgb_gen_keys_uniform": (st, [vp, vp, i64, i32, u64, i64, vp]),
         "tbgb_gen_values_uniform": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
         "tbgb_gen_values_normal": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
@@ -136,7 +141,7 @@ HEADER_SYMBOLS = (
     "tbgb_gen_inject_nonfinite", "tbgb_groupby_dense_columns", "tbgb_groupby_hash", "tbgb_set_table_mode",
     "tbgb_gen_keys_cdf", "tbgb_gen_keys_ids", "tbgb_gen_values_lognormal_f32", "tbgb_hash_partition",
     "tbgb_scatter_multi_phi_masked", "tbgb_scatter_phi", "tbgb_scatter_multi_phi", "tbgb_scatter_phi_masked",
-    "tbgb_scatter_extremum",
+    "tbgb_scatter_extremum", "tbgb_group_index_build", "tbgb_factorize_i64",
 )
 
 # phi expressions by the reference's source spelling (phi_scatter_eval, compute_engine.rs:593-609)

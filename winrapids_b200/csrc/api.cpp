@@ -1,6 +1,7 @@
 // api.cpp -- C ABI of the groupby path (include/tambear_gb.h).
 #include <cuda_runtime.h>
 
+#include <climits>
 #include <cstdio>
 #include <cstring>
 #include <string>
@@ -10,6 +11,7 @@
 #include "dense.cuh"
 #include "errbits.hpp"
 #include "gen.cuh"
+#include "group_index.cuh"
 #include "partition.cuh"
 #include "phi.cuh"
 #include "table.cuh"
@@ -131,7 +133,7 @@ tbgb_status dense_common(tbgb_ctx* ctx, const int32_t* keys, const double* vals,
 }
 
 bool wants_full(const tbgb_moments* out) {
-  return !out || out->min || out->max || out->m2 || out->var_pop || out->var_samp;
+  return !out || out->min || out->max || out->m2 || out->var_pop || out->var_samp || out->m3 || out->m4;
 }
 
 tbgb_status check_columns(tbgb_ctx* ctx, const tbgb_columns* c, int64_t n) {
@@ -226,6 +228,7 @@ tbgb_status table_common(tbgb_ctx* ctx, bool hash, const void* keys, const tbgb_
   a.ngroups = tbgb::table_counter(P, T);
   a.max_groups = groups;
   a.err = ctx->err;
+  a.m34 = full && (state_out != nullptr || (out && (out->m3 || out->m4)));
   if (B == 1) {
     a.keys = keys;
     a.cols = *cols;
@@ -325,17 +328,23 @@ tbgb_status bucketed_dense(tbgb_ctx* ctx, const int32_t* keys, const tbgb_column
   pa.err = ctx->err;
   cudaError_t e = tbgb::partition_launch(pa, scratch, pcounts, pstarts, s, &ctx->launches);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "key-range partition launch", e);
+  // The column kernel takes its row count at launch: read the part sizes (a few dozen bytes).
+  int64_t hc[tbgb::kMaxParts], hs[tbgb::kMaxParts];
+  e = cudaMemcpyAsync(hc, pcounts, static_cast<size_t>(nb) * 8, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaMemcpyAsync(hs, pstarts, static_cast<size_t>(nb) * 8, cudaMemcpyDeviceToHost, s);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(s);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_TRANSFER, "part sizes", e);
   for (int b = 0; b < nb; ++b) {
     const int Gb = (b + 1) * W <= G ? W : G - b * W;
     const tbgb::DenseLaunch Lb = tbgb::dense_plan(Gb, ctx->num_sms);
     tbgb_moments ob = *out;
-    double** f[] = {&ob.count, &ob.sum, &ob.min, &ob.max, &ob.mean, &ob.m2, &ob.var_pop, &ob.var_samp};
+    double** f[] = {&ob.count, &ob.sum, &ob.min, &ob.max, &ob.mean, &ob.m2, &ob.var_pop, &ob.var_samp, &ob.m3, &ob.m4};
     for (double** q : f)
       if (*q) *q += static_cast<size_t>(b) * W;
     e = cudaMemsetAsync(dw.zfirst, 0xFF, static_cast<size_t>(Gb) * 8, s);
     if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "memset", e);
-    e = tbgb::dense_moments_launch(Lb, pkeys, pvals, nullptr, 0, 0, Gb, dw.part, dw.spill, dw.zfirst, ctx->err, &ob,
-                                   nullptr, s, &ctx->launches, nullptr, nullptr, pcounts + b, pstarts + b);
+    e = tbgb::dense_moments_launch(Lb, pkeys + hs[b], pvals + hs[b], nullptr, hc[b], 0, Gb, dw.part, dw.spill,
+                                   dw.zfirst, ctx->err, &ob, nullptr, s, &ctx->launches);
     if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "dense groupby launch", e);
   }
   if (e1) cudaEventRecord(e1, s);
@@ -557,6 +566,43 @@ tbgb_status tbgb_scatter_extremum(tbgb_ctx* ctx, int32_t is_max, const int32_t* 
                                         static_cast<unsigned long long*>(ctx->ws), ctx->err, ctx->num_sms,
                                         static_cast<cudaStream_t>(stream), &ctx->launches);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "extremum launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_group_index_build(tbgb_ctx* ctx, const int32_t* d_keys, int64_t n, int32_t max_key,
+                                   uint32_t* d_row_to_group, uint32_t* d_group_counts, uint32_t* d_group_offsets,
+                                   uint32_t* d_rows_by_group, int64_t* d_n_active, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (n <= 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "GroupIndex::build called on empty column");
+  if (n >= (1ll << 32)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "row ids are u32: n must be < 2^32");
+  if (max_key < 0 || max_key == INT32_MAX) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "max_key out of range");
+  if (!d_keys || !d_row_to_group || !d_group_counts || !d_group_offsets || !d_rows_by_group || !d_n_active)
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "NULL pointer");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  tbgb_status st = ensure_ws(ctx, tbgb::group_index_scratch_bytes(n));
+  if (st != TBGB_OK) return st;
+  cudaError_t e = tbgb::group_index_launch(d_keys, n, max_key + 1, d_row_to_group, d_group_counts, d_group_offsets,
+                                           d_rows_by_group, d_n_active, ctx->ws, ctx->err, ctx->num_sms,
+                                           static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "group index launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_factorize_i64(tbgb_ctx* ctx, const int64_t* d_keys, int64_t n, int64_t max_groups, int32_t* d_codes,
+                               int64_t* d_uniques, int64_t* d_n_uniques, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (n < 0 || n >= (1ll << 32)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n must be in [0, 2^32)");
+  if (max_groups < 1 || max_groups > INT32_MAX) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "max_groups out of range");
+  if (!d_uniques || !d_n_uniques || (n > 0 && (!d_keys || !d_codes)))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "NULL pointer");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  tbgb_status st = ensure_ws(ctx, tbgb::factorize_scratch_bytes(n, max_groups));
+  if (st != TBGB_OK) return st;
+  cudaError_t e = tbgb::factorize_launch(d_keys, n, max_groups, d_codes, d_uniques, d_n_uniques, ctx->ws, ctx->err,
+                                         ctx->num_sms, static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "factorize launch", e);
   return TBGB_OK;
 }
 

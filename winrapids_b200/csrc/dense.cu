@@ -62,7 +62,8 @@ constexpr unsigned long long K_UNSET = 0x7FF8000000000001ull;  // NaN payload no
 constexpr uint32_t NO_RANK = 0xFFFFFFFFu;
 
 // spill state, per CTA, SoA over groups (u64 words)
-enum { SP_N = 0, SP_NINFP, SP_NINFN, SP_K, SP_S1, SP_S2, SP_MN, SP_MX, SP_COUNT };
+enum { SP_N = 0, SP_NINFP, SP_NINFN, SP_K, SP_S1, SP_S2, SP_MN, SP_MX, SP_S3, SP_S4, SP_COUNT };
+static_assert(SP_COUNT == kDenseSpillFields, "spill state size exported in dense.cuh");
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -104,8 +105,6 @@ struct DenseArgs {
   const uint64_t* mask;  // nullable (MASKED template flag)
   long long n;
   long long row_offset;  // global index of row 0 (zero-tie ordering across shards)
-  const int64_t* dev_count;  // when set: n = *dev_count rows starting at row *dev_start (a partition's part)
-  const int64_t* dev_start;
   int G, C, opg, slots;
   double* part;                // owner partials [ST_COUNT][gridDim.x * TEAMS * slots]
   unsigned long long* spill;   // [gridDim.x][SP_COUNT][G]
@@ -137,13 +136,18 @@ DenseLaunch dense_plan(int G, int num_sms) {
 }
 
 // Rare path: a finite row that found its column full.
+template <bool M34>
 __device__ __forceinline__ void spill_add(unsigned long long* sp, int G, int g, double v) {
   const unsigned long long vb = static_cast<unsigned long long>(__double_as_longlong(v));
   const unsigned long long kb = atomicCAS(sp + SP_K * G + g, K_UNSET, vb);
   const double K = kb == K_UNSET ? v : __longlong_as_double(static_cast<long long>(kb));
-  const double d = v - K;
+  const double d = v - K, d2 = d * d;
   atomicAdd(reinterpret_cast<double*>(sp + SP_S1 * G + g), d);
-  atomicAdd(reinterpret_cast<double*>(sp + SP_S2 * G + g), d * d);
+  atomicAdd(reinterpret_cast<double*>(sp + SP_S2 * G + g), d2);
+  if constexpr (M34) {
+    atomicAdd(reinterpret_cast<double*>(sp + SP_S3 * G + g), d2 * d);
+    atomicAdd(reinterpret_cast<double*>(sp + SP_S4 * G + g), d2 * d2);
+  }
   atomicAdd(sp + SP_N * G + g, 1ull);
   atomicMin(sp + SP_MN * G + g, f2o(v));
   atomicMax(sp + SP_MX * G + g, f2o(v));
@@ -151,8 +155,19 @@ __device__ __forceinline__ void spill_add(unsigned long long* sp, int G, int g, 
 
 // Register accumulators of one owner slot; NCH independent chains shorten the
 // dependency path through S1/S2.
+// With M34 the third and fourth power sums are kept too (m3 / m4 requested).
+template <int NCH, bool M34>
+struct OwnerAcc;
+
 template <int NCH>
-struct OwnerAcc {
+struct HigherSums {  // sum(d^3), sum(d^4) per chain
+  double s3[NCH], s4[NCH];
+};
+template <>
+struct HigherSums<0> {};
+
+template <int NCH, bool M34>
+struct OwnerAcc : HigherSums<M34 ? NCH : 0> {
   double K, s1[NCH], s2[NCH], mn, mx;
   unsigned long long nf;
   bool kset;
@@ -160,18 +175,38 @@ struct OwnerAcc {
     K = 0.0;
 #pragma unroll
     for (int j = 0; j < NCH; ++j) { s1[j] = 0.0; s2[j] = 0.0; }
+    if constexpr (M34) {
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) { this->s3[j] = 0.0; this->s4[j] = 0.0; }
+    }
     mn = pos_inf(); mx = neg_inf(); nf = 0; kset = false;
+  }
+  __device__ __forceinline__ void pw(int j, double d) {
+    const double dd = d * d;
+    s1[j] += d;
+    s2[j] += dd;
+    if constexpr (M34) {
+      this->s3[j] = fma(dd, d, this->s3[j]);
+      this->s4[j] = fma(dd, dd, this->s4[j]);
+    }
   }
   __device__ __forceinline__ void quad(double x0, double x1, double x2, double x3) {
     const double d0 = x0 - K, d1 = x1 - K, d2 = x2 - K, d3 = x3 - K;
-    s1[0 % NCH] += d0;
-    s2[0 % NCH] = fma(d0, d0, s2[0 % NCH]);
-    s1[1 % NCH] += d1;
-    s2[1 % NCH] = fma(d1, d1, s2[1 % NCH]);
-    s1[2 % NCH] += d2;
-    s2[2 % NCH] = fma(d2, d2, s2[2 % NCH]);
-    s1[3 % NCH] += d3;
-    s2[3 % NCH] = fma(d3, d3, s2[3 % NCH]);
+    if constexpr (M34) {
+      pw(0 % NCH, d0);
+      pw(1 % NCH, d1);
+      pw(2 % NCH, d2);
+      pw(3 % NCH, d3);
+    } else {
+      s1[0 % NCH] += d0;
+      s2[0 % NCH] = fma(d0, d0, s2[0 % NCH]);
+      s1[1 % NCH] += d1;
+      s2[1 % NCH] = fma(d1, d1, s2[1 % NCH]);
+      s1[2 % NCH] += d2;
+      s2[2 % NCH] = fma(d2, d2, s2[2 % NCH]);
+      s1[3 % NCH] += d3;
+      s2[3 % NCH] = fma(d3, d3, s2[3 % NCH]);
+    }
     // extrema by plain compares (no NaN reaches a column); +-0 ties are settled
     // later from the first-zero tracker
     const bool l01 = x0 < x1, l23 = x2 < x3;
@@ -183,8 +218,12 @@ struct OwnerAcc {
   }
   __device__ __forceinline__ void one(double x) {
     const double d = x - K;
-    s1[0] += d;
-    s2[0] = fma(d, d, s2[0]);
+    if constexpr (M34) {
+      pw(0, d);
+    } else {
+      s1[0] += d;
+      s2[0] = fma(d, d, s2[0]);
+    }
     mn = x < mn ? x : mn;
     mx = x > mx ? x : mx;
   }
@@ -231,18 +270,27 @@ struct OwnerAcc {
     for (int j = 0; j < NCH; ++j) r += s2[j];
     return r;
   }
+  __device__ __forceinline__ double sum_s3() const {
+    double r = 0.0;
+    if constexpr (M34) {
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) r += this->s3[j];
+    }
+    return r;
+  }
+  __device__ __forceinline__ double sum_s4() const {
+    double r = 0.0;
+    if constexpr (M34) {
+#pragma unroll
+      for (int j = 0; j < NCH; ++j) r += this->s4[j];
+    }
+    return r;
+  }
 };
 
-template <int MAXSLOTS, bool MASKED, bool TMA>
-__global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a_in) {
+template <int MAXSLOTS, bool MASKED, bool TMA, bool M34>
+__global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
-  DenseArgs a = a_in;
-  if (a.dev_count) {  // one part of a partition: the part's start keeps the 16-byte alignment of the buffers
-    const long long start = *a.dev_start;
-    a.n = *a.dev_count;
-    a.keys += start;
-    a.vals += start;
-  }
   const int tid = threadIdx.x;
   const int G = a.G, C = a.C;
   const int gp = (G + 3) & ~3;
@@ -280,6 +328,8 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a_in) {
     sp[SP_S2 * G + g] = 0;
     sp[SP_MN * G + g] = ~0ull;
     sp[SP_MX * G + g] = 0;
+    sp[SP_S3 * G + g] = 0;
+    sp[SP_S4 * G + g] = 0;
   }
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], SCATTER_WARPS); }
@@ -453,7 +503,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a_in) {
             if ((over >> i) & 1u) {
               const uint32_t slot = atomicAdd(&splc[k & 3], 1u);
               if (slot < SPL) { splk[slot] = g; splv[slot] = x; }
-              else spill_add(sp, G, g, x);
+              else spill_add<M34>(sp, G, g, x);
             }
             if (!((rare >> i) & 1u)) continue;
             if (static_cast<unsigned>(g) >= static_cast<unsigned>(G)) {
@@ -475,8 +525,8 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a_in) {
     // ------------------------------------------------------------ owner warps
     const int team = (tid - NSC) / NOW;
     const int o = tid - NSC - team * NOW;  // owner index within the team
-    constexpr int NCH = MAXSLOTS == 1 ? 4 : (MAXSLOTS == 2 ? 2 : 1);
-    OwnerAcc<NCH> acc[MAXSLOTS];
+    constexpr int NCH = MAXSLOTS == 1 ? (M34 ? 2 : 4) : (MAXSLOTS == 2 && !M34 ? 2 : 1);
+    OwnerAcc<NCH, M34> acc[MAXSLOTS];
     int og[MAXSLOTS], osub[MAXSLOTS];
 #pragma unroll
     for (int q = 0; q < MAXSLOTS; ++q) {
@@ -540,10 +590,14 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a_in) {
       const long long idx = (static_cast<long long>(b) * TEAMS + team) * a.slots + (o + q * NOW);
       const auto& A = acc[q];
       const double s1 = A.sum_s1(), s2 = A.sum_s2();
-      double meanoff = 0.0, m2 = 0.0;
+      double meanoff = 0.0, m2 = 0.0, m3 = 0.0, m4 = 0.0;
       if (A.nf > 0) {
-        meanoff = s1 / static_cast<double>(A.nf);
-        m2 = fmax(s2 - s1 * meanoff, 0.0);
+        if constexpr (M34) {
+          central_from_power(static_cast<double>(A.nf), s1, s2, A.sum_s3(), A.sum_s4(), &meanoff, &m2, &m3, &m4);
+        } else {
+          meanoff = s1 / static_cast<double>(A.nf);
+          m2 = fmax(s2 - s1 * meanoff, 0.0);
+        }
       }
       a.part[ST_NN * stride + idx] = static_cast<double>(A.nf);
       a.part[ST_NF * stride + idx] = static_cast<double>(A.nf);
@@ -553,6 +607,8 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a_in) {
       a.part[ST_M2 * stride + idx] = m2;
       a.part[ST_MIN * stride + idx] = A.mn;
       a.part[ST_MAX * stride + idx] = A.mx;
+      a.part[ST_M3 * stride + idx] = m3;
+      a.part[ST_M4 * stride + idx] = m4;
     }
   }
   __syncthreads();
@@ -572,8 +628,10 @@ __device__ __forceinline__ GState spill_state(const unsigned long long* sp, int 
     s.nf = static_cast<double>(n);
     s.K = __longlong_as_double(static_cast<long long>(sp[SP_K * G + g]));
     s.sumoff = __longlong_as_double(static_cast<long long>(sp[SP_S1 * G + g]));
-    s.meanoff = s.sumoff / s.nf;
-    s.m2 = fmax(__longlong_as_double(static_cast<long long>(sp[SP_S2 * G + g])) - s.sumoff * s.meanoff, 0.0);
+    central_from_power(s.nf, s.sumoff, __longlong_as_double(static_cast<long long>(sp[SP_S2 * G + g])),
+                       __longlong_as_double(static_cast<long long>(sp[SP_S3 * G + g])),
+                       __longlong_as_double(static_cast<long long>(sp[SP_S4 * G + g])), &s.meanoff, &s.m2, &s.m3,
+                       &s.m4);
     s.mn = o2f(sp[SP_MN * G + g]);
     s.mx = o2f(sp[SP_MX * G + g]);
   }
@@ -614,6 +672,8 @@ __global__ void __launch_bounds__(256) dense_fold_kernel(const double* __restric
       B.m2 = part[ST_M2 * stride + idx];
       B.mn = part[ST_MIN * stride + idx];
       B.mx = part[ST_MAX * stride + idx];
+      B.m3 = part[ST_M3 * stride + idx];
+      B.m4 = part[ST_M4 * stride + idx];
       B.zf = ~0ull;
     } else {
       B = spill_state(spill + static_cast<size_t>(p) * SP_COUNT * G, G, g);
@@ -648,31 +708,38 @@ __global__ void __launch_bounds__(256) merge_states_kernel(const double* __restr
 // host launchers
 // ---------------------------------------------------------------------------
 
-template <int MAXSLOTS, bool MASKED, bool TMA>
+template <int MAXSLOTS, bool MASKED, bool TMA, bool M34>
 static cudaError_t launch_main(const DenseLaunch& L, const DenseArgs& a, cudaStream_t stream) {
-  auto kern = dense_moments_kernel<MAXSLOTS, MASKED, TMA>;
+  auto kern = dense_moments_kernel<MAXSLOTS, MASKED, TMA, M34>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L.smem));
   if (e != cudaSuccess) return e;
   kern<<<L.grid, NT, L.smem, stream>>>(a);
   return cudaGetLastError();
 }
 
-template <int MAXSLOTS>
+template <int MAXSLOTS, bool M34>
 static cudaError_t launch_slots(const DenseLaunch& L, const DenseArgs& a, bool masked, bool aligned,
                                 cudaStream_t stream) {
   if (masked)
-    return aligned ? launch_main<MAXSLOTS, true, true>(L, a, stream) : launch_main<MAXSLOTS, true, false>(L, a, stream);
-  return aligned ? launch_main<MAXSLOTS, false, true>(L, a, stream) : launch_main<MAXSLOTS, false, false>(L, a, stream);
+    return aligned ? launch_main<MAXSLOTS, true, true, M34>(L, a, stream)
+                   : launch_main<MAXSLOTS, true, false, M34>(L, a, stream);
+  return aligned ? launch_main<MAXSLOTS, false, true, M34>(L, a, stream)
+                 : launch_main<MAXSLOTS, false, false, M34>(L, a, stream);
+}
+
+template <bool M34>
+static cudaError_t launch_m(const DenseLaunch& L, const DenseArgs& a, bool masked, bool aligned, cudaStream_t stream) {
+  if (L.maxslots == 1) return launch_slots<1, M34>(L, a, masked, aligned, stream);
+  if (L.maxslots == 2) return launch_slots<2, M34>(L, a, masked, aligned, stream);
+  return launch_slots<4, M34>(L, a, masked, aligned, stream);
 }
 
 cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, const double* vals, const uint64_t* mask,
                                  long long n, long long row_offset, int G, double* part, unsigned long long* spill,
                                  unsigned long long* zfirst, uint32_t* err, const tbgb_moments* out, double* state_out,
-                                 cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start, cudaEvent_t ev_stop,
-                                 const int64_t* dev_count, const int64_t* dev_start) {
+                                 cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start, cudaEvent_t ev_stop) {
   DenseArgs a;
   a.keys = keys; a.vals = vals; a.mask = mask; a.n = n; a.row_offset = row_offset;
-  a.dev_count = dev_count; a.dev_start = dev_start;
   a.G = G; a.C = L.C; a.opg = L.opg; a.slots = L.slots;
   a.part = part; a.spill = spill; a.zfirst = zfirst; a.err = err;
   const bool aligned = (reinterpret_cast<uintptr_t>(keys) % 16 == 0) && (reinterpret_cast<uintptr_t>(vals) % 16 == 0) &&
@@ -680,9 +747,8 @@ cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, cons
   const bool masked = mask != nullptr;
   cudaError_t e;
   if (ev_start) cudaEventRecord(ev_start, stream);
-  if (L.maxslots == 1) e = launch_slots<1>(L, a, masked, aligned, stream);
-  else if (L.maxslots == 2) e = launch_slots<2>(L, a, masked, aligned, stream);
-  else e = launch_slots<4>(L, a, masked, aligned, stream);
+  const bool m34 = state_out != nullptr || (out && (out->m3 || out->m4));
+  e = m34 ? launch_m<true>(L, a, masked, aligned, stream) : launch_m<false>(L, a, masked, aligned, stream);
   if (e != cudaSuccess) return e;
   if (ev_stop) cudaEventRecord(ev_stop, stream);
   (*launches)++;

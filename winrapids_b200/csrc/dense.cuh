@@ -19,7 +19,11 @@ constexpr int kDenseColBudget = 12288;  // 2 * C * n_groups doubles of column bu
 //   K        shift of this state   sumoff   sum(v - K) over finite rows
 //   meanoff  mean(v) - K           m2       sum((v - mean)^2) over finite rows
 //   min/max  over non-NaN rows     zfirst   (first zero row << 1 | sign), bits of a u64
-enum { ST_NN = 0, ST_NF, ST_K, ST_SUMOFF, ST_MEANOFF, ST_M2, ST_MIN, ST_MAX, ST_ZFIRST, ST_COUNT };
+//   m3, m4   sum((v - mean)^3), sum((v - mean)^4) over finite rows (0 when not requested)
+enum { ST_NN = 0, ST_NF, ST_K, ST_SUMOFF, ST_MEANOFF, ST_M2, ST_MIN, ST_MAX, ST_ZFIRST, ST_M3, ST_M4, ST_COUNT };
+
+// u64 words per group of a CTA's spill state (counts, +-inf counts, shift, power sums, extrema).
+constexpr int kDenseSpillFields = 10;
 
 struct DenseLaunch {
   int grid;       // CTAs
@@ -37,15 +41,12 @@ size_t dense_smem_bytes(int G, int C);
 
 // Enqueue the dense moments pipeline.  `part` holds part_doubles, `spill`
 // spill_words u64, `zfirst` G u64, `err` one u32.  Writes either final outputs (`out`) or, when `state_out` is not
-// NULL, the merged state table of this call (ST_COUNT * G doubles).  With dev_count / dev_start the
-// kernel reads its row count and first row from device memory (one part of a partition; `n` is
-// then ignored and the part start must keep keys and values 16-byte aligned).
+// NULL, the merged state table of this call (ST_COUNT * G doubles).
 cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, const double* vals, const uint64_t* mask,
                                  long long n, long long row_offset, int G, double* part, unsigned long long* spill,
                                  unsigned long long* zfirst, uint32_t* err, const tbgb_moments* out, double* state_out,
                                  cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start = nullptr,
-                                 cudaEvent_t ev_stop = nullptr, const int64_t* dev_count = nullptr,
-                                 const int64_t* dev_start = nullptr);
+                                 cudaEvent_t ev_stop = nullptr);
 
 cudaError_t merge_states_launch(const double* states, int n_states, int G, const tbgb_moments* out,
                                 cudaStream_t stream, uint64_t* launches);

@@ -8,7 +8,7 @@
 // tbgb_groupby_dense, but its scratch (per-CTA partial states, spill states,
 // first-zero trackers, the device error word) lives in one file-scope device
 // array.  That array is part of this library's image: every GPU that loads the
-// library holds it (about 8.5 MB) until the process exits.
+// library holds it (about 10.5 MB) until the process exits.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -25,7 +25,7 @@ constexpr int kMaxDevices = 64;
 
 // Word counts of the scratch regions at the largest accepted size.
 constexpr size_t kPartWords = static_cast<size_t>(tbgb::ST_COUNT) * kNoAllocMaxCtas * 2 * 256;
-constexpr size_t kSpillWords = static_cast<size_t>(8) * kNoAllocMaxCtas * kNoAllocMaxGroups;
+constexpr size_t kSpillWords = static_cast<size_t>(tbgb::kDenseSpillFields) * kNoAllocMaxCtas * kNoAllocMaxGroups;
 constexpr size_t kZeroWords = kNoAllocMaxGroups;
 constexpr size_t kErrWords = 32;
 constexpr size_t kScratchWords = kPartWords + kSpillWords + kZeroWords + kErrWords;

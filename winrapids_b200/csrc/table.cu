@@ -96,14 +96,18 @@ __device__ __forceinline__ double slot_shift(unsigned long long* kw, double v) {
 
 // One non-NaN row into a global slot.
 template <bool FULL>
-__device__ __forceinline__ void global_row(unsigned long long* p, double v, long long grow) {
+__device__ __forceinline__ void global_row(unsigned long long* p, double v, long long grow, bool m34) {
   if constexpr (FULL) {
     atomicAdd(p + FL_NN, 1ull);
     if (is_finite(v)) {
-      const double d = v - slot_shift(p + FL_K, v);
+      const double d = v - slot_shift(p + FL_K, v), dd = d * d;
       atomicAdd(reinterpret_cast<double*>(p + FL_S1), d);
-      atomicAdd(reinterpret_cast<double*>(p + FL_S2), d * d);
+      atomicAdd(reinterpret_cast<double*>(p + FL_S2), dd);
       atomicAdd(p + FL_NF, 1ull);
+      if (m34) {
+        atomicAdd(reinterpret_cast<double*>(p + FL_S3), dd * d);
+        atomicAdd(reinterpret_cast<double*>(p + FL_S4), dd * dd);
+      }
     }
     const unsigned long long o = f2o(v);
     if (o < __ldcg(p + FL_MN)) atomicMin(p + FL_MN, o);
@@ -124,6 +128,8 @@ struct LocalTable {
   unsigned long long* K;     // FULL
   double* s1;                // FULL: sum(v - K); SUMCOUNT: sum(v)
   double* s2;                // FULL
+  double* s3;                // FULL: sum((v - K)^3)
+  double* s4;                // FULL: sum((v - K)^4)
   unsigned long long* mn;    // FULL
   unsigned long long* mx;    // FULL
   unsigned long long* zf;    // FULL
@@ -132,7 +138,7 @@ struct LocalTable {
   uint32_t* fill;
 
   static constexpr size_t bytes() {
-    return FULL ? static_cast<size_t>(LS) * (7 * 8 + 2 * 4) + 16 : static_cast<size_t>(LS) * (2 * 8 + 4) + 16;
+    return FULL ? static_cast<size_t>(LS) * (9 * 8 + 2 * 4) + 16 : static_cast<size_t>(LS) * (2 * 8 + 4) + 16;
   }
 
   __device__ __forceinline__ void carve(unsigned char* sm) {
@@ -142,6 +148,8 @@ struct LocalTable {
       K = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
       s1 = reinterpret_cast<double*>(q); q += LS * 8;
       s2 = reinterpret_cast<double*>(q); q += LS * 8;
+      s3 = reinterpret_cast<double*>(q); q += LS * 8;
+      s4 = reinterpret_cast<double*>(q); q += LS * 8;
       mn = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
       mx = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
       zf = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
@@ -162,6 +170,8 @@ struct LocalTable {
       if constexpr (FULL) {
         K[s] = K_UNSET;
         s2[s] = 0.0;
+        s3[s] = 0.0;
+        s4[s] = 0.0;
         mn[s] = f2o(pos_inf());
         mx[s] = f2o(neg_inf());
         zf[s] = ~0ull;
@@ -193,7 +203,7 @@ struct LocalTable {
     return -1;
   }
 
-  __device__ __forceinline__ void row(int s, double v, long long grow) {
+  __device__ __forceinline__ void row(int s, double v, long long grow, bool m34) {
     atomicAdd(nn + s, 1u);
     if constexpr (FULL) {
       if (is_finite(v)) {
@@ -202,10 +212,14 @@ struct LocalTable {
           kb = atomicCAS(K + s, K_UNSET, dbits(v));
           if (kb == K_UNSET) kb = dbits(v);
         }
-        const double d = v - bitsd(kb);
+        const double d = v - bitsd(kb), dd = d * d;
         atomicAdd(s1 + s, d);
-        atomicAdd(s2 + s, d * d);
+        atomicAdd(s2 + s, dd);
         atomicAdd(nf + s, 1u);
+        if (m34) {
+          atomicAdd(s3 + s, dd * d);
+          atomicAdd(s4 + s, dd * dd);
+        }
       }
       const unsigned long long o = f2o(v);
       if (o < *reinterpret_cast<volatile unsigned long long*>(mn + s)) atomicMin(mn + s, o);
@@ -216,8 +230,9 @@ struct LocalTable {
     }
   }
 
-  // Merges local slot s into global slot p.
-  __device__ __forceinline__ void flush(int s, unsigned long long* p) {
+  // Merges local slot s into global slot p: power sums re-centred from the local shift K_l
+  // to the global K_g, sum (d + off)^k with off = K_l - K_g.
+  __device__ __forceinline__ void flush(int s, unsigned long long* p, bool m34) {
     if constexpr (FULL) {
       const unsigned long long n_nn = nn[s], n_f = nf[s];
       if (n_nn) atomicAdd(p + FL_NN, n_nn);
@@ -225,9 +240,16 @@ struct LocalTable {
         const double Kl = bitsd(K[s]);
         const double Kg = slot_shift(p + FL_K, Kl);
         const double off = Kl - Kg, a1 = s1[s], a2 = s2[s], nfd = static_cast<double>(n_f);
+        const double o2 = off * off;
         atomicAdd(reinterpret_cast<double*>(p + FL_S1), a1 + nfd * off);
         atomicAdd(reinterpret_cast<double*>(p + FL_S2), a2 + off * (2.0 * a1 + nfd * off));
         atomicAdd(p + FL_NF, n_f);
+        if (m34) {
+          const double a3 = s3[s], a4 = s4[s];
+          atomicAdd(reinterpret_cast<double*>(p + FL_S3), a3 + 3.0 * off * a2 + 3.0 * o2 * a1 + nfd * o2 * off);
+          atomicAdd(reinterpret_cast<double*>(p + FL_S4),
+                    a4 + 4.0 * off * a3 + 6.0 * o2 * a2 + 4.0 * o2 * off * a1 + nfd * o2 * o2);
+        }
       }
       if (n_nn) {
         if (mn[s] < __ldcg(p + FL_MN)) atomicMin(p + FL_MN, mn[s]);
@@ -332,7 +354,7 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
       const long long grow = a.row_offset + base + r * TNT + tid;
       if constexpr (LOCAL) {
         if (ls[r] >= 0) {
-          if (!is_nan(v[r])) lt.row(ls[r], v[r], grow);
+          if (!is_nan(v[r])) lt.row(ls[r], v[r], grow, a.m34 != 0);
           continue;
         }
       }
@@ -343,7 +365,7 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
       } else {
         gs = kk[r];
       }
-      if (!is_nan(v[r])) global_row<FULL>(T + static_cast<unsigned long long>(gs) * W, v[r], grow);
+      if (!is_nan(v[r])) global_row<FULL>(T + static_cast<unsigned long long>(gs) * W, v[r], grow, a.m34 != 0);
     }
   }
 
@@ -360,7 +382,7 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
       } else {
         gs = static_cast<long long>(k);
       }
-      lt.flush(s, T + static_cast<unsigned long long>(gs) * W);
+      lt.flush(s, T + static_cast<unsigned long long>(gs) * W, a.m34 != 0);
     }
   }
 }
@@ -398,8 +420,8 @@ __device__ __forceinline__ GState slot_state(const unsigned long long* p) {
     s.nf = static_cast<double>(nf);
     s.K = bitsd(p[FL_K]);
     s.sumoff = bitsd(p[FL_S1]);
-    s.meanoff = s.sumoff / s.nf;
-    s.m2 = fmax(bitsd(p[FL_S2]) - s.sumoff * s.meanoff, 0.0);
+    central_from_power(s.nf, s.sumoff, bitsd(p[FL_S2]), bitsd(p[FL_S3]), bitsd(p[FL_S4]), &s.meanoff, &s.m2, &s.m3,
+                       &s.m4);
   }
   s.mn = o2f(p[FL_MN]);
   s.mx = o2f(p[FL_MX]);

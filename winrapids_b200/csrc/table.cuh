@@ -16,7 +16,7 @@ namespace tbgb {
 //   S1   sum(v - K) over finite rows             S2  sum((v - K)^2) over finite rows
 //   MN/MX extrema over non-NaN rows, order-preserving u64 encoding
 //   ID   output row of the group (hash mode)     ZF  first zero row code (row << 1 | sign)
-//   S3/S4 reserved
+//   S3/S4 sum((v - K)^3), sum((v - K)^4) over finite rows, when m3 / m4 are requested
 // SUMCOUNT slot, 32 bytes (one sector): KEY, NN, SUM (finite values), ID.
 enum { FL_KEY = 0, FL_K, FL_NN, FL_NF, FL_S1, FL_S2, FL_MN, FL_MX, FL_ID, FL_ZF, FL_S3, FL_S4, FL_WORDS };
 enum { SC_KEY = 0, SC_NN, SC_SUM, SC_ID, SC_WORDS };
@@ -38,6 +38,7 @@ struct TableArgs {
   unsigned long long* ngroups;  // hash: distinct-key counter
   long long max_groups;
   uint32_t* err;
+  int m34;               // FULL slots: also accumulate sum((v-K)^3), sum((v-K)^4)
 };
 
 struct TablePlan {
