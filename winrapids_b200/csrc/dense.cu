@@ -28,6 +28,7 @@
 //   barriers inside each warp group, so the two roles overlap instead of meeting
 //   at CTA-wide barriers.
 #include <cstdint>
+#include <type_traits>
 
 #include "common.cuh"
 #include "dense.cuh"
@@ -62,8 +63,11 @@ constexpr unsigned long long K_UNSET = 0x7FF8000000000001ull;  // NaN payload no
 constexpr uint32_t NO_RANK = 0xFFFFFFFFu;
 
 // spill state, per CTA, SoA over groups (u64 words)
-enum { SP_N = 0, SP_NINFP, SP_NINFN, SP_K, SP_S1, SP_S2, SP_MN, SP_MX, SP_S3, SP_S4, SP_COUNT };
+// (the third and fourth power sums exist only when m3 / m4 are computed: SP_BASE fields otherwise)
+enum { SP_N = 0, SP_NINFP, SP_NINFN, SP_K, SP_S1, SP_S2, SP_MN, SP_MX, SP_BASE, SP_S3 = SP_BASE, SP_S4, SP_COUNT };
 static_assert(SP_COUNT == kDenseSpillFields, "spill state size exported in dense.cuh");
+template <bool M34>
+__host__ __device__ constexpr int spill_fields() { return M34 ? SP_COUNT : SP_BASE; }
 
 __device__ __forceinline__ void named_bar_sync(int id, int n) {
   asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
@@ -141,12 +145,14 @@ __device__ __forceinline__ void spill_add(unsigned long long* sp, int G, int g, 
   const unsigned long long vb = static_cast<unsigned long long>(__double_as_longlong(v));
   const unsigned long long kb = atomicCAS(sp + SP_K * G + g, K_UNSET, vb);
   const double K = kb == K_UNSET ? v : __longlong_as_double(static_cast<long long>(kb));
-  const double d = v - K, d2 = d * d;
+  const double d = v - K;
   atomicAdd(reinterpret_cast<double*>(sp + SP_S1 * G + g), d);
-  atomicAdd(reinterpret_cast<double*>(sp + SP_S2 * G + g), d2);
+  atomicAdd(reinterpret_cast<double*>(sp + SP_S2 * G + g), d * d);
+  // (written as in the two-moment kernel: how this rare path is written changed the
+  // scheduling of the whole kernel measurably)
   if constexpr (M34) {
-    atomicAdd(reinterpret_cast<double*>(sp + SP_S3 * G + g), d2 * d);
-    atomicAdd(reinterpret_cast<double*>(sp + SP_S4 * G + g), d2 * d2);
+    atomicAdd(reinterpret_cast<double*>(sp + SP_S3 * G + g), d * d * d);
+    atomicAdd(reinterpret_cast<double*>(sp + SP_S4 * G + g), (d * d) * (d * d));
   }
   atomicAdd(sp + SP_N * G + g, 1ull);
   atomicMin(sp + SP_MN * G + g, f2o(v));
@@ -155,19 +161,8 @@ __device__ __forceinline__ void spill_add(unsigned long long* sp, int G, int g, 
 
 // Register accumulators of one owner slot; NCH independent chains shorten the
 // dependency path through S1/S2.
-// With M34 the third and fourth power sums are kept too (m3 / m4 requested).
-template <int NCH, bool M34>
-struct OwnerAcc;
-
 template <int NCH>
-struct HigherSums {  // sum(d^3), sum(d^4) per chain
-  double s3[NCH], s4[NCH];
-};
-template <>
-struct HigherSums<0> {};
-
-template <int NCH, bool M34>
-struct OwnerAcc : HigherSums<M34 ? NCH : 0> {
+struct OwnerAcc {
   double K, s1[NCH], s2[NCH], mn, mx;
   unsigned long long nf;
   bool kset;
@@ -175,38 +170,18 @@ struct OwnerAcc : HigherSums<M34 ? NCH : 0> {
     K = 0.0;
 #pragma unroll
     for (int j = 0; j < NCH; ++j) { s1[j] = 0.0; s2[j] = 0.0; }
-    if constexpr (M34) {
-#pragma unroll
-      for (int j = 0; j < NCH; ++j) { this->s3[j] = 0.0; this->s4[j] = 0.0; }
-    }
     mn = pos_inf(); mx = neg_inf(); nf = 0; kset = false;
-  }
-  __device__ __forceinline__ void pw(int j, double d) {
-    const double dd = d * d;
-    s1[j] += d;
-    s2[j] += dd;
-    if constexpr (M34) {
-      this->s3[j] = fma(dd, d, this->s3[j]);
-      this->s4[j] = fma(dd, dd, this->s4[j]);
-    }
   }
   __device__ __forceinline__ void quad(double x0, double x1, double x2, double x3) {
     const double d0 = x0 - K, d1 = x1 - K, d2 = x2 - K, d3 = x3 - K;
-    if constexpr (M34) {
-      pw(0 % NCH, d0);
-      pw(1 % NCH, d1);
-      pw(2 % NCH, d2);
-      pw(3 % NCH, d3);
-    } else {
-      s1[0 % NCH] += d0;
-      s2[0 % NCH] = fma(d0, d0, s2[0 % NCH]);
-      s1[1 % NCH] += d1;
-      s2[1 % NCH] = fma(d1, d1, s2[1 % NCH]);
-      s1[2 % NCH] += d2;
-      s2[2 % NCH] = fma(d2, d2, s2[2 % NCH]);
-      s1[3 % NCH] += d3;
-      s2[3 % NCH] = fma(d3, d3, s2[3 % NCH]);
-    }
+    s1[0 % NCH] += d0;
+    s2[0 % NCH] = fma(d0, d0, s2[0 % NCH]);
+    s1[1 % NCH] += d1;
+    s2[1 % NCH] = fma(d1, d1, s2[1 % NCH]);
+    s1[2 % NCH] += d2;
+    s2[2 % NCH] = fma(d2, d2, s2[2 % NCH]);
+    s1[3 % NCH] += d3;
+    s2[3 % NCH] = fma(d3, d3, s2[3 % NCH]);
     // extrema by plain compares (no NaN reaches a column); +-0 ties are settled
     // later from the first-zero tracker
     const bool l01 = x0 < x1, l23 = x2 < x3;
@@ -218,12 +193,8 @@ struct OwnerAcc : HigherSums<M34 ? NCH : 0> {
   }
   __device__ __forceinline__ void one(double x) {
     const double d = x - K;
-    if constexpr (M34) {
-      pw(0, d);
-    } else {
-      s1[0] += d;
-      s2[0] = fma(d, d, s2[0]);
-    }
+    s1[0] += d;
+    s2[0] = fma(d, d, s2[0]);
     mn = x < mn ? x : mn;
     mx = x > mx ? x : mx;
   }
@@ -270,23 +241,102 @@ struct OwnerAcc : HigherSums<M34 ? NCH : 0> {
     for (int j = 0; j < NCH; ++j) r += s2[j];
     return r;
   }
+};
+
+// The accumulator of an owner slot when m3 / m4 are requested: the third and fourth
+// power sums as well (kept apart from OwnerAcc so that the common path is unchanged).
+template <int NCH>
+struct OwnerAcc4 {
+  double K, s1[NCH], s2[NCH], s3[NCH], s4[NCH], mn, mx;
+  unsigned long long nf;
+  bool kset;
+  __device__ __forceinline__ void init() {
+    K = 0.0;
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) { s1[j] = 0.0; s2[j] = 0.0; s3[j] = 0.0; s4[j] = 0.0; }
+    mn = pos_inf(); mx = neg_inf(); nf = 0; kset = false;
+  }
+  __device__ __forceinline__ void pw(int j, double d) {
+    const double dd = d * d;
+    s1[j] += d;
+    s2[j] += dd;
+    s3[j] = fma(dd, d, s3[j]);
+    s4[j] = fma(dd, dd, s4[j]);
+  }
+  __device__ __forceinline__ void quad(double x0, double x1, double x2, double x3) {
+    pw(0 % NCH, x0 - K);
+    pw(1 % NCH, x1 - K);
+    pw(2 % NCH, x2 - K);
+    pw(3 % NCH, x3 - K);
+    const bool l01 = x0 < x1, l23 = x2 < x3;
+    const double lo01 = l01 ? x0 : x1, hi01 = l01 ? x1 : x0;
+    const double lo23 = l23 ? x2 : x3, hi23 = l23 ? x3 : x2;
+    const double lo = lo01 < lo23 ? lo01 : lo23, hi = hi01 > hi23 ? hi01 : hi23;
+    mn = lo < mn ? lo : mn;
+    mx = hi > mx ? hi : mx;
+  }
+  __device__ __forceinline__ void one(double x) {
+    pw(0, x - K);
+    mn = x < mn ? x : mn;
+    mx = x > mx ? x : mx;
+  }
+  __device__ __forceinline__ void sweep(const double* cg, int c, int sub, int opg, int G) {
+    if (c <= sub) return;
+    const size_t step = static_cast<size_t>(opg) * G;
+    const double* p = cg + static_cast<size_t>(sub) * G;
+    const int m = (c - sub + opg - 1) / opg;
+    if (!kset) { K = p[0]; kset = true; }
+    int i = 0;
+    if (m >= 4) {
+      double y0 = p[0], y1 = p[step], y2 = p[2 * step], y3 = p[3 * step];
+      for (; i + 8 <= m; i += 4) {
+        const double x0 = y0, x1 = y1, x2 = y2, x3 = y3;
+        const double* q = p + static_cast<size_t>(i + 4) * step;
+        y0 = q[0];
+        y1 = q[step];
+        y2 = q[2 * step];
+        y3 = q[3 * step];
+        quad(x0, x1, x2, x3);
+      }
+      quad(y0, y1, y2, y3);
+      i += 4;
+    }
+    for (; i < m; ++i) one(p[static_cast<size_t>(i) * step]);
+    nf += static_cast<unsigned long long>(m);
+  }
+  __device__ __forceinline__ void add1(double x) {
+    if (!kset) { K = x; kset = true; }
+    one(x);
+    nf += 1;
+  }
+  __device__ __forceinline__ double sum_s1() const {
+    double r = 0.0;
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) r += s1[j];
+    return r;
+  }
+  __device__ __forceinline__ double sum_s2() const {
+    double r = 0.0;
+#pragma unroll
+    for (int j = 0; j < NCH; ++j) r += s2[j];
+    return r;
+  }
   __device__ __forceinline__ double sum_s3() const {
     double r = 0.0;
-    if constexpr (M34) {
 #pragma unroll
-      for (int j = 0; j < NCH; ++j) r += this->s3[j];
-    }
+    for (int j = 0; j < NCH; ++j) r += s3[j];
     return r;
   }
   __device__ __forceinline__ double sum_s4() const {
     double r = 0.0;
-    if constexpr (M34) {
 #pragma unroll
-      for (int j = 0; j < NCH; ++j) r += this->s4[j];
-    }
+    for (int j = 0; j < NCH; ++j) r += s4[j];
     return r;
   }
 };
+
+template <int NCH, bool M34>
+using OwnerAccT = typename std::conditional<M34, OwnerAcc4<NCH>, OwnerAcc<NCH>>::type;
 
 template <int MAXSLOTS, bool MASKED, bool TMA, bool M34>
 __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
@@ -315,7 +365,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   const long long mytiles = t_end - t_begin;
   const bool has_tail = (b == P - 1) && (a.n % TILE) != 0;
   const long long nbatch = mytiles + (has_tail ? 1 : 0);
-  unsigned long long* sp = a.spill + static_cast<size_t>(b) * SP_COUNT * G;
+  unsigned long long* sp = a.spill + static_cast<size_t>(b) * spill_fields<M34>() * G;
 
   for (int i = tid; i < 2 * gp; i += NT) cnt0[i] = 0;
   if (tid < 4) splc[tid] = 0;
@@ -328,8 +378,10 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     sp[SP_S2 * G + g] = 0;
     sp[SP_MN * G + g] = ~0ull;
     sp[SP_MX * G + g] = 0;
-    sp[SP_S3 * G + g] = 0;
-    sp[SP_S4 * G + g] = 0;
+    if constexpr (M34) {
+      sp[SP_S3 * G + g] = 0;
+      sp[SP_S4 * G + g] = 0;
+    }
   }
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], SCATTER_WARPS); }
@@ -526,7 +578,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     const int team = (tid - NSC) / NOW;
     const int o = tid - NSC - team * NOW;  // owner index within the team
     constexpr int NCH = MAXSLOTS == 1 ? (M34 ? 2 : 4) : (MAXSLOTS == 2 && !M34 ? 2 : 1);
-    OwnerAcc<NCH, M34> acc[MAXSLOTS];
+    OwnerAccT<NCH, M34> acc[MAXSLOTS];
     int og[MAXSLOTS], osub[MAXSLOTS];
 #pragma unroll
     for (int q = 0; q < MAXSLOTS; ++q) {
@@ -607,8 +659,10 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
       a.part[ST_M2 * stride + idx] = m2;
       a.part[ST_MIN * stride + idx] = A.mn;
       a.part[ST_MAX * stride + idx] = A.mx;
-      a.part[ST_M3 * stride + idx] = m3;
-      a.part[ST_M4 * stride + idx] = m4;
+      if constexpr (M34) {
+        a.part[ST_M3 * stride + idx] = m3;
+        a.part[ST_M4 * stride + idx] = m4;
+      }
     }
   }
   __syncthreads();
@@ -619,7 +673,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
 // ---------------------------------------------------------------------------
 
 // The spill state of one CTA for group g as a mergeable state.
-__device__ __forceinline__ GState spill_state(const unsigned long long* sp, int G, int g) {
+__device__ __forceinline__ GState spill_state(const unsigned long long* sp, int G, int g, bool m34) {
   GState s = gstate_empty();
   const unsigned long long n = sp[SP_N * G + g];
   const unsigned long long np = sp[SP_NINFP * G + g], nm = sp[SP_NINFN * G + g];
@@ -629,9 +683,9 @@ __device__ __forceinline__ GState spill_state(const unsigned long long* sp, int 
     s.K = __longlong_as_double(static_cast<long long>(sp[SP_K * G + g]));
     s.sumoff = __longlong_as_double(static_cast<long long>(sp[SP_S1 * G + g]));
     central_from_power(s.nf, s.sumoff, __longlong_as_double(static_cast<long long>(sp[SP_S2 * G + g])),
-                       __longlong_as_double(static_cast<long long>(sp[SP_S3 * G + g])),
-                       __longlong_as_double(static_cast<long long>(sp[SP_S4 * G + g])), &s.meanoff, &s.m2, &s.m3,
-                       &s.m4);
+                       m34 ? __longlong_as_double(static_cast<long long>(sp[SP_S3 * G + g])) : 0.0,
+                       m34 ? __longlong_as_double(static_cast<long long>(sp[SP_S4 * G + g])) : 0.0, &s.meanoff, &s.m2,
+                       &s.m3, &s.m4);
     s.mn = o2f(sp[SP_MN * G + g]);
     s.mx = o2f(sp[SP_MX * G + g]);
   }
@@ -648,7 +702,7 @@ __device__ __forceinline__ GState spill_state(const unsigned long long* sp, int 
 __global__ void __launch_bounds__(256) dense_fold_kernel(const double* __restrict__ part,
                                                           const unsigned long long* __restrict__ spill, int P, int G,
                                                           int opg, const unsigned long long* __restrict__ zfirst,
-                                                          tbgb_moments out, double* state_out) {
+                                                          tbgb_moments out, double* state_out, int m34) {
   const int lane = threadIdx.x & 31;
   const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   if (g >= G) return;
@@ -676,7 +730,7 @@ __global__ void __launch_bounds__(256) dense_fold_kernel(const double* __restric
       B.m4 = part[ST_M4 * stride + idx];
       B.zf = ~0ull;
     } else {
-      B = spill_state(spill + static_cast<size_t>(p) * SP_COUNT * G, G, g);
+      B = spill_state(spill + static_cast<size_t>(p) * (m34 ? SP_COUNT : SP_BASE) * G, G, g, m34 != 0);
     }
     gstate_fold(A, B);
   }
@@ -754,7 +808,7 @@ cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, cons
   (*launches)++;
   tbgb_moments o = out ? *out : tbgb_moments{};
   const int blocks = (G * 32 + 255) / 256;
-  dense_fold_kernel<<<blocks, 256, 0, stream>>>(part, spill, L.grid, G, L.opg, zfirst, o, state_out);
+  dense_fold_kernel<<<blocks, 256, 0, stream>>>(part, spill, L.grid, G, L.opg, zfirst, o, state_out, m34 ? 1 : 0);
   e = cudaGetLastError();
   if (e == cudaSuccess) (*launches)++;
   return e;
