@@ -229,6 +229,7 @@ tbgb_status table_common(tbgb_ctx* ctx, bool hash, const void* keys, const tbgb_
   a.max_groups = groups;
   a.err = ctx->err;
   a.m34 = full && (state_out != nullptr || (out && (out->m3 || out->m4)));
+  a.extrema = full && (state_out != nullptr || !out || out->min || out->max);
   if (B == 1) {
     a.keys = keys;
     a.cols = *cols;

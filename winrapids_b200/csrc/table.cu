@@ -15,10 +15,10 @@
 // descriptive.rs:383-435 and extrema the strict `<` / `>` scans of
 // compute_engine.rs:304-322.
 //
-// One persistent 1024-thread CTA per SM streams rows with coalesced evict-first
-// loads, four rows per thread per tile with their loads issued together.  Rows
-// either update the global table with atomics (the first probe of all four rows is
-// issued before any of them is resolved), or -- for skewed keys -- first go to a
+// Persistent CTAs of 1024 threads stream rows with coalesced evict-first loads, one
+// row per thread per step (measured: more rows per thread, with their loads and first
+// probes issued together, ran slower -- the larger body stalls on instruction fetch).
+// Rows either update the global table with atomics, or -- for skewed keys -- first go to a
 // per-CTA shared-memory table of a few thousand slots that absorbs the hot keys and
 // is merged into the global table once at the end (shifted sums re-centred on the
 // global slot's K).  Rows whose key is not admitted to the shared table (it is full)
@@ -35,7 +35,7 @@ namespace tbgb {
 namespace {
 
 constexpr int TNT = 1024;           // threads per CTA
-constexpr int TR = 4;               // rows per thread per tile
+constexpr int TR = 1;               // rows per thread per tile (more per thread measured slower: a larger body)
 constexpr int TTILE = TNT * TR;     // rows per tile
 constexpr int LS_FULL = 2048;       // shared-table slots with the FULL layout (64 B each)
 constexpr int LS_SC = 4096;         // shared-table slots with the SUMCOUNT layout (20 B each)
@@ -96,7 +96,7 @@ __device__ __forceinline__ double slot_shift(unsigned long long* kw, double v) {
 
 // One non-NaN row into a global slot.
 template <bool FULL>
-__device__ __forceinline__ void global_row(unsigned long long* p, double v, long long grow, bool m34) {
+__device__ __forceinline__ void global_row(unsigned long long* p, double v, long long grow, bool m34, bool extrema) {
   if constexpr (FULL) {
     atomicAdd(p + FL_NN, 1ull);
     if (is_finite(v)) {
@@ -109,10 +109,12 @@ __device__ __forceinline__ void global_row(unsigned long long* p, double v, long
         atomicAdd(reinterpret_cast<double*>(p + FL_S4), dd * dd);
       }
     }
-    const unsigned long long o = f2o(v);
-    if (o < __ldcg(p + FL_MN)) atomicMin(p + FL_MN, o);
-    if (o > __ldcg(p + FL_MX)) atomicMax(p + FL_MX, o);
-    if (v == 0.0) atomicMin(p + FL_ZF, zero_code(grow, v));
+    if (extrema) {
+      const unsigned long long o = f2o(v);
+      if (o < __ldcg(p + FL_MN)) atomicMin(p + FL_MN, o);
+      if (o > __ldcg(p + FL_MX)) atomicMax(p + FL_MX, o);
+      if (v == 0.0) atomicMin(p + FL_ZF, zero_code(grow, v));
+    }
   } else {
     atomicAdd(p + SC_NN, 1ull);
     if (is_finite(v)) atomicAdd(reinterpret_cast<double*>(p + SC_SUM), v);
@@ -133,12 +135,12 @@ struct LocalTable {
   unsigned long long* mn;    // FULL
   unsigned long long* mx;    // FULL
   unsigned long long* zf;    // FULL
-  uint32_t* nn;
-  uint32_t* nf;              // FULL
+  unsigned long long* cnt;   // FULL: non-NaN rows (low 32 bits) + finite rows (high 32 bits), one atomic
+  uint32_t* nn;              // SUMCOUNT: non-NaN rows
   uint32_t* fill;
 
   static constexpr size_t bytes() {
-    return FULL ? static_cast<size_t>(LS) * (9 * 8 + 2 * 4) + 16 : static_cast<size_t>(LS) * (2 * 8 + 4) + 16;
+    return FULL ? static_cast<size_t>(LS) * (10 * 8) + 16 : static_cast<size_t>(LS) * (2 * 8 + 4) + 16;
   }
 
   __device__ __forceinline__ void carve(unsigned char* sm) {
@@ -153,8 +155,7 @@ struct LocalTable {
       mn = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
       mx = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
       zf = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
-      nn = reinterpret_cast<uint32_t*>(q); q += LS * 4;
-      nf = reinterpret_cast<uint32_t*>(q); q += LS * 4;
+      cnt = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
     } else {
       s1 = reinterpret_cast<double*>(q); q += LS * 8;
       nn = reinterpret_cast<uint32_t*>(q); q += LS * 4;
@@ -166,7 +167,7 @@ struct LocalTable {
     for (int s = tid; s < LS; s += TNT) {
       key[s] = kEmptyKey;
       s1[s] = 0.0;
-      nn[s] = 0;
+      if constexpr (!FULL) nn[s] = 0;
       if constexpr (FULL) {
         K[s] = K_UNSET;
         s2[s] = 0.0;
@@ -175,7 +176,7 @@ struct LocalTable {
         mn[s] = f2o(pos_inf());
         mx[s] = f2o(neg_inf());
         zf[s] = ~0ull;
-        nf[s] = 0;
+        cnt[s] = 0;
       }
     }
     if (tid == 0) *fill = 0;
@@ -203,10 +204,11 @@ struct LocalTable {
     return -1;
   }
 
-  __device__ __forceinline__ void row(int s, double v, long long grow, bool m34) {
-    atomicAdd(nn + s, 1u);
+  __device__ __forceinline__ void row(int s, double v, long long grow, bool m34, bool extrema) {
     if constexpr (FULL) {
-      if (is_finite(v)) {
+      const bool fin = is_finite(v);
+      atomicAdd(cnt + s, fin ? 0x100000001ull : 1ull);
+      if (fin) {
         unsigned long long kb = *reinterpret_cast<volatile unsigned long long*>(K + s);
         if (kb == K_UNSET) {
           kb = atomicCAS(K + s, K_UNSET, dbits(v));
@@ -215,26 +217,28 @@ struct LocalTable {
         const double d = v - bitsd(kb), dd = d * d;
         atomicAdd(s1 + s, d);
         atomicAdd(s2 + s, dd);
-        atomicAdd(nf + s, 1u);
         if (m34) {
           atomicAdd(s3 + s, dd * d);
           atomicAdd(s4 + s, dd * dd);
         }
       }
-      const unsigned long long o = f2o(v);
-      if (o < *reinterpret_cast<volatile unsigned long long*>(mn + s)) atomicMin(mn + s, o);
-      if (o > *reinterpret_cast<volatile unsigned long long*>(mx + s)) atomicMax(mx + s, o);
-      if (v == 0.0) atomicMin(zf + s, zero_code(grow, v));
+      if (extrema) {
+        const unsigned long long o = f2o(v);
+        if (o < *reinterpret_cast<volatile unsigned long long*>(mn + s)) atomicMin(mn + s, o);
+        if (o > *reinterpret_cast<volatile unsigned long long*>(mx + s)) atomicMax(mx + s, o);
+        if (v == 0.0) atomicMin(zf + s, zero_code(grow, v));
+      }
     } else {
+      atomicAdd(nn + s, 1u);
       if (is_finite(v)) atomicAdd(s1 + s, v);
     }
   }
 
   // Merges local slot s into global slot p: power sums re-centred from the local shift K_l
   // to the global K_g, sum (d + off)^k with off = K_l - K_g.
-  __device__ __forceinline__ void flush(int s, unsigned long long* p, bool m34) {
+  __device__ __forceinline__ void flush(int s, unsigned long long* p, bool m34, bool extrema) {
     if constexpr (FULL) {
-      const unsigned long long n_nn = nn[s], n_f = nf[s];
+      const unsigned long long n_nn = cnt[s] & 0xFFFFFFFFull, n_f = cnt[s] >> 32;
       if (n_nn) atomicAdd(p + FL_NN, n_nn);
       if (n_f) {
         const double Kl = bitsd(K[s]);
@@ -251,7 +255,7 @@ struct LocalTable {
                     a4 + 4.0 * off * a3 + 6.0 * o2 * a2 + 4.0 * o2 * off * a1 + nfd * o2 * o2);
         }
       }
-      if (n_nn) {
+      if (n_nn && extrema) {
         if (mn[s] < __ldcg(p + FL_MN)) atomicMin(p + FL_MN, mn[s]);
         if (mx[s] > __ldcg(p + FL_MX)) atomicMax(p + FL_MX, mx[s]);
         if (zf[s] != ~0ull) atomicMin(p + FL_ZF, zf[s]);
@@ -354,7 +358,7 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
       const long long grow = a.row_offset + base + r * TNT + tid;
       if constexpr (LOCAL) {
         if (ls[r] >= 0) {
-          if (!is_nan(v[r])) lt.row(ls[r], v[r], grow, a.m34 != 0);
+          if (!is_nan(v[r])) lt.row(ls[r], v[r], grow, a.m34 != 0, a.extrema != 0);
           continue;
         }
       }
@@ -365,7 +369,8 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
       } else {
         gs = kk[r];
       }
-      if (!is_nan(v[r])) global_row<FULL>(T + static_cast<unsigned long long>(gs) * W, v[r], grow, a.m34 != 0);
+      if (!is_nan(v[r]))
+        global_row<FULL>(T + static_cast<unsigned long long>(gs) * W, v[r], grow, a.m34 != 0, a.extrema != 0);
     }
   }
 
@@ -382,7 +387,7 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
       } else {
         gs = static_cast<long long>(k);
       }
-      lt.flush(s, T + static_cast<unsigned long long>(gs) * W, a.m34 != 0);
+      lt.flush(s, T + static_cast<unsigned long long>(gs) * W, a.m34 != 0, a.extrema != 0);
     }
   }
 }

@@ -39,6 +39,7 @@ struct TableArgs {
   long long max_groups;
   uint32_t* err;
   int m34;               // FULL slots: also accumulate sum((v-K)^3), sum((v-K)^4)
+  int extrema;           // FULL slots: also track min / max / first zero
 };
 
 struct TablePlan {
