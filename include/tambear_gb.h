@@ -38,6 +38,13 @@
  *                                   on the device instead of the host
  *   tbgb_factorize_i64              Dictionary::encode (crates/tambear/src/dictionary.rs:40-75):
  *                                   codes in first-seen order, for int64 keys
+ *   tbgb_filter_mask                FilterJit::filter_mask (crates/tambear/src/filter_jit.rs:71-121)
+ *   tbgb_mask_and / _or / _xor /    MaskOp::mask_*_gpu (filter_jit.rs:339-440) and the host
+ *   tbgb_mask_not / _popcount       mask_and / mask_or / mask_xor / mask_not / mask_popcount (:130-181)
+ *   tbgb_tile_stats_build           TileColumnStats::from_slice (crates/tambear/src/format.rs:82-107)
+ *   tbgb_tile_skip_mask             tile_skip_mask_gt / _lt (format.rs:182-189), can_skip_* (:111-136)
+ *   tbgb_mask_skip_tiles            no counterpart: applies a tile-skip mask to a row mask so the
+ *                                   groupby kernels never read skipped tiles
  *   tbgb_hash_partition             no counterpart in the reference (single GPU); routes rows to
  *                                   the GPU that owns their key for the sharded high-cardinality path
  *
@@ -227,6 +234,60 @@ tbgb_status tbgb_group_index_build(tbgb_ctx* ctx, const int32_t* d_keys, int64_t
  * tbgb_sync report TBGB_ERR_TABLE_FULL). */
 tbgb_status tbgb_factorize_i64(tbgb_ctx* ctx, const int64_t* d_keys, int64_t n, int64_t max_groups, int32_t* d_codes,
                                int64_t* d_uniques, int64_t* d_n_uniques, void* stream);
+
+/* ---- row masks and tile statistics (mask-not-filter) --------------------------------
+ * A row mask for n_rows rows is ceil(n_rows / 64) u64 words in device memory, row i in
+ * bit i % 64 of word i / 64, the bits of rows >= n_rows of the last word 0
+ * (FilterJit::filter_mask, crates/tambear/src/filter_jit.rs:71-121 and :196-243).  Every
+ * groupby entry point takes such a mask (d_mask); the table-path kernels test a row's
+ * bit before they read its columns, so rows in all-zero mask regions cost no column
+ * reads.  Word pointers must be 8-byte aligned; out may alias an input. */
+
+/* FilterJit::filter_mask (filter_jit.rs:71-121): bit i = in(i) && pred(col[i]) (tbgb_pred; a
+ * comparison with NaN fails, TBGB_PRED_NONE passes every row), with in(i) the bit of
+ * d_in_mask (NULL: every row).  col[i] is read only where in(i) is set, so a mask from
+ * tbgb_mask_skip_tiles keeps skipped tiles unread.  d_mask may alias d_in_mask. */
+tbgb_status tbgb_filter_mask(tbgb_ctx* ctx, const void* d_col, int32_t dtype, int64_t n, int32_t pred,
+                             double threshold, const uint64_t* d_in_mask, uint64_t* d_mask, void* stream);
+/* MaskOp::mask_and_gpu / mask_or_gpu / mask_xor_gpu (filter_jit.rs:339-396): word by
+ * word over n_words words. */
+tbgb_status tbgb_mask_and(tbgb_ctx* ctx, const uint64_t* d_a, const uint64_t* d_b, uint64_t* d_out, int64_t n_words,
+                          void* stream);
+tbgb_status tbgb_mask_or(tbgb_ctx* ctx, const uint64_t* d_a, const uint64_t* d_b, uint64_t* d_out, int64_t n_words,
+                         void* stream);
+tbgb_status tbgb_mask_xor(tbgb_ctx* ctx, const uint64_t* d_a, const uint64_t* d_b, uint64_t* d_out, int64_t n_words,
+                          void* stream);
+/* MaskOp::mask_not_gpu (filter_jit.rs:397-416): ~a with the bits of rows >= n_rows
+ * cleared; n_words must be ceil(n_rows / 64). */
+tbgb_status tbgb_mask_not(tbgb_ctx* ctx, const uint64_t* d_a, uint64_t* d_out, int64_t n_words, int64_t n_rows,
+                          void* stream);
+/* MaskOp::mask_popcount_gpu (filter_jit.rs:418-440), mask_popcount (:130-144): set bits of
+ * rows [0, n_rows) into *d_count (device u64); n_words must be ceil(n_rows / 64). */
+tbgb_status tbgb_mask_popcount(tbgb_ctx* ctx, const uint64_t* d_mask, int64_t n_words, int64_t n_rows,
+                               uint64_t* d_count, void* stream);
+
+/* TileColumnStats (crates/tambear/src/format.rs:60-73), 40 bytes. */
+typedef struct {
+  double min;        /* strict `<` scan from +inf (NaN never wins)                    */
+  double max;        /* strict `>` scan from -inf                                     */
+  double sum;        /* compensated sum (the serial Kahan result within a few ulps)   */
+  uint32_t count;    /* rows of the tile                                              */
+  uint32_t n_valid;  /* = count (dense columns)                                       */
+  uint64_t reserved; /* 0                                                             */
+} tbgb_tile_stats;
+/* TileColumnStats::from_slice (format.rs:82-107) for every tile of tile_rows rows
+ * (1 <= tile_rows < 2^32; the last tile may be shorter): ceil(n / tile_rows) entries. */
+tbgb_status tbgb_tile_stats_build(tbgb_ctx* ctx, const void* d_col, int32_t dtype, int64_t n, int64_t tile_rows,
+                                  tbgb_tile_stats* d_stats, void* stream);
+/* tile_skip_mask_gt / _lt (format.rs:182-189) and can_skip_gte / _lte (:125-136):
+ * d_skip[t] = 1 when no row of tile t can pass pred (TBGB_PRED_GT / GE / LT / LE only). */
+tbgb_status tbgb_tile_skip_mask(tbgb_ctx* ctx, const tbgb_tile_stats* d_stats, int64_t n_tiles, int32_t pred,
+                                double threshold, uint8_t* d_skip, void* stream);
+/* Row mask of the rows outside skipped tiles: d_out = d_mask (every row when NULL) with
+ * the rows of tiles t with d_skip[t] != 0 cleared (ceil(n_rows / 64) words; d_skip has
+ * ceil(n_rows / tile_rows) entries).  Passing d_out to a groupby skips those tiles' reads. */
+tbgb_status tbgb_mask_skip_tiles(tbgb_ctx* ctx, const uint64_t* d_mask, const uint8_t* d_skip, int64_t tile_rows,
+                                 int64_t n_rows, uint64_t* d_out, void* stream);
 
 /* ---- sharded int64-key groupby (one process / GPU per shard) ----------------------
  * Routes the rows of this shard that pass mask and pred to their owner part

@@ -8,6 +8,7 @@ CPU baseline; the product (winrapids_b200/) never imports it.
 from __future__ import annotations
 
 import ctypes as C
+import math
 from pathlib import Path
 
 import numpy as np
@@ -51,6 +52,13 @@ def lib() -> C.CDLL:
         "orc_nan_mask": (i64, [vp, i64, vp]),
         "orc_filter_mask": (None, [C.c_int, f64, vp, i64, vp]),
         "orc_map2": (None, [C.c_int, vp, vp, i64, vp]),
+        "orc_mask_and": (None, [vp, vp, i64, vp]),
+        "orc_mask_or": (None, [vp, vp, i64, vp]),
+        "orc_mask_xor": (None, [vp, vp, i64, vp]),
+        "orc_mask_not": (None, [vp, i64, i64, vp]),
+        "orc_mask_popcount": (i64, [vp, i64]),
+        "orc_tile_stats_build": (None, [vp, i64, i64, vp]),
+        "orc_tile_skip": (None, [vp, i64, C.c_int, f64, vp]),
         "orc_moments_grouped": (C.c_int, [vp, vp, i64, i32, C.POINTER(_Moments)]),
         "orc_moments_grouped_mt": (C.c_int, [vp, vp, vp, i64, i32, C.c_int, C.POINTER(_Moments)]),
         "orc_moments_grouped_masked": (C.c_int, [vp, vp, vp, i64, i32, C.POINTER(_Moments)]),
@@ -146,6 +154,109 @@ def filter_mask(pred, threshold, values):
     m = np.zeros(max(1, (v.size + 63) // 64), np.uint64)
     lib().orc_filter_mask(PRED_IDS[pred], float(threshold), _p(v), v.size, _p(m))
     return m[: (v.size + 63) // 64]
+
+
+def _words(m):
+    return np.ascontiguousarray(m, dtype=np.uint64)
+
+
+def mask_and(a, b):
+    """mask_and (filter_jit.rs:151-154)."""
+    a, b = _words(a), _words(b)
+    if a.size != b.size:
+        raise ValueError("mask_and: length mismatch")
+    out = np.empty_like(a)
+    lib().orc_mask_and(_p(a), _p(b), a.size, _p(out))
+    return out
+
+
+def mask_or(a, b):
+    """mask_or (filter_jit.rs:157-160)."""
+    a, b = _words(a), _words(b)
+    if a.size != b.size:
+        raise ValueError("mask_or: length mismatch")
+    out = np.empty_like(a)
+    lib().orc_mask_or(_p(a), _p(b), a.size, _p(out))
+    return out
+
+
+def mask_xor(a, b):
+    """mask_xor (filter_jit.rs:163-166)."""
+    a, b = _words(a), _words(b)
+    if a.size != b.size:
+        raise ValueError("mask_xor: length mismatch")
+    out = np.empty_like(a)
+    lib().orc_mask_xor(_p(a), _p(b), a.size, _p(out))
+    return out
+
+
+def mask_not(m, n_rows):
+    """mask_not (filter_jit.rs:173-181)."""
+    m = _words(m)
+    if n_rows % 64 and n_rows // 64 >= m.size:
+        raise IndexError("mask_not: n_rows beyond the mask")
+    out = np.empty_like(m)
+    lib().orc_mask_not(_p(m), m.size, int(n_rows), _p(out))
+    return out
+
+
+def mask_popcount(m, n_rows):
+    """mask_popcount (filter_jit.rs:130-144)."""
+    m = _words(m)
+    if (n_rows + 63) // 64 > m.size:
+        raise IndexError("mask_popcount: n_rows beyond the mask")
+    return int(lib().orc_mask_popcount(_p(m), int(n_rows)))
+
+
+TILE_STATS_DTYPE = np.dtype([("min", "<f8"), ("max", "<f8"), ("sum", "<f8"), ("count", "<u4"),
+                             ("n_valid", "<u4"), ("reserved", "<u8")])
+
+
+def tile_stats(values, tile_rows):
+    """TileColumnStats::from_slice (format.rs:82-107) of every tile of tile_rows rows."""
+    v = _f64(values)
+    n_tiles = (v.size + tile_rows - 1) // tile_rows
+    out = np.zeros(max(1, n_tiles), TILE_STATS_DTYPE)
+    lib().orc_tile_stats_build(_p(v), v.size, int(tile_rows), _p(out))
+    return out[:n_tiles]
+
+
+def tile_skip(stats, pred, threshold):
+    """can_skip_gt / _gte / _lt / _lte (format.rs:111-136): 1 where the tile can be skipped."""
+    st = np.ascontiguousarray(stats, dtype=TILE_STATS_DTYPE)
+    out = np.zeros(max(1, st.size), np.uint8)
+    lib().orc_tile_skip(_p(st), st.size, PRED_IDS[pred], float(threshold), _p(out))
+    return out[: st.size]
+
+
+def _fmin(a, b):
+    """Rust f64::min: the other operand when one is NaN."""
+    if a != a:
+        return b
+    if b != b:
+        return a
+    return a if a < b else b
+
+
+def _fmax(a, b):
+    if a != a:
+        return b
+    if b != b:
+        return a
+    return a if a > b else b
+
+
+def tile_global_stats(stats):
+    """global_min / global_max / global_sum / global_count / global_mean (format.rs:144-175):
+    header-only folds over the tiles (min / max over tiles with n_valid > 0)."""
+    mn, mx, s, c = math.inf, -math.inf, 0.0, 0
+    for t in stats:
+        if int(t["n_valid"]) > 0:
+            mn = _fmin(mn, float(t["min"]))
+            mx = _fmax(mx, float(t["max"]))
+        s += float(t["sum"])
+        c += int(t["count"])
+    return {"min": mn, "max": mx, "sum": s, "count": c, "mean": (s / c) if c else math.nan}
 
 
 def map2(expr, a, b):

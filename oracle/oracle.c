@@ -317,6 +317,74 @@ void orc_filter_mask(int pred, double thr, const double* vals, int64_t n, uint64
   }
 }
 
+/* mask_and / mask_or / mask_xor (filter_jit.rs:151-166): word by word. */
+void orc_mask_and(const uint64_t* a, const uint64_t* b, int64_t n_words, uint64_t* out) {
+  for (int64_t i = 0; i < n_words; ++i) out[i] = a[i] & b[i];
+}
+void orc_mask_or(const uint64_t* a, const uint64_t* b, int64_t n_words, uint64_t* out) {
+  for (int64_t i = 0; i < n_words; ++i) out[i] = a[i] | b[i];
+}
+void orc_mask_xor(const uint64_t* a, const uint64_t* b, int64_t n_words, uint64_t* out) {
+  for (int64_t i = 0; i < n_words; ++i) out[i] = a[i] ^ b[i];
+}
+
+/* mask_not (filter_jit.rs:173-181): flip every word, then keep only the n_rows % 64
+ * valid bits of word n_rows / 64 when n_rows is not a multiple of 64. */
+void orc_mask_not(const uint64_t* a, int64_t n_words, int64_t n_rows, uint64_t* out) {
+  for (int64_t i = 0; i < n_words; ++i) out[i] = ~a[i];
+  const int64_t rem = n_rows % 64;
+  if (rem != 0) out[n_rows / 64] &= (1ULL << rem) - 1;
+}
+
+/* mask_popcount (filter_jit.rs:130-144): full words, then the valid bits of the last. */
+int64_t orc_mask_popcount(const uint64_t* mask, int64_t n_rows) {
+  const int64_t full = n_rows / 64, rem = n_rows % 64;
+  int64_t c = 0;
+  for (int64_t i = 0; i < full; ++i) c += __builtin_popcountll(mask[i]);
+  if (rem != 0) c += __builtin_popcountll(mask[full] & ((1ULL << rem) - 1));
+  return c;
+}
+
+/* TileColumnStats::from_slice (format.rs:82-107): strict `<` / `>` scans from +-inf and a
+ * Kahan-compensated running sum, in row order. */
+void orc_tile_stats_build(const double* vals, int64_t n, int64_t tile_rows, orc_tile_stats* out) {
+  const int64_t n_tiles = n > 0 ? (n + tile_rows - 1) / tile_rows : 0;
+  for (int64_t t = 0; t < n_tiles; ++t) {
+    const int64_t lo = t * tile_rows, hi = lo + tile_rows < n ? lo + tile_rows : n;
+    double mn = INFINITY, mx = -INFINITY, sum = 0.0, c = 0.0;
+    for (int64_t i = lo; i < hi; ++i) {
+      const double v = vals[i];
+      if (v < mn) mn = v;
+      if (v > mx) mx = v;
+      const double y = v - c;
+      const double tt = sum + y;
+      c = (tt - sum) - y;
+      sum = tt;
+    }
+    out[t].min = mn;
+    out[t].max = mx;
+    out[t].sum = sum;
+    out[t].count = (uint32_t)(hi - lo);
+    out[t].n_valid = (uint32_t)(hi - lo);
+    out[t].reserved = 0;
+  }
+}
+
+/* can_skip_gt / _lt / _gte / _lte (format.rs:111-136), tile_skip_mask_gt / _lt (:182-189). */
+void orc_tile_skip(const orc_tile_stats* st, int64_t n_tiles, int pred, double thr, uint8_t* skip) {
+  for (int64_t t = 0; t < n_tiles; ++t) {
+    int s = 0;
+    switch (pred) {
+      case ORC_PRED_GT: s = st[t].max <= thr; break;
+      case ORC_PRED_LT: s = st[t].min >= thr; break;
+      case ORC_PRED_GE: s = st[t].max < thr; break;
+      case ORC_PRED_LE: s = st[t].min > thr; break;
+      default: s = 0;
+    }
+    skip[t] = (uint8_t)s;
+  }
+}
+
 /* phi_map2_eval (compute_engine.rs:627-636). */
 void orc_map2(int op, const double* a, const double* b, int64_t n, double* out) {
   for (int64_t i = 0; i < n; ++i) {

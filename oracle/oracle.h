@@ -13,6 +13,9 @@
  *   - moments_grouped      crates/tambear/src/descriptive.rs:383-435, nan_mask_count :591-603,
  *                          extremum_grouped_nan_safe :606-620, MomentStats :97-114
  *   - filter mask          crates/tambear/src/filter_jit.rs:196-243 (bit i of word i/64 <-> row i)
+ *   - mask algebra         crates/tambear/src/filter_jit.rs:130-181 (mask_and / or / xor / not / popcount)
+ *   - tile statistics      crates/tambear/src/format.rs:82-136,182-189 (TileColumnStats::from_slice,
+ *                          can_skip_*, tile_skip_mask_gt / _lt)
  *   - SplitMix64 / u01 / Box-Muller  crates/tambear/src/rng.rs:34-36,64-85,165-176
  *
  * Parity is pinned by the reference's own golden vectors (see tests/test_oracle_golden.py).
@@ -70,6 +73,24 @@ enum { ORC_PRED_GT = 0, ORC_PRED_NOT_NAN = 1, ORC_PRED_FINITE = 2, ORC_PRED_LT =
 void orc_filter_mask(int pred, double threshold, const double* vals, int64_t n, uint64_t* mask);
 enum { ORC_MAP2_ADD = 0, ORC_MAP2_MUL = 1, ORC_MAP2_SUB = 2, ORC_MAP2_MUL_PLUS1 = 3 };
 void orc_map2(int op, const double* a, const double* b, int64_t n, double* out);
+
+/* ---- mask algebra (filter_jit.rs:130-181) ---- */
+void orc_mask_and(const uint64_t* a, const uint64_t* b, int64_t n_words, uint64_t* out);
+void orc_mask_or(const uint64_t* a, const uint64_t* b, int64_t n_words, uint64_t* out);
+void orc_mask_xor(const uint64_t* a, const uint64_t* b, int64_t n_words, uint64_t* out);
+void orc_mask_not(const uint64_t* a, int64_t n_words, int64_t n_rows, uint64_t* out);
+int64_t orc_mask_popcount(const uint64_t* mask, int64_t n_rows);
+
+/* ---- per-tile column statistics (format.rs:60-136,182-189) ---- */
+typedef struct {
+  double min, max, sum;
+  uint32_t count, n_valid;
+  uint64_t reserved;
+} orc_tile_stats;
+/* TileColumnStats::from_slice of every tile of tile_rows rows (serial Kahan sum). */
+void orc_tile_stats_build(const double* vals, int64_t n, int64_t tile_rows, orc_tile_stats* out);
+/* can_skip_gt / _gte / _lt / _lte with pred ORC_PRED_GT / GE / LT / LE. */
+void orc_tile_skip(const orc_tile_stats* st, int64_t n_tiles, int pred, double threshold, uint8_t* skip);
 
 /* ---- grouped moments: descriptive.rs:383-435 (counts, sums, mins, maxs, m2s, m3s, m4s) ---- */
 typedef struct {

@@ -248,6 +248,51 @@ def main():
              "values": encl(vals), "keys": [0] * 100, "n_groups": 1,
              "expect": {"var_pop": [(100 * 100 - 1) * 0.001 * 0.001 / 12.0]}, "tol": 0.01, "rel": True})
 
+    # ---- FilterJit::filter_mask tests (filter_jit.rs:565-614): words as hex, `check` = asserted bits
+    def fm(cite, pred, thr, vals, expect, check):
+        add({"kind": "filter_mask", "cite": cite, "pred": pred, "threshold": enc(thr), "values": encl(vals),
+             "expect": [hex(w) for w in expect], "check": [hex(c) for c in check]})
+    fm("filter_jit.rs:565-575 filter_gt_threshold", "gt", 4.0, [1.0, 5.0, 3.0, 7.0, 2.0, 8.0], [0b101010], [0x3F])
+    fm("filter_jit.rs:577-582 filter_all_pass", "gt", 0.0, [1.0, 2.0, 3.0, 4.0], [0xF], [0xF])
+    fm("filter_jit.rs:585-590 filter_none_pass", "gt", 100.0, [1.0, 2.0, 3.0], [0], [0x7])
+    fm("filter_jit.rs:593-602 filter_exactly_64_rows", "gt", 0.5, [0.0 if i % 2 == 0 else 1.0 for i in range(64)],
+       [0xAAAAAAAAAAAAAAAA], [0xFFFFFFFFFFFFFFFF])
+    fm("filter_jit.rs:605-614 filter_65_rows_two_words", "gt", 0.5, [1.0] * 65,
+       [0xFFFFFFFFFFFFFFFF, 0x1], [0xFFFFFFFFFFFFFFFF, 0xFFFFFFFFFFFFFFFF])
+
+    # ---- mask algebra (filter_jit.rs:616-628, 643-744; CPU and GPU variants assert the same values)
+    def mw(xs):
+        return [hex(x) for x in xs]
+    for op, exp, cites in (("and", 0b0100, "643-646 cpu_mask_and / 688-693 gpu_mask_and"),
+                           ("or", 0b0111, "649-652 cpu_mask_or / 695-700 gpu_mask_or"),
+                           ("xor", 0b0011, "655-658 cpu_mask_xor / 702-707 gpu_mask_xor")):
+        add({"kind": "mask_binary", "cite": f"filter_jit.rs:{cites}", "op": op,
+             "a": mw([0b0101]), "b": mw([0b0110]), "expect": mw([exp])})
+    add({"kind": "mask_not", "cite": "filter_jit.rs:661-664 cpu_mask_not_full_word",
+         "a": mw([0xFFFFFFFFFFFFFFFF]), "n_rows": 64, "expect": mw([0])})
+    add({"kind": "mask_not", "cite": "filter_jit.rs:667-673 cpu_mask_not_partial_last_word / 709-714 gpu",
+         "a": mw([0b0101]), "n_rows": 4, "expect": mw([0b1010])})
+    add({"kind": "mask_not", "cite": "filter_jit.rs:676-681 cpu_mask_not_trailing_bits_zeroed",
+         "a": mw([0]), "n_rows": 4, "expect": mw([0b1111])})
+    for n_rows, exp in ((128, 4), (66, 3), (6, 2)):
+        add({"kind": "mask_popcount", "cite": f"filter_jit.rs:616-627 filter_mask_popcount n_rows={n_rows}",
+             "mask": mw([0b0110, 0b1001]), "n_rows": n_rows, "expect": exp})
+    add({"kind": "mask_popcount", "cite": "filter_jit.rs:717-724 gpu_mask_popcount_full_words",
+         "mask": mw([0b0101, 0b1001]), "n_rows": 128, "expect": 4})
+    add({"kind": "mask_popcount", "cite": "filter_jit.rs:727-734 gpu_mask_popcount_partial_last_word",
+         "mask": mw([0xFFFFFFFFFFFFFFFF, 0b11]), "n_rows": 66, "expect": 66})
+    add({"kind": "mask_and_popcount", "cite": "filter_jit.rs:737-744 gpu_mask_and_then_popcount",
+         "a": mw([0b0101, 0b0101]), "b": mw([0b0110, 0b0110]), "n_rows": 128, "expect": 2})
+
+    # ---- tile statistics (tb_io.rs:295-333 roundtrip_simple, :336-366 multi_tile_roundtrip):
+    # global min / max / count / mean over the tiles' TileColumnStats (format.rs:141-175)
+    add({"kind": "tile_stats_global", "cite": "tb_io.rs:295-333 roundtrip_simple",
+         "values": encl([1.0, 2.0, 3.0, 4.0, 5.0]), "tile_rows": 65536, "n_tiles": 1,
+         "expect": {"min": enc(1.0), "max": enc(5.0), "count": 5, "mean": enc(3.0)}, "tol": 1e-10})
+    add({"kind": "tile_stats_global", "cite": "tb_io.rs:336-366 multi_tile_roundtrip", "arange": 10000,
+         "tile_rows": 1024, "n_tiles": 10,
+         "expect": {"min": enc(0.0), "max": enc(9999.0), "count": 10000, "mean": enc(4999.5)}, "tol": 0.01})
+
     OUT.write_text(json.dumps(g, indent=1))
     print(f"wrote {OUT} ({len(g['cases'])} cases)")
 

@@ -239,3 +239,74 @@ def test_factorize_oracle_first_seen_order():
     codes, uniq = oracle.factorize_first_seen([5, 3, 5, -7, 3, 2**63 - 1, -(2**63)])
     assert codes.tolist() == [0, 1, 0, 2, 1, 3, 4]
     assert uniq.tolist() == [5, 3, -7, 2**63 - 1, -(2**63)]
+
+
+# ---- mask-not-filter plumbing: FilterJit masks, mask algebra, tile statistics ----
+
+def words(xs):
+    return np.array([int(x, 16) for x in xs], dtype=np.uint64)
+
+
+@pytest.mark.parametrize("case", ids("filter_mask"), ids=lambda c: c["cite"])
+def test_filter_mask_golden(case):
+    vals = [dec(v) for v in case["values"]]
+    m = oracle.filter_mask(case["pred"], dec(case["threshold"]), vals)
+    exp, chk = words(case["expect"]), words(case["check"])
+    assert m.size == exp.size == (len(vals) + 63) // 64
+    assert np.array_equal(m & chk, exp)
+
+
+@pytest.mark.parametrize("case", ids("mask_binary"), ids=lambda c: c["cite"])
+def test_mask_binary_golden(case):
+    f = {"and": oracle.mask_and, "or": oracle.mask_or, "xor": oracle.mask_xor}[case["op"]]
+    assert np.array_equal(f(words(case["a"]), words(case["b"])), words(case["expect"]))
+
+
+@pytest.mark.parametrize("case", ids("mask_not"), ids=lambda c: c["cite"])
+def test_mask_not_golden(case):
+    out = oracle.mask_not(words(case["a"]), case["n_rows"])
+    assert np.array_equal(out, words(case["expect"]))
+
+
+@pytest.mark.parametrize("case", ids("mask_popcount") + ids("mask_and_popcount"), ids=lambda c: c["cite"])
+def test_mask_popcount_golden(case):
+    if case["kind"] == "mask_and_popcount":
+        m = oracle.mask_and(words(case["a"]), words(case["b"]))
+    else:
+        m = words(case["mask"])
+    assert oracle.mask_popcount(m, case["n_rows"]) == case["expect"]
+
+
+@pytest.mark.parametrize("case", ids("tile_stats_global"), ids=lambda c: c["cite"])
+def test_tile_stats_golden(case):
+    vals = [float(i) for i in range(case["arange"])] if "arange" in case else [dec(v) for v in case["values"]]
+    st = oracle.tile_stats(vals, case["tile_rows"])
+    assert st.size == case["n_tiles"]
+    g = oracle.tile_global_stats(st)
+    e = case["expect"]
+    assert same(g["min"], dec(e["min"])) and same(g["max"], dec(e["max"]))
+    assert g["count"] == e["count"]
+    assert abs(g["mean"] - dec(e["mean"])) < case["tol"]
+
+
+def test_tile_stats_kahan_nonfinite():
+    """The serial Kahan loop of TileColumnStats::from_slice: NaN anywhere -> NaN; an infinity
+    followed by any value -> NaN; a single infinity as the tile's last value -> that infinity."""
+    inf, nan = math.inf, math.nan
+    st = oracle.tile_stats([1.0, 2.0, inf, 3.0, 1.0, 2.0, 3.0, -inf, 7.0, nan, -0.0, 0.0], 4)
+    assert math.isnan(st["sum"][0])                 # inf then 3.0
+    assert st["sum"][1] == -inf                     # -inf last
+    assert math.isnan(st["sum"][2])                 # NaN
+    assert st["min"][2] == 0.0 and math.copysign(1.0, st["min"][2]) == -1.0  # first zero (-0.0) kept
+    assert st["max"][2] == 7.0
+    allnan = oracle.tile_stats([nan, nan], 2)
+    assert allnan["min"][0] == inf and allnan["max"][0] == -inf
+
+
+def test_tile_skip_rules():
+    st = oracle.tile_stats([1.0, 2.0, 3.0, 4.0, 5.0, 6.0], 2)   # tiles [1,2] [3,4] [5,6]
+    assert list(oracle.tile_skip(st, "gt", 4.0)) == [1, 1, 0]    # max <= 4
+    assert list(oracle.tile_skip(st, "ge", 4.0)) == [1, 0, 0]    # max < 4
+    assert list(oracle.tile_skip(st, "lt", 3.0)) == [0, 1, 1]    # min >= 3
+    assert list(oracle.tile_skip(st, "le", 3.0)) == [0, 0, 1]    # min > 3
+    assert list(oracle.tile_skip(st, "gt", math.nan)) == [0, 0, 0]

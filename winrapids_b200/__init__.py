@@ -16,13 +16,14 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._lib import (DTYPES, EXPRS, HIGHER_FIELDS, MOMENT_FIELDS, PREDS, Columns, InvalidArgument, KeyOutOfRange,
-                   Moments, TableFull, TambearGbError, error_for, lib)
+from ._lib import (DTYPES, EXPRS, HIGHER_FIELDS, MOMENT_FIELDS, PREDS, TILE_STATS_BYTES, TILE_STATS_FIELDS, Columns,
+                   EntryNotFound, InvalidArgument, KeyOutOfRange, Moments, TableFull, TambearGbError, error_for, lib)
 
 __all__ = [
     "ComputeEngine", "AccumulateEngine", "HashScatterEngine", "GroupByResult", "Grouping", "Op", "GroupIndex",
     "Context", "DescriptiveEngine", "GroupedMomentStats", "MomentStats", "TambearGbError", "KeyOutOfRange",
-    "InvalidArgument", "TableFull", "MOMENT_FIELDS", "HIGHER_FIELDS", "SUMCOUNT_FIELDS",
+    "InvalidArgument", "TableFull", "EntryNotFound", "MOMENT_FIELDS", "HIGHER_FIELDS", "SUMCOUNT_FIELDS",
+    "FilterJit", "MaskOp", "Frame", "GroupByBuilder", "from_columns",
 ]
 
 SUMCOUNT_FIELDS = ("count", "sum", "mean")
@@ -185,6 +186,96 @@ class Context:
                                                _ptr(nu), _stream_handle(stream)))
         self.sync(stream)
         return codes, uniques[:int(nu.item())]
+
+    # ---- row masks (mask-not-filter) and tile statistics ----
+    # A device row mask is an int64 tensor of ceil(n_rows / 64) words holding the u64 bit
+    # patterns (row i in bit i % 64 of word i // 64).
+
+    def _words_out(self, n_words: int, out):
+        torch = _torch()
+        if out is None:
+            return torch.empty(int(n_words), dtype=torch.int64, device=f"cuda:{self.device}")
+        if int(out.numel()) != int(n_words):
+            raise InvalidArgument(7, "output mask has the wrong number of words")
+        return out
+
+    def filter_mask(self, col, pred: str, threshold: float = 0.0, in_mask=None, out=None, stream=None):
+        """FilterJit::filter_mask on a device column (f64 or f32): bit i = in_mask(i) and
+        pred(col[i]); col is read only where in_mask is set."""
+        torch = _torch()
+        n = int(col.numel())
+        if pred not in PREDS:
+            raise EntryNotFound(6, f"unknown predicate {pred!r}")
+        dt = DTYPES["f32"] if col.dtype == torch.float32 else DTYPES["f64"]
+        if col.dtype not in (torch.float32, torch.float64):
+            raise InvalidArgument(7, "filter column must be f64 or f32")
+        m = self._words_out((n + 63) // 64, out)
+        self._check(self._L.tbgb_filter_mask(self._h, _ptr(col), dt, n, PREDS[pred], float(threshold),
+                                             _ptr(in_mask), _ptr(m), _stream_handle(stream)))
+        return m
+
+    def _mask_binary(self, fn, a, b, out, stream):
+        if int(a.numel()) != int(b.numel()):
+            raise InvalidArgument(7, "mask length mismatch")
+        m = self._words_out(a.numel(), out)
+        self._check(fn(self._h, _ptr(a), _ptr(b), _ptr(m), int(a.numel()), _stream_handle(stream)))
+        return m
+
+    def mask_and(self, a, b, out=None, stream=None):
+        return self._mask_binary(self._L.tbgb_mask_and, a, b, out, stream)
+
+    def mask_or(self, a, b, out=None, stream=None):
+        return self._mask_binary(self._L.tbgb_mask_or, a, b, out, stream)
+
+    def mask_xor(self, a, b, out=None, stream=None):
+        return self._mask_binary(self._L.tbgb_mask_xor, a, b, out, stream)
+
+    def mask_not(self, a, n_rows: int, out=None, stream=None):
+        m = self._words_out(a.numel(), out)
+        self._check(self._L.tbgb_mask_not(self._h, _ptr(a), _ptr(m), int(a.numel()), int(n_rows),
+                                          _stream_handle(stream)))
+        return m
+
+    def mask_popcount(self, m, n_rows: int, stream=None) -> int:
+        """Set bits of rows [0, n_rows) (synchronises the stream)."""
+        torch = _torch()
+        cnt = torch.zeros(1, dtype=torch.int64, device=f"cuda:{self.device}")
+        self._check(self._L.tbgb_mask_popcount(self._h, _ptr(m), int(m.numel()), int(n_rows), _ptr(cnt),
+                                               _stream_handle(stream)))
+        self.sync(stream)
+        return int(cnt.item())
+
+    def tile_stats(self, col, tile_rows: int = 65536, stream=None):
+        """TileColumnStats of every tile of a device column: a uint8 tensor [n_tiles, 40]
+        (field layout TILE_STATS_FIELDS; see tile_stats_numpy)."""
+        torch = _torch()
+        n = int(col.numel())
+        if col.dtype not in (torch.float32, torch.float64):
+            raise InvalidArgument(7, "tile statistics need an f64 or f32 column")
+        n_tiles = (n + int(tile_rows) - 1) // int(tile_rows) if tile_rows >= 1 else 0
+        st = torch.empty((max(n_tiles, 0), TILE_STATS_BYTES), dtype=torch.uint8, device=f"cuda:{self.device}")
+        dt = DTYPES["f32"] if col.dtype == torch.float32 else DTYPES["f64"]
+        self._check(self._L.tbgb_tile_stats_build(self._h, _ptr(col), dt, n, int(tile_rows), _ptr(st),
+                                                  _stream_handle(stream)))
+        return st
+
+    def tile_skip_mask(self, stats, pred: str, threshold: float, stream=None):
+        """1 per tile that no row can pass (pred one of '>', '>=', '<', '<=')."""
+        torch = _torch()
+        if pred not in PREDS:
+            raise EntryNotFound(6, f"unknown predicate {pred!r}")
+        n_tiles = int(stats.shape[0])
+        skip = torch.empty(n_tiles, dtype=torch.uint8, device=f"cuda:{self.device}")
+        self._check(self._L.tbgb_tile_skip_mask(self._h, _ptr(stats), n_tiles, PREDS[pred], float(threshold),
+                                                _ptr(skip), _stream_handle(stream)))
+        return skip
+
+    def mask_skip_tiles(self, skip, tile_rows: int, n_rows: int, mask=None, out=None, stream=None):
+        """Row mask of the rows outside skipped tiles (and inside `mask` when given)."""
+        m = self._words_out((int(n_rows) + 63) // 64, out)
+        self._check(self._L.tbgb_mask_skip_tiles(self._h, _ptr(mask), _ptr(skip), int(tile_rows), int(n_rows),
+                                                 _ptr(m), _stream_handle(stream)))
+        return m
 
     def groupby_hash_into(self, keys, a, max_groups: int, out_keys, out: dict, n_groups, b=None, c=None,
                           expr: str = "a", pred: str | None = None, threshold: float = 0.0, mask=None,
@@ -435,3 +526,4 @@ class DescriptiveEngine:
 
 from .engines import AccumulateEngine, ComputeEngine, GroupByResult, Grouping, HashScatterEngine, Op  # noqa: E402
 from .group_index import GroupIndex  # noqa: E402
+from .frame import FilterJit, Frame, GroupByBuilder, MaskOp, from_columns  # noqa: E402

@@ -42,6 +42,10 @@ class InvalidArgument(TambearGbError):
     pass
 
 
+class EntryNotFound(TambearGbError):
+    pass
+
+
 def error_for(status: int, message: str) -> TambearGbError:
     if status == 8:
         return KeyOutOfRange(status, message)
@@ -49,6 +53,8 @@ def error_for(status: int, message: str) -> TambearGbError:
         return InvalidArgument(status, message)
     if status == 9:
         return TableFull(status, message)
+    if status == 6:
+        return EntryNotFound(status, message)
     return TambearGbError(status, message)
 
 
@@ -116,6 +122,15 @@ def lib() -> C.CDLL:
         "tbgb_scatter_extremum": (st, [vp, i32, vp, vp, i64, i32, vp, vp]),
         "tbgb_group_index_build": (st, [vp, vp, i64, i32, vp, vp, vp, vp, vp, vp]),
         "tbgb_factorize_i64": (st, [vp, vp, i64, i64, vp, vp, vp, vp]),
+        "tbgb_filter_mask": (st, [vp, vp, i32, i64, i32, f64, vp, vp, vp]),
+        "tbgb_mask_and": (st, [vp, vp, vp, vp, i64, vp]),
+        "tbgb_mask_or": (st, [vp, vp, vp, vp, i64, vp]),
+        "tbgb_mask_xor": (st, [vp, vp, vp, vp, i64, vp]),
+        "tbgb_mask_not": (st, [vp, vp, vp, i64, i64, vp]),
+        "tbgb_mask_popcount": (st, [vp, vp, i64, i64, vp, vp]),
+        "tbgb_tile_stats_build": (st, [vp, vp, i32, i64, i64, vp, vp]),
+        "tbgb_tile_skip_mask": (st, [vp, vp, i64, i32, f64, vp, vp]),
+        "tbgb_mask_skip_tiles": (st, [vp, vp, vp, i64, i64, vp, vp]),
         "tbgb_gen_keys_uniform": (st, [vp, vp, i64, i32, u64, i64, vp]),
         "tbgb_gen_values_uniform": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
         "tbgb_gen_values_normal": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
@@ -142,7 +157,14 @@ HEADER_SYMBOLS = (
     "tbgb_gen_keys_cdf", "tbgb_gen_keys_ids", "tbgb_gen_values_lognormal_f32", "tbgb_hash_partition",
     "tbgb_scatter_multi_phi_masked", "tbgb_scatter_phi", "tbgb_scatter_multi_phi", "tbgb_scatter_phi_masked",
     "tbgb_scatter_extremum", "tbgb_group_index_build", "tbgb_factorize_i64",
+    "tbgb_filter_mask", "tbgb_mask_and", "tbgb_mask_or", "tbgb_mask_xor", "tbgb_mask_not", "tbgb_mask_popcount",
+    "tbgb_tile_stats_build", "tbgb_tile_skip_mask", "tbgb_mask_skip_tiles",
 )
+
+# TileColumnStats (format.rs:60-73) as laid out by tbgb_tile_stats: 40 bytes
+TILE_STATS_FIELDS = (("min", "f8"), ("max", "f8"), ("sum", "f8"), ("count", "u4"), ("n_valid", "u4"),
+                     ("reserved", "u8"))
+TILE_STATS_BYTES = 40
 
 # phi expressions by the reference's source spelling (phi_scatter_eval, compute_engine.rs:593-609)
 PHI_IDS = {"v": 0, "v * v": 1, "1.0": 2, "v - r": 3, "(v - r)": 3, "(v - r) * (v - r)": 4, "fabs(v - r)": 5,

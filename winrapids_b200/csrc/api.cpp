@@ -12,6 +12,7 @@
 #include "errbits.hpp"
 #include "gen.cuh"
 #include "group_index.cuh"
+#include "mask.cuh"
 #include "partition.cuh"
 #include "phi.cuh"
 #include "table.cuh"
@@ -70,6 +71,9 @@ tbgb_status ensure_ws(tbgb_ctx* ctx, size_t bytes) {
 }
 
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+// A device pointer the kernels read as `bytes`-wide elements must be aligned to them.
+bool misaligned(const void* p, size_t bytes) { return (reinterpret_cast<uintptr_t>(p) % bytes) != 0; }
 
 struct DenseWs {
   double* part;
@@ -147,6 +151,9 @@ tbgb_status check_columns(tbgb_ctx* ctx, const tbgb_columns* c, int64_t n) {
     if (!c->a) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "column a is NULL");
     if (c->expr != TBGB_EXPR_A && !c->b) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "column b is NULL");
     if (c->expr == TBGB_EXPR_MUL_ADD && !c->c) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "column c is NULL");
+    const size_t eb = c->dtype == TBGB_F32 ? 4 : 8;
+    if (misaligned(c->a, eb) || misaligned(c->b, eb) || misaligned(c->c, eb))
+      return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "column pointer not aligned to its element size");
   }
   return TBGB_OK;
 }
@@ -604,6 +611,157 @@ tbgb_status tbgb_factorize_i64(tbgb_ctx* ctx, const int64_t* d_keys, int64_t n, 
   cudaError_t e = tbgb::factorize_launch(d_keys, n, max_groups, d_codes, d_uniques, d_n_uniques, ctx->ws, ctx->err,
                                          ctx->num_sms, static_cast<cudaStream_t>(stream), &ctx->launches);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "factorize launch", e);
+  return TBGB_OK;
+}
+
+// ---- row masks and tile statistics ----
+
+namespace {
+
+tbgb_status check_words(tbgb_ctx* ctx, const void* p, int64_t n_words, const char* what) {
+  if (n_words > 0 && !p) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, std::string(what) + " is NULL");
+  if (misaligned(p, 8)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, std::string(what) + " is not 8-byte aligned");
+  return TBGB_OK;
+}
+
+tbgb_status mask_binary(tbgb_ctx* ctx, int op, const uint64_t* a, const uint64_t* b, uint64_t* out, int64_t n_words,
+                        void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (n_words < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_words < 0");
+  tbgb_status st = check_words(ctx, a, n_words, "mask a");
+  if (st == TBGB_OK) st = check_words(ctx, b, n_words, "mask b");
+  if (st == TBGB_OK) st = check_words(ctx, out, n_words, "output mask");
+  if (st != TBGB_OK) return st;
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  cudaError_t e = tbgb::mask_op_launch(op, a, b, out, n_words, n_words * 64, ctx->num_sms,
+                                       static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "mask launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status check_rows_words(tbgb_ctx* ctx, int64_t n_words, int64_t n_rows) {
+  if (n_rows < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_rows < 0");
+  if (n_words != (n_rows + 63) / 64) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_words must be ceil(n_rows / 64)");
+  return TBGB_OK;
+}
+
+}  // namespace
+
+tbgb_status tbgb_filter_mask(tbgb_ctx* ctx, const void* d_col, int32_t dtype, int64_t n, int32_t pred,
+                             double threshold, const uint64_t* d_in_mask, uint64_t* d_mask, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (n < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n < 0");
+  if (dtype != TBGB_F64 && dtype != TBGB_F32) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "unknown dtype");
+  if (pred < TBGB_PRED_NONE || pred > TBGB_PRED_FINITE) return fail(ctx, TBGB_ERR_ENTRY_NOT_FOUND, "unknown predicate id");
+  if (n > 0 && !d_col) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "column is NULL");
+  if (misaligned(d_col, dtype == TBGB_F32 ? 4 : 8))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "column pointer not aligned to its element size");
+  tbgb_status st = check_words(ctx, d_mask, (n + 63) / 64, "mask");
+  if (st != TBGB_OK) return st;
+  if (misaligned(d_in_mask, 8)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "input mask not 8-byte aligned");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  cudaError_t e = tbgb::filter_mask_launch(d_col, dtype, n, pred, threshold, d_in_mask, d_mask, ctx->num_sms,
+                                           static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "filter mask launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_mask_and(tbgb_ctx* ctx, const uint64_t* d_a, const uint64_t* d_b, uint64_t* d_out, int64_t n_words,
+                          void* stream) {
+  return mask_binary(ctx, tbgb::MASK_AND, d_a, d_b, d_out, n_words, stream);
+}
+
+tbgb_status tbgb_mask_or(tbgb_ctx* ctx, const uint64_t* d_a, const uint64_t* d_b, uint64_t* d_out, int64_t n_words,
+                         void* stream) {
+  return mask_binary(ctx, tbgb::MASK_OR, d_a, d_b, d_out, n_words, stream);
+}
+
+tbgb_status tbgb_mask_xor(tbgb_ctx* ctx, const uint64_t* d_a, const uint64_t* d_b, uint64_t* d_out, int64_t n_words,
+                          void* stream) {
+  return mask_binary(ctx, tbgb::MASK_XOR, d_a, d_b, d_out, n_words, stream);
+}
+
+tbgb_status tbgb_mask_not(tbgb_ctx* ctx, const uint64_t* d_a, uint64_t* d_out, int64_t n_words, int64_t n_rows,
+                          void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  tbgb_status st = check_rows_words(ctx, n_words, n_rows);
+  if (st == TBGB_OK) st = check_words(ctx, d_a, n_words, "mask");
+  if (st == TBGB_OK) st = check_words(ctx, d_out, n_words, "output mask");
+  if (st != TBGB_OK) return st;
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  cudaError_t e = tbgb::mask_op_launch(tbgb::MASK_NOT, d_a, nullptr, d_out, n_words, n_rows, ctx->num_sms,
+                                       static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "mask launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_mask_popcount(tbgb_ctx* ctx, const uint64_t* d_mask, int64_t n_words, int64_t n_rows,
+                               uint64_t* d_count, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  tbgb_status st = check_rows_words(ctx, n_words, n_rows);
+  if (st == TBGB_OK) st = check_words(ctx, d_mask, n_words, "mask");
+  if (st == TBGB_OK) st = check_words(ctx, d_count, 1, "count");
+  if (st != TBGB_OK) return st;
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  cudaError_t e = tbgb::mask_popcount_launch(d_mask, n_rows, reinterpret_cast<unsigned long long*>(d_count),
+                                             ctx->num_sms, static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "popcount launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_tile_stats_build(tbgb_ctx* ctx, const void* d_col, int32_t dtype, int64_t n, int64_t tile_rows,
+                                  tbgb_tile_stats* d_stats, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (n < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n < 0");
+  if (tile_rows < 1 || tile_rows > static_cast<int64_t>(UINT32_MAX))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "tile_rows must be in [1, 2^32)");
+  if (dtype != TBGB_F64 && dtype != TBGB_F32) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "unknown dtype");
+  if (n > 0 && (!d_col || !d_stats)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "NULL pointer");
+  if (misaligned(d_col, dtype == TBGB_F32 ? 4 : 8) || misaligned(d_stats, 8))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "pointer not aligned");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  cudaError_t e = tbgb::tile_stats_launch(d_col, dtype, n, tile_rows, d_stats, ctx->num_sms,
+                                          static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "tile stats launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_tile_skip_mask(tbgb_ctx* ctx, const tbgb_tile_stats* d_stats, int64_t n_tiles, int32_t pred,
+                                double threshold, uint8_t* d_skip, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (n_tiles < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_tiles < 0");
+  if (pred != TBGB_PRED_GT && pred != TBGB_PRED_GE && pred != TBGB_PRED_LT && pred != TBGB_PRED_LE)
+    return fail(ctx, TBGB_ERR_ENTRY_NOT_FOUND, "tile skipping needs a >, >=, < or <= predicate");
+  if (n_tiles > 0 && (!d_stats || !d_skip)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "NULL pointer");
+  if (misaligned(d_stats, 8)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "stats not 8-byte aligned");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  cudaError_t e = tbgb::tile_skip_launch(d_stats, n_tiles, pred, threshold, d_skip,
+                                         static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "tile skip launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_mask_skip_tiles(tbgb_ctx* ctx, const uint64_t* d_mask, const uint8_t* d_skip, int64_t tile_rows,
+                                 int64_t n_rows, uint64_t* d_out, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (n_rows < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_rows < 0");
+  if (tile_rows < 1) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "tile_rows < 1");
+  const int64_t n_words = (n_rows + 63) / 64;
+  if (n_rows > 0 && !d_skip) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "skip is NULL");
+  if (misaligned(d_mask, 8)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "mask not 8-byte aligned");
+  tbgb_status st = check_words(ctx, d_out, n_words, "output mask");
+  if (st != TBGB_OK) return st;
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  cudaError_t e = tbgb::mask_skip_tiles_launch(d_mask, d_skip, tile_rows, n_rows, d_out, ctx->num_sms,
+                                               static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "mask skip-tiles launch", e);
   return TBGB_OK;
 }
 

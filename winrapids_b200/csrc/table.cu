@@ -302,11 +302,14 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
        base += static_cast<long long>(gridDim.x) * TTILE) {
     long long kk[TR];
     double va[TR], vb[TR], vc[TR];
+    bool in[TR];  // inside the rows and selected by the mask; other rows' columns are not read
 #pragma unroll
     for (int r = 0; r < TR; ++r) {
       const long long row = base + r * TNT + tid;
       kk[r] = 0; va[r] = 0.0; vb[r] = 0.0; vc[r] = 0.0;
-      if (row < n) {
+      in[r] = row < n;
+      if (in[r] && mask) in[r] = (__ldg(mask + (row >> 6)) >> (row & 63)) & 1ull;
+      if (in[r]) {
         kk[r] = load_key<KEY64>(keys, row);
         va[r] = load_val<F32>(col_a, row);
         if (need_b) vb[r] = load_val<F32>(a.cols.b, row);
@@ -318,9 +321,7 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
     double v[TR];
 #pragma unroll
     for (int r = 0; r < TR; ++r) {
-      const long long row = base + r * TNT + tid;
-      bool ok = row < n;
-      if (ok && mask) ok = (__ldg(mask + (row >> 6)) >> (row & 63)) & 1ull;
+      bool ok = in[r];
       if (ok) ok = eval_pred(pred, va[r], thr);
       if (ok && !KEY64 && static_cast<unsigned long long>(kk[r]) >= a.slots) {
         atomicOr(a.err, KERR_KEY_RANGE);
