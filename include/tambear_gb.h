@@ -262,7 +262,8 @@ tbgb_status tbgb_mask_xor(tbgb_ctx* ctx, const uint64_t* d_a, const uint64_t* d_
 tbgb_status tbgb_mask_not(tbgb_ctx* ctx, const uint64_t* d_a, uint64_t* d_out, int64_t n_words, int64_t n_rows,
                           void* stream);
 /* MaskOp::mask_popcount_gpu (filter_jit.rs:418-440), mask_popcount (:130-144): set bits of
- * rows [0, n_rows) into *d_count (device u64); n_words must be ceil(n_rows / 64). */
+ * rows [0, n_rows) into *d_count (device u64); n_words >= ceil(n_rows / 64), later words
+ * and the bits of rows >= n_rows are not counted. */
 tbgb_status tbgb_mask_popcount(tbgb_ctx* ctx, const uint64_t* d_mask, int64_t n_words, int64_t n_rows,
                                uint64_t* d_count, void* stream);
 

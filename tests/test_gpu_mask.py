@@ -177,8 +177,9 @@ def test_mask_errors(ctx):
     a = words_dev(np.zeros(2, np.uint64))
     with pytest.raises(wb.InvalidArgument):
         ctx.mask_not(a, 200)          # needs ceil(200 / 64) = 4 words
+    assert ctx.mask_popcount(a, 10) == 0   # words past ceil(n_rows / 64) are ignored
     with pytest.raises(wb.InvalidArgument):
-        ctx.mask_popcount(a, 10)      # needs 1 word
+        ctx.mask_popcount(a, 129)     # needs 3 words
     with pytest.raises(wb.InvalidArgument):
         ctx.mask_and(a, words_dev(np.zeros(3, np.uint64)))
     with pytest.raises(wb.EntryNotFound):

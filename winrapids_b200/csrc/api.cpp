@@ -701,8 +701,9 @@ tbgb_status tbgb_mask_not(tbgb_ctx* ctx, const uint64_t* d_a, uint64_t* d_out, i
 tbgb_status tbgb_mask_popcount(tbgb_ctx* ctx, const uint64_t* d_mask, int64_t n_words, int64_t n_rows,
                                uint64_t* d_count, void* stream) {
   if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
-  tbgb_status st = check_rows_words(ctx, n_words, n_rows);
-  if (st == TBGB_OK) st = check_words(ctx, d_mask, n_words, "mask");
+  if (n_rows < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_rows < 0");
+  if (n_words < (n_rows + 63) / 64) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_words < ceil(n_rows / 64)");
+  tbgb_status st = check_words(ctx, d_mask, n_words, "mask");
   if (st == TBGB_OK) st = check_words(ctx, d_count, 1, "count");
   if (st != TBGB_OK) return st;
   DeviceGuard dg(ctx->device);
