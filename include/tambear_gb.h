@@ -45,6 +45,8 @@
  *   tbgb_tile_skip_mask             tile_skip_mask_gt / _lt (format.rs:182-189), can_skip_* (:111-136)
  *   tbgb_mask_skip_tiles            no counterpart: applies a tile-skip mask to a row mask so the
  *                                   groupby kernels never read skipped tiles
+ *   tbgb_fused_bin_stats            fused_bin_stats / fused_bin_stats_multi
+ *                                   (src/winrapids/kernels/bin_stats.cu:25-151)
  *   tbgb_hash_partition             no counterpart in the reference (single GPU); routes rows to
  *                                   the GPU that owns their key for the sharded high-cardinality path
  *
@@ -289,6 +291,39 @@ tbgb_status tbgb_tile_skip_mask(tbgb_ctx* ctx, const tbgb_tile_stats* d_stats, i
  * ceil(n_rows / tile_rows) entries).  Passing d_out to a groupby skips those tiles' reads. */
 tbgb_status tbgb_mask_skip_tiles(tbgb_ctx* ctx, const uint64_t* d_mask, const uint8_t* d_skip, int64_t tile_rows,
                                  int64_t n_rows, uint64_t* d_out, void* stream);
+
+/* ---- statistics of sorted contiguous bins ----------------------------------------
+ * fused_bin_stats / fused_bin_stats_multi (src/winrapids/kernels/bin_stats.cu:25-151):
+ * bin b is rows [boundaries[b], boundaries[b + 1]) (n_bins + 1 non-decreasing int64
+ * boundaries within [0, n_ticks]) of each of n_columns f64 columns (column j at
+ * d_data + j * n_ticks).  Outputs are device arrays, NULL to skip: count [n_bins] (int32,
+ * < 2^31 rows per bin), the others [n_columns][n_bins]:
+ *   sum, sum_sq   plain f64 sums of v and v*v (NaN / infinities propagate)
+ *   min, max      strict `<` / `>` scans starting from the bin's first value (a NaN first
+ *                 value is the result; a later NaN never wins; ties keep the first row)
+ *   first, last   data[lo], data[hi - 1]
+ *   mean, variance, std   sum / count, max(sum_sq / count - mean^2, 0) for count > 1 and
+ *                 its square root, as the reference's Python wrapper derives them
+ *                 (archive/fintek-contributions/src/fused_bin_stats.py:121-127)
+ * An empty bin has count 0 and NaN elsewhere.  Counts, extrema, first and last are exact;
+ * sums agree with the serial loop to within rounding (the rows are summed in parallel).
+ * Boundaries that are not non-decreasing within [0, n_ticks] make tbgb_sync report
+ * TBGB_ERR_INVALID_ARGUMENT (their bins' outputs are then unspecified). */
+typedef struct {
+  int32_t* count;
+  double* sum;
+  double* sum_sq;
+  double* min;
+  double* max;
+  double* first;
+  double* last;
+  double* mean;
+  double* variance;
+  double* std;
+} tbgb_bin_stats;
+tbgb_status tbgb_fused_bin_stats(tbgb_ctx* ctx, const double* d_data, int64_t n_ticks, int32_t n_columns,
+                                 const int64_t* d_boundaries, int64_t n_bins, const tbgb_bin_stats* out,
+                                 void* stream);
 
 /* ---- sharded int64-key groupby (one process / GPU per shard) ----------------------
  * Routes the rows of this shard that pass mask and pred to their owner part

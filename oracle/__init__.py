@@ -59,6 +59,7 @@ def lib() -> C.CDLL:
         "orc_mask_popcount": (i64, [vp, i64]),
         "orc_tile_stats_build": (None, [vp, i64, i64, vp]),
         "orc_tile_skip": (None, [vp, i64, C.c_int, f64, vp]),
+        "orc_bin_stats": (None, [vp, vp, i64, vp, vp, vp, vp, vp, vp, vp]),
         "orc_moments_grouped": (C.c_int, [vp, vp, i64, i32, C.POINTER(_Moments)]),
         "orc_moments_grouped_mt": (C.c_int, [vp, vp, vp, i64, i32, C.c_int, C.POINTER(_Moments)]),
         "orc_moments_grouped_masked": (C.c_int, [vp, vp, vp, i64, i32, C.POINTER(_Moments)]),
@@ -227,6 +228,28 @@ def tile_skip(stats, pred, threshold):
     out = np.zeros(max(1, st.size), np.uint8)
     lib().orc_tile_skip(_p(st), st.size, PRED_IDS[pred], float(threshold), _p(out))
     return out[: st.size]
+
+
+def bin_stats(data, boundaries):
+    """fused_bin_stats (bin_stats.cu:25-77) plus the Python wrapper's derived mean / variance /
+    std (archive/fintek-contributions/src/fused_bin_stats.py:121-127), serial per bin."""
+    d = _f64(data)
+    b = np.ascontiguousarray(boundaries, dtype=np.int64)
+    nb = max(b.size - 1, 0)
+    out = {k: np.zeros(max(nb, 1)) for k in ("sum", "sum_sq", "min", "max", "first", "last")}
+    cnt = np.zeros(max(nb, 1), np.int32)
+    if nb:
+        lib().orc_bin_stats(_p(d), _p(b), nb, _p(out["sum"]), _p(out["sum_sq"]), _p(out["min"]), _p(out["max"]),
+                            _p(out["first"]), _p(out["last"]), _p(cnt))
+    res = {k: v[:nb] for k, v in out.items()}
+    res["count"] = cnt[:nb]
+    c = res["count"].astype(np.float64)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        mean = np.where(c > 0, res["sum"] / np.where(c > 0, c, 1.0), np.nan)
+        var = np.where(c > 1, res["sum_sq"] / np.where(c > 0, c, 1.0) - mean * mean, np.nan)
+        var = np.where(var < 0.0, 0.0, var)
+    res["mean"], res["variance"], res["std"] = mean, var, np.sqrt(var)
+    return res
 
 
 def _fmin(a, b):

@@ -385,6 +385,37 @@ void orc_tile_skip(const orc_tile_stats* st, int64_t n_tiles, int pred, double t
   }
 }
 
+/* fused_bin_stats (bin_stats.cu:25-77): per bin, count = hi - lo; an empty bin is NaN
+ * everywhere; otherwise sum and sum_sq accumulate in row order, min and max start from the
+ * bin's first value with strict `<` / `>`, first / last are the end values.  (The reference
+ * kernel is compiled with fused multiply-add contraction on, so its sum_sq rounds once per
+ * row; this restatement rounds the product and the sum separately, a last-bit difference.) */
+void orc_bin_stats(const double* data, const int64_t* boundaries, int64_t n_bins, double* sum, double* sum_sq,
+                   double* mn, double* mx, double* first, double* last, int32_t* count) {
+  for (int64_t b = 0; b < n_bins; ++b) {
+    const int64_t lo = boundaries[b], hi = boundaries[b + 1];
+    count[b] = (int32_t)(hi - lo);
+    if (hi - lo == 0) {
+      sum[b] = sum_sq[b] = mn[b] = mx[b] = first[b] = last[b] = NAN;
+      continue;
+    }
+    double s = 0.0, q = 0.0, lo_v = data[lo], hi_v = data[lo];
+    for (int64_t i = lo; i < hi; ++i) {
+      const double v = data[i];
+      s += v;
+      q += v * v;
+      if (v < lo_v) lo_v = v;
+      if (v > hi_v) hi_v = v;
+    }
+    sum[b] = s;
+    sum_sq[b] = q;
+    mn[b] = lo_v;
+    mx[b] = hi_v;
+    first[b] = data[lo];
+    last[b] = data[hi - 1];
+  }
+}
+
 /* phi_map2_eval (compute_engine.rs:627-636). */
 void orc_map2(int op, const double* a, const double* b, int64_t n, double* out) {
   for (int64_t i = 0; i < n; ++i) {

@@ -16,6 +16,7 @@
  *   - mask algebra         crates/tambear/src/filter_jit.rs:130-181 (mask_and / or / xor / not / popcount)
  *   - tile statistics      crates/tambear/src/format.rs:82-136,182-189 (TileColumnStats::from_slice,
  *                          can_skip_*, tile_skip_mask_gt / _lt)
+ *   - bin statistics       src/winrapids/kernels/bin_stats.cu:25-77 (fused_bin_stats, one bin's loop)
  *   - SplitMix64 / u01 / Box-Muller  crates/tambear/src/rng.rs:34-36,64-85,165-176
  *
  * Parity is pinned by the reference's own golden vectors (see tests/test_oracle_golden.py).
@@ -91,6 +92,10 @@ typedef struct {
 void orc_tile_stats_build(const double* vals, int64_t n, int64_t tile_rows, orc_tile_stats* out);
 /* can_skip_gt / _gte / _lt / _lte with pred ORC_PRED_GT / GE / LT / LE. */
 void orc_tile_skip(const orc_tile_stats* st, int64_t n_tiles, int pred, double threshold, uint8_t* skip);
+
+/* ---- statistics of sorted contiguous bins (bin_stats.cu:25-77), serial per bin ---- */
+void orc_bin_stats(const double* data, const int64_t* boundaries, int64_t n_bins, double* sum, double* sum_sq,
+                   double* mn, double* mx, double* first, double* last, int32_t* count);
 
 /* ---- grouped moments: descriptive.rs:383-435 (counts, sums, mins, maxs, m2s, m3s, m4s) ---- */
 typedef struct {

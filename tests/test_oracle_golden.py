@@ -310,3 +310,15 @@ def test_tile_skip_rules():
     assert list(oracle.tile_skip(st, "lt", 3.0)) == [0, 1, 1]    # min >= 3
     assert list(oracle.tile_skip(st, "le", 3.0)) == [0, 0, 1]    # min > 3
     assert list(oracle.tile_skip(st, "gt", math.nan)) == [0, 0, 0]
+
+
+def test_bin_stats_restatement_hand_case():
+    """fused_bin_stats (bin_stats.cu:25-77) on a hand case: an empty bin is NaN with count 0, a
+    NaN first value is the bin's min and max, and the serial scan keeps the first of +-0."""
+    r = oracle.bin_stats([1.0, 2.0, 3.0, math.nan, 5.0, -0.0, 0.0, 7.0], [0, 3, 3, 5, 8])
+    assert list(r["count"]) == [3, 0, 2, 3]
+    assert r["sum"][0] == 6.0 and r["sum_sq"][0] == 14.0 and r["min"][0] == 1.0 and r["max"][0] == 3.0
+    assert all(math.isnan(r[k][1]) for k in ("sum", "sum_sq", "min", "max", "first", "last", "mean", "variance"))
+    assert math.isnan(r["min"][2]) and math.isnan(r["max"][2]) and r["last"][2] == 5.0
+    assert r["min"][3] == 0.0 and math.copysign(1.0, r["min"][3]) == -1.0 and r["max"][3] == 7.0
+    assert r["first"][3] == 0.0 and math.copysign(1.0, r["first"][3]) == -1.0

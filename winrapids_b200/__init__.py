@@ -16,14 +16,16 @@ from dataclasses import dataclass
 
 import numpy as np
 
-from ._lib import (DTYPES, EXPRS, HIGHER_FIELDS, MOMENT_FIELDS, PREDS, TILE_STATS_BYTES, TILE_STATS_FIELDS, Columns,
+from ._lib import (BIN_STATS_FIELDS, DTYPES, EXPRS, HIGHER_FIELDS, MOMENT_FIELDS, PREDS, TILE_STATS_BYTES,
+                   TILE_STATS_FIELDS, BinStats, Columns,
                    EntryNotFound, InvalidArgument, KeyOutOfRange, Moments, TableFull, TambearGbError, error_for, lib)
 
 __all__ = [
     "ComputeEngine", "AccumulateEngine", "HashScatterEngine", "GroupByResult", "Grouping", "Op", "GroupIndex",
     "Context", "DescriptiveEngine", "GroupedMomentStats", "MomentStats", "TambearGbError", "KeyOutOfRange",
     "InvalidArgument", "TableFull", "EntryNotFound", "MOMENT_FIELDS", "HIGHER_FIELDS", "SUMCOUNT_FIELDS",
-    "FilterJit", "MaskOp", "Frame", "GroupByBuilder", "from_columns",
+    "FilterJit", "MaskOp", "Frame", "GroupByBuilder", "from_columns", "fused_bin_stats",
+    "fused_multi_column_bin_stats",
 ]
 
 SUMCOUNT_FIELDS = ("count", "sum", "mean")
@@ -269,6 +271,35 @@ class Context:
         self._check(self._L.tbgb_tile_skip_mask(self._h, _ptr(stats), n_tiles, PREDS[pred], float(threshold),
                                                 _ptr(skip), _stream_handle(stream)))
         return skip
+
+    def fused_bin_stats(self, data, boundaries, fields=BIN_STATS_FIELDS, stream=None, sync: bool = True) -> dict:
+        """Statistics of sorted contiguous bins (tbgb_fused_bin_stats): data is an f64 device
+        tensor [n_ticks] or [n_columns, n_ticks], boundaries int64 [n_bins + 1].  Returns
+        {field: tensor} with count int32 [n_bins] and the others f64 [n_bins] (one column) or
+        [n_columns, n_bins]."""
+        torch = _torch()
+        if data.dtype != torch.float64:
+            raise InvalidArgument(7, "bin statistics need an f64 column")
+        if boundaries.dtype != torch.int64:
+            raise InvalidArgument(7, "boundaries must be int64")
+        data = data.contiguous()
+        ncol = 1 if data.dim() == 1 else int(data.shape[0])
+        n_ticks = int(data.shape[-1])
+        nb = max(int(boundaries.numel()) - 1, 0)
+        dev = f"cuda:{self.device}"
+        shape = (nb,) if data.dim() == 1 else (ncol, nb)
+        out = {}
+        for f in fields:
+            out[f] = torch.empty(nb if f == "count" else shape, dtype=torch.int32 if f == "count" else torch.float64,
+                                 device=dev)
+        bs = BinStats()
+        for f in BIN_STATS_FIELDS:
+            setattr(bs, f, _ptr(out.get(f)))
+        self._check(self._L.tbgb_fused_bin_stats(self._h, _ptr(data), n_ticks, ncol, _ptr(boundaries), nb,
+                                                 C.byref(bs), _stream_handle(stream)))
+        if sync:
+            self.sync(stream)
+        return out
 
     def mask_skip_tiles(self, skip, tile_rows: int, n_rows: int, mask=None, out=None, stream=None):
         """Row mask of the rows outside skipped tiles (and inside `mask` when given)."""
@@ -527,3 +558,4 @@ class DescriptiveEngine:
 from .engines import AccumulateEngine, ComputeEngine, GroupByResult, Grouping, HashScatterEngine, Op  # noqa: E402
 from .group_index import GroupIndex  # noqa: E402
 from .frame import FilterJit, Frame, GroupByBuilder, MaskOp, from_columns  # noqa: E402
+from .bins import fused_bin_stats, fused_multi_column_bin_stats  # noqa: E402

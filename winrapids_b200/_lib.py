@@ -131,6 +131,7 @@ def lib() -> C.CDLL:
         "tbgb_tile_stats_build": (st, [vp, vp, i32, i64, i64, vp, vp]),
         "tbgb_tile_skip_mask": (st, [vp, vp, i64, i32, f64, vp, vp]),
         "tbgb_mask_skip_tiles": (st, [vp, vp, vp, i64, i64, vp, vp]),
+        "tbgb_fused_bin_stats": (st, [vp, vp, i64, i32, vp, i64, vp, vp]),
         "tbgb_gen_keys_uniform": (st, [vp, vp, i64, i32, u64, i64, vp]),
         "tbgb_gen_values_uniform": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
         "tbgb_gen_values_normal": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
@@ -158,8 +159,15 @@ HEADER_SYMBOLS = (
     "tbgb_scatter_multi_phi_masked", "tbgb_scatter_phi", "tbgb_scatter_multi_phi", "tbgb_scatter_phi_masked",
     "tbgb_scatter_extremum", "tbgb_group_index_build", "tbgb_factorize_i64",
     "tbgb_filter_mask", "tbgb_mask_and", "tbgb_mask_or", "tbgb_mask_xor", "tbgb_mask_not", "tbgb_mask_popcount",
-    "tbgb_tile_stats_build", "tbgb_tile_skip_mask", "tbgb_mask_skip_tiles",
+    "tbgb_tile_stats_build", "tbgb_tile_skip_mask", "tbgb_mask_skip_tiles", "tbgb_fused_bin_stats",
 )
+
+# tbgb_bin_stats field order
+BIN_STATS_FIELDS = ("count", "sum", "sum_sq", "min", "max", "first", "last", "mean", "variance", "std")
+
+
+class BinStats(C.Structure):
+    _fields_ = [(f, C.c_void_p) for f in BIN_STATS_FIELDS]
 
 # TileColumnStats (format.rs:60-73) as laid out by tbgb_tile_stats: 40 bytes
 TILE_STATS_FIELDS = (("min", "f8"), ("max", "f8"), ("sum", "f8"), ("count", "u4"), ("n_valid", "u4"),

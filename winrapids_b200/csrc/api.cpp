@@ -8,6 +8,7 @@
 #include <utility>
 #include <vector>
 
+#include "bin_stats.cuh"
 #include "dense.cuh"
 #include "errbits.hpp"
 #include "gen.cuh"
@@ -614,6 +615,32 @@ tbgb_status tbgb_factorize_i64(tbgb_ctx* ctx, const int64_t* d_keys, int64_t n, 
   return TBGB_OK;
 }
 
+// ---- statistics of sorted contiguous bins ----
+
+tbgb_status tbgb_fused_bin_stats(tbgb_ctx* ctx, const double* d_data, int64_t n_ticks, int32_t n_columns,
+                                 const int64_t* d_boundaries, int64_t n_bins, const tbgb_bin_stats* out,
+                                 void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (!out) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "out is NULL");
+  if (n_ticks < 0 || n_bins < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_ticks and n_bins must be >= 0");
+  if (n_columns < 1 || n_columns > 65535) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_columns must be in [1, 65535]");
+  if (n_ticks > 0 && !d_data) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "data is NULL");
+  if (!d_boundaries) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "boundaries is NULL");
+  const void* ptrs[] = {d_data, d_boundaries, out->sum, out->sum_sq, out->min, out->max, out->first, out->last,
+                        out->mean, out->variance, out->std};
+  for (const void* p : ptrs)
+    if (misaligned(p, 8)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "pointer not 8-byte aligned");
+  if (misaligned(out->count, 4)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "count not 4-byte aligned");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  tbgb_status st = ensure_ws(ctx, tbgb::bin_stats_scratch_bytes(n_ticks, n_columns));
+  if (st != TBGB_OK) return st;
+  cudaError_t e = tbgb::bin_stats_launch(d_data, n_ticks, n_columns, d_boundaries, n_bins, out, ctx->ws, ctx->err,
+                                         ctx->num_sms, static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "bin stats launch", e);
+  return TBGB_OK;
+}
+
 // ---- row masks and tile statistics ----
 
 namespace {
@@ -815,6 +842,9 @@ tbgb_status tbgb_sync(tbgb_ctx* ctx, void* stream) {
   if (bits & tbgb::KERR_KEY_RANGE) return fail(ctx, TBGB_ERR_KEY_OUT_OF_RANGE, "a key is outside [0, n_groups)");
   if (bits & tbgb::KERR_TABLE_FULL) return fail(ctx, TBGB_ERR_TABLE_FULL, "hash table full");
   if (bits & tbgb::KERR_TIMEOUT) return fail(ctx, TBGB_ERR_TIMEOUT, "device-side wait timed out");
+  if (bits & tbgb::KERR_BOUNDARIES)
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "bin boundaries are not non-decreasing within [0, n_ticks]");
+  if (bits & tbgb::KERR_MISALIGNED) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "a staged column is not 16-byte aligned");
   return fail(ctx, TBGB_ERR_BACKEND, "unknown device error bits " + std::to_string(bits));
 }
 

@@ -11,6 +11,7 @@ enum : uint32_t {
   KERR_TIMEOUT = 1u << 1,     // a bounded wait gave up
   KERR_TABLE_FULL = 1u << 2,  // hash table probe limit reached
   KERR_MISALIGNED = 1u << 3,  // staged copy source not 16-byte aligned
+  KERR_BOUNDARIES = 1u << 4,  // bin boundaries not non-decreasing within [0, n_ticks]
 };
 
 }  // namespace tbgb
