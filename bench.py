@@ -12,7 +12,9 @@ Other workloads (--workload): `pipeline` (100,000,000 rows, int64 Zipf(1.1) keys
 rows, int64 keys over 2^28 random ids, f32 LogNormal values, sum/count/mean; rows
 hash-partitioned to their key's owner GPU over NCCL all-to-all), `stress`
 (200,000,000 rows, 10,000 groups, 1e9 + N(0,1e-3) with NaN / +-inf), `cpu-ref`
-(1,000,000 rows, 1,000 groups) and `stress-1k`.
+(1,000,000 rows, 1,000 groups), `stress-1k` and `bins` (1,000,000,000 f64 ticks in sorted
+contiguous bins of 1..831 rows, mean 416: count/sum/sum_sq/min/max/first/last/mean/variance/std
+per bin; its reference arm runs the reference's own CUDA kernel).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload NAME]
 
@@ -60,6 +62,10 @@ WORKLOADS = {
     "pipeline": dict(kind="pipeline", rows=100_000_000, ids=1_000_000, zipf=1.1, seed=0,
                      desc="fused pipeline: 100,000,000 rows; int64 key Zipf(1.1) over 1,000,000 random ids; "
                           "columns a,b,c f64 ~N(0,1); filter a>0, then v=a*b+c; sum/count/mean/var of v per key"),
+    "bins": dict(kind="bins", rows=1_000_000_000, mean_bin=416, seed=0,
+                 desc="segmented bin statistics: 1,000,000,000 f64 ticks ~N(100,1) in sorted contiguous bins of "
+                      "1..831 rows (mean 416, about 2.4 M bins); count/sum/sum_sq/min/max/first/last/mean/"
+                      "variance/std per bin"),
     "highcard": dict(kind="highcard", rows=2_000_000_000, ids=1 << 28, seed=0,
                      desc="high-cardinality sharded: 2,000,000,000 rows; int64 key uniform over 2^28 random ids; "
                           "f32 value ~LogNormal(0,1); sum/count/mean; rows hash-partitioned to the owner GPU of "
@@ -176,12 +182,30 @@ def zipf_table(wl):
     return oracle.zipf_cdf(wl["ids"], wl["zipf"])
 
 
+def bin_boundaries(wl, n_rows):
+    """Boundaries of the `bins` workload: bin sizes 1 + u, u uniform in [0, 2 * mean_bin - 1) from the
+    workload's SplitMix64 stream, cut at n_rows (int64, n_bins + 1 entries)."""
+    import numpy as np
+
+    import oracle
+
+    m = wl["mean_bin"]
+    est = n_rows // m + n_rows // (4 * m) + 16
+    sizes = oracle.gen_keys_uniform(est, 2 * m - 1, wl["seed"] + 7, 0).astype(np.int64) + 1
+    b = np.concatenate([[0], np.cumsum(sizes)])
+    b = b[b < n_rows]
+    return np.append(b, n_rows).astype(np.int64)
+
+
 def host_inputs(wl, start, count):
     """Rows [start, start+count) of the workload generated on the host (same recipes as the device
     generators; integer columns bit-identical)."""
     import oracle
 
     seed = wl["seed"]
+    if wl["kind"] == "bins":
+        return {"a": oracle.gen_values_normal(count, 100.0, 1.0, seed, start),
+                "bounds": bin_boundaries(wl, start + count)}
     if wl["kind"] == "dense":
         keys = oracle.gen_keys_uniform(count, wl["groups"], seed, start)
         kind, a, b = wl["values"]
@@ -209,6 +233,23 @@ def cpu_groupby(wl, cols, threads):
 
     if wl["kind"] == "dense":
         return oracle.moments_grouped_mt(cols["a"], cols["keys"], wl["groups"], threads=threads)
+    if wl["kind"] == "bins":
+        # contiguous bin ranges per thread (the C oracle runs without the GIL)
+        b, d = cols["bounds"], cols["a"]
+        nb = b.size - 1
+        cuts = [nb * t // threads for t in range(threads + 1)]
+        res = [None] * threads
+
+        def bwork(t):
+            lo, hi = cuts[t], cuts[t + 1]
+            res[t] = oracle.bin_stats(d, b[lo:hi + 1])
+
+        ths = [threading.Thread(target=bwork, args=(t,)) for t in range(threads)]
+        for th in ths:
+            th.start()
+        for th in ths:
+            th.join()
+        return res
     keys = cols["keys"]
     if wl["kind"] == "pipeline":
         mask = oracle.filter_mask("gt", 0.0, cols["a"])
@@ -251,7 +292,7 @@ def cpu_sample_rows(wl, target_s, threads, n_rows):
 
 def bytes_per_row(wl) -> int:
     """Algorithmic input bytes per row: every column read once."""
-    return {"dense": 12, "pipeline": 32, "highcard": 12}[wl["kind"]]
+    return {"dense": 12, "pipeline": 32, "highcard": 12, "bins": 8}[wl["kind"]]
 
 
 def base_line(args, wl, n_rows, world):
@@ -261,8 +302,10 @@ def base_line(args, wl, n_rows, world):
            if n_rows * bpr > 1 << 30 else "inputs smaller than L2: L2 flushed between steps"}
     if "groups" in wl:
         cfg["n_groups"] = wl["groups"]
-    else:
+    elif "ids" in wl:
         cfg["distinct_ids"] = wl["ids"]
+    else:
+        cfg["mean_bin_rows"] = wl["mean_bin"]
     if args.table_mode != "auto":
         cfg["table_mode"] = args.table_mode
     return {
@@ -284,8 +327,67 @@ def base_line(args, wl, n_rows, world):
 # the reference arm: the reference's CPU groupby (oracle port) on the host cores
 # ---------------------------------------------------------------------------------
 
+def run_reference_bins(args, wl, n_rows, world):
+    """The reference's own bin-statistics CUDA kernel (src/winrapids/kernels/bin_stats.cu, built
+    from its source into oracle/_ref) on this GPU: the reference has no CPU path for this row."""
+    import ctypes as C
+
+    import numpy as np
+    import torch
+
+    lib_path = ROOT / "oracle" / "_ref" / "libref_bin_stats.so"
+    line = base_line(args, wl, n_rows, world)
+    if not lib_path.exists():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libref_bin_stats.so was not built "
+                                                                "(the reference tree was absent at build time)"}))
+        return
+    L = C.CDLL(str(lib_path))
+    dev = torch.device("cuda:0")
+    import winrapids_b200 as wb
+
+    ctx = wb.Context(0)
+    data = torch.empty(n_rows, dtype=torch.float64, device=dev)
+    ctx.gen_values_normal(data, 100.0, 1.0, wl["seed"], 0)
+    bnd = torch.as_tensor(bin_boundaries(wl, n_rows)).to(dev)
+    nb = int(bnd.numel()) - 1
+    outs = [torch.empty(nb, dtype=torch.float64, device=dev) for _ in range(6)]
+    cnt = torch.empty(nb, dtype=torch.int32, device=dev)
+    stream = torch.cuda.current_stream()
+    args_c = [C.c_void_p(data.data_ptr()), C.c_void_p(bnd.data_ptr())] + [C.c_void_p(o.data_ptr()) for o in outs]
+    args_c += [C.c_void_p(cnt.data_ptr()), C.c_int(nb), C.c_void_p(stream.cuda_stream)]
+
+    def step():
+        assert L.ref_fused_bin_stats(*args_c) == 0
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    ev0.record(stream)
+    for _ in range(args.steps):
+        step()
+    ev1.record(stream)
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    value = n_rows * args.steps / (ms / 1e3)
+    line.update({
+        "impl": "reference",
+        "value": value,
+        "ms_per_step": ms / args.steps,
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": 0, "kind": "reference",
+                         "sample": "the whole workload per step on the GPU: the reference's fused_bin_stats "
+                                   "kernel (one thread per bin), built from its source"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "device": ctx.name,
+    })
+    print(json.dumps(line), flush=True)
+
+
 def run_reference(args, wl, n_rows, world, rank):
     if rank != 0:
+        return
+    if wl["kind"] == "bins":
+        run_reference_bins(args, wl, n_rows, world)
         return
     threads = cpu_threads()
     per_step_s = max(2.0, min(20.0, 150.0 / max(1, args.steps + args.warmup)))
@@ -299,8 +401,9 @@ def run_reference(args, wl, n_rows, world, rank):
     dt = time.perf_counter() - t0
     value = sample * args.steps / dt
     line = base_line(args, wl, n_rows, world)
-    how = ("exact Kulisch groupby, per-thread registers merged in row-range order" if wl["kind"] == "dense" else
-           "sort-based exact groupby of int64 keys, key-disjoint buckets per thread")
+    how = {"dense": "exact Kulisch groupby, per-thread registers merged in row-range order",
+           "bins": "serial per-bin loop of the reference kernel, contiguous bin ranges per thread"}.get(
+        wl["kind"], "sort-based exact groupby of int64 keys, key-disjoint buckets per thread")
     line.update({
         "impl": "reference",
         "value": value,
@@ -445,6 +548,52 @@ class HashJob:
         return total
 
 
+class BinsJob:
+    """Sorted contiguous bins (tbgb_fused_bin_stats).  With N GPUs each takes a contiguous range of
+    bins and the rows they cover (no exchange: bins are independent)."""
+
+    def __init__(self, ctx, wl, lo, hi, world, dist, dev, rank=0):
+        import numpy as np
+        import torch
+
+        import winrapids_b200 as wb
+
+        self.ctx = ctx
+        self.kernel = "bin_chunk_kernel"
+        self.bpr = 8
+        n = wl["rows_total"]
+        b = bin_boundaries(wl, n)
+        nb = b.size - 1
+        b0, b1 = nb * rank // world, nb * (rank + 1) // world
+        r0, r1 = int(b[b0]), int(b[b1])
+        self.n_local = r1 - r0
+        self.nb = b1 - b0
+        data = torch.empty(self.n_local, dtype=torch.float64, device=dev)
+        ctx.gen_values_normal(data, 100.0, 1.0, wl["seed"], r0)
+        bnd = torch.as_tensor(np.ascontiguousarray(b[b0:b1 + 1] - r0)).to(dev)
+        self.inputs = [data, bnd]
+        self.out = {f: torch.empty(self.nb, dtype=torch.int32 if f == "count" else torch.float64, device=dev)
+                    for f in wb._lib.BIN_STATS_FIELDS}
+
+    def step(self, inputs):
+        self.ctx.fused_bin_stats(inputs[0], inputs[1], out=self.out, sync=False)
+
+    def kernel_bytes(self) -> int:
+        # ticks read once, boundaries read, 9 f64 + 1 int32 outputs written per bin
+        return self.n_local * 8 + (self.nb + 1) * 8 + self.nb * 76
+
+    def read_result(self, host: dict) -> int:
+        import torch
+
+        total = 0
+        for f, t in self.out.items():
+            if f not in host:
+                host[f] = torch.empty(t.numel(), dtype=t.dtype, pin_memory=True)
+            host[f].copy_(t, non_blocking=True)
+            total += t.numel() * t.element_size()
+        return total
+
+
 def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
     import torch
 
@@ -455,7 +604,11 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
     ctx = wb.Context(local_rank)
     ctx.set_table_mode(args.table_mode)
     lo, hi = n_rows * rank // world, n_rows * (rank + 1) // world
-    job = (DenseJob if wl["kind"] == "dense" else HashJob)(ctx, wl, lo, hi, world, dist, dev)
+    if wl["kind"] == "bins":
+        wl["rows_total"] = n_rows
+        job = BinsJob(ctx, wl, lo, hi, world, dist, dev, rank)
+    else:
+        job = (DenseJob if wl["kind"] == "dense" else HashJob)(ctx, wl, lo, hi, world, dist, dev)
     n_local = job.n_local
     stream = torch.cuda.current_stream()
     torch.cuda.synchronize()

@@ -272,7 +272,8 @@ class Context:
                                                 _ptr(skip), _stream_handle(stream)))
         return skip
 
-    def fused_bin_stats(self, data, boundaries, fields=BIN_STATS_FIELDS, stream=None, sync: bool = True) -> dict:
+    def fused_bin_stats(self, data, boundaries, fields=BIN_STATS_FIELDS, stream=None, sync: bool = True,
+                        out: dict | None = None) -> dict:
         """Statistics of sorted contiguous bins (tbgb_fused_bin_stats): data is an f64 device
         tensor [n_ticks] or [n_columns, n_ticks], boundaries int64 [n_bins + 1].  Returns
         {field: tensor} with count int32 [n_bins] and the others f64 [n_bins] (one column) or
@@ -288,10 +289,11 @@ class Context:
         nb = max(int(boundaries.numel()) - 1, 0)
         dev = f"cuda:{self.device}"
         shape = (nb,) if data.dim() == 1 else (ncol, nb)
-        out = {}
-        for f in fields:
-            out[f] = torch.empty(nb if f == "count" else shape, dtype=torch.int32 if f == "count" else torch.float64,
-                                 device=dev)
+        if out is None:
+            out = {}
+            for f in fields:
+                out[f] = torch.empty(nb if f == "count" else shape,
+                                     dtype=torch.int32 if f == "count" else torch.float64, device=dev)
         bs = BinStats()
         for f in BIN_STATS_FIELDS:
             setattr(bs, f, _ptr(out.get(f)))

@@ -635,9 +635,15 @@ tbgb_status tbgb_fused_bin_stats(tbgb_ctx* ctx, const double* d_data, int64_t n_
   if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
   tbgb_status st = ensure_ws(ctx, tbgb::bin_stats_scratch_bytes(n_ticks, n_columns));
   if (st != TBGB_OK) return st;
+  cudaEvent_t e0, e1;
+  st = profile_events(ctx, &e0, &e1);
+  if (st != TBGB_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (e0) cudaEventRecord(e0, s);
   cudaError_t e = tbgb::bin_stats_launch(d_data, n_ticks, n_columns, d_boundaries, n_bins, out, ctx->ws, ctx->err,
-                                         ctx->num_sms, static_cast<cudaStream_t>(stream), &ctx->launches);
+                                         ctx->num_sms, s, &ctx->launches);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "bin stats launch", e);
+  if (e1) cudaEventRecord(e1, s);
   return TBGB_OK;
 }
 
