@@ -14,7 +14,9 @@ hash-partitioned to their key's owner GPU over NCCL all-to-all), `stress`
 (200,000,000 rows, 10,000 groups, 1e9 + N(0,1e-3) with NaN / +-inf), `cpu-ref`
 (1,000,000 rows, 1,000 groups), `stress-1k` and `bins` (1,000,000,000 f64 ticks in sorted
 contiguous bins of 1..831 rows, mean 416: count/sum/sum_sq/min/max/first/last/mean/variance/std
-per bin; its reference arm runs the reference's own CUDA kernel).
+per bin; its reference arm runs the reference's own CUDA kernel) and `pushdown` (1,000,000,000
+rows, 256 int32 keys, a time-trending f64 price; `price > 190` over per-tile statistics built
+once like a .tb header: skipped tiles are neither read on the device nor copied from the host).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference] [--workload NAME]
 
@@ -66,6 +68,11 @@ WORKLOADS = {
                  desc="segmented bin statistics: 1,000,000,000 f64 ticks ~N(100,1) in sorted contiguous bins of "
                       "1..831 rows (mean 416, about 2.4 M bins); count/sum/sum_sq/min/max/first/last/mean/"
                       "variance/std per bin"),
+    "pushdown": dict(kind="pushdown", rows=1_000_000_000, groups=256, tile_rows=65536, threshold=190.0, seed=0,
+                     desc="tile-skip pushdown: 1,000,000,000 rows; int32 key uniform in [0,256); f64 price = "
+                          "100 + 100*row/rows + N(0,0.5) (time-ordered); filter price > 190 then "
+                          "count/sum/mean/var of price per key; per-tile min/max statistics (65,536-row tiles) "
+                          "built once outside the timed region, as a .tb file header holds them"),
     "highcard": dict(kind="highcard", rows=2_000_000_000, ids=1 << 28, seed=0,
                      desc="high-cardinality sharded: 2,000,000,000 rows; int64 key uniform over 2^28 random ids; "
                           "f32 value ~LogNormal(0,1); sum/count/mean; rows hash-partitioned to the owner GPU of "
@@ -206,6 +213,13 @@ def host_inputs(wl, start, count):
     if wl["kind"] == "bins":
         return {"a": oracle.gen_values_normal(count, 100.0, 1.0, seed, start),
                 "bounds": bin_boundaries(wl, start + count)}
+    if wl["kind"] == "pushdown":
+        import numpy as np
+
+        total = wl.get("rows_total", wl["rows"])
+        price = oracle.gen_values_normal(count, 0.0, 0.5, seed + 1, start) + (
+            100.0 + 100.0 * (np.arange(start, start + count, dtype=np.float64) / total))
+        return {"keys": oracle.gen_keys_uniform(count, wl["groups"], seed, start), "a": price}
     if wl["kind"] == "dense":
         keys = oracle.gen_keys_uniform(count, wl["groups"], seed, start)
         kind, a, b = wl["values"]
@@ -233,6 +247,9 @@ def cpu_groupby(wl, cols, threads):
 
     if wl["kind"] == "dense":
         return oracle.moments_grouped_mt(cols["a"], cols["keys"], wl["groups"], threads=threads)
+    if wl["kind"] == "pushdown":
+        mask = oracle.filter_mask("gt", wl["threshold"], cols["a"])
+        return oracle.moments_grouped_mt(cols["a"], cols["keys"], wl["groups"], threads=threads, mask=mask)
     if wl["kind"] == "bins":
         # contiguous bin ranges per thread (the C oracle runs without the GIL)
         b, d = cols["bounds"], cols["a"]
@@ -292,7 +309,7 @@ def cpu_sample_rows(wl, target_s, threads, n_rows):
 
 def bytes_per_row(wl) -> int:
     """Algorithmic input bytes per row: every column read once."""
-    return {"dense": 12, "pipeline": 32, "highcard": 12, "bins": 8}[wl["kind"]]
+    return {"dense": 12, "pipeline": 32, "highcard": 12, "bins": 8, "pushdown": 12}[wl["kind"]]
 
 
 def base_line(args, wl, n_rows, world):
@@ -402,6 +419,7 @@ def run_reference(args, wl, n_rows, world, rank):
     value = sample * args.steps / dt
     line = base_line(args, wl, n_rows, world)
     how = {"dense": "exact Kulisch groupby, per-thread registers merged in row-range order",
+           "pushdown": "filter mask, then exact Kulisch groupby of the passing rows (no tile skipping)",
            "bins": "serial per-bin loop of the reference kernel, contiguous bin ranges per thread"}.get(
         wl["kind"], "sort-based exact groupby of int64 keys, key-disjoint buckets per thread")
     line.update({
@@ -548,6 +566,94 @@ class HashJob:
         return total
 
 
+class PushdownJob:
+    """Filter + groupby with tile skipping: the skip mask from per-tile statistics, the row mask of
+    the surviving tiles, then the fused filter + groupby, which reads no column of a masked-out row."""
+
+    def __init__(self, ctx, wl, lo, hi, world, dist, dev):
+        import torch
+
+        self.ctx, self.wl = ctx, wl
+        self.kernel = "table_kernel"
+        self.bpr = 12
+        self.G = wl["groups"]
+        self.tile_rows = wl["tile_rows"]
+        self.thr = wl["threshold"]
+        n = self.n_local = hi - lo
+        total = wl["rows_total"]
+        keys = torch.empty(n, dtype=torch.int32, device=dev)
+        ctx.gen_keys_uniform(keys, self.G, wl["seed"], lo)
+        price = torch.empty(n, dtype=torch.float64, device=dev)
+        ctx.gen_values_normal(price, 0.0, 0.5, wl["seed"] + 1, lo)
+        price += 100.0 + 100.0 * (torch.arange(lo, hi, dtype=torch.float64, device=dev) / total)
+        self.inputs = [keys, price]
+        self.stats = ctx.tile_stats(price, self.tile_rows)  # the header: built once, outside the timed region
+        self.n_tiles = int(self.stats.shape[0])
+        self.mask = torch.empty((n + 63) // 64, dtype=torch.int64, device=dev)
+        self.out = ctx.alloc_moments(self.G, ("count", "sum", "mean", "m2", "var_pop", "var_samp"))
+        skip = ctx.tile_skip_mask(self.stats, ">", self.thr).cpu().numpy()
+        self.live_tiles = int((skip == 0).sum())
+        self.live_rows = sum(min(self.tile_rows, n - t * self.tile_rows) for t in range(self.n_tiles) if not skip[t])
+
+    def step(self, inputs):
+        keys, price = inputs
+        skip = self.ctx.tile_skip_mask(self.stats, ">", self.thr)
+        self.ctx.mask_skip_tiles(skip, self.tile_rows, self.n_local, out=self.mask)
+        self.ctx.groupby_dense_columns(keys, price, self.G, pred=">", threshold=self.thr, mask=self.mask,
+                                       out=self.out, sync=False)
+
+    def kernel_bytes(self) -> int:
+        # the table kernel reads the row mask and the key and price of the rows of surviving tiles
+        return self.n_local // 8 + self.live_rows * 12
+
+    def e2e_copy(self, dev_in, host_in) -> int:
+        """Host -> device only for the runs of tiles the skip mask keeps (the skip flags come back
+        from the device first, n_tiles bytes)."""
+        skip = self.ctx.tile_skip_mask(self.stats, ">", self.thr).cpu().numpy()
+        total, t, tr, n = 0, 0, self.tile_rows, self.n_local
+        while t < self.n_tiles:
+            if skip[t]:
+                t += 1
+                continue
+            u = t
+            while u < self.n_tiles and not skip[u]:
+                u += 1
+            r0, r1 = t * tr, min(u * tr, n)
+            for d, h in zip(dev_in, host_in):
+                d[r0:r1].copy_(h[r0:r1], non_blocking=True)
+                total += (r1 - r0) * h.element_size()
+            t = u
+        return total + self.n_tiles
+
+    def extra(self, args) -> dict:
+        """The same query without tile skipping (every row's price read and compared)."""
+        import torch
+
+        keys, price = self.inputs
+        for _ in range(2):
+            self.ctx.groupby_dense_columns(keys, price, self.G, pred=">", threshold=self.thr, out=self.out, sync=False)
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        k = max(3, min(args.steps, 10))
+        e0.record()
+        for _ in range(k):
+            self.ctx.groupby_dense_columns(keys, price, self.G, pred=">", threshold=self.thr, out=self.out, sync=False)
+        e1.record()
+        torch.cuda.synchronize()
+        self.ctx.sync()
+        return {"pushdown": {"tiles": self.n_tiles, "tiles_read": self.live_tiles, "rows_read": self.live_rows,
+                             "ms_per_step_without_skipping": e0.elapsed_time(e1) / k}}
+
+    def read_result(self, host: dict) -> int:
+        import torch
+
+        for f, t in self.out.items():
+            if f not in host:
+                host[f] = torch.empty(t.numel(), dtype=t.dtype, pin_memory=True)
+            host[f].copy_(t, non_blocking=True)
+        return sum(t.numel() * 8 for t in self.out.values())
+
+
 class BinsJob:
     """Sorted contiguous bins (tbgb_fused_bin_stats).  With N GPUs each takes a contiguous range of
     bins and the rows they cover (no exchange: bins are independent)."""
@@ -607,6 +713,9 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
     if wl["kind"] == "bins":
         wl["rows_total"] = n_rows
         job = BinsJob(ctx, wl, lo, hi, world, dist, dev, rank)
+    elif wl["kind"] == "pushdown":
+        wl["rows_total"] = n_rows
+        job = PushdownJob(ctx, wl, lo, hi, world, dist, dev)
     else:
         job = (DenseJob if wl["kind"] == "dense" else HashJob)(ctx, wl, lo, hi, world, dist, dev)
     n_local = job.n_local
@@ -657,20 +766,25 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
 
     # ---- end to end through the public API, host buffers in pinned memory
     e2e_steps = args.e2e_steps if args.e2e_steps is not None else max(3, min(args.steps, 10))
+    extra = job.extra(args) if hasattr(job, "extra") else {}
     host_in = []
     for t in job.inputs:
         h = torch.empty(t.numel(), dtype=t.dtype, pin_memory=True)
         h.copy_(t)
         host_in.append(h)
-    h2d = sum(h.numel() * h.element_size() for h in host_in)
+    h2d_all = sum(h.numel() * h.element_size() for h in host_in)
     dev_in = [torch.empty_like(t) for t in job.inputs]
     job.inputs = None
     host_out = {}
     d2h = [0]
+    h2d_step = [h2d_all]
 
     def e2e_step():
-        for d, h in zip(dev_in, host_in):
-            d.copy_(h, non_blocking=True)
+        if hasattr(job, "e2e_copy"):
+            h2d_step[0] = job.e2e_copy(dev_in, host_in)
+        else:
+            for d, h in zip(dev_in, host_in):
+                d.copy_(h, non_blocking=True)
         job.step(dev_in)
         d2h[0] = job.read_result(host_out)
 
@@ -690,7 +804,7 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
 
     # ---- max over ranks
     kern_gbs = kbytes / args.steps / (kms / max(klaunches, 1) / 1e3) / 1e9 if kms > 0 else 0.0
-    t = torch.tensor([ms, e2e_ms, -kern_gbs, float(launches), float(h2d), float(d2h[0])], dtype=torch.float64,
+    t = torch.tensor([ms, e2e_ms, -kern_gbs, float(launches), float(h2d_step[0]), float(d2h[0])], dtype=torch.float64,
                      device=dev)
     if dist is not None:
         mx = t[:3].clone()
@@ -733,6 +847,7 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
         "clocks": clk,
         "device": ctx.name,
     })
+    line.update(extra)
     if world == 1 and not args.no_cpu_baseline:
         threads = cpu_threads()
         sample = cpu_sample_rows(wl, args.cpu_seconds, threads, n_rows)

@@ -362,3 +362,39 @@ def test_frame_filter_is_mask_not_filter(ctx):
     assert hot.active_rows() == int(sel.sum())  # the parent frame's mask is unchanged
     gi = df.group_index_for("k", G - 1)
     assert gi is df.group_index_for("k", G - 1)
+
+
+@pytest.mark.parametrize("G", [1, 256, 1000])
+def test_dense_predicate_route_with_zero_tiles(ctx, G):
+    """A predicate on a plain f64 column with <= 1024 groups runs as a row mask plus the masked
+    column kernel, which skips tiles whose mask words are all zero; results as the oracle's, and
+    counts / extrema bit-identical to the table path's."""
+    rng = np.random.default_rng(G)
+    n = 3_000_017
+    a = column(rng, n) * 10.0
+    keys = rng.integers(0, G, n).astype(np.int32)
+    # rows outside [0.3n, 0.35n) and [0.8n, 0.81n) masked out: most 2048-row tiles are all zero
+    inm_rows = np.zeros(n, bool)
+    inm_rows[int(0.3 * n):int(0.35 * n)] = True
+    inm_rows[int(0.8 * n):int(0.81 * n)] = True
+    inm = np.packbits(inm_rows, bitorder="little")
+    inm = np.concatenate([inm, np.zeros((-inm.size) % 8, np.uint8)]).view(np.uint64)
+    fields = ("count", "sum", "min", "max", "mean", "m2", "var_pop", "var_samp", "m3", "m4")
+    for mask in (None, inm):
+        M = None if mask is None else words_dev(mask)
+        out = ctx.groupby_dense_columns(dev(keys), dev(a), G, pred=">=", threshold=-2.5, mask=M,
+                                        out=ctx.alloc_moments(G, fields))
+        fm = oracle.filter_mask("ge", -2.5, a)
+        if mask is not None:
+            fm = oracle.mask_and(fm, mask)
+        want = oracle.moments_grouped_masked(a, keys, fm, G, m34=True)
+        rows = rows_of(fm, n)
+        got = to_host(out)
+        check(got, want, abs_sums(keys, a, G, rows), f"G={G} masked={mask is not None}")
+        ctx.set_table_mode("direct")
+        try:
+            t = to_host(ctx.groupby_dense_columns(dev(keys), dev(a), G, pred=">=", threshold=-2.5, mask=M))
+        finally:
+            ctx.set_table_mode("auto")
+        for f in ("count", "min", "max"):
+            assert np.array_equal(got[f].view(np.uint64), t[f].view(np.uint64)), f

@@ -26,6 +26,8 @@ struct tbgb_ctx {
   std::string last_error;
   void* ws = nullptr;  // workspace: partial states, zero trackers
   size_t ws_bytes = 0;
+  void* ws_mask = nullptr;  // row mask of a predicate evaluated ahead of the column kernel
+  size_t ws_mask_bytes = 0;
   uint32_t* err = nullptr;  // deferred kernel error bits (persist until tbgb_sync)
   uint64_t launches = 0;
   int table_mode = 0;    // tbgb_set_table_mode
@@ -71,6 +73,20 @@ tbgb_status ensure_ws(tbgb_ctx* ctx, size_t bytes) {
   return TBGB_OK;
 }
 
+tbgb_status ensure_ws_mask(tbgb_ctx* ctx, size_t bytes) {
+  if (bytes <= ctx->ws_mask_bytes) return TBGB_OK;
+  if (ctx->ws_mask) {
+    cudaFree(ctx->ws_mask);
+    ctx->ws_mask = nullptr;
+    ctx->ws_mask_bytes = 0;
+  }
+  const size_t want = (bytes + bytes / 4 + 255) / 256 * 256;
+  cudaError_t e = cudaMalloc(&ctx->ws_mask, want);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_ALLOC, "mask workspace allocation", e);
+  ctx->ws_mask_bytes = want;
+  return TBGB_OK;
+}
+
 size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 
 // A device pointer the kernels read as `bytes`-wide elements must be aligned to them.
@@ -80,18 +96,22 @@ struct DenseWs {
   double* part;
   unsigned long long* spill;
   unsigned long long* zfirst;
+  unsigned* live;  // live-tile list of a masked launch
   size_t bytes;
 };
 
-DenseWs dense_ws_layout(void* base, const tbgb::DenseLaunch& L, int G) {
+DenseWs dense_ws_layout(void* base, const tbgb::DenseLaunch& L, int G, int64_t n_masked = 0) {
   DenseWs w{};
   const size_t part_bytes = align_up(L.part_doubles * 8, 256);
   const size_t spill_bytes = align_up(L.spill_words * 8, 256);
+  const size_t zf_bytes = align_up(static_cast<size_t>(G) * 8, 256);
   char* p = static_cast<char*>(base);
   w.part = reinterpret_cast<double*>(p);
   w.spill = reinterpret_cast<unsigned long long*>(p + part_bytes);
   w.zfirst = reinterpret_cast<unsigned long long*>(p + part_bytes + spill_bytes);
-  w.bytes = part_bytes + spill_bytes + align_up(static_cast<size_t>(G) * 8, 256);
+  w.live = n_masked > 0 ? reinterpret_cast<unsigned*>(p + part_bytes + spill_bytes + zf_bytes) : nullptr;
+  w.bytes = part_bytes + spill_bytes + zf_bytes +
+            (n_masked > 0 ? align_up(tbgb::dense_live_scratch_bytes(n_masked), 256) : 0);
   return w;
 }
 
@@ -121,10 +141,11 @@ tbgb_status dense_common(tbgb_ctx* ctx, const int32_t* keys, const double* vals,
   DeviceGuard dg(ctx->device);
   if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
   const tbgb::DenseLaunch L = tbgb::dense_plan(G, ctx->num_sms);
-  DenseWs w = dense_ws_layout(nullptr, L, G);
+  const int64_t n_masked = mask ? n : 0;
+  DenseWs w = dense_ws_layout(nullptr, L, G, n_masked);
   st = ensure_ws(ctx, w.bytes);
   if (st != TBGB_OK) return st;
-  w = dense_ws_layout(ctx->ws, L, G);
+  w = dense_ws_layout(ctx->ws, L, G, n_masked);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   cudaError_t e = cudaMemsetAsync(w.zfirst, 0xFF, static_cast<size_t>(G) * 8, s);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "memset", e);
@@ -132,7 +153,7 @@ tbgb_status dense_common(tbgb_ctx* ctx, const int32_t* keys, const double* vals,
   st = profile_events(ctx, &e0, &e1);
   if (st != TBGB_OK) return st;
   e = tbgb::dense_moments_launch(L, keys, vals, mask, n, row_offset, G, w.part, w.spill, w.zfirst, ctx->err, out,
-                                 state_out, s, &ctx->launches, e0, e1);
+                                 state_out, s, &ctx->launches, e0, e1, w.live);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "dense groupby launch", e);
   return TBGB_OK;
 }
@@ -396,6 +417,7 @@ void tbgb_destroy(tbgb_ctx* ctx) {
       cudaEventDestroy(pr.second);
     }
     if (ctx->ws) cudaFree(ctx->ws);
+    if (ctx->ws_mask) cudaFree(ctx->ws_mask);
     if (ctx->err) cudaFree(ctx->err);
   }
   delete ctx;
@@ -474,6 +496,22 @@ tbgb_status tbgb_groupby_dense_columns(tbgb_ctx* ctx, const int32_t* d_keys, con
   if (plain && n_groups >= 1 && n_groups <= tbgb::kDenseMaxGroups)
     return dense_common(ctx, d_keys, static_cast<const double*>(cols->a), d_mask, n, n_groups, 0, out, nullptr,
                         stream);
+  // A predicate on a plain f64 column with few groups: the predicate as a row mask (reading
+  // column a only where d_mask selects), then the masked column kernel, which skips tiles
+  // whose mask words are all zero.
+  const bool filtered = cols->dtype == TBGB_F64 && cols->expr == TBGB_EXPR_A && cols->pred != TBGB_PRED_NONE;
+  if (filtered && ctx->table_mode == 0 && n_groups >= 1 && n_groups <= tbgb::kDenseMaxGroups && n > 0) {
+    if (misaligned(d_mask, 8)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "mask not 8-byte aligned");
+    DeviceGuard dg(ctx->device);
+    if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+    st = ensure_ws_mask(ctx, static_cast<size_t>((n + 63) / 64) * 8);
+    if (st != TBGB_OK) return st;
+    uint64_t* m = static_cast<uint64_t*>(ctx->ws_mask);
+    cudaError_t e = tbgb::filter_mask_launch(cols->a, TBGB_F64, n, cols->pred, cols->threshold, d_mask, m,
+                                             ctx->num_sms, static_cast<cudaStream_t>(stream), &ctx->launches);
+    if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "filter mask launch", e);
+    return dense_common(ctx, d_keys, static_cast<const double*>(cols->a), m, n, n_groups, 0, out, nullptr, stream);
+  }
   if (n_groups >= 1 && use_buckets(ctx, n_groups))
     return bucketed_dense(ctx, d_keys, cols, d_mask, n, n_groups, out, stream);
   return table_common(ctx, false, d_keys, cols, d_mask, n, n_groups, 0, nullptr, out, nullptr, nullptr, stream);

@@ -114,6 +114,37 @@ struct DenseArgs {
   unsigned long long* spill;   // [gridDim.x][SP_COUNT][G]
   unsigned long long* zfirst;  // [G], preset to ~0
   uint32_t* err;
+  // masked launches: tiles with a selected row (bit j of live_bits[w] = tile 32w + j) and the
+  // exclusive prefix of their counts (live_pre[live_words] = all of them); NULL: every tile
+  const unsigned* live_bits;
+  const unsigned* live_pre;
+  long long live_words;
+};
+
+// Walks the live tiles from a given rank (0-based among all live tiles) in increasing order.
+struct LiveCursor {
+  const unsigned* bits;
+  long long w, nw;
+  unsigned cur;
+  __device__ __forceinline__ void init(const unsigned* b, const unsigned* pre, long long nw_, long long rank) {
+    bits = b;
+    nw = nw_;
+    long long lo = 0, hi = nw_;  // the last word with pre[w] <= rank
+    while (hi - lo > 1) {
+      const long long mid = (lo + hi) >> 1;
+      if (static_cast<long long>(pre[mid]) <= rank) lo = mid;
+      else hi = mid;
+    }
+    w = lo;
+    cur = nw_ > 0 ? b[lo] : 0u;
+    for (long long s = rank - static_cast<long long>(pre[lo]); s > 0 && cur; --s) cur &= cur - 1u;
+  }
+  __device__ __forceinline__ long long next() {
+    while (cur == 0u && w + 1 < nw) cur = bits[++w];
+    const int j = __ffs(cur) - 1;
+    cur &= cur - 1u;
+    return w * 32 + j;
+  }
 };
 
 size_t dense_smem_bytes(int G, int C) {
@@ -361,7 +392,15 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
 
   const long long ntiles = a.n / TILE;
   const int P = gridDim.x, b = blockIdx.x;
-  const long long t_begin = ntiles * b / P, t_end = ntiles * (b + 1) / P;
+  long long t_begin = ntiles * b / P, t_end = ntiles * (b + 1) / P;
+  if constexpr (MASKED) {
+    // ranks among the live tiles: every CTA takes an equal share of the tiles that have a row
+    if (a.live_bits) {
+      const long long nl = a.live_pre[a.live_words];
+      t_begin = nl * b / P;
+      t_end = nl * (b + 1) / P;
+    }
+  }
   const long long mytiles = t_end - t_begin;
   const bool has_tail = (b == P - 1) && (a.n % TILE) != 0;
   const long long nbatch = mytiles + (has_tail ? 1 : 0);
@@ -411,7 +450,67 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     // ------------------------------------------------------------ producer warp
     // Refills each stage as soon as all scatter warps released it, and keeps
     // PF_AHEAD further tiles streaming into L2.
-    if (TMA && lane == 0) {
+    if constexpr (MASKED) {
+      // With a live-tile list the producer issues (and prefetches) only tiles that have a
+      // selected row: tiles whose mask words are all zero are never read.
+      if (TMA && lane == 0 && a.live_bits) {
+        LiveCursor ic, pc;
+        ic.init(a.live_bits, a.live_pre, a.live_words, t_begin);
+        pc.init(a.live_bits, a.live_pre, a.live_words, t_begin + (mytiles > STAGES ? STAGES : mytiles));
+        long long issued = 0;
+        for (int st = 0; st < STAGES && st < mytiles; ++st) issue(st, ic.next());
+        issued = mytiles < STAGES ? mytiles : STAGES;
+        for (long long j = STAGES; j < STAGES + PF_AHEAD && j < mytiles; ++j) prefetch(pc.next());
+        bool failed = false;
+        for (long long k = 0; k + STAGES < mytiles; ++k) {
+          const int st = static_cast<int>(k % STAGES);
+          if (!wait_or_abort(&empty[st], static_cast<uint32_t>((k / STAGES) & 1), a.err, abort)) {
+            failed = true;
+            *abort = 1;
+            break;
+          }
+          fence_proxy_async_smem();
+          issue(st, ic.next());
+          ++issued;
+          if (k + STAGES + PF_AHEAD < mytiles) prefetch(pc.next());
+        }
+        if (failed || *abort) {
+          // leave no bulk copy in flight into this CTA's shared memory (bounded waits)
+          for (long long j = issued - STAGES < 0 ? 0 : issued - STAGES; j < issued; ++j) {
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(&full[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1))) {
+              if (globaltimer_ns() - t0 > 500000000ull) break;
+            }
+          }
+        }
+      } else if (TMA && lane == 0) {
+        long long issued = 0;
+        for (int s = 0; s < STAGES && s < mytiles; ++s) issue(s, t_begin + s);
+        issued = mytiles < STAGES ? mytiles : STAGES;
+        for (long long j = STAGES; j < STAGES + PF_AHEAD && j < mytiles; ++j) prefetch(t_begin + j);
+        bool failed = false;
+        for (long long k = 0; k + STAGES < mytiles; ++k) {
+          const int st = static_cast<int>(k % STAGES);
+          if (!wait_or_abort(&empty[st], static_cast<uint32_t>((k / STAGES) & 1), a.err, abort)) {
+            failed = true;
+            *abort = 1;
+            break;
+          }
+          fence_proxy_async_smem();
+          issue(st, t_begin + k + STAGES);
+          ++issued;
+          if (k + STAGES + PF_AHEAD < mytiles) prefetch(t_begin + k + STAGES + PF_AHEAD);
+        }
+        if (failed || *abort) {
+          for (long long j = issued - STAGES < 0 ? 0 : issued - STAGES; j < issued; ++j) {
+            const uint64_t t0 = globaltimer_ns();
+            while (!mbar_try_wait(&full[j % STAGES], static_cast<uint32_t>((j / STAGES) & 1))) {
+              if (globaltimer_ns() - t0 > 500000000ull) break;
+            }
+          }
+        }
+      }
+    } else if (TMA && lane == 0) {
       long long issued = 0;
       for (int s = 0; s < STAGES && s < mytiles; ++s) issue(s, t_begin + s);
       issued = mytiles < STAGES ? mytiles : STAGES;
@@ -445,6 +544,10 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     // completion with one mbarrier arrival per warp.  A thread's 8 rows of a tile
     // are handled as two halves of 4 (register budget of a 25-warp CTA).
     const int t = tid;
+    LiveCursor sc;
+    if constexpr (MASKED) {
+      if (a.live_bits) sc.init(a.live_bits, a.live_pre, a.live_words, t_begin);
+    }
     for (long long k = 0; k < nbatch; ++k) {
       const int bs = static_cast<int>(k & 1);
       double* col = bs ? col1 : col0;
@@ -454,7 +557,10 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
       bool ok = true;
       if (k >= 2) ok = wait_or_abort(&colempty[bs], static_cast<uint32_t>(((k >> 1) - 1) & 1), a.err, abort);
       const bool tail = k >= mytiles;
-      const long long row0 = tail ? ntiles * TILE : (t_begin + k) * TILE;
+      long long row0 = tail ? ntiles * TILE : (t_begin + k) * TILE;
+      if constexpr (MASKED) {
+        if (a.live_bits && !tail) row0 = sc.next() * TILE;
+      }
       const int s = static_cast<int>(k % STAGES);
       const bool staged = TMA && !tail;
       if (staged) ok = ok && wait_or_abort(&full[s], static_cast<uint32_t>((k / STAGES) & 1), a.err, abort);
@@ -788,19 +894,108 @@ static cudaError_t launch_m(const DenseLaunch& L, const DenseArgs& a, bool maske
   return launch_slots<4, M34>(L, a, masked, aligned, stream);
 }
 
+constexpr int LT_NT = 256;
+constexpr int LS_NT = 1024;
+
+// Bit j of bits[w]: full tile 32w + j has a selected row; cnt[w] = popcount(bits[w]).
+__global__ void __launch_bounds__(LT_NT) live_tiles_kernel(const uint64_t* __restrict__ mask, long long ntiles,
+                                                           unsigned* bits, unsigned* cnt, long long nw) {
+  const int lane = threadIdx.x & 31;
+  const long long warp = (static_cast<long long>(blockIdx.x) * LT_NT + threadIdx.x) >> 5;
+  const long long nwarps = static_cast<long long>(gridDim.x) * (LT_NT / 32);
+  for (long long w = warp; w < nw; w += nwarps) {
+    const long long t = w * 32 + lane;
+    bool any = false;
+    if (t < ntiles) {
+      const uint64_t* mw = mask + t * (TILE / 64);
+      uint64_t acc = 0;
+#pragma unroll 8
+      for (int i = 0; i < TILE / 64; ++i) acc |= __ldg(mw + i);
+      any = acc != 0;
+    }
+    const unsigned bal = __ballot_sync(0xffffffffu, any);
+    if (lane == 0) {
+      bits[w] = bal;
+      cnt[w] = static_cast<unsigned>(__popc(bal));
+    }
+  }
+}
+
+// pre[w] = cnt[0] + ... + cnt[w - 1] for w <= nw (one block).
+__global__ void __launch_bounds__(LS_NT) live_scan_kernel(const unsigned* __restrict__ cnt, long long nw,
+                                                          unsigned* pre) {
+  __shared__ unsigned warp_sums[LS_NT / 32];
+  __shared__ unsigned carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (long long base = 0; base < nw; base += LS_NT) {
+    const long long i = base + threadIdx.x;
+    const unsigned x = i < nw ? cnt[i] : 0u;
+    unsigned inc = x;
+    for (int d = 1; d < 32; d <<= 1) {
+      const unsigned y = __shfl_up_sync(0xffffffffu, inc, d);
+      if (lane >= d) inc += y;
+    }
+    if (lane == 31) warp_sums[warp] = inc;
+    __syncthreads();
+    if (warp == 0) {
+      unsigned ws = warp_sums[lane];
+      for (int d = 1; d < 32; d <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, ws, d);
+        if (lane >= d) ws += y;
+      }
+      warp_sums[lane] = ws;
+    }
+    __syncthreads();
+    const unsigned before = carry + (warp > 0 ? warp_sums[warp - 1] : 0u) + inc - x;
+    if (i < nw) pre[i] = before;
+    __syncthreads();
+    if (threadIdx.x == LS_NT - 1) carry = before + x;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) pre[nw] = carry;
+}
+
+size_t dense_live_scratch_bytes(long long n) {
+  const long long nw = (n / TILE + 31) / 32;
+  return static_cast<size_t>(3 * nw + 1) * sizeof(unsigned);
+}
+
 cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, const double* vals, const uint64_t* mask,
                                  long long n, long long row_offset, int G, double* part, unsigned long long* spill,
                                  unsigned long long* zfirst, uint32_t* err, const tbgb_moments* out, double* state_out,
-                                 cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start, cudaEvent_t ev_stop) {
+                                 cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start, cudaEvent_t ev_stop,
+                                 unsigned* live_scratch) {
   DenseArgs a;
   a.keys = keys; a.vals = vals; a.mask = mask; a.n = n; a.row_offset = row_offset;
   a.G = G; a.C = L.C; a.opg = L.opg; a.slots = L.slots;
   a.part = part; a.spill = spill; a.zfirst = zfirst; a.err = err;
+  a.live_bits = nullptr; a.live_pre = nullptr; a.live_words = 0;
   const bool aligned = (reinterpret_cast<uintptr_t>(keys) % 16 == 0) && (reinterpret_cast<uintptr_t>(vals) % 16 == 0) &&
                        (mask == nullptr || reinterpret_cast<uintptr_t>(mask) % 16 == 0);
   const bool masked = mask != nullptr;
   cudaError_t e;
   if (ev_start) cudaEventRecord(ev_start, stream);
+  const long long ntiles = n / TILE;
+  if (masked && aligned && live_scratch && ntiles > 0) {
+    // list the tiles that have a selected row, so that the kernel never reads the others
+    const long long nw = (ntiles + 31) / 32;
+    unsigned* bits = live_scratch;
+    unsigned* cnt = bits + nw;
+    unsigned* pre = cnt + nw;
+    long long blocks = (nw * 32 + LT_NT - 1) / LT_NT;
+    const long long cap = static_cast<long long>(L.grid) * 8;
+    if (blocks > cap) blocks = cap;
+    live_tiles_kernel<<<static_cast<unsigned>(blocks), LT_NT, 0, stream>>>(mask, ntiles, bits, cnt, nw);
+    live_scan_kernel<<<1, LS_NT, 0, stream>>>(cnt, nw, pre);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    *launches += 2;
+    a.live_bits = bits;
+    a.live_pre = pre;
+    a.live_words = nw;
+  }
   const bool m34 = state_out != nullptr || (out && (out->m3 || out->m4));
   e = m34 ? launch_m<true>(L, a, masked, aligned, stream) : launch_m<false>(L, a, masked, aligned, stream);
   if (e != cudaSuccess) return e;

@@ -111,6 +111,10 @@ __global__ void __launch_bounds__(MNT) filter_mask_kernel(const void* col, long 
   for (long long w0 = warp * 32; w0 < n_words; w0 += nwarps * 32) {
     const long long row0 = w0 * 64;
     const unsigned long long inw = !in_mask ? ~0ull : (w0 + lane < n_words ? in_mask[w0 + lane] : 0ull);
+    if (__all_sync(0xffffffffu, inw == 0ull)) {  // 2048 rows none of which is selected
+      if (w0 + lane < n_words) mask[w0 + lane] = 0ull;
+      continue;
+    }
     unsigned long long word = 0;
 #pragma unroll 16
     for (int k = 0; k < 64; ++k) {
