@@ -18,8 +18,8 @@
 // of small bins (<= 16 rows, inside the chunk) are taken one bin per lane; pairs of medium bins
 // (<= 2048 rows, inside the chunk) one bin per half-warp; any other bin by the whole warp --
 // always with coalesced loads and a butterfly reduction over the lanes that share a bin.
-// (Measured on 1e9 ticks in bins of 1..831 rows: one bin per warp 2.8 ms, per quarter-warp 2.3,
-// per eighth 2.3, per half-warp 2.06; the reference's one thread per bin 2.06.)  A bin wholly inside the chunk is written at once; a bin that
+// (Measured on 1e9 ticks in bins of 1..831 rows: one bin per warp 2.79 ms, per quarter-warp 2.14,
+// per eighth 2.28, per half-warp 2.06; the reference's one thread per bin 2.06.)  A bin wholly inside the chunk is written at once; a bin that
 // crosses a chunk edge leaves a partial state per chunk (its first chunk's in slot 1, the
 // others' in slot 0), and a second kernel merges them (one warp per bin, the extrema's
 // first-row rule kept through row offsets).  Sums therefore differ from the serial order in
