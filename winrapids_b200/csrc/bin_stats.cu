@@ -12,14 +12,16 @@
 // variance = max(sum_sq / count - mean^2, 0) for count > 1, std = sqrt(variance).
 //
 // The reference runs one thread per bin over its rows, which leaves lanes idle on uneven bins
-// and serialises a large bin on one thread.  Here the rows are cut into fixed chunks of 16384,
-// one warp per chunk (the grid sized to the resident warps): the warp finds the chunk's first
-// bin with a 32-way search of the boundaries, then walks the bins that overlap the chunk.  Runs
+// and serialises a large bin on one thread.  Here the rows are cut into fixed chunks of 16384;
+// warps take chunks from an atomic counter (so they finish together) at full occupancy (32
+// registers): the warp finds the chunk's first bin with a 32-way search of the boundaries, then
+// walks the bins that overlap the chunk.  Runs
 // of small bins (<= 16 rows, inside the chunk) are taken one bin per lane; pairs of medium bins
 // (<= 2048 rows, inside the chunk) one bin per half-warp; any other bin by the whole warp --
 // always with coalesced loads and a butterfly reduction over the lanes that share a bin.
 // (Measured on 1e9 ticks in bins of 1..831 rows: one bin per warp 2.79 ms, per quarter-warp 2.14,
-// per eighth 2.28, per half-warp 2.06; the reference's one thread per bin 2.06.)  A bin wholly inside the chunk is written at once; a bin that
+// per eighth 2.28, per half-warp 2.06, with chunks handed out dynamically 1.85, and at 8 blocks
+// per SM 1.70; the reference's one thread per bin 2.06.)  A bin wholly inside the chunk is written at once; a bin that
 // crosses a chunk edge leaves a partial state per chunk (its first chunk's in slot 1, the
 // others' in slot 0), and a second kernel merges them (one warp per bin, the extrema's
 // first-row rule kept through row offsets).  Sums therefore differ from the serial order in
@@ -107,6 +109,7 @@ struct BinArgs {
   tbgb_bin_stats out;
   BinPart* part;  // [n_chunks][2][ncol]
   long long n_chunks;
+  unsigned long long* next_chunk;  // per column: chunks handed out so far (zeroed before the launch)
   uint32_t* err;
 };
 
@@ -189,12 +192,15 @@ __device__ __forceinline__ long long first_bin_after(const long long* B, long lo
   return bal ? lo + (__ffs(bal) - 1) : hi;
 }
 
-__global__ void __launch_bounds__(BNT) bin_chunk_kernel(BinArgs a) {
+__global__ void __launch_bounds__(BNT, 8) bin_chunk_kernel(BinArgs a) {
   const int lane = threadIdx.x & 31;
   const int col = blockIdx.y;
   const double* x = a.data + static_cast<long long>(col) * a.n;
-  const long long nw = static_cast<long long>(gridDim.x) * BWARPS;
-  for (long long c = static_cast<long long>(blockIdx.x) * BWARPS + (threadIdx.x >> 5); c < a.n_chunks; c += nw) {
+  for (;;) {
+    unsigned long long cc = 0;
+    if (lane == 0) cc = atomicAdd(a.next_chunk + col, 1ull);
+    const long long c = static_cast<long long>(__shfl_sync(0xffffffffu, cc, 0));
+    if (c >= a.n_chunks) break;
     const long long c0 = c * BCH;
     const long long c1 = c0 + BCH < a.n ? c0 + BCH : a.n;
     BinPart* slots = a.part + (c * 2) * a.ncol + col;  // slot s at slots[s * ncol]
@@ -321,7 +327,8 @@ int chunk_grid(long long n_chunks, int num_sms) {
 
 size_t bin_stats_scratch_bytes(long long n_ticks, int n_columns) {
   const long long n_chunks = (n_ticks + BCH - 1) / BCH;
-  return static_cast<size_t>(n_chunks > 0 ? n_chunks : 1) * 2 * static_cast<size_t>(n_columns) * sizeof(BinPart);
+  return static_cast<size_t>(n_chunks > 0 ? n_chunks : 1) * 2 * static_cast<size_t>(n_columns) * sizeof(BinPart) +
+         static_cast<size_t>(n_columns) * 8;
 }
 
 cudaError_t bin_stats_launch(const double* data, long long n_ticks, int n_columns, const int64_t* boundaries,
@@ -337,6 +344,8 @@ cudaError_t bin_stats_launch(const double* data, long long n_ticks, int n_column
   a.out = *out;
   a.part = static_cast<BinPart*>(scratch);
   a.n_chunks = (n_ticks + BCH - 1) / BCH;
+  a.next_chunk = reinterpret_cast<unsigned long long*>(static_cast<char*>(scratch) +
+                 static_cast<size_t>(a.n_chunks > 0 ? a.n_chunks : 1) * 2 * n_columns * sizeof(BinPart));
   a.err = err;
   long long pb = (n_bins + BNT - 1) / BNT;
   if (pb > 65536) pb = 65536;
@@ -345,6 +354,8 @@ cudaError_t bin_stats_launch(const double* data, long long n_ticks, int n_column
   if (e != cudaSuccess) return e;
   (*launches)++;
   if (a.n_chunks == 0) return cudaSuccess;
+  e = cudaMemsetAsync(a.next_chunk, 0, static_cast<size_t>(n_columns) * 8, s);
+  if (e != cudaSuccess) return e;
   const dim3 grid(chunk_grid(a.n_chunks, num_sms), static_cast<unsigned>(n_columns));
   bin_chunk_kernel<<<grid, BNT, 0, s>>>(a);
   e = cudaGetLastError();
