@@ -574,7 +574,7 @@ class PushdownJob:
         import torch
 
         self.ctx, self.wl = ctx, wl
-        self.kernel = "table_kernel"
+        self.kernel = "dense_moments_kernel"
         self.bpr = 12
         self.G = wl["groups"]
         self.tile_rows = wl["tile_rows"]

@@ -476,6 +476,7 @@ tbgb_status tbgb_set_table_mode(tbgb_ctx* ctx, int mode) {
 tbgb_status tbgb_groupby_dense(tbgb_ctx* ctx, const int32_t* d_keys, const double* d_vals, const uint64_t* d_mask,
                                int64_t n, int32_t n_groups, const tbgb_moments* out, void* stream) {
   if (!out) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "out is NULL");
+
   if (n_groups > tbgb::kDenseMaxGroups) {
     if (n > 0 && !d_vals) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "values pointer is NULL");
     const tbgb_columns c = plain_f64(d_vals);
