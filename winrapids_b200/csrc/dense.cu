@@ -805,19 +805,27 @@ __device__ __forceinline__ GState spill_state(const unsigned long long* sp, int 
 // One warp per group: lane l folds partials l, l+32, ... (each CTA contributes
 // TEAMS * opg owner partials and one spill partial), then a fixed shuffle tree
 // folds the lanes.
-__global__ void __launch_bounds__(256) dense_fold_kernel(const double* __restrict__ part,
-                                                          const unsigned long long* __restrict__ spill, int P, int G,
-                                                          int opg, const unsigned long long* __restrict__ zfirst,
-                                                          tbgb_moments out, double* state_out, int m34) {
-  const int lane = threadIdx.x & 31;
-  const int g = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  if (g >= G) return;
+// One block per group: every thread folds a few of the group's partial states (the CTAs' owner
+// partials and spill states), then warps shuffle and thread 0 folds the eight warp results in
+// warp order (a fixed tree: the same bits every run).  A warp per group left the GPU nearly idle
+// while each lane walked a chain of a dozen dependent loads and merges.
+constexpr int FOLD_NT = 256;
+
+__global__ void __launch_bounds__(FOLD_NT) dense_fold_kernel(const double* __restrict__ part,
+                                                             const unsigned long long* __restrict__ spill, int P,
+                                                             int G, int opg,
+                                                             const unsigned long long* __restrict__ zfirst,
+                                                             tbgb_moments out, double* state_out, int m34) {
+  __shared__ GState warp_state[FOLD_NT / 32];
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int g = blockIdx.x;
+  if (g >= G) return;  // uniform over the block
   const int slots = G * opg;
   const long long stride = static_cast<long long>(P) * TEAMS * slots;
   const int per = TEAMS * opg + 1;
   const int nparts = P * per;
   GState A = gstate_empty();
-  for (int i = lane; i < nparts; i += 32) {
+  for (int i = threadIdx.x; i < nparts; i += FOLD_NT) {
     const int p = i / per, j = i - p * per;
     GState B;
     if (j < TEAMS * opg) {
@@ -844,7 +852,10 @@ __global__ void __launch_bounds__(256) dense_fold_kernel(const double* __restric
     const GState B = gstate_shfl_down(A, d);
     if ((lane & (2 * d - 1)) == 0) gstate_fold(A, B);
   }
-  if (lane == 0) {
+  if (lane == 0) warp_state[warp] = A;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    for (int w = 1; w < FOLD_NT / 32; ++w) gstate_fold(A, warp_state[w]);
     A.zf = zfirst[g];
     if (state_out) gstate_store(state_out, G, g, A);
     else gstate_finalize(A, g, out);
@@ -1002,8 +1013,7 @@ cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, cons
   if (ev_stop) cudaEventRecord(ev_stop, stream);
   (*launches)++;
   tbgb_moments o = out ? *out : tbgb_moments{};
-  const int blocks = (G * 32 + 255) / 256;
-  dense_fold_kernel<<<blocks, 256, 0, stream>>>(part, spill, L.grid, G, L.opg, zfirst, o, state_out, m34 ? 1 : 0);
+  dense_fold_kernel<<<G, FOLD_NT, 0, stream>>>(part, spill, L.grid, G, L.opg, zfirst, o, state_out, m34 ? 1 : 0);
   e = cudaGetLastError();
   if (e == cudaSuccess) (*launches)++;
   return e;
