@@ -806,9 +806,10 @@ __device__ __forceinline__ GState spill_state(const unsigned long long* sp, int 
 // TEAMS * opg owner partials and one spill partial), then a fixed shuffle tree
 // folds the lanes.
 // One block per group: every thread folds a few of the group's partial states (the CTAs' owner
-// partials and spill states), then warps shuffle and thread 0 folds the eight warp results in
-// warp order (a fixed tree: the same bits every run).  A warp per group left the GPU nearly idle
-// while each lane walked a chain of a dozen dependent loads and merges.
+// partials and spill states), warps shuffle, and the eight warp results fold as a three-level tree
+// (a fixed order: the same bits every run).  Chains stay short because a merge has a long latency
+// (its divisions): a warp per group, or a warp per slice of partials, walked chains of dozens of
+// dependent merges and ran 2-4 times longer.
 constexpr int FOLD_NT = 256;
 
 __global__ void __launch_bounds__(FOLD_NT) dense_fold_kernel(const double* __restrict__ part,
@@ -854,8 +855,13 @@ __global__ void __launch_bounds__(FOLD_NT) dense_fold_kernel(const double* __res
   }
   if (lane == 0) warp_state[warp] = A;
   __syncthreads();
+  for (int d = 1; d < FOLD_NT / 32; d <<= 1) {
+    if (threadIdx.x < FOLD_NT / 32 && (threadIdx.x & (2 * d - 1)) == 0) gstate_fold(warp_state[threadIdx.x],
+                                                                                   warp_state[threadIdx.x + d]);
+    __syncthreads();
+  }
   if (threadIdx.x == 0) {
-    for (int w = 1; w < FOLD_NT / 32; ++w) gstate_fold(A, warp_state[w]);
+    A = warp_state[0];
     A.zf = zfirst[g];
     if (state_out) gstate_store(state_out, G, g, A);
     else gstate_finalize(A, g, out);

@@ -17,9 +17,9 @@
 //
 // Three launches over fixed tiles of 65,536 rows: per-tile part counts, one block scanning
 // the [part][tile] count matrix into write offsets (plus the part counts and padded part
-// starts), and the scatter (per 1024-row step: one ballot per part inside each warp, one
+// starts), and the scatter (per 1024-row step: the lanes of each part found with one match, one
 // warp per part scanning the warps' counts, rows written at running offset + prefix +
-// rank in warp).  Counting uses the same ballots, each lane keeping one part's count.
+// rank in warp, from one __match_any_sync over the part ids).  Counting uses the same match.
 #include <cstdint>
 
 #include "common.cuh"
@@ -75,17 +75,14 @@ __global__ void __launch_bounds__(PNT) part_count_kernel(PartitionArgs a, long l
   if (threadIdx.x < a.P) cnt[threadIdx.x] = 0;
   __syncthreads();
   const long long base = t * PTILE;
-  unsigned int mine = 0;  // lane p counts this warp's rows of part p
   for (int s = 0; s < PSTEPS; ++s) {
     long long key;
     double v;
     const int d = route_row<RANGE, F32>(a, base + static_cast<long long>(s) * PNT + threadIdx.x, &key, &v);
-    for (int p = 0; p < a.P; ++p) {
-      const unsigned bal = __ballot_sync(0xffffffffu, d == p);
-      if (lane == p) mine += __popc(bal);
-    }
+    // the lanes of each part: the lowest adds their number
+    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    if (d >= 0 && lane == __ffs(peers) - 1) atomicAdd(cnt + d, static_cast<unsigned>(__popc(peers)));
   }
-  if (lane < a.P && mine) atomicAdd(cnt + lane, mine);
   __syncthreads();
   if (threadIdx.x < a.P) tile_counts[static_cast<long long>(threadIdx.x) * ntiles + t] = cnt[threadIdx.x];
 }
@@ -159,12 +156,12 @@ __global__ void __launch_bounds__(PNT) part_scatter_kernel(PartitionArgs a, long
     long long key = 0;
     double v = 0.0;
     const int d = route_row<RANGE, F32>(a, base + static_cast<long long>(s) * PNT + threadIdx.x, &key, &v);
-    unsigned int rank = 0;
-    for (int p = 0; p < P; ++p) {
-      const unsigned bal = __ballot_sync(0xffffffffu, d == p);
-      if (d == p) rank = __popc(bal & lt);
-      if (lane == p) wcnt[warp][p] = __popc(bal);
-    }
+    // rank among this warp's rows of the same part; the part's lowest lane records their number
+    if (lane < P) wcnt[warp][lane] = 0;
+    __syncwarp();
+    const unsigned peers = __match_any_sync(0xffffffffu, d);
+    const unsigned int rank = __popc(peers & lt);
+    if (d >= 0 && rank == 0) wcnt[warp][d] = __popc(peers);
     __syncthreads();
     // warp p turns column p of wcnt into exclusive prefixes over the warps (lane = warp index)
     if (warp < P) {
