@@ -9,10 +9,10 @@
 namespace tbgb {
 
 constexpr int kDenseThreads = 800;  // threads per CTA (25 warps)
-constexpr int kDenseTile = 2048;    // rows per staged tile
-constexpr int kDenseStages = 4;     // depth of the TMA ring
+constexpr int kDenseTile = 4096;    // rows per staged tile (one batch of the column buffers)
+constexpr int kDenseStages = 2;     // depth of the TMA ring (2 x 48.5 KB in flight per CTA)
 constexpr int kDenseMaxGroups = 1024;
-constexpr int kDenseColBudget = 12288;  // 2 * C * n_groups doubles of column buffers (96 KiB)
+constexpr int kDenseColBudget = 14336;  // 2 * C * n_groups doubles of column buffers (112 KiB; C = 28 at 256 groups)
 
 // Mergeable per-group state, stored as structure-of-arrays with ST_COUNT rows.
 //   nn       non-NaN rows          nf       finite rows
