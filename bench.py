@@ -446,7 +446,7 @@ class DenseJob:
         self.ctx, self.wl, self.lo, self.world, self.dist = ctx, wl, lo, world, dist
         G = self.G = wl["groups"]
         n = self.n_local = hi - lo
-        self.kernel = "dense_moments_kernel" if G <= 1024 else "table_kernel"
+        self.kernel = "dense_moments_kernel" if G <= 512 else "table_kernel"
         self.bpr = 12
         dk = torch.empty(n, dtype=torch.int32, device=dev)
         dv = torch.empty(n, dtype=torch.float64, device=dev)

@@ -120,8 +120,9 @@ typedef struct {
  * (bit i of mask[i/64] set <=> row i participates, filter_jit.rs:202-243 layout;
  * NULL = all rows).  Enqueued on `stream` (a cudaStream_t, NULL = legacy default
  * stream); returns after the launch.  Deferred device errors (key out of range,
- * timeouts) are reported by tbgb_sync.  1 <= n_groups <= 2^31 - 1: up to 1024
- * groups run the shared-memory column kernel, more groups the global-table kernel. */
+ * timeouts) are reported by tbgb_sync.  1 <= n_groups <= 2^31 - 1: up to 512
+ * groups run the shared-memory column kernel, more groups the global-table kernel
+ * (with tbgb_set_table_mode != 0 the column kernel serves up to 1024 groups). */
 tbgb_status tbgb_groupby_dense(tbgb_ctx* ctx, const int32_t* d_keys, const double* d_vals, const uint64_t* d_mask,
                                int64_t n, int32_t n_groups, const tbgb_moments* out, void* stream);
 
