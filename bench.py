@@ -714,6 +714,8 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
         wl["rows_total"] = n_rows
         job = BinsJob(ctx, wl, lo, hi, world, dist, dev, rank)
     elif wl["kind"] == "pushdown":
+        if world > 1:
+            raise SystemExit("the pushdown workload runs on one GPU (its per-rank groups are not merged)")
         wl["rows_total"] = n_rows
         job = PushdownJob(ctx, wl, lo, hi, world, dist, dev)
     else:
