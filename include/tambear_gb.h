@@ -47,6 +47,8 @@
  *                                   groupby kernels never read skipped tiles
  *   tbgb_fused_bin_stats            fused_bin_stats / fused_bin_stats_multi
  *                                   (src/winrapids/kernels/bin_stats.cu:25-151)
+ *   tbgb_groupby_dense_sharded      no counterpart (single GPU): row shards merged over NVLink peer
+ *                                   memory, tables pushed into every rank's buffer by plain stores
  *   tbgb_hash_partition             no counterpart in the reference (single GPU); routes rows to
  *                                   the GPU that owns their key for the sharded high-cardinality path
  *
@@ -325,6 +327,29 @@ typedef struct {
 tbgb_status tbgb_fused_bin_stats(tbgb_ctx* ctx, const double* d_data, int64_t n_ticks, int32_t n_columns,
                                  const int64_t* d_boundaries, int64_t n_bins, const tbgb_bin_stats* out,
                                  void* stream);
+
+/* ---- sharded dense groupby over NVLink peer memory (one process per GPU) ----------------
+ * The exchange step without a library collective: every rank owns an exchange buffer
+ * (tbgb_exchange_alloc: tbgb_exchange_bytes(world, n_groups) bytes, zeroed) and maps every
+ * other rank's buffer with tbgb_peer_export / tbgb_peer_import (CUDA IPC handles, 64 bytes,
+ * passed between the processes by the caller).  tbgb_groupby_dense_sharded then reduces the
+ * rank's rows to its state table, stores it into its slot of every rank's buffer (plain stores
+ * over NVLink), raises its flag there, waits until all ranks' flags show `epoch` and folds the
+ * tables in rank order into `out` -- the same result as tbgb_groupby_dense_state + all-gather
+ * + tbgb_merge_states.  h_exchange is a host array of `world` device pointers (entry q: rank
+ * q's buffer as mapped in this process, entry `rank`: the own buffer); `epoch` starts at 1 and
+ * increases by one per call on every rank.  A rank that never arrives makes the wait give up
+ * after about 2 s: tbgb_sync then reports TBGB_ERR_TIMEOUT.  world <= 8. */
+size_t tbgb_exchange_bytes(int32_t world, int32_t n_groups);
+tbgb_status tbgb_exchange_alloc(tbgb_ctx* ctx, int32_t world, int32_t n_groups, void** d_buf);
+tbgb_status tbgb_exchange_free(tbgb_ctx* ctx, void* d_buf);
+tbgb_status tbgb_peer_export(tbgb_ctx* ctx, void* d_buf, uint8_t* handle /* 64 bytes */);
+tbgb_status tbgb_peer_import(tbgb_ctx* ctx, const uint8_t* handle /* 64 bytes */, void** d_peer);
+tbgb_status tbgb_peer_close(tbgb_ctx* ctx, void* d_peer);
+tbgb_status tbgb_groupby_dense_sharded(tbgb_ctx* ctx, const int32_t* d_keys, const double* d_vals,
+                                       const uint64_t* d_mask, int64_t n, int32_t n_groups, int64_t row_offset,
+                                       int32_t rank, int32_t world, void* const* h_exchange, uint64_t epoch,
+                                       const tbgb_moments* out, void* stream);
 
 /* ---- sharded int64-key groupby (one process / GPU per shard) ----------------------
  * Routes the rows of this shard that pass mask and pred to their owner part

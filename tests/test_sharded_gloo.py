@@ -189,3 +189,74 @@ def test_sharded_dense_gloo():
         assert np.array_equal(out["min"], want["mins"]) and np.array_equal(out["max"], want["maxs"])
         absum = np.bincount(keys, weights=np.abs(vals), minlength=G)
         assert np.all(np.abs(out["sum"] - want["sums"]) <= 1e-12 * absum)
+
+
+# ---- the exchange over peer memory: setup choreography (the kernels need GPUs) ----------
+
+class FakePeerCtx:
+    """Stand-in for the exchange-buffer and IPC methods of winrapids_b200.Context: buffers are
+    numbers, handles carry the owner's rank; rank `fail_on` cannot map one peer."""
+
+    def __init__(self, rank, fail_on=None):
+        self.rank, self.fail_on = rank, fail_on
+        self.log = []
+
+    def exchange_alloc(self, world, G):
+        self.log.append(("alloc", world, G))
+        return 1000 + self.rank
+
+    def exchange_free(self, p):
+        self.log.append(("free", p))
+
+    def peer_export(self, p):
+        return bytes([self.rank]) * 64
+
+    def peer_import(self, handle):
+        if self.rank == self.fail_on:
+            raise RuntimeError("cudaIpcOpenMemHandle: mapping refused")
+        return 2000 + handle[0]
+
+    def peer_close(self, p):
+        self.log.append(("close", p))
+
+    def groupby_dense_sharded(self, keys, vals, G, row_offset, rank, buffers, epoch, out, mask=None):
+        self.log.append(("step", tuple(buffers), epoch, row_offset))
+
+
+def _peer_worker(rank, port, fail_on, q):
+    from winrapids_b200.sharded import PeerMappingError, PeerShardedDenseGroupby
+
+    _init(rank, port)
+    try:
+        ctx = FakePeerCtx(rank, fail_on)
+        try:
+            sh = PeerShardedDenseGroupby(ctx, dist, WORLD, rank, 256, {}, "cpu")
+        except PeerMappingError as e:
+            q.put((rank, "raised", ctx.log, str(e)))
+            return
+        sh.step(torch.zeros(4, dtype=torch.int32), torch.zeros(4), 10 * rank)
+        sh.step(torch.zeros(4, dtype=torch.int32), torch.zeros(4), 10 * rank)
+        sh.finish()
+        q.put((rank, "ok", ctx.log, ""))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_peer_exchange_setup_gloo():
+    res = _spawn(_peer_worker, free_port(), None)
+    for rank, status, log, _ in res:
+        assert status == "ok"
+        steps = [e for e in log if e[0] == "step"]
+        # buffers in rank order: the own buffer at its rank, the peer's mapped one elsewhere
+        want = tuple(1000 + rank if q == rank else 2000 + q for q in range(WORLD))
+        assert [s[1] for s in steps] == [want, want]
+        assert [s[2] for s in steps] == [1, 2]          # epochs start at 1 and step by one
+        assert log[-2:] == [("close", 2000 + (1 - rank)), ("free", 1000 + rank)]
+
+
+def test_peer_exchange_mapping_failure_raises_on_every_rank():
+    res = _spawn(_peer_worker, free_port(), 1)
+    assert [r[1] for r in res] == ["raised", "raised"]
+    for rank, _, log, msg in res:
+        assert ("free", 1000 + rank) in log            # the own buffer released
+        assert ("another rank" in msg) == (rank == 0)

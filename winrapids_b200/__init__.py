@@ -351,6 +351,42 @@ class Context:
         g = int(ng.item())
         return out_keys[:g], {k: v[:g] for k, v in out.items()}
 
+    # ---- the exchange step over NVLink peer memory ----
+    def exchange_alloc(self, world: int, n_groups: int) -> int:
+        """A zeroed exchange buffer (device pointer as an int); free with exchange_free."""
+        p = C.c_void_p()
+        self._check(self._L.tbgb_exchange_alloc(self._h, int(world), int(n_groups), C.byref(p)))
+        return int(p.value)
+
+    def exchange_free(self, ptr: int):
+        self._check(self._L.tbgb_exchange_free(self._h, C.c_void_p(ptr)))
+
+    def peer_export(self, ptr: int) -> bytes:
+        h = (C.c_uint8 * 64)()
+        self._check(self._L.tbgb_peer_export(self._h, C.c_void_p(ptr), h))
+        return bytes(h)
+
+    def peer_import(self, handle: bytes) -> int:
+        h = (C.c_uint8 * 64).from_buffer_copy(handle)
+        p = C.c_void_p()
+        self._check(self._L.tbgb_peer_import(self._h, h, C.byref(p)))
+        return int(p.value)
+
+    def peer_close(self, ptr: int):
+        self._check(self._L.tbgb_peer_close(self._h, C.c_void_p(ptr)))
+
+    def groupby_dense_sharded(self, keys, vals, n_groups: int, row_offset: int, rank: int, exchange, epoch: int,
+                              out: dict, mask=None, stream=None):
+        """Enqueue the shard's groupby, the push of its state table into every rank's exchange
+        buffer and the rank-ordered merge into `out` (exchange: device pointers of all ranks'
+        buffers as mapped here)."""
+        arr = (C.c_void_p * len(exchange))(*[C.c_void_p(int(p)) for p in exchange])
+        m = self.moments_struct(out)
+        self._check(self._L.tbgb_groupby_dense_sharded(self._h, _ptr(keys), _ptr(vals), _ptr(mask),
+                                                       int(vals.numel()), int(n_groups), int(row_offset), int(rank),
+                                                       len(exchange), arr, int(epoch), C.byref(m),
+                                                       _stream_handle(stream)))
+
     def state_bytes(self, n_groups: int) -> int:
         return int(self._L.tbgb_state_bytes(int(n_groups)))
 

@@ -132,6 +132,13 @@ def lib() -> C.CDLL:
         "tbgb_tile_skip_mask": (st, [vp, vp, i64, i32, f64, vp, vp]),
         "tbgb_mask_skip_tiles": (st, [vp, vp, vp, i64, i64, vp, vp]),
         "tbgb_fused_bin_stats": (st, [vp, vp, i64, i32, vp, i64, vp, vp]),
+        "tbgb_exchange_bytes": (C.c_size_t, [i32, i32]),
+        "tbgb_exchange_alloc": (st, [vp, i32, i32, C.POINTER(vp)]),
+        "tbgb_exchange_free": (st, [vp, vp]),
+        "tbgb_peer_export": (st, [vp, vp, vp]),
+        "tbgb_peer_import": (st, [vp, vp, C.POINTER(vp)]),
+        "tbgb_peer_close": (st, [vp, vp]),
+        "tbgb_groupby_dense_sharded": (st, [vp, vp, vp, vp, i64, i32, i64, i32, i32, vp, u64, vp, vp]),
         "tbgb_gen_keys_uniform": (st, [vp, vp, i64, i32, u64, i64, vp]),
         "tbgb_gen_values_uniform": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
         "tbgb_gen_values_normal": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
@@ -160,6 +167,8 @@ HEADER_SYMBOLS = (
     "tbgb_scatter_extremum", "tbgb_group_index_build", "tbgb_factorize_i64",
     "tbgb_filter_mask", "tbgb_mask_and", "tbgb_mask_or", "tbgb_mask_xor", "tbgb_mask_not", "tbgb_mask_popcount",
     "tbgb_tile_stats_build", "tbgb_tile_skip_mask", "tbgb_mask_skip_tiles", "tbgb_fused_bin_stats",
+    "tbgb_exchange_bytes", "tbgb_exchange_alloc", "tbgb_exchange_free", "tbgb_peer_export", "tbgb_peer_import",
+    "tbgb_peer_close", "tbgb_groupby_dense_sharded",
 )
 
 # tbgb_bin_stats field order

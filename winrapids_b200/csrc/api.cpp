@@ -10,6 +10,7 @@
 
 #include "bin_stats.cuh"
 #include "dense.cuh"
+#include "exchange.cuh"
 #include "errbits.hpp"
 #include "gen.cuh"
 #include "group_index.cuh"
@@ -556,6 +557,93 @@ tbgb_status tbgb_groupby_dense_state(tbgb_ctx* ctx, const int32_t* d_keys, const
   }
   return dense_common(ctx, d_keys, d_vals, d_mask, n, n_groups, row_offset, nullptr, static_cast<double*>(d_state),
                       stream);
+}
+
+size_t tbgb_exchange_bytes(int32_t world, int32_t n_groups) {
+  if (world < 1 || world > tbgb::kMaxRanks || n_groups < 1) return 0;
+  return tbgb::exchange_bytes(world, n_groups);
+}
+
+tbgb_status tbgb_exchange_alloc(tbgb_ctx* ctx, int32_t world, int32_t n_groups, void** d_buf) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (!d_buf || world < 1 || world > tbgb::kMaxRanks || n_groups < 1)
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "exchange_alloc: bad arguments (world <= 8)");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  const size_t bytes = tbgb::exchange_bytes(world, n_groups);
+  cudaError_t e = cudaMalloc(d_buf, bytes);  // its own allocation: an IPC handle maps exactly this buffer
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_ALLOC, "exchange buffer", e);
+  e = cudaMemset(*d_buf, 0, bytes);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_BACKEND, "exchange buffer memset", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_exchange_free(tbgb_ctx* ctx, void* d_buf) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  DeviceGuard dg(ctx->device);
+  if (d_buf) cudaFree(d_buf);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_peer_export(tbgb_ctx* ctx, void* d_buf, uint8_t* handle) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (!d_buf || !handle) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "peer_export: NULL pointer");
+  DeviceGuard dg(ctx->device);
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, d_buf);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_BACKEND, "cudaIpcGetMemHandle", e);
+  static_assert(sizeof(h) == 64, "CUDA IPC handles are 64 bytes");
+  std::memcpy(handle, &h, sizeof(h));
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_peer_import(tbgb_ctx* ctx, const uint8_t* handle, void** d_peer) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (!handle || !d_peer) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "peer_import: NULL pointer");
+  DeviceGuard dg(ctx->device);
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  cudaError_t e = cudaIpcOpenMemHandle(d_peer, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_BACKEND, "cudaIpcOpenMemHandle", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_peer_close(tbgb_ctx* ctx, void* d_peer) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  DeviceGuard dg(ctx->device);
+  if (d_peer) cudaIpcCloseMemHandle(d_peer);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_groupby_dense_sharded(tbgb_ctx* ctx, const int32_t* d_keys, const double* d_vals,
+                                       const uint64_t* d_mask, int64_t n, int32_t n_groups, int64_t row_offset,
+                                       int32_t rank, int32_t world, void* const* h_exchange, uint64_t epoch,
+                                       const tbgb_moments* out, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (!out || !h_exchange) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "NULL pointer");
+  if (world < 1 || world > tbgb::kMaxRanks || rank < 0 || rank >= world)
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "rank / world out of range (world <= 8)");
+  if (epoch < 1) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "epoch must start at 1");
+  if (n_groups < 1) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_groups must be >= 1");
+  tbgb::PeerPtrs peers{};
+  for (int q = 0; q < world; ++q) {
+    if (!h_exchange[q] || misaligned(h_exchange[q], 256))
+      return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "exchange buffer NULL or not 256-byte aligned");
+    peers.p[q] = h_exchange[q];
+  }
+  const int parity = static_cast<int>(epoch & 1ull);
+  double* own_slot = reinterpret_cast<double*>(static_cast<char*>(h_exchange[rank]) +
+                                               tbgb::exchange_slot_offset(world, n_groups, parity, rank));
+  // this shard's state table, written straight into its slot of the own buffer
+  tbgb_status st = tbgb_groupby_dense_state(ctx, d_keys, d_vals, d_mask, n, n_groups, row_offset, own_slot, stream);
+  if (st != TBGB_OK) return st;
+  DeviceGuard dg(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaError_t e = tbgb::exchange_push_launch(peers, world, rank, n_groups, epoch, s, &ctx->launches);
+  if (e == cudaSuccess)
+    e = tbgb::exchange_merge_launch(h_exchange[rank], world, n_groups, epoch, ctx->err, out, s, &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "exchange launch", e);
+  return TBGB_OK;
 }
 
 tbgb_status tbgb_merge_states(tbgb_ctx* ctx, const void* d_states, int32_t n_states, int32_t n_groups,

@@ -64,6 +64,70 @@ class ShardedDenseGroupby:
         self.ctx.merge_states(self.gathered, self.world, self.G, out=self.out)
 
 
+class PeerMappingError(RuntimeError):
+    """The exchange buffers could not be mapped across the ranks (raised on every rank)."""
+
+
+class PeerShardedDenseGroupby:
+    """Row-sharded dense-key groupby with the exchange over NVLink peer memory: each rank's
+    state table is stored straight into every rank's exchange buffer and each rank folds the
+    tables in rank order (tbgb_groupby_dense_sharded) -- no library collective in the step.
+    Setup maps the buffers across the processes: the CUDA IPC handles travel once through
+    ``dist.all_gather_object``; a ``dist.barrier`` then makes sure every mapping exists."""
+
+    def __init__(self, ctx, dist, world: int, rank: int, n_groups: int, out: dict, device, group=None):
+        self.ctx, self.dist, self.world, self.rank, self.G = ctx, dist, int(world), int(rank), int(n_groups)
+        self.out, self.group = out, group
+        self.own = ctx.exchange_alloc(self.world, self.G)
+        handles = [None] * self.world
+        dist.all_gather_object(handles, ctx.peer_export(self.own), group=group)
+        self.mapped = []
+        self.buffers = []
+        failure = None
+        try:
+            for q in range(self.world):
+                if q == self.rank:
+                    self.buffers.append(self.own)
+                else:
+                    p = ctx.peer_import(handles[q])
+                    self.mapped.append(p)
+                    self.buffers.append(p)
+        except Exception as exc:  # every rank learns of it below, so none is left waiting
+            failure = exc
+        import torch
+
+        ok = torch.tensor([0 if failure else 1], dtype=torch.int32, device=device)
+        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+        if int(ok.item()) == 0:
+            self.close()
+            raise PeerMappingError(f"peer memory mapping failed on rank {self.rank}: {failure}" if failure
+                                   else "peer memory mapping failed on another rank")
+        dist.barrier(group=group)
+        self.epoch = 0
+
+    def step(self, keys, vals, row_offset: int, mask=None):
+        self.epoch += 1
+        self.ctx.groupby_dense_sharded(keys, vals, self.G, row_offset, self.rank, self.buffers, self.epoch,
+                                       self.out, mask=mask)
+
+    def close(self):
+        """Unmap the peers' buffers and free the own one (finish() first when all ranks are alive)."""
+        for p in self.mapped:
+            self.ctx.peer_close(p)
+        self.mapped = []
+        if self.own:
+            self.ctx.exchange_free(self.own)
+            self.own = 0
+
+    def finish(self):
+        """Orderly teardown on every rank: unmap, wait until no rank maps this buffer, free it."""
+        for p in self.mapped:
+            self.ctx.peer_close(p)
+        self.mapped = []
+        self.dist.barrier(group=self.group)
+        self.close()
+
+
 class ShardedHashGroupby:
     """Owner-sharded int64-key groupby of one shard's rows (see the module docstring).
 
