@@ -92,7 +92,7 @@ def parse():
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU work of the baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--ids", type=int, default=None, help="override the distinct-id count of a hash workload")
-    ap.add_argument("--table-mode", default="auto", choices=["auto", "local", "direct", "bucket"],
+    ap.add_argument("--table-mode", default="auto", choices=["auto", "local", "direct", "bucket", "range"],
                     help="global-table kernel: shared-memory pre-aggregation or direct atomics")
     return ap.parse_args()
 

@@ -365,13 +365,18 @@ tbgb_status tbgb_hash_partition(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb
                                 double* d_out_vals, int64_t* d_part_counts, void* stream);
 
 /* Strategy for groupbys the shared-memory column kernel cannot take alone (int64 keys,
- * more than 1024 dense groups, filter / expression / f32 columns): 0 = choose by size
- * (default: the global table, shared-memory pre-aggregation unless the keys are many);
- * 3 = bucket first (dense keys: stable key-range partition into parts of at
- * most 512 groups, each reduced by the column kernel, up to 16384 groups; int64 keys:
- * stable partition by high hash bits into sub-tables of about 64 MB); 1 = global table
- * with per-CTA shared-memory pre-aggregation (skewed keys); 2 = global table, direct
- * updates (uniform high-cardinality keys).  Modes 1 and 2 never bucket. */
+ * more than 512 dense groups, filter / expression / f32 columns): 0 = choose by size
+ * (default: dense keys take group ranges in shared memory while at most 8 ranges cover
+ * them, about 32,900 groups with all moments; otherwise the global table, shared-memory
+ * pre-aggregation unless the keys are many); 3 = bucket first (dense keys: stable
+ * key-range partition into parts of at most 512 groups, each reduced by the column
+ * kernel, up to 16384 groups; int64 keys: stable partition by high hash bits into
+ * sub-tables of about 64 MB); 1 = global table with per-CTA shared-memory
+ * pre-aggregation (skewed keys); 2 = global table, direct updates (uniform
+ * high-cardinality keys); 4 = dense keys split into ranges of groups, each range's
+ * accumulators held whole in one CTA's shared memory, the CTAs of one range sharing the
+ * rows (falls back to mode 2 beyond 8 ranges; int64 keys as mode 0).  Modes 1, 2 and 4
+ * never bucket. */
 tbgb_status tbgb_set_table_mode(tbgb_ctx* ctx, int mode);
 
 /* Waits for `stream` and returns the first deferred device error of the calls

@@ -9,7 +9,7 @@ from parity import SUM_TOL, abs_sums, bits, check, to_host
 pytestmark = pytest.mark.gpu
 
 SALT = 0x5EED5EED12345678
-MODES = ("local", "direct", "bucket")
+MODES = ("local", "direct", "bucket", "range")
 
 
 def dev(x):
@@ -139,6 +139,70 @@ def test_dense_state_merge_many_groups(ctx):
     ctx.sync()
     want = oracle.moments_grouped_mt(vals, keys, G, threads=8)
     check(got, want, abs_sums(keys, vals, G), "sharded table")
+
+
+@pytest.mark.parametrize("G", [1500, 9000, 30000])
+@pytest.mark.parametrize("f32", [False, True])
+def test_dense_range_ragged_unaligned(ctx, G, f32):
+    """Group ranges in shared memory: a row count that is not a multiple of four, columns that
+    start on and off a 16-byte boundary, a row mask, a predicate and a*b+c (1, 3 and 8 ranges)."""
+    import torch
+
+    n, seed = 1_000_003, 51
+    keys = oracle.gen_keys_uniform(n + 1, G, seed)
+    cols = [oracle.gen_values_normal(n + 1, 0.0, 1.0, seed + i) for i in (1, 2, 3)]
+    if f32:
+        cols = [x.astype(np.float32) for x in cols]
+    cols[0][::777] = np.nan
+    cols[0][3::1201] = np.inf
+    user = host_mask(n)
+    user[::5] = np.uint64(0x0F0F0F0F0F0F0F0F)
+    dk = torch.as_tensor(keys).cuda()
+    dc = [torch.as_tensor(x).cuda() for x in cols]
+    ctx.set_table_mode("range")
+    try:
+        for off in (0, 1):
+            a, b, c = (x[off:off + n] for x in dc)
+            got = to_host(ctx.groupby_dense_columns(dk[off:off + n], a, G, b=b, c=c, expr="a*b+c", pred=">",
+                                                    threshold=-0.5, mask=dev_mask(user)))
+            ha, hb, hc = (x[off:off + n].astype(np.float64) for x in cols)
+            m = host_mask(n, ha, ">", -0.5, user)
+            v = host_value(ha, hb, hc, "a*b+c")
+            k = keys[off:off + n]
+            want = oracle.moments_grouped_mt(v, k, G, threads=8, mask=m)
+            check(got, want, abs_sums(k, v, G, rows_of(m, n)), f"range G={G} f32={f32} off={off}")
+    finally:
+        ctx.set_table_mode("auto")
+
+
+def test_dense_range_key_out_of_range_only_when_selected(ctx):
+    """Keys outside [0, G) raise only on rows that the mask and the predicate select."""
+    import winrapids_b200 as wb
+
+    n, G = 200_001, 9000
+    keys = oracle.gen_keys_uniform(n, G, 8)
+    vals = oracle.gen_values_normal(n, 0.0, 1.0, 8)
+    keys[100], keys[70_001], keys[n - 1] = G + 5, -3, G
+    vals[70_001] = -1.0
+    user = host_mask(n)
+    for r in (100, n - 1):
+        user[r // 64] &= ~np.uint64(1 << (r % 64))
+    ctx.set_table_mode("range")
+    try:
+        got = to_host(ctx.groupby_dense_columns(dev(keys), dev(vals), G, pred=">", threshold=0.0,
+                                                mask=dev_mask(user)))
+        with pytest.raises(wb.KeyOutOfRange):
+            ctx.groupby_dense(dev(keys), dev(vals), G)
+        again = to_host(ctx.groupby_dense_columns(dev(keys), dev(vals), G, pred=">", threshold=0.0,
+                                                  mask=dev_mask(user)))
+    finally:
+        ctx.set_table_mode("auto")
+    m = host_mask(n, vals, ">", 0.0, user)
+    k = np.where((keys >= 0) & (keys < G), keys, 0).astype(np.int32)
+    want = oracle.moments_grouped_mt(vals, k, G, threads=8, mask=m)
+    check(got, want, abs_sums(k, vals, G, rows_of(m, n)), "range oor masked")
+    for f in ("count", "min", "max"):
+        assert np.array_equal(bits(got[f]), bits(again[f])), f
 
 
 # ---- fused filter + expression over dense keys ------------------------------------------

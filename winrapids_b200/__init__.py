@@ -117,9 +117,10 @@ class Context:
         self._check(self._L.tbgb_sync(self._h, _stream_handle(stream)))
 
     def set_table_mode(self, mode: str | int):
-        """'auto' (0), 'local' (1: per-CTA shared-memory pre-aggregation), 'direct' (2) or
-        'bucket' (3: partition first; see tbgb_set_table_mode)."""
-        m = {"auto": 0, "local": 1, "direct": 2, "bucket": 3}.get(mode, mode)
+        """'auto' (0), 'local' (1: per-CTA shared-memory pre-aggregation), 'direct' (2),
+        'bucket' (3: partition first) or 'range' (4: dense keys, group ranges held whole in
+        shared memory); see tbgb_set_table_mode."""
+        m = {"auto": 0, "local": 1, "direct": 2, "bucket": 3, "range": 4}.get(mode, mode)
         self._check(self._L.tbgb_set_table_mode(self._h, int(m)))
 
     @staticmethod

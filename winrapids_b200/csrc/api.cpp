@@ -226,7 +226,8 @@ tbgb_status table_common(tbgb_ctx* ctx, bool hash, const void* keys, const tbgb_
   if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
   const int B = hash ? hash_buckets(ctx, full, groups) : 1;
   const int mode = ctx->table_mode == 3 ? 0 : ctx->table_mode;
-  const tbgb::TablePlan P = tbgb::table_plan(hash, full, mode, groups, ctx->num_sms, B);
+  const bool m34 = full && (state_out != nullptr || (out && (out->m3 || out->m4)));
+  const tbgb::TablePlan P = tbgb::table_plan(hash, full, mode, groups, ctx->num_sms, B, m34);
   // workspace: table | partition scratch | part counts | part starts | routed keys | routed values
   const size_t t_bytes = align256(P.table_bytes);
   const size_t sc_bytes = B > 1 ? align256(tbgb::partition_scratch_bytes(n, B)) : 0;
@@ -258,7 +259,7 @@ tbgb_status table_common(tbgb_ctx* ctx, bool hash, const void* keys, const tbgb_
   a.ngroups = tbgb::table_counter(P, T);
   a.max_groups = groups;
   a.err = ctx->err;
-  a.m34 = full && (state_out != nullptr || (out && (out->m3 || out->m4)));
+  a.m34 = m34;
   a.extrema = full && (state_out != nullptr || !out || out->min || out->max);
   if (B == 1) {
     a.keys = keys;
@@ -478,7 +479,7 @@ size_t tbgb_workspace_bytes(const tbgb_ctx* ctx, int64_t n, int32_t n_groups) {
 
 tbgb_status tbgb_set_table_mode(tbgb_ctx* ctx, int mode) {
   if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
-  if (mode < 0 || mode > 3) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "table mode must be 0, 1, 2 or 3");
+  if (mode < 0 || mode > 4) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "table mode must be 0, 1, 2, 3 or 4");
   ctx->table_mode = mode;
   return TBGB_OK;
 }

@@ -40,6 +40,8 @@ constexpr int TTILE = TNT * TR;     // rows per tile
 constexpr int LS_FULL = 2048;       // shared-table slots with the FULL layout (64 B each)
 constexpr int LS_SC = 4096;         // shared-table slots with the SUMCOUNT layout (20 B each)
 constexpr int LPROBE = 8;           // shared-table probe limit
+constexpr int kRangeSmemBytes = 225 * 1024;  // shared memory of one group range's table
+constexpr int kMaxRanges = 8;       // more ranges: every CTA would read too many keys it drops
 constexpr unsigned long long K_UNSET = 0x7FF8000000000001ull;  // NaN payload no finite value has
 
 template <bool FULL>
@@ -121,12 +123,10 @@ __device__ __forceinline__ void global_row(unsigned long long* p, double v, long
   }
 }
 
-// Per-CTA shared-memory table.
+// Accumulators of a shared-memory table, one array entry per slot: the per-row update
+// and the merge of a slot into a global slot.
 template <bool FULL>
-struct LocalTable {
-  static constexpr int LS = FULL ? LS_FULL : LS_SC;
-  static constexpr int LIMIT = LS * 3 / 4;  // admission stops at this fill
-  unsigned long long* key;
+struct SlotArrays {
   unsigned long long* K;     // FULL
   double* s1;                // FULL: sum(v - K); SUMCOUNT: sum(v)
   double* s2;                // FULL
@@ -137,71 +137,20 @@ struct LocalTable {
   unsigned long long* zf;    // FULL
   unsigned long long* cnt;   // FULL: non-NaN rows (low 32 bits) + finite rows (high 32 bits), one atomic
   uint32_t* nn;              // SUMCOUNT: non-NaN rows
-  uint32_t* fill;
 
-  static constexpr size_t bytes() {
-    return FULL ? static_cast<size_t>(LS) * (10 * 8) + 16 : static_cast<size_t>(LS) * (2 * 8 + 4) + 16;
-  }
-
-  __device__ __forceinline__ void carve(unsigned char* sm) {
-    unsigned char* q = sm;
-    key = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+  __device__ __forceinline__ void clear(int s) {
+    s1[s] = 0.0;
+    if constexpr (!FULL) nn[s] = 0;
     if constexpr (FULL) {
-      K = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
-      s1 = reinterpret_cast<double*>(q); q += LS * 8;
-      s2 = reinterpret_cast<double*>(q); q += LS * 8;
-      s3 = reinterpret_cast<double*>(q); q += LS * 8;
-      s4 = reinterpret_cast<double*>(q); q += LS * 8;
-      mn = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
-      mx = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
-      zf = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
-      cnt = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
-    } else {
-      s1 = reinterpret_cast<double*>(q); q += LS * 8;
-      nn = reinterpret_cast<uint32_t*>(q); q += LS * 4;
+      K[s] = K_UNSET;
+      s2[s] = 0.0;
+      if (s3) s3[s] = 0.0;
+      if (s4) s4[s] = 0.0;
+      mn[s] = f2o(pos_inf());
+      mx[s] = f2o(neg_inf());
+      zf[s] = ~0ull;
+      cnt[s] = 0;
     }
-    fill = reinterpret_cast<uint32_t*>(q);
-  }
-
-  __device__ __forceinline__ void init(int tid) {
-    for (int s = tid; s < LS; s += TNT) {
-      key[s] = kEmptyKey;
-      s1[s] = 0.0;
-      if constexpr (!FULL) nn[s] = 0;
-      if constexpr (FULL) {
-        K[s] = K_UNSET;
-        s2[s] = 0.0;
-        s3[s] = 0.0;
-        s4[s] = 0.0;
-        mn[s] = f2o(pos_inf());
-        mx[s] = f2o(neg_inf());
-        zf[s] = ~0ull;
-        cnt[s] = 0;
-      }
-    }
-    if (tid == 0) *fill = 0;
-  }
-
-  // Slot of `k` (inserted if there is room), or -1.
-  __device__ __forceinline__ int find(unsigned long long k) {
-    if (k == kEmptyKey) return -1;
-    volatile unsigned long long* vk = key;
-    unsigned int h = static_cast<unsigned int>(fmix64(k)) & (LS - 1);
-    for (int probe = 0; probe < LPROBE; ++probe) {
-      const unsigned long long cur = vk[h];
-      if (cur == k) return static_cast<int>(h);
-      if (cur == kEmptyKey) {
-        if (*reinterpret_cast<volatile uint32_t*>(fill) >= static_cast<uint32_t>(LIMIT)) return -1;
-        const unsigned long long old = atomicCAS(key + h, kEmptyKey, k);
-        if (old == kEmptyKey) {
-          atomicAdd(fill, 1u);
-          return static_cast<int>(h);
-        }
-        if (old == k) return static_cast<int>(h);
-      }
-      h = (h + 1) & (LS - 1);
-    }
-    return -1;
   }
 
   __device__ __forceinline__ void row(int s, double v, long long grow, bool m34, bool extrema) {
@@ -234,8 +183,8 @@ struct LocalTable {
     }
   }
 
-  // Merges local slot s into global slot p: power sums re-centred from the local shift K_l
-  // to the global K_g, sum (d + off)^k with off = K_l - K_g.
+  // Merges slot s into global slot p: power sums re-centred from the local shift K_l to
+  // the global K_g, sum (d + off)^k with off = K_l - K_g.
   __device__ __forceinline__ void flush(int s, unsigned long long* p, bool m34, bool extrema) {
     if constexpr (FULL) {
       const unsigned long long n_nn = cnt[s] & 0xFFFFFFFFull, n_f = cnt[s] >> 32;
@@ -266,6 +215,69 @@ struct LocalTable {
         atomicAdd(reinterpret_cast<double*>(p + SC_SUM), s1[s]);
       }
     }
+  }
+};
+
+// Per-CTA shared-memory hash table of a few thousand slots.
+template <bool FULL>
+struct LocalTable : SlotArrays<FULL> {
+  static constexpr int LS = FULL ? LS_FULL : LS_SC;
+  static constexpr int LIMIT = LS * 3 / 4;  // admission stops at this fill
+  unsigned long long* key;
+  uint32_t* fill;
+
+  static constexpr size_t bytes() {
+    return FULL ? static_cast<size_t>(LS) * (10 * 8) + 16 : static_cast<size_t>(LS) * (2 * 8 + 4) + 16;
+  }
+
+  __device__ __forceinline__ void carve(unsigned char* sm) {
+    unsigned char* q = sm;
+    key = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+    if constexpr (FULL) {
+      this->K = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+      this->s1 = reinterpret_cast<double*>(q); q += LS * 8;
+      this->s2 = reinterpret_cast<double*>(q); q += LS * 8;
+      this->s3 = reinterpret_cast<double*>(q); q += LS * 8;
+      this->s4 = reinterpret_cast<double*>(q); q += LS * 8;
+      this->mn = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+      this->mx = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+      this->zf = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+      this->cnt = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+    } else {
+      this->s1 = reinterpret_cast<double*>(q); q += LS * 8;
+      this->nn = reinterpret_cast<uint32_t*>(q); q += LS * 4;
+    }
+    fill = reinterpret_cast<uint32_t*>(q);
+  }
+
+  __device__ __forceinline__ void init(int tid) {
+    for (int s = tid; s < LS; s += TNT) {
+      key[s] = kEmptyKey;
+      this->clear(s);
+    }
+    if (tid == 0) *fill = 0;
+  }
+
+  // Slot of `k` (inserted if there is room), or -1.
+  __device__ __forceinline__ int find(unsigned long long k) {
+    if (k == kEmptyKey) return -1;
+    volatile unsigned long long* vk = key;
+    unsigned int h = static_cast<unsigned int>(fmix64(k)) & (LS - 1);
+    for (int probe = 0; probe < LPROBE; ++probe) {
+      const unsigned long long cur = vk[h];
+      if (cur == k) return static_cast<int>(h);
+      if (cur == kEmptyKey) {
+        if (*reinterpret_cast<volatile uint32_t*>(fill) >= static_cast<uint32_t>(LIMIT)) return -1;
+        const unsigned long long old = atomicCAS(key + h, kEmptyKey, k);
+        if (old == kEmptyKey) {
+          atomicAdd(fill, 1u);
+          return static_cast<int>(h);
+        }
+        if (old == k) return static_cast<int>(h);
+      }
+      h = (h + 1) & (LS - 1);
+    }
+    return -1;
   }
 };
 
@@ -391,6 +403,144 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
       lt.flush(s, T + static_cast<unsigned long long>(gs) * W, a.m34 != 0, a.extrema != 0);
     }
   }
+}
+
+// ---- dense keys: group ranges held whole in shared memory ---------------------------------
+// The G groups are split into R ranges of at most Gr groups, each small enough for a
+// shared-memory table indexed by key (no hashing, no admission limit).  CTA b owns range
+// b % R and walks tiles b / R, b / R + P, ... (P = grid / R): the R CTAs that read one tile
+// run side by side, so the tile crosses HBM about once and the other reads hit L2.  A CTA
+// reads the keys of all its tiles and the value columns only around rows in its range;
+// range 0 also takes rows whose key is outside [0, G), so that a selected one raises
+// KERR_KEY_RANGE as in table_kernel.  At the end every CTA merges its slots into the global
+// table (SlotArrays::flush), whose finaliser gives the outputs.
+constexpr int RROWS = 4;              // rows per thread per step: one 16-byte key load
+constexpr int RTILE = TNT * RROWS;    // rows per CTA per step
+
+template <bool FULL>
+__host__ __device__ constexpr int range_slot_bytes(bool m34) {
+  return FULL ? 8 * (m34 ? 9 : 7) : 12;
+}
+
+template <bool FULL>
+__device__ __forceinline__ void range_carve(SlotArrays<FULL>& t, unsigned char* q, int Gr, bool m34) {
+  if constexpr (FULL) {
+    t.cnt = reinterpret_cast<unsigned long long*>(q); q += Gr * 8;
+    t.K = reinterpret_cast<unsigned long long*>(q); q += Gr * 8;
+    t.s1 = reinterpret_cast<double*>(q); q += Gr * 8;
+    t.s2 = reinterpret_cast<double*>(q); q += Gr * 8;
+    t.mn = reinterpret_cast<unsigned long long*>(q); q += Gr * 8;
+    t.mx = reinterpret_cast<unsigned long long*>(q); q += Gr * 8;
+    t.zf = reinterpret_cast<unsigned long long*>(q); q += Gr * 8;
+    t.s3 = nullptr;
+    t.s4 = nullptr;
+    if (m34) {
+      t.s3 = reinterpret_cast<double*>(q); q += Gr * 8;
+      t.s4 = reinterpret_cast<double*>(q);
+    }
+    t.nn = nullptr;
+  } else {
+    t.s1 = reinterpret_cast<double*>(q); q += Gr * 8;
+    t.nn = reinterpret_cast<uint32_t*>(q);
+  }
+}
+
+// Four consecutive values of a column starting at row0 (a multiple of four): one or two
+// 16-byte loads when `vec` (the column 16-byte aligned, all four rows inside), else one
+// load per selected row.
+template <bool F32>
+__device__ __forceinline__ void range_load4(const void* col, long long row0, bool vec, unsigned sel, double* v) {
+  if (vec) {
+    if constexpr (F32) {
+      const float4 f = __ldg(reinterpret_cast<const float4*>(static_cast<const float*>(col) + row0));
+      v[0] = f.x; v[1] = f.y; v[2] = f.z; v[3] = f.w;
+    } else {
+      const double2* p = reinterpret_cast<const double2*>(static_cast<const double*>(col) + row0);
+      const double2 lo = __ldg(p), hi = __ldg(p + 1);
+      v[0] = lo.x; v[1] = lo.y; v[2] = hi.x; v[3] = hi.y;
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < RROWS; ++j) {
+      v[j] = 0.0;
+      if ((sel >> j) & 1u) {
+        if constexpr (F32) v[j] = static_cast<double>(__ldg(static_cast<const float*>(col) + row0 + j));
+        else v[j] = __ldg(static_cast<const double*>(col) + row0 + j);
+      }
+    }
+  }
+}
+
+template <bool F32, bool FULL>
+__global__ void __launch_bounds__(TNT, 1) range_table_kernel(TableArgs a, int R, int Gr, int vec_ok) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  constexpr int W = slot_words<FULL>();
+  const int tid = threadIdx.x;
+  const int r = static_cast<int>(blockIdx.x % R);
+  const long long P = gridDim.x / R, p = blockIdx.x / R;
+  const long long G = static_cast<long long>(a.slots);
+  const long long g0 = static_cast<long long>(r) * Gr;
+  const long long left = G - g0;
+  const int gr = left < Gr ? static_cast<int>(left) : Gr;
+  const bool m34 = a.m34 != 0, extrema = a.extrema != 0;
+  SlotArrays<FULL> t;
+  range_carve<FULL>(t, sm, Gr, m34);
+  for (int s = tid; s < gr; s += TNT) t.clear(s);
+  __syncthreads();
+
+  const long long n = a.n;
+  const int* keys = static_cast<const int*>(a.keys);
+  const int expr = a.cols.expr, pred = a.cols.pred;
+  const double thr = a.cols.threshold;
+  const bool need_b = expr != TBGB_EXPR_A, need_c = expr == TBGB_EXPR_MUL_ADD;
+  const uint64_t* mask = a.mask;
+  const unsigned long long ugr = static_cast<unsigned long long>(gr), uG = static_cast<unsigned long long>(G);
+
+  for (long long base = p * RTILE; base < n; base += P * RTILE) {
+    const long long row0 = base + static_cast<long long>(tid) * RROWS;
+    if (row0 >= n) continue;
+    const bool whole = row0 + RROWS <= n;
+    const bool vec = vec_ok && whole;
+    int kk[RROWS];
+    if (vec) {
+      const int4 k4 = __ldg(reinterpret_cast<const int4*>(keys + row0));
+      kk[0] = k4.x; kk[1] = k4.y; kk[2] = k4.z; kk[3] = k4.w;
+    } else {
+#pragma unroll
+      for (int j = 0; j < RROWS; ++j) kk[j] = row0 + j < n ? __ldg(keys + row0 + j) : 0;
+    }
+    unsigned sel = 0;  // bit j: row row0 + j is this CTA's
+#pragma unroll
+    for (int j = 0; j < RROWS; ++j) {
+      const unsigned long long k = static_cast<unsigned long long>(static_cast<long long>(kk[j]));
+      bool take = row0 + j < n && k - static_cast<unsigned long long>(g0) < ugr;
+      if (r == 0 && row0 + j < n && k >= uG) take = true;
+      sel |= static_cast<unsigned>(take) << j;
+    }
+    // the four rows share one mask word (row0 is a multiple of four)
+    if (sel && mask) sel &= static_cast<unsigned>(__ldg(mask + (row0 >> 6)) >> (row0 & 63)) & 0xFu;
+    if (!sel) continue;
+    double va[RROWS], vb[RROWS] = {0.0, 0.0, 0.0, 0.0}, vc[RROWS] = {0.0, 0.0, 0.0, 0.0};
+    range_load4<F32>(a.cols.a, row0, vec, sel, va);
+    if (need_b) range_load4<F32>(a.cols.b, row0, vec, sel, vb);
+    if (need_c) range_load4<F32>(a.cols.c, row0, vec, sel, vc);
+#pragma unroll
+    for (int j = 0; j < RROWS; ++j) {
+      if (!((sel >> j) & 1u)) continue;
+      if (!eval_pred(pred, va[j], thr)) continue;
+      const unsigned long long k = static_cast<unsigned long long>(static_cast<long long>(kk[j]));
+      if (k >= uG) {
+        atomicOr(a.err, KERR_KEY_RANGE);
+        continue;
+      }
+      const double v = eval_expr(expr, va[j], vb[j], vc[j]);
+      if (is_nan(v)) continue;
+      t.row(static_cast<int>(k - static_cast<unsigned long long>(g0)), v, a.row_offset + row0 + j, m34, extrema);
+    }
+  }
+
+  __syncthreads();
+  for (int s = tid; s < gr; s += TNT) t.flush(s, a.table + static_cast<unsigned long long>(g0 + s) * W, m34, extrema);
 }
 
 __global__ void table_init_kernel(unsigned long long* T, unsigned long long nslots, int full) {
@@ -578,6 +728,15 @@ cudaError_t launch_table(const TablePlan& P, const TableArgs& a, cudaStream_t s)
   return cudaGetLastError();
 }
 
+template <bool F32, bool FULL>
+cudaError_t launch_range(const TablePlan& P, const TableArgs& a, int vec, cudaStream_t s) {
+  auto k = range_table_kernel<F32, FULL>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(P.smem));
+  if (e != cudaSuccess) return e;
+  k<<<P.grid, P.block, P.smem, s>>>(a, P.ranges, P.range_groups, vec);
+  return cudaGetLastError();
+}
+
 template <bool KEY64, bool F32>
 cudaError_t launch_table_kf(const TablePlan& P, const TableArgs& a, cudaStream_t s) {
   if (P.full)
@@ -595,7 +754,7 @@ unsigned long long next_pow2(unsigned long long x) {
 
 size_t table_slot_words(bool full) { return full ? size_t(FL_WORDS) : size_t(SC_WORDS); }
 
-TablePlan table_plan(bool hash, bool full, int mode, long long groups, int num_sms, int buckets) {
+TablePlan table_plan(bool hash, bool full, int mode, long long groups, int num_sms, int buckets, bool m34) {
   TablePlan P{};
   P.hash = hash;
   P.full = full;
@@ -617,6 +776,21 @@ TablePlan table_plan(bool hash, bool full, int mode, long long groups, int num_s
   P.grid = num_sms;
   P.block = TNT;
   P.smem = P.local ? (full ? LocalTable<true>::bytes() : LocalTable<false>::bytes()) : 0;
+  // dense keys: group ranges in shared memory (mode 4, and the default while R stays small)
+  if (!hash && (mode == 0 || mode == 4)) {
+    const long long per = full ? range_slot_bytes<true>(m34) : range_slot_bytes<false>(m34);
+    const long long gr_max = static_cast<long long>(kRangeSmemBytes) / per;
+    const long long R0 = (groups + gr_max - 1) / gr_max;
+    if (R0 <= kMaxRanges && R0 <= num_sms) {
+      const long long Gr = (groups + R0 - 1) / R0;
+      const long long R = (groups + Gr - 1) / Gr;  // every range holds at least one group
+      P.local = false;
+      P.ranges = static_cast<int>(R);
+      P.range_groups = static_cast<int>(Gr);
+      P.grid = static_cast<int>(num_sms / R * R);
+      P.smem = static_cast<size_t>(Gr * per);
+    }
+  }
   return P;
 }
 
@@ -645,7 +819,23 @@ cudaError_t table_accumulate(const TablePlan& P, const TableArgs& a, cudaStream_
   const bool f32 = a.cols.dtype == TBGB_F32;
   if (ev0) cudaEventRecord(ev0, s);
   cudaError_t e;
-  if (P.hash) e = f32 ? launch_table_kf<true, true>(P, a, s) : launch_table_kf<true, false>(P, a, s);
+  // group ranges: a CTA's packed 32-bit row counts must not wrap
+  const bool range = P.ranges > 0 && !a.dev_count &&
+                     a.n / (P.grid / P.ranges) + RTILE < (1ll << 32);
+  if (P.ranges > 0 && !range) {
+    TablePlan D = P;
+    D.ranges = 0;
+    D.smem = 0;
+    D.grid = P.grid > 0 ? P.grid : 1;
+    e = f32 ? launch_table_kf<false, true>(D, a, s) : launch_table_kf<false, false>(D, a, s);
+  } else if (range) {
+    const auto al = [](const void* q) { return (reinterpret_cast<uintptr_t>(q) & 15u) == 0; };
+    const int expr = a.cols.expr;
+    const int vec = al(a.keys) && al(a.cols.a) && (expr == TBGB_EXPR_A || al(a.cols.b)) &&
+                    (expr != TBGB_EXPR_MUL_ADD || al(a.cols.c));
+    if (P.full) e = f32 ? launch_range<true, true>(P, a, vec, s) : launch_range<false, true>(P, a, vec, s);
+    else e = f32 ? launch_range<true, false>(P, a, vec, s) : launch_range<false, false>(P, a, vec, s);
+  } else if (P.hash) e = f32 ? launch_table_kf<true, true>(P, a, s) : launch_table_kf<true, false>(P, a, s);
   else e = f32 ? launch_table_kf<false, true>(P, a, s) : launch_table_kf<false, false>(P, a, s);
   if (e != cudaSuccess) return e;
   if (ev1) cudaEventRecord(ev1, s);

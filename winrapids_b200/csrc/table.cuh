@@ -46,6 +46,8 @@ struct TablePlan {
   bool hash;       // int64 keys
   bool full;       // FULL slot (else SUMCOUNT)
   bool local;      // per-CTA shared-memory pre-aggregation
+  int ranges;      // dense keys: group ranges held whole in shared memory (range_table_kernel), 0 = none
+  int range_groups;  // groups per range
   int buckets;     // hash: sub-tables (rows bucketed by their key's high hash bits first), 1 = one table
   unsigned long long slots;       // dense: n_groups; hash: slots of each sub-table (a power of two)
   size_t table_bytes;  // including the sentinel slot and the counter word
@@ -55,9 +57,11 @@ struct TablePlan {
 };
 
 size_t table_slot_words(bool full);
-// mode: 0 auto, 1 shared-memory pre-aggregation, 2 direct global updates; `buckets` > 1 splits
-// a hash table into that many sub-tables (power of two).
-TablePlan table_plan(bool hash, bool full, int mode, long long n_groups_or_max, int num_sms, int buckets = 1);
+// mode: 0 auto, 1 shared-memory pre-aggregation, 2 direct global updates, 4 group ranges in
+// shared memory (dense keys); `buckets` > 1 splits a hash table into that many sub-tables
+// (power of two); `m34` sizes the group-range slots for sum((v-K)^3) and sum((v-K)^4).
+TablePlan table_plan(bool hash, bool full, int mode, long long n_groups_or_max, int num_sms, int buckets = 1,
+                     bool m34 = true);
 // Sub-table b of a bucketed hash table, and where the distinct-key counter lives.
 unsigned long long* table_bucket(const TablePlan& P, unsigned long long* table, int b);
 unsigned long long* table_counter(const TablePlan& P, unsigned long long* table);
