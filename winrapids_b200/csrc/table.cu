@@ -471,11 +471,51 @@ __device__ __forceinline__ void range_load4(const void* col, long long row0, boo
   }
 }
 
-template <bool F32, bool FULL>
+// Position of the n-th (0-based) set bit of m; m holds more than n set bits.
+__device__ __forceinline__ int nth_set_bit(unsigned m, int n) {
+  int r = 0;
+  int c = __popc(m & 0xFFFFu);
+  if (n >= c) { n -= c; m >>= 16; r += 16; }
+  c = __popc(m & 0xFFu);
+  if (n >= c) { n -= c; m >>= 8; r += 8; }
+  c = __popc(m & 0xFu);
+  if (n >= c) { n -= c; m >>= 4; r += 4; }
+  c = __popc(m & 0x3u);
+  if (n >= c) { n -= c; m >>= 2; r += 2; }
+  if (n >= static_cast<int>(m & 1u)) r += 1;
+  return r;
+}
+
+// One row the CTA took: predicate, key check, expression, NaN drop, then the slot update.
+template <bool FULL>
+__device__ __forceinline__ void range_row(SlotArrays<FULL>& t, const TableArgs& a, int key, long long g0,
+                                          unsigned long long uG, double av, double bv, double cv, long long row,
+                                          bool m34, bool extrema) {
+  if (!eval_pred(a.cols.pred, av, a.cols.threshold)) return;
+  const unsigned long long k = static_cast<unsigned long long>(static_cast<long long>(key));
+  if (k >= uG) {
+    atomicOr(a.err, KERR_KEY_RANGE);
+    return;
+  }
+  const double v = eval_expr(a.cols.expr, av, bv, cv);
+  if (is_nan(v)) return;
+  t.row(static_cast<int>(k - static_cast<unsigned long long>(g0)), v, a.row_offset + row, m34, extrema);
+}
+
+template <bool F32>
+__device__ __forceinline__ double range_load1(const void* col, long long row) {
+  if constexpr (F32) return static_cast<double>(__ldg(static_cast<const float*>(col) + row));
+  else return __ldg(static_cast<const double*>(col) + row);
+}
+
+// COMPACT (more than one range): a lane takes about 1 / R of its rows, so before the updates
+// the warp gathers its selected rows onto consecutive lanes (ballots per row slot, the n-th
+// set bit, key shuffles) and every lane then loads and updates one row per round.
+template <bool F32, bool FULL, bool COMPACT>
 __global__ void __launch_bounds__(TNT, 1) range_table_kernel(TableArgs a, int R, int Gr, int vec_ok) {
   extern __shared__ __align__(16) unsigned char sm[];
   constexpr int W = slot_words<FULL>();
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31;
   const int r = static_cast<int>(blockIdx.x % R);
   const long long P = gridDim.x / R, p = blockIdx.x / R;
   const long long G = static_cast<long long>(a.slots);
@@ -490,24 +530,24 @@ __global__ void __launch_bounds__(TNT, 1) range_table_kernel(TableArgs a, int R,
 
   const long long n = a.n;
   const int* keys = static_cast<const int*>(a.keys);
-  const int expr = a.cols.expr, pred = a.cols.pred;
-  const double thr = a.cols.threshold;
+  const int expr = a.cols.expr;
   const bool need_b = expr != TBGB_EXPR_A, need_c = expr == TBGB_EXPR_MUL_ADD;
   const uint64_t* mask = a.mask;
   const unsigned long long ugr = static_cast<unsigned long long>(gr), uG = static_cast<unsigned long long>(G);
 
   for (long long base = p * RTILE; base < n; base += P * RTILE) {
     const long long row0 = base + static_cast<long long>(tid) * RROWS;
-    if (row0 >= n) continue;
+    if (!COMPACT && row0 >= n) continue;  // COMPACT: every lane stays for the warp's ballots
     const bool whole = row0 + RROWS <= n;
     const bool vec = vec_ok && whole;
-    int kk[RROWS];
+    int kk[RROWS] = {0, 0, 0, 0};
     if (vec) {
       const int4 k4 = __ldg(reinterpret_cast<const int4*>(keys + row0));
       kk[0] = k4.x; kk[1] = k4.y; kk[2] = k4.z; kk[3] = k4.w;
     } else {
 #pragma unroll
-      for (int j = 0; j < RROWS; ++j) kk[j] = row0 + j < n ? __ldg(keys + row0 + j) : 0;
+      for (int j = 0; j < RROWS; ++j)
+        if (row0 + j < n) kk[j] = __ldg(keys + row0 + j);
     }
     unsigned sel = 0;  // bit j: row row0 + j is this CTA's
 #pragma unroll
@@ -519,23 +559,43 @@ __global__ void __launch_bounds__(TNT, 1) range_table_kernel(TableArgs a, int R,
     }
     // the four rows share one mask word (row0 is a multiple of four)
     if (sel && mask) sel &= static_cast<unsigned>(__ldg(mask + (row0 >> 6)) >> (row0 & 63)) & 0xFu;
-    if (!sel) continue;
-    double va[RROWS], vb[RROWS] = {0.0, 0.0, 0.0, 0.0}, vc[RROWS] = {0.0, 0.0, 0.0, 0.0};
-    range_load4<F32>(a.cols.a, row0, vec, sel, va);
-    if (need_b) range_load4<F32>(a.cols.b, row0, vec, sel, vb);
-    if (need_c) range_load4<F32>(a.cols.c, row0, vec, sel, vc);
+    if constexpr (COMPACT) {
+      // selected rows in (slot j, lane) order; round q gives lane L the (q * 32 + L)-th
+      unsigned bj[RROWS];
+      int cum[RROWS + 1];
+      cum[0] = 0;
 #pragma unroll
-    for (int j = 0; j < RROWS; ++j) {
-      if (!((sel >> j) & 1u)) continue;
-      if (!eval_pred(pred, va[j], thr)) continue;
-      const unsigned long long k = static_cast<unsigned long long>(static_cast<long long>(kk[j]));
-      if (k >= uG) {
-        atomicOr(a.err, KERR_KEY_RANGE);
-        continue;
+      for (int j = 0; j < RROWS; ++j) {
+        bj[j] = __ballot_sync(0xffffffffu, (sel >> j) & 1u);
+        cum[j + 1] = cum[j] + __popc(bj[j]);
       }
-      const double v = eval_expr(expr, va[j], vb[j], vc[j]);
-      if (is_nan(v)) continue;
-      t.row(static_cast<int>(k - static_cast<unsigned long long>(g0)), v, a.row_offset + row0 + j, m34, extrema);
+      const long long wrow0 = row0 - static_cast<long long>(lane) * RROWS;  // the warp's first row
+      for (int q = 0; q < cum[RROWS]; q += 32) {
+        const int i = q + lane;
+        const bool act = i < cum[RROWS];
+        const int j = (i >= cum[1]) + (i >= cum[2]) + (i >= cum[3]);
+        const unsigned m = j == 0 ? bj[0] : j == 1 ? bj[1] : j == 2 ? bj[2] : bj[3];
+        const int src = act ? nth_set_bit(m, i - cum[j]) : lane;
+        const int k0 = __shfl_sync(0xffffffffu, kk[0], src), k1 = __shfl_sync(0xffffffffu, kk[1], src);
+        const int k2 = __shfl_sync(0xffffffffu, kk[2], src), k3 = __shfl_sync(0xffffffffu, kk[3], src);
+        if (act) {
+          const int key = j == 0 ? k0 : j == 1 ? k1 : j == 2 ? k2 : k3;
+          const long long row = wrow0 + static_cast<long long>(src) * RROWS + j;
+          const double av = range_load1<F32>(a.cols.a, row);
+          const double bv = need_b ? range_load1<F32>(a.cols.b, row) : 0.0;
+          const double cv = need_c ? range_load1<F32>(a.cols.c, row) : 0.0;
+          range_row<FULL>(t, a, key, g0, uG, av, bv, cv, row, m34, extrema);
+        }
+      }
+    } else {
+      if (!sel) continue;
+      double va[RROWS], vb[RROWS] = {0.0, 0.0, 0.0, 0.0}, vc[RROWS] = {0.0, 0.0, 0.0, 0.0};
+      range_load4<F32>(a.cols.a, row0, vec, sel, va);
+      if (need_b) range_load4<F32>(a.cols.b, row0, vec, sel, vb);
+      if (need_c) range_load4<F32>(a.cols.c, row0, vec, sel, vc);
+#pragma unroll
+      for (int j = 0; j < RROWS; ++j)
+        if ((sel >> j) & 1u) range_row<FULL>(t, a, kk[j], g0, uG, va[j], vb[j], vc[j], row0 + j, m34, extrema);
     }
   }
 
@@ -730,7 +790,7 @@ cudaError_t launch_table(const TablePlan& P, const TableArgs& a, cudaStream_t s)
 
 template <bool F32, bool FULL>
 cudaError_t launch_range(const TablePlan& P, const TableArgs& a, int vec, cudaStream_t s) {
-  auto k = range_table_kernel<F32, FULL>;
+  auto k = P.ranges > 1 ? range_table_kernel<F32, FULL, true> : range_table_kernel<F32, FULL, false>;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(P.smem));
   if (e != cudaSuccess) return e;
   k<<<P.grid, P.block, P.smem, s>>>(a, P.ranges, P.range_groups, vec);
