@@ -437,6 +437,15 @@ def run_reference(args, wl, n_rows, world, rank):
 # our arm
 # ---------------------------------------------------------------------------------
 
+def dense_kernel_name(G: int, mode: str) -> str:
+    """Main kernel of a plain dense groupby (count/sum/min/max/mean/var) under a table mode."""
+    if G <= 512 or (mode != "auto" and G <= 1024):
+        return "dense_moments_kernel"
+    if mode in ("auto", "range") and -(-G // (225 * 1024 // 56)) <= 8:
+        return "range_table_kernel"
+    return "table_kernel"
+
+
 class DenseJob:
     """int32 keys in [0, G): the shared-memory column kernel (G <= 1024) or the global table."""
 
@@ -446,7 +455,7 @@ class DenseJob:
         self.ctx, self.wl, self.lo, self.world, self.dist = ctx, wl, lo, world, dist
         G = self.G = wl["groups"]
         n = self.n_local = hi - lo
-        self.kernel = "dense_moments_kernel" if G <= 512 else "table_kernel"
+        self.kernel = dense_kernel_name(G, wl.get("table_mode", "auto"))
         self.bpr = 12
         dk = torch.empty(n, dtype=torch.int32, device=dev)
         dv = torch.empty(n, dtype=torch.float64, device=dev)
@@ -716,6 +725,7 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
     torch.cuda.set_device(dev)
     ctx = wb.Context(local_rank)
     ctx.set_table_mode(args.table_mode)
+    wl["table_mode"] = args.table_mode
     lo, hi = n_rows * rank // world, n_rows * (rank + 1) // world
     if wl["kind"] == "bins":
         wl["rows_total"] = n_rows
