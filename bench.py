@@ -748,6 +748,8 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
         if dist is not None:
             dist.barrier()
 
+    # the ranks enter every phase together: a step's exchange waits (bounded) for the other ranks
+    barrier()
     for _ in range(args.warmup):
         if flush is not None:
             flush.zero_()
@@ -807,6 +809,8 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
         job.step(dev_in)
         d2h[0] = job.read_result(host_out)
 
+    torch.cuda.synchronize()
+    barrier()  # pinning the host copies takes each rank its own time
     e2e_step()
     torch.cuda.synchronize()
     barrier()
