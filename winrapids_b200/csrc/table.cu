@@ -310,24 +310,37 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
   unsigned long long* T = a.table;
   const unsigned long long hmask = a.slots - 1;
 
-  for (long long base = static_cast<long long>(blockIdx.x) * TTILE; base < n;
-       base += static_cast<long long>(gridDim.x) * TTILE) {
-    long long kk[TR];
-    double va[TR], vb[TR], vc[TR];
-    bool in[TR];  // inside the rows and selected by the mask; other rows' columns are not read
+  // The row loads run one step ahead: the next step's key and columns are in flight while
+  // this step's row probes and updates the table.
+  const long long step = static_cast<long long>(gridDim.x) * TTILE;
+  long long nk[TR];
+  double na[TR], nb[TR], nc[TR];
+  bool nin[TR];  // inside the rows and selected by the mask; other rows' columns are not read
+  auto load_rows = [&](long long b0) {
 #pragma unroll
     for (int r = 0; r < TR; ++r) {
-      const long long row = base + r * TNT + tid;
-      kk[r] = 0; va[r] = 0.0; vb[r] = 0.0; vc[r] = 0.0;
-      in[r] = row < n;
-      if (in[r] && mask) in[r] = (__ldg(mask + (row >> 6)) >> (row & 63)) & 1ull;
-      if (in[r]) {
-        kk[r] = load_key<KEY64>(keys, row);
-        va[r] = load_val<F32>(col_a, row);
-        if (need_b) vb[r] = load_val<F32>(a.cols.b, row);
-        if (need_c) vc[r] = load_val<F32>(a.cols.c, row);
+      const long long row = b0 + r * TNT + tid;
+      nk[r] = 0; na[r] = 0.0; nb[r] = 0.0; nc[r] = 0.0;
+      nin[r] = row < n;
+      if (nin[r] && mask) nin[r] = (__ldg(mask + (row >> 6)) >> (row & 63)) & 1ull;
+      if (nin[r]) {
+        nk[r] = load_key<KEY64>(keys, row);
+        na[r] = load_val<F32>(col_a, row);
+        if (need_b) nb[r] = load_val<F32>(a.cols.b, row);
+        if (need_c) nc[r] = load_val<F32>(a.cols.c, row);
       }
     }
+  };
+  load_rows(static_cast<long long>(blockIdx.x) * TTILE);
+  for (long long base = static_cast<long long>(blockIdx.x) * TTILE; base < n; base += step) {
+    long long kk[TR];
+    double va[TR], vb[TR], vc[TR];
+    bool in[TR];
+#pragma unroll
+    for (int r = 0; r < TR; ++r) {
+      kk[r] = nk[r]; va[r] = na[r]; vb[r] = nb[r]; vc[r] = nc[r]; in[r] = nin[r];
+    }
+    load_rows(base + step);
     // filter + expression; `live` rows have passed mask and predicate
     bool live[TR];
     double v[TR];
