@@ -43,7 +43,7 @@ def _worker(rank, port, mode, q):
     try:
         n, G = 3_000_017, 256
         lo, hi = n * rank // WORLD, n * (rank + 1) // WORLD
-        out = ctx.alloc_moments(G)
+        out = ctx.alloc_moments(G, wb.MOMENT_FIELDS + (("m3", "m4") if mode == "m34" else ()))
         sh = PeerShardedDenseGroupby(ctx, dist, WORLD, rank, G, out, f"cuda:{rank}")
         results = []
         for seed in (1, 2, 3):
@@ -96,11 +96,14 @@ def _need_two_gpus():
         pytest.skip("needs two GPUs")
 
 
-def test_peer_exchange_matches_oracle():
+@pytest.mark.parametrize("mode", ["ok", "m34"])
+def test_peer_exchange_matches_oracle(mode):
+    """Without m3 / m4 among the outputs the shards' states skip them; with them they travel too."""
     _need_two_gpus()
     from parity import abs_sums, check
+    from test_gpu_higher_moments import check_m34
 
-    res = _spawn("ok")
+    res = _spawn(mode)
     n, G = 3_000_017, 256
     for i, seed in enumerate((1, 2, 3)):
         keys = oracle.gen_keys_uniform(n, G, seed)
@@ -109,9 +112,40 @@ def test_peer_exchange_matches_oracle():
         vals[::101] = -0.0
         vals[::1009] = np.inf
         vals[::1013] = np.nan
-        want = oracle.moments_grouped_mt(vals, keys, G, threads=8)
+        want = oracle.moments_grouped_mt(vals, keys, G, threads=8, m34=mode == "m34")
         for rank, results in res:  # every rank holds the merged result of every epoch
             check(results[i], want, abs_sums(keys, vals, G), f"rank {rank} epoch {i + 1}")
+            if mode == "m34":
+                check_m34(results[i], want, keys, vals, G, f"rank {rank} epoch {i + 1}")
+
+
+@pytest.mark.parametrize("m34", [False, True])
+def test_sharded_entry_one_rank(ctx, m34):
+    """tbgb_groupby_dense_sharded with one rank (no peers): the shard's state table goes through
+    the exchange buffer and the merge, over several epochs, with and without m3 / m4."""
+    import torch
+
+    import winrapids_b200 as wb
+    from parity import abs_sums, check
+    from test_gpu_higher_moments import check_m34
+
+    n, G = 1_000_003, 300
+    own = ctx.exchange_alloc(1, G)
+    try:
+        for epoch, seed in enumerate((4, 5, 6), start=1):
+            keys = oracle.gen_keys_uniform(n, G, seed)
+            vals = oracle.inject_nonfinite(oracle.gen_values_normal(n, 3.0, 2.0, seed), 0.01, 0.002, seed)
+            out = ctx.alloc_moments(G, wb.MOMENT_FIELDS + (("m3", "m4") if m34 else ()))
+            ctx.groupby_dense_sharded(torch.from_numpy(keys).cuda(), torch.from_numpy(vals).cuda(), G, 0, 0, [own],
+                                      epoch, out)
+            ctx.sync()
+            got = {f: t.cpu().numpy() for f, t in out.items()}
+            want = oracle.moments_grouped_mt(vals, keys, G, threads=8, m34=m34)
+            check(got, want, abs_sums(keys, vals, G), f"epoch {epoch}")
+            if m34:
+                check_m34(got, want, keys, vals, G, f"epoch {epoch}")
+    finally:
+        ctx.exchange_free(own)
 
 
 def test_peer_exchange_wait_is_bounded():

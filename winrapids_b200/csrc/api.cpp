@@ -136,7 +136,8 @@ tbgb_status profile_events(tbgb_ctx* ctx, cudaEvent_t* e0, cudaEvent_t* e1) {
 }
 
 tbgb_status dense_common(tbgb_ctx* ctx, const int32_t* keys, const double* vals, const uint64_t* mask, int64_t n,
-                         int32_t G, int64_t row_offset, const tbgb_moments* out, double* state_out, void* stream) {
+                         int32_t G, int64_t row_offset, const tbgb_moments* out, double* state_out, void* stream,
+                         bool state_m34 = true) {
   tbgb_status st = check_dense_args(ctx, keys, vals, n, G);
   if (st != TBGB_OK) return st;
   DeviceGuard dg(ctx->device);
@@ -154,7 +155,7 @@ tbgb_status dense_common(tbgb_ctx* ctx, const int32_t* keys, const double* vals,
   st = profile_events(ctx, &e0, &e1);
   if (st != TBGB_OK) return st;
   e = tbgb::dense_moments_launch(L, keys, vals, mask, n, row_offset, G, w.part, w.spill, w.zfirst, ctx->err, out,
-                                 state_out, s, &ctx->launches, e0, e1, w.live);
+                                 state_out, s, &ctx->launches, e0, e1, w.live, state_m34);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "dense groupby launch", e);
   return TBGB_OK;
 }
@@ -212,7 +213,8 @@ size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 // and the expression), then each sub-table takes its rows.
 tbgb_status table_common(tbgb_ctx* ctx, bool hash, const void* keys, const tbgb_columns* cols, const uint64_t* mask,
                          int64_t n, long long groups, int64_t row_offset, int64_t* out_keys,
-                         const tbgb_moments* out, double* state_out, int64_t* d_n_groups, void* stream) {
+                         const tbgb_moments* out, double* state_out, int64_t* d_n_groups, void* stream,
+                         bool state_m34 = true) {
   if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
   if (n < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n must be >= 0");
   if (groups < 1) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "the group count must be >= 1");
@@ -226,7 +228,7 @@ tbgb_status table_common(tbgb_ctx* ctx, bool hash, const void* keys, const tbgb_
   if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
   const int B = hash ? hash_buckets(ctx, full, groups) : 1;
   const int mode = ctx->table_mode == 3 ? 0 : ctx->table_mode;
-  const bool m34 = full && (state_out != nullptr || (out && (out->m3 || out->m4)));
+  const bool m34 = full && ((state_out != nullptr && state_m34) || (out && (out->m3 || out->m4)));
   const tbgb::TablePlan P = tbgb::table_plan(hash, full, mode, groups, ctx->num_sms, B, m34);
   // workspace: table | partition scratch | part counts | part starts | routed keys | routed values
   const size_t t_bytes = align256(P.table_bytes);
@@ -545,19 +547,29 @@ size_t tbgb_state_bytes(int32_t n_groups) {
   return n_groups > 0 ? static_cast<size_t>(tbgb::ST_COUNT) * n_groups * sizeof(double) : 0;
 }
 
-tbgb_status tbgb_groupby_dense_state(tbgb_ctx* ctx, const int32_t* d_keys, const double* d_vals,
-                                     const uint64_t* d_mask, int64_t n, int32_t n_groups, int64_t row_offset,
-                                     void* d_state, void* stream) {
+namespace {
+
+// A shard's mergeable state table; with m34 = false its m3 / m4 stay zero (the cheaper kernels).
+tbgb_status dense_state(tbgb_ctx* ctx, const int32_t* d_keys, const double* d_vals, const uint64_t* d_mask, int64_t n,
+                        int32_t n_groups, int64_t row_offset, void* d_state, void* stream, bool m34) {
   if (!d_state) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "state buffer is NULL");
   if (row_offset < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "row_offset must be >= 0");
   if (n_groups > tbgb::kDenseMaxGroups) {
     if (n > 0 && !d_vals) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "values pointer is NULL");
     const tbgb_columns c = plain_f64(d_vals);
     return table_common(ctx, false, d_keys, &c, d_mask, n, n_groups, row_offset, nullptr, nullptr,
-                        static_cast<double*>(d_state), nullptr, stream);
+                        static_cast<double*>(d_state), nullptr, stream, m34);
   }
   return dense_common(ctx, d_keys, d_vals, d_mask, n, n_groups, row_offset, nullptr, static_cast<double*>(d_state),
-                      stream);
+                      stream, m34);
+}
+
+}  // namespace
+
+tbgb_status tbgb_groupby_dense_state(tbgb_ctx* ctx, const int32_t* d_keys, const double* d_vals,
+                                     const uint64_t* d_mask, int64_t n, int32_t n_groups, int64_t row_offset,
+                                     void* d_state, void* stream) {
+  return dense_state(ctx, d_keys, d_vals, d_mask, n, n_groups, row_offset, d_state, stream, true);
 }
 
 size_t tbgb_exchange_bytes(int32_t world, int32_t n_groups) {
@@ -635,8 +647,10 @@ tbgb_status tbgb_groupby_dense_sharded(tbgb_ctx* ctx, const int32_t* d_keys, con
   const int parity = static_cast<int>(epoch & 1ull);
   double* own_slot = reinterpret_cast<double*>(static_cast<char*>(h_exchange[rank]) +
                                                tbgb::exchange_slot_offset(world, n_groups, parity, rank));
-  // this shard's state table, written straight into its slot of the own buffer
-  tbgb_status st = tbgb_groupby_dense_state(ctx, d_keys, d_vals, d_mask, n, n_groups, row_offset, own_slot, stream);
+  // this shard's state table, written straight into its slot of the own buffer (without the
+  // third and fourth moments unless `out` asks for them: the merge of the others never reads them)
+  tbgb_status st = dense_state(ctx, d_keys, d_vals, d_mask, n, n_groups, row_offset, own_slot, stream,
+                               out->m3 != nullptr || out->m4 != nullptr);
   if (st != TBGB_OK) return st;
   DeviceGuard dg(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);

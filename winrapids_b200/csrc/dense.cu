@@ -844,8 +844,8 @@ __global__ void __launch_bounds__(FOLD_NT) dense_fold_kernel(const double* __res
       B.m2 = part[ST_M2 * stride + idx];
       B.mn = part[ST_MIN * stride + idx];
       B.mx = part[ST_MAX * stride + idx];
-      B.m3 = part[ST_M3 * stride + idx];
-      B.m4 = part[ST_M4 * stride + idx];
+      B.m3 = m34 ? part[ST_M3 * stride + idx] : 0.0;  // written only by the M34 kernels
+      B.m4 = m34 ? part[ST_M4 * stride + idx] : 0.0;
       B.zf = ~0ull;
     } else {
       B = spill_state(spill + static_cast<size_t>(p) * (m34 ? SP_COUNT : SP_BASE) * G, G, g, m34 != 0);
@@ -986,7 +986,7 @@ cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, cons
                                  long long n, long long row_offset, int G, double* part, unsigned long long* spill,
                                  unsigned long long* zfirst, uint32_t* err, const tbgb_moments* out, double* state_out,
                                  cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start, cudaEvent_t ev_stop,
-                                 unsigned* live_scratch) {
+                                 unsigned* live_scratch, bool state_m34) {
   DenseArgs a;
   a.keys = keys; a.vals = vals; a.mask = mask; a.n = n; a.row_offset = row_offset;
   a.G = G; a.C = L.C; a.opg = L.opg; a.slots = L.slots;
@@ -1016,7 +1016,7 @@ cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, cons
     a.live_pre = pre;
     a.live_words = nw;
   }
-  const bool m34 = state_out != nullptr || (out && (out->m3 || out->m4));
+  const bool m34 = (state_out != nullptr && state_m34) || (out && (out->m3 || out->m4));
   e = m34 ? launch_m<true>(L, a, masked, aligned, stream) : launch_m<false>(L, a, masked, aligned, stream);
   if (e != cudaSuccess) return e;
   if (ev_stop) cudaEventRecord(ev_stop, stream);

@@ -46,7 +46,10 @@ cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, cons
                                  long long n, long long row_offset, int G, double* part, unsigned long long* spill,
                                  unsigned long long* zfirst, uint32_t* err, const tbgb_moments* out, double* state_out,
                                  cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start = nullptr,
-                                 cudaEvent_t ev_stop = nullptr, unsigned* live_scratch = nullptr);
+                                 cudaEvent_t ev_stop = nullptr, unsigned* live_scratch = nullptr,
+                                 bool state_m34 = true);
+// state_m34 = false: the state table's m3 / m4 are left at zero (cheaper kernel) for callers
+// whose final outputs need neither.
 // Scratch of the live-tile list of a masked launch over n rows (u32 words).
 size_t dense_live_scratch_bytes(long long n);
 
