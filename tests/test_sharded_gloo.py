@@ -83,10 +83,10 @@ class FakeCtx:
         out["max"][:] = torch.from_numpy(s[:, 3].max(axis=0))
 
 
-def _init(rank, port):
+def _init(rank, port, world=WORLD):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=WORLD)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
 
 
 def _hash_worker(rank, port, n, ids, q):
@@ -141,13 +141,13 @@ def _dense_worker(rank, port, n, G, q):
         dist.destroy_process_group()
 
 
-def _spawn(fn, *args):
+def _spawn(fn, *args, world=WORLD):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    procs = [ctx.Process(target=fn, args=(r, *args, q)) for r in range(WORLD)]
+    procs = [ctx.Process(target=fn, args=(r, *args, q)) for r in range(world)]
     for p in procs:
         p.start()
-    res = [q.get(timeout=120) for _ in range(WORLD)]
+    res = [q.get(timeout=120) for _ in range(world)]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -223,14 +223,14 @@ class FakePeerCtx:
         self.log.append(("step", tuple(buffers), epoch, row_offset))
 
 
-def _peer_worker(rank, port, fail_on, q):
+def _peer_worker(rank, port, fail_on, world, q):
     from winrapids_b200.sharded import PeerMappingError, PeerShardedDenseGroupby
 
-    _init(rank, port)
+    _init(rank, port, world)
     try:
         ctx = FakePeerCtx(rank, fail_on)
         try:
-            sh = PeerShardedDenseGroupby(ctx, dist, WORLD, rank, 256, {}, "cpu")
+            sh = PeerShardedDenseGroupby(ctx, dist, world, rank, 256, {}, "cpu")
         except PeerMappingError as e:
             q.put((rank, "raised", ctx.log, str(e)))
             return
@@ -242,21 +242,25 @@ def _peer_worker(rank, port, fail_on, q):
         dist.destroy_process_group()
 
 
-def test_peer_exchange_setup_gloo():
-    res = _spawn(_peer_worker, free_port(), None)
+@pytest.mark.parametrize("world", [2, 4])
+def test_peer_exchange_setup_gloo(world):
+    res = _spawn(_peer_worker, free_port(), None, world, world=world)
     for rank, status, log, _ in res:
         assert status == "ok"
         steps = [e for e in log if e[0] == "step"]
-        # buffers in rank order: the own buffer at its rank, the peer's mapped one elsewhere
-        want = tuple(1000 + rank if q == rank else 2000 + q for q in range(WORLD))
+        # buffers in rank order: the own buffer at its rank, the peers' mapped ones elsewhere
+        want = tuple(1000 + rank if q == rank else 2000 + q for q in range(world))
         assert [s[1] for s in steps] == [want, want]
         assert [s[2] for s in steps] == [1, 2]          # epochs start at 1 and step by one
-        assert log[-2:] == [("close", 2000 + (1 - rank)), ("free", 1000 + rank)]
+        closes = [e for e in log if e[0] == "close"]
+        assert sorted(closes) == [("close", 2000 + q) for q in range(world) if q != rank]  # every peer unmapped
+        assert log[-1] == ("free", 1000 + rank)         # the own buffer freed last
 
 
-def test_peer_exchange_mapping_failure_raises_on_every_rank():
-    res = _spawn(_peer_worker, free_port(), 1)
-    assert [r[1] for r in res] == ["raised", "raised"]
+@pytest.mark.parametrize("world,fail_on", [(2, 1), (4, 2)])
+def test_peer_exchange_mapping_failure_raises_on_every_rank(world, fail_on):
+    res = _spawn(_peer_worker, free_port(), fail_on, world, world=world)
+    assert [r[1] for r in res] == ["raised"] * world
     for rank, _, log, msg in res:
         assert ("free", 1000 + rank) in log            # the own buffer released
-        assert ("another rank" in msg) == (rank == 0)
+        assert ("another rank" in msg) == (rank != fail_on)
