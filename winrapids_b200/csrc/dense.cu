@@ -40,9 +40,9 @@
 namespace tbgb {
 
 constexpr int NT = kDenseThreads;   // 800: 8 scatter + 2 x 8 owner + 1 producer warp
-constexpr int NSC = 256;            // scatter threads (warps 0-7)
-constexpr int NOW = 256;            // owner threads per team (team 0: warps 8-15, team 1: 16-23)
-constexpr int TEAMS = 2;            // team t sweeps the column buffer of batches k with k % 2 == t
+constexpr int NSC = 512;            // scatter threads (warps 0-15)
+constexpr int NOW = 256;            // owner threads per team (warps 16-23)
+constexpr int TEAMS = 1;            // one team sweeps the column buffers of all batches in turn
 constexpr int SCATTER_WARPS = NSC / 32;
 constexpr int PRODUCER_WARP = (NSC + TEAMS * NOW) / 32;  // warp 24
 // 25 warps put up to 7 warps on one SM sub-partition: 72 registers per thread.
@@ -428,7 +428,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   if (tid == 0) {
     for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], SCATTER_WARPS); }
     for (int s = 0; s < 2; ++s) { mbar_init(&colfull[s], SCATTER_WARPS); mbar_init(&colempty[s], NOW / 32); }
-    static_assert(TEAMS == 2, "one owner team per column buffer");
+    static_assert(TEAMS == 1, "one owner team sweeps both column buffers");
     *abort = 0;
     mbar_fence_init();
   }
@@ -701,7 +701,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     // group meet at a named barrier before its count is reset.
     const bool shared_counts = a.opg > 1;
     for (long long k = team; k < nbatch; k += TEAMS) {
-      const int bs = team;
+      const int bs = static_cast<int>(k & 1);
       const double* col = bs ? col1 : col0;
       uint32_t* cnt = bs ? cnt1 : cnt0;
       const double* splv = splv0 + bs * SPL;
