@@ -98,10 +98,10 @@ def test_dense_table_key_out_of_range(ctx):
     ctx.groupby_dense(dev(keys[:700]), dev(np.ones(700)), G)  # the context stays usable
 
 
-@pytest.mark.parametrize("mode", MODES)
-def test_dense_table_zero_ties_and_infs(ctx, mode):
-    """+-0 ties resolve to the first zero in row order; +-inf rows count, leave the sum."""
-    G = 1500
+@pytest.mark.parametrize("mode,G", [(m, 1500) for m in MODES] + [("auto", 5000), ("range", 12000)])
+def test_dense_table_zero_ties_and_infs(ctx, mode, G):
+    """+-0 ties resolve to the first zero in row order; +-inf rows count, leave the sum (5,000 and
+    12,000 groups: group ranges whose shift and first-zero code live in the global slots)."""
     rng = np.random.default_rng(7)
     n = 400_000
     keys = rng.integers(0, G, n).astype(np.int32)

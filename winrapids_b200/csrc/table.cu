@@ -142,13 +142,13 @@ struct SlotArrays {
     s1[s] = 0.0;
     if constexpr (!FULL) nn[s] = 0;
     if constexpr (FULL) {
-      K[s] = K_UNSET;
+      if (K) K[s] = K_UNSET;
       s2[s] = 0.0;
       if (s3) s3[s] = 0.0;
       if (s4) s4[s] = 0.0;
       mn[s] = f2o(pos_inf());
       mx[s] = f2o(neg_inf());
-      zf[s] = ~0ull;
+      if (zf) zf[s] = ~0ull;
       cnt[s] = 0;
     }
   }
@@ -430,21 +430,25 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
 constexpr int RROWS = 4;              // rows per thread per step: one 16-byte key load
 constexpr int RTILE = TNT * RROWS;    // rows per CTA per step
 
+// Shared bytes of a group's slot.  GK (FULL only): the shift K and the first-zero code stay in
+// the group's global slot (FL_K, FL_ZF), 16 bytes less a group in shared memory.
 template <bool FULL>
-__host__ __device__ constexpr int range_slot_bytes(bool m34) {
-  return FULL ? 8 * (m34 ? 9 : 7) : 12;
+__host__ __device__ constexpr int range_slot_bytes(bool m34, bool gk = false) {
+  return FULL ? 8 * ((gk ? 5 : 7) + (m34 ? 2 : 0)) : 12;
 }
 
-template <bool FULL>
+template <bool FULL, bool GK>
 __device__ __forceinline__ void range_carve(SlotArrays<FULL>& t, unsigned char* q, int Gr, bool m34) {
   if constexpr (FULL) {
     t.cnt = reinterpret_cast<unsigned long long*>(q); q += Gr * 8;
-    t.K = reinterpret_cast<unsigned long long*>(q); q += Gr * 8;
+    t.K = nullptr;
+    if (!GK) { t.K = reinterpret_cast<unsigned long long*>(q); q += Gr * 8; }
     t.s1 = reinterpret_cast<double*>(q); q += Gr * 8;
     t.s2 = reinterpret_cast<double*>(q); q += Gr * 8;
     t.mn = reinterpret_cast<unsigned long long*>(q); q += Gr * 8;
     t.mx = reinterpret_cast<unsigned long long*>(q); q += Gr * 8;
-    t.zf = reinterpret_cast<unsigned long long*>(q); q += Gr * 8;
+    t.zf = nullptr;
+    if (!GK) { t.zf = reinterpret_cast<unsigned long long*>(q); q += Gr * 8; }
     t.s3 = nullptr;
     t.s4 = nullptr;
     if (m34) {
@@ -499,8 +503,51 @@ __device__ __forceinline__ int nth_set_bit(unsigned m, int n) {
   return r;
 }
 
+// GK slot update: the shared accumulators are sums about the global slot's K (p + FL_K, the
+// first finite value that reached the group), and zeros go to the global first-zero code.
+__device__ __forceinline__ void row_gk(SlotArrays<true>& t, int s, unsigned long long* p, double v, long long grow,
+                                       bool m34, bool extrema) {
+  const bool fin = is_finite(v);
+  atomicAdd(t.cnt + s, fin ? 0x100000001ull : 1ull);
+  if (fin) {
+    const double d = v - slot_shift(p + FL_K, v), dd = d * d;
+    atomicAdd(t.s1 + s, d);
+    atomicAdd(t.s2 + s, dd);
+    if (m34) {
+      atomicAdd(t.s3 + s, dd * d);
+      atomicAdd(t.s4 + s, dd * dd);
+    }
+  }
+  if (extrema) {
+    const unsigned long long o = f2o(v);
+    if (o < *reinterpret_cast<volatile unsigned long long*>(t.mn + s)) atomicMin(t.mn + s, o);
+    if (o > *reinterpret_cast<volatile unsigned long long*>(t.mx + s)) atomicMax(t.mx + s, o);
+    if (v == 0.0) atomicMin(p + FL_ZF, zero_code(grow, v));
+  }
+}
+
+// GK merge of slot s into global slot p: the sums already share its K.
+__device__ __forceinline__ void flush_gk(const SlotArrays<true>& t, int s, unsigned long long* p, bool m34,
+                                         bool extrema) {
+  const unsigned long long n_nn = t.cnt[s] & 0xFFFFFFFFull, n_f = t.cnt[s] >> 32;
+  if (n_nn) atomicAdd(p + FL_NN, n_nn);
+  if (n_f) {
+    atomicAdd(reinterpret_cast<double*>(p + FL_S1), t.s1[s]);
+    atomicAdd(reinterpret_cast<double*>(p + FL_S2), t.s2[s]);
+    atomicAdd(p + FL_NF, n_f);
+    if (m34) {
+      atomicAdd(reinterpret_cast<double*>(p + FL_S3), t.s3[s]);
+      atomicAdd(reinterpret_cast<double*>(p + FL_S4), t.s4[s]);
+    }
+  }
+  if (n_nn && extrema) {
+    if (t.mn[s] < __ldcg(p + FL_MN)) atomicMin(p + FL_MN, t.mn[s]);
+    if (t.mx[s] > __ldcg(p + FL_MX)) atomicMax(p + FL_MX, t.mx[s]);
+  }
+}
+
 // One row the CTA took: predicate, key check, expression, NaN drop, then the slot update.
-template <bool FULL>
+template <bool FULL, bool GK>
 __device__ __forceinline__ void range_row(SlotArrays<FULL>& t, const TableArgs& a, int key, long long g0,
                                           unsigned long long uG, double av, double bv, double cv, long long row,
                                           bool m34, bool extrema) {
@@ -512,7 +559,9 @@ __device__ __forceinline__ void range_row(SlotArrays<FULL>& t, const TableArgs& 
   }
   const double v = eval_expr(a.cols.expr, av, bv, cv);
   if (is_nan(v)) return;
-  t.row(static_cast<int>(k - static_cast<unsigned long long>(g0)), v, a.row_offset + row, m34, extrema);
+  const int s = static_cast<int>(k - static_cast<unsigned long long>(g0));
+  if constexpr (GK) row_gk(t, s, a.table + k * slot_words<true>(), v, a.row_offset + row, m34, extrema);
+  else t.row(s, v, a.row_offset + row, m34, extrema);
 }
 
 template <bool F32>
@@ -524,8 +573,9 @@ __device__ __forceinline__ double range_load1(const void* col, long long row) {
 // COMPACT (more than one range): a lane takes about 1 / R of its rows, so before the updates
 // the warp gathers its selected rows onto consecutive lanes (ballots per row slot, the n-th
 // set bit, key shuffles) and every lane then loads and updates one row per round.
-template <bool F32, bool FULL, bool COMPACT>
+template <bool F32, bool FULL, bool COMPACT, bool GK>
 __global__ void __launch_bounds__(TNT, 1) range_table_kernel(TableArgs a, int R, int Gr, int vec_ok) {
+  static_assert(FULL || !GK, "the global shift applies to FULL slots");
   extern __shared__ __align__(16) unsigned char sm[];
   constexpr int W = slot_words<FULL>();
   const int tid = threadIdx.x, lane = tid & 31;
@@ -537,7 +587,7 @@ __global__ void __launch_bounds__(TNT, 1) range_table_kernel(TableArgs a, int R,
   const int gr = left < Gr ? static_cast<int>(left) : Gr;
   const bool m34 = a.m34 != 0, extrema = a.extrema != 0;
   SlotArrays<FULL> t;
-  range_carve<FULL>(t, sm, Gr, m34);
+  range_carve<FULL, GK>(t, sm, Gr, m34);
   for (int s = tid; s < gr; s += TNT) t.clear(s);
   __syncthreads();
 
@@ -597,7 +647,7 @@ __global__ void __launch_bounds__(TNT, 1) range_table_kernel(TableArgs a, int R,
           const double av = range_load1<F32>(a.cols.a, row);
           const double bv = need_b ? range_load1<F32>(a.cols.b, row) : 0.0;
           const double cv = need_c ? range_load1<F32>(a.cols.c, row) : 0.0;
-          range_row<FULL>(t, a, key, g0, uG, av, bv, cv, row, m34, extrema);
+          range_row<FULL, GK>(t, a, key, g0, uG, av, bv, cv, row, m34, extrema);
         }
       }
     } else {
@@ -608,12 +658,17 @@ __global__ void __launch_bounds__(TNT, 1) range_table_kernel(TableArgs a, int R,
       if (need_c) range_load4<F32>(a.cols.c, row0, vec, sel, vc);
 #pragma unroll
       for (int j = 0; j < RROWS; ++j)
-        if ((sel >> j) & 1u) range_row<FULL>(t, a, kk[j], g0, uG, va[j], vb[j], vc[j], row0 + j, m34, extrema);
+        if ((sel >> j) & 1u)
+          range_row<FULL, GK>(t, a, kk[j], g0, uG, va[j], vb[j], vc[j], row0 + j, m34, extrema);
     }
   }
 
   __syncthreads();
-  for (int s = tid; s < gr; s += TNT) t.flush(s, a.table + static_cast<unsigned long long>(g0 + s) * W, m34, extrema);
+  for (int s = tid; s < gr; s += TNT) {
+    unsigned long long* p = a.table + static_cast<unsigned long long>(g0 + s) * W;
+    if constexpr (GK) flush_gk(t, s, p, m34, extrema);
+    else t.flush(s, p, m34, extrema);
+  }
 }
 
 __global__ void table_init_kernel(unsigned long long* T, unsigned long long nslots, int full) {
@@ -803,7 +858,11 @@ cudaError_t launch_table(const TablePlan& P, const TableArgs& a, cudaStream_t s)
 
 template <bool F32, bool FULL>
 cudaError_t launch_range(const TablePlan& P, const TableArgs& a, int vec, cudaStream_t s) {
-  auto k = P.ranges > 1 ? range_table_kernel<F32, FULL, true> : range_table_kernel<F32, FULL, false>;
+  auto k = P.ranges > 1 ? range_table_kernel<F32, FULL, true, false> : range_table_kernel<F32, FULL, false, false>;
+  if constexpr (FULL) {
+    if (P.range_gk)
+      k = P.ranges > 1 ? range_table_kernel<F32, true, true, true> : range_table_kernel<F32, true, false, true>;
+  }
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(P.smem));
   if (e != cudaSuccess) return e;
   k<<<P.grid, P.block, P.smem, s>>>(a, P.ranges, P.range_groups, vec);
@@ -851,13 +910,23 @@ TablePlan table_plan(bool hash, bool full, int mode, long long groups, int num_s
   P.smem = P.local ? (full ? LocalTable<true>::bytes() : LocalTable<false>::bytes()) : 0;
   // dense keys: group ranges in shared memory (mode 4, and the default while R stays small)
   if (!hash && (mode == 0 || mode == 4)) {
-    const long long per = full ? range_slot_bytes<true>(m34) : range_slot_bytes<false>(m34);
-    const long long gr_max = static_cast<long long>(kRangeSmemBytes) / per;
-    const long long R0 = (groups + gr_max - 1) / gr_max;
+    long long per = full ? range_slot_bytes<true>(m34) : range_slot_bytes<false>(m34);
+    long long R0 = (groups + kRangeSmemBytes / per - 1) / (kRangeSmemBytes / per);
+    bool gk = false;
+    if (full) {  // the global shift when it saves a range
+      const long long per_gk = range_slot_bytes<true>(m34, true);
+      const long long R_gk = (groups + kRangeSmemBytes / per_gk - 1) / (kRangeSmemBytes / per_gk);
+      if (R_gk < R0) {
+        per = per_gk;
+        R0 = R_gk;
+        gk = true;
+      }
+    }
     if (R0 <= kMaxRanges && R0 <= num_sms) {
       const long long Gr = (groups + R0 - 1) / R0;
       const long long R = (groups + Gr - 1) / Gr;  // every range holds at least one group
       P.local = false;
+      P.range_gk = gk;
       P.ranges = static_cast<int>(R);
       P.range_groups = static_cast<int>(Gr);
       P.grid = static_cast<int>(num_sms / R * R);
