@@ -91,6 +91,7 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=None)
     ap.add_argument("--cpu-seconds", type=float, default=12.0, help="target CPU work of the baseline sample")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-check", action="store_true", help="skip the parity check after the timed region")
     ap.add_argument("--ids", type=int, default=None, help="override the distinct-id count of a hash workload")
     ap.add_argument("--table-mode", default="auto", choices=["auto", "local", "direct", "bucket", "range"],
                     help="global-table kernel: shared-memory pre-aggregation or direct atomics")
@@ -297,6 +298,29 @@ def cpu_groupby(wl, cols, threads):
     return res
 
 
+def cpu_model() -> str:
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def single_thread_baseline(wl, n_rows, target_s=6.0):
+    """The reference's own execution model: its CPU path is single-threaded
+    (compute_engine.rs:229-230), so the oracle port on one thread over a bounded prefix."""
+    sample = cpu_sample_rows(wl, target_s, 1, n_rows)
+    cols = host_inputs(wl, 0, sample)
+    t0 = time.perf_counter()
+    cpu_groupby(wl, cols, 1)
+    dt = time.perf_counter() - t0
+    return {"value": sample / dt, "unit": "rows/s", "cores": 1, "kind": "port",
+            "sample": f"first {sample} rows of the workload on one thread",
+            "cpu_model": cpu_model(), "nproc": os.cpu_count()}
+
+
 def cpu_sample_rows(wl, target_s, threads, n_rows):
     """Rows the oracle processes in about target_s seconds on `threads` threads (calibrated)."""
     n0 = min(2_000_000, n_rows)
@@ -430,7 +454,70 @@ def run_reference(args, wl, n_rows, world, rank):
                          "sample": f"first {sample} rows of the workload per step ({how})"},
         "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     })
+    line["cpu_baseline"]["cpu_model"] = cpu_model()
+    line["cpu_baseline"]["nproc"] = os.cpu_count()
+    if wl["kind"] != "bins":
+        line["cpu_baseline"]["single_thread"] = single_thread_baseline(wl, n_rows)
+    if wl["kind"] == "dense" and world == 1:
+        line["reference_gpu"] = reference_gpu_scatter(args, wl, n_rows)
     print(json.dumps(line), flush=True)
+
+
+def reference_gpu_scatter(args, wl, n_rows):
+    """The reference's own best GPU groupby kernels (scatter_stats_smem / scatter_stats_warp of
+    crates/tambear/src/hash_scatter.rs, built from its source into oracle/_ref) timed on this GPU
+    over the same workload: they compute sum, sum of squares and count per group (no min / max,
+    no NaN handling), one row per thread, with the reference's launch configuration."""
+    import ctypes as C
+
+    try:
+        import torch
+    except Exception as exc:  # pragma: no cover
+        return {"unavailable": f"torch: {exc}"}
+    lib_path = ROOT / "oracle" / "_ref" / "libref_hash_scatter.so"
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    if not lib_path.exists():
+        return {"unavailable": "oracle/_ref/libref_hash_scatter.so was not built"}
+    if n_rows >= 1 << 31:
+        return {"unavailable": "the reference kernels take an int row count (< 2^31)"}
+    import winrapids_b200 as wb
+
+    L = C.CDLL(str(lib_path))
+    ctx = wb.Context(0)  # input generation only (the workload's SplitMix64 recipe)
+    G = wl["groups"]
+    dk = torch.empty(n_rows, dtype=torch.int32, device="cuda:0")
+    dv = torch.empty(n_rows, dtype=torch.float64, device="cuda:0")
+    ctx.gen_keys_uniform(dk, G, wl["seed"], 0)
+    kind, a, b = wl["values"]
+    (ctx.gen_values_uniform if kind == "uniform" else ctx.gen_values_normal)(dv, a, b, wl["seed"], 0)
+    if wl["nonfinite"]:
+        ctx.gen_inject_nonfinite(dv, wl["nonfinite"][0], wl["nonfinite"][1], wl["seed"], 0)
+    outs = [torch.empty(G, dtype=torch.float64, device="cuda:0") for _ in range(3)]
+    stream = torch.cuda.current_stream()
+    peak, peak_kind = measured_peak()
+    res = {"config": "same rows as the workload; outputs sum / sum_sq / count only", "kernels": {}}
+    for kid, name in ((1, "scatter_stats_smem"), (2, "scatter_stats_warp")):
+        argv = [C.c_int(kid), C.c_void_p(dk.data_ptr()), C.c_void_p(dv.data_ptr())]
+        argv += [C.c_void_p(o.data_ptr()) for o in outs]
+        argv += [C.c_longlong(n_rows), C.c_int(G), C.c_void_p(stream.cuda_stream)]
+        if L.ref_scatter_stats(*argv) != 0:
+            res["kernels"][name] = {"unavailable": "launch failed (shared memory beyond the limit?)"}
+            continue
+        torch.cuda.synchronize()
+        steps = max(3, min(args.steps, 10))
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(steps):
+            L.ref_scatter_stats(*argv)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / steps
+        gbs = n_rows * 12 / (ms / 1e3) / 1e9
+        res["kernels"][name] = {"ms_per_step": ms, "rows_per_s": n_rows / (ms / 1e3), "hbm_gbs": gbs,
+                                "frac": gbs / peak, "peak": peak, "peak_source": peak_kind}
+    ctx.close()
+    return res
 
 
 # ---------------------------------------------------------------------------------
@@ -492,6 +579,9 @@ class DenseJob:
 
     def kernel_bytes(self) -> int:
         return self.n_local * self.bpr
+
+    def check(self, dev_in, dist, world):
+        return dense_check(dev_in[0], dev_in[1], self.out, self.G, dist)
 
     def read_result(self, host: dict) -> int:
         import torch
@@ -564,6 +654,9 @@ class HashJob:
                                        **self.op)
         else:
             self.sharded.step(keys, a, b=b, c=c, **self.op)
+
+    def check(self, dev_in, dist, world):
+        return hash_check(self, dev_in, dist, world)
 
     def kernel_bytes(self) -> int:
         # the table kernel reads the shard's columns (one GPU) or the received (key, f64 value) rows
@@ -716,6 +809,223 @@ class BinsJob:
         return total
 
 
+# ---------------------------------------------------------------------------------
+# parity check after the timed region (every N): the merged result against torch
+# reductions of the same device inputs, all-reduced over the ranks
+# ---------------------------------------------------------------------------------
+
+SUM_TOL = 1e-12   # |sum - want| <= 1e-12 * sum |x| over the group's finite values
+VAR_RTOL = 1e-9   # m2 / variances relative
+CHUNK_ROWS = 1 << 22
+
+
+def _allreduce(dist, t, op):
+    if dist is not None:
+        dist.all_reduce(t, op=op)
+    return t
+
+
+def _chunked_index(keys_long, G):
+    """Row -> chunk * G + key, so that per-(chunk, group) partials see few rows each
+    (few atomics on one address, and short f64 sums)."""
+    import torch
+
+    n = keys_long.numel()
+    chunk = torch.arange(n, device=keys_long.device, dtype=torch.int64) // CHUNK_ROWS
+    return chunk * G + keys_long, (n + CHUNK_ROWS - 1) // CHUNK_ROWS
+
+
+def dense_check(keys, vals, out, G, dist):
+    """Counts bit-exact, min/max bit-exact (a zero is compared by value: torch's reduction does not
+    order +-0 ties), sums within 1e-12 * sum|x|, mean consistent, m2 / variances within 1e-9
+    relative, against chunked torch reductions of this rank's rows all-reduced over the ranks."""
+    import torch
+
+    RO = dist.ReduceOp if dist is not None else None
+    dev = vals.device
+    k = keys.long()
+    if keys.numel() and (int(k.min()) < 0 or int(k.max()) >= G):
+        return {"ok": False, "why": "key outside [0, G)"}
+    idx, nch = _chunked_index(k, G)
+    nan = torch.isnan(vals)
+    fin = torch.isfinite(vals)
+    zero = torch.zeros((), dtype=torch.float64, device=dev)
+
+    def gsum(w):
+        t = torch.zeros(nch * G, dtype=torch.float64, device=dev).index_add_(0, idx, w)
+        return t.view(nch, G).sum(0)
+
+    cnt = gsum((~nan).double())
+    nf = gsum(fin.double())
+    s = gsum(torch.where(fin, vals, zero))
+    absum = gsum(torch.where(fin, vals.abs(), zero))
+    inf = torch.tensor(float("inf"), dtype=torch.float64, device=dev)
+    mn = torch.full((nch * G,), float("inf"), dtype=torch.float64, device=dev).scatter_reduce_(
+        0, idx, torch.where(nan, inf, vals), "amin").view(nch, G).amin(0)
+    mx = torch.full((nch * G,), float("-inf"), dtype=torch.float64, device=dev).scatter_reduce_(
+        0, idx, torch.where(nan, -inf, vals), "amax").view(nch, G).amax(0)
+    K = torch.full((nch * G,), float("inf"), dtype=torch.float64, device=dev).scatter_reduce_(
+        0, idx, torch.where(fin, vals, inf), "amin").view(nch, G).amin(0)
+    sums = torch.stack([cnt, nf, s, absum])
+    _allreduce(dist, sums, RO.SUM if RO else None)
+    _allreduce(dist, mn, RO.MIN if RO else None)
+    _allreduce(dist, mx, RO.MAX if RO else None)
+    _allreduce(dist, K, RO.MIN if RO else None)
+    cnt, nf, s, absum = sums
+    K = torch.where(torch.isfinite(K), K, zero)
+    # m2 = sum over finite v of (v - mean)^2, mean = sum / count; shifted by K so the sums stay exact
+    d = torch.where(fin, vals - K[k], zero)
+    S1 = gsum(d)
+    _allreduce(dist, S1, RO.SUM if RO else None)
+    c1 = torch.where(cnt > 0, cnt, torch.ones_like(cnt))
+    c = torch.where(cnt > 0, S1 / c1 + K * (nf / c1 - 1.0), zero)  # mean - K
+    m2 = gsum(torch.where(fin, (d - c[k]) ** 2, zero))
+    _allreduce(dist, m2, RO.SUM if RO else None)
+
+    got = {f: t.double() for f, t in out.items()}
+    res = {}
+    res["count"] = bool(torch.equal(got["count"], cnt))
+    for f, w in (("min", mn), ("max", mx)):
+        g = got[f]
+        same_bits = g.view(torch.int64) == w.view(torch.int64)
+        res[f] = bool(torch.all(same_bits | ((w == 0) & (g == 0))))
+    res["sum"] = bool(torch.all((got["sum"] - s).abs() <= SUM_TOL * absum))
+    mean_w = torch.where(cnt > 0, s / c1, torch.full_like(s, float("nan")))
+    res["mean"] = bool(torch.all(torch.where(cnt > 0, (got["mean"] - mean_w).abs() <= SUM_TOL * absum / c1 + 1e-300,
+                                             torch.isnan(got["mean"]))))
+    worst = 0.0
+    for f, w in (("m2", torch.where(cnt > 0, m2, zero)),
+                 ("var_pop", torch.where(cnt > 0, m2 / c1, torch.full_like(m2, float("nan")))),
+                 ("var_samp", torch.where(cnt > 1, m2 / (cnt - 1).clamp(min=1), torch.full_like(m2, float("nan"))))):
+        if f not in got:
+            continue
+        g = got[f]
+        nanw = torch.isnan(w)
+        okf = torch.equal(torch.isnan(g), nanw)
+        rel = ((g - w).abs() / w.abs().clamp(min=1e-300))[~nanw & (w != 0)]
+        worst = max(worst, float(rel.max()) if rel.numel() else 0.0)
+        okf = okf and bool(torch.all(torch.where(nanw, True, (g - w).abs() <= VAR_RTOL * w.abs())))
+        res[f] = okf
+    return {"ok": all(res.values()), "fields": res, "worst_var_rel": worst, "groups": G,
+            "method": "chunked torch reductions of the same device inputs, all-reduced over ranks"}
+
+
+def _fingerprint_bucket(keys, bits):
+    """A bucket of 2^bits per int64 key (multiplicative hash; independent of the library's)."""
+    import torch
+
+    h = keys * -7046029254386353131  # 0x9E3779B97F4A7C15 as a signed int64 (wrapping product)
+    return (h >> (64 - bits)) & ((1 << bits) - 1)
+
+
+def _globally_unique(keys, dist, world, dev):
+    """No key appears twice in the union of the ranks' key lists (keys routed by a hash of their
+    own to a checking rank, then sorted there)."""
+    import torch
+
+    if dist is None or world == 1:
+        sk = torch.sort(keys).values
+        return bool(sk.numel() < 2 or torch.all(sk[1:] != sk[:-1]))
+    dest = _fingerprint_bucket(keys, 20) % world
+    order = torch.argsort(dest)
+    send = keys[order]
+    sc = torch.bincount(dest, minlength=world)
+    rc = torch.empty_like(sc)
+    dist.all_to_all_single(rc, sc)
+    recv = torch.empty(int(rc.sum()), dtype=torch.int64, device=dev)
+    dist.all_to_all_single(recv, send, output_split_sizes=rc.tolist(), input_split_sizes=sc.tolist())
+    sk = torch.sort(recv).values
+    return bool(sk.numel() < 2 or torch.all(sk[1:] != sk[:-1]))
+
+
+def hash_check(job, dev_in, dist, world):
+    """int64 keys.  Every rank: its result groups' keys are unique across all ranks; per bucket of
+    2^24 key hashes, the result's counts equal the input's (exact) and its sums are within
+    1e-12 * sum|x| of the input's (all-reduced over ranks); mean = sum / count.  With one rank,
+    additionally every group's count, sum and (when present) m2 against torch reductions over the
+    rows mapped to their group by a sorted search.  Rows are visited in chunks to bound memory."""
+    import torch
+
+    RO = dist.ReduceOp if dist is not None else None
+    dev = dev_in[0].device
+    n = dev_in[0].numel()
+    step = 1 << 27
+
+    def rows(lo, hi):
+        """(keys, v) of rows [lo, hi) that take part, v in f64."""
+        keys = dev_in[0][lo:hi]
+        a = dev_in[1][lo:hi].double()
+        if len(dev_in) > 2:  # the fused pipeline: a > 0 (NaN fails), v = (a * b) + c with two roundings
+            live = a > job.op["threshold"]
+            prod = a * dev_in[2][lo:hi]
+            v = prod + dev_in[3][lo:hi]
+            return keys[live], v[live]
+        return keys, a
+
+    g = int(job.ng.item())
+    rk = job.out_keys[:g]
+    got = {f: t[:g] for f, t in job.out.items()}
+    res = {"unique": _globally_unique(rk, dist, world, dev)}
+    bits = 24
+    nb = 1 << bits
+    zero = torch.zeros((), dtype=torch.float64, device=dev)
+    want = torch.zeros(3, nb, dtype=torch.float64, device=dev)
+    for lo in range(0, n, step):
+        keys, v = rows(lo, min(n, lo + step))
+        fin = torch.isfinite(v)
+        bi = _fingerprint_bucket(keys, bits)
+        want[0].index_add_(0, bi, (~torch.isnan(v)).double())
+        want[1].index_add_(0, bi, torch.where(fin, v, zero))
+        want[2].index_add_(0, bi, torch.where(fin, v.abs(), zero))
+        del keys, v, fin, bi
+    br = _fingerprint_bucket(rk, bits)
+    have = torch.stack([torch.zeros(nb, dtype=torch.float64, device=dev).index_add_(0, br, got[f])
+                        for f in ("count", "sum")])
+    _allreduce(dist, want, RO.SUM if RO else None)
+    _allreduce(dist, have, RO.SUM if RO else None)
+    res["bucket_counts"] = bool(torch.equal(have[0], want[0]))
+    res["bucket_sums"] = bool(torch.all((have[1] - want[1]).abs() <= SUM_TOL * want[2] + 1e-300))
+    del want, have, br
+    c = got["count"]
+    c1 = torch.where(c > 0, c, torch.ones_like(c))
+    mean_w = torch.where(c > 0, got["sum"] / c1, torch.full_like(c, float("nan")))
+    res["mean"] = bool(torch.all(torch.where(c > 0, (got["mean"] - mean_w).abs() <= 1e-15 * mean_w.abs(),
+                                             torch.isnan(got["mean"]))))
+    if world == 1 and g > 0:
+        sk, perm = torch.sort(rk)
+        cnt = torch.zeros(g, dtype=torch.float64, device=dev)
+        s = torch.zeros(g, dtype=torch.float64, device=dev)
+        absum = torch.zeros(g, dtype=torch.float64, device=dev)
+        found = True
+        for lo in range(0, n, step):
+            keys, v = rows(lo, min(n, lo + step))
+            pos = torch.searchsorted(sk, keys).clamp(max=g - 1)
+            found = found and bool(torch.equal(sk[pos], keys))
+            gi = perm[pos]
+            fin = torch.isfinite(v)
+            cnt.index_add_(0, gi, (~torch.isnan(v)).double())
+            s.index_add_(0, gi, torch.where(fin, v, zero))
+            absum.index_add_(0, gi, torch.where(fin, v.abs(), zero))
+            del keys, v, pos, gi, fin
+        res["every_row_has_its_group"] = found
+        res["count"] = bool(torch.equal(c, cnt))
+        res["sum"] = bool(torch.all((got["sum"] - s).abs() <= SUM_TOL * absum))
+        if "m2" in got:
+            mu = torch.where(cnt > 0, s / torch.where(cnt > 0, cnt, torch.ones_like(cnt)), zero)
+            m2 = torch.zeros(g, dtype=torch.float64, device=dev)
+            for lo in range(0, n, step):
+                keys, v = rows(lo, min(n, lo + step))
+                gi = perm[torch.searchsorted(sk, keys).clamp(max=g - 1)]
+                m2.index_add_(0, gi, torch.where(torch.isfinite(v), (v - mu[gi]) ** 2, zero))
+                del keys, v, gi
+            res["m2"] = bool(torch.all((got["m2"] - m2).abs() <= VAR_RTOL * m2.abs() + 1e-300))
+    ok = torch.tensor([1.0 if all(res.values()) else 0.0], device=dev)
+    _allreduce(dist, ok, RO.MIN if RO else None)
+    return {"ok": bool(ok.item() == 1.0), "fields": res, "groups_this_rank": g,
+            "method": "global key uniqueness, per-bucket count/sum fingerprints over 2^24 key hashes"
+                      + ("; per-group count/sum/m2 by sorted search" if world == 1 else "")}
+
+
 def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
     import torch
 
@@ -825,6 +1135,15 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
     ctx.sync()
     clk = clocks.stop()
 
+    # ---- parity of the last step's result (outside every timed region)
+    check = None
+    if not args.no_check and hasattr(job, "check"):
+        check = job.check(dev_in, dist, world)
+        if dist is not None:
+            okt = torch.tensor([1.0 if check.get("ok") else 0.0], device=dev)
+            dist.all_reduce(okt, op=dist.ReduceOp.MIN)
+            check["ok_all_ranks"] = bool(okt.item() == 1.0)
+
     # ---- max over ranks
     kern_gbs = kbytes / args.steps / (kms / max(klaunches, 1) / 1e3) / 1e9 if kms > 0 else 0.0
     t = torch.tensor([ms, e2e_ms, -kern_gbs, float(launches), float(h2d_step[0]), float(d2h[0])], dtype=torch.float64,
@@ -876,6 +1195,8 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
         "device": ctx.name,
     })
     line.update(extra)
+    if check is not None:
+        line["check"] = check
     if world == 1 and not args.no_cpu_baseline:
         threads = cpu_threads()
         sample = cpu_sample_rows(wl, args.cpu_seconds, threads, n_rows)
@@ -886,7 +1207,10 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
         how = ("exact Kulisch groupby" if wl["kind"] == "dense" else "sort-based exact groupby of int64 keys")
         line["cpu_baseline"] = {"value": sample / dt, "unit": "rows/s", "cores": threads, "kind": "port",
                                 "sample": f"first {sample} rows of the workload, {how} "
-                                          f"(oracle port of the reference's CPU path), {threads} threads"}
+                                          f"(oracle port of the reference's CPU path), {threads} threads",
+                                "cpu_model": cpu_model(), "nproc": os.cpu_count()}
+        if wl["kind"] != "bins":
+            line["cpu_baseline"]["single_thread"] = single_thread_baseline(wl, n_rows)
     print(json.dumps(line), flush=True)
 
 

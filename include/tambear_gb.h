@@ -403,12 +403,26 @@ tbgb_status tbgb_merge_states(tbgb_ctx* ctx, const void* d_states, int32_t n_sta
  * synchronisation).  No counterpart in the reference.
  * Same semantics and outputs as tbgb_groupby_dense, on the current device.
  * Limits: 1 <= n_groups <= 256 (TBGB_ERR_INVALID_ARGUMENT otherwise).  Scratch is
- * a fixed device array of about 10.5 MB inside this library, held by every GPU that
- * loads the library until the process exits.  The first call on a device looks up
- * that array's address (make it before any stream capture).  All calls share the
- * array: calls that overlap on the GPU (other streams, other threads) race and
- * must be serialised by the caller.  The call waits for `stream` and returns any
- * device-side error (e.g. TBGB_ERR_KEY_OUT_OF_RANGE). */
+ * a fixed device array of about 10.5 MB inside this library.  With CUDA's default
+ * lazy module loading that array is mapped on a device by the first call made there,
+ * and stays mapped until the process exits: a caller that is about to reserve nearly
+ * all of a device's memory makes one call on that device first (n = 0 is enough), or
+ * runs with CUDA_MODULE_LOADING=EAGER.  Every call looks up the array's address on the
+ * current device (cudaGetSymbolAddress); make the first call on each device before any
+ * stream capture.  All calls share the array and it keeps the last call's contents
+ * (the call clears what must start empty): calls that overlap on the GPU (other
+ * streams, other threads) race and must be serialised by the caller.  The call waits
+ * for `stream` and then returns:
+ *   TBGB_OK                    outputs written
+ *   TBGB_ERR_INVALID_ARGUMENT  n < 0, NULL pointers, n_groups outside [1, 256]
+ *   TBGB_ERR_KEY_OUT_OF_RANGE  a selected non-NaN row has a key outside [0, n_groups)
+ *   TBGB_ERR_TIMEOUT           a bounded wait inside the kernel gave up
+ *   TBGB_ERR_BACKEND           no usable device (not sm_100, the array cannot be mapped)
+ *                              or a device-side error bit this entry point does not name
+ *   TBGB_ERR_DISPATCH          a launch or the wait for `stream` failed (for example
+ *                              the stream already held an error)
+ *   TBGB_ERR_TRANSFER          the read-back of the device error word failed
+ * There is no context, so no message is kept for tbgb_last_error. */
 tbgb_status tbgb_groupby_dense_noalloc(const int32_t* d_keys, const double* d_vals, const uint64_t* d_mask,
                                        int64_t n, int32_t n_groups, const tbgb_moments* out, void* stream);
 

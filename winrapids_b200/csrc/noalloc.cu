@@ -35,32 +35,36 @@ constexpr size_t kScratchWords = kPartWords + kSpillWords + kZeroWords + kErrWor
 // cudaGetSymbolAddress and passed to the kernels.
 static __device__ __align__(256) unsigned long long g_noalloc_scratch[kScratchWords];
 
-struct DeviceScratch {
-  unsigned long long* base = nullptr;
+struct DeviceInfo {
   int sms = 0;
   bool ready = false;
 };
 
 std::mutex g_setup_mutex;
-DeviceScratch g_scratch_of[kMaxDevices];
+DeviceInfo g_info_of[kMaxDevices];
 
-// Looks up (once per device, with that device current) the scratch address and
-// the SM count.
-tbgb_status device_scratch(int dev, DeviceScratch* out) {
+// The scratch address on the current device and that device's SM count.  The address is
+// looked up on every call, with the device current: a reset of the device or another
+// context made current reloads this library's module there, and a cached address would
+// then point at memory that is no longer ours.  Only the SM count (a property of the
+// hardware) is cached.  The first lookup on a device loads the module and maps the array
+// (with CUDA's default lazy module loading), which can fail with TBGB_ERR_BACKEND when
+// the device has no free memory left.
+tbgb_status device_scratch(int dev, unsigned long long** base, int* sms_out) {
+  void* p = nullptr;
+  if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return TBGB_ERR_BACKEND;
   std::lock_guard<std::mutex> lock(g_setup_mutex);
-  DeviceScratch& d = g_scratch_of[dev];
+  DeviceInfo& d = g_info_of[dev];
   if (!d.ready) {
-    void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess) return TBGB_ERR_BACKEND;
     int sms = 0, major = 0;
     if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return TBGB_ERR_BACKEND;
     if (cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) return TBGB_ERR_BACKEND;
     if (major != 10) return TBGB_ERR_BACKEND;  // built for sm_100a only
-    d.base = static_cast<unsigned long long*>(p);
     d.sms = sms;
     d.ready = true;
   }
-  *out = d;
+  *base = static_cast<unsigned long long*>(p);
+  *sms_out = d.sms;
   return TBGB_OK;
 }
 
@@ -73,15 +77,16 @@ extern "C" tbgb_status tbgb_groupby_dense_noalloc(const int32_t* d_keys, const d
   if (n > 0 && (!d_keys || !d_vals)) return TBGB_ERR_INVALID_ARGUMENT;
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return TBGB_ERR_BACKEND;
-  DeviceScratch ds;
-  tbgb_status st = device_scratch(dev, &ds);
+  unsigned long long* base = nullptr;
+  int sms = 0;
+  tbgb_status st = device_scratch(dev, &base, &sms);
   if (st != TBGB_OK) return st;
 
-  const int ctas = ds.sms < kNoAllocMaxCtas ? ds.sms : kNoAllocMaxCtas;
+  const int ctas = sms < kNoAllocMaxCtas ? sms : kNoAllocMaxCtas;
   const tbgb::DenseLaunch L = tbgb::dense_plan(n_groups, ctas);
   if (L.part_doubles > kPartWords || L.spill_words > kSpillWords) return TBGB_ERR_INVALID_ARGUMENT;
-  double* part = reinterpret_cast<double*>(ds.base);
-  unsigned long long* spill = ds.base + kPartWords;
+  double* part = reinterpret_cast<double*>(base);
+  unsigned long long* spill = base + kPartWords;
   unsigned long long* zfirst = spill + kSpillWords;
   uint32_t* err = reinterpret_cast<uint32_t*>(zfirst + kZeroWords);
 
