@@ -44,5 +44,5 @@ def test_reference_kernels_agree_with_ours(ctx, ref, kind, G):
     absum = abs_sums(keys, vals, G)
     assert np.array_equal(r_cnt, mine["count"])
     assert np.all(np.abs(r_sum - mine["sum"]) <= 2e-12 * absum)
-    sq = oracle.scatter_phi("v*v", keys, vals, None, G)
+    sq = oracle.scatter_phi("v * v", keys, vals, None, G)
     assert np.all(np.abs(r_sq - sq) <= 1e-9 * sq)

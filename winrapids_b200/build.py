@@ -19,7 +19,7 @@ INCLUDE = ROOT / "include"
 BUILD = PKG / "_build"
 LIB = PKG / "libtambear_gb.so"
 
-SOURCES = ["dense.cu", "table.cu", "partition.cu", "phi.cu", "sort.cu", "group_index.cu", "mask.cu", "bin_stats.cu", "exchange.cu", "gen.cu", "noalloc.cu", "api.cpp"]
+SOURCES = ["dense.cu", "table.cu", "partition.cu", "phi.cu", "sort.cu", "group_index.cu", "mask.cu", "bin_stats.cu", "exchange.cu", "gen.cu", "radix.cu", "noalloc.cu", "api.cpp"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-std=c++17", "-lineinfo", "-Xcompiler", "-fPIC", "-I", str(INCLUDE), "-I", str(CSRC)]
 

@@ -17,6 +17,7 @@
 #include "mask.cuh"
 #include "partition.cuh"
 #include "phi.cuh"
+#include "radix.cuh"
 #include "table.cuh"
 #include "tambear_gb.h"
 
@@ -67,7 +68,8 @@ tbgb_status ensure_ws(tbgb_ctx* ctx, size_t bytes) {
     ctx->ws = nullptr;
     ctx->ws_bytes = 0;
   }
-  size_t want = bytes + bytes / 4;
+  const size_t extra = bytes / 4 < (size_t(256) << 20) ? bytes / 4 : (size_t(256) << 20);  // room to grow
+  size_t want = bytes + extra;
   cudaError_t e = cudaMalloc(&ctx->ws, want);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_ALLOC, "workspace allocation", e);
   ctx->ws_bytes = want;
@@ -182,8 +184,62 @@ tbgb_status check_columns(tbgb_ctx* ctx, const tbgb_columns* c, int64_t n) {
   return TBGB_OK;
 }
 
-// Global-table groupby: dense keys (hash == false, `groups` = n_groups) or int64
-// keys (`groups` = max_groups).
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+// int64-key count / sum / mean by radix partitioning (radix.cu); when a bucket overflows, the
+// global table recomputes the whole result, its kernels gated on the radix passes' fallback word
+// (they return at once when it is zero).  The fallback table lives where the second pass's
+// buffer was.
+tbgb_status radix_hash(tbgb_ctx* ctx, const int64_t* keys, const tbgb_columns* cols, const uint64_t* mask, int64_t n,
+                       long long groups, int64_t* out_keys, const tbgb_moments* out, int64_t* d_n_groups,
+                       void* stream) {
+  const tbgb::RadixPlan R = tbgb::radix_plan(*cols, n, ctx->num_sms);
+  const tbgb::TablePlan P = tbgb::table_plan(true, false, 0, groups, ctx->num_sms, 1, false);
+  const size_t fb_bytes = align256(P.table_bytes) + align256(tbgb::table_finalize_scratch_bytes(P));
+  const size_t t2_region = R.t2_bytes > fb_bytes ? R.t2_bytes : fb_bytes;
+  tbgb_status st = ensure_ws(ctx, tbgb::radix_t2_offset(R) + t2_region);
+  if (st != TBGB_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaEvent_t e0, e1;
+  st = profile_events(ctx, &e0, &e1);
+  if (st != TBGB_OK) return st;
+  tbgb::RadixArgs ra{};
+  ra.keys = keys;
+  ra.cols = *cols;
+  ra.mask = mask;
+  ra.n = n;
+  ra.max_groups = groups;
+  ra.out_keys = out_keys;
+  ra.out = *out;
+  ra.d_n_groups = d_n_groups;
+  ra.err = ctx->err;
+  uint32_t* gate = nullptr;
+  cudaError_t e = tbgb::radix_groupby(R, ra, ctx->ws, &gate, s, &ctx->launches, e0, e1);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "radix groupby launch", e);
+  char* w = static_cast<char*>(ctx->ws) + tbgb::radix_t2_offset(R);
+  unsigned long long* T = reinterpret_cast<unsigned long long*>(w);
+  unsigned long long* fin = reinterpret_cast<unsigned long long*>(w + align256(P.table_bytes));
+  e = tbgb::table_init(P, T, s, &ctx->launches, gate);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback table init", e);
+  tbgb::TableArgs a{};
+  a.keys = keys;
+  a.cols = *cols;
+  a.mask = mask;
+  a.n = n;
+  a.slots = P.slots;
+  a.ngroups = tbgb::table_counter(P, T);
+  a.max_groups = groups;
+  a.err = ctx->err;
+  a.table = T;
+  a.gate = gate;
+  e = tbgb::table_accumulate(P, a, s, &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback table launch", e);
+  e = tbgb::table_finalize_hash(P, T, groups, out_keys, out, d_n_groups, fin, s, &ctx->launches, gate);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback table finalize", e);
+  return TBGB_OK;
+}
+
+// The column set of a plain f64 value column (no filter, no expression).
 tbgb_columns plain_f64(const double* vals) {
   tbgb_columns c{};
   c.a = vals;
@@ -205,8 +261,6 @@ int hash_buckets(tbgb_ctx* ctx, bool full, long long groups) {
   return b < 2 ? 2 : b;
 }
 
-size_t align256(size_t x) { return (x + 255) / 256 * 256; }
-
 // Global-table groupby: dense keys (hash == false, `groups` = n_groups) or int64
 // keys (`groups` = max_groups).  int64 keys with a large table are first routed to
 // sub-tables by their high hash bits (a stable partition that also applies the filter
@@ -226,6 +280,10 @@ tbgb_status table_common(tbgb_ctx* ctx, bool hash, const void* keys, const tbgb_
   const bool full = state_out != nullptr || wants_full(out);
   DeviceGuard dg(ctx->device);
   if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  if (hash && !full && groups <= tbgb::kRadixMaxGroups &&
+      (ctx->table_mode == 5 || (ctx->table_mode == 0 && tbgb::radix_eligible(*cols, out, n, groups))))
+    return radix_hash(ctx, static_cast<const int64_t*>(keys), cols, mask, n, groups, out_keys, out, d_n_groups,
+                      stream);
   const int B = hash ? hash_buckets(ctx, full, groups) : 1;
   const int mode = ctx->table_mode == 3 ? 0 : ctx->table_mode;
   const bool m34 = full && ((state_out != nullptr && state_m34) || (out && (out->m3 || out->m4)));
@@ -481,7 +539,7 @@ size_t tbgb_workspace_bytes(const tbgb_ctx* ctx, int64_t n, int32_t n_groups) {
 
 tbgb_status tbgb_set_table_mode(tbgb_ctx* ctx, int mode) {
   if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
-  if (mode < 0 || mode > 4) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "table mode must be 0, 1, 2, 3 or 4");
+  if (mode < 0 || mode > 5) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "table mode must be 0 to 5");
   ctx->table_mode = mode;
   return TBGB_OK;
 }

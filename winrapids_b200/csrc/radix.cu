@@ -1,0 +1,817 @@
+// radix.cu -- int64-key groupby (count, sum, mean) by radix partitioning.
+//
+// A single open-addressing table over hundreds of millions of keys lives far outside L2 and
+// the TLB's reach: every row then pays a random DRAM sector and a TLB miss.  Here the rows are
+// instead moved twice, in streaming passes, until each bucket's keys fit one CTA's shared
+// memory:
+//   pass 1  rows -> 256 buckets by the top 8 bits of h = fmix64(key)   (mask, predicate and
+//           expression applied here; rows that fail them are dropped)
+//   pass 2  each of those -> 256 buckets by the next 8 bits            (65,536 buckets)
+//   pass 3  one CTA per bucket: a shared-memory table of 8,192 slots keyed by the low 48 bits of
+//           h (the top 16 are the bucket) takes the bucket's rows, then writes its groups.
+// fmix64 (MurmurHash3's finaliser) is a bijection, so the rows carry h instead of the key and
+// pass 3 recovers each group's key by inverting it.  A row is (h, value): 12 bytes for an f32
+// column without an expression, 16 otherwise.
+//
+// Each pass-1/2 CTA stages a tile of 4,096 rows: per row a shared-memory atomic gives its rank
+// among the tile's rows of the same bucket, one global atomic per (tile, bucket) claims a run in
+// the bucket's region, the rows are reordered by bucket in shared memory and then written as
+// runs (consecutive threads, consecutive addresses).  Buckets have fixed regions with slack
+// over an even share (tens of standard deviations for hashed keys); a bucket that still
+// overflows -- heavily skewed or adversarial keys -- or a final bucket with more distinct keys
+// than its table takes sets the fallback word, the remaining passes stop early, and the caller
+// recomputes the result with the global-table strategy gated on that word.
+//
+// No counterpart in the reference, which groups int64 keys on the host (GroupIndex::build,
+// crates/tambear/src/group_index.rs:117-204, i32 codes only); the outputs follow the same
+// semantics as the global table: count = non-NaN rows, sum = sum of finite values, mean =
+// sum / count (NaN when count is 0), and a key whose rows are all NaN is a group of count 0.
+#include <cstdint>
+#include <type_traits>
+
+#include "common.cuh"
+#include "radix.cuh"
+#include "rowops.cuh"
+
+namespace tbgb {
+
+namespace {
+
+constexpr int RX_NT = 512;                     // threads per scatter CTA
+constexpr int RX_TILE = 4096;                  // rows per scatter tile
+constexpr int RX_PER = RX_TILE / RX_NT;        // rows per thread per tile
+constexpr int AGG_NT = 1024;                   // threads per aggregation CTA
+constexpr int AGG_SLOTS = 8192;                // shared-memory table slots per bucket
+constexpr int AGG_MAX_PROBE = 512;             // probes before a row gives up (fallback)
+constexpr int AGG_UNROLL = 4;
+constexpr unsigned long long kLow48 = (1ull << 48) - 1;
+constexpr unsigned long long kFree = ~0ull;    // never a 48-bit value
+constexpr unsigned int kPrefetchChunk = 32768;
+
+static_assert(RX_TILE <= 65536, "ranks are packed in 16 bits");
+
+__host__ __device__ constexpr unsigned long long inverse_odd(unsigned long long c) {
+  unsigned long long x = c;  // Newton's iteration for the inverse mod 2^64 (3 correct bits to start)
+  for (int i = 0; i < 6; ++i) x *= 2ull - c * x;
+  return x;
+}
+static_assert(0xff51afd7ed558ccdull * inverse_odd(0xff51afd7ed558ccdull) == 1ull, "inverse");
+static_assert(0xc4ceb9fe1a85ec53ull * inverse_odd(0xc4ceb9fe1a85ec53ull) == 1ull, "inverse");
+
+// fmix64's inverse: each x ^= x >> 33 undoes itself (33 >= 64 / 2), each multiply by an odd
+// constant is undone by its inverse mod 2^64.
+__device__ __forceinline__ unsigned long long unfmix64(unsigned long long h) {
+  constexpr unsigned long long i2 = inverse_odd(0xc4ceb9fe1a85ec53ull);
+  constexpr unsigned long long i1 = inverse_odd(0xff51afd7ed558ccdull);
+  h ^= h >> 33;
+  h *= i2;
+  h ^= h >> 33;
+  h *= i1;
+  h ^= h >> 33;
+  return h;
+}
+
+constexpr int kMaxSeg = 4096;  // second-pass segments: (sender, digit) pairs of a routed groupby
+
+struct Aux {  // device bookkeeping inside the workspace
+  unsigned long long cur1[kRadixDigits];
+  unsigned long long cur2[kRadixBuckets];
+  unsigned long long route_base[kRadixDigits];  // exact placement of a routing pass
+  unsigned long long route_cap[kRadixDigits];
+  long long seg_base[kMaxSeg];
+  long long seg_count[kMaxSeg];
+  int seg_digit[kMaxSeg];                       // destination digit, relative to the first owned one
+  long long seg_tiles[kMaxSeg + 1];
+  unsigned long long n_groups;
+  uint32_t fallback;
+  uint32_t pad[13];
+};
+
+struct RxScatter {
+  // pass 1: the caller's rows
+  const int64_t* keys;
+  tbgb_columns cols;
+  const uint64_t* mask;
+  long long n;
+  // pass 2: segments of the first pass's buffer
+  const unsigned long long* src_h;
+  const void* src_v;
+  const long long* seg_base;
+  const long long* seg_count;
+  const int* seg_digit;
+  const long long* seg_tiles;  // exclusive prefix of tiles per segment, n_seg + 1 entries
+  int n_seg;
+  int shift;                   // digit = (h >> shift) & 255
+  // destination
+  unsigned long long* dst_h;
+  void* dst_v;
+  unsigned long long* cursor;  // rows claimed per destination bucket
+  unsigned long long cap;      // rows per destination bucket region (when out_base is NULL)
+  const unsigned long long* out_base;  // nullable: first row of each destination bucket
+  const unsigned long long* out_cap;   // with out_base: rows of each destination bucket
+  uint32_t* fallback;
+};
+
+template <bool VF32>
+constexpr size_t scatter_smem() {
+  return static_cast<size_t>(RX_TILE) * (8 + (VF32 ? 4 : 8) + 1);
+}
+
+// SRC: 0 = the caller's key and value columns as they are, 1 = the caller's columns with mask /
+// predicate / expression, 2 = segments of a partitioned buffer.  VF32: rows carry an f32 value.
+// F32IN: the caller's columns are f32.
+template <int SRC, bool VF32, bool F32IN>
+__global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
+  using VT = typename std::conditional<VF32, float, double>::type;
+  extern __shared__ __align__(16) unsigned char rx_sm[];
+  unsigned long long* sh_h = reinterpret_cast<unsigned long long*>(rx_sm);
+  VT* sh_v = reinterpret_cast<VT*>(sh_h + RX_TILE);
+  unsigned char* sh_d = reinterpret_cast<unsigned char*>(sh_v + RX_TILE);
+  __shared__ unsigned int hist[kRadixDigits];
+  __shared__ unsigned int lstart[kRadixDigits];
+  __shared__ unsigned int wlim[kRadixDigits];
+  __shared__ unsigned long long gdst[kRadixDigits];
+  __shared__ unsigned int wsum[kRadixDigits / 32];
+  __shared__ unsigned int tile_total;
+
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if constexpr (SRC == 2) {
+    if (*reinterpret_cast<volatile const uint32_t*>(a.fallback)) return;  // pass 1 overflowed
+  }
+  if (tid < kRadixDigits) hist[tid] = 0;
+  const long long ntiles = SRC == 2 ? a.seg_tiles[a.n_seg] : (a.n + RX_TILE - 1) / RX_TILE;
+  const VT* src_v = static_cast<const VT*>(a.src_v);
+  VT* dst_v = static_cast<VT*>(a.dst_v);
+  int seg = 0;
+  __syncthreads();
+  for (long long t = blockIdx.x; t < ntiles; t += gridDim.x) {
+    long long row0, rows;
+    unsigned long long obase = 0;  // first destination bucket of this tile's source segment
+    if constexpr (SRC == 2) {
+      while (__ldg(a.seg_tiles + seg + 1) <= t) ++seg;
+      const long long tin = t - __ldg(a.seg_tiles + seg);
+      row0 = __ldg(a.seg_base + seg) + tin * RX_TILE;
+      rows = __ldg(a.seg_count + seg) - tin * RX_TILE;
+      obase = static_cast<unsigned long long>(__ldg(a.seg_digit + seg)) * kRadixDigits;
+    } else {
+      row0 = t * RX_TILE;
+      rows = a.n - row0;
+    }
+    if (rows > RX_TILE) rows = RX_TILE;
+
+    // ---- phase A: load, hash, rank inside the tile
+    unsigned long long hv[RX_PER];
+    VT vv[RX_PER];
+    unsigned int rk[RX_PER];  // bit 31 valid, bits 16-23 digit, bits 0-15 rank
+    if constexpr (SRC == 2) {
+#pragma unroll
+      for (int j = 0; j < RX_PER; ++j) {
+        const int li = j * RX_NT + tid;
+        if (li < rows) {
+          hv[j] = __ldcs(a.src_h + row0 + li);
+          vv[j] = __ldcs(src_v + row0 + li);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < RX_PER; ++j) {
+        const int li = j * RX_NT + tid;
+        rk[j] = 0;
+        if (li < rows) {
+          const unsigned d = static_cast<unsigned>(hv[j] >> a.shift) & 255u;
+          rk[j] = 0x80000000u | (d << 16) | atomicAdd(hist + d, 1u);
+        }
+      }
+    } else if constexpr (SRC == 0) {
+#pragma unroll
+      for (int j = 0; j < RX_PER; ++j) {
+        const int li = j * RX_NT + tid;
+        if (li < rows) {
+          hv[j] = static_cast<unsigned long long>(__ldcs(a.keys + row0 + li));
+          vv[j] = __ldcs(static_cast<const VT*>(a.cols.a) + row0 + li);
+        }
+      }
+#pragma unroll
+      for (int j = 0; j < RX_PER; ++j) {
+        const int li = j * RX_NT + tid;
+        rk[j] = 0;
+        if (li < rows) {
+          hv[j] = fmix64(hv[j]);
+          const unsigned d = static_cast<unsigned>(hv[j] >> 56);
+          rk[j] = 0x80000000u | (d << 16) | atomicAdd(hist + d, 1u);
+        }
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < RX_PER; ++j) {
+        const int li = j * RX_NT + tid;
+        rk[j] = 0;
+        if (li >= rows) continue;
+        const long long row = row0 + li;
+        if (a.mask && !((__ldg(a.mask + (row >> 6)) >> (row & 63)) & 1ull)) continue;
+        const double av = load_val<F32IN>(a.cols.a, row);
+        if (!eval_pred(a.cols.pred, av, a.cols.threshold)) continue;
+        if constexpr (VF32) {
+          vv[j] = static_cast<float>(av);  // an f32 column without expression: exact
+        } else {
+          const int expr = a.cols.expr;
+          const double bv = expr != TBGB_EXPR_A ? load_val<F32IN>(a.cols.b, row) : 0.0;
+          const double cv = expr == TBGB_EXPR_MUL_ADD ? load_val<F32IN>(a.cols.c, row) : 0.0;
+          vv[j] = eval_expr(expr, av, bv, cv);
+        }
+        hv[j] = fmix64(static_cast<unsigned long long>(__ldcs(a.keys + row)));
+        const unsigned d = static_cast<unsigned>(hv[j] >> 56);
+        rk[j] = 0x80000000u | (d << 16) | atomicAdd(hist + d, 1u);
+      }
+    }
+    __syncthreads();
+
+    // ---- phase B: claim a run per bucket, offsets of the buckets inside the tile
+    unsigned int c = 0, inc = 0;
+    if (tid < kRadixDigits) {
+      c = hist[tid];
+      hist[tid] = 0;
+      unsigned long long g = 0;
+      unsigned int w = 0;
+      if (c) {
+        const unsigned long long b = obase + tid;
+        const unsigned long long pos = atomicAdd(a.cursor + b, static_cast<unsigned long long>(c));
+        const unsigned long long cap = a.out_base ? a.out_cap[b] : a.cap;
+        if (pos < cap) w = cap - pos < c ? static_cast<unsigned int>(cap - pos) : c;
+        if (w < c) atomicOr(a.fallback, 1u);
+        g = (a.out_base ? a.out_base[b] : b * a.cap) + pos;
+      }
+      gdst[tid] = g;
+      wlim[tid] = w;
+      inc = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+      }
+      if (lane == 31) wsum[warp] = inc;
+    }
+    __syncthreads();
+    if (tid < kRadixDigits) {
+      unsigned int before = inc - c;
+      for (int w = 0; w < warp; ++w) before += wsum[w];
+      lstart[tid] = before;
+      if (tid == kRadixDigits - 1) tile_total = before + c;
+    }
+    __syncthreads();
+
+    // ---- phase C: reorder the tile by bucket in shared memory
+#pragma unroll
+    for (int j = 0; j < RX_PER; ++j) {
+      if (rk[j] >> 31) {
+        const unsigned d = (rk[j] >> 16) & 255u;
+        const unsigned p = lstart[d] + (rk[j] & 0xFFFFu);
+        sh_h[p] = hv[j];
+        sh_v[p] = vv[j];
+        sh_d[p] = static_cast<unsigned char>(d);
+      }
+    }
+    __syncthreads();
+
+    // ---- phase D: write each bucket's run (consecutive threads, consecutive addresses)
+    const unsigned int tot = tile_total;
+    for (unsigned int p = tid; p < tot; p += RX_NT) {
+      const unsigned d = sh_d[p];
+      const unsigned i = p - lstart[d];
+      if (i < wlim[d]) {
+        const unsigned long long dst = gdst[d] + i;
+        a.dst_h[dst] = sh_h[p];
+        dst_v[dst] = sh_v[p];
+      }
+    }
+    // the next tile's first barrier orders these reads before lstart / gdst / sh_* change
+  }
+}
+
+// Segments of pass 2 (one per first-pass bucket): base row, rows written, tiles.
+__global__ void rx_segments_kernel(Aux* x, unsigned long long cap1) {
+  __shared__ long long tiles[kRadixDigits];
+  const int d = threadIdx.x;
+  unsigned long long c = x->cur1[d];
+  if (c > cap1) c = cap1;
+  x->seg_base[d] = static_cast<long long>(d * cap1);
+  x->seg_count[d] = static_cast<long long>(c);
+  x->seg_digit[d] = d;
+  tiles[d] = static_cast<long long>((c + RX_TILE - 1) / RX_TILE);
+  __syncthreads();
+  if (d == 0) {
+    long long s = 0;
+    for (int i = 0; i < kRadixDigits; ++i) {
+      x->seg_tiles[i] = s;
+      s += tiles[i];
+    }
+    x->seg_tiles[kRadixDigits] = s;
+  }
+}
+
+// Rows per top digit of a routing pass (the rows that pass mask and predicate).
+template <bool PLAIN, bool F32IN>
+__global__ void __launch_bounds__(RX_NT) rx_count_kernel(RxScatter a) {
+  __shared__ unsigned int hist[kRadixDigits];
+  const int tid = threadIdx.x;
+  if (tid < kRadixDigits) hist[tid] = 0;
+  __syncthreads();
+  const long long stride = static_cast<long long>(gridDim.x) * RX_NT;
+  for (long long row = static_cast<long long>(blockIdx.x) * RX_NT + tid; row < a.n; row += stride) {
+    if constexpr (!PLAIN) {
+      if (a.mask && !((__ldg(a.mask + (row >> 6)) >> (row & 63)) & 1ull)) continue;
+      if (!eval_pred(a.cols.pred, load_val<F32IN>(a.cols.a, row), a.cols.threshold)) continue;
+    }
+    const unsigned long long h = fmix64(static_cast<unsigned long long>(__ldcs(a.keys + row)));
+    atomicAdd(hist + (h >> 56), 1u);
+  }
+  __syncthreads();
+  if (tid < kRadixDigits && hist[tid]) atomicAdd(a.cursor + tid, static_cast<unsigned long long>(hist[tid]));
+}
+
+// Exact placement of a routing pass: digit d's rows start after those of the digits below it.
+__global__ void rx_route_bases_kernel(Aux* x, int64_t* digit_counts) {
+  if (threadIdx.x == 0) {
+    unsigned long long s = 0;
+    for (int d = 0; d < kRadixDigits; ++d) {
+      const unsigned long long c = x->cur1[d];
+      x->route_base[d] = s;
+      x->route_cap[d] = c;
+      digit_counts[d] = static_cast<int64_t>(c);
+      s += c;
+      x->cur1[d] = 0;  // the scatter claims from zero again
+    }
+  }
+}
+
+// Segments of a routed groupby: the received rows are n_senders blocks, each holding digits
+// [digit_lo, digit_lo + n_digits) in order; counts[sender * n_digits + j].
+__global__ void rx_routed_segments_kernel(Aux* x, const int64_t* counts, int n_seg, int n_digits) {
+  if (threadIdx.x == 0) {
+    long long base = 0, tiles = 0;
+    for (int i = 0; i < n_seg; ++i) {
+      const long long c = counts[i] > 0 ? counts[i] : 0;
+      x->seg_base[i] = base;
+      x->seg_count[i] = c;
+      x->seg_digit[i] = i % n_digits;
+      x->seg_tiles[i] = tiles;
+      base += c;
+      tiles += (c + RX_TILE - 1) / RX_TILE;
+    }
+    x->seg_tiles[n_seg] = tiles;
+  }
+}
+
+// Group keys of a fallback that grouped the hashes themselves: each output key is a hash; turn
+// it back into the key (runs only when the fallback ran).
+__global__ void rx_unhash_kernel(int64_t* keys, const int64_t* d_n_groups, long long max_groups,
+                                 const uint32_t* gate) {
+  if (*gate == 0u) return;
+  long long g = *d_n_groups;
+  if (g > max_groups) g = max_groups;
+  const long long stride = static_cast<long long>(gridDim.x) * blockDim.x;
+  for (long long i = static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x; i < g; i += stride)
+    keys[i] = static_cast<int64_t>(unfmix64(static_cast<unsigned long long>(keys[i])));
+}
+
+struct RxAgg {
+  const unsigned long long* src_h;
+  const void* src_v;
+  const unsigned long long* cursor;
+  int n_buckets;               // buckets of this call (all 65,536, or an owner's share)
+  int bucket0;                 // bucket index of local bucket 0 (the top 16 bits of its hashes)
+  unsigned long long cap;
+  long long max_groups;
+  int64_t* out_keys;
+  tbgb_moments out;
+  unsigned long long* n_groups;
+  uint32_t* fallback;
+};
+
+constexpr size_t agg_smem() { return static_cast<size_t>(AGG_SLOTS) * (8 + 8 + 4); }
+
+template <bool VF32>
+__global__ void __launch_bounds__(AGG_NT, 1) rx_agg_kernel(RxAgg a) {
+  using VT = typename std::conditional<VF32, float, double>::type;
+  extern __shared__ __align__(16) unsigned char ag_sm[];
+  unsigned long long* tk = reinterpret_cast<unsigned long long*>(ag_sm);
+  double* ts = reinterpret_cast<double*>(tk + AGG_SLOTS);
+  unsigned int* tc = reinterpret_cast<unsigned int*>(ts + AGG_SLOTS);
+  __shared__ unsigned int wcount[AGG_NT / 32];
+  __shared__ unsigned long long gbase;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  volatile const uint32_t* fb = a.fallback;
+  if (*fb) return;  // an earlier pass overflowed
+  const VT* src_v = static_cast<const VT*>(a.src_v);
+  for (int b = blockIdx.x; b < a.n_buckets; b += gridDim.x) {
+    const unsigned long long base = static_cast<unsigned long long>(b) * a.cap;
+    unsigned long long rows = a.cursor[b];
+    if (rows > a.cap) rows = a.cap;
+    // the next bucket of this CTA streams into L2 while this one is reduced
+    const int nb = b + gridDim.x;
+    if (nb < a.n_buckets && warp == 0) {
+      unsigned long long nrows = a.cursor[nb];
+      if (nrows > a.cap) nrows = a.cap;
+      const unsigned long long nbase = static_cast<unsigned long long>(nb) * a.cap;
+      const unsigned long long hb = (nrows * 8 + 15) & ~15ull, vb = (nrows * sizeof(VT) + 15) & ~15ull;
+      const char* hp = reinterpret_cast<const char*>(a.src_h + nbase);
+      const char* vp = reinterpret_cast<const char*>(src_v + nbase);
+      for (unsigned long long o = static_cast<unsigned long long>(lane) * kPrefetchChunk; o < hb;
+           o += 32ull * kPrefetchChunk)
+        bulk_prefetch_l2(hp + o, static_cast<uint32_t>(hb - o < kPrefetchChunk ? hb - o : kPrefetchChunk));
+      for (unsigned long long o = static_cast<unsigned long long>(lane) * kPrefetchChunk; o < vb;
+           o += 32ull * kPrefetchChunk)
+        bulk_prefetch_l2(vp + o, static_cast<uint32_t>(vb - o < kPrefetchChunk ? vb - o : kPrefetchChunk));
+    }
+    for (int i = tid; i < AGG_SLOTS; i += AGG_NT) {
+      tk[i] = kFree;
+      ts[i] = 0.0;
+      tc[i] = 0u;
+    }
+    __syncthreads();
+    for (unsigned long long p0 = 0; p0 < rows; p0 += static_cast<unsigned long long>(AGG_NT) * AGG_UNROLL) {
+      unsigned long long hv[AGG_UNROLL];
+      double vv[AGG_UNROLL];
+#pragma unroll
+      for (int u = 0; u < AGG_UNROLL; ++u) {
+        const unsigned long long p = p0 + static_cast<unsigned long long>(u) * AGG_NT + tid;
+        if (p < rows) {
+          hv[u] = a.src_h[base + p];
+          vv[u] = static_cast<double>(src_v[base + p]);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < AGG_UNROLL; ++u) {
+        const unsigned long long p = p0 + static_cast<unsigned long long>(u) * AGG_NT + tid;
+        if (p >= rows) continue;
+        const unsigned long long low = hv[u] & kLow48;
+        unsigned int slot = static_cast<unsigned int>(hv[u]) & (AGG_SLOTS - 1);
+        bool found = false;
+        for (int probe = 0; probe < AGG_MAX_PROBE; ++probe) {
+          const unsigned long long k = tk[slot];
+          if (k == low) {
+            found = true;
+            break;
+          }
+          if (k == kFree) {
+            const unsigned long long prev = atomicCAS(tk + slot, kFree, low);
+            if (prev == kFree || prev == low) {
+              found = true;
+              break;
+            }
+          }
+          slot = (slot + 1) & (AGG_SLOTS - 1);
+        }
+        if (!found) {
+          atomicOr(a.fallback, 2u);  // more distinct keys than the table takes: recompute elsewhere
+          continue;
+        }
+        const double v = vv[u];
+        if (!is_nan(v)) atomicAdd(tc + slot, 1u);
+        if (is_finite(v)) atomicAdd(ts + slot, v);
+      }
+    }
+    __syncthreads();
+    // the occupied slots, compacted in slot order: warp w takes slots k * AGG_NT + w * 32 + lane
+    unsigned int mine = 0;
+    for (int k = 0; k < AGG_SLOTS / AGG_NT; ++k)
+      mine += __popc(__ballot_sync(0xffffffffu, tk[k * AGG_NT + tid] != kFree));
+    if (lane == 0) wcount[warp] = mine;
+    __syncthreads();
+    if (warp == 0) {
+      const unsigned int cnt = wcount[lane];
+      unsigned int incl = cnt;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += y;
+      }
+      wcount[lane] = incl - cnt;
+      if (lane == 31) gbase = atomicAdd(a.n_groups, static_cast<unsigned long long>(incl));
+    }
+    __syncthreads();
+    unsigned long long pos = gbase + wcount[warp];
+    const unsigned long long top = static_cast<unsigned long long>(b + a.bucket0) << 48;
+    for (int k = 0; k < AGG_SLOTS / AGG_NT; ++k) {
+      const int i = k * AGG_NT + tid;
+      const unsigned long long key48 = tk[i];
+      const bool occ = key48 != kFree;
+      const unsigned bal = __ballot_sync(0xffffffffu, occ);
+      if (occ) {
+        const unsigned long long j = pos + __popc(bal & ((1u << lane) - 1u));
+        if (j < static_cast<unsigned long long>(a.max_groups)) {
+          const double cnt = static_cast<double>(tc[i]);
+          const double sum = ts[i];
+          a.out_keys[j] = static_cast<int64_t>(unfmix64(top | key48));
+          if (a.out.count) a.out.count[j] = cnt;
+          if (a.out.sum) a.out.sum[j] = sum;
+          if (a.out.mean) a.out.mean[j] = cnt > 0.0 ? sum / cnt : qnan();
+        }
+      }
+      pos += __popc(bal);
+    }
+    __syncthreads();  // the table is cleared for the next bucket only after every thread wrote
+  }
+}
+
+__global__ void rx_finish_kernel(const Aux* x, long long max_groups, int64_t* d_n_groups, uint32_t* err) {
+  if (x->fallback) return;  // the fallback strategy writes the group count
+  unsigned long long g = x->n_groups;
+  if (g > static_cast<unsigned long long>(max_groups)) {
+    atomicOr(err, KERR_TABLE_FULL);
+    g = static_cast<unsigned long long>(max_groups);
+  }
+  *d_n_groups = static_cast<int64_t>(g);
+}
+
+size_t align256(size_t x) { return (x + 255) / 256 * 256; }
+
+unsigned long long round16(unsigned long long x) { return (x + 15) / 16 * 16; }
+
+template <int SRC, bool VF32, bool F32IN>
+cudaError_t launch_scatter(const RxScatter& s, int grid, cudaStream_t st) {
+  auto k = rx_scatter_kernel<SRC, VF32, F32IN>;
+  constexpr size_t smem = scatter_smem<VF32>();
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  k<<<grid, RX_NT, smem, st>>>(s);
+  return cudaGetLastError();
+}
+
+template <bool VF32>
+cudaError_t launch_agg(const RxAgg& g, int grid, cudaStream_t st) {
+  auto k = rx_agg_kernel<VF32>;
+  constexpr size_t smem = agg_smem();
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  k<<<grid, AGG_NT, smem, st>>>(g);
+  return cudaGetLastError();
+}
+
+int scatter_blocks_per_sm(bool vf32) {
+  static int cached[2] = {0, 0};
+  int& c = cached[vf32 ? 1 : 0];
+  if (c == 0) {
+    int v = 0;
+    const size_t smem = vf32 ? scatter_smem<true>() : scatter_smem<false>();
+    cudaError_t e = vf32 ? cudaFuncSetAttribute(rx_scatter_kernel<2, true, true>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))
+                         : cudaFuncSetAttribute(rx_scatter_kernel<2, false, false>,
+                                                cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e == cudaSuccess) {
+      e = vf32 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, rx_scatter_kernel<2, true, true>, RX_NT, smem)
+               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, rx_scatter_kernel<2, false, false>, RX_NT, smem);
+    }
+    c = (e == cudaSuccess && v > 0) ? v : 1;
+  }
+  return c;
+}
+
+}  // namespace
+
+bool radix_eligible(const tbgb_columns& cols, const tbgb_moments* out, long long n, long long max_groups) {
+  (void)cols;
+  if (!out || out->min || out->max || out->m2 || out->var_pop || out->var_samp || out->m3 || out->m4) return false;
+  return n >= (1ll << 24) && max_groups >= (1ll << 22) && max_groups <= kRadixMaxGroups;
+}
+
+RadixPlan radix_plan(const tbgb_columns& cols, long long n, int num_sms) {
+  RadixPlan P{};
+  P.vf32 = cols.dtype == TBGB_F32 && cols.expr == TBGB_EXPR_A;
+  const unsigned long long rows = static_cast<unsigned long long>(n > 0 ? n : 0);
+  const unsigned long long e1 = rows / kRadixDigits, e2 = rows / kRadixBuckets;
+  P.cap1 = round16(e1 + e1 / 16 + 4096);
+  P.cap2 = round16(e2 + e2 / 16 + 512);
+  const size_t row_bytes = 8 + (P.vf32 ? 4 : 8);
+  P.t1_bytes = align256(static_cast<size_t>(P.cap1) * kRadixDigits * 8) +
+               align256(static_cast<size_t>(P.cap1) * kRadixDigits * (row_bytes - 8));
+  P.t2_bytes = align256(static_cast<size_t>(P.cap2) * kRadixBuckets * 8) +
+               align256(static_cast<size_t>(P.cap2) * kRadixBuckets * (row_bytes - 8));
+  P.aux_bytes = align256(sizeof(Aux));
+  P.grid_scatter = num_sms * scatter_blocks_per_sm(P.vf32);
+  P.grid_agg = num_sms;
+  return P;
+}
+
+size_t radix_t2_offset(const RadixPlan& P) { return P.aux_bytes + P.t1_bytes; }
+
+cudaError_t radix_groupby(const RadixPlan& P, const RadixArgs& a, void* ws, uint32_t** fallback, cudaStream_t s,
+                          uint64_t* launches, cudaEvent_t ev0, cudaEvent_t ev1) {
+  char* w = static_cast<char*>(ws);
+  Aux* x = reinterpret_cast<Aux*>(w);
+  const size_t vb = P.vf32 ? 4 : 8;
+  unsigned long long* t1h = reinterpret_cast<unsigned long long*>(w + P.aux_bytes);
+  void* t1v = w + P.aux_bytes + align256(static_cast<size_t>(P.cap1) * kRadixDigits * 8);
+  unsigned long long* t2h = reinterpret_cast<unsigned long long*>(w + radix_t2_offset(P));
+  void* t2v = w + radix_t2_offset(P) + align256(static_cast<size_t>(P.cap2) * kRadixBuckets * 8);
+  (void)vb;
+  *fallback = &x->fallback;
+  cudaError_t e = cudaMemsetAsync(x, 0, sizeof(Aux), s);
+  if (e != cudaSuccess) return e;
+  if (ev0) cudaEventRecord(ev0, s);
+
+  RxScatter p1{};
+  p1.keys = a.keys;
+  p1.cols = a.cols;
+  p1.mask = a.mask;
+  p1.n = a.n;
+  p1.dst_h = t1h;
+  p1.dst_v = t1v;
+  p1.cursor = x->cur1;
+  p1.cap = P.cap1;
+  p1.fallback = &x->fallback;
+  const bool plain = a.mask == nullptr && a.cols.pred == TBGB_PRED_NONE && a.cols.expr == TBGB_EXPR_A;
+  const bool f32in = a.cols.dtype == TBGB_F32;
+  if (a.n > 0) {
+    if (plain) e = f32in ? launch_scatter<0, true, true>(p1, P.grid_scatter, s)
+                         : launch_scatter<0, false, false>(p1, P.grid_scatter, s);
+    else if (P.vf32) e = launch_scatter<1, true, true>(p1, P.grid_scatter, s);
+    else e = f32in ? launch_scatter<1, false, true>(p1, P.grid_scatter, s)
+                   : launch_scatter<1, false, false>(p1, P.grid_scatter, s);
+    if (e != cudaSuccess) return e;
+    (*launches)++;
+  }
+  rx_segments_kernel<<<1, kRadixDigits, 0, s>>>(x, P.cap1);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  (*launches)++;
+
+  RxScatter p2{};
+  p2.src_h = t1h;
+  p2.src_v = t1v;
+  p2.seg_base = x->seg_base;
+  p2.seg_count = x->seg_count;
+  p2.seg_digit = x->seg_digit;
+  p2.seg_tiles = x->seg_tiles;
+  p2.n_seg = kRadixDigits;
+  p2.shift = 48;
+  p2.dst_h = t2h;
+  p2.dst_v = t2v;
+  p2.cursor = x->cur2;
+  p2.cap = P.cap2;
+  p2.fallback = &x->fallback;
+  if (a.n > 0) {
+    e = P.vf32 ? launch_scatter<2, true, true>(p2, P.grid_scatter, s)
+               : launch_scatter<2, false, false>(p2, P.grid_scatter, s);
+    if (e != cudaSuccess) return e;
+    (*launches)++;
+  }
+
+  RxAgg g{};
+  g.src_h = t2h;
+  g.src_v = t2v;
+  g.cursor = x->cur2;
+  g.n_buckets = kRadixBuckets;
+  g.bucket0 = 0;
+  g.cap = P.cap2;
+  g.max_groups = a.max_groups;
+  g.out_keys = a.out_keys;
+  g.out = a.out;
+  g.n_groups = &x->n_groups;
+  g.fallback = &x->fallback;
+  if (a.n > 0) {
+    e = P.vf32 ? launch_agg<true>(g, P.grid_agg, s) : launch_agg<false>(g, P.grid_agg, s);
+    if (e != cudaSuccess) return e;
+    (*launches)++;
+  }
+  if (ev1) cudaEventRecord(ev1, s);
+  rx_finish_kernel<<<1, 1, 0, s>>>(x, a.max_groups, a.d_n_groups, a.err);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) (*launches)++;
+  return e;
+}
+
+size_t radix_route_aux_bytes() { return align256(sizeof(Aux)); }
+
+bool radix_value_f32(const tbgb_columns& cols) { return cols.dtype == TBGB_F32 && cols.expr == TBGB_EXPR_A; }
+
+cudaError_t radix_route(const RadixArgs& a, unsigned long long* out_h, void* out_v, int64_t* digit_counts, void* aux,
+                        int num_sms, cudaStream_t s, uint64_t* launches) {
+  Aux* x = static_cast<Aux*>(aux);
+  cudaError_t e = cudaMemsetAsync(x, 0, sizeof(Aux), s);
+  if (e != cudaSuccess) return e;
+  RxScatter p1{};
+  p1.keys = a.keys;
+  p1.cols = a.cols;
+  p1.mask = a.mask;
+  p1.n = a.n;
+  p1.dst_h = out_h;
+  p1.dst_v = out_v;
+  p1.cursor = x->cur1;
+  p1.out_base = x->route_base;
+  p1.out_cap = x->route_cap;
+  p1.fallback = &x->fallback;
+  const bool plain = a.mask == nullptr && a.cols.pred == TBGB_PRED_NONE && a.cols.expr == TBGB_EXPR_A;
+  const bool f32in = a.cols.dtype == TBGB_F32;
+  const bool vf32 = radix_value_f32(a.cols);
+  if (a.n > 0) {
+    long long blocks = (a.n + RX_NT - 1) / RX_NT;
+    const long long cap = static_cast<long long>(num_sms) * 4;
+    if (blocks > cap) blocks = cap;
+    if (plain) rx_count_kernel<true, false><<<static_cast<unsigned>(blocks), RX_NT, 0, s>>>(p1);
+    else if (f32in) rx_count_kernel<false, true><<<static_cast<unsigned>(blocks), RX_NT, 0, s>>>(p1);
+    else rx_count_kernel<false, false><<<static_cast<unsigned>(blocks), RX_NT, 0, s>>>(p1);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return e;
+    (*launches)++;
+  }
+  rx_route_bases_kernel<<<1, 32, 0, s>>>(x, digit_counts);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  (*launches)++;
+  if (a.n > 0) {
+    const int grid = num_sms * scatter_blocks_per_sm(vf32);
+    if (plain) e = f32in ? launch_scatter<0, true, true>(p1, grid, s) : launch_scatter<0, false, false>(p1, grid, s);
+    else if (vf32) e = launch_scatter<1, true, true>(p1, grid, s);
+    else e = f32in ? launch_scatter<1, false, true>(p1, grid, s) : launch_scatter<1, false, false>(p1, grid, s);
+    if (e != cudaSuccess) return e;
+    (*launches)++;
+  }
+  return cudaSuccess;
+}
+
+RadixPlan radix_routed_plan(bool vf32, long long n_rows, int n_digits, int num_sms) {
+  RadixPlan P{};
+  P.vf32 = vf32;
+  const unsigned long long rows = static_cast<unsigned long long>(n_rows > 0 ? n_rows : 0);
+  const unsigned long long nb = static_cast<unsigned long long>(n_digits) * kRadixDigits;
+  const unsigned long long e2 = rows / nb;
+  P.cap1 = 0;
+  P.cap2 = round16(e2 + e2 / 16 + 512);
+  const size_t vb = vf32 ? 4 : 8;
+  P.t1_bytes = 0;
+  P.t2_bytes = align256(static_cast<size_t>(P.cap2) * nb * 8) + align256(static_cast<size_t>(P.cap2) * nb * vb);
+  P.aux_bytes = align256(sizeof(Aux));
+  P.grid_scatter = num_sms * scatter_blocks_per_sm(vf32);
+  P.grid_agg = num_sms;
+  return P;
+}
+
+cudaError_t radix_groupby_routed(const RadixPlan& P, const RoutedArgs& r, void* ws, uint32_t** fallback,
+                                 cudaStream_t s, uint64_t* launches, cudaEvent_t ev0, cudaEvent_t ev1) {
+  char* w = static_cast<char*>(ws);
+  Aux* x = reinterpret_cast<Aux*>(w);
+  const unsigned long long nb = static_cast<unsigned long long>(r.n_digits) * kRadixDigits;
+  unsigned long long* t2h = reinterpret_cast<unsigned long long*>(w + radix_t2_offset(P));
+  void* t2v = w + radix_t2_offset(P) + align256(static_cast<size_t>(P.cap2) * nb * 8);
+  *fallback = &x->fallback;
+  cudaError_t e = cudaMemsetAsync(x, 0, sizeof(Aux), s);
+  if (e != cudaSuccess) return e;
+  if (ev0) cudaEventRecord(ev0, s);
+  const int n_seg = r.n_senders * r.n_digits;
+  rx_routed_segments_kernel<<<1, 32, 0, s>>>(x, r.seg_counts, n_seg, r.n_digits);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  (*launches)++;
+  RxScatter p2{};
+  p2.src_h = r.hashes;
+  p2.src_v = r.vals;
+  p2.seg_base = x->seg_base;
+  p2.seg_count = x->seg_count;
+  p2.seg_digit = x->seg_digit;
+  p2.seg_tiles = x->seg_tiles;
+  p2.n_seg = n_seg;
+  p2.shift = 48;
+  p2.dst_h = t2h;
+  p2.dst_v = t2v;
+  p2.cursor = x->cur2;
+  p2.cap = P.cap2;
+  p2.fallback = &x->fallback;
+  if (r.n_rows > 0) {
+    e = P.vf32 ? launch_scatter<2, true, true>(p2, P.grid_scatter, s)
+               : launch_scatter<2, false, false>(p2, P.grid_scatter, s);
+    if (e != cudaSuccess) return e;
+    (*launches)++;
+  }
+  RxAgg g{};
+  g.src_h = t2h;
+  g.src_v = t2v;
+  g.cursor = x->cur2;
+  g.n_buckets = static_cast<int>(nb);
+  g.bucket0 = r.digit_lo * kRadixDigits;
+  g.cap = P.cap2;
+  g.max_groups = r.max_groups;
+  g.out_keys = r.out_keys;
+  g.out = r.out;
+  g.n_groups = &x->n_groups;
+  g.fallback = &x->fallback;
+  if (r.n_rows > 0) {
+    e = P.vf32 ? launch_agg<true>(g, P.grid_agg, s) : launch_agg<false>(g, P.grid_agg, s);
+    if (e != cudaSuccess) return e;
+    (*launches)++;
+  }
+  if (ev1) cudaEventRecord(ev1, s);
+  rx_finish_kernel<<<1, 1, 0, s>>>(x, r.max_groups, r.d_n_groups, r.err);
+  e = cudaGetLastError();
+  if (e == cudaSuccess) (*launches)++;
+  return e;
+}
+
+cudaError_t radix_unhash_keys(int64_t* keys, const int64_t* d_n_groups, long long max_groups, const uint32_t* gate,
+                              int num_sms, cudaStream_t s, uint64_t* launches) {
+  rx_unhash_kernel<<<num_sms * 4, 256, 0, s>>>(keys, d_n_groups, max_groups, gate);
+  cudaError_t e = cudaGetLastError();
+  if (e == cudaSuccess) (*launches)++;
+  return e;
+}
+
+}  // namespace tbgb

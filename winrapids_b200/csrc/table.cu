@@ -284,6 +284,7 @@ struct LocalTable : SlotArrays<FULL> {
 template <bool KEY64, bool F32, bool FULL, bool LOCAL>
 __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
   extern __shared__ __align__(16) unsigned char sm[];
+  if (a.gate && *a.gate == 0u) return;
   // The rows: the call's columns, or one part of a partition (plain f64 values, no mask)
   // whose row count and first row are read from device memory.
   long long n = a.n;
@@ -671,7 +672,8 @@ __global__ void __launch_bounds__(TNT, 1) range_table_kernel(TableArgs a, int R,
   }
 }
 
-__global__ void table_init_kernel(unsigned long long* T, unsigned long long nslots, int full) {
+__global__ void table_init_kernel(unsigned long long* T, unsigned long long nslots, int full, const uint32_t* gate) {
+  if (gate && *gate == 0u) return;
   const unsigned long long i0 = blockIdx.x * static_cast<unsigned long long>(blockDim.x) + threadIdx.x;
   const unsigned long long stride = static_cast<unsigned long long>(gridDim.x) * blockDim.x;
   if (full) {
@@ -752,7 +754,9 @@ __device__ __forceinline__ bool slot_occupied(const unsigned long long* T, unsig
 
 __global__ void __launch_bounds__(FIN_NT) table_occ_count_kernel(const unsigned long long* __restrict__ T,
                                                                  unsigned long long slots, unsigned long long total,
-                                                                 int full, unsigned long long* counts) {
+                                                                 int full, unsigned long long* counts,
+                                                                 const uint32_t* gate) {
+  if (gate && *gate == 0u) return;
   const int W = full ? FL_WORDS : SC_WORDS, ID = full ? FL_ID : SC_ID;
   const unsigned long long i0 = static_cast<unsigned long long>(blockIdx.x) * FIN_CHUNK;
   unsigned int c = 0;
@@ -774,7 +778,9 @@ __global__ void __launch_bounds__(FIN_NT) table_occ_count_kernel(const unsigned 
 // Exclusive scan of `len` counts in one block (in place); the total goes to *n_groups,
 // clipped to max_groups.
 __global__ void __launch_bounds__(1024) table_occ_scan_kernel(unsigned long long* counts, long long len,
-                                                             long long max_groups, int64_t* n_groups) {
+                                                             long long max_groups, int64_t* n_groups,
+                                                             const uint32_t* gate) {
+  if (gate && *gate == 0u) return;
   __shared__ unsigned long long warp_sums[32];
   __shared__ unsigned long long carry;
   if (threadIdx.x == 0) carry = 0;
@@ -813,7 +819,8 @@ __global__ void __launch_bounds__(FIN_NT) table_compact_kernel(const unsigned lo
                                                                unsigned long long slots, unsigned long long total,
                                                                int full, const unsigned long long* __restrict__ offsets,
                                                                long long max_groups, int64_t* out_keys,
-                                                               tbgb_moments out) {
+                                                               tbgb_moments out, const uint32_t* gate) {
+  if (gate && *gate == 0u) return;
   const int W = full ? FL_WORDS : SC_WORDS, ID = full ? FL_ID : SC_ID;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   __shared__ unsigned int wpre[FIN_NT / 32];
@@ -944,12 +951,13 @@ unsigned long long* table_counter(const TablePlan& P, unsigned long long* table)
   return table_bucket(P, table, P.buckets);
 }
 
-cudaError_t table_init(const TablePlan& P, unsigned long long* table, cudaStream_t s, uint64_t* launches) {
+cudaError_t table_init(const TablePlan& P, unsigned long long* table, cudaStream_t s, uint64_t* launches,
+                       const uint32_t* gate) {
   const unsigned long long nslots = static_cast<unsigned long long>(P.buckets) * (P.slots + (P.hash ? 1 : 0));
   unsigned long long blocks = (nslots + 255) / 256;
   if (blocks > 65536ull) blocks = 65536ull;
   if (blocks < 1) blocks = 1;
-  table_init_kernel<<<static_cast<unsigned int>(blocks), 256, 0, s>>>(table, nslots, P.full ? 1 : 0);
+  table_init_kernel<<<static_cast<unsigned int>(blocks), 256, 0, s>>>(table, nslots, P.full ? 1 : 0, gate);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) (*launches)++;
   return e;
@@ -1004,14 +1012,16 @@ size_t table_finalize_scratch_bytes(const TablePlan& P) {
 
 cudaError_t table_finalize_hash(const TablePlan& P, const unsigned long long* table, long long max_groups,
                                 int64_t* out_keys, const tbgb_moments* out, int64_t* d_n_groups,
-                                unsigned long long* scratch, cudaStream_t s, uint64_t* launches) {
+                                unsigned long long* scratch, cudaStream_t s, uint64_t* launches,
+                                const uint32_t* gate) {
   const unsigned long long total = static_cast<unsigned long long>(P.buckets) * (P.slots + 1);
   const unsigned long long nblk = (total + FIN_CHUNK - 1) / FIN_CHUNK;
   const int full = P.full ? 1 : 0;
-  table_occ_count_kernel<<<static_cast<unsigned int>(nblk), FIN_NT, 0, s>>>(table, P.slots, total, full, scratch);
-  table_occ_scan_kernel<<<1, 1024, 0, s>>>(scratch, static_cast<long long>(nblk), max_groups, d_n_groups);
+  table_occ_count_kernel<<<static_cast<unsigned int>(nblk), FIN_NT, 0, s>>>(table, P.slots, total, full, scratch,
+                                                                            gate);
+  table_occ_scan_kernel<<<1, 1024, 0, s>>>(scratch, static_cast<long long>(nblk), max_groups, d_n_groups, gate);
   table_compact_kernel<<<static_cast<unsigned int>(nblk), FIN_NT, 0, s>>>(table, P.slots, total, full, scratch,
-                                                                          max_groups, out_keys, *out);
+                                                                          max_groups, out_keys, *out, gate);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) *launches += 3;
   return e;

@@ -40,6 +40,7 @@ struct TableArgs {
   uint32_t* err;
   int m34;               // FULL slots: also accumulate sum((v-K)^3), sum((v-K)^4)
   int extrema;           // FULL slots: also track min / max / first zero
+  const uint32_t* gate;  // when set, the kernels do nothing unless *gate != 0 (a fallback path)
 };
 
 struct TablePlan {
@@ -68,7 +69,9 @@ unsigned long long* table_bucket(const TablePlan& P, unsigned long long* table, 
 unsigned long long* table_counter(const TablePlan& P, unsigned long long* table);
 
 // Fills every slot with its empty pattern and clears the counter.
-cudaError_t table_init(const TablePlan& P, unsigned long long* table, cudaStream_t s, uint64_t* launches);
+// `gate` (nullable): run only when *gate != 0, read on the device.
+cudaError_t table_init(const TablePlan& P, unsigned long long* table, cudaStream_t s, uint64_t* launches,
+                       const uint32_t* gate = nullptr);
 // One pass over the rows.
 cudaError_t table_accumulate(const TablePlan& P, const TableArgs& a, cudaStream_t s, uint64_t* launches,
                              cudaEvent_t ev0 = nullptr, cudaEvent_t ev1 = nullptr);
@@ -80,6 +83,7 @@ cudaError_t table_finalize_dense(const TablePlan& P, const unsigned long long* t
 size_t table_finalize_scratch_bytes(const TablePlan& P);
 cudaError_t table_finalize_hash(const TablePlan& P, const unsigned long long* table, long long max_groups,
                                 int64_t* out_keys, const tbgb_moments* out, int64_t* d_n_groups,
-                                unsigned long long* scratch, cudaStream_t s, uint64_t* launches);
+                                unsigned long long* scratch, cudaStream_t s, uint64_t* launches,
+                                const uint32_t* gate = nullptr);
 
 }  // namespace tbgb
