@@ -5,12 +5,15 @@ Default workload (the low-cardinality sharded configuration): 1,000,000,000 rows
 int32 keys uniform in [0,256), f64 values ~U(-1,1); count/sum/min/max/mean/var per
 key.  Rows are split evenly over N GPUs (one process per GPU, launched by
 torch.distributed.run); each GPU reduces its shard to a mergeable per-group state
-table, the tables are all-gathered over NCCL and folded in rank order.
+table and stores it into every other GPU's exchange buffer over NVLink peer memory,
+and every GPU folds the tables in rank order (an NCCL all-gather when the peer
+mappings cannot be made).
 
 Other workloads (--workload): `pipeline` (100,000,000 rows, int64 Zipf(1.1) keys over
 1,000,000 ids, filter a>0, v=a*b+c, sum/count/mean/var), `highcard` (2,000,000,000
-rows, int64 keys over 2^28 random ids, f32 LogNormal values, sum/count/mean; rows
-hash-partitioned to their key's owner GPU over NCCL all-to-all), `stress`
+rows, int64 keys over 2^28 random ids, f32 LogNormal values, sum/count/mean: radix
+partitioning by key hash on one GPU; with N GPUs the first pass routes every row to the
+GPU owning its hash digit, one NCCL all-to-all, the owner runs the rest), `stress`
 (200,000,000 rows, 10,000 groups, 1e9 + N(0,1e-3) with NaN / +-inf), `cpu-ref`
 (1,000,000 rows, 1,000 groups), `stress-1k` and `bins` (1,000,000,000 f64 ticks in sorted
 contiguous bins of 1..831 rows, mean 416: count/sum/sum_sq/min/max/first/last/mean/variance/std
@@ -49,7 +52,7 @@ WORKLOADS = {
                     seed=0,
                     desc="low-cardinality sharded: 1,000,000,000 rows; int32 key uniform in [0,256); "
                          "f64 value ~U(-1,1); sum/count/min/max/mean/var; rows split evenly over the GPUs, "
-                         "partial tables all-gathered over NCCL and merged"),
+                         "per-GPU state tables exchanged over NVLink peer memory and merged in rank order"),
     "cpu-ref": dict(kind="dense", rows=1_000_000, groups=1000, values=("normal", 0.0, 1.0), nonfinite=None, seed=0,
                     desc="1,000,000 rows; int32 key uniform in [0,1000); f64 value ~N(0,1); "
                          "sum/count/min/max/mean/var; seed 0"),
@@ -75,8 +78,9 @@ WORKLOADS = {
                           "built once outside the timed region, as a .tb file header holds them"),
     "highcard": dict(kind="highcard", rows=2_000_000_000, ids=1 << 28, seed=0,
                      desc="high-cardinality sharded: 2,000,000,000 rows; int64 key uniform over 2^28 random ids; "
-                          "f32 value ~LogNormal(0,1); sum/count/mean; rows hash-partitioned to the owner GPU of "
-                          "their key (NCCL all-to-all), each GPU groups the keys it owns"),
+                          "f32 value ~LogNormal(0,1); sum/count/mean; radix partitioning by key hash (with N GPUs "
+                          "rows routed to the owner of their hash digit over one NCCL all-to-all, each GPU groups "
+                          "the keys it owns)"),
 }
 
 
@@ -604,7 +608,9 @@ class HashJob:
 
         self.ctx, self.wl, self.world, self.dist = ctx, wl, world, dist
         n = self.n_local = hi - lo
-        self.kernel = "table_kernel"
+        radix = (wl["kind"] == "highcard" and wl.get("table_mode", "auto") in ("auto", "radix")
+                 and (world > 1 or (n >= 1 << 24 and (1 << 22) <= wl["ids"] <= (1 << 28))))
+        self.kernel = "rx_scatter_kernel + rx_agg_kernel (radix passes)" if radix else "table_kernel"
         seed = wl["seed"]
         keys = torch.empty(n, dtype=torch.int64, device=dev)
         if wl["kind"] == "pipeline":
@@ -659,8 +665,8 @@ class HashJob:
         return hash_check(self, dev_in, dist, world)
 
     def kernel_bytes(self) -> int:
-        # the table kernel reads the shard's columns (one GPU) or the received (key, f64 value) rows
-        return self.n_local * self.bpr if self.sharded is None else self.sharded.n_recv * 16
+        # the shard's columns (one GPU) or the received rows (hash and value, or key and f64 value)
+        return self.n_local * self.bpr if self.sharded is None else self.sharded.n_recv * self.sharded.recv_bytes_per_row
 
     def read_result(self, host: dict) -> int:
         import torch

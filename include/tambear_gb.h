@@ -51,6 +51,8 @@
  *                                   memory, tables pushed into every rank's buffer by plain stores
  *   tbgb_hash_partition             no counterpart in the reference (single GPU); routes rows to
  *                                   the GPU that owns their key for the sharded high-cardinality path
+ *   tbgb_radix_route /              no counterpart (single GPU): owner routing by hash digit and the
+ *   tbgb_radix_groupby_routed       owner's radix-partitioned grouping of what it received
  *
  * Threading: one context per device; calls on one context are serialised by the
  * caller (the context's workspace is reused by every call); different contexts
@@ -364,6 +366,36 @@ tbgb_status tbgb_hash_partition(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb
                                 const uint64_t* d_mask, int64_t n, int32_t n_parts, int64_t* d_out_keys,
                                 double* d_out_vals, int64_t* d_part_counts, void* stream);
 
+/* ---- owner-sharded high-cardinality groupby (count / sum / mean) -------------------------
+ * No counterpart in the reference (single GPU, host-side GroupIndex::build,
+ * crates/tambear/src/group_index.rs:117-204).  Rows are routed by the top 8 bits of
+ * h = fmix64(key) (MurmurHash3's 64-bit finaliser, a bijection): digit d = h >> 56 belongs to rank
+ * d * world / 256, so each rank owns a contiguous digit range [ceil(256 r / world),
+ * ceil(256 (r + 1) / world)).
+ *
+ * tbgb_radix_route: the rows of this shard that pass mask and pred, written as (h, v) ordered by
+ * digit (all rows of digit 0, then digit 1, ...; order inside a digit unspecified), v = expr(a, b,
+ * c) in f64, or the f32 column itself when the columns are f32 without expression
+ * (tbgb_radix_value_bytes: 4 or 8 bytes per value).  d_digit_counts (256 int64, device) receives
+ * the rows of each digit; the output buffers hold n rows.  The rows for rank r are then one
+ * contiguous run, ready for an all-to-all.
+ *
+ * tbgb_radix_groupby_routed: the owner's side.  The received rows are n_senders blocks in sender
+ * order, each holding the sender's rows of digits [digit_lo, digit_lo + n_digits) in digit order;
+ * d_seg_counts (device, n_senders * n_digits int64, sender-major) gives their row counts and
+ * n_rows their total.  Groups the rows by key (recovered from h) into d_out_keys / out (count,
+ * sum, mean only; other outputs must be NULL) and *d_n_groups, with the semantics and errors of
+ * tbgb_groupby_hash. */
+int32_t tbgb_radix_value_bytes(const tbgb_columns* cols);
+tbgb_status tbgb_radix_route(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb_columns* cols, const uint64_t* d_mask,
+                             int64_t n, uint64_t* d_out_hashes, void* d_out_vals, int64_t* d_digit_counts,
+                             void* stream);
+tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, const uint64_t* d_hashes, const void* d_vals,
+                                      int32_t value_bytes, const int64_t* d_seg_counts, int32_t n_senders,
+                                      int32_t digit_lo, int32_t n_digits, int64_t n_rows, int64_t max_groups,
+                                      int64_t* d_out_keys, const tbgb_moments* out, int64_t* d_n_groups,
+                                      void* stream);
+
 /* Strategy for groupbys the shared-memory column kernel cannot take alone (int64 keys,
  * more than 512 dense groups, filter / expression / f32 columns): 0 = choose by size
  * (default: dense keys take group ranges in shared memory while at most 8 ranges cover
@@ -375,8 +407,11 @@ tbgb_status tbgb_hash_partition(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb
  * pre-aggregation (skewed keys); 2 = global table, direct updates (uniform
  * high-cardinality keys); 4 = dense keys split into ranges of groups, each range's
  * accumulators held whole in one CTA's shared memory, the CTAs of one range sharing the
- * rows (falls back to mode 2 beyond 8 ranges; int64 keys as mode 0).  Modes 1, 2 and 4
- * never bucket. */
+ * rows (falls back to mode 2 beyond 8 ranges; int64 keys as mode 0); 5 = int64 keys with
+ * count / sum / mean outputs only and max_groups <= 2^28: radix partitioning (two streaming
+ * passes by hash bits, then a shared-memory table per bucket; mode 0 chooses it for at least
+ * 2^24 rows and 2^22 <= max_groups <= 2^28), other calls as mode 0.  Modes 1, 2 and 4 never
+ * bucket. */
 tbgb_status tbgb_set_table_mode(tbgb_ctx* ctx, int mode);
 
 /* Waits for `stream` and returns the first deferred device error of the calls

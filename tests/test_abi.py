@@ -63,3 +63,14 @@ def test_state_bytes_without_gpu(libpath):
 
     assert lib().tbgb_state_bytes(256) == 11 * 256 * 8  # 11 state fields per group
     assert lib().tbgb_state_bytes(0) == 0
+
+
+def test_rust_bindings_declare_every_header_symbol():
+    """rust/src/ffi.rs (the Rust side of the boundary, not compiled here: no Rust toolchain)
+    declares every entry point of the header, and the backend names every dispatched entry."""
+    ffi = (ROOT / "rust" / "src" / "ffi.rs").read_text()
+    declared = set(re.findall(r"pub fn (tbgb_\w+)\s*\(", ffi))
+    assert declared == set(header_functions()), sorted(set(header_functions()) ^ declared)
+    backend = (ROOT / "rust" / "src" / "backend.rs").read_text()
+    for entry in ("scatter_phi", "scatter_multi_phi", "scatter_phi_masked", "scatter_extremum"):
+        assert f'"{entry}"' in backend, entry

@@ -26,6 +26,34 @@ def free_port():
     return p
 
 
+def fmix64_np(keys):
+    k = np.asarray(keys).view(np.uint64).copy()
+    with np.errstate(over="ignore"):
+        k ^= k >> np.uint64(33)
+        k *= np.uint64(0xFF51AFD7ED558CCD)
+        k ^= k >> np.uint64(33)
+        k *= np.uint64(0xC4CEB9FE1A85EC53)
+        k ^= k >> np.uint64(33)
+    return k
+
+
+def unfmix64_np(h):
+    inv = lambda c: pow(c, -1, 1 << 64)  # noqa: E731
+    x = np.asarray(h, dtype=np.uint64).copy()
+    with np.errstate(over="ignore"):
+        x ^= x >> np.uint64(33)
+        x *= np.uint64(inv(0xC4CEB9FE1A85EC53))
+        x ^= x >> np.uint64(33)
+        x *= np.uint64(inv(0xFF51AFD7ED558CCD))
+        x ^= x >> np.uint64(33)
+    return x.view(np.int64)
+
+
+def radix_owner_np(keys, P):
+    d = (fmix64_np(keys) >> np.uint64(56)).astype(np.int64)
+    return d * P // 256
+
+
 def owner_np(keys, P):
     k = np.asarray(keys).view(np.uint64).copy()
     with np.errstate(over="ignore"):
@@ -53,6 +81,37 @@ class FakeCtx:
 
     def groupby_hash_into(self, keys, a, max_groups, out_keys, out, n_groups, **kw):
         res = oracle.groupby_i64(keys.numpy(), a.numpy().astype(np.float64))
+        g = res["keys"].size
+        out_keys[:g] = torch.from_numpy(res["keys"])
+        out["count"][:g] = torch.from_numpy(res["counts"])
+        out["sum"][:g] = torch.from_numpy(res["sums"])
+        n_groups[0] = g
+
+    # radix routing -----------------------------------------------------------------------
+    def radix_value_bytes(self, a, b=None, c=None, expr="a", pred=None, threshold=0.0):
+        return 4 if a.dtype == torch.float32 and expr == "a" else 8
+
+    def radix_route(self, keys, a, out_hashes, out_vals, digit_counts, b=None, c=None, expr="a", pred=None,
+                    threshold=0.0, mask=None):
+        h = fmix64_np(keys.numpy())
+        d = (h >> np.uint64(56)).astype(np.int64)
+        order = np.argsort(d, kind="stable")
+        m = h.size
+        out_hashes[:m] = torch.from_numpy(h[order].view(np.int64))
+        out_vals[:m] = a[torch.from_numpy(order)]
+        digit_counts[:] = torch.from_numpy(np.bincount(d, minlength=256).astype(np.int64))
+
+    def radix_groupby_routed(self, hashes, vals, seg_counts, n_senders, digit_lo, n_digits, n_rows, max_groups,
+                             out_keys, out, n_groups):
+        h = hashes[:n_rows].numpy().view(np.uint64)
+        d = (h >> np.uint64(56)).astype(np.int64)
+        assert np.all((d >= digit_lo) & (d < digit_lo + n_digits)), "a row routed to a rank that does not own it"
+        # the blocks are in sender order, each in digit order, with the announced sizes
+        sizes = seg_counts.numpy().reshape(n_senders, n_digits)
+        assert sizes.sum() == n_rows
+        exp = np.concatenate([np.repeat(np.arange(digit_lo, digit_lo + n_digits), sizes[s]) for s in range(n_senders)])
+        assert np.array_equal(d, exp)
+        res = oracle.groupby_i64(unfmix64_np(h), vals[:n_rows].numpy().astype(np.float64))
         g = res["keys"].size
         out_keys[:g] = torch.from_numpy(res["keys"])
         out["count"][:g] = torch.from_numpy(res["counts"])
@@ -89,7 +148,7 @@ def _init(rank, port, world=WORLD):
     dist.init_process_group("gloo", rank=rank, world_size=world)
 
 
-def _hash_worker(rank, port, n, ids, q):
+def _hash_worker(rank, port, n, ids, fields, q):
     from winrapids_b200.sharded import ShardedHashGroupby
 
     _init(rank, port)
@@ -97,7 +156,7 @@ def _hash_worker(rank, port, n, ids, q):
         keys = oracle.gen_keys_ids(n, ids, 77, 3)
         vals = oracle.gen_values_normal(n, 0.0, 1.0, 3)
         lo, hi = n * rank // WORLD, n * (rank + 1) // WORLD
-        sh = ShardedHashGroupby(FakeCtx(), dist, WORLD, hi - lo, ids, ("count", "sum"), "cpu")
+        sh = ShardedHashGroupby(FakeCtx(), dist, WORLD, hi - lo, ids, fields, "cpu")
         sh.step(torch.from_numpy(keys[lo:hi]), torch.from_numpy(vals[lo:hi]))
         gk, out = sh.result()
         q.put((rank, gk.numpy().copy(), out["count"].numpy().copy(), out["sum"].numpy().copy(), sh.n_recv))
@@ -154,9 +213,13 @@ def _spawn(fn, *args, world=WORLD):
     return sorted(res, key=lambda x: x[0])
 
 
-def test_sharded_hash_groupby_gloo():
+@pytest.mark.parametrize("route", ["radix", "stable"])
+def test_sharded_hash_groupby_gloo(route):
+    """count / sum take the radix routing (digit owners); with min among the outputs the stable
+    owner partition runs instead."""
     n, ids = 60_000, 5_000
-    res = _spawn(_hash_worker, free_port(), n, ids)
+    fields = ("count", "sum") if route == "radix" else ("count", "sum", "min")
+    res = _spawn(_hash_worker, free_port(), n, ids, fields)
     keys = oracle.gen_keys_ids(n, ids, 77, 3)
     vals = oracle.gen_values_normal(n, 0.0, 1.0, 3)
     want = oracle.groupby_i64(keys, vals)
@@ -164,8 +227,9 @@ def test_sharded_hash_groupby_gloo():
     cnt = np.concatenate([r[2] for r in res])
     sm = np.concatenate([r[3] for r in res])
     assert sum(r[4] for r in res) == n
+    own = radix_owner_np if route == "radix" else owner_np
     for rank, k, *_ in res:
-        assert np.all(owner_np(k, WORLD) == rank), "a group on a rank that does not own it"
+        assert np.all(own(k, WORLD) == rank), "a group on a rank that does not own it"
     order = np.argsort(gk)
     assert np.array_equal(gk[order], want["keys"])
     assert np.array_equal(cnt[order], want["counts"])

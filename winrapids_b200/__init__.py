@@ -331,6 +331,30 @@ class Context:
                                                 int(n_parts), _ptr(out_keys), _ptr(out_vals), _ptr(part_counts),
                                                 _stream_handle(stream)))
 
+    def radix_value_bytes(self, a, b=None, c=None, expr: str = "a", pred: str | None = None,
+                          threshold: float = 0.0) -> int:
+        """Bytes per value of routed rows: 4 (an f32 column without expression) or 8."""
+        return int(self._L.tbgb_radix_value_bytes(C.byref(self.columns(a, b, c, expr, pred, threshold))))
+
+    def radix_route(self, keys, a, out_hashes, out_vals, digit_counts, b=None, c=None, expr: str = "a",
+                    pred: str | None = None, threshold: float = 0.0, mask=None, stream=None):
+        """Enqueue the owner routing of this shard's rows (see tbgb_radix_route): rows as
+        (fmix64(key), value) ordered by the top 8 hash bits; digit_counts (256 int64) per digit."""
+        cols = self.columns(a, b, c, expr, pred, threshold)
+        self._check(self._L.tbgb_radix_route(self._h, _ptr(keys), C.byref(cols), _ptr(mask), int(keys.numel()),
+                                             _ptr(out_hashes), _ptr(out_vals), _ptr(digit_counts),
+                                             _stream_handle(stream)))
+
+    def radix_groupby_routed(self, hashes, vals, seg_counts, n_senders: int, digit_lo: int, n_digits: int,
+                             n_rows: int, max_groups: int, out_keys, out: dict, n_groups, stream=None):
+        """Enqueue the owner's grouping of routed rows (see tbgb_radix_groupby_routed): count / sum /
+        mean into caller-owned buffers."""
+        m = self.moments_struct(out)
+        self._check(self._L.tbgb_radix_groupby_routed(self._h, _ptr(hashes), _ptr(vals), int(vals.element_size()),
+                                                      _ptr(seg_counts), int(n_senders), int(digit_lo),
+                                                      int(n_digits), int(n_rows), int(max_groups), _ptr(out_keys),
+                                                      C.byref(m), _ptr(n_groups), _stream_handle(stream)))
+
     def groupby_hash(self, keys, a, max_groups: int, b=None, c=None, expr: str = "a", pred: str | None = None,
                      threshold: float = 0.0, mask=None, fields=MOMENT_FIELDS, stream=None):
         """int64-key groupby; returns (group keys, {field: tensor}) trimmed to the group count

@@ -1044,6 +1044,118 @@ tbgb_status tbgb_hash_partition(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb
   return TBGB_OK;
 }
 
+int32_t tbgb_radix_value_bytes(const tbgb_columns* cols) {
+  if (!cols) return 0;
+  return tbgb::radix_value_f32(*cols) ? 4 : 8;
+}
+
+tbgb_status tbgb_radix_route(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb_columns* cols, const uint64_t* d_mask,
+                             int64_t n, uint64_t* d_out_hashes, void* d_out_vals, int64_t* d_digit_counts,
+                             void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (n < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n must be >= 0");
+  if (!d_digit_counts) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "digit_counts is NULL");
+  if (n > 0 && (!d_keys || !d_out_hashes || !d_out_vals))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "keys / output pointers are NULL");
+  if (misaligned(d_keys, 8) || misaligned(d_out_hashes, 8) ||
+      misaligned(d_out_vals, static_cast<size_t>(tbgb_radix_value_bytes(cols))))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "pointer not aligned to its element size");
+  tbgb_status st = check_columns(ctx, cols, n);
+  if (st != TBGB_OK) return st;
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  st = ensure_ws(ctx, tbgb::radix_route_aux_bytes());
+  if (st != TBGB_OK) return st;
+  tbgb::RadixArgs a{};
+  a.keys = d_keys;
+  a.cols = *cols;
+  a.mask = d_mask;
+  a.n = n;
+  cudaError_t e = tbgb::radix_route(a, reinterpret_cast<unsigned long long*>(d_out_hashes), d_out_vals,
+                                    d_digit_counts, ctx->ws, ctx->num_sms, static_cast<cudaStream_t>(stream),
+                                    &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "radix route launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, const uint64_t* d_hashes, const void* d_vals,
+                                      int32_t value_bytes, const int64_t* d_seg_counts, int32_t n_senders,
+                                      int32_t digit_lo, int32_t n_digits, int64_t n_rows, int64_t max_groups,
+                                      int64_t* d_out_keys, const tbgb_moments* out, int64_t* d_n_groups,
+                                      void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (!out || !d_out_keys || !d_n_groups || !d_seg_counts)
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "out, out_keys, n_groups and seg_counts must not be NULL");
+  if (out->min || out->max || out->m2 || out->var_pop || out->var_samp || out->m3 || out->m4)
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "the routed groupby computes count, sum and mean only");
+  if (value_bytes != 4 && value_bytes != 8) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "value_bytes must be 4 or 8");
+  if (n_senders < 1 || n_digits < 1 || digit_lo < 0 || digit_lo + n_digits > tbgb::kRadixDigits ||
+      static_cast<long long>(n_senders) * n_digits > 4096)
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "bad sender / digit ranges (digits within [0, 256), senders x "
+                                                "digits <= 4096)");
+  if (n_rows < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_rows must be >= 0");
+  if (max_groups < 1 || max_groups > (1ll << 40))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "max_groups must be in [1, 2^40]");
+  if (n_rows > 0 && (!d_hashes || !d_vals)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "row pointers are NULL");
+  if (misaligned(d_hashes, 8) || misaligned(d_vals, static_cast<size_t>(value_bytes)))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "pointer not aligned to its element size");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  const bool vf32 = value_bytes == 4;
+  const tbgb::RadixPlan R = tbgb::radix_routed_plan(vf32, n_rows, n_digits, ctx->num_sms);
+  const tbgb::TablePlan P = tbgb::table_plan(true, false, 0, max_groups, ctx->num_sms, 1, false);
+  const size_t fb_bytes = align256(P.table_bytes) + align256(tbgb::table_finalize_scratch_bytes(P));
+  const size_t t2_region = R.t2_bytes > fb_bytes ? R.t2_bytes : fb_bytes;
+  tbgb_status st = ensure_ws(ctx, tbgb::radix_t2_offset(R) + t2_region);
+  if (st != TBGB_OK) return st;
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  cudaEvent_t e0, e1;
+  st = profile_events(ctx, &e0, &e1);
+  if (st != TBGB_OK) return st;
+  tbgb::RoutedArgs r{};
+  r.hashes = reinterpret_cast<const unsigned long long*>(d_hashes);
+  r.vals = d_vals;
+  r.seg_counts = d_seg_counts;
+  r.n_senders = n_senders;
+  r.digit_lo = digit_lo;
+  r.n_digits = n_digits;
+  r.n_rows = n_rows;
+  r.max_groups = max_groups;
+  r.out_keys = d_out_keys;
+  r.out = *out;
+  r.d_n_groups = d_n_groups;
+  r.err = ctx->err;
+  uint32_t* gate = nullptr;
+  cudaError_t e = tbgb::radix_groupby_routed(R, r, ctx->ws, &gate, s, &ctx->launches, e0, e1);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "routed radix groupby launch", e);
+  // fallback (gated): group the hashes themselves in the global table, then turn them into keys
+  char* w = static_cast<char*>(ctx->ws) + tbgb::radix_t2_offset(R);
+  unsigned long long* T = reinterpret_cast<unsigned long long*>(w);
+  unsigned long long* fin = reinterpret_cast<unsigned long long*>(w + align256(P.table_bytes));
+  e = tbgb::table_init(P, T, s, &ctx->launches, gate);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback table init", e);
+  tbgb::TableArgs a{};
+  a.keys = d_hashes;
+  a.cols.a = d_vals;
+  a.cols.dtype = vf32 ? TBGB_F32 : TBGB_F64;
+  a.cols.expr = TBGB_EXPR_A;
+  a.cols.pred = TBGB_PRED_NONE;
+  a.n = n_rows;
+  a.slots = P.slots;
+  a.ngroups = tbgb::table_counter(P, T);
+  a.max_groups = max_groups;
+  a.err = ctx->err;
+  a.table = T;
+  a.gate = gate;
+  e = tbgb::table_accumulate(P, a, s, &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback table launch", e);
+  e = tbgb::table_finalize_hash(P, T, max_groups, d_out_keys, out, d_n_groups, fin, s, &ctx->launches, gate);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback table finalize", e);
+  e = tbgb::radix_unhash_keys(d_out_keys, d_n_groups, max_groups, gate, ctx->num_sms, s, &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback key launch", e);
+  return TBGB_OK;
+}
+
 tbgb_status tbgb_sync(tbgb_ctx* ctx, void* stream) {
   if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
   DeviceGuard dg(ctx->device);

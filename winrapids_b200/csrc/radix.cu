@@ -6,9 +6,11 @@
 // memory:
 //   pass 1  rows -> 256 buckets by the top 8 bits of h = fmix64(key)   (mask, predicate and
 //           expression applied here; rows that fail them are dropped)
-//   pass 2  each of those -> 256 buckets by the next 8 bits            (65,536 buckets)
-//   pass 3  one CTA per bucket: a shared-memory table of 8,192 slots keyed by the low 48 bits of
-//           h (the top 16 are the bucket) takes the bucket's rows, then writes its groups.
+//   pass 2  each of those -> 512 buckets by the next 9 bits            (131,072 buckets)
+//   pass 3  one CTA per bucket: a shared-memory table of 4,096 slots keyed by the low 47 bits of
+//           h (the top 17 are the bucket) takes the bucket's rows, then writes its groups.  A
+//           slot is two words: (key47 << 17 | count) and the f64 sum, so a row costs one probe
+//           read, one 64-bit atomic and one f64 add; 64 KB a table lets three CTAs share an SM.
 // fmix64 (MurmurHash3's finaliser) is a bijection, so the rows carry h instead of the key and
 // pass 3 recovers each group's key by inverting it.  A row is (h, value): 12 bytes for an f32
 // column without an expression, 16 otherwise.
@@ -40,13 +42,22 @@ namespace {
 constexpr int RX_NT = 512;                     // threads per scatter CTA
 constexpr int RX_TILE = 4096;                  // rows per scatter tile
 constexpr int RX_PER = RX_TILE / RX_NT;        // rows per thread per tile
-constexpr int AGG_NT = 1024;                   // threads per aggregation CTA
-constexpr int AGG_SLOTS = 8192;                // shared-memory table slots per bucket
+constexpr int D1_BITS = 8, D2_BITS = 9;        // digits of pass 1 and pass 2
+constexpr int BUCKET_BITS = D1_BITS + D2_BITS;  // final buckets: the top 17 bits of h
+constexpr int KEY_BITS = 64 - BUCKET_BITS;      // bits of h a table slot keeps (47)
+constexpr int CNT_BITS = 64 - KEY_BITS;         // count field of a slot word (17)
+constexpr unsigned long long kCntMask = (1ull << CNT_BITS) - 1;
+constexpr unsigned long long kKeyMask = (1ull << KEY_BITS) - 1;
+constexpr int AGG_NT = 512;                    // threads per aggregation CTA
+constexpr int AGG_SLOTS = 4096;                // shared-memory table slots per bucket
 constexpr int AGG_MAX_PROBE = 512;             // probes before a row gives up (fallback)
-constexpr int AGG_UNROLL = 4;
-constexpr unsigned long long kLow48 = (1ull << 48) - 1;
-constexpr unsigned long long kFree = ~0ull;    // never a 48-bit value
+constexpr int AGG_UNROLL = 2;
+// A free slot.  A used slot never equals it: its count stays below kCntMask - 1 (a key with
+// more rows in one bucket sends the call to the fallback).
+constexpr unsigned long long kFree = ~0ull;
 constexpr unsigned int kPrefetchChunk = 32768;
+static_assert(kRadixBuckets == (1 << BUCKET_BITS), "bucket count");
+static_assert(kRadixDigits == (1 << D1_BITS), "first-pass digits");
 
 static_assert(RX_TILE <= 65536, "ranks are packed in 16 bits");
 
@@ -114,31 +125,34 @@ struct RxScatter {
 
 template <bool VF32>
 constexpr size_t scatter_smem() {
-  return static_cast<size_t>(RX_TILE) * (8 + (VF32 ? 4 : 8) + 1);
+  return static_cast<size_t>(RX_TILE) * (8 + (VF32 ? 4 : 8) + 2);
 }
 
 // SRC: 0 = the caller's key and value columns as they are, 1 = the caller's columns with mask /
 // predicate / expression, 2 = segments of a partitioned buffer.  VF32: rows carry an f32 value.
 // F32IN: the caller's columns are f32.
-template <int SRC, bool VF32, bool F32IN>
+template <int SRC, bool VF32, bool F32IN, int DBITS>
 __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
   using VT = typename std::conditional<VF32, float, double>::type;
+  constexpr int ND = 1 << DBITS;  // destination digits of this pass
+  static_assert(ND <= RX_NT, "one thread per digit in phase B");
   extern __shared__ __align__(16) unsigned char rx_sm[];
   unsigned long long* sh_h = reinterpret_cast<unsigned long long*>(rx_sm);
   VT* sh_v = reinterpret_cast<VT*>(sh_h + RX_TILE);
-  unsigned char* sh_d = reinterpret_cast<unsigned char*>(sh_v + RX_TILE);
-  __shared__ unsigned int hist[kRadixDigits];
-  __shared__ unsigned int lstart[kRadixDigits];
-  __shared__ unsigned int wlim[kRadixDigits];
-  __shared__ unsigned long long gdst[kRadixDigits];
-  __shared__ unsigned int wsum[kRadixDigits / 32];
+  unsigned short* sh_d = reinterpret_cast<unsigned short*>(sh_v + RX_TILE);
+  __shared__ unsigned int hist[ND];
+  __shared__ unsigned int lstart[ND];
+  __shared__ unsigned int wlim[ND];
+  __shared__ unsigned long long gdst[ND];
+  __shared__ unsigned int wsum[ND / 32];
   __shared__ unsigned int tile_total;
+  constexpr unsigned int DMASK = ND - 1;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   if constexpr (SRC == 2) {
     if (*reinterpret_cast<volatile const uint32_t*>(a.fallback)) return;  // pass 1 overflowed
   }
-  if (tid < kRadixDigits) hist[tid] = 0;
+  if (tid < ND) hist[tid] = 0;
   const long long ntiles = SRC == 2 ? a.seg_tiles[a.n_seg] : (a.n + RX_TILE - 1) / RX_TILE;
   const VT* src_v = static_cast<const VT*>(a.src_v);
   VT* dst_v = static_cast<VT*>(a.dst_v);
@@ -152,7 +166,7 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
       const long long tin = t - __ldg(a.seg_tiles + seg);
       row0 = __ldg(a.seg_base + seg) + tin * RX_TILE;
       rows = __ldg(a.seg_count + seg) - tin * RX_TILE;
-      obase = static_cast<unsigned long long>(__ldg(a.seg_digit + seg)) * kRadixDigits;
+      obase = static_cast<unsigned long long>(__ldg(a.seg_digit + seg)) * ND;
     } else {
       row0 = t * RX_TILE;
       rows = a.n - row0;
@@ -162,7 +176,7 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
     // ---- phase A: load, hash, rank inside the tile
     unsigned long long hv[RX_PER];
     VT vv[RX_PER];
-    unsigned int rk[RX_PER];  // bit 31 valid, bits 16-23 digit, bits 0-15 rank
+    unsigned int rk[RX_PER];  // bit 31 valid, bits 16-24 digit, bits 0-15 rank
     if constexpr (SRC == 2) {
 #pragma unroll
       for (int j = 0; j < RX_PER; ++j) {
@@ -177,7 +191,7 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
         const int li = j * RX_NT + tid;
         rk[j] = 0;
         if (li < rows) {
-          const unsigned d = static_cast<unsigned>(hv[j] >> a.shift) & 255u;
+          const unsigned d = static_cast<unsigned>(hv[j] >> a.shift) & DMASK;
           rk[j] = 0x80000000u | (d << 16) | atomicAdd(hist + d, 1u);
         }
       }
@@ -196,7 +210,7 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
         rk[j] = 0;
         if (li < rows) {
           hv[j] = fmix64(hv[j]);
-          const unsigned d = static_cast<unsigned>(hv[j] >> 56);
+          const unsigned d = static_cast<unsigned>(hv[j] >> (64 - DBITS));
           rk[j] = 0x80000000u | (d << 16) | atomicAdd(hist + d, 1u);
         }
       }
@@ -219,7 +233,7 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
           vv[j] = eval_expr(expr, av, bv, cv);
         }
         hv[j] = fmix64(static_cast<unsigned long long>(__ldcs(a.keys + row)));
-        const unsigned d = static_cast<unsigned>(hv[j] >> 56);
+        const unsigned d = static_cast<unsigned>(hv[j] >> (64 - DBITS));
         rk[j] = 0x80000000u | (d << 16) | atomicAdd(hist + d, 1u);
       }
     }
@@ -227,7 +241,7 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
 
     // ---- phase B: claim a run per bucket, offsets of the buckets inside the tile
     unsigned int c = 0, inc = 0;
-    if (tid < kRadixDigits) {
+    if (tid < ND) {
       c = hist[tid];
       hist[tid] = 0;
       unsigned long long g = 0;
@@ -251,11 +265,11 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
       if (lane == 31) wsum[warp] = inc;
     }
     __syncthreads();
-    if (tid < kRadixDigits) {
+    if (tid < ND) {
       unsigned int before = inc - c;
       for (int w = 0; w < warp; ++w) before += wsum[w];
       lstart[tid] = before;
-      if (tid == kRadixDigits - 1) tile_total = before + c;
+      if (tid == ND - 1) tile_total = before + c;
     }
     __syncthreads();
 
@@ -263,11 +277,11 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
 #pragma unroll
     for (int j = 0; j < RX_PER; ++j) {
       if (rk[j] >> 31) {
-        const unsigned d = (rk[j] >> 16) & 255u;
+        const unsigned d = (rk[j] >> 16) & DMASK;
         const unsigned p = lstart[d] + (rk[j] & 0xFFFFu);
         sh_h[p] = hv[j];
         sh_v[p] = vv[j];
-        sh_d[p] = static_cast<unsigned char>(d);
+        sh_d[p] = static_cast<unsigned short>(d);
       }
     }
     __syncthreads();
@@ -378,7 +392,7 @@ struct RxAgg {
   const void* src_v;
   const unsigned long long* cursor;
   int n_buckets;               // buckets of this call (all 65,536, or an owner's share)
-  int bucket0;                 // bucket index of local bucket 0 (the top 16 bits of its hashes)
+  int bucket0;                 // bucket index of local bucket 0 (the top 17 bits of its hashes)
   unsigned long long cap;
   long long max_groups;
   int64_t* out_keys;
@@ -387,15 +401,14 @@ struct RxAgg {
   uint32_t* fallback;
 };
 
-constexpr size_t agg_smem() { return static_cast<size_t>(AGG_SLOTS) * (8 + 8 + 4); }
+constexpr size_t agg_smem() { return static_cast<size_t>(AGG_SLOTS) * (8 + 8); }
 
 template <bool VF32>
-__global__ void __launch_bounds__(AGG_NT, 1) rx_agg_kernel(RxAgg a) {
+__global__ void __launch_bounds__(AGG_NT, 3) rx_agg_kernel(RxAgg a) {
   using VT = typename std::conditional<VF32, float, double>::type;
   extern __shared__ __align__(16) unsigned char ag_sm[];
-  unsigned long long* tk = reinterpret_cast<unsigned long long*>(ag_sm);
-  double* ts = reinterpret_cast<double*>(tk + AGG_SLOTS);
-  unsigned int* tc = reinterpret_cast<unsigned int*>(ts + AGG_SLOTS);
+  unsigned long long* tk = reinterpret_cast<unsigned long long*>(ag_sm);  // key47 << 17 | count
+  double* ts = reinterpret_cast<double*>(tk + AGG_SLOTS);                 // sum of finite values
   __shared__ unsigned int wcount[AGG_NT / 32];
   __shared__ unsigned long long gbase;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -425,7 +438,6 @@ __global__ void __launch_bounds__(AGG_NT, 1) rx_agg_kernel(RxAgg a) {
     for (int i = tid; i < AGG_SLOTS; i += AGG_NT) {
       tk[i] = kFree;
       ts[i] = 0.0;
-      tc[i] = 0u;
     }
     __syncthreads();
     for (unsigned long long p0 = 0; p0 < rows; p0 += static_cast<unsigned long long>(AGG_NT) * AGG_UNROLL) {
@@ -443,31 +455,35 @@ __global__ void __launch_bounds__(AGG_NT, 1) rx_agg_kernel(RxAgg a) {
       for (int u = 0; u < AGG_UNROLL; ++u) {
         const unsigned long long p = p0 + static_cast<unsigned long long>(u) * AGG_NT + tid;
         if (p >= rows) continue;
-        const unsigned long long low = hv[u] & kLow48;
+        const double v = vv[u];
+        const unsigned long long inc = is_nan(v) ? 0ull : 1ull;  // a NaN row makes its group, uncounted
+        const unsigned long long key = hv[u] & kKeyMask;
         unsigned int slot = static_cast<unsigned int>(hv[u]) & (AGG_SLOTS - 1);
-        bool found = false;
+        int found = -1;
         for (int probe = 0; probe < AGG_MAX_PROBE; ++probe) {
-          const unsigned long long k = tk[slot];
-          if (k == low) {
-            found = true;
-            break;
-          }
-          if (k == kFree) {
-            const unsigned long long prev = atomicCAS(tk + slot, kFree, low);
-            if (prev == kFree || prev == low) {
-              found = true;
+          unsigned long long w = tk[slot];
+          if (w == kFree) {
+            w = atomicCAS(tk + slot, kFree, (key << CNT_BITS) | inc);
+            if (w == kFree) {
+              found = static_cast<int>(slot);
               break;
             }
           }
+          if ((w >> CNT_BITS) == key) {
+            if (inc) {
+              const unsigned long long old = atomicAdd(tk + slot, 1ull);
+              if ((old & kCntMask) >= kCntMask - 2) atomicOr(a.fallback, 4u);  // count field nearly full
+            }
+            found = static_cast<int>(slot);
+            break;
+          }
           slot = (slot + 1) & (AGG_SLOTS - 1);
         }
-        if (!found) {
+        if (found < 0) {
           atomicOr(a.fallback, 2u);  // more distinct keys than the table takes: recompute elsewhere
           continue;
         }
-        const double v = vv[u];
-        if (!is_nan(v)) atomicAdd(tc + slot, 1u);
-        if (is_finite(v)) atomicAdd(ts + slot, v);
+        if (is_finite(v)) atomicAdd(ts + found, v);
       }
     }
     __syncthreads();
@@ -478,30 +494,30 @@ __global__ void __launch_bounds__(AGG_NT, 1) rx_agg_kernel(RxAgg a) {
     if (lane == 0) wcount[warp] = mine;
     __syncthreads();
     if (warp == 0) {
-      const unsigned int cnt = wcount[lane];
+      const unsigned int cnt = lane < AGG_NT / 32 ? wcount[lane] : 0u;
       unsigned int incl = cnt;
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
         const unsigned y = __shfl_up_sync(0xffffffffu, incl, o);
         if (lane >= o) incl += y;
       }
-      wcount[lane] = incl - cnt;
+      if (lane < AGG_NT / 32) wcount[lane] = incl - cnt;
       if (lane == 31) gbase = atomicAdd(a.n_groups, static_cast<unsigned long long>(incl));
     }
     __syncthreads();
     unsigned long long pos = gbase + wcount[warp];
-    const unsigned long long top = static_cast<unsigned long long>(b + a.bucket0) << 48;
+    const unsigned long long top = static_cast<unsigned long long>(b + a.bucket0) << KEY_BITS;
     for (int k = 0; k < AGG_SLOTS / AGG_NT; ++k) {
       const int i = k * AGG_NT + tid;
-      const unsigned long long key48 = tk[i];
-      const bool occ = key48 != kFree;
+      const unsigned long long w = tk[i];
+      const bool occ = w != kFree;
       const unsigned bal = __ballot_sync(0xffffffffu, occ);
       if (occ) {
         const unsigned long long j = pos + __popc(bal & ((1u << lane) - 1u));
         if (j < static_cast<unsigned long long>(a.max_groups)) {
-          const double cnt = static_cast<double>(tc[i]);
+          const double cnt = static_cast<double>(w & kCntMask);
           const double sum = ts[i];
-          a.out_keys[j] = static_cast<int64_t>(unfmix64(top | key48));
+          a.out_keys[j] = static_cast<int64_t>(unfmix64(top | (w >> CNT_BITS)));
           if (a.out.count) a.out.count[j] = cnt;
           if (a.out.sum) a.out.sum[j] = sum;
           if (a.out.mean) a.out.mean[j] = cnt > 0.0 ? sum / cnt : qnan();
@@ -529,7 +545,7 @@ unsigned long long round16(unsigned long long x) { return (x + 15) / 16 * 16; }
 
 template <int SRC, bool VF32, bool F32IN>
 cudaError_t launch_scatter(const RxScatter& s, int grid, cudaStream_t st) {
-  auto k = rx_scatter_kernel<SRC, VF32, F32IN>;
+  auto k = rx_scatter_kernel<SRC, VF32, F32IN, SRC == 2 ? D2_BITS : D1_BITS>;
   constexpr size_t smem = scatter_smem<VF32>();
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
@@ -547,19 +563,33 @@ cudaError_t launch_agg(const RxAgg& g, int grid, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+int agg_blocks_per_sm(bool vf32) {
+  static int cached[2] = {0, 0};
+  int& c = cached[vf32 ? 1 : 0];
+  if (c == 0) {
+    int v = 0;
+    const size_t smem = agg_smem();
+    auto k = vf32 ? rx_agg_kernel<true> : rx_agg_kernel<false>;
+    cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k, AGG_NT, smem);
+    c = (e == cudaSuccess && v > 0) ? v : 1;
+  }
+  return c;
+}
+
 int scatter_blocks_per_sm(bool vf32) {
   static int cached[2] = {0, 0};
   int& c = cached[vf32 ? 1 : 0];
   if (c == 0) {
     int v = 0;
     const size_t smem = vf32 ? scatter_smem<true>() : scatter_smem<false>();
-    cudaError_t e = vf32 ? cudaFuncSetAttribute(rx_scatter_kernel<2, true, true>,
+    cudaError_t e = vf32 ? cudaFuncSetAttribute(rx_scatter_kernel<2, true, true, D2_BITS>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))
-                         : cudaFuncSetAttribute(rx_scatter_kernel<2, false, false>,
+                         : cudaFuncSetAttribute(rx_scatter_kernel<2, false, false, D2_BITS>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
     if (e == cudaSuccess) {
-      e = vf32 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, rx_scatter_kernel<2, true, true>, RX_NT, smem)
-               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, rx_scatter_kernel<2, false, false>, RX_NT, smem);
+      e = vf32 ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, rx_scatter_kernel<2, true, true, D2_BITS>, RX_NT, smem)
+               : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, rx_scatter_kernel<2, false, false, D2_BITS>, RX_NT, smem);
     }
     c = (e == cudaSuccess && v > 0) ? v : 1;
   }
@@ -588,7 +618,7 @@ RadixPlan radix_plan(const tbgb_columns& cols, long long n, int num_sms) {
                align256(static_cast<size_t>(P.cap2) * kRadixBuckets * (row_bytes - 8));
   P.aux_bytes = align256(sizeof(Aux));
   P.grid_scatter = num_sms * scatter_blocks_per_sm(P.vf32);
-  P.grid_agg = num_sms;
+  P.grid_agg = num_sms * agg_blocks_per_sm(P.vf32);
   return P;
 }
 
@@ -643,7 +673,7 @@ cudaError_t radix_groupby(const RadixPlan& P, const RadixArgs& a, void* ws, uint
   p2.seg_digit = x->seg_digit;
   p2.seg_tiles = x->seg_tiles;
   p2.n_seg = kRadixDigits;
-  p2.shift = 48;
+  p2.shift = KEY_BITS;
   p2.dst_h = t2h;
   p2.dst_v = t2v;
   p2.cursor = x->cur2;
@@ -733,7 +763,7 @@ RadixPlan radix_routed_plan(bool vf32, long long n_rows, int n_digits, int num_s
   RadixPlan P{};
   P.vf32 = vf32;
   const unsigned long long rows = static_cast<unsigned long long>(n_rows > 0 ? n_rows : 0);
-  const unsigned long long nb = static_cast<unsigned long long>(n_digits) * kRadixDigits;
+  const unsigned long long nb = static_cast<unsigned long long>(n_digits) << D2_BITS;
   const unsigned long long e2 = rows / nb;
   P.cap1 = 0;
   P.cap2 = round16(e2 + e2 / 16 + 512);
@@ -742,7 +772,7 @@ RadixPlan radix_routed_plan(bool vf32, long long n_rows, int n_digits, int num_s
   P.t2_bytes = align256(static_cast<size_t>(P.cap2) * nb * 8) + align256(static_cast<size_t>(P.cap2) * nb * vb);
   P.aux_bytes = align256(sizeof(Aux));
   P.grid_scatter = num_sms * scatter_blocks_per_sm(vf32);
-  P.grid_agg = num_sms;
+  P.grid_agg = num_sms * agg_blocks_per_sm(P.vf32);
   return P;
 }
 
@@ -750,7 +780,7 @@ cudaError_t radix_groupby_routed(const RadixPlan& P, const RoutedArgs& r, void* 
                                  cudaStream_t s, uint64_t* launches, cudaEvent_t ev0, cudaEvent_t ev1) {
   char* w = static_cast<char*>(ws);
   Aux* x = reinterpret_cast<Aux*>(w);
-  const unsigned long long nb = static_cast<unsigned long long>(r.n_digits) * kRadixDigits;
+  const unsigned long long nb = static_cast<unsigned long long>(r.n_digits) << D2_BITS;
   unsigned long long* t2h = reinterpret_cast<unsigned long long*>(w + radix_t2_offset(P));
   void* t2v = w + radix_t2_offset(P) + align256(static_cast<size_t>(P.cap2) * nb * 8);
   *fallback = &x->fallback;
@@ -770,7 +800,7 @@ cudaError_t radix_groupby_routed(const RadixPlan& P, const RoutedArgs& r, void* 
   p2.seg_digit = x->seg_digit;
   p2.seg_tiles = x->seg_tiles;
   p2.n_seg = n_seg;
-  p2.shift = 48;
+  p2.shift = KEY_BITS;
   p2.dst_h = t2h;
   p2.dst_v = t2v;
   p2.cursor = x->cur2;
@@ -787,7 +817,7 @@ cudaError_t radix_groupby_routed(const RadixPlan& P, const RoutedArgs& r, void* 
   g.src_v = t2v;
   g.cursor = x->cur2;
   g.n_buckets = static_cast<int>(nb);
-  g.bucket0 = r.digit_lo * kRadixDigits;
+  g.bucket0 = r.digit_lo << D2_BITS;
   g.cap = P.cap2;
   g.max_groups = r.max_groups;
   g.out_keys = r.out_keys;

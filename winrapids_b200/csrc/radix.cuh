@@ -9,9 +9,9 @@
 
 namespace tbgb {
 
-constexpr int kRadixDigits = 256;               // buckets per pass (8 hash bits)
-constexpr int kRadixBuckets = 65536;            // final buckets after two passes (16 hash bits)
-constexpr long long kRadixMaxGroups = 1ll << 28;  // distinct keys one call serves (4096 per bucket)
+constexpr int kRadixDigits = 256;               // first-pass buckets (the top 8 hash bits)
+constexpr int kRadixBuckets = 131072;           // final buckets after the second pass (17 hash bits)
+constexpr long long kRadixMaxGroups = 1ll << 28;  // distinct keys one call serves (2048 per bucket)
 
 struct RadixPlan {
   bool vf32;                  // rows carry the value as f32 (an f32 column without expression)

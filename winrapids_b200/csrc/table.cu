@@ -758,20 +758,24 @@ __global__ void __launch_bounds__(FIN_NT) table_occ_count_kernel(const unsigned 
                                                                  const uint32_t* gate) {
   if (gate && *gate == 0u) return;
   const int W = full ? FL_WORDS : SC_WORDS, ID = full ? FL_ID : SC_ID;
-  const unsigned long long i0 = static_cast<unsigned long long>(blockIdx.x) * FIN_CHUNK;
-  unsigned int c = 0;
-  for (int k = 0; k < FIN_CHUNK / FIN_NT; ++k) {
-    const unsigned long long i = i0 + static_cast<unsigned long long>(k) * FIN_NT + threadIdx.x;
-    if (i < total && slot_occupied(T, i, slots, W, ID)) ++c;
-  }
-  for (int o = 16; o > 0; o >>= 1) c += __shfl_down_sync(0xffffffffu, c, o);
+  const unsigned long long nchunks = (total + FIN_CHUNK - 1) / FIN_CHUNK;
   __shared__ unsigned int ws[FIN_NT / 32];
-  if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = c;
-  __syncthreads();
-  if (threadIdx.x == 0) {
-    unsigned long long t = 0;
-    for (int w = 0; w < FIN_NT / 32; ++w) t += ws[w];
-    counts[blockIdx.x] = t;
+  for (unsigned long long chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
+    const unsigned long long i0 = chunk * FIN_CHUNK;
+    unsigned int c = 0;
+    for (int k = 0; k < FIN_CHUNK / FIN_NT; ++k) {
+      const unsigned long long i = i0 + static_cast<unsigned long long>(k) * FIN_NT + threadIdx.x;
+      if (i < total && slot_occupied(T, i, slots, W, ID)) ++c;
+    }
+    for (int o = 16; o > 0; o >>= 1) c += __shfl_down_sync(0xffffffffu, c, o);
+    if ((threadIdx.x & 31) == 0) ws[threadIdx.x >> 5] = c;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      unsigned long long t = 0;
+      for (int w = 0; w < FIN_NT / 32; ++w) t += ws[w];
+      counts[chunk] = t;
+    }
+    __syncthreads();
   }
 }
 
@@ -824,8 +828,10 @@ __global__ void __launch_bounds__(FIN_NT) table_compact_kernel(const unsigned lo
   const int W = full ? FL_WORDS : SC_WORDS, ID = full ? FL_ID : SC_ID;
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   __shared__ unsigned int wpre[FIN_NT / 32];
-  unsigned long long pos = offsets[blockIdx.x];
-  const unsigned long long i0 = static_cast<unsigned long long>(blockIdx.x) * FIN_CHUNK;
+  const unsigned long long nchunks = (total + FIN_CHUNK - 1) / FIN_CHUNK;
+  for (unsigned long long chunk = blockIdx.x; chunk < nchunks; chunk += gridDim.x) {
+  unsigned long long pos = offsets[chunk];
+  const unsigned long long i0 = chunk * FIN_CHUNK;
   for (int k = 0; k < FIN_CHUNK / FIN_NT; ++k) {
     const unsigned long long i = i0 + static_cast<unsigned long long>(k) * FIN_NT + threadIdx.x;
     const bool occ = i < total && slot_occupied(T, i, slots, W, ID);
@@ -849,6 +855,7 @@ __global__ void __launch_bounds__(FIN_NT) table_compact_kernel(const unsigned lo
     }
     pos += all;
     __syncthreads();
+  }
   }
 }
 
@@ -955,7 +962,8 @@ cudaError_t table_init(const TablePlan& P, unsigned long long* table, cudaStream
                        const uint32_t* gate) {
   const unsigned long long nslots = static_cast<unsigned long long>(P.buckets) * (P.slots + (P.hash ? 1 : 0));
   unsigned long long blocks = (nslots + 255) / 256;
-  if (blocks > 65536ull) blocks = 65536ull;
+  const unsigned long long cap = gate ? static_cast<unsigned long long>(P.grid > 0 ? P.grid : 148) * 16 : 65536ull;
+  if (blocks > cap) blocks = cap;
   if (blocks < 1) blocks = 1;
   table_init_kernel<<<static_cast<unsigned int>(blocks), 256, 0, s>>>(table, nslots, P.full ? 1 : 0, gate);
   cudaError_t e = cudaGetLastError();
@@ -1017,11 +1025,13 @@ cudaError_t table_finalize_hash(const TablePlan& P, const unsigned long long* ta
   const unsigned long long total = static_cast<unsigned long long>(P.buckets) * (P.slots + 1);
   const unsigned long long nblk = (total + FIN_CHUNK - 1) / FIN_CHUNK;
   const int full = P.full ? 1 : 0;
-  table_occ_count_kernel<<<static_cast<unsigned int>(nblk), FIN_NT, 0, s>>>(table, P.slots, total, full, scratch,
-                                                                            gate);
+  // grid-stride over the chunks: a gated launch that finds its gate closed costs a few CTAs only
+  const unsigned long long cap = static_cast<unsigned long long>(P.grid > 0 ? P.grid : 148) * 16;
+  const unsigned int grid = static_cast<unsigned int>(nblk < cap ? nblk : cap);
+  table_occ_count_kernel<<<grid, FIN_NT, 0, s>>>(table, P.slots, total, full, scratch, gate);
   table_occ_scan_kernel<<<1, 1024, 0, s>>>(scratch, static_cast<long long>(nblk), max_groups, d_n_groups, gate);
-  table_compact_kernel<<<static_cast<unsigned int>(nblk), FIN_NT, 0, s>>>(table, P.slots, total, full, scratch,
-                                                                          max_groups, out_keys, *out, gate);
+  table_compact_kernel<<<grid, FIN_NT, 0, s>>>(table, P.slots, total, full, scratch, max_groups, out_keys, *out,
+                                               gate);
   cudaError_t e = cudaGetLastError();
   if (e == cudaSuccess) *launches += 3;
   return e;

@@ -4,13 +4,17 @@ Low cardinality (dense keys): every shard reduces its rows to a mergeable per-gr
 state table (``Context.groupby_dense_state``), the tables are all-gathered and folded
 in rank order (``Context.merge_states``) -- a few KB per GPU, latency-bound.
 
-High cardinality (int64 keys): every shard routes its rows to the owner of their key
-(``Context.hash_partition``, a stable partition with the filter and expression applied),
-one all-to-all moves each owner's rows to it (senders concatenated in rank order, so
-every key's rows keep their global order), and the owner groups what it received
-(``Context.groupby_hash``).  The result is sharded by owner.  Raw rows are shipped
-rather than per-shard partial tables: with 2^28 distinct keys a shard's partial table
-is about as large as its rows, and the owner's table is 1/world of the full one.
+High cardinality (int64 keys): every shard routes its rows to the owner of their key,
+one all-to-all moves each owner's rows to it, and the owner groups what it received.  The
+result is sharded by owner.  Raw rows are shipped rather than per-shard partial tables:
+with 2^28 distinct keys a shard's partial table is about as large as its rows.
+  * count / sum / mean: the routing is the radix path's first pass (``Context.radix_route``:
+    rows as (fmix64(key), value) ordered by the top 8 hash bits, digit d owned by rank
+    d * world // 256; an f32 column travels as f32, 12 bytes a row), and the owner runs the
+    remaining passes on what it received (``Context.radix_groupby_routed``).
+  * other outputs (extrema, variances): a stable owner partition (``Context.hash_partition``,
+    senders concatenated in rank order, so every key's rows keep their global order and the
+    +-0 tie rule of the extrema stays exact) and ``Context.groupby_hash`` on the owner.
 
 The collective calls take any ``torch.distributed`` group, so the same code runs on
 gloo with CPU tensors in the CPU test suite.
@@ -128,12 +132,20 @@ class PeerShardedDenseGroupby:
         self.close()
 
 
+RADIX_FIELDS = ("count", "sum", "mean")
+
+
+def owned_digits(world: int):
+    """First hash digit owned by each rank, world + 1 entries: rank r owns [lo[r], lo[r + 1])."""
+    return [(256 * r + world - 1) // world for r in range(world + 1)]
+
+
 class ShardedHashGroupby:
     """Owner-sharded int64-key groupby of one shard's rows (see the module docstring).
 
-    ``ctx`` is a ``winrapids_b200.Context`` (or an object with the same ``hash_partition`` /
-    ``groupby_hash_into`` methods).  Buffers are allocated once for shards of up to
-    ``max_rows`` rows, receive buffers with ``recv_slack`` headroom over an even share.
+    ``ctx`` is a ``winrapids_b200.Context`` (or an object with the same methods).  Buffers
+    are allocated once for shards of up to ``max_rows`` rows, receive buffers with
+    ``recv_slack`` headroom over an even share.
     """
 
     def __init__(self, ctx, dist, world: int, max_rows: int, max_groups_per_owner: int, fields, device,
@@ -141,29 +153,88 @@ class ShardedHashGroupby:
         import torch
 
         self.ctx, self.dist, self.world, self.group = ctx, dist, int(world), group
+        self.rank = dist.get_rank(group) if group is not None else dist.get_rank()
+        self.device = device
+        self.max_rows = int(max_rows)
         self.max_groups = int(max_groups_per_owner)
-        cap = int(max_rows * recv_slack) + 4096
-        self.part_keys = torch.empty(max_rows, dtype=torch.int64, device=device)
-        self.part_vals = torch.empty(max_rows, dtype=torch.float64, device=device)
-        self.part_counts = torch.zeros(self.world, dtype=torch.int64, device=device)
-        self.recv_keys = torch.empty(cap, dtype=torch.int64, device=device)
-        self.recv_vals = torch.empty(cap, dtype=torch.float64, device=device)
+        self.cap = int(max_rows * recv_slack) + 4096
+        self.radix = set(fields) <= set(RADIX_FIELDS)
         self.out_keys = torch.empty(self.max_groups, dtype=torch.int64, device=device)
         self.out = {f: torch.empty(self.max_groups, dtype=torch.float64, device=device) for f in fields}
         self.n_groups = torch.zeros(1, dtype=torch.int64, device=device)
         self.n_recv = 0
+        self.value_bytes = 8
+        self._vdtype = None
+        if not self.radix:
+            self.part_keys = torch.empty(max_rows, dtype=torch.int64, device=device)
+            self.part_vals = torch.empty(max_rows, dtype=torch.float64, device=device)
+            self.part_counts = torch.zeros(self.world, dtype=torch.int64, device=device)
+            self.recv_keys = torch.empty(self.cap, dtype=torch.int64, device=device)
+            self.recv_vals = torch.empty(self.cap, dtype=torch.float64, device=device)
+        else:
+            self.lo = owned_digits(self.world)
+            self.n_digits = self.lo[self.rank + 1] - self.lo[self.rank]
+            self.digit_counts = torch.zeros(256, dtype=torch.int64, device=device)
+            self.seg_counts = torch.zeros(self.world * self.n_digits, dtype=torch.int64, device=device)
+            self.send_h = torch.empty(max_rows, dtype=torch.int64, device=device)
+            self.recv_h = torch.empty(self.cap, dtype=torch.int64, device=device)
+
+    def _value_buffers(self, vb):
+        import torch
+
+        dt = torch.float32 if vb == 4 else torch.float64
+        if self._vdtype != dt:
+            self.send_v = torch.empty(self.max_rows, dtype=dt, device=self.device)
+            self.recv_v = torch.empty(self.cap, dtype=dt, device=self.device)
+            self._vdtype = dt
+            self.value_bytes = vb
 
     def step(self, keys, a, b=None, c=None, expr: str = "a", pred=None, threshold: float = 0.0, mask=None):
         """Route, exchange and group one shard; results stay in self.out_keys / self.out (the
         first self.n_groups entries)."""
-        if keys.numel() > self.part_keys.numel():
+        if keys.numel() > self.max_rows:
             raise ValueError("shard larger than the buffers")
-        self.ctx.hash_partition(keys, a, self.world, self.part_keys, self.part_vals, self.part_counts, b=b, c=c,
-                                expr=expr, pred=pred, threshold=threshold, mask=mask)
-        self.n_recv = exchange_parts(self.dist, self.part_keys, self.part_vals, self.part_counts, self.recv_keys,
-                                     self.recv_vals, group=self.group)
-        self.ctx.groupby_hash_into(self.recv_keys[:self.n_recv], self.recv_vals[:self.n_recv], self.max_groups,
-                                   self.out_keys, self.out, self.n_groups)
+        if not self.radix:
+            self.ctx.hash_partition(keys, a, self.world, self.part_keys, self.part_vals, self.part_counts, b=b, c=c,
+                                    expr=expr, pred=pred, threshold=threshold, mask=mask)
+            self.n_recv = exchange_parts(self.dist, self.part_keys, self.part_vals, self.part_counts, self.recv_keys,
+                                         self.recv_vals, group=self.group)
+            self.ctx.groupby_hash_into(self.recv_keys[:self.n_recv], self.recv_vals[:self.n_recv], self.max_groups,
+                                       self.out_keys, self.out, self.n_groups)
+            return
+        self._value_buffers(self.ctx.radix_value_bytes(a, b, c, expr, pred, threshold))
+        self.ctx.radix_route(keys, a, self.send_h, self.send_v, self.digit_counts, b=b, c=c, expr=expr, pred=pred,
+                             threshold=threshold, mask=mask)
+        self.n_recv = self._exchange()
+        self.ctx.radix_groupby_routed(self.recv_h, self.recv_v, self.seg_counts, self.world, self.lo[self.rank],
+                                      self.n_digits, self.n_recv, self.max_groups, self.out_keys, self.out,
+                                      self.n_groups)
+
+    def _exchange(self) -> int:
+        """Digit counts to their owners, then the rows (senders concatenated in rank order, each
+        sender's block in digit order).  Every rank takes the same collective steps; a rank whose
+        receive buffers are too small makes every rank raise before the rows move."""
+        import torch
+
+        dist, g, lo = self.dist, self.group, self.lo
+        nd = [lo[r + 1] - lo[r] for r in range(self.world)]
+        dist.all_to_all_single(self.seg_counts, self.digit_counts, [self.n_digits] * self.world, nd, group=g)
+        dc = self.digit_counts.cpu().tolist()
+        s = [int(sum(dc[lo[r]:lo[r + 1]])) for r in range(self.world)]
+        rc = self.seg_counts.view(self.world, self.n_digits).sum(1).cpu().tolist()
+        r = [int(x) for x in rc]
+        n_send, n_recv = sum(s), sum(r)
+        fits = torch.tensor([1 if n_recv <= self.cap else 0], dtype=torch.int64, device=self.digit_counts.device)
+        dist.all_reduce(fits, op=dist.ReduceOp.MIN, group=g)
+        if int(fits.item()) == 0:
+            raise RuntimeError(f"receive buffers too small on some rank (this rank needs {n_recv} rows)")
+        dist.all_to_all_single(self.recv_h[:n_recv], self.send_h[:n_send], r, s, group=g)
+        dist.all_to_all_single(self.recv_v[:n_recv], self.send_v[:n_send], r, s, group=g)
+        return n_recv
+
+    @property
+    def recv_bytes_per_row(self) -> int:
+        return 8 + (self.value_bytes if self.radix else 8)
 
     def result(self):
         """(keys, {field: values}) of the groups this rank owns (host synchronisation)."""
