@@ -664,6 +664,12 @@ class HashJob:
     def check(self, dev_in, dist, world):
         return hash_check(self, dev_in, dist, world)
 
+    def extra(self, args) -> dict:
+        """Whether the last timed step's radix passes fell back to the global table (0: no)."""
+        if "rx_" not in self.kernel:
+            return {}
+        return {"radix_fallback": self.ctx.radix_fallback()}
+
     def kernel_bytes(self) -> int:
         # the shard's columns (one GPU) or the received rows (hash and value, or key and f64 value)
         return self.n_local * self.bpr if self.sharded is None else self.sharded.n_recv * self.sharded.recv_bytes_per_row

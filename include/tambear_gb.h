@@ -396,6 +396,14 @@ tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, const uint64_t* d_hashes, c
                                       int64_t* d_out_keys, const tbgb_moments* out, int64_t* d_n_groups,
                                       void* stream);
 
+/* Diagnostic: whether the last radix-partitioned call on `ctx` (table mode 5, or mode 0 choosing
+ * it; or tbgb_radix_groupby_routed) recomputed its result with the global table.  Waits for the
+ * device, then *bits = 0 (it did not) or an OR of 1 (a bucket outgrew its region: keys with very
+ * many rows), 2 (a bucket held more distinct keys than its shared-memory table), 4 (one key had
+ * more rows in a bucket than a slot counts).  Valid until the next groupby call on `ctx`; 0 when
+ * no radix call was made.  No counterpart in the reference. */
+tbgb_status tbgb_radix_fallback(tbgb_ctx* ctx, uint32_t* bits);
+
 /* Strategy for groupbys the shared-memory column kernel cannot take alone (int64 keys,
  * more than 512 dense groups, filter / expression / f32 columns): 0 = choose by size
  * (default: dense keys take group ranges in shared memory while at most 8 ranges cover

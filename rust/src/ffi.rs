@@ -237,6 +237,7 @@ extern "C" {
                                n: i64, n_parts: i32, out_keys: *mut i64, out_vals: *mut f64,
                                part_counts: *mut i64, stream: *mut c_void) -> tbgb_status;
     pub fn tbgb_radix_value_bytes(cols: *const tbgb_columns) -> i32;
+    pub fn tbgb_radix_fallback(ctx: *mut tbgb_ctx, bits: *mut u32) -> tbgb_status;
     pub fn tbgb_radix_route(ctx: *mut tbgb_ctx, keys: *const i64, cols: *const tbgb_columns, mask: *const u64,
                             n: i64, out_hashes: *mut u64, out_vals: *mut c_void, digit_counts: *mut i64,
                             stream: *mut c_void) -> tbgb_status;

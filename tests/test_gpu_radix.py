@@ -2,7 +2,8 @@
 many rows over a large key space) through the C ABI, against the oracle: plain f32 and f64
 columns, mask + predicate + expression, edge keys and non-finite values, empty input, the
 fallback to the global table when a bucket overflows its region (a heavy key, and crafted keys
-whose hashes share their top 16 bits), and TABLE_FULL when the keys outnumber max_groups."""
+whose hashes share their top 17 bits), and TABLE_FULL when the keys outnumber max_groups.  Every
+call reports whether it fell back (tbgb_radix_fallback): the ordinary cases must not."""
 import numpy as np
 import pytest
 
@@ -45,15 +46,19 @@ def unfmix64_np(h):
     return x.view(np.int64)
 
 
-def run(ctx, keys, a, max_groups, **kw):
+def run(ctx, keys, a, max_groups, fallback=0, **kw):
+    """The radix groupby; `fallback`: the fallback bits the call must report (0: the radix passes
+    produced the result themselves)."""
     import winrapids_b200 as wb
 
     ctx.set_table_mode("radix")
     try:
         gk, out = ctx.groupby_hash(dev(keys), dev(a) if not hasattr(a, "cuda") else a, max_groups,
                                    fields=wb.SUMCOUNT_FIELDS, **kw)
+        bits = ctx.radix_fallback()
     finally:
         ctx.set_table_mode("auto")
+    assert bits == fallback, f"fallback bits {bits}, expected {fallback}"
     return gk.cpu().numpy(), {f: t.cpu().numpy() for f, t in out.items()}
 
 
@@ -85,7 +90,7 @@ def test_f64_values_plain_with_nonfinite_and_edge_keys(ctx):
     n = 3_000_000
     keys = rng.integers(-2**62, 2**62, n).astype(np.int64)
     pool = np.array([np.iinfo(np.int64).min, np.iinfo(np.int64).max, 0, -1, 1], dtype=np.int64)
-    pick = rng.random(n) < 0.2
+    pick = rng.random(n) < 1e-4  # about 60 rows of each edge key: present, but no heavy hitter
     keys[pick] = pool[rng.integers(0, pool.size, pick.sum())]
     vals = rng.normal(size=n)
     vals[rng.random(n) < 0.02] = np.nan
@@ -134,22 +139,23 @@ def test_heavy_key_overflows_a_first_pass_bucket(ctx):
     keys = oracle.gen_keys_ids(n, ids, SALT, 11)
     keys[np.random.default_rng(1).random(n) < 0.6] = 424242
     vals = oracle.gen_values_normal(n, 0.0, 1.0, 11)
-    gk, got = run(ctx, keys, vals, ids)
+    gk, got = run(ctx, keys, vals, ids, fallback=1)
     compare(gk, got, keys, vals, np.ones(n, bool), "heavy key")
 
 
 def test_crafted_hashes_overflow_a_final_bucket(ctx):
-    """6,000 distinct keys whose hashes share their top 16 bits (plus ordinary keys): their final
-    bucket outgrows its region in the second pass; the global table recomputes the result."""
+    """1,500 distinct keys (two rows each) whose hashes share their top 17 bits, among ordinary keys:
+    their first-pass bucket still fits its region, their final bucket does not (second pass); the
+    global table recomputes the result."""
     rng = np.random.default_rng(12)
     n_ord = 2_000_000
     ordinary = oracle.gen_keys_ids(n_ord, 1 << 20, SALT, 12)
-    low = rng.choice(1 << 40, 6000, replace=False).astype(np.uint64)
-    crafted = unfmix64_np((np.uint64(0xABCD) << np.uint64(48)) | low)
-    assert np.all((fmix64_np(crafted) >> np.uint64(48)) == 0xABCD)
+    low = rng.choice(1 << 40, 1500, replace=False).astype(np.uint64)
+    crafted = unfmix64_np((np.uint64(0x1ABCD) << np.uint64(47)) | low)
+    assert np.all((fmix64_np(crafted) >> np.uint64(47)) == 0x1ABCD)
     keys = np.concatenate([ordinary, crafted, crafted])
     vals = rng.normal(size=keys.size)
-    gk, got = run(ctx, keys, vals, 1 << 21)
+    gk, got = run(ctx, keys, vals, 1 << 21, fallback=1)
     compare(gk, got, keys, vals, np.ones(keys.size, bool), "crafted")
 
 

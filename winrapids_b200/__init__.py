@@ -331,6 +331,13 @@ class Context:
                                                 int(n_parts), _ptr(out_keys), _ptr(out_vals), _ptr(part_counts),
                                                 _stream_handle(stream)))
 
+    def radix_fallback(self) -> int:
+        """Bits of the last radix call's fallback to the global table (0: none); see
+        tbgb_radix_fallback.  Waits for the device."""
+        bits = C.c_uint32(0)
+        self._check(self._L.tbgb_radix_fallback(self._h, C.byref(bits)))
+        return int(bits.value)
+
     def radix_value_bytes(self, a, b=None, c=None, expr: str = "a", pred: str | None = None,
                           threshold: float = 0.0) -> int:
         """Bytes per value of routed rows: 4 (an f32 column without expression) or 8."""

@@ -116,6 +116,7 @@ def lib() -> C.CDLL:
         "tbgb_set_table_mode": (st, [vp, C.c_int]),
         "tbgb_hash_partition": (st, [vp, vp, C.POINTER(Columns), vp, i64, i32, vp, vp, vp, vp]),
         "tbgb_radix_value_bytes": (i32, [C.POINTER(Columns)]),
+        "tbgb_radix_fallback": (st, [vp, C.POINTER(C.c_uint32)]),
         "tbgb_radix_route": (st, [vp, vp, C.POINTER(Columns), vp, i64, vp, vp, vp, vp]),
         "tbgb_radix_groupby_routed": (st, [vp, vp, vp, i32, vp, i32, i32, i32, i64, i64, vp, C.POINTER(Moments),
                                            vp, vp]),
@@ -173,7 +174,7 @@ HEADER_SYMBOLS = (
     "tbgb_tile_stats_build", "tbgb_tile_skip_mask", "tbgb_mask_skip_tiles", "tbgb_fused_bin_stats",
     "tbgb_exchange_bytes", "tbgb_exchange_alloc", "tbgb_exchange_free", "tbgb_peer_export", "tbgb_peer_import",
     "tbgb_peer_close", "tbgb_groupby_dense_sharded", "tbgb_radix_value_bytes", "tbgb_radix_route",
-    "tbgb_radix_groupby_routed",
+    "tbgb_radix_groupby_routed", "tbgb_radix_fallback",
 )
 
 # tbgb_bin_stats field order

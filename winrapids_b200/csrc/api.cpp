@@ -35,6 +35,7 @@ struct tbgb_ctx {
   int table_mode = 0;    // tbgb_set_table_mode
   bool profile = false;  // record events around main kernels
   std::vector<std::pair<cudaEvent_t, cudaEvent_t>> events;
+  const uint32_t* radix_gate = nullptr;  // fallback word of the last radix call (inside ws)
 };
 
 namespace {
@@ -139,7 +140,7 @@ tbgb_status profile_events(tbgb_ctx* ctx, cudaEvent_t* e0, cudaEvent_t* e1) {
 
 tbgb_status dense_common(tbgb_ctx* ctx, const int32_t* keys, const double* vals, const uint64_t* mask, int64_t n,
                          int32_t G, int64_t row_offset, const tbgb_moments* out, double* state_out, void* stream,
-                         bool state_m34 = true) {
+                         bool state_m34 = true, const tbgb::PushArgs* push = nullptr) {
   tbgb_status st = check_dense_args(ctx, keys, vals, n, G);
   if (st != TBGB_OK) return st;
   DeviceGuard dg(ctx->device);
@@ -157,7 +158,7 @@ tbgb_status dense_common(tbgb_ctx* ctx, const int32_t* keys, const double* vals,
   st = profile_events(ctx, &e0, &e1);
   if (st != TBGB_OK) return st;
   e = tbgb::dense_moments_launch(L, keys, vals, mask, n, row_offset, G, w.part, w.spill, w.zfirst, ctx->err, out,
-                                 state_out, s, &ctx->launches, e0, e1, w.live, state_m34);
+                                 state_out, s, &ctx->launches, e0, e1, w.live, state_m34, push);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "dense groupby launch", e);
   return TBGB_OK;
 }
@@ -216,6 +217,7 @@ tbgb_status radix_hash(tbgb_ctx* ctx, const int64_t* keys, const tbgb_columns* c
   uint32_t* gate = nullptr;
   cudaError_t e = tbgb::radix_groupby(R, ra, ctx->ws, &gate, s, &ctx->launches, e0, e1);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "radix groupby launch", e);
+  ctx->radix_gate = gate;
   char* w = static_cast<char*>(ctx->ws) + tbgb::radix_t2_offset(R);
   unsigned long long* T = reinterpret_cast<unsigned long long*>(w);
   unsigned long long* fin = reinterpret_cast<unsigned long long*>(w + align256(P.table_bytes));
@@ -707,12 +709,22 @@ tbgb_status tbgb_groupby_dense_sharded(tbgb_ctx* ctx, const int32_t* d_keys, con
                                                tbgb::exchange_slot_offset(world, n_groups, parity, rank));
   // this shard's state table, written straight into its slot of the own buffer (without the
   // third and fourth moments unless `out` asks for them: the merge of the others never reads them)
-  tbgb_status st = dense_state(ctx, d_keys, d_vals, d_mask, n, n_groups, row_offset, own_slot, stream,
-                               out->m3 != nullptr || out->m4 != nullptr);
-  if (st != TBGB_OK) return st;
+  const bool m34 = out->m3 != nullptr || out->m4 != nullptr;
+  cudaError_t e = cudaSuccess;
   DeviceGuard dg(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
-  cudaError_t e = tbgb::exchange_push_launch(peers, world, rank, n_groups, epoch, s, &ctx->launches);
+  if (n_groups <= tbgb::kDenseMaxGroups) {
+    // the column kernel's fold stores the table into every peer's slot and raises the flags
+    const tbgb::PushArgs push = tbgb::exchange_push_args(peers, world, rank, n_groups, epoch);
+    if (row_offset < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "row_offset must be >= 0");
+    tbgb_status st = dense_common(ctx, d_keys, d_vals, d_mask, n, n_groups, row_offset, nullptr, own_slot, stream,
+                                  m34, &push);
+    if (st != TBGB_OK) return st;
+  } else {
+    tbgb_status st = dense_state(ctx, d_keys, d_vals, d_mask, n, n_groups, row_offset, own_slot, stream, m34);
+    if (st != TBGB_OK) return st;
+    e = tbgb::exchange_push_launch(peers, world, rank, n_groups, epoch, s, &ctx->launches);
+  }
   if (e == cudaSuccess)
     e = tbgb::exchange_merge_launch(h_exchange[rank], world, n_groups, epoch, ctx->err, out, s, &ctx->launches);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "exchange launch", e);
@@ -1128,6 +1140,7 @@ tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, const uint64_t* d_hashes, c
   uint32_t* gate = nullptr;
   cudaError_t e = tbgb::radix_groupby_routed(R, r, ctx->ws, &gate, s, &ctx->launches, e0, e1);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "routed radix groupby launch", e);
+  ctx->radix_gate = gate;
   // fallback (gated): group the hashes themselves in the global table, then turn them into keys
   char* w = static_cast<char*>(ctx->ws) + tbgb::radix_t2_offset(R);
   unsigned long long* T = reinterpret_cast<unsigned long long*>(w);
@@ -1153,6 +1166,17 @@ tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, const uint64_t* d_hashes, c
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback table finalize", e);
   e = tbgb::radix_unhash_keys(d_out_keys, d_n_groups, max_groups, gate, ctx->num_sms, s, &ctx->launches);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback key launch", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_radix_fallback(tbgb_ctx* ctx, uint32_t* bits) {
+  if (!ctx || !bits) return TBGB_ERR_INVALID_ARGUMENT;
+  *bits = 0;
+  if (!ctx->radix_gate) return TBGB_OK;
+  DeviceGuard dg(ctx->device);
+  cudaError_t e = cudaDeviceSynchronize();
+  if (e == cudaSuccess) e = cudaMemcpy(bits, ctx->radix_gate, sizeof(uint32_t), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_TRANSFER, "reading the radix fallback word", e);
   return TBGB_OK;
 }
 

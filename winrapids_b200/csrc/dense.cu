@@ -38,6 +38,7 @@
 
 #include "common.cuh"
 #include "dense.cuh"
+#include "exchange.cuh"
 #include "gstate.cuh"
 
 namespace tbgb {
@@ -412,6 +413,19 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   const long long nbatch = mytiles + (has_tail ? 1 : 0);
   unsigned long long* sp = a.spill + static_cast<size_t>(b) * spill_fields<M34>() * G;
 
+  // Unmasked staged launches: the first tiles' bulk copies leave before the rest of the setup
+  // (the mbarriers first), so the ring fills while the counters and spill states are cleared.
+  constexpr bool EARLY = TMA && !MASKED;
+  if (EARLY && tid == PRODUCER_WARP * 32) {
+    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], SCATTER_WARPS); }
+    mbar_fence_init();
+    for (int s = 0; s < STAGES && s < mytiles; ++s) {
+      unsigned char* st = smem + static_cast<size_t>(s) * STAGE_BYTES;
+      mbar_arrive_expect_tx(&full[s], KEY_BYTES + VAL_BYTES);
+      bulk_g2s(st, a.keys + (t_begin + s) * TILE, KEY_BYTES, &full[s]);
+      bulk_g2s(st + KEY_BYTES, a.vals + (t_begin + s) * TILE, VAL_BYTES, &full[s]);
+    }
+  }
   for (int i = tid; i < 2 * gp; i += NT) cnt0[i] = 0;
   if (tid < 4) splc[tid] = 0;
   for (int g = tid; g < G; g += NT) {
@@ -429,7 +443,8 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     }
   }
   if (tid == 0) {
-    for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], SCATTER_WARPS); }
+    if (!EARLY)
+      for (int s = 0; s < STAGES; ++s) { mbar_init(&full[s], 1); mbar_init(&empty[s], SCATTER_WARPS); }
     for (int s = 0; s < 2; ++s) { mbar_init(&colfull[s], SCATTER_WARPS); mbar_init(&colempty[s], NOW / 32); }
     static_assert(TEAMS == 1, "one owner team sweeps both column buffers");
     *abort = 0;
@@ -518,7 +533,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
       }
     } else if (TMA && lane == 0) {
       long long issued = 0;
-      for (int s = 0; s < STAGES && s < mytiles; ++s) issue(s, t_begin + s);
+      // the first STAGES tiles were issued before the setup (EARLY)
       issued = mytiles < STAGES ? mytiles : STAGES;
       for (long long j = STAGES; j < STAGES + PF_AHEAD && j < mytiles; ++j) prefetch(t_begin + j);
       bool failed = false;
@@ -818,11 +833,16 @@ __device__ __forceinline__ GState spill_state(const unsigned long long* sp, int 
 // dependent merges and ran 2-4 times longer.
 constexpr int FOLD_NT = 256;
 
+__device__ __forceinline__ void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+  asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 __global__ void __launch_bounds__(FOLD_NT) dense_fold_kernel(const double* __restrict__ part,
                                                              const unsigned long long* __restrict__ spill, int P,
                                                              int G, int opg,
                                                              const unsigned long long* __restrict__ zfirst,
-                                                             tbgb_moments out, double* state_out, int m34) {
+                                                             tbgb_moments out, double* state_out, int m34,
+                                                             PushArgs push) {
   __shared__ GState warp_state[FOLD_NT / 32];
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int g = blockIdx.x;
@@ -871,6 +891,24 @@ __global__ void __launch_bounds__(FOLD_NT) dense_fold_kernel(const double* __res
     A.zf = zfirst[g];
     if (state_out) gstate_store(state_out, G, g, A);
     else gstate_finalize(A, g, out);
+    warp_state[0] = A;
+  }
+  if (push.world > 0) {
+    // the fused exchange: the group's state goes straight into this rank's slot of every peer
+    // (plain stores over NVLink; thread q stores into peer q), then the last block to finish
+    // raises this rank's flag in every buffer
+    __syncthreads();
+    if (threadIdx.x < push.world && threadIdx.x != push.rank) gstate_store(push.slot[threadIdx.x], G, g, warp_state[0]);
+    __threadfence_system();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      const unsigned int done = atomicAdd(push.counter, 1u);
+      if (done == static_cast<unsigned int>(gridDim.x) - 1u) {
+        __threadfence_system();
+        for (int q = 0; q < push.world; ++q) st_release_sys_u64(push.flag[q], push.epoch);
+        *push.counter = 0u;  // the next step's fold (stream-ordered after this one) counts from zero
+      }
+    }
   }
 }
 
@@ -989,7 +1027,7 @@ cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, cons
                                  long long n, long long row_offset, int G, double* part, unsigned long long* spill,
                                  unsigned long long* zfirst, uint32_t* err, const tbgb_moments* out, double* state_out,
                                  cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start, cudaEvent_t ev_stop,
-                                 unsigned* live_scratch, bool state_m34) {
+                                 unsigned* live_scratch, bool state_m34, const PushArgs* push) {
   DenseArgs a;
   a.keys = keys; a.vals = vals; a.mask = mask; a.n = n; a.row_offset = row_offset;
   a.G = G; a.C = L.C; a.opg = L.opg; a.slots = L.slots;
@@ -1025,7 +1063,10 @@ cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, cons
   if (ev_stop) cudaEventRecord(ev_stop, stream);
   (*launches)++;
   tbgb_moments o = out ? *out : tbgb_moments{};
-  dense_fold_kernel<<<G, FOLD_NT, 0, stream>>>(part, spill, L.grid, G, L.opg, zfirst, o, state_out, m34 ? 1 : 0);
+  PushArgs pa{};
+  if (push && state_out) pa = *push;
+  dense_fold_kernel<<<G, FOLD_NT, 0, stream>>>(part, spill, L.grid, G, L.opg, zfirst, o, state_out, m34 ? 1 : 0,
+                                               pa);
   e = cudaGetLastError();
   if (e == cudaSuccess) (*launches)++;
   return e;

@@ -42,12 +42,15 @@ size_t dense_smem_bytes(int G, int C);
 // Enqueue the dense moments pipeline.  `part` holds part_doubles, `spill`
 // spill_words u64, `zfirst` G u64, `err` one u32.  Writes either final outputs (`out`) or, when `state_out` is not
 // NULL, the merged state table of this call (ST_COUNT * G doubles).
+struct PushArgs;
 cudaError_t dense_moments_launch(const DenseLaunch& L, const int32_t* keys, const double* vals, const uint64_t* mask,
                                  long long n, long long row_offset, int G, double* part, unsigned long long* spill,
                                  unsigned long long* zfirst, uint32_t* err, const tbgb_moments* out, double* state_out,
                                  cudaStream_t stream, uint64_t* launches, cudaEvent_t ev_start = nullptr,
                                  cudaEvent_t ev_stop = nullptr, unsigned* live_scratch = nullptr,
-                                 bool state_m34 = true);
+                                 bool state_m34 = true, const PushArgs* push = nullptr);
+// push (nullable, with state_out): the fold also stores the state table into the same slot of
+// every peer's exchange buffer and its last block raises this rank's flag there (exchange.cuh).
 // state_m34 = false: the state table's m3 / m4 are left at zero (cheaper kernel) for callers
 // whose final outputs need neither.
 // Scratch of the live-tile list of a masked launch over n rows (u32 words).

@@ -102,7 +102,27 @@ size_t exchange_flags_offset(int world, int G) {
 }
 
 size_t exchange_bytes(int world, int G) {
-  return exchange_flags_offset(world, G) + round256(static_cast<size_t>(world) * 8);
+  return exchange_flags_offset(world, G) + round256(static_cast<size_t>(world + 1) * 8);
+}
+
+PushArgs exchange_push_args(const PeerPtrs& peers, int world, int rank, int G, unsigned long long epoch) {
+  PushArgs a{};
+  const int parity = static_cast<int>(epoch & 1ull);
+  const size_t slot_off = exchange_slot_offset(world, G, parity, rank);
+  const size_t flags_off = exchange_flags_offset(world, G);
+  for (int q = 0; q < world; ++q) {
+    char* base = static_cast<char*>(peers.p[q]);
+    a.slot[q] = reinterpret_cast<double*>(base + slot_off);
+    a.flag[q] = reinterpret_cast<unsigned long long*>(base + flags_off) + rank;
+  }
+  // the word after the world flags of the own buffer (inside its 256-byte rounding; zeroed at
+  // allocation, and returned to zero by the block that uses it)
+  a.counter = reinterpret_cast<unsigned int*>(reinterpret_cast<unsigned long long*>(
+      static_cast<char*>(peers.p[rank]) + flags_off) + world);
+  a.world = world;
+  a.rank = rank;
+  a.epoch = epoch;
+  return a;
 }
 
 cudaError_t exchange_push_launch(const PeerPtrs& peers, int world, int rank, int G, unsigned long long epoch,

@@ -14,6 +14,19 @@ struct PeerPtrs {
   void* p[kMaxRanks];
 };
 
+// The fold kernel's push into the peers (the fused exchange): where this rank's slot lies in
+// every buffer (its own included), every buffer's flag of this rank, and a block counter in the
+// own buffer (the last block to finish raises the flags).  world == 0: no push.
+struct PushArgs {
+  double* slot[kMaxRanks];
+  unsigned long long* flag[kMaxRanks];
+  unsigned int* counter;
+  int world;
+  int rank;
+  unsigned long long epoch;
+};
+PushArgs exchange_push_args(const PeerPtrs& peers, int world, int rank, int G, unsigned long long epoch);
+
 // Doubles of one rank's slot (a state table of G groups).
 long long exchange_slot_words(int G);
 // Bytes of an exchange buffer: [2 parities][world slots] state tables, then world u64 flags.

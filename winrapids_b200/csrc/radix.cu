@@ -28,6 +28,7 @@
 // crates/tambear/src/group_index.rs:117-204, i32 codes only); the outputs follow the same
 // semantics as the global table: count = non-NaN rows, sum = sum of finite values, mean =
 // sum / count (NaN when count is 0), and a key whose rows are all NaN is a group of count 0.
+#include <cmath>
 #include <cstdint>
 #include <type_traits>
 
@@ -121,11 +122,12 @@ struct RxScatter {
   const unsigned long long* out_base;  // nullable: first row of each destination bucket
   const unsigned long long* out_cap;   // with out_base: rows of each destination bucket
   uint32_t* fallback;
+  int prefetch;                // tile starts are 16-byte aligned: prefetch the next tile into L2
 };
 
 template <bool VF32>
 constexpr size_t scatter_smem() {
-  return static_cast<size_t>(RX_TILE) * (8 + (VF32 ? 4 : 8) + 2);
+  return static_cast<size_t>(RX_TILE) * 16;  // one 16-byte (hash, value) entry a row
 }
 
 // SRC: 0 = the caller's key and value columns as they are, 1 = the caller's columns with mask /
@@ -137,9 +139,9 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
   constexpr int ND = 1 << DBITS;  // destination digits of this pass
   static_assert(ND <= RX_NT, "one thread per digit in phase B");
   extern __shared__ __align__(16) unsigned char rx_sm[];
-  unsigned long long* sh_h = reinterpret_cast<unsigned long long*>(rx_sm);
-  VT* sh_v = reinterpret_cast<VT*>(sh_h + RX_TILE);
-  unsigned short* sh_d = reinterpret_cast<unsigned short*>(sh_v + RX_TILE);
+  // the tile reordered by bucket: one 16-byte entry a row (hash, value), written and read with one
+  // vector access each; the bucket is recomputed from the hash when the runs are written out
+  uint4* sh_row = reinterpret_cast<uint4*>(rx_sm);
   __shared__ unsigned int hist[ND];
   __shared__ unsigned int lstart[ND];
   __shared__ unsigned int wlim[ND];
@@ -279,22 +281,52 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
       if (rk[j] >> 31) {
         const unsigned d = (rk[j] >> 16) & DMASK;
         const unsigned p = lstart[d] + (rk[j] & 0xFFFFu);
-        sh_h[p] = hv[j];
-        sh_v[p] = vv[j];
-        sh_d[p] = static_cast<unsigned short>(d);
+        uint4 e;
+        e.x = static_cast<unsigned>(hv[j]);
+        e.y = static_cast<unsigned>(hv[j] >> 32);
+        if constexpr (VF32) {
+          e.z = __float_as_uint(vv[j]);
+          e.w = 0u;
+        } else {
+          const unsigned long long vb = static_cast<unsigned long long>(__double_as_longlong(vv[j]));
+          e.z = static_cast<unsigned>(vb);
+          e.w = static_cast<unsigned>(vb >> 32);
+        }
+        sh_row[p] = e;
       }
     }
     __syncthreads();
 
+    // the next tile of this CTA streams into L2 while this one is written out (issued here, where
+    // the row registers are free); a partial tile at the end of the rows or of a segment is not
+    // prefetched (tile starts are 16-byte aligned: checked on the host)
+    if (a.prefetch && tid == 0) {
+      const long long tn = t + gridDim.x;
+      const long long full_end = SRC == 2 ? __ldg(a.seg_tiles + seg + 1) - 1 : a.n / RX_TILE;
+      if (tn < full_end) {
+        const long long r0 = row0 + static_cast<long long>(gridDim.x) * RX_TILE;  // same segment
+        if constexpr (SRC == 2) {
+          bulk_prefetch_l2(a.src_h + r0, RX_TILE * 8);
+          bulk_prefetch_l2(src_v + r0, RX_TILE * sizeof(VT));
+        } else {
+          bulk_prefetch_l2(a.keys + r0, RX_TILE * 8);
+          bulk_prefetch_l2(static_cast<const VT*>(a.cols.a) + r0, RX_TILE * sizeof(VT));
+        }
+      }
+    }
+
     // ---- phase D: write each bucket's run (consecutive threads, consecutive addresses)
     const unsigned int tot = tile_total;
     for (unsigned int p = tid; p < tot; p += RX_NT) {
-      const unsigned d = sh_d[p];
+      const uint4 e = sh_row[p];
+      const unsigned long long h = (static_cast<unsigned long long>(e.y) << 32) | e.x;
+      const unsigned d = SRC == 2 ? static_cast<unsigned>(h >> a.shift) & DMASK : static_cast<unsigned>(h >> (64 - DBITS));
       const unsigned i = p - lstart[d];
       if (i < wlim[d]) {
         const unsigned long long dst = gdst[d] + i;
-        a.dst_h[dst] = sh_h[p];
-        dst_v[dst] = sh_v[p];
+        a.dst_h[dst] = h;
+        if constexpr (VF32) dst_v[dst] = __uint_as_float(e.z);
+        else dst_v[dst] = __longlong_as_double(static_cast<long long>((static_cast<unsigned long long>(e.w) << 32) | e.z));
       }
     }
     // the next tile's first barrier orders these reads before lstart / gdst / sh_* change
@@ -543,11 +575,23 @@ size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 unsigned long long round16(unsigned long long x) { return (x + 15) / 16 * 16; }
 
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Rows of a bucket's region: its even share e plus slack.  A bucket's rows arrive in clumps (all
+// rows of a key land in one bucket), so its row count varies with the keys' multiplicity, not
+// only as a Poisson count of rows: with about 7.5 rows a key the standard deviation is about
+// 2.9 sqrt(e) (360 rows on a final bucket of 15,300).  40 sqrt(e) is ten deviations for keys of up
+// to about 15 rows each; heavier keys overflow into the fallback.
+unsigned long long bucket_cap(unsigned long long e, unsigned long long margin) {
+  return round16(e + static_cast<unsigned long long>(40.0 * std::sqrt(static_cast<double>(e))) + margin);
+}
+
 template <int SRC, bool VF32, bool F32IN>
 cudaError_t launch_scatter(const RxScatter& s, int grid, cudaStream_t st) {
   auto k = rx_scatter_kernel<SRC, VF32, F32IN, SRC == 2 ? D2_BITS : D1_BITS>;
   constexpr size_t smem = scatter_smem<VF32>();
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e != cudaSuccess) return e;
   k<<<grid, RX_NT, smem, st>>>(s);
   return cudaGetLastError();
@@ -558,6 +602,7 @@ cudaError_t launch_agg(const RxAgg& g, int grid, cudaStream_t st) {
   auto k = rx_agg_kernel<VF32>;
   constexpr size_t smem = agg_smem();
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e != cudaSuccess) return e;
   k<<<grid, AGG_NT, smem, st>>>(g);
   return cudaGetLastError();
@@ -571,6 +616,7 @@ int agg_blocks_per_sm(bool vf32) {
     const size_t smem = agg_smem();
     auto k = vf32 ? rx_agg_kernel<true> : rx_agg_kernel<false>;
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+    if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e == cudaSuccess) e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&v, k, AGG_NT, smem);
     c = (e == cudaSuccess && v > 0) ? v : 1;
   }
@@ -609,8 +655,8 @@ RadixPlan radix_plan(const tbgb_columns& cols, long long n, int num_sms) {
   P.vf32 = cols.dtype == TBGB_F32 && cols.expr == TBGB_EXPR_A;
   const unsigned long long rows = static_cast<unsigned long long>(n > 0 ? n : 0);
   const unsigned long long e1 = rows / kRadixDigits, e2 = rows / kRadixBuckets;
-  P.cap1 = round16(e1 + e1 / 16 + 4096);
-  P.cap2 = round16(e2 + e2 / 16 + 512);
+  P.cap1 = bucket_cap(e1, 4096);
+  P.cap2 = bucket_cap(e2, 256);
   const size_t row_bytes = 8 + (P.vf32 ? 4 : 8);
   P.t1_bytes = align256(static_cast<size_t>(P.cap1) * kRadixDigits * 8) +
                align256(static_cast<size_t>(P.cap1) * kRadixDigits * (row_bytes - 8));
@@ -651,6 +697,7 @@ cudaError_t radix_groupby(const RadixPlan& P, const RadixArgs& a, void* ws, uint
   p1.fallback = &x->fallback;
   const bool plain = a.mask == nullptr && a.cols.pred == TBGB_PRED_NONE && a.cols.expr == TBGB_EXPR_A;
   const bool f32in = a.cols.dtype == TBGB_F32;
+  p1.prefetch = plain && aligned16(a.keys) && aligned16(a.cols.a);
   if (a.n > 0) {
     if (plain) e = f32in ? launch_scatter<0, true, true>(p1, P.grid_scatter, s)
                          : launch_scatter<0, false, false>(p1, P.grid_scatter, s);
@@ -679,6 +726,7 @@ cudaError_t radix_groupby(const RadixPlan& P, const RadixArgs& a, void* ws, uint
   p2.cursor = x->cur2;
   p2.cap = P.cap2;
   p2.fallback = &x->fallback;
+  p2.prefetch = 1;  // segment starts are multiples of 16 rows into 256-byte aligned buffers
   if (a.n > 0) {
     e = P.vf32 ? launch_scatter<2, true, true>(p2, P.grid_scatter, s)
                : launch_scatter<2, false, false>(p2, P.grid_scatter, s);
@@ -733,6 +781,7 @@ cudaError_t radix_route(const RadixArgs& a, unsigned long long* out_h, void* out
   const bool plain = a.mask == nullptr && a.cols.pred == TBGB_PRED_NONE && a.cols.expr == TBGB_EXPR_A;
   const bool f32in = a.cols.dtype == TBGB_F32;
   const bool vf32 = radix_value_f32(a.cols);
+  p1.prefetch = plain && aligned16(a.keys) && aligned16(a.cols.a);
   if (a.n > 0) {
     long long blocks = (a.n + RX_NT - 1) / RX_NT;
     const long long cap = static_cast<long long>(num_sms) * 4;
@@ -766,7 +815,7 @@ RadixPlan radix_routed_plan(bool vf32, long long n_rows, int n_digits, int num_s
   const unsigned long long nb = static_cast<unsigned long long>(n_digits) << D2_BITS;
   const unsigned long long e2 = rows / nb;
   P.cap1 = 0;
-  P.cap2 = round16(e2 + e2 / 16 + 512);
+  P.cap2 = bucket_cap(e2, 256);
   const size_t vb = vf32 ? 4 : 8;
   P.t1_bytes = 0;
   P.t2_bytes = align256(static_cast<size_t>(P.cap2) * nb * 8) + align256(static_cast<size_t>(P.cap2) * nb * vb);
@@ -806,6 +855,7 @@ cudaError_t radix_groupby_routed(const RadixPlan& P, const RoutedArgs& r, void* 
   p2.cursor = x->cur2;
   p2.cap = P.cap2;
   p2.fallback = &x->fallback;
+  p2.prefetch = 0;  // received segments start anywhere
   if (r.n_rows > 0) {
     e = P.vf32 ? launch_scatter<2, true, true>(p2, P.grid_scatter, s)
                : launch_scatter<2, false, false>(p2, P.grid_scatter, s);
