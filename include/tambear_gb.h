@@ -399,8 +399,8 @@ tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, const uint64_t* d_hashes, c
 /* Diagnostic: whether the last radix-partitioned call on `ctx` (table mode 5, or mode 0 choosing
  * it; or tbgb_radix_groupby_routed) recomputed its result with the global table.  Waits for the
  * device, then *bits = 0 (it did not) or an OR of 1 (a bucket outgrew its region: keys with very
- * many rows), 2 (a bucket held more distinct keys than its shared-memory table), 4 (one key had
- * more rows in a bucket than a slot counts).  Valid until the next groupby call on `ctx`; 0 when
+ * many rows), 2 (a bucket held more distinct keys than its shared-memory table), 4 (the call had
+ * so many rows that a bucket could outgrow a slot's 17-bit count: more than about 10^10).  Valid until the next groupby call on `ctx`; 0 when
  * no radix call was made.  No counterpart in the reference. */
 tbgb_status tbgb_radix_fallback(tbgb_ctx* ctx, uint32_t* bits);
 

@@ -53,8 +53,8 @@ constexpr int AGG_NT = 512;                    // threads per aggregation CTA
 constexpr int AGG_SLOTS = 4096;                // shared-memory table slots per bucket
 constexpr int AGG_MAX_PROBE = 512;             // probes before a row gives up (fallback)
 constexpr int AGG_UNROLL = 2;
-// A free slot.  A used slot never equals it: its count stays below kCntMask - 1 (a key with
-// more rows in one bucket sends the call to the fallback).
+// A free slot.  A used slot never equals it: its count stays below kCntMask (a bucket region
+// never holds kCntMask rows: larger calls go to the fallback before the passes).
 constexpr unsigned long long kFree = ~0ull;
 constexpr unsigned int kPrefetchChunk = 32768;
 static_assert(kRadixBuckets == (1 << BUCKET_BITS), "bucket count");
@@ -151,9 +151,8 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
   constexpr unsigned int DMASK = ND - 1;
 
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-  if constexpr (SRC == 2) {
-    if (*reinterpret_cast<volatile const uint32_t*>(a.fallback)) return;  // pass 1 overflowed
-  }
+  // an earlier pass overflowed, or the call was sent to the fallback before the passes
+  if (*reinterpret_cast<volatile const uint32_t*>(a.fallback)) return;
   if (tid < ND) hist[tid] = 0;
   const long long ntiles = SRC == 2 ? a.seg_tiles[a.n_seg] : (a.n + RX_TILE - 1) / RX_TILE;
   const VT* src_v = static_cast<const VT*>(a.src_v);
@@ -502,10 +501,10 @@ __global__ void __launch_bounds__(AGG_NT, 3) rx_agg_kernel(RxAgg a) {
             }
           }
           if ((w >> CNT_BITS) == key) {
-            if (inc) {
-              const unsigned long long old = atomicAdd(tk + slot, 1ull);
-              if ((old & kCntMask) >= kCntMask - 2) atomicOr(a.fallback, 4u);  // count field nearly full
-            }
+            // no key has more rows in a bucket than the bucket holds (cap < kCntMask, checked when
+            // the call is planned), so the count field cannot carry into the key: the add needs
+            // no result
+            if (inc) atomicAdd(tk + slot, 1ull);
             found = static_cast<int>(slot);
             break;
           }
@@ -683,6 +682,10 @@ cudaError_t radix_groupby(const RadixPlan& P, const RadixArgs& a, void* ws, uint
   *fallback = &x->fallback;
   cudaError_t e = cudaMemsetAsync(x, 0, sizeof(Aux), s);
   if (e != cudaSuccess) return e;
+  // a bucket region longer than a slot's count field could carry into the key bits: such calls
+  // (more than about 1.7e10 rows) go to the fallback before the passes
+  if (P.cap2 >= kCntMask) e = cudaMemsetAsync(&x->fallback, 4, 1, s);
+  if (e != cudaSuccess) return e;
   if (ev0) cudaEventRecord(ev0, s);
 
   RxScatter p1{};
@@ -834,6 +837,8 @@ cudaError_t radix_groupby_routed(const RadixPlan& P, const RoutedArgs& r, void* 
   void* t2v = w + radix_t2_offset(P) + align256(static_cast<size_t>(P.cap2) * nb * 8);
   *fallback = &x->fallback;
   cudaError_t e = cudaMemsetAsync(x, 0, sizeof(Aux), s);
+  if (e != cudaSuccess) return e;
+  if (P.cap2 >= kCntMask) e = cudaMemsetAsync(&x->fallback, 4, 1, s);  // as in radix_groupby
   if (e != cudaSuccess) return e;
   if (ev0) cudaEventRecord(ev0, s);
   const int n_seg = r.n_senders * r.n_digits;
