@@ -368,15 +368,15 @@ tbgb_status tbgb_hash_partition(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb
 
 /* ---- owner-sharded high-cardinality groupby (count / sum / mean) -------------------------
  * No counterpart in the reference (single GPU, host-side GroupIndex::build,
- * crates/tambear/src/group_index.rs:117-204).  Rows are routed by the top 8 bits of
- * h = fmix64(key) (MurmurHash3's 64-bit finaliser, a bijection): digit d = h >> 56 belongs to rank
- * d * world / 256, so each rank owns a contiguous digit range [ceil(256 r / world),
- * ceil(256 (r + 1) / world)).
+ * crates/tambear/src/group_index.rs:117-204).  Rows are routed by the top 9 bits of
+ * h = fmix64(key) (MurmurHash3's 64-bit finaliser, a bijection): digit d = h >> 55 belongs to rank
+ * d * world / 512, so each rank owns a contiguous digit range [ceil(512 r / world),
+ * ceil(512 (r + 1) / world)).
  *
  * tbgb_radix_route: the rows of this shard that pass mask and pred, written as (h, v) ordered by
  * digit (all rows of digit 0, then digit 1, ...; order inside a digit unspecified), v = expr(a, b,
  * c) in f64, or the f32 column itself when the columns are f32 without expression
- * (tbgb_radix_value_bytes: 4 or 8 bytes per value).  d_digit_counts (256 int64, device) receives
+ * (tbgb_radix_value_bytes: 4 or 8 bytes per value).  d_digit_counts (512 int64, device) receives
  * the rows of each digit; the output buffers hold n rows.  The rows for rank r are then one
  * contiguous run, ready for an all-to-all.
  *
@@ -399,8 +399,7 @@ tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, const uint64_t* d_hashes, c
 /* Diagnostic: whether the last radix-partitioned call on `ctx` (table mode 5, or mode 0 choosing
  * it; or tbgb_radix_groupby_routed) recomputed its result with the global table.  Waits for the
  * device, then *bits = 0 (it did not) or an OR of 1 (a bucket outgrew its region: keys with very
- * many rows), 2 (a bucket held more distinct keys than its shared-memory table), 4 (the call had
- * so many rows that a bucket could outgrow a slot's 17-bit count: more than about 10^10).  Valid until the next groupby call on `ctx`; 0 when
+ * many rows) or 2 (a bucket held more distinct keys than its shared-memory table).  Valid until the next groupby call on `ctx`; 0 when
  * no radix call was made.  No counterpart in the reference. */
 tbgb_status tbgb_radix_fallback(tbgb_ctx* ctx, uint32_t* bits);
 

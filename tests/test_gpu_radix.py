@@ -2,7 +2,7 @@
 many rows over a large key space) through the C ABI, against the oracle: plain f32 and f64
 columns, mask + predicate + expression, edge keys and non-finite values, empty input, the
 fallback to the global table when a bucket overflows its region (a heavy key, and crafted keys
-whose hashes share their top 17 bits), and TABLE_FULL when the keys outnumber max_groups.  Every
+whose hashes share their top 18 bits), and TABLE_FULL when the keys outnumber max_groups.  Every
 call reports whether it fell back (tbgb_radix_fallback): the ordinary cases must not."""
 import numpy as np
 import pytest
@@ -144,15 +144,15 @@ def test_heavy_key_overflows_a_first_pass_bucket(ctx):
 
 
 def test_crafted_hashes_overflow_a_final_bucket(ctx):
-    """1,500 distinct keys (two rows each) whose hashes share their top 17 bits, among ordinary keys:
+    """1,500 distinct keys (two rows each) whose hashes share their top 18 bits, among ordinary keys:
     their first-pass bucket still fits its region, their final bucket does not (second pass); the
     global table recomputes the result."""
     rng = np.random.default_rng(12)
     n_ord = 2_000_000
     ordinary = oracle.gen_keys_ids(n_ord, 1 << 20, SALT, 12)
     low = rng.choice(1 << 40, 1500, replace=False).astype(np.uint64)
-    crafted = unfmix64_np((np.uint64(0x1ABCD) << np.uint64(47)) | low)
-    assert np.all((fmix64_np(crafted) >> np.uint64(47)) == 0x1ABCD)
+    crafted = unfmix64_np((np.uint64(0x2ABCD) << np.uint64(46)) | low)
+    assert np.all((fmix64_np(crafted) >> np.uint64(46)) == 0x2ABCD)
     keys = np.concatenate([ordinary, crafted, crafted])
     vals = rng.normal(size=keys.size)
     gk, got = run(ctx, keys, vals, 1 << 21, fallback=1)

@@ -50,8 +50,8 @@ def unfmix64_np(h):
 
 
 def radix_owner_np(keys, P):
-    d = (fmix64_np(keys) >> np.uint64(56)).astype(np.int64)
-    return d * P // 256
+    d = (fmix64_np(keys) >> np.uint64(55)).astype(np.int64)
+    return d * P // 512
 
 
 def owner_np(keys, P):
@@ -94,17 +94,17 @@ class FakeCtx:
     def radix_route(self, keys, a, out_hashes, out_vals, digit_counts, b=None, c=None, expr="a", pred=None,
                     threshold=0.0, mask=None):
         h = fmix64_np(keys.numpy())
-        d = (h >> np.uint64(56)).astype(np.int64)
+        d = (h >> np.uint64(55)).astype(np.int64)
         order = np.argsort(d, kind="stable")
         m = h.size
         out_hashes[:m] = torch.from_numpy(h[order].view(np.int64))
         out_vals[:m] = a[torch.from_numpy(order)]
-        digit_counts[:] = torch.from_numpy(np.bincount(d, minlength=256).astype(np.int64))
+        digit_counts[:] = torch.from_numpy(np.bincount(d, minlength=512).astype(np.int64))
 
     def radix_groupby_routed(self, hashes, vals, seg_counts, n_senders, digit_lo, n_digits, n_rows, max_groups,
                              out_keys, out, n_groups):
         h = hashes[:n_rows].numpy().view(np.uint64)
-        d = (h >> np.uint64(56)).astype(np.int64)
+        d = (h >> np.uint64(55)).astype(np.int64)
         assert np.all((d >= digit_lo) & (d < digit_lo + n_digits)), "a row routed to a rank that does not own it"
         # the blocks are in sender order, each in digit order, with the announced sizes
         sizes = seg_counts.numpy().reshape(n_senders, n_digits)

@@ -346,7 +346,7 @@ class Context:
     def radix_route(self, keys, a, out_hashes, out_vals, digit_counts, b=None, c=None, expr: str = "a",
                     pred: str | None = None, threshold: float = 0.0, mask=None, stream=None):
         """Enqueue the owner routing of this shard's rows (see tbgb_radix_route): rows as
-        (fmix64(key), value) ordered by the top 8 hash bits; digit_counts (256 int64) per digit."""
+        (fmix64(key), value) ordered by the top 9 hash bits; digit_counts (512 int64) per digit."""
         cols = self.columns(a, b, c, expr, pred, threshold)
         self._check(self._L.tbgb_radix_route(self._h, _ptr(keys), C.byref(cols), _ptr(mask), int(keys.numel()),
                                              _ptr(out_hashes), _ptr(out_vals), _ptr(digit_counts),

@@ -4,13 +4,14 @@
 // the TLB's reach: every row then pays a random DRAM sector and a TLB miss.  Here the rows are
 // instead moved twice, in streaming passes, until each bucket's keys fit one CTA's shared
 // memory:
-//   pass 1  rows -> 256 buckets by the top 8 bits of h = fmix64(key)   (mask, predicate and
+//   pass 1  rows -> 512 buckets by the top 9 bits of h = fmix64(key)   (mask, predicate and
 //           expression applied here; rows that fail them are dropped)
-//   pass 2  each of those -> 512 buckets by the next 9 bits            (131,072 buckets)
-//   pass 3  one CTA per bucket: a shared-memory table of 4,096 slots keyed by the low 47 bits of
-//           h (the top 17 are the bucket) takes the bucket's rows, then writes its groups.  A
-//           slot is two words: (key47 << 17 | count) and the f64 sum, so a row costs one probe
-//           read, one 64-bit atomic and one f64 add; 64 KB a table lets three CTAs share an SM.
+//   pass 2  each of those -> 512 buckets by the next 9 bits            (262,144 buckets)
+//   pass 3  one CTA per bucket: a shared-memory table of 2,048 slots keyed by the low 46 bits of
+//           h (the top 18 are the bucket) takes the bucket's rows, then writes its groups.  A
+//           slot is the key (claimed by a 64-bit compare-and-swap), a u32 count and an f64 sum:
+//           a row costs one probe read, one 32-bit add and one f64 add; 40 KB a table lets four
+//           CTAs share an SM.
 // fmix64 (MurmurHash3's finaliser) is a bijection, so the rows carry h instead of the key and
 // pass 3 recovers each group's key by inverting it.  A row is (h, value): 12 bytes for an f32
 // column without an expression, 16 otherwise.
@@ -43,20 +44,15 @@ namespace {
 constexpr int RX_NT = 512;                     // threads per scatter CTA
 constexpr int RX_TILE = 4096;                  // rows per scatter tile
 constexpr int RX_PER = RX_TILE / RX_NT;        // rows per thread per tile
-constexpr int D1_BITS = 8, D2_BITS = 9;        // digits of pass 1 and pass 2
-constexpr int BUCKET_BITS = D1_BITS + D2_BITS;  // final buckets: the top 17 bits of h
-constexpr int KEY_BITS = 64 - BUCKET_BITS;      // bits of h a table slot keeps (47)
-constexpr int CNT_BITS = 64 - KEY_BITS;         // count field of a slot word (17)
-constexpr unsigned long long kCntMask = (1ull << CNT_BITS) - 1;
+constexpr int D1_BITS = 9, D2_BITS = 9;        // digits of pass 1 and pass 2
+constexpr int BUCKET_BITS = D1_BITS + D2_BITS;  // final buckets: the top 18 bits of h
+constexpr int KEY_BITS = 64 - BUCKET_BITS;      // bits of h a table slot keeps (46)
 constexpr unsigned long long kKeyMask = (1ull << KEY_BITS) - 1;
 constexpr int AGG_NT = 512;                    // threads per aggregation CTA
-constexpr int AGG_SLOTS = 4096;                // shared-memory table slots per bucket
+constexpr int AGG_SLOTS = 2048;                // shared-memory table slots per bucket
 constexpr int AGG_MAX_PROBE = 512;             // probes before a row gives up (fallback)
 constexpr int AGG_UNROLL = 2;
-// A free slot.  A used slot never equals it: its count stays below kCntMask (a bucket region
-// never holds kCntMask rows: larger calls go to the fallback before the passes).
-constexpr unsigned long long kFree = ~0ull;
-constexpr unsigned int kPrefetchChunk = 32768;
+constexpr unsigned long long kFree = ~0ull;  // a free slot (never a 46-bit key)
 static_assert(kRadixBuckets == (1 << BUCKET_BITS), "bucket count");
 static_assert(kRadixDigits == (1 << D1_BITS), "first-pass digits");
 
@@ -122,7 +118,6 @@ struct RxScatter {
   const unsigned long long* out_base;  // nullable: first row of each destination bucket
   const unsigned long long* out_cap;   // with out_base: rows of each destination bucket
   uint32_t* fallback;
-  int prefetch;                // tile starts are 16-byte aligned: prefetch the next tile into L2
 };
 
 template <bool VF32>
@@ -296,24 +291,6 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
     }
     __syncthreads();
 
-    // the next tile of this CTA streams into L2 while this one is written out (issued here, where
-    // the row registers are free); a partial tile at the end of the rows or of a segment is not
-    // prefetched (tile starts are 16-byte aligned: checked on the host)
-    if (a.prefetch && tid == 0) {
-      const long long tn = t + gridDim.x;
-      const long long full_end = SRC == 2 ? __ldg(a.seg_tiles + seg + 1) - 1 : a.n / RX_TILE;
-      if (tn < full_end) {
-        const long long r0 = row0 + static_cast<long long>(gridDim.x) * RX_TILE;  // same segment
-        if constexpr (SRC == 2) {
-          bulk_prefetch_l2(a.src_h + r0, RX_TILE * 8);
-          bulk_prefetch_l2(src_v + r0, RX_TILE * sizeof(VT));
-        } else {
-          bulk_prefetch_l2(a.keys + r0, RX_TILE * 8);
-          bulk_prefetch_l2(static_cast<const VT*>(a.cols.a) + r0, RX_TILE * sizeof(VT));
-        }
-      }
-    }
-
     // ---- phase D: write each bucket's run (consecutive threads, consecutive addresses)
     const unsigned int tot = tile_total;
     for (unsigned int p = tid; p < tot; p += RX_NT) {
@@ -367,7 +344,7 @@ __global__ void __launch_bounds__(RX_NT) rx_count_kernel(RxScatter a) {
       if (!eval_pred(a.cols.pred, load_val<F32IN>(a.cols.a, row), a.cols.threshold)) continue;
     }
     const unsigned long long h = fmix64(static_cast<unsigned long long>(__ldcs(a.keys + row)));
-    atomicAdd(hist + (h >> 56), 1u);
+    atomicAdd(hist + (h >> (64 - D1_BITS)), 1u);
   }
   __syncthreads();
   if (tid < kRadixDigits && hist[tid]) atomicAdd(a.cursor + tid, static_cast<unsigned long long>(hist[tid]));
@@ -432,14 +409,15 @@ struct RxAgg {
   uint32_t* fallback;
 };
 
-constexpr size_t agg_smem() { return static_cast<size_t>(AGG_SLOTS) * (8 + 8); }
+constexpr size_t agg_smem() { return static_cast<size_t>(AGG_SLOTS) * (8 + 8 + 4); }
 
 template <bool VF32>
 __global__ void __launch_bounds__(AGG_NT, 3) rx_agg_kernel(RxAgg a) {
   using VT = typename std::conditional<VF32, float, double>::type;
   extern __shared__ __align__(16) unsigned char ag_sm[];
-  unsigned long long* tk = reinterpret_cast<unsigned long long*>(ag_sm);  // key47 << 17 | count
+  unsigned long long* tk = reinterpret_cast<unsigned long long*>(ag_sm);  // key (low 46 bits of h)
   double* ts = reinterpret_cast<double*>(tk + AGG_SLOTS);                 // sum of finite values
+  unsigned int* tc = reinterpret_cast<unsigned int*>(ts + AGG_SLOTS);     // non-NaN rows
   __shared__ unsigned int wcount[AGG_NT / 32];
   __shared__ unsigned long long gbase;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -450,25 +428,10 @@ __global__ void __launch_bounds__(AGG_NT, 3) rx_agg_kernel(RxAgg a) {
     const unsigned long long base = static_cast<unsigned long long>(b) * a.cap;
     unsigned long long rows = a.cursor[b];
     if (rows > a.cap) rows = a.cap;
-    // the next bucket of this CTA streams into L2 while this one is reduced
-    const int nb = b + gridDim.x;
-    if (nb < a.n_buckets && warp == 0) {
-      unsigned long long nrows = a.cursor[nb];
-      if (nrows > a.cap) nrows = a.cap;
-      const unsigned long long nbase = static_cast<unsigned long long>(nb) * a.cap;
-      const unsigned long long hb = (nrows * 8 + 15) & ~15ull, vb = (nrows * sizeof(VT) + 15) & ~15ull;
-      const char* hp = reinterpret_cast<const char*>(a.src_h + nbase);
-      const char* vp = reinterpret_cast<const char*>(src_v + nbase);
-      for (unsigned long long o = static_cast<unsigned long long>(lane) * kPrefetchChunk; o < hb;
-           o += 32ull * kPrefetchChunk)
-        bulk_prefetch_l2(hp + o, static_cast<uint32_t>(hb - o < kPrefetchChunk ? hb - o : kPrefetchChunk));
-      for (unsigned long long o = static_cast<unsigned long long>(lane) * kPrefetchChunk; o < vb;
-           o += 32ull * kPrefetchChunk)
-        bulk_prefetch_l2(vp + o, static_cast<uint32_t>(vb - o < kPrefetchChunk ? vb - o : kPrefetchChunk));
-    }
     for (int i = tid; i < AGG_SLOTS; i += AGG_NT) {
       tk[i] = kFree;
       ts[i] = 0.0;
+      tc[i] = 0u;
     }
     __syncthreads();
     for (unsigned long long p0 = 0; p0 < rows; p0 += static_cast<unsigned long long>(AGG_NT) * AGG_UNROLL) {
@@ -486,25 +449,13 @@ __global__ void __launch_bounds__(AGG_NT, 3) rx_agg_kernel(RxAgg a) {
       for (int u = 0; u < AGG_UNROLL; ++u) {
         const unsigned long long p = p0 + static_cast<unsigned long long>(u) * AGG_NT + tid;
         if (p >= rows) continue;
-        const double v = vv[u];
-        const unsigned long long inc = is_nan(v) ? 0ull : 1ull;  // a NaN row makes its group, uncounted
         const unsigned long long key = hv[u] & kKeyMask;
         unsigned int slot = static_cast<unsigned int>(hv[u]) & (AGG_SLOTS - 1);
         int found = -1;
         for (int probe = 0; probe < AGG_MAX_PROBE; ++probe) {
           unsigned long long w = tk[slot];
-          if (w == kFree) {
-            w = atomicCAS(tk + slot, kFree, (key << CNT_BITS) | inc);
-            if (w == kFree) {
-              found = static_cast<int>(slot);
-              break;
-            }
-          }
-          if ((w >> CNT_BITS) == key) {
-            // no key has more rows in a bucket than the bucket holds (cap < kCntMask, checked when
-            // the call is planned), so the count field cannot carry into the key: the add needs
-            // no result
-            if (inc) atomicAdd(tk + slot, 1ull);
+          if (w == kFree) w = atomicCAS(tk + slot, kFree, key);
+          if (w == kFree || w == key) {  // claimed it, or found it
             found = static_cast<int>(slot);
             break;
           }
@@ -514,6 +465,8 @@ __global__ void __launch_bounds__(AGG_NT, 3) rx_agg_kernel(RxAgg a) {
           atomicOr(a.fallback, 2u);  // more distinct keys than the table takes: recompute elsewhere
           continue;
         }
+        const double v = vv[u];
+        if (!is_nan(v)) atomicAdd(tc + found, 1u);  // a NaN row makes its group, uncounted
         if (is_finite(v)) atomicAdd(ts + found, v);
       }
     }
@@ -546,9 +499,9 @@ __global__ void __launch_bounds__(AGG_NT, 3) rx_agg_kernel(RxAgg a) {
       if (occ) {
         const unsigned long long j = pos + __popc(bal & ((1u << lane) - 1u));
         if (j < static_cast<unsigned long long>(a.max_groups)) {
-          const double cnt = static_cast<double>(w & kCntMask);
+          const double cnt = static_cast<double>(tc[i]);
           const double sum = ts[i];
-          a.out_keys[j] = static_cast<int64_t>(unfmix64(top | (w >> CNT_BITS)));
+          a.out_keys[j] = static_cast<int64_t>(unfmix64(top | w));
           if (a.out.count) a.out.count[j] = cnt;
           if (a.out.sum) a.out.sum[j] = sum;
           if (a.out.mean) a.out.mean[j] = cnt > 0.0 ? sum / cnt : qnan();
@@ -574,12 +527,11 @@ size_t align256(size_t x) { return (x + 255) / 256 * 256; }
 
 unsigned long long round16(unsigned long long x) { return (x + 15) / 16 * 16; }
 
-bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
 // Rows of a bucket's region: its even share e plus slack.  A bucket's rows arrive in clumps (all
 // rows of a key land in one bucket), so its row count varies with the keys' multiplicity, not
 // only as a Poisson count of rows: with about 7.5 rows a key the standard deviation is about
-// 2.9 sqrt(e) (360 rows on a final bucket of 15,300).  40 sqrt(e) is ten deviations for keys of up
+// 2.9 sqrt(e) (250 rows on a final bucket of 7,600 at 2^28 keys of 7.5 rows).  40 sqrt(e) is ten deviations for keys of up
 // to about 15 rows each; heavier keys overflow into the fallback.
 unsigned long long bucket_cap(unsigned long long e, unsigned long long margin) {
   return round16(e + static_cast<unsigned long long>(40.0 * std::sqrt(static_cast<double>(e))) + margin);
@@ -682,10 +634,6 @@ cudaError_t radix_groupby(const RadixPlan& P, const RadixArgs& a, void* ws, uint
   *fallback = &x->fallback;
   cudaError_t e = cudaMemsetAsync(x, 0, sizeof(Aux), s);
   if (e != cudaSuccess) return e;
-  // a bucket region longer than a slot's count field could carry into the key bits: such calls
-  // (more than about 1.7e10 rows) go to the fallback before the passes
-  if (P.cap2 >= kCntMask) e = cudaMemsetAsync(&x->fallback, 4, 1, s);
-  if (e != cudaSuccess) return e;
   if (ev0) cudaEventRecord(ev0, s);
 
   RxScatter p1{};
@@ -700,7 +648,6 @@ cudaError_t radix_groupby(const RadixPlan& P, const RadixArgs& a, void* ws, uint
   p1.fallback = &x->fallback;
   const bool plain = a.mask == nullptr && a.cols.pred == TBGB_PRED_NONE && a.cols.expr == TBGB_EXPR_A;
   const bool f32in = a.cols.dtype == TBGB_F32;
-  p1.prefetch = plain && aligned16(a.keys) && aligned16(a.cols.a);
   if (a.n > 0) {
     if (plain) e = f32in ? launch_scatter<0, true, true>(p1, P.grid_scatter, s)
                          : launch_scatter<0, false, false>(p1, P.grid_scatter, s);
@@ -729,7 +676,6 @@ cudaError_t radix_groupby(const RadixPlan& P, const RadixArgs& a, void* ws, uint
   p2.cursor = x->cur2;
   p2.cap = P.cap2;
   p2.fallback = &x->fallback;
-  p2.prefetch = 1;  // segment starts are multiples of 16 rows into 256-byte aligned buffers
   if (a.n > 0) {
     e = P.vf32 ? launch_scatter<2, true, true>(p2, P.grid_scatter, s)
                : launch_scatter<2, false, false>(p2, P.grid_scatter, s);
@@ -784,7 +730,6 @@ cudaError_t radix_route(const RadixArgs& a, unsigned long long* out_h, void* out
   const bool plain = a.mask == nullptr && a.cols.pred == TBGB_PRED_NONE && a.cols.expr == TBGB_EXPR_A;
   const bool f32in = a.cols.dtype == TBGB_F32;
   const bool vf32 = radix_value_f32(a.cols);
-  p1.prefetch = plain && aligned16(a.keys) && aligned16(a.cols.a);
   if (a.n > 0) {
     long long blocks = (a.n + RX_NT - 1) / RX_NT;
     const long long cap = static_cast<long long>(num_sms) * 4;
@@ -838,8 +783,6 @@ cudaError_t radix_groupby_routed(const RadixPlan& P, const RoutedArgs& r, void* 
   *fallback = &x->fallback;
   cudaError_t e = cudaMemsetAsync(x, 0, sizeof(Aux), s);
   if (e != cudaSuccess) return e;
-  if (P.cap2 >= kCntMask) e = cudaMemsetAsync(&x->fallback, 4, 1, s);  // as in radix_groupby
-  if (e != cudaSuccess) return e;
   if (ev0) cudaEventRecord(ev0, s);
   const int n_seg = r.n_senders * r.n_digits;
   rx_routed_segments_kernel<<<1, 32, 0, s>>>(x, r.seg_counts, n_seg, r.n_digits);
@@ -860,7 +803,6 @@ cudaError_t radix_groupby_routed(const RadixPlan& P, const RoutedArgs& r, void* 
   p2.cursor = x->cur2;
   p2.cap = P.cap2;
   p2.fallback = &x->fallback;
-  p2.prefetch = 0;  // received segments start anywhere
   if (r.n_rows > 0) {
     e = P.vf32 ? launch_scatter<2, true, true>(p2, P.grid_scatter, s)
                : launch_scatter<2, false, false>(p2, P.grid_scatter, s);

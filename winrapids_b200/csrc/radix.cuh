@@ -9,15 +9,15 @@
 
 namespace tbgb {
 
-constexpr int kRadixDigits = 256;               // first-pass buckets (the top 8 hash bits)
-constexpr int kRadixBuckets = 131072;           // final buckets after the second pass (17 hash bits)
-constexpr long long kRadixMaxGroups = 1ll << 28;  // distinct keys one call serves (2048 per bucket)
+constexpr int kRadixDigits = 512;               // first-pass buckets (the top 9 hash bits)
+constexpr int kRadixBuckets = 262144;           // final buckets after the second pass (18 hash bits)
+constexpr long long kRadixMaxGroups = 1ll << 28;  // distinct keys one call serves (1024 per bucket)
 
 struct RadixPlan {
   bool vf32;                  // rows carry the value as f32 (an f32 column without expression)
   unsigned long long cap1;    // rows per first-pass bucket (slack over an even share)
   unsigned long long cap2;    // rows per final bucket
-  size_t t1_bytes;            // first-pass buffer: cap1 * 256 hashes + values
+  size_t t1_bytes;            // first-pass buffer: cap1 * 512 hashes + values
   size_t t2_bytes;            // final buffer: cap2 * 65536 hashes + values
   size_t aux_bytes;           // cursors, tile prefix, flags
   int grid_scatter;           // CTAs of the scatter passes
@@ -58,8 +58,8 @@ size_t radix_t2_offset(const RadixPlan& P);
 bool radix_value_f32(const tbgb_columns& cols);
 size_t radix_route_aux_bytes();
 // The first pass with exact placement (a counting pass first): the rows that pass mask and
-// predicate, as (h, v) ordered by the top 8 bits of h; digit_counts (256 int64, device) receives
-// the rows of each digit.  `aux` holds radix_route_aux_bytes().
+// predicate, as (h, v) ordered by the top 9 bits of h; digit_counts (kRadixDigits int64, device)
+// receives the rows of each digit.  `aux` holds radix_route_aux_bytes().
 cudaError_t radix_route(const RadixArgs& a, unsigned long long* out_h, void* out_v, int64_t* digit_counts, void* aux,
                         int num_sms, cudaStream_t s, uint64_t* launches);
 

@@ -9,8 +9,8 @@ one all-to-all moves each owner's rows to it, and the owner groups what it recei
 result is sharded by owner.  Raw rows are shipped rather than per-shard partial tables:
 with 2^28 distinct keys a shard's partial table is about as large as its rows.
   * count / sum / mean: the routing is the radix path's first pass (``Context.radix_route``:
-    rows as (fmix64(key), value) ordered by the top 8 hash bits, digit d owned by rank
-    d * world // 256; an f32 column travels as f32, 12 bytes a row), and the owner runs the
+    rows as (fmix64(key), value) ordered by the top 9 hash bits, digit d owned by rank
+    d * world // 512; an f32 column travels as f32, 12 bytes a row), and the owner runs the
     remaining passes on what it received (``Context.radix_groupby_routed``).
   * other outputs (extrema, variances): a stable owner partition (``Context.hash_partition``,
     senders concatenated in rank order, so every key's rows keep their global order and the
@@ -135,9 +135,12 @@ class PeerShardedDenseGroupby:
 RADIX_FIELDS = ("count", "sum", "mean")
 
 
+RADIX_DIGITS = 512  # first-pass digits of the radix path (the top 9 bits of the key's hash)
+
+
 def owned_digits(world: int):
     """First hash digit owned by each rank, world + 1 entries: rank r owns [lo[r], lo[r + 1])."""
-    return [(256 * r + world - 1) // world for r in range(world + 1)]
+    return [(RADIX_DIGITS * r + world - 1) // world for r in range(world + 1)]
 
 
 class ShardedHashGroupby:
@@ -174,7 +177,7 @@ class ShardedHashGroupby:
         else:
             self.lo = owned_digits(self.world)
             self.n_digits = self.lo[self.rank + 1] - self.lo[self.rank]
-            self.digit_counts = torch.zeros(256, dtype=torch.int64, device=device)
+            self.digit_counts = torch.zeros(RADIX_DIGITS, dtype=torch.int64, device=device)
             self.seg_counts = torch.zeros(self.world * self.n_digits, dtype=torch.int64, device=device)
             self.send_h = torch.empty(max_rows, dtype=torch.int64, device=device)
             self.recv_h = torch.empty(self.cap, dtype=torch.int64, device=device)
