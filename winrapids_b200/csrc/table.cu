@@ -281,7 +281,10 @@ struct LocalTable : SlotArrays<FULL> {
   }
 };
 
-template <bool KEY64, bool F32, bool FULL, bool LOCAL>
+// M34 / EXT: the m3 / m4 sums and the extrema (with the first-zero code) are compiled in only
+// where the call asks for them, which keeps the common bodies small (instruction fetch stalls
+// dominated a body that carried every path).
+template <bool KEY64, bool F32, bool FULL, bool LOCAL, bool M34, bool EXT>
 __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
   extern __shared__ __align__(16) unsigned char sm[];
   if (a.gate && *a.gate == 0u) return;
@@ -385,7 +388,7 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
       const long long grow = a.row_offset + base + r * TNT + tid;
       if constexpr (LOCAL) {
         if (ls[r] >= 0) {
-          if (!is_nan(v[r])) lt.row(ls[r], v[r], grow, a.m34 != 0, a.extrema != 0);
+          if (!is_nan(v[r])) lt.row(ls[r], v[r], grow, M34, EXT);
           continue;
         }
       }
@@ -397,7 +400,7 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
         gs = kk[r];
       }
       if (!is_nan(v[r]))
-        global_row<FULL>(T + static_cast<unsigned long long>(gs) * W, v[r], grow, a.m34 != 0, a.extrema != 0);
+        global_row<FULL>(T + static_cast<unsigned long long>(gs) * W, v[r], grow, M34, EXT);
     }
   }
 
@@ -414,7 +417,7 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
       } else {
         gs = static_cast<long long>(k);
       }
-      lt.flush(s, T + static_cast<unsigned long long>(gs) * W, a.m34 != 0, a.extrema != 0);
+      lt.flush(s, T + static_cast<unsigned long long>(gs) * W, M34, EXT);
     }
   }
 }
@@ -861,7 +864,12 @@ __global__ void __launch_bounds__(FIN_NT) table_compact_kernel(const unsigned lo
 
 template <bool KEY64, bool F32, bool FULL, bool LOCAL>
 cudaError_t launch_table(const TablePlan& P, const TableArgs& a, cudaStream_t s) {
-  auto k = table_kernel<KEY64, F32, FULL, LOCAL>;
+  auto k = table_kernel<KEY64, F32, FULL, LOCAL, false, false>;
+  if constexpr (FULL) {
+    if (a.m34 && a.extrema) k = table_kernel<KEY64, F32, FULL, LOCAL, true, true>;
+    else if (a.m34) k = table_kernel<KEY64, F32, FULL, LOCAL, true, false>;
+    else if (a.extrema) k = table_kernel<KEY64, F32, FULL, LOCAL, false, true>;
+  }
   if (P.smem > 0) {
     cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(P.smem));
     if (e != cudaSuccess) return e;
