@@ -99,6 +99,9 @@ def parse():
     ap.add_argument("--ids", type=int, default=None, help="override the distinct-id count of a hash workload")
     ap.add_argument("--table-mode", default="auto", choices=["auto", "local", "direct", "bucket", "range"],
                     help="global-table kernel: shared-memory pre-aggregation or direct atomics")
+    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
+                    help="multi-GPU high-cardinality exchange: stores into the owners' buffers over NVLink peer "
+                         "memory, or NCCL all-to-all")
     return ap.parse_args()
 
 
@@ -599,7 +602,8 @@ class DenseJob:
 
 class HashJob:
     """int64 keys through the hash table: `pipeline` (filter + expression, Zipf keys) and `highcard`
-    (f32 values, sum/count/mean; owner-sharded over NCCL all-to-all when world > 1)."""
+    (f32 values, sum/count/mean; owner-sharded when world > 1: rows routed by hash digit and stored
+    into the owners' buffers over NVLink peer memory)."""
 
     def __init__(self, ctx, wl, lo, hi, world, dist, dev):
         import torch
@@ -641,10 +645,17 @@ class HashJob:
             self.ng = torch.zeros(1, dtype=torch.int64, device=dev)
             self.sharded = None
         else:
-            from winrapids_b200.sharded import ShardedHashGroupby
+            from winrapids_b200.sharded import PeerMappingError, ShardedHashGroupby
 
             per_owner = int(ids / world * 1.05) + 4096
-            self.sharded = ShardedHashGroupby(ctx, dist, world, n, per_owner, self.fields, dev)
+            how = wl.get("exchange", "peer") if radix else "nccl"
+            try:
+                self.sharded = ShardedHashGroupby(ctx, dist, world, n, per_owner, self.fields, dev, exchange=how)
+                self.exchange = {"peer": "peer memory (routed rows stored into the owners' buffers over NVLink)",
+                                 "nccl": "NCCL all-to-all of the routed rows"}[how]
+            except PeerMappingError as exc:
+                self.sharded = ShardedHashGroupby(ctx, dist, world, n, per_owner, self.fields, dev)
+                self.exchange = f"NCCL all-to-all ({exc})"
             self.out_keys, self.out, self.ng = self.sharded.out_keys, self.sharded.out, self.sharded.n_groups
 
     def _cols(self, inputs):
@@ -1048,6 +1059,7 @@ def run_ours(args, wl, n_rows, world, rank, local_rank, dist):
     ctx = wb.Context(local_rank)
     ctx.set_table_mode(args.table_mode)
     wl["table_mode"] = args.table_mode
+    wl["exchange"] = args.exchange
     lo, hi = n_rows * rank // world, n_rows * (rank + 1) // world
     if wl["kind"] == "bins":
         wl["rows_total"] = n_rows

@@ -348,6 +348,19 @@ tbgb_status tbgb_exchange_free(tbgb_ctx* ctx, void* d_buf);
 tbgb_status tbgb_peer_export(tbgb_ctx* ctx, void* d_buf, uint8_t* handle /* 64 bytes */);
 tbgb_status tbgb_peer_import(tbgb_ctx* ctx, const uint8_t* handle /* 64 bytes */, void** d_peer);
 tbgb_status tbgb_peer_close(tbgb_ctx* ctx, void* d_peer);
+/* A device buffer of `bytes` in its own allocation, so that tbgb_peer_export's handle maps
+ * exactly it (e.g. the receive buffer of the owner-sharded groupby's rows); free with
+ * tbgb_ipc_free.  No counterpart in the reference (single GPU). */
+tbgb_status tbgb_ipc_alloc(tbgb_ctx* ctx, size_t bytes, void** d_buf);
+tbgb_status tbgb_ipc_free(tbgb_ctx* ctx, void* d_buf);
+/* Copies n <= 32 blocks: h_bytes[i] bytes from device address h_src[i] to h_dst[i] (host arrays
+ * of device pointers; a pointer may be a peer's buffer mapped by tbgb_peer_import, so one launch
+ * can scatter a shard's rows into every owner's receive buffer over NVLink with plain stores).
+ * Enqueued on `stream`; the kernel ends with a system-scope fence: once `stream` has been waited
+ * for, the peers see the data.  The caller orders the copies against the receivers' use of their
+ * buffers (e.g. a barrier).  No counterpart in the reference (single GPU). */
+tbgb_status tbgb_copy_blocks(tbgb_ctx* ctx, int32_t n, const void* const* h_src, void* const* h_dst,
+                             const int64_t* h_bytes, void* stream);
 tbgb_status tbgb_groupby_dense_sharded(tbgb_ctx* ctx, const int32_t* d_keys, const double* d_vals,
                                        const uint64_t* d_mask, int64_t n, int32_t n_groups, int64_t row_offset,
                                        int32_t rank, int32_t world, void* const* h_exchange, uint64_t epoch,

@@ -229,6 +229,10 @@ extern "C" {
     pub fn tbgb_peer_import(ctx: *mut tbgb_ctx, handle: *const u8 /* 64 bytes */, peer: *mut *mut c_void)
                             -> tbgb_status;
     pub fn tbgb_peer_close(ctx: *mut tbgb_ctx, peer: *mut c_void) -> tbgb_status;
+    pub fn tbgb_ipc_alloc(ctx: *mut tbgb_ctx, bytes: usize, buf: *mut *mut c_void) -> tbgb_status;
+    pub fn tbgb_ipc_free(ctx: *mut tbgb_ctx, buf: *mut c_void) -> tbgb_status;
+    pub fn tbgb_copy_blocks(ctx: *mut tbgb_ctx, n: i32, src: *const *const c_void, dst: *const *mut c_void,
+                            bytes: *const i64, stream: *mut c_void) -> tbgb_status;
     pub fn tbgb_groupby_dense_sharded(ctx: *mut tbgb_ctx, keys: *const i32, vals: *const f64, mask: *const u64,
                                       n: i64, n_groups: i32, row_offset: i64, rank: i32, world: i32,
                                       exchange: *const *mut c_void, epoch: u64, out: *const tbgb_moments,

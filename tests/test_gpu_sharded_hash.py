@@ -1,6 +1,7 @@
 """The owner-sharded int64-key groupby (winrapids_b200.sharded.ShardedHashGroupby) on two GPUs,
 one process each over NCCL: every rank routes its rows to the owner of their key, the parts cross
-NVLink in one all-to-all, and each owner groups what it received.  The union of the ranks' groups
+NVLink (one NCCL all-to-all, or one copy launch storing into the owners' buffers through peer
+memory), and each owner groups what it received.  The union of the ranks' groups
 must equal the oracle's groupby of all rows (each key on exactly one rank; counts bit-exact, sums
 within 1e-12 * sum|x|), for the high-cardinality shape (f32 values) and the fused pipeline shape
 (filter a > 0, v = a*b + c).  Needs two GPUs: skipped otherwise."""
@@ -35,7 +36,7 @@ def _inputs(shape, n):
     return keys, [oracle.gen_values_normal(n, 0.0, 1.0, 8 + j) for j in (1, 2, 3)]
 
 
-def _worker(rank, port, shape, q):
+def _worker(rank, port, shape, exchange, q):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     os.environ["NCCL_NVLS_ENABLE"] = "0"
@@ -56,20 +57,23 @@ def _worker(rank, port, shape, q):
         lo, hi = n * rank // WORLD, n * (rank + 1) // WORLD
         keys, cols = _inputs(shape, n)
         dcols = [torch.from_numpy(c[lo:hi]).cuda() for c in cols]
-        sh = ShardedHashGroupby(ctx, dist, WORLD, hi - lo, 1 << 20, wb.SUMCOUNT_FIELDS, f"cuda:{rank}")
+        sh = ShardedHashGroupby(ctx, dist, WORLD, hi - lo, 1 << 20, wb.SUMCOUNT_FIELDS, f"cuda:{rank}",
+                                exchange=exchange)
         kw = {} if shape == "highcard" else dict(b=dcols[1], c=dcols[2], expr="a*b+c", pred=">", threshold=0.0)
         for _ in range(2):  # the second step reuses every buffer
             sh.step(torch.from_numpy(keys[lo:hi]).cuda(), dcols[0], **kw)
         gk, out = sh.result()
         q.put((rank, gk.cpu().numpy(), {f: t.cpu().numpy() for f, t in out.items()}))
+        sh.finish()
         dist.barrier()
     finally:
         ctx.close()
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("exchange", ["nccl", "peer"])
 @pytest.mark.parametrize("shape", ["highcard", "pipeline"])
-def test_sharded_hash_groupby_matches_oracle(shape):
+def test_sharded_hash_groupby_matches_oracle(shape, exchange):
     import torch
     import torch.multiprocessing as mp
 
@@ -78,7 +82,7 @@ def test_sharded_hash_groupby_matches_oracle(shape):
     spawn = mp.get_context("spawn")
     q = spawn.Queue()
     port = free_port()
-    procs = [spawn.Process(target=_worker, args=(r, port, shape, q)) for r in range(WORLD)]
+    procs = [spawn.Process(target=_worker, args=(r, port, shape, exchange, q)) for r in range(WORLD)]
     for p in procs:
         p.start()
     res = sorted([q.get(timeout=300) for _ in range(WORLD)], key=lambda x: x[0])

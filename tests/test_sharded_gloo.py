@@ -102,7 +102,8 @@ class FakeCtx:
         digit_counts[:] = torch.from_numpy(np.bincount(d, minlength=512).astype(np.int64))
 
     def radix_groupby_routed(self, hashes, vals, seg_counts, n_senders, digit_lo, n_digits, n_rows, max_groups,
-                             out_keys, out, n_groups):
+                             out_keys, out, n_groups, value_bytes=None):
+        assert value_bytes in (None, vals.element_size())
         h = hashes[:n_rows].numpy().view(np.uint64)
         d = (h >> np.uint64(55)).astype(np.int64)
         assert np.all((d >= digit_lo) & (d < digit_lo + n_digits)), "a row routed to a rank that does not own it"

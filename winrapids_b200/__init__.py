@@ -38,7 +38,10 @@ def _torch():
 
 
 def _ptr(t) -> int | None:
-    return None if t is None else int(t.data_ptr())
+    """Device address of a tensor; an int is taken as an address already (peer mappings)."""
+    if t is None or isinstance(t, int):
+        return t
+    return int(t.data_ptr())
 
 
 def _stream_handle(stream) -> int | None:
@@ -353,11 +356,14 @@ class Context:
                                              _stream_handle(stream)))
 
     def radix_groupby_routed(self, hashes, vals, seg_counts, n_senders: int, digit_lo: int, n_digits: int,
-                             n_rows: int, max_groups: int, out_keys, out: dict, n_groups, stream=None):
+                             n_rows: int, max_groups: int, out_keys, out: dict, n_groups, stream=None,
+                             value_bytes: int | None = None):
         """Enqueue the owner's grouping of routed rows (see tbgb_radix_groupby_routed): count / sum /
-        mean into caller-owned buffers."""
+        mean into caller-owned buffers.  hashes / vals may be device addresses (ints), then
+        value_bytes (4 or 8) says how wide the values are."""
         m = self.moments_struct(out)
-        self._check(self._L.tbgb_radix_groupby_routed(self._h, _ptr(hashes), _ptr(vals), int(vals.element_size()),
+        vb = int(value_bytes) if value_bytes is not None else int(vals.element_size())
+        self._check(self._L.tbgb_radix_groupby_routed(self._h, _ptr(hashes), _ptr(vals), vb,
                                                       _ptr(seg_counts), int(n_senders), int(digit_lo),
                                                       int(n_digits), int(n_rows), int(max_groups), _ptr(out_keys),
                                                       C.byref(m), _ptr(n_groups), _stream_handle(stream)))
@@ -407,6 +413,24 @@ class Context:
 
     def peer_close(self, ptr: int):
         self._check(self._L.tbgb_peer_close(self._h, C.c_void_p(ptr)))
+
+    def ipc_alloc(self, nbytes: int) -> int:
+        """A device buffer in its own allocation, exportable with peer_export; free with ipc_free."""
+        p = C.c_void_p()
+        self._check(self._L.tbgb_ipc_alloc(self._h, int(nbytes), C.byref(p)))
+        return int(p.value)
+
+    def ipc_free(self, ptr: int):
+        self._check(self._L.tbgb_ipc_free(self._h, C.c_void_p(ptr)))
+
+    def copy_blocks(self, copies, stream=None):
+        """Enqueue one launch copying [(src, dst, nbytes), ...] (device addresses, a peer's mapped
+        buffer included; at most 32 blocks) -- see tbgb_copy_blocks."""
+        n = len(copies)
+        src = (C.c_void_p * max(n, 1))(*[C.c_void_p(int(c[0])) for c in copies])
+        dst = (C.c_void_p * max(n, 1))(*[C.c_void_p(int(c[1])) for c in copies])
+        nb = (C.c_int64 * max(n, 1))(*[int(c[2]) for c in copies])
+        self._check(self._L.tbgb_copy_blocks(self._h, n, src, dst, nb, _stream_handle(stream)))
 
     def groupby_dense_sharded(self, keys, vals, n_groups: int, row_offset: int, rank: int, exchange, epoch: int,
                               out: dict, mask=None, stream=None):

@@ -143,6 +143,9 @@ def lib() -> C.CDLL:
         "tbgb_peer_export": (st, [vp, vp, vp]),
         "tbgb_peer_import": (st, [vp, vp, C.POINTER(vp)]),
         "tbgb_peer_close": (st, [vp, vp]),
+        "tbgb_ipc_alloc": (st, [vp, sz, C.POINTER(vp)]),
+        "tbgb_ipc_free": (st, [vp, vp]),
+        "tbgb_copy_blocks": (st, [vp, i32, C.POINTER(vp), C.POINTER(vp), C.POINTER(i64), vp]),
         "tbgb_groupby_dense_sharded": (st, [vp, vp, vp, vp, i64, i32, i64, i32, i32, vp, u64, vp, vp]),
         "tbgb_gen_keys_uniform": (st, [vp, vp, i64, i32, u64, i64, vp]),
         "tbgb_gen_values_uniform": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
@@ -174,7 +177,7 @@ HEADER_SYMBOLS = (
     "tbgb_tile_stats_build", "tbgb_tile_skip_mask", "tbgb_mask_skip_tiles", "tbgb_fused_bin_stats",
     "tbgb_exchange_bytes", "tbgb_exchange_alloc", "tbgb_exchange_free", "tbgb_peer_export", "tbgb_peer_import",
     "tbgb_peer_close", "tbgb_groupby_dense_sharded", "tbgb_radix_value_bytes", "tbgb_radix_route",
-    "tbgb_radix_groupby_routed", "tbgb_radix_fallback",
+    "tbgb_radix_groupby_routed", "tbgb_radix_fallback", "tbgb_ipc_alloc", "tbgb_ipc_free", "tbgb_copy_blocks",
 )
 
 # tbgb_bin_stats field order

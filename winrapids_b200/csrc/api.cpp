@@ -658,6 +658,42 @@ tbgb_status tbgb_exchange_free(tbgb_ctx* ctx, void* d_buf) {
   return TBGB_OK;
 }
 
+tbgb_status tbgb_ipc_alloc(tbgb_ctx* ctx, size_t bytes, void** d_buf) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (!d_buf || bytes == 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "ipc_alloc: bad arguments");
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  cudaError_t e = cudaMalloc(d_buf, bytes);  // its own allocation: an IPC handle maps exactly this buffer
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_ALLOC, "ipc buffer", e);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_ipc_free(tbgb_ctx* ctx, void* d_buf) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  DeviceGuard dg(ctx->device);
+  if (d_buf) cudaFree(d_buf);
+  return TBGB_OK;
+}
+
+tbgb_status tbgb_copy_blocks(tbgb_ctx* ctx, int32_t n, const void* const* h_src, void* const* h_dst,
+                             const int64_t* h_bytes, void* stream) {
+  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
+  if (n < 0 || n > tbgb::kMaxCopies || (n > 0 && (!h_src || !h_dst || !h_bytes)))
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "copy_blocks: 0..32 blocks, host arrays not NULL");
+  std::vector<long long> bytes(static_cast<size_t>(n));
+  for (int i = 0; i < n; ++i) {
+    if (h_bytes[i] < 0 || (h_bytes[i] > 0 && (!h_src[i] || !h_dst[i])))
+      return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "copy_blocks: negative size or NULL pointer");
+    bytes[static_cast<size_t>(i)] = h_bytes[i];
+  }
+  DeviceGuard dg(ctx->device);
+  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
+  cudaError_t e = tbgb::copy_blocks_launch(n, h_src, h_dst, bytes.data(), ctx->num_sms,
+                                           static_cast<cudaStream_t>(stream), &ctx->launches);
+  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "copy_blocks launch", e);
+  return TBGB_OK;
+}
+
 tbgb_status tbgb_peer_export(tbgb_ctx* ctx, void* d_buf, uint8_t* handle) {
   if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
   if (!d_buf || !handle) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "peer_export: NULL pointer");
@@ -1103,7 +1139,7 @@ tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, const uint64_t* d_hashes, c
   if (value_bytes != 4 && value_bytes != 8) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "value_bytes must be 4 or 8");
   if (n_senders < 1 || n_digits < 1 || digit_lo < 0 || digit_lo + n_digits > tbgb::kRadixDigits ||
       static_cast<long long>(n_senders) * n_digits > 4096)
-    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "bad sender / digit ranges (digits within [0, 256), senders x "
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "bad sender / digit ranges (digits within [0, 512), senders x "
                                                 "digits <= 4096)");
   if (n_rows < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_rows must be >= 0");
   if (max_groups < 1 || max_groups > (1ll << 40))

@@ -42,7 +42,7 @@ struct RadixArgs {
   uint32_t* err;         // KERR_TABLE_FULL when more than max_groups keys
 };
 
-// Enqueues the three passes (partition by the top 8 hash bits, then by the next 8, then one CTA
+// Enqueues the three passes (partition by the top 9 hash bits, then by the next 9, then one CTA
 // per bucket aggregating in a shared-memory table) and the group count.  `ws` holds
 // t1_bytes + t2_bytes + aux_bytes.  `*fallback` (a device word inside ws, returned) is non-zero
 // after the passes when a bucket overflowed its slack or its shared-memory table: the caller

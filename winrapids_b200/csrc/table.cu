@@ -135,7 +135,10 @@ struct SlotArrays {
   unsigned long long* mn;    // FULL
   unsigned long long* mx;    // FULL
   unsigned long long* zf;    // FULL
-  unsigned long long* cnt;   // FULL: non-NaN rows (low 32 bits) + finite rows (high 32 bits), one atomic
+  // FULL: non-NaN rows (low 32-bit word) and +-inf rows (high word); finite rows = the difference.
+  // A row costs one 32-bit atomic (the high word only for the rare +-inf rows): 32-bit shared-memory
+  // atomics run well ahead of 64-bit ones.
+  unsigned long long* cnt;
   uint32_t* nn;              // SUMCOUNT: non-NaN rows
 
   __device__ __forceinline__ void clear(int s) {
@@ -156,7 +159,8 @@ struct SlotArrays {
   __device__ __forceinline__ void row(int s, double v, long long grow, bool m34, bool extrema) {
     if constexpr (FULL) {
       const bool fin = is_finite(v);
-      atomicAdd(cnt + s, fin ? 0x100000001ull : 1ull);
+      atomicAdd(reinterpret_cast<unsigned int*>(cnt + s), 1u);
+      if (!fin) atomicAdd(reinterpret_cast<unsigned int*>(cnt + s) + 1, 1u);
       if (fin) {
         unsigned long long kb = *reinterpret_cast<volatile unsigned long long*>(K + s);
         if (kb == K_UNSET) {
@@ -187,7 +191,7 @@ struct SlotArrays {
   // the global K_g, sum (d + off)^k with off = K_l - K_g.
   __device__ __forceinline__ void flush(int s, unsigned long long* p, bool m34, bool extrema) {
     if constexpr (FULL) {
-      const unsigned long long n_nn = cnt[s] & 0xFFFFFFFFull, n_f = cnt[s] >> 32;
+      const unsigned long long n_nn = cnt[s] & 0xFFFFFFFFull, n_f = n_nn - (cnt[s] >> 32);
       if (n_nn) atomicAdd(p + FL_NN, n_nn);
       if (n_f) {
         const double Kl = bitsd(K[s]);
@@ -512,7 +516,8 @@ __device__ __forceinline__ int nth_set_bit(unsigned m, int n) {
 __device__ __forceinline__ void row_gk(SlotArrays<true>& t, int s, unsigned long long* p, double v, long long grow,
                                        bool m34, bool extrema) {
   const bool fin = is_finite(v);
-  atomicAdd(t.cnt + s, fin ? 0x100000001ull : 1ull);
+  atomicAdd(reinterpret_cast<unsigned int*>(t.cnt + s), 1u);
+  if (!fin) atomicAdd(reinterpret_cast<unsigned int*>(t.cnt + s) + 1, 1u);
   if (fin) {
     const double d = v - slot_shift(p + FL_K, v), dd = d * d;
     atomicAdd(t.s1 + s, d);
@@ -533,7 +538,7 @@ __device__ __forceinline__ void row_gk(SlotArrays<true>& t, int s, unsigned long
 // GK merge of slot s into global slot p: the sums already share its K.
 __device__ __forceinline__ void flush_gk(const SlotArrays<true>& t, int s, unsigned long long* p, bool m34,
                                          bool extrema) {
-  const unsigned long long n_nn = t.cnt[s] & 0xFFFFFFFFull, n_f = t.cnt[s] >> 32;
+  const unsigned long long n_nn = t.cnt[s] & 0xFFFFFFFFull, n_f = n_nn - (t.cnt[s] >> 32);
   if (n_nn) atomicAdd(p + FL_NN, n_nn);
   if (n_f) {
     atomicAdd(reinterpret_cast<double*>(p + FL_S1), t.s1[s]);

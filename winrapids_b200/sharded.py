@@ -72,6 +72,38 @@ class PeerMappingError(RuntimeError):
     """The exchange buffers could not be mapped across the ranks (raised on every rank)."""
 
 
+def map_peers(ctx, dist, world: int, rank: int, own: int, device, group=None):
+    """Every rank's buffer as mapped in this process, [own if q == rank else peer q's] for q in
+    range(world), plus the list of the mappings made (to unmap).  The CUDA IPC handles travel
+    once through ``dist.all_gather_object``; a failure on any rank raises PeerMappingError on
+    every rank (each unmaps what it mapped), and a ``dist.barrier`` then makes sure every
+    mapping exists before any rank stores into a peer's buffer."""
+    import torch
+
+    handles = [None] * world
+    dist.all_gather_object(handles, ctx.peer_export(own), group=group)
+    buffers, mapped, failure = [], [], None
+    try:
+        for q in range(world):
+            if q == rank:
+                buffers.append(own)
+            else:
+                p = ctx.peer_import(handles[q])
+                mapped.append(p)
+                buffers.append(p)
+    except Exception as exc:  # every rank learns of it below, so none is left waiting
+        failure = exc
+    ok = torch.tensor([0 if failure else 1], dtype=torch.int32, device=device)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
+    if int(ok.item()) == 0:
+        for p in mapped:
+            ctx.peer_close(p)
+        raise PeerMappingError(f"peer memory mapping failed on rank {rank}: {failure}" if failure
+                               else "peer memory mapping failed on another rank")
+    dist.barrier(group=group)
+    return buffers, mapped
+
+
 class PeerShardedDenseGroupby:
     """Row-sharded dense-key groupby with the exchange over NVLink peer memory: each rank's
     state table is stored straight into every rank's exchange buffer and each rank folds the
@@ -83,30 +115,12 @@ class PeerShardedDenseGroupby:
         self.ctx, self.dist, self.world, self.rank, self.G = ctx, dist, int(world), int(rank), int(n_groups)
         self.out, self.group = out, group
         self.own = ctx.exchange_alloc(self.world, self.G)
-        handles = [None] * self.world
-        dist.all_gather_object(handles, ctx.peer_export(self.own), group=group)
         self.mapped = []
-        self.buffers = []
-        failure = None
         try:
-            for q in range(self.world):
-                if q == self.rank:
-                    self.buffers.append(self.own)
-                else:
-                    p = ctx.peer_import(handles[q])
-                    self.mapped.append(p)
-                    self.buffers.append(p)
-        except Exception as exc:  # every rank learns of it below, so none is left waiting
-            failure = exc
-        import torch
-
-        ok = torch.tensor([0 if failure else 1], dtype=torch.int32, device=device)
-        dist.all_reduce(ok, op=dist.ReduceOp.MIN, group=group)
-        if int(ok.item()) == 0:
+            self.buffers, self.mapped = map_peers(ctx, dist, self.world, self.rank, self.own, device, group)
+        except PeerMappingError:
             self.close()
-            raise PeerMappingError(f"peer memory mapping failed on rank {self.rank}: {failure}" if failure
-                                   else "peer memory mapping failed on another rank")
-        dist.barrier(group=group)
+            raise
         self.epoch = 0
 
     def step(self, keys, vals, row_offset: int, mask=None):
@@ -143,18 +157,59 @@ def owned_digits(world: int):
     return [(RADIX_DIGITS * r + world - 1) // world for r in range(world + 1)]
 
 
+def owner_totals(counts, lo):
+    """rows[s][q]: rows sender s routes to owner q, from every sender's 512 digit counts."""
+    w = len(counts)
+    return [[int(sum(counts[s][lo[q]:lo[q + 1]])) for q in range(w)] for s in range(w)]
+
+
+def peer_copy_plan(counts, rank: int, lo, cap: int, value_bytes: int, send_h: int, send_v: int, recv_bases):
+    """The blocks this rank stores into the owners' receive buffers, and each owner's row count.
+
+    counts[s][d]: rows sender s routed to digit d (every rank's digit counts); send_h / send_v:
+    this rank's routed rows (digit order); recv_bases[q]: owner q's receive buffer as mapped
+    here, hashes at its start and values cap * 8 bytes in (cap: the same on every rank).  Every
+    owner's buffer ends up laid out as the all-to-all lays it out: senders in rank order, each
+    sender's rows in digit order.
+    Returns ([(src, dst, nbytes), ...], [rows owner q receives for q in range(world)])."""
+    rows = owner_totals(counts, lo)
+    w = len(counts)
+    n_recv = [sum(rows[s][q] for s in range(w)) for q in range(w)]
+    copies, send_off = [], 0
+    for q in range(w):
+        r = rows[rank][q]
+        if r:
+            recv_off = sum(rows[s][q] for s in range(rank))
+            copies.append((send_h + send_off * 8, recv_bases[q] + recv_off * 8, r * 8))
+            copies.append((send_v + send_off * value_bytes, recv_bases[q] + cap * 8 + recv_off * value_bytes,
+                           r * value_bytes))
+        send_off += r
+    return copies, n_recv
+
+
 class ShardedHashGroupby:
     """Owner-sharded int64-key groupby of one shard's rows (see the module docstring).
 
     ``ctx`` is a ``winrapids_b200.Context`` (or an object with the same methods).  Buffers
     are allocated once for shards of up to ``max_rows`` rows, receive buffers with
     ``recv_slack`` headroom over an even share.
+
+    ``exchange`` (count / sum / mean only): "nccl" moves the routed rows with
+    ``all_to_all_single``; "peer" maps every rank's receive buffer into every process (CUDA IPC)
+    and one launch of ``Context.copy_blocks`` stores this rank's rows straight into the owners'
+    buffers over NVLink.  The peer step: all-gather of the 512 digit counts of every rank (every
+    rank then knows every offset), the copy, a one-word all-reduce after it (the owners' groupby
+    starts only when every sender's copy is done), the owner's grouping.  A rank joins the next
+    step's all-gather only once its stream has finished grouping, so no sender overwrites a
+    buffer that is still being read.  Raises PeerMappingError when the mapping fails.
     """
 
     def __init__(self, ctx, dist, world: int, max_rows: int, max_groups_per_owner: int, fields, device,
-                 recv_slack: float = 1.25, group=None):
+                 recv_slack: float = 1.25, group=None, exchange: str = "nccl"):
         import torch
 
+        if exchange not in ("nccl", "peer"):
+            raise ValueError(f"exchange must be 'nccl' or 'peer', not {exchange!r}")
         self.ctx, self.dist, self.world, self.group = ctx, dist, int(world), group
         self.rank = dist.get_rank(group) if group is not None else dist.get_rank()
         self.device = device
@@ -180,6 +235,22 @@ class ShardedHashGroupby:
             self.digit_counts = torch.zeros(RADIX_DIGITS, dtype=torch.int64, device=device)
             self.seg_counts = torch.zeros(self.world * self.n_digits, dtype=torch.int64, device=device)
             self.send_h = torch.empty(max_rows, dtype=torch.int64, device=device)
+        self.peer = self.radix and exchange == "peer"
+        self.own, self.mapped = 0, []
+        if self.peer:
+            # senders place values at cap * 8 bytes into the owner's buffer: one cap on every rank
+            cap = torch.tensor([self.cap], dtype=torch.int64, device=device)
+            dist.all_reduce(cap, op=dist.ReduceOp.MAX, group=group)
+            self.cap = int(cap.item())
+            self.all_counts = torch.zeros(self.world * RADIX_DIGITS, dtype=torch.int64, device=device)
+            self.one = torch.zeros(1, dtype=torch.int64, device=device)
+            self.own = ctx.ipc_alloc(self.cap * 16)  # hashes, then values (8 bytes a row at most)
+            try:
+                self.recv_bases, self.mapped = map_peers(ctx, dist, self.world, self.rank, self.own, device, group)
+            except PeerMappingError:
+                self.close()
+                raise
+        elif self.radix:
             self.recv_h = torch.empty(self.cap, dtype=torch.int64, device=device)
 
     def _value_buffers(self, vb):
@@ -188,7 +259,8 @@ class ShardedHashGroupby:
         dt = torch.float32 if vb == 4 else torch.float64
         if self._vdtype != dt:
             self.send_v = torch.empty(self.max_rows, dtype=dt, device=self.device)
-            self.recv_v = torch.empty(self.cap, dtype=dt, device=self.device)
+            if not self.peer:
+                self.recv_v = torch.empty(self.cap, dtype=dt, device=self.device)
             self._vdtype = dt
             self.value_bytes = vb
 
@@ -208,10 +280,55 @@ class ShardedHashGroupby:
         self._value_buffers(self.ctx.radix_value_bytes(a, b, c, expr, pred, threshold))
         self.ctx.radix_route(keys, a, self.send_h, self.send_v, self.digit_counts, b=b, c=c, expr=expr, pred=pred,
                              threshold=threshold, mask=mask)
-        self.n_recv = self._exchange()
-        self.ctx.radix_groupby_routed(self.recv_h, self.recv_v, self.seg_counts, self.world, self.lo[self.rank],
+        if self.peer:
+            self.n_recv = self._exchange_peer()
+            recv_h, recv_v = self.own, self.own + self.cap * 8
+        else:
+            self.n_recv = self._exchange()
+            recv_h, recv_v = self.recv_h, self.recv_v
+        self.ctx.radix_groupby_routed(recv_h, recv_v, self.seg_counts, self.world, self.lo[self.rank],
                                       self.n_digits, self.n_recv, self.max_groups, self.out_keys, self.out,
-                                      self.n_groups)
+                                      self.n_groups, value_bytes=self.value_bytes)
+
+    def _exchange_peer(self) -> int:
+        """Every rank's digit counts to every rank, then this rank's rows into the owners' buffers
+        (one copy launch), then a one-word all-reduce: after it every owner's buffer is complete.
+        Every rank computes every owner's row count, so all raise together, before any row moves,
+        when some owner's buffer is too small."""
+        dist, g, w = self.dist, self.group, self.world
+        dist.all_gather_into_tensor(self.all_counts, self.digit_counts, group=g)
+        table = self.all_counts.view(w, RADIX_DIGITS)
+        lo, hi = self.lo[self.rank], self.lo[self.rank + 1]
+        self.seg_counts.view(w, self.n_digits).copy_(table[:, lo:hi])
+        counts = table.cpu().tolist()
+        copies, n_recv = peer_copy_plan(counts, self.rank, self.lo, self.cap, self.value_bytes,
+                                        self.send_h.data_ptr(), self.send_v.data_ptr(), self.recv_bases)
+        if max(n_recv) > self.cap:
+            raise RuntimeError(f"receive buffers too small (an owner needs {max(n_recv)} rows, room for {self.cap})")
+        self.ctx.copy_blocks(copies)
+        dist.all_reduce(self.one, group=g)
+        return n_recv[self.rank]
+
+    def close(self):
+        """Unmap the peers' receive buffers and free the own one (finish() first when every rank
+        is alive)."""
+        for p in self.mapped:
+            self.ctx.peer_close(p)
+        self.mapped = []
+        if self.own:
+            self.ctx.ipc_free(self.own)
+            self.own = 0
+
+    def finish(self):
+        """Orderly teardown on every rank: unmap, wait until no rank maps this rank's buffer, free it."""
+        if not self.peer:
+            return
+        self.ctx.sync()
+        for p in self.mapped:
+            self.ctx.peer_close(p)
+        self.mapped = []
+        self.dist.barrier(group=self.group)
+        self.close()
 
     def _exchange(self) -> int:
         """Digit counts to their owners, then the rows (senders concatenated in rank order, each
