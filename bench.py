@@ -79,8 +79,8 @@ WORKLOADS = {
     "highcard": dict(kind="highcard", rows=2_000_000_000, ids=1 << 28, seed=0,
                      desc="high-cardinality sharded: 2,000,000,000 rows; int64 key uniform over 2^28 random ids; "
                           "f32 value ~LogNormal(0,1); sum/count/mean; radix partitioning by key hash (with N GPUs "
-                          "rows routed to the owner of their hash digit over one NCCL all-to-all, each GPU groups "
-                          "the keys it owns)"),
+                          "rows routed to the owner of their hash digit and stored into its buffer over NVLink peer "
+                          "memory, each GPU groups the keys it owns)"),
 }
 
 
@@ -99,9 +99,9 @@ def parse():
     ap.add_argument("--ids", type=int, default=None, help="override the distinct-id count of a hash workload")
     ap.add_argument("--table-mode", default="auto", choices=["auto", "local", "direct", "bucket", "range"],
                     help="global-table kernel: shared-memory pre-aggregation or direct atomics")
-    ap.add_argument("--exchange", default="peer", choices=["peer", "nccl"],
-                    help="multi-GPU high-cardinality exchange: stores into the owners' buffers over NVLink peer "
-                         "memory, or NCCL all-to-all")
+    ap.add_argument("--exchange", default="pull", choices=["pull", "nccl"],
+                    help="multi-GPU high-cardinality exchange: owners read the senders' routed rows in place over "
+                         "NVLink (pull), or NCCL all-to-all")
     return ap.parse_args()
 
 
@@ -648,10 +648,10 @@ class HashJob:
             from winrapids_b200.sharded import PeerMappingError, ShardedHashGroupby
 
             per_owner = int(ids / world * 1.05) + 4096
-            how = wl.get("exchange", "peer") if radix else "nccl"
+            how = wl.get("exchange", "pull") if radix else "nccl"
             try:
                 self.sharded = ShardedHashGroupby(ctx, dist, world, n, per_owner, self.fields, dev, exchange=how)
-                self.exchange = {"peer": "peer memory (routed rows stored into the owners' buffers over NVLink)",
+                self.exchange = {"pull": "peer memory (owners read the senders' routed rows in place over NVLink)",
                                  "nccl": "NCCL all-to-all of the routed rows"}[how]
             except PeerMappingError as exc:
                 self.sharded = ShardedHashGroupby(ctx, dist, world, n, per_owner, self.fields, dev)

@@ -349,18 +349,10 @@ tbgb_status tbgb_peer_export(tbgb_ctx* ctx, void* d_buf, uint8_t* handle /* 64 b
 tbgb_status tbgb_peer_import(tbgb_ctx* ctx, const uint8_t* handle /* 64 bytes */, void** d_peer);
 tbgb_status tbgb_peer_close(tbgb_ctx* ctx, void* d_peer);
 /* A device buffer of `bytes` in its own allocation, so that tbgb_peer_export's handle maps
- * exactly it (e.g. the receive buffer of the owner-sharded groupby's rows); free with
- * tbgb_ipc_free.  No counterpart in the reference (single GPU). */
+ * exactly it (e.g. the send buffer of the owner-sharded groupby's routed rows, which the owners
+ * read in place); free with tbgb_ipc_free.  No counterpart in the reference (single GPU). */
 tbgb_status tbgb_ipc_alloc(tbgb_ctx* ctx, size_t bytes, void** d_buf);
 tbgb_status tbgb_ipc_free(tbgb_ctx* ctx, void* d_buf);
-/* Copies n <= 32 blocks: h_bytes[i] bytes from device address h_src[i] to h_dst[i] (host arrays
- * of device pointers; a pointer may be a peer's buffer mapped by tbgb_peer_import, so one launch
- * can scatter a shard's rows into every owner's receive buffer over NVLink with plain stores).
- * Enqueued on `stream`; the kernel ends with a system-scope fence: once `stream` has been waited
- * for, the peers see the data.  The caller orders the copies against the receivers' use of their
- * buffers (e.g. a barrier).  No counterpart in the reference (single GPU). */
-tbgb_status tbgb_copy_blocks(tbgb_ctx* ctx, int32_t n, const void* const* h_src, void* const* h_dst,
-                             const int64_t* h_bytes, void* stream);
 tbgb_status tbgb_groupby_dense_sharded(tbgb_ctx* ctx, const int32_t* d_keys, const double* d_vals,
                                        const uint64_t* d_mask, int64_t n, int32_t n_groups, int64_t row_offset,
                                        int32_t rank, int32_t world, void* const* h_exchange, uint64_t epoch,
@@ -393,21 +385,24 @@ tbgb_status tbgb_hash_partition(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb
  * the rows of each digit; the output buffers hold n rows.  The rows for rank r are then one
  * contiguous run, ready for an all-to-all.
  *
- * tbgb_radix_groupby_routed: the owner's side.  The received rows are n_senders blocks in sender
- * order, each holding the sender's rows of digits [digit_lo, digit_lo + n_digits) in digit order;
- * d_seg_counts (device, n_senders * n_digits int64, sender-major) gives their row counts and
- * n_rows their total.  Groups the rows by key (recovered from h) into d_out_keys / out (count,
- * sum, mean only; other outputs must be NULL) and *d_n_groups, with the semantics and errors of
- * tbgb_groupby_hash. */
+ * tbgb_radix_groupby_routed: the owner's side.  Sender i (0 <= i < n_senders <= 64) contributes
+ * h_rows[i] rows of digits [digit_lo, digit_lo + n_digits) in digit order, starting at the device
+ * addresses h_hashes[i] / h_vals[i] (host arrays): a block of a receive buffer after an
+ * all-to-all, or the sender's own routed rows read in place through a peer mapping
+ * (tbgb_peer_import), in which case the owner's pass reads them over NVLink and no copy is made.
+ * d_seg_counts (device, n_senders * n_digits int64, sender-major) gives the rows of each
+ * (sender, digit).  Groups the rows by key (recovered from h) into d_out_keys / out (count, sum,
+ * mean only; other outputs must be NULL) and *d_n_groups, with the semantics and errors of
+ * tbgb_groupby_hash.  The senders' rows must stay unchanged until the call's stream work is done. */
 int32_t tbgb_radix_value_bytes(const tbgb_columns* cols);
 tbgb_status tbgb_radix_route(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb_columns* cols, const uint64_t* d_mask,
                              int64_t n, uint64_t* d_out_hashes, void* d_out_vals, int64_t* d_digit_counts,
                              void* stream);
-tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, const uint64_t* d_hashes, const void* d_vals,
-                                      int32_t value_bytes, const int64_t* d_seg_counts, int32_t n_senders,
-                                      int32_t digit_lo, int32_t n_digits, int64_t n_rows, int64_t max_groups,
-                                      int64_t* d_out_keys, const tbgb_moments* out, int64_t* d_n_groups,
-                                      void* stream);
+tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, int32_t n_senders, const uint64_t* const* h_hashes,
+                                      const void* const* h_vals, const int64_t* h_rows, int32_t value_bytes,
+                                      const int64_t* d_seg_counts, int32_t digit_lo, int32_t n_digits,
+                                      int64_t max_groups, int64_t* d_out_keys, const tbgb_moments* out,
+                                      int64_t* d_n_groups, void* stream);
 
 /* Diagnostic: whether the last radix-partitioned call on `ctx` (table mode 5, or mode 0 choosing
  * it; or tbgb_radix_groupby_routed) recomputed its result with the global table.  Waits for the

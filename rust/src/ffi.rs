@@ -231,8 +231,6 @@ extern "C" {
     pub fn tbgb_peer_close(ctx: *mut tbgb_ctx, peer: *mut c_void) -> tbgb_status;
     pub fn tbgb_ipc_alloc(ctx: *mut tbgb_ctx, bytes: usize, buf: *mut *mut c_void) -> tbgb_status;
     pub fn tbgb_ipc_free(ctx: *mut tbgb_ctx, buf: *mut c_void) -> tbgb_status;
-    pub fn tbgb_copy_blocks(ctx: *mut tbgb_ctx, n: i32, src: *const *const c_void, dst: *const *mut c_void,
-                            bytes: *const i64, stream: *mut c_void) -> tbgb_status;
     pub fn tbgb_groupby_dense_sharded(ctx: *mut tbgb_ctx, keys: *const i32, vals: *const f64, mask: *const u64,
                                       n: i64, n_groups: i32, row_offset: i64, rank: i32, world: i32,
                                       exchange: *const *mut c_void, epoch: u64, out: *const tbgb_moments,
@@ -245,10 +243,11 @@ extern "C" {
     pub fn tbgb_radix_route(ctx: *mut tbgb_ctx, keys: *const i64, cols: *const tbgb_columns, mask: *const u64,
                             n: i64, out_hashes: *mut u64, out_vals: *mut c_void, digit_counts: *mut i64,
                             stream: *mut c_void) -> tbgb_status;
-    pub fn tbgb_radix_groupby_routed(ctx: *mut tbgb_ctx, hashes: *const u64, vals: *const c_void, value_bytes: i32,
-                                     seg_counts: *const i64, n_senders: i32, digit_lo: i32, n_digits: i32,
-                                     n_rows: i64, max_groups: i64, out_keys: *mut i64, out: *const tbgb_moments,
-                                     n_groups: *mut i64, stream: *mut c_void) -> tbgb_status;
+    pub fn tbgb_radix_groupby_routed(ctx: *mut tbgb_ctx, n_senders: i32, hashes: *const *const u64,
+                                     vals: *const *const c_void, rows: *const i64, value_bytes: i32,
+                                     seg_counts: *const i64, digit_lo: i32, n_digits: i32, max_groups: i64,
+                                     out_keys: *mut i64, out: *const tbgb_moments, n_groups: *mut i64,
+                                     stream: *mut c_void) -> tbgb_status;
 
     // ---- synthetic inputs (counter-based SplitMix64 streams) ------------------------------
     pub fn tbgb_gen_keys_uniform(ctx: *mut tbgb_ctx, keys: *mut i32, n: i64, n_groups: i32, seed: u64,

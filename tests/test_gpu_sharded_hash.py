@@ -1,7 +1,7 @@
 """The owner-sharded int64-key groupby (winrapids_b200.sharded.ShardedHashGroupby) on two GPUs,
 one process each over NCCL: every rank routes its rows to the owner of their key, the parts cross
-NVLink (one NCCL all-to-all, or one copy launch storing into the owners' buffers through peer
-memory), and each owner groups what it received.  The union of the ranks' groups
+NVLink (one NCCL all-to-all, or the owner's second radix pass reading the senders' buffers in
+place through peer memory), and each owner groups its keys.  The union of the ranks' groups
 must equal the oracle's groupby of all rows (each key on exactly one rank; counts bit-exact, sums
 within 1e-12 * sum|x|), for the high-cardinality shape (f32 values) and the fused pipeline shape
 (filter a > 0, v = a*b + c).  Needs two GPUs: skipped otherwise."""
@@ -71,7 +71,7 @@ def _worker(rank, port, shape, exchange, q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("exchange", ["nccl", "peer"])
+@pytest.mark.parametrize("exchange", ["nccl", "pull"])
 @pytest.mark.parametrize("shape", ["highcard", "pipeline"])
 def test_sharded_hash_groupby_matches_oracle(shape, exchange):
     import torch

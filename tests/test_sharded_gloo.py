@@ -101,15 +101,16 @@ class FakeCtx:
         out_vals[:m] = a[torch.from_numpy(order)]
         digit_counts[:] = torch.from_numpy(np.bincount(d, minlength=512).astype(np.int64))
 
-    def radix_groupby_routed(self, hashes, vals, seg_counts, n_senders, digit_lo, n_digits, n_rows, max_groups,
+    def radix_groupby_routed(self, hashes, vals, sender_rows, seg_counts, digit_lo, n_digits, max_groups,
                              out_keys, out, n_groups, value_bytes=None):
         assert value_bytes in (None, vals.element_size())
+        n_senders, n_rows = len(sender_rows), sum(sender_rows)
         h = hashes[:n_rows].numpy().view(np.uint64)
         d = (h >> np.uint64(55)).astype(np.int64)
         assert np.all((d >= digit_lo) & (d < digit_lo + n_digits)), "a row routed to a rank that does not own it"
         # the blocks are in sender order, each in digit order, with the announced sizes
         sizes = seg_counts.numpy().reshape(n_senders, n_digits)
-        assert sizes.sum() == n_rows
+        assert sizes.sum() == n_rows and list(sizes.sum(1)) == list(sender_rows)
         exp = np.concatenate([np.repeat(np.arange(digit_lo, digit_lo + n_digits), sizes[s]) for s in range(n_senders)])
         assert np.array_equal(d, exp)
         res = oracle.groupby_i64(unfmix64_np(h), vals[:n_rows].numpy().astype(np.float64))

@@ -355,18 +355,30 @@ class Context:
                                              _ptr(out_hashes), _ptr(out_vals), _ptr(digit_counts),
                                              _stream_handle(stream)))
 
-    def radix_groupby_routed(self, hashes, vals, seg_counts, n_senders: int, digit_lo: int, n_digits: int,
-                             n_rows: int, max_groups: int, out_keys, out: dict, n_groups, stream=None,
-                             value_bytes: int | None = None):
+    def radix_groupby_routed(self, hashes, vals, sender_rows, seg_counts, digit_lo: int, n_digits: int,
+                             max_groups: int, out_keys, out: dict, n_groups, value_bytes: int | None = None,
+                             stream=None):
         """Enqueue the owner's grouping of routed rows (see tbgb_radix_groupby_routed): count / sum /
-        mean into caller-owned buffers.  hashes / vals may be device addresses (ints), then
-        value_bytes (4 or 8) says how wide the values are."""
+        mean into caller-owned buffers.  hashes / vals: per sender, the device address (int) of its
+        first routed row -- or one tensor each holding the senders' blocks back to back (a receive
+        buffer); sender_rows: rows per sender (host ints); value_bytes: 4 or 8 (taken from the
+        tensor when vals is one)."""
+        rows = [int(x) for x in sender_rows]
+        n = len(rows)
+        if not isinstance(hashes, (list, tuple)):
+            vb = int(vals.element_size())
+            offs = [sum(rows[:i]) for i in range(n)]
+            hashes = [int(hashes.data_ptr()) + 8 * o for o in offs]
+            vals = [int(vals.data_ptr()) + vb * o for o in offs]
+        else:
+            vb = int(value_bytes)
         m = self.moments_struct(out)
-        vb = int(value_bytes) if value_bytes is not None else int(vals.element_size())
-        self._check(self._L.tbgb_radix_groupby_routed(self._h, _ptr(hashes), _ptr(vals), vb,
-                                                      _ptr(seg_counts), int(n_senders), int(digit_lo),
-                                                      int(n_digits), int(n_rows), int(max_groups), _ptr(out_keys),
-                                                      C.byref(m), _ptr(n_groups), _stream_handle(stream)))
+        hp = (C.c_void_p * n)(*[C.c_void_p(_ptr(p)) for p in hashes])
+        vp_ = (C.c_void_p * n)(*[C.c_void_p(_ptr(p)) for p in vals])
+        rp = (C.c_int64 * n)(*rows)
+        self._check(self._L.tbgb_radix_groupby_routed(self._h, n, hp, vp_, rp, vb, _ptr(seg_counts), int(digit_lo),
+                                                      int(n_digits), int(max_groups), _ptr(out_keys), C.byref(m),
+                                                      _ptr(n_groups), _stream_handle(stream)))
 
     def groupby_hash(self, keys, a, max_groups: int, b=None, c=None, expr: str = "a", pred: str | None = None,
                      threshold: float = 0.0, mask=None, fields=MOMENT_FIELDS, stream=None):
@@ -422,15 +434,6 @@ class Context:
 
     def ipc_free(self, ptr: int):
         self._check(self._L.tbgb_ipc_free(self._h, C.c_void_p(ptr)))
-
-    def copy_blocks(self, copies, stream=None):
-        """Enqueue one launch copying [(src, dst, nbytes), ...] (device addresses, a peer's mapped
-        buffer included; at most 32 blocks) -- see tbgb_copy_blocks."""
-        n = len(copies)
-        src = (C.c_void_p * max(n, 1))(*[C.c_void_p(int(c[0])) for c in copies])
-        dst = (C.c_void_p * max(n, 1))(*[C.c_void_p(int(c[1])) for c in copies])
-        nb = (C.c_int64 * max(n, 1))(*[int(c[2]) for c in copies])
-        self._check(self._L.tbgb_copy_blocks(self._h, n, src, dst, nb, _stream_handle(stream)))
 
     def groupby_dense_sharded(self, keys, vals, n_groups: int, row_offset: int, rank: int, exchange, epoch: int,
                               out: dict, mask=None, stream=None):

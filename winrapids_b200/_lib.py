@@ -118,8 +118,8 @@ def lib() -> C.CDLL:
         "tbgb_radix_value_bytes": (i32, [C.POINTER(Columns)]),
         "tbgb_radix_fallback": (st, [vp, C.POINTER(C.c_uint32)]),
         "tbgb_radix_route": (st, [vp, vp, C.POINTER(Columns), vp, i64, vp, vp, vp, vp]),
-        "tbgb_radix_groupby_routed": (st, [vp, vp, vp, i32, vp, i32, i32, i32, i64, i64, vp, C.POINTER(Moments),
-                                           vp, vp]),
+        "tbgb_radix_groupby_routed": (st, [vp, i32, C.POINTER(vp), C.POINTER(vp), C.POINTER(i64), i32, vp, i32,
+                                           i32, i64, vp, C.POINTER(Moments), vp, vp]),
         "tbgb_scatter_multi_phi_masked": (st, [vp, C.POINTER(i32), i32, vp, vp, vp, vp, i64, i32, vp, vp]),
         "tbgb_scatter_phi": (st, [vp, i32, vp, vp, vp, i64, i32, vp, vp]),
         "tbgb_scatter_multi_phi": (st, [vp, C.POINTER(i32), i32, vp, vp, vp, i64, i32, vp, vp]),
@@ -145,7 +145,6 @@ def lib() -> C.CDLL:
         "tbgb_peer_close": (st, [vp, vp]),
         "tbgb_ipc_alloc": (st, [vp, sz, C.POINTER(vp)]),
         "tbgb_ipc_free": (st, [vp, vp]),
-        "tbgb_copy_blocks": (st, [vp, i32, C.POINTER(vp), C.POINTER(vp), C.POINTER(i64), vp]),
         "tbgb_groupby_dense_sharded": (st, [vp, vp, vp, vp, i64, i32, i64, i32, i32, vp, u64, vp, vp]),
         "tbgb_gen_keys_uniform": (st, [vp, vp, i64, i32, u64, i64, vp]),
         "tbgb_gen_values_uniform": (st, [vp, vp, i64, f64, f64, u64, i64, vp]),
@@ -177,7 +176,7 @@ HEADER_SYMBOLS = (
     "tbgb_tile_stats_build", "tbgb_tile_skip_mask", "tbgb_mask_skip_tiles", "tbgb_fused_bin_stats",
     "tbgb_exchange_bytes", "tbgb_exchange_alloc", "tbgb_exchange_free", "tbgb_peer_export", "tbgb_peer_import",
     "tbgb_peer_close", "tbgb_groupby_dense_sharded", "tbgb_radix_value_bytes", "tbgb_radix_route",
-    "tbgb_radix_groupby_routed", "tbgb_radix_fallback", "tbgb_ipc_alloc", "tbgb_ipc_free", "tbgb_copy_blocks",
+    "tbgb_radix_groupby_routed", "tbgb_radix_fallback", "tbgb_ipc_alloc", "tbgb_ipc_free",
 )
 
 # tbgb_bin_stats field order

@@ -675,25 +675,6 @@ tbgb_status tbgb_ipc_free(tbgb_ctx* ctx, void* d_buf) {
   return TBGB_OK;
 }
 
-tbgb_status tbgb_copy_blocks(tbgb_ctx* ctx, int32_t n, const void* const* h_src, void* const* h_dst,
-                             const int64_t* h_bytes, void* stream) {
-  if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
-  if (n < 0 || n > tbgb::kMaxCopies || (n > 0 && (!h_src || !h_dst || !h_bytes)))
-    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "copy_blocks: 0..32 blocks, host arrays not NULL");
-  std::vector<long long> bytes(static_cast<size_t>(n));
-  for (int i = 0; i < n; ++i) {
-    if (h_bytes[i] < 0 || (h_bytes[i] > 0 && (!h_src[i] || !h_dst[i])))
-      return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "copy_blocks: negative size or NULL pointer");
-    bytes[static_cast<size_t>(i)] = h_bytes[i];
-  }
-  DeviceGuard dg(ctx->device);
-  if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
-  cudaError_t e = tbgb::copy_blocks_launch(n, h_src, h_dst, bytes.data(), ctx->num_sms,
-                                           static_cast<cudaStream_t>(stream), &ctx->launches);
-  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "copy_blocks launch", e);
-  return TBGB_OK;
-}
-
 tbgb_status tbgb_peer_export(tbgb_ctx* ctx, void* d_buf, uint8_t* handle) {
   if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
   if (!d_buf || !handle) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "peer_export: NULL pointer");
@@ -1126,27 +1107,33 @@ tbgb_status tbgb_radix_route(tbgb_ctx* ctx, const int64_t* d_keys, const tbgb_co
   return TBGB_OK;
 }
 
-tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, const uint64_t* d_hashes, const void* d_vals,
-                                      int32_t value_bytes, const int64_t* d_seg_counts, int32_t n_senders,
-                                      int32_t digit_lo, int32_t n_digits, int64_t n_rows, int64_t max_groups,
-                                      int64_t* d_out_keys, const tbgb_moments* out, int64_t* d_n_groups,
-                                      void* stream) {
+tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, int32_t n_senders, const uint64_t* const* h_hashes,
+                                      const void* const* h_vals, const int64_t* h_rows, int32_t value_bytes,
+                                      const int64_t* d_seg_counts, int32_t digit_lo, int32_t n_digits,
+                                      int64_t max_groups, int64_t* d_out_keys, const tbgb_moments* out,
+                                      int64_t* d_n_groups, void* stream) {
   if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
   if (!out || !d_out_keys || !d_n_groups || !d_seg_counts)
     return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "out, out_keys, n_groups and seg_counts must not be NULL");
   if (out->min || out->max || out->m2 || out->var_pop || out->var_samp || out->m3 || out->m4)
     return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "the routed groupby computes count, sum and mean only");
   if (value_bytes != 4 && value_bytes != 8) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "value_bytes must be 4 or 8");
-  if (n_senders < 1 || n_digits < 1 || digit_lo < 0 || digit_lo + n_digits > tbgb::kRadixDigits ||
-      static_cast<long long>(n_senders) * n_digits > 4096)
-    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "bad sender / digit ranges (digits within [0, 512), senders x "
-                                                "digits <= 4096)");
-  if (n_rows < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "n_rows must be >= 0");
+  if (n_senders < 1 || n_senders > tbgb::kRadixMaxSenders || n_digits < 1 || digit_lo < 0 ||
+      digit_lo + n_digits > tbgb::kRadixDigits || static_cast<long long>(n_senders) * n_digits > 4096)
+    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "bad sender / digit ranges (1..64 senders, digits within [0, 512), "
+                                                "senders x digits <= 4096)");
+  if (!h_hashes || !h_vals || !h_rows) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "sender arrays must not be NULL");
+  long long n_rows = 0;
+  for (int i = 0; i < n_senders; ++i) {
+    if (h_rows[i] < 0) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "a sender's row count is negative");
+    if (h_rows[i] > 0 && (!h_hashes[i] || !h_vals[i]))
+      return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "row pointers are NULL");
+    if (misaligned(h_hashes[i], 8) || misaligned(h_vals[i], static_cast<size_t>(value_bytes)))
+      return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "pointer not aligned to its element size");
+    n_rows += h_rows[i];
+  }
   if (max_groups < 1 || max_groups > (1ll << 40))
     return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "max_groups must be in [1, 2^40]");
-  if (n_rows > 0 && (!d_hashes || !d_vals)) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "row pointers are NULL");
-  if (misaligned(d_hashes, 8) || misaligned(d_vals, static_cast<size_t>(value_bytes)))
-    return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "pointer not aligned to its element size");
   DeviceGuard dg(ctx->device);
   if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
   const bool vf32 = value_bytes == 4;
@@ -1161,8 +1148,10 @@ tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, const uint64_t* d_hashes, c
   st = profile_events(ctx, &e0, &e1);
   if (st != TBGB_OK) return st;
   tbgb::RoutedArgs r{};
-  r.hashes = reinterpret_cast<const unsigned long long*>(d_hashes);
-  r.vals = d_vals;
+  for (int i = 0; i < n_senders; ++i) {
+    r.hashes[i] = reinterpret_cast<const unsigned long long*>(h_hashes[i]);
+    r.vals[i] = h_vals[i];
+  }
   r.seg_counts = d_seg_counts;
   r.n_senders = n_senders;
   r.digit_lo = digit_lo;
@@ -1183,21 +1172,24 @@ tbgb_status tbgb_radix_groupby_routed(tbgb_ctx* ctx, const uint64_t* d_hashes, c
   unsigned long long* fin = reinterpret_cast<unsigned long long*>(w + align256(P.table_bytes));
   e = tbgb::table_init(P, T, s, &ctx->launches, gate);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback table init", e);
-  tbgb::TableArgs a{};
-  a.keys = d_hashes;
-  a.cols.a = d_vals;
-  a.cols.dtype = vf32 ? TBGB_F32 : TBGB_F64;
-  a.cols.expr = TBGB_EXPR_A;
-  a.cols.pred = TBGB_PRED_NONE;
-  a.n = n_rows;
-  a.slots = P.slots;
-  a.ngroups = tbgb::table_counter(P, T);
-  a.max_groups = max_groups;
-  a.err = ctx->err;
-  a.table = T;
-  a.gate = gate;
-  e = tbgb::table_accumulate(P, a, s, &ctx->launches);
-  if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback table launch", e);
+  for (int i = 0; i < n_senders; ++i) {  // one gated pass over each sender's rows
+    if (h_rows[i] == 0) continue;
+    tbgb::TableArgs a{};
+    a.keys = reinterpret_cast<const int64_t*>(h_hashes[i]);
+    a.cols.a = h_vals[i];
+    a.cols.dtype = vf32 ? TBGB_F32 : TBGB_F64;
+    a.cols.expr = TBGB_EXPR_A;
+    a.cols.pred = TBGB_PRED_NONE;
+    a.n = h_rows[i];
+    a.slots = P.slots;
+    a.ngroups = tbgb::table_counter(P, T);
+    a.max_groups = max_groups;
+    a.err = ctx->err;
+    a.table = T;
+    a.gate = gate;
+    e = tbgb::table_accumulate(P, a, s, &ctx->launches);
+    if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback table launch", e);
+  }
   e = tbgb::table_finalize_hash(P, T, max_groups, d_out_keys, out, d_n_groups, fin, s, &ctx->launches, gate);
   if (e != cudaSuccess) return cuda_fail(ctx, TBGB_ERR_DISPATCH, "fallback table finalize", e);
   e = tbgb::radix_unhash_keys(d_out_keys, d_n_groups, max_groups, gate, ctx->num_sms, s, &ctx->launches);

@@ -89,86 +89,7 @@ __global__ void __launch_bounds__(XNT) exchange_merge_kernel(const double* own, 
   gstate_finalize(A, g, out);
 }
 
-constexpr long long CP_CHUNK = 65536;  // bytes a CTA copies per step
-constexpr int CP_NT = 256;
-
-struct CopyList {
-  const char* src[kMaxCopies];
-  char* dst[kMaxCopies];
-  long long bytes[kMaxCopies];
-  long long first_chunk[kMaxCopies + 1];  // exclusive prefix of the blocks' chunks
-  int width[kMaxCopies];                  // access width in bytes: 16, 8, 4 or 1
-  int n;
-};
-
-template <typename T>
-__device__ __forceinline__ void copy_span(const char* src, char* dst, long long len) {
-  const T* s = reinterpret_cast<const T*>(src);
-  T* d = reinterpret_cast<T*>(dst);
-  const long long m = len / static_cast<long long>(sizeof(T));
-  constexpr int U = 4;  // loads in flight before their stores
-  for (long long i0 = threadIdx.x; i0 < m; i0 += static_cast<long long>(CP_NT) * U) {
-    T v[U];
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const long long i = i0 + static_cast<long long>(u) * CP_NT;
-      if (i < m) v[u] = s[i];
-    }
-#pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const long long i = i0 + static_cast<long long>(u) * CP_NT;
-      if (i < m) d[i] = v[u];
-    }
-  }
-}
-
-__global__ void __launch_bounds__(CP_NT) copy_blocks_kernel(CopyList L) {
-  const long long total = L.first_chunk[L.n];
-  int b = 0;
-  for (long long c = blockIdx.x; c < total; c += gridDim.x) {
-    while (L.first_chunk[b + 1] <= c) ++b;  // c only grows, so b only moves forward
-    const long long off = (c - L.first_chunk[b]) * CP_CHUNK;
-    long long len = L.bytes[b] - off;
-    if (len > CP_CHUNK) len = CP_CHUNK;
-    const char* src = L.src[b] + off;
-    char* dst = L.dst[b] + off;
-    switch (L.width[b]) {
-      case 16: copy_span<uint4>(src, dst, len); break;
-      case 8: copy_span<unsigned long long>(src, dst, len); break;
-      case 4: copy_span<unsigned int>(src, dst, len); break;
-      default: copy_span<unsigned char>(src, dst, len); break;
-    }
-  }
-  __threadfence_system();
-}
-
 }  // namespace
-
-cudaError_t copy_blocks_launch(int n, const void* const* src, void* const* dst, const long long* bytes, int num_sms,
-                               cudaStream_t s, uint64_t* launches) {
-  if (n < 0 || n > kMaxCopies) return cudaErrorInvalidValue;
-  CopyList L{};
-  L.n = n;
-  long long chunks = 0;
-  for (int i = 0; i < n; ++i) {
-    L.src[i] = static_cast<const char*>(src[i]);
-    L.dst[i] = static_cast<char*>(dst[i]);
-    L.bytes[i] = bytes[i] > 0 ? bytes[i] : 0;
-    const uintptr_t a = reinterpret_cast<uintptr_t>(src[i]) | reinterpret_cast<uintptr_t>(dst[i]) |
-                        static_cast<uintptr_t>(L.bytes[i]);
-    L.width[i] = (a % 16 == 0) ? 16 : (a % 8 == 0) ? 8 : (a % 4 == 0) ? 4 : 1;
-    L.first_chunk[i] = chunks;
-    chunks += (L.bytes[i] + CP_CHUNK - 1) / CP_CHUNK;
-  }
-  L.first_chunk[n] = chunks;
-  if (chunks == 0) return cudaSuccess;
-  long long grid = static_cast<long long>(num_sms) * 4;
-  if (grid > chunks) grid = chunks;
-  copy_blocks_kernel<<<static_cast<unsigned>(grid), CP_NT, 0, s>>>(L);
-  cudaError_t e = cudaGetLastError();
-  if (e == cudaSuccess) (*launches)++;
-  return e;
-}
 
 long long exchange_slot_words(int G) { return static_cast<long long>(ST_COUNT) * G; }
 

@@ -45,12 +45,4 @@ cudaError_t exchange_push_launch(const PeerPtrs& peers, int world, int rank, int
 cudaError_t exchange_merge_launch(const void* own, int world, int G, unsigned long long epoch, uint32_t* err,
                                   const tbgb_moments* out, cudaStream_t s, uint64_t* launches);
 
-// Copies up to kMaxCopies blocks (src, dst, bytes) in one launch; the pointers may be peers'
-// memory mapped here (plain loads and stores over NVLink, no copy engine, no multicast).  Each
-// block uses the widest of 16 / 8 / 4 / 1-byte accesses its addresses and size allow.  Ends with a
-// system-scope fence, so a host synchronisation after it makes the writes visible to the peers.
-constexpr int kMaxCopies = 32;
-cudaError_t copy_blocks_launch(int n, const void* const* src, void* const* dst, const long long* bytes, int num_sms,
-                               cudaStream_t s, uint64_t* launches);
-
 }  // namespace tbgb

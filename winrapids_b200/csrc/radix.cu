@@ -80,13 +80,20 @@ __device__ __forceinline__ unsigned long long unfmix64(unsigned long long h) {
 }
 
 constexpr int kMaxSeg = 4096;  // second-pass segments: (sender, digit) pairs of a routed groupby
+constexpr int kMaxSenders = kRadixMaxSenders;
+
+struct SenderBases {  // first row of each sender's routed rows (addresses)
+  unsigned long long h[kMaxSenders];
+  unsigned long long v[kMaxSenders];
+};
 
 struct Aux {  // device bookkeeping inside the workspace
   unsigned long long cur1[kRadixDigits];
   unsigned long long cur2[kRadixBuckets];
   unsigned long long route_base[kRadixDigits];  // exact placement of a routing pass
   unsigned long long route_cap[kRadixDigits];
-  long long seg_base[kMaxSeg];
+  unsigned long long seg_h[kMaxSeg];            // address of a segment's first hash
+  unsigned long long seg_v[kMaxSeg];            // address of its first value
   long long seg_count[kMaxSeg];
   int seg_digit[kMaxSeg];                       // destination digit, relative to the first owned one
   long long seg_tiles[kMaxSeg + 1];
@@ -101,10 +108,10 @@ struct RxScatter {
   tbgb_columns cols;
   const uint64_t* mask;
   long long n;
-  // pass 2: segments of the first pass's buffer
-  const unsigned long long* src_h;
-  const void* src_v;
-  const long long* seg_base;
+  // pass 2: segments of rows ordered by the previous digit (the first pass's buffer, or routed rows
+  // in the senders' buffers), each at its own address
+  const unsigned long long* seg_h;
+  const unsigned long long* seg_v;
   const long long* seg_count;
   const int* seg_digit;
   const long long* seg_tiles;  // exclusive prefix of tiles per segment, n_seg + 1 entries
@@ -150,18 +157,21 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
   if (*reinterpret_cast<volatile const uint32_t*>(a.fallback)) return;
   if (tid < ND) hist[tid] = 0;
   const long long ntiles = SRC == 2 ? a.seg_tiles[a.n_seg] : (a.n + RX_TILE - 1) / RX_TILE;
-  const VT* src_v = static_cast<const VT*>(a.src_v);
   VT* dst_v = static_cast<VT*>(a.dst_v);
   int seg = 0;
   __syncthreads();
   for (long long t = blockIdx.x; t < ntiles; t += gridDim.x) {
     long long row0, rows;
     unsigned long long obase = 0;  // first destination bucket of this tile's source segment
+    const unsigned long long* src_h = nullptr;
+    const VT* src_v = nullptr;
     if constexpr (SRC == 2) {
       while (__ldg(a.seg_tiles + seg + 1) <= t) ++seg;
       const long long tin = t - __ldg(a.seg_tiles + seg);
-      row0 = __ldg(a.seg_base + seg) + tin * RX_TILE;
-      rows = __ldg(a.seg_count + seg) - tin * RX_TILE;
+      row0 = tin * RX_TILE;
+      rows = __ldg(a.seg_count + seg) - row0;
+      src_h = reinterpret_cast<const unsigned long long*>(__ldg(a.seg_h + seg));
+      src_v = reinterpret_cast<const VT*>(__ldg(a.seg_v + seg));
       obase = static_cast<unsigned long long>(__ldg(a.seg_digit + seg)) * ND;
     } else {
       row0 = t * RX_TILE;
@@ -178,7 +188,7 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
       for (int j = 0; j < RX_PER; ++j) {
         const int li = j * RX_NT + tid;
         if (li < rows) {
-          hv[j] = __ldcs(a.src_h + row0 + li);
+          hv[j] = __ldcs(src_h + row0 + li);
           vv[j] = __ldcs(src_v + row0 + li);
         }
       }
@@ -309,13 +319,15 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
   }
 }
 
-// Segments of pass 2 (one per first-pass bucket): base row, rows written, tiles.
-__global__ void rx_segments_kernel(Aux* x, unsigned long long cap1) {
+// Segments of pass 2 (one per first-pass bucket): addresses, rows written, tiles.
+__global__ void rx_segments_kernel(Aux* x, unsigned long long cap1, const unsigned long long* t1h, const char* t1v,
+                                   int value_bytes) {
   __shared__ long long tiles[kRadixDigits];
   const int d = threadIdx.x;
   unsigned long long c = x->cur1[d];
   if (c > cap1) c = cap1;
-  x->seg_base[d] = static_cast<long long>(d * cap1);
+  x->seg_h[d] = reinterpret_cast<unsigned long long>(t1h + d * cap1);
+  x->seg_v[d] = reinterpret_cast<unsigned long long>(t1v + d * cap1 * value_bytes);
   x->seg_count[d] = static_cast<long long>(c);
   x->seg_digit[d] = d;
   tiles[d] = static_cast<long long>((c + RX_TILE - 1) / RX_TILE);
@@ -365,21 +377,31 @@ __global__ void rx_route_bases_kernel(Aux* x, int64_t* digit_counts) {
   }
 }
 
-// Segments of a routed groupby: the received rows are n_senders blocks, each holding digits
-// [digit_lo, digit_lo + n_digits) in order; counts[sender * n_digits + j].
-__global__ void rx_routed_segments_kernel(Aux* x, const int64_t* counts, int n_seg, int n_digits) {
+// Segments of a routed groupby: sender s's rows of digits [digit_lo, digit_lo + n_digits) start
+// at B.h[s] / B.v[s], in digit order; counts[s * n_digits + j].  Segments are numbered digit-major
+// (digit j of every sender, then digit j + 1), so the second pass's tiles alternate between the
+// senders' buffers: peers' rows over NVLink and local rows from HBM are read at the same time.
+__global__ void rx_routed_segments_kernel(Aux* x, const int64_t* counts, SenderBases B, int n_senders, int n_digits,
+                                          int value_bytes) {
   if (threadIdx.x == 0) {
-    long long base = 0, tiles = 0;
-    for (int i = 0; i < n_seg; ++i) {
-      const long long c = counts[i] > 0 ? counts[i] : 0;
-      x->seg_base[i] = base;
-      x->seg_count[i] = c;
-      x->seg_digit[i] = i % n_digits;
-      x->seg_tiles[i] = tiles;
-      base += c;
-      tiles += (c + RX_TILE - 1) / RX_TILE;
+    unsigned long long off[kMaxSenders];
+    for (int s = 0; s < n_senders; ++s) off[s] = 0;
+    long long tiles = 0;
+    int i = 0;
+    for (int j = 0; j < n_digits; ++j) {
+      for (int s = 0; s < n_senders; ++s, ++i) {
+        const long long c0 = counts[static_cast<long long>(s) * n_digits + j];
+        const long long c = c0 > 0 ? c0 : 0;
+        x->seg_h[i] = B.h[s] + off[s] * 8;
+        x->seg_v[i] = B.v[s] + off[s] * static_cast<unsigned long long>(value_bytes);
+        x->seg_count[i] = c;
+        x->seg_digit[i] = j;
+        x->seg_tiles[i] = tiles;
+        off[s] += static_cast<unsigned long long>(c);
+        tiles += (c + RX_TILE - 1) / RX_TILE;
+      }
     }
-    x->seg_tiles[n_seg] = tiles;
+    x->seg_tiles[i] = tiles;
   }
 }
 
@@ -657,15 +679,14 @@ cudaError_t radix_groupby(const RadixPlan& P, const RadixArgs& a, void* ws, uint
     if (e != cudaSuccess) return e;
     (*launches)++;
   }
-  rx_segments_kernel<<<1, kRadixDigits, 0, s>>>(x, P.cap1);
+  rx_segments_kernel<<<1, kRadixDigits, 0, s>>>(x, P.cap1, t1h, static_cast<const char*>(t1v), P.vf32 ? 4 : 8);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   (*launches)++;
 
   RxScatter p2{};
-  p2.src_h = t1h;
-  p2.src_v = t1v;
-  p2.seg_base = x->seg_base;
+  p2.seg_h = x->seg_h;
+  p2.seg_v = x->seg_v;
   p2.seg_count = x->seg_count;
   p2.seg_digit = x->seg_digit;
   p2.seg_tiles = x->seg_tiles;
@@ -785,14 +806,18 @@ cudaError_t radix_groupby_routed(const RadixPlan& P, const RoutedArgs& r, void* 
   if (e != cudaSuccess) return e;
   if (ev0) cudaEventRecord(ev0, s);
   const int n_seg = r.n_senders * r.n_digits;
-  rx_routed_segments_kernel<<<1, 32, 0, s>>>(x, r.seg_counts, n_seg, r.n_digits);
+  SenderBases B{};
+  for (int i = 0; i < r.n_senders; ++i) {
+    B.h[i] = reinterpret_cast<unsigned long long>(r.hashes[i]);
+    B.v[i] = reinterpret_cast<unsigned long long>(r.vals[i]);
+  }
+  rx_routed_segments_kernel<<<1, 32, 0, s>>>(x, r.seg_counts, B, r.n_senders, r.n_digits, P.vf32 ? 4 : 8);
   e = cudaGetLastError();
   if (e != cudaSuccess) return e;
   (*launches)++;
   RxScatter p2{};
-  p2.src_h = r.hashes;
-  p2.src_v = r.vals;
-  p2.seg_base = x->seg_base;
+  p2.seg_h = x->seg_h;
+  p2.seg_v = x->seg_v;
   p2.seg_count = x->seg_count;
   p2.seg_digit = x->seg_digit;
   p2.seg_tiles = x->seg_tiles;

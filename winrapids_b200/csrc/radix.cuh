@@ -12,6 +12,7 @@ namespace tbgb {
 constexpr int kRadixDigits = 512;               // first-pass buckets (the top 9 hash bits)
 constexpr int kRadixBuckets = 262144;           // final buckets after the second pass (18 hash bits)
 constexpr long long kRadixMaxGroups = 1ll << 28;  // distinct keys one call serves (1024 per bucket)
+constexpr int kRadixMaxSenders = 64;            // senders of a routed groupby
 
 struct RadixPlan {
   bool vf32;                  // rows carry the value as f32 (an f32 column without expression)
@@ -64,8 +65,10 @@ cudaError_t radix_route(const RadixArgs& a, unsigned long long* out_h, void* out
                         int num_sms, cudaStream_t s, uint64_t* launches);
 
 struct RoutedArgs {
-  const unsigned long long* hashes;  // received rows: n_senders blocks of digits [digit_lo, +n_digits)
-  const void* vals;
+  // sender s's rows of digits [digit_lo, digit_lo + n_digits), in digit order, start at hashes[s] /
+  // vals[s] (device addresses: this GPU's memory or a peer's buffer mapped here)
+  const unsigned long long* hashes[kRadixMaxSenders];
+  const void* vals[kRadixMaxSenders];
   const int64_t* seg_counts;         // rows per (sender, digit), sender-major (device)
   int n_senders;
   int digit_lo;

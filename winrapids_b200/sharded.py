@@ -9,9 +9,11 @@ one all-to-all moves each owner's rows to it, and the owner groups what it recei
 result is sharded by owner.  Raw rows are shipped rather than per-shard partial tables:
 with 2^28 distinct keys a shard's partial table is about as large as its rows.
   * count / sum / mean: the routing is the radix path's first pass (``Context.radix_route``:
-    rows as (fmix64(key), value) ordered by the top 9 hash bits, digit d owned by rank
-    d * world // 512; an f32 column travels as f32, 12 bytes a row), and the owner runs the
-    remaining passes on what it received (``Context.radix_groupby_routed``).
+    rows as (fmix64(key), value) ordered by the top 9 hash bits, rank r owning the digits
+    [ceil(512 r / world), ceil(512 (r + 1) / world)); an f32 column travels as f32, 12 bytes a
+    row), and the owner runs the remaining passes on its digits (``Context.radix_groupby_routed``),
+    reading them in place from the senders' buffers over NVLink ("pull"), or after an NCCL
+    all-to-all into its own buffer.
   * other outputs (extrema, variances): a stable owner partition (``Context.hash_partition``,
     senders concatenated in rank order, so every key's rows keep their global order and the
     +-0 tie rule of the extrema stays exact) and ``Context.groupby_hash`` on the owner.
@@ -157,36 +159,6 @@ def owned_digits(world: int):
     return [(RADIX_DIGITS * r + world - 1) // world for r in range(world + 1)]
 
 
-def owner_totals(counts, lo):
-    """rows[s][q]: rows sender s routes to owner q, from every sender's 512 digit counts."""
-    w = len(counts)
-    return [[int(sum(counts[s][lo[q]:lo[q + 1]])) for q in range(w)] for s in range(w)]
-
-
-def peer_copy_plan(counts, rank: int, lo, cap: int, value_bytes: int, send_h: int, send_v: int, recv_bases):
-    """The blocks this rank stores into the owners' receive buffers, and each owner's row count.
-
-    counts[s][d]: rows sender s routed to digit d (every rank's digit counts); send_h / send_v:
-    this rank's routed rows (digit order); recv_bases[q]: owner q's receive buffer as mapped
-    here, hashes at its start and values cap * 8 bytes in (cap: the same on every rank).  Every
-    owner's buffer ends up laid out as the all-to-all lays it out: senders in rank order, each
-    sender's rows in digit order.
-    Returns ([(src, dst, nbytes), ...], [rows owner q receives for q in range(world)])."""
-    rows = owner_totals(counts, lo)
-    w = len(counts)
-    n_recv = [sum(rows[s][q] for s in range(w)) for q in range(w)]
-    copies, send_off = [], 0
-    for q in range(w):
-        r = rows[rank][q]
-        if r:
-            recv_off = sum(rows[s][q] for s in range(rank))
-            copies.append((send_h + send_off * 8, recv_bases[q] + recv_off * 8, r * 8))
-            copies.append((send_v + send_off * value_bytes, recv_bases[q] + cap * 8 + recv_off * value_bytes,
-                           r * value_bytes))
-        send_off += r
-    return copies, n_recv
-
-
 class ShardedHashGroupby:
     """Owner-sharded int64-key groupby of one shard's rows (see the module docstring).
 
@@ -194,22 +166,22 @@ class ShardedHashGroupby:
     are allocated once for shards of up to ``max_rows`` rows, receive buffers with
     ``recv_slack`` headroom over an even share.
 
-    ``exchange`` (count / sum / mean only): "nccl" moves the routed rows with
-    ``all_to_all_single``; "peer" maps every rank's receive buffer into every process (CUDA IPC)
-    and one launch of ``Context.copy_blocks`` stores this rank's rows straight into the owners'
-    buffers over NVLink.  The peer step: all-gather of the 512 digit counts of every rank (every
-    rank then knows every offset), the copy, a one-word all-reduce after it (the owners' groupby
-    starts only when every sender's copy is done), the owner's grouping.  A rank joins the next
-    step's all-gather only once its stream has finished grouping, so no sender overwrites a
-    buffer that is still being read.  Raises PeerMappingError when the mapping fails.
+    ``exchange`` says how routed rows (count / sum / mean) reach their owner:
+      * "nccl": ``all_to_all_single`` into every owner's receive buffer;
+      * "pull": no copy.  Every rank routes into a send buffer mapped into every process (CUDA
+        IPC); after an all-gather of the 512 digit counts of every rank, each owner's second
+        radix pass reads its digits straight from the senders' buffers (over NVLink for peers,
+        the tiles of different senders interleaved), and a one-word all-reduce at the end of the
+        step says that no owner reads a send buffer any more.  Raises PeerMappingError (on
+        every rank) when the mapping fails.
     """
 
     def __init__(self, ctx, dist, world: int, max_rows: int, max_groups_per_owner: int, fields, device,
                  recv_slack: float = 1.25, group=None, exchange: str = "nccl"):
         import torch
 
-        if exchange not in ("nccl", "peer"):
-            raise ValueError(f"exchange must be 'nccl' or 'peer', not {exchange!r}")
+        if exchange not in ("nccl", "pull"):
+            raise ValueError(f"exchange must be 'nccl' or 'pull', not {exchange!r}")
         self.ctx, self.dist, self.world, self.group = ctx, dist, int(world), group
         self.rank = dist.get_rank(group) if group is not None else dist.get_rank()
         self.device = device
@@ -217,49 +189,50 @@ class ShardedHashGroupby:
         self.max_groups = int(max_groups_per_owner)
         self.cap = int(max_rows * recv_slack) + 4096
         self.radix = set(fields) <= set(RADIX_FIELDS)
+        self.mode = exchange if self.radix else "nccl"
         self.out_keys = torch.empty(self.max_groups, dtype=torch.int64, device=device)
         self.out = {f: torch.empty(self.max_groups, dtype=torch.float64, device=device) for f in fields}
         self.n_groups = torch.zeros(1, dtype=torch.int64, device=device)
         self.n_recv = 0
         self.value_bytes = 8
         self._vdtype = None
+        self.own, self.mapped = 0, []
         if not self.radix:
             self.part_keys = torch.empty(max_rows, dtype=torch.int64, device=device)
             self.part_vals = torch.empty(max_rows, dtype=torch.float64, device=device)
             self.part_counts = torch.zeros(self.world, dtype=torch.int64, device=device)
             self.recv_keys = torch.empty(self.cap, dtype=torch.int64, device=device)
             self.recv_vals = torch.empty(self.cap, dtype=torch.float64, device=device)
-        else:
-            self.lo = owned_digits(self.world)
-            self.n_digits = self.lo[self.rank + 1] - self.lo[self.rank]
-            self.digit_counts = torch.zeros(RADIX_DIGITS, dtype=torch.int64, device=device)
-            self.seg_counts = torch.zeros(self.world * self.n_digits, dtype=torch.int64, device=device)
+            return
+        self.lo = owned_digits(self.world)
+        self.n_digits = self.lo[self.rank + 1] - self.lo[self.rank]
+        self.digit_counts = torch.zeros(RADIX_DIGITS, dtype=torch.int64, device=device)
+        self.seg_counts = torch.zeros(self.world * self.n_digits, dtype=torch.int64, device=device)
+        if self.mode == "nccl":
             self.send_h = torch.empty(max_rows, dtype=torch.int64, device=device)
-        self.peer = self.radix and exchange == "peer"
-        self.own, self.mapped = 0, []
-        if self.peer:
-            # senders place values at cap * 8 bytes into the owner's buffer: one cap on every rank
-            cap = torch.tensor([self.cap], dtype=torch.int64, device=device)
-            dist.all_reduce(cap, op=dist.ReduceOp.MAX, group=group)
-            self.cap = int(cap.item())
-            self.all_counts = torch.zeros(self.world * RADIX_DIGITS, dtype=torch.int64, device=device)
-            self.one = torch.zeros(1, dtype=torch.int64, device=device)
-            self.own = ctx.ipc_alloc(self.cap * 16)  # hashes, then values (8 bytes a row at most)
-            try:
-                self.recv_bases, self.mapped = map_peers(ctx, dist, self.world, self.rank, self.own, device, group)
-            except PeerMappingError:
-                self.close()
-                raise
-        elif self.radix:
             self.recv_h = torch.empty(self.cap, dtype=torch.int64, device=device)
+            return
+        self.all_counts = torch.zeros(self.world * RADIX_DIGITS, dtype=torch.int64, device=device)
+        self.one = torch.zeros(1, dtype=torch.int64, device=device)
+        # the send buffer holds hashes, then values from `span` rows in (8 bytes a value at most):
+        # one span on every rank, so any rank finds the values of any other
+        span = torch.tensor([self.max_rows], dtype=torch.int64, device=device)
+        dist.all_reduce(span, op=dist.ReduceOp.MAX, group=group)
+        self.span = int(span.item())
+        self.own = ctx.ipc_alloc(max(self.span, 1) * 16)
+        try:
+            self.bases, self.mapped = map_peers(ctx, dist, self.world, self.rank, self.own, device, group)
+        except PeerMappingError:
+            self.close()
+            raise
 
     def _value_buffers(self, vb):
         import torch
 
         dt = torch.float32 if vb == 4 else torch.float64
         if self._vdtype != dt:
-            self.send_v = torch.empty(self.max_rows, dtype=dt, device=self.device)
-            if not self.peer:
+            if self.mode == "nccl":
+                self.send_v = torch.empty(self.max_rows, dtype=dt, device=self.device)
                 self.recv_v = torch.empty(self.cap, dtype=dt, device=self.device)
             self._vdtype = dt
             self.value_bytes = vb
@@ -277,63 +250,30 @@ class ShardedHashGroupby:
             self.ctx.groupby_hash_into(self.recv_keys[:self.n_recv], self.recv_vals[:self.n_recv], self.max_groups,
                                        self.out_keys, self.out, self.n_groups)
             return
-        self._value_buffers(self.ctx.radix_value_bytes(a, b, c, expr, pred, threshold))
-        self.ctx.radix_route(keys, a, self.send_h, self.send_v, self.digit_counts, b=b, c=c, expr=expr, pred=pred,
-                             threshold=threshold, mask=mask)
-        if self.peer:
-            self.n_recv = self._exchange_peer()
-            recv_h, recv_v = self.own, self.own + self.cap * 8
+        vb = self.ctx.radix_value_bytes(a, b, c, expr, pred, threshold)
+        self._value_buffers(vb)
+        if self.mode == "pull":
+            send_h, send_v = self.own, self.own + self.span * 8
         else:
-            self.n_recv = self._exchange()
-            recv_h, recv_v = self.recv_h, self.recv_v
-        self.ctx.radix_groupby_routed(recv_h, recv_v, self.seg_counts, self.world, self.lo[self.rank],
-                                      self.n_digits, self.n_recv, self.max_groups, self.out_keys, self.out,
-                                      self.n_groups, value_bytes=self.value_bytes)
+            send_h, send_v = self.send_h, self.send_v
+        self.ctx.radix_route(keys, a, send_h, send_v, self.digit_counts, b=b, c=c, expr=expr, pred=pred,
+                             threshold=threshold, mask=mask)
+        if self.mode == "nccl":
+            rows = self._exchange()
+            hashes, vals = self.recv_h, self.recv_v
+        else:
+            rows, hashes, vals = self._senders_in_place(vb)
+        self.n_recv = sum(rows)
+        self.ctx.radix_groupby_routed(hashes, vals, rows, self.seg_counts, self.lo[self.rank], self.n_digits,
+                                      self.max_groups, self.out_keys, self.out, self.n_groups, value_bytes=vb)
+        if self.mode == "pull":  # every owner has read its rows: the send buffers may change again
+            self.dist.all_reduce(self.one, group=self.group)
 
-    def _exchange_peer(self) -> int:
-        """Every rank's digit counts to every rank, then this rank's rows into the owners' buffers
-        (one copy launch), then a one-word all-reduce: after it every owner's buffer is complete.
-        Every rank computes every owner's row count, so all raise together, before any row moves,
-        when some owner's buffer is too small."""
-        dist, g, w = self.dist, self.group, self.world
-        dist.all_gather_into_tensor(self.all_counts, self.digit_counts, group=g)
-        table = self.all_counts.view(w, RADIX_DIGITS)
-        lo, hi = self.lo[self.rank], self.lo[self.rank + 1]
-        self.seg_counts.view(w, self.n_digits).copy_(table[:, lo:hi])
-        counts = table.cpu().tolist()
-        copies, n_recv = peer_copy_plan(counts, self.rank, self.lo, self.cap, self.value_bytes,
-                                        self.send_h.data_ptr(), self.send_v.data_ptr(), self.recv_bases)
-        if max(n_recv) > self.cap:
-            raise RuntimeError(f"receive buffers too small (an owner needs {max(n_recv)} rows, room for {self.cap})")
-        self.ctx.copy_blocks(copies)
-        dist.all_reduce(self.one, group=g)
-        return n_recv[self.rank]
-
-    def close(self):
-        """Unmap the peers' receive buffers and free the own one (finish() first when every rank
-        is alive)."""
-        for p in self.mapped:
-            self.ctx.peer_close(p)
-        self.mapped = []
-        if self.own:
-            self.ctx.ipc_free(self.own)
-            self.own = 0
-
-    def finish(self):
-        """Orderly teardown on every rank: unmap, wait until no rank maps this rank's buffer, free it."""
-        if not self.peer:
-            return
-        self.ctx.sync()
-        for p in self.mapped:
-            self.ctx.peer_close(p)
-        self.mapped = []
-        self.dist.barrier(group=self.group)
-        self.close()
-
-    def _exchange(self) -> int:
+    def _exchange(self):
         """Digit counts to their owners, then the rows (senders concatenated in rank order, each
         sender's block in digit order).  Every rank takes the same collective steps; a rank whose
-        receive buffers are too small makes every rank raise before the rows move."""
+        receive buffers are too small makes every rank raise before the rows move.  Returns the
+        rows received from each sender."""
         import torch
 
         dist, g, lo = self.dist, self.group, self.lo
@@ -350,7 +290,43 @@ class ShardedHashGroupby:
             raise RuntimeError(f"receive buffers too small on some rank (this rank needs {n_recv} rows)")
         dist.all_to_all_single(self.recv_h[:n_recv], self.send_h[:n_send], r, s, group=g)
         dist.all_to_all_single(self.recv_v[:n_recv], self.send_v[:n_send], r, s, group=g)
-        return n_recv
+        return r
+
+    def _senders_in_place(self, vb):
+        """Every rank's digit counts to every rank, then where this owner's rows start in each
+        sender's buffer.  Returns (rows per sender, address of each sender's first row of this
+        rank's digits, of its first value)."""
+        dist, g, w = self.dist, self.group, self.world
+        dist.all_gather_into_tensor(self.all_counts, self.digit_counts, group=g)
+        table = self.all_counts.view(w, RADIX_DIGITS)
+        lo, hi = self.lo[self.rank], self.lo[self.rank + 1]
+        self.seg_counts.view(w, self.n_digits).copy_(table[:, lo:hi])
+        counts = table.cpu().tolist()
+        rows = [int(sum(counts[q][lo:hi])) for q in range(w)]
+        before = [int(sum(counts[q][:lo])) for q in range(w)]  # sender q's rows of lower digits
+        hashes = [self.bases[q] + 8 * before[q] for q in range(w)]
+        vals = [self.bases[q] + self.span * 8 + vb * before[q] for q in range(w)]
+        return rows, hashes, vals
+
+    def close(self):
+        """Unmap the peers' buffers and free the own one (finish() first when every rank is alive)."""
+        for p in self.mapped:
+            self.ctx.peer_close(p)
+        self.mapped = []
+        if self.own:
+            self.ctx.ipc_free(self.own)
+            self.own = 0
+
+    def finish(self):
+        """Orderly teardown on every rank: unmap, wait until no rank maps this rank's buffer, free it."""
+        if self.mode == "nccl":
+            return
+        self.ctx.sync()
+        for p in self.mapped:
+            self.ctx.peer_close(p)
+        self.mapped = []
+        self.dist.barrier(group=self.group)
+        self.close()
 
     @property
     def recv_bytes_per_row(self) -> int:
