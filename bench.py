@@ -79,8 +79,8 @@ WORKLOADS = {
     "highcard": dict(kind="highcard", rows=2_000_000_000, ids=1 << 28, seed=0,
                      desc="high-cardinality sharded: 2,000,000,000 rows; int64 key uniform over 2^28 random ids; "
                           "f32 value ~LogNormal(0,1); sum/count/mean; radix partitioning by key hash (with N GPUs "
-                          "rows routed to the owner of their hash digit and stored into its buffer over NVLink peer "
-                          "memory, each GPU groups the keys it owns)"),
+                          "rows routed by hash digit, each GPU reads the rows of the digits it owns from the other "
+                          "GPUs' buffers over NVLink peer memory and groups them)"),
 }
 
 
