@@ -614,7 +614,9 @@ class HashJob:
         n = self.n_local = hi - lo
         radix = (wl["kind"] == "highcard" and wl.get("table_mode", "auto") in ("auto", "radix")
                  and (world > 1 or (n >= 1 << 24 and (1 << 22) <= wl["ids"] <= (1 << 28))))
-        self.kernel = "rx_scatter_kernel + rx_agg_kernel (radix passes)" if radix else "table_kernel"
+        # the pipeline's outputs carry no extrema: its rows take the per-warp queued shared table
+        self.kernel = ("rx_scatter_kernel + rx_agg_kernel (radix passes)" if radix else
+                       "table_queue_kernel" if wl["kind"] == "pipeline" else "table_kernel")
         seed = wl["seed"]
         keys = torch.empty(n, dtype=torch.int64, device=dev)
         if wl["kind"] == "pipeline":

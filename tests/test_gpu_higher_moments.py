@@ -127,3 +127,31 @@ def test_descriptive_engine_returns_m3_m4():
     check_m34(got, want, keys, vals, G, "engine")
     s = g.group(3)
     assert s.skewness(True) > 0  # chi-square-like values are right-skewed
+
+
+NO_EXTREMA = ("count", "sum", "mean", "m2", "var_pop", "var_samp", "m3", "m4")
+
+
+@pytest.mark.parametrize("mode", ["local", "auto"])
+def test_table_hash_without_extrema(ctx, mode):
+    """Outputs without min / max: the int64-key shared-table path that queues rows per warp and
+    leaves the extrema arrays out, with m3 / m4."""
+    n, ids = 1_000_000, 50_000
+    keys = oracle.gen_keys_ids(n, ids, 0x78, 7)
+    vals = oracle.gen_values_normal(n, 2.0, 3.0, 7) ** 3
+    ctx.set_table_mode(mode)
+    try:
+        gk, out = ctx.groupby_hash(dev(keys), dev(vals), ids, fields=NO_EXTREMA)
+    finally:
+        ctx.set_table_mode("auto")
+    assert "min" not in out and "max" not in out
+    got = to_host(out)
+    order = np.argsort(gk.cpu().numpy())
+    got = {f: a[order] for f, a in got.items()}
+    want = oracle.groupby_i64(keys, vals, m34=True)
+    assert np.array_equal(gk.cpu().numpy()[order], want["keys"])
+    codes = np.searchsorted(want["keys"], keys)
+    # count / sum / mean / m2 / variances as `check` has them, extrema taken from the oracle
+    got["min"], got["max"] = want["mins"], want["maxs"]
+    check(got, want, abs_sums(codes, vals, want["keys"].size), f"hash no-extrema {mode}")
+    check_m34(got, want, codes, vals, want["keys"].size, f"hash no-extrema {mode}")

@@ -335,6 +335,75 @@ def test_hash_edge_keys_and_values(ctx, mode):
     hash_check(gk.cpu().numpy(), got, want, vals, keys, user, f"edge {mode}")
 
 
+PIPELINE_FIELDS = ("count", "sum", "mean", "m2", "var_pop", "var_samp")
+
+
+def check_no_extrema(got, want, absum, label):
+    got = dict(got)
+    got["min"], got["max"] = want["mins"], want["maxs"]
+    check(got, want, absum, label)
+
+
+@pytest.mark.parametrize("mode", ["auto", "local"])
+def test_fused_pipeline_bench_fields(ctx, mode):
+    """The fused pipeline with the bench's outputs (no extrema): the int64-key shared table with
+    rows queued per warp, Zipf head keys and a long tail through the global table."""
+    n, seed, ids = 3_000_000, 5, 1_000_000
+    cdf = oracle.zipf_cdf(ids, 1.1)
+    keys = oracle.gen_keys_cdf(n, cdf, SALT, seed)
+    a = oracle.gen_values_normal(n, 0.0, 1.0, seed + 1)
+    b = oracle.gen_values_normal(n, 0.0, 1.0, seed + 2)
+    c = oracle.gen_values_normal(n, 0.0, 1.0, seed + 3)
+    ctx.set_table_mode(mode)
+    try:
+        gk, out = ctx.groupby_hash(dev(keys), dev(a), ids, b=dev(b), c=dev(c), expr="a*b+c", pred=">",
+                                   threshold=0.0, fields=PIPELINE_FIELDS)
+    finally:
+        ctx.set_table_mode("auto")
+    got = to_host(out)
+    gk = gk.cpu().numpy()
+    m = host_mask(n, a, ">", 0.0)
+    v = host_value(a, b, c, "a*b+c")
+    want = oracle.groupby_i64(keys, v, mask=m)
+    order = np.argsort(gk, kind="stable")
+    assert np.array_equal(gk[order], want["keys"])
+    live = rows_of(m, n)
+    codes = np.searchsorted(want["keys"], keys[live])
+    check_no_extrema({f: x[order] for f, x in got.items()}, want, abs_sums(codes, v[live], want["keys"].size),
+                     f"pipeline fields {mode}")
+
+
+def test_hash_edge_keys_without_extrema(ctx):
+    """INT64_MIN / INT64_MAX / 0 / -1 keys, a NaN-only group, +-inf and masked rows, without extrema
+    (the queued shared-table path, INT64_MIN through the global table's sentinel slot)."""
+    rng = np.random.default_rng(98)
+    n = 400_000
+    pool = np.array([np.iinfo(np.int64).min, np.iinfo(np.int64).max, 0, -1, 1, 12345], dtype=np.int64)
+    keys = np.where(rng.random(n) < 0.5, pool[rng.integers(0, pool.size, n)], rng.integers(-2**62, 2**62, n))
+    keys = keys.astype(np.int64)
+    vals = rng.normal(size=n)
+    vals[rng.random(n) < 0.01] = np.inf
+    vals[rng.random(n) < 0.01] = -np.inf
+    vals[keys == 12345] = np.nan
+    user = host_mask(n)
+    user[::7] = np.uint64(0)
+    ctx.set_table_mode("local")
+    try:
+        gk, out = ctx.groupby_hash(dev(keys), dev(vals), n, mask=dev_mask(user), fields=PIPELINE_FIELDS)
+    finally:
+        ctx.set_table_mode("auto")
+    got = to_host(out)
+    gk = gk.cpu().numpy()
+    want = oracle.groupby_i64(keys, vals, mask=user)
+    assert 12345 in want["keys"] and np.iinfo(np.int64).min in want["keys"]
+    order = np.argsort(gk, kind="stable")
+    assert np.array_equal(gk[order], want["keys"])
+    live = rows_of(user, n)
+    codes = np.searchsorted(want["keys"], keys[live])
+    check_no_extrema({f: x[order] for f, x in got.items()}, want, abs_sums(codes, vals[live], want["keys"].size),
+                     "edge no-extrema")
+
+
 def test_hash_filter_rejects_everything(ctx):
     n = 50_000
     keys = np.arange(n, dtype=np.int64)

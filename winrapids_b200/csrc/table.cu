@@ -149,8 +149,8 @@ struct SlotArrays {
       s2[s] = 0.0;
       if (s3) s3[s] = 0.0;
       if (s4) s4[s] = 0.0;
-      mn[s] = f2o(pos_inf());
-      mx[s] = f2o(neg_inf());
+      if (mn) mn[s] = f2o(pos_inf());
+      if (mx) mx[s] = f2o(neg_inf());
       if (zf) zf[s] = ~0ull;
       cnt[s] = 0;
     }
@@ -423,6 +423,196 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
       }
       lt.flush(s, T + static_cast<unsigned long long>(gs) * W, M34, EXT);
     }
+  }
+}
+
+// ---- int64 keys, shared-memory pre-aggregation with full warps ---------------------------
+// table_kernel runs one row per lane: with a filter about half the lanes idle, and a warp whose
+// lanes split between the shared table and the global one runs both paths one after the other
+// (in the fused pipeline ncu counted 11 active lanes per warp instruction).  Here each warp
+// queues its live rows in a shared-memory ring and takes them 32 at a time: every lane probes
+// the shared table; rows it cannot take are queued again and go to the global table 32 at a
+// time, with the first probe's key and shift words loaded together.  Extrema are not compiled
+// in (table_kernel keeps that variant), so the slot arrays skip min / max / first-zero.
+constexpr int QN = 64;  // ring entries per warp: fewer than 32 pending + 32 pushed
+
+template <bool FULL>
+__host__ __device__ constexpr size_t queue_table_bytes(bool m34) {
+  return FULL ? static_cast<size_t>(LS_FULL) * 8 * (m34 ? 7 : 5) + 16 : static_cast<size_t>(LS_SC) * 20 + 16;
+}
+constexpr size_t kQueueRingBytes = static_cast<size_t>(2) * (TNT / 32) * QN * 16;
+
+template <bool FULL>
+__device__ __forceinline__ unsigned char* carve_queue_table(LocalTable<FULL>& lt, unsigned char* sm, bool m34) {
+  constexpr int LS = LocalTable<FULL>::LS;
+  unsigned char* q = sm;
+  lt.key = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+  if constexpr (FULL) {
+    lt.K = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+    lt.s1 = reinterpret_cast<double*>(q); q += LS * 8;
+    lt.s2 = reinterpret_cast<double*>(q); q += LS * 8;
+    lt.cnt = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
+    lt.s3 = lt.s4 = nullptr;
+    if (m34) {
+      lt.s3 = reinterpret_cast<double*>(q); q += LS * 8;
+      lt.s4 = reinterpret_cast<double*>(q); q += LS * 8;
+    }
+    lt.mn = lt.mx = lt.zf = nullptr;
+  } else {
+    lt.s1 = reinterpret_cast<double*>(q); q += LS * 8;
+    lt.nn = reinterpret_cast<uint32_t*>(q); q += LS * 4;
+  }
+  lt.fill = reinterpret_cast<uint32_t*>(q);
+  return q + 16;
+}
+
+// One non-NaN row into global slot p; kb: the slot's shift word as loaded with the first probe
+// (K_UNSET: not known, read it again).  The shift is set once, so a loaded value stays valid.
+template <bool FULL, bool M34>
+__device__ __forceinline__ void global_row_k(unsigned long long* p, double v, unsigned long long kb) {
+  if constexpr (FULL) {
+    atomicAdd(p + FL_NN, 1ull);
+    if (is_finite(v)) {
+      const double K = kb != K_UNSET ? bitsd(kb) : slot_shift(p + FL_K, v);
+      const double d = v - K, dd = d * d;
+      atomicAdd(reinterpret_cast<double*>(p + FL_S1), d);
+      atomicAdd(reinterpret_cast<double*>(p + FL_S2), dd);
+      atomicAdd(p + FL_NF, 1ull);
+      if constexpr (M34) {
+        atomicAdd(reinterpret_cast<double*>(p + FL_S3), dd * d);
+        atomicAdd(reinterpret_cast<double*>(p + FL_S4), dd * dd);
+      }
+    }
+  } else {
+    atomicAdd(p + SC_NN, 1ull);
+    if (is_finite(v)) atomicAdd(reinterpret_cast<double*>(p + SC_SUM), v);
+  }
+}
+
+template <bool F32, bool FULL, bool M34>
+__global__ void __launch_bounds__(TNT, 1) table_queue_kernel(TableArgs a) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  if (a.gate && *a.gate == 0u) return;
+  constexpr int W = slot_words<FULL>();
+  constexpr unsigned FULLMASK = 0xFFFFFFFFu;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const unsigned below = (1u << lane) - 1u;
+  LocalTable<FULL> lt;
+  unsigned char* rq = carve_queue_table<FULL>(lt, sm, M34);
+  rq += (16 - reinterpret_cast<uintptr_t>(rq) % 16) % 16;
+  // this warp's rings: rows waiting for the shared table (lk / lv), rows for the global table (gk / gv)
+  unsigned long long* lk = reinterpret_cast<unsigned long long*>(rq) + static_cast<size_t>(warp) * QN;
+  double* lv = reinterpret_cast<double*>(rq) + static_cast<size_t>(TNT / 32 + warp) * QN;
+  unsigned long long* gk = reinterpret_cast<unsigned long long*>(rq) + static_cast<size_t>(2 * (TNT / 32) + warp) * QN;
+  double* gv = reinterpret_cast<double*>(rq) + static_cast<size_t>(3 * (TNT / 32) + warp) * QN;
+  lt.init(tid);
+  __syncthreads();
+
+  const long long n = a.n;
+  const char* keys = static_cast<const char*>(a.keys);
+  const char* col_a = static_cast<const char*>(a.cols.a);
+  const int expr = a.cols.expr, pred = a.cols.pred;
+  const double thr = a.cols.threshold;
+  const bool need_b = expr != TBGB_EXPR_A, need_c = expr == TBGB_EXPR_MUL_ADD;
+  const uint64_t* mask = a.mask;
+  unsigned long long* T = a.table;
+  const unsigned long long hmask = a.slots - 1;
+  unsigned lhead = 0, ltail = 0, ghead = 0, gtail = 0;  // ring positions (the same in every lane)
+
+  auto push = [&](unsigned long long* rk, double* rv, unsigned& head, bool live, unsigned long long k, double v) {
+    const unsigned bal = __ballot_sync(FULLMASK, live);
+    if (live) {
+      const unsigned i = (head + __popc(bal & below)) & (QN - 1);
+      rk[i] = k;
+      rv[i] = v;
+    }
+    head += __popc(bal);
+    __syncwarp();
+  };
+  // cnt (<= 32) rows from the global ring: first probe with the key and shift words together
+  auto global_batch = [&](unsigned cnt) {
+    const bool act = static_cast<unsigned>(lane) < cnt;
+    unsigned long long k = 0;
+    double v = 0.0;
+    if (act) {
+      const unsigned i = (gtail + lane) & (QN - 1);
+      k = gk[i];
+      v = gv[i];
+    }
+    gtail += cnt;
+    __syncwarp();
+    if (act) {
+      const unsigned long long h = fmix64(k) & hmask;
+      unsigned long long cur = 0, kb = K_UNSET;
+      if (k != kEmptyKey) {
+        cur = __ldcg(T + h * W);
+        if constexpr (FULL) kb = __ldcg(T + h * W + FL_K);
+      }
+      const long long gs = hash_slot_from<FULL>(a, k, h, cur);
+      if (gs >= 0 && !is_nan(v)) {
+        if (static_cast<unsigned long long>(gs) != h) kb = K_UNSET;
+        global_row_k<FULL, M34>(T + static_cast<unsigned long long>(gs) * W, v, kb);
+      }
+    }
+  };
+  // cnt (<= 32) rows from the shared-table ring; the ones the table cannot take are queued again
+  auto local_batch = [&](unsigned cnt) {
+    const bool act = static_cast<unsigned>(lane) < cnt;
+    unsigned long long k = 0;
+    double v = 0.0;
+    if (act) {
+      const unsigned i = (ltail + lane) & (QN - 1);
+      k = lk[i];
+      v = lv[i];
+    }
+    ltail += cnt;
+    __syncwarp();
+    int ls = -1;
+    if (act) {
+      ls = lt.find(k);
+      if (ls >= 0 && !is_nan(v)) lt.row(ls, v, 0, M34, false);
+    }
+    push(gk, gv, ghead, act && ls < 0, k, v);
+    if (ghead - gtail >= 32u) global_batch(32u);
+  };
+
+  // the row loads run one step ahead, as in table_kernel
+  const long long step = static_cast<long long>(gridDim.x) * TNT;
+  long long nk = 0;
+  double na = 0.0, nb = 0.0, nc = 0.0;
+  bool nin = false;
+  auto load_row = [&](long long row) {
+    nk = 0; na = 0.0; nb = 0.0; nc = 0.0;
+    nin = row < n;
+    if (nin && mask) nin = (__ldg(mask + (row >> 6)) >> (row & 63)) & 1ull;
+    if (nin) {
+      nk = load_key<true>(keys, row);
+      na = load_val<F32>(col_a, row);
+      if (need_b) nb = load_val<F32>(a.cols.b, row);
+      if (need_c) nc = load_val<F32>(a.cols.c, row);
+    }
+  };
+  load_row(static_cast<long long>(blockIdx.x) * TNT + tid);
+  for (long long base = static_cast<long long>(blockIdx.x) * TNT; base < n; base += step) {
+    const long long k = nk;
+    const double va = na, vb = nb, vc = nc;
+    const bool in = nin;
+    load_row(base + step + tid);
+    const bool live = in && eval_pred(pred, va, thr);
+    push(lk, lv, lhead, live, static_cast<unsigned long long>(k), eval_expr(expr, va, vb, vc));
+    if (lhead - ltail >= 32u) local_batch(32u);
+  }
+  if (lhead != ltail) local_batch(lhead - ltail);
+  while (ghead != gtail) global_batch(ghead - gtail < 32u ? ghead - gtail : 32u);
+
+  __syncthreads();
+  for (int s = tid; s < LocalTable<FULL>::LS; s += TNT) {
+    const unsigned long long k = lt.key[s];
+    if (k == kEmptyKey) continue;
+    const unsigned long long h = fmix64(k) & hmask;
+    const long long gs = hash_slot_from<FULL>(a, k, h, __ldcg(T + h * W));
+    if (gs < 0) continue;
+    lt.flush(s, T + static_cast<unsigned long long>(gs) * W, M34, false);
   }
 }
 
@@ -867,8 +1057,24 @@ __global__ void __launch_bounds__(FIN_NT) table_compact_kernel(const unsigned lo
   }
 }
 
+template <bool F32, bool FULL>
+cudaError_t launch_queue(const TablePlan& P, const TableArgs& a, cudaStream_t s) {
+  const bool m34 = FULL && a.m34;
+  auto k = m34 ? table_queue_kernel<F32, FULL, true> : table_queue_kernel<F32, FULL, false>;
+  const size_t smem = queue_table_bytes<FULL>(m34) + 16 + kQueueRingBytes;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
+  if (e != cudaSuccess) return e;
+  k<<<P.grid, TNT, smem, s>>>(a);
+  return cudaGetLastError();
+}
+
 template <bool KEY64, bool F32, bool FULL, bool LOCAL>
 cudaError_t launch_table(const TablePlan& P, const TableArgs& a, cudaStream_t s) {
+  // int64 keys into a per-CTA shared table: the full-warp variant, unless extrema are asked for
+  // or the rows are a partition's part (row count on the device)
+  if constexpr (KEY64 && LOCAL) {
+    if (!(FULL && a.extrema) && a.dev_count == nullptr) return launch_queue<F32, FULL>(P, a, s);
+  }
   auto k = table_kernel<KEY64, F32, FULL, LOCAL, false, false>;
   if constexpr (FULL) {
     if (a.m34 && a.extrema) k = table_kernel<KEY64, F32, FULL, LOCAL, true, true>;
