@@ -105,11 +105,12 @@ __device__ __forceinline__ void global_row(unsigned long long* p, double v, long
       const double d = v - slot_shift(p + FL_K, v), dd = d * d;
       atomicAdd(reinterpret_cast<double*>(p + FL_S1), d);
       atomicAdd(reinterpret_cast<double*>(p + FL_S2), dd);
-      atomicAdd(p + FL_NF, 1ull);
       if (m34) {
         atomicAdd(reinterpret_cast<double*>(p + FL_S3), dd * d);
         atomicAdd(reinterpret_cast<double*>(p + FL_S4), dd * dd);
       }
+    } else {
+      atomicAdd(p + FL_NI, 1ull);
     }
     if (extrema) {
       const unsigned long long o = f2o(v);
@@ -191,8 +192,9 @@ struct SlotArrays {
   // the global K_g, sum (d + off)^k with off = K_l - K_g.
   __device__ __forceinline__ void flush(int s, unsigned long long* p, bool m34, bool extrema) {
     if constexpr (FULL) {
-      const unsigned long long n_nn = cnt[s] & 0xFFFFFFFFull, n_f = n_nn - (cnt[s] >> 32);
+      const unsigned long long n_nn = cnt[s] & 0xFFFFFFFFull, n_inf = cnt[s] >> 32, n_f = n_nn - n_inf;
       if (n_nn) atomicAdd(p + FL_NN, n_nn);
+      if (n_inf) atomicAdd(p + FL_NI, n_inf);
       if (n_f) {
         const double Kl = bitsd(K[s]);
         const double Kg = slot_shift(p + FL_K, Kl);
@@ -200,7 +202,6 @@ struct SlotArrays {
         const double o2 = off * off;
         atomicAdd(reinterpret_cast<double*>(p + FL_S1), a1 + nfd * off);
         atomicAdd(reinterpret_cast<double*>(p + FL_S2), a2 + off * (2.0 * a1 + nfd * off));
-        atomicAdd(p + FL_NF, n_f);
         if (m34) {
           const double a3 = s3[s], a4 = s4[s];
           atomicAdd(reinterpret_cast<double*>(p + FL_S3), a3 + 3.0 * off * a2 + 3.0 * o2 * a1 + nfd * o2 * off);
@@ -222,10 +223,10 @@ struct SlotArrays {
   }
 };
 
-// Per-CTA shared-memory hash table of a few thousand slots.
-template <bool FULL>
+// Per-CTA shared-memory hash table of a few thousand slots (LSV: slots, a power of two).
+template <bool FULL, int LSV = (FULL ? LS_FULL : LS_SC)>
 struct LocalTable : SlotArrays<FULL> {
-  static constexpr int LS = FULL ? LS_FULL : LS_SC;
+  static constexpr int LS = LSV;
   static constexpr int LIMIT = LS * 3 / 4;  // admission stops at this fill
   unsigned long long* key;
   uint32_t* fill;
@@ -436,15 +437,21 @@ __global__ void __launch_bounds__(TNT, 1) table_kernel(TableArgs a) {
 // in (table_kernel keeps that variant), so the slot arrays skip min / max / first-zero.
 constexpr int QN = 64;  // ring entries per warp: fewer than 32 pending + 32 pushed
 
-template <bool FULL>
-__host__ __device__ constexpr size_t queue_table_bytes(bool m34) {
-  return FULL ? static_cast<size_t>(LS_FULL) * 8 * (m34 ? 7 : 5) + 16 : static_cast<size_t>(LS_SC) * 20 + 16;
+// Slots of the queued kernel's table: with the five FULL arrays (no m3 / m4) 4096 slots still
+// fit beside the rings, which keeps more of a long-tailed key set in shared memory.
+template <bool FULL, bool M34>
+__host__ __device__ constexpr int queue_slots() { return FULL ? (M34 ? LS_FULL : 2 * LS_FULL) : LS_SC; }
+
+template <bool FULL, bool M34>
+__host__ __device__ constexpr size_t queue_table_bytes() {
+  return FULL ? static_cast<size_t>(queue_slots<FULL, M34>()) * 8 * (M34 ? 7 : 5) + 16
+              : static_cast<size_t>(queue_slots<FULL, M34>()) * 20 + 16;
 }
 constexpr size_t kQueueRingBytes = static_cast<size_t>(2) * (TNT / 32) * QN * 16;
 
-template <bool FULL>
-__device__ __forceinline__ unsigned char* carve_queue_table(LocalTable<FULL>& lt, unsigned char* sm, bool m34) {
-  constexpr int LS = LocalTable<FULL>::LS;
+template <bool FULL, int LSV>
+__device__ __forceinline__ unsigned char* carve_queue_table(LocalTable<FULL, LSV>& lt, unsigned char* sm, bool m34) {
+  constexpr int LS = LSV;
   unsigned char* q = sm;
   lt.key = reinterpret_cast<unsigned long long*>(q); q += LS * 8;
   if constexpr (FULL) {
@@ -477,11 +484,12 @@ __device__ __forceinline__ void global_row_k(unsigned long long* p, double v, un
       const double d = v - K, dd = d * d;
       atomicAdd(reinterpret_cast<double*>(p + FL_S1), d);
       atomicAdd(reinterpret_cast<double*>(p + FL_S2), dd);
-      atomicAdd(p + FL_NF, 1ull);
       if constexpr (M34) {
         atomicAdd(reinterpret_cast<double*>(p + FL_S3), dd * d);
         atomicAdd(reinterpret_cast<double*>(p + FL_S4), dd * dd);
       }
+    } else {
+      atomicAdd(p + FL_NI, 1ull);
     }
   } else {
     atomicAdd(p + SC_NN, 1ull);
@@ -497,8 +505,9 @@ __global__ void __launch_bounds__(TNT, 1) table_queue_kernel(TableArgs a) {
   constexpr unsigned FULLMASK = 0xFFFFFFFFu;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const unsigned below = (1u << lane) - 1u;
-  LocalTable<FULL> lt;
-  unsigned char* rq = carve_queue_table<FULL>(lt, sm, M34);
+  using LT = LocalTable<FULL, queue_slots<FULL, M34>()>;
+  LT lt;
+  unsigned char* rq = carve_queue_table(lt, sm, M34);
   rq += (16 - reinterpret_cast<uintptr_t>(rq) % 16) % 16;
   // this warp's rings: rows waiting for the shared table (lk / lv), rows for the global table (gk / gv)
   unsigned long long* lk = reinterpret_cast<unsigned long long*>(rq) + static_cast<size_t>(warp) * QN;
@@ -568,45 +577,134 @@ __global__ void __launch_bounds__(TNT, 1) table_queue_kernel(TableArgs a) {
     ltail += cnt;
     __syncwarp();
     int ls = -1;
-    if (act) {
-      ls = lt.find(k);
-      if (ls >= 0 && !is_nan(v)) lt.row(ls, v, 0, M34, false);
+    if (act) ls = lt.find(k);
+    bool mine = act && ls >= 0 && !is_nan(v);  // the lane updates the shared table itself
+    if constexpr (FULL) {
+      // Skewed keys put several lanes of a batch on one slot.  The largest such group is summed
+      // across the warp first and applied once by its lowest lane, which takes those same-address
+      // atomics (serialised within the instruction and across warps) off the hottest slots.
+      const unsigned g = __match_any_sync(FULLMASK, mine ? ls : -1 - lane);
+      const unsigned sz = mine ? static_cast<unsigned>(__popc(g)) : 0u;
+      const unsigned best = __reduce_max_sync(FULLMASK, (sz << 5) | (31u - static_cast<unsigned>(lane)));
+      if ((best >> 5) >= 2u) {
+        const int bl = 31 - static_cast<int>(best & 31u);
+        const unsigned bg = __shfl_sync(FULLMASK, g, bl);
+        const int slot = __shfl_sync(FULLMASK, ls, bl);
+        const bool in = (bg >> lane) & 1u;
+        const bool fin = in && is_finite(v);
+        const unsigned finm = __ballot_sync(FULLMASK, fin);
+        const int leader = __ffs(bg) - 1;
+        const double v0 = __shfl_sync(FULLMASK, v, finm ? __ffs(finm) - 1 : 0);
+        unsigned long long kb = K_UNSET;
+        if (lane == leader && finm) {  // the slot's shift, set by the group's first finite row when unset
+          kb = *reinterpret_cast<volatile unsigned long long*>(lt.K + slot);
+          if (kb == K_UNSET) {
+            kb = atomicCAS(lt.K + slot, K_UNSET, dbits(v0));
+            if (kb == K_UNSET) kb = dbits(v0);
+          }
+        }
+        kb = __shfl_sync(FULLMASK, kb, leader);
+        const double d = fin ? v - bitsd(kb) : 0.0, dd = d * d;
+        double s1 = d, s2 = dd, s3 = 0.0, s4 = 0.0;
+        if constexpr (M34) {
+          s3 = dd * d;
+          s4 = dd * dd;
+        }
+#pragma unroll
+        for (int off = 16; off > 0; off >>= 1) {
+          s1 += __shfl_xor_sync(FULLMASK, s1, off);
+          s2 += __shfl_xor_sync(FULLMASK, s2, off);
+          if constexpr (M34) {
+            s3 += __shfl_xor_sync(FULLMASK, s3, off);
+            s4 += __shfl_xor_sync(FULLMASK, s4, off);
+          }
+        }
+        if (lane == leader) {
+          unsigned int* c32 = reinterpret_cast<unsigned int*>(lt.cnt + slot);
+          atomicAdd(c32, static_cast<unsigned>(__popc(bg)));
+          const unsigned ninf = static_cast<unsigned>(__popc(bg & ~finm));
+          if (ninf) atomicAdd(c32 + 1, ninf);
+          if (finm) {
+            atomicAdd(lt.s1 + slot, s1);
+            atomicAdd(lt.s2 + slot, s2);
+            if constexpr (M34) {
+              atomicAdd(lt.s3 + slot, s3);
+              atomicAdd(lt.s4 + slot, s4);
+            }
+          }
+        }
+        if (in) mine = false;
+      }
     }
+    if (mine) lt.row(ls, v, 0, M34, false);
     push(gk, gv, ghead, act && ls < 0, k, v);
     if (ghead - gtail >= 32u) global_batch(32u);
   };
 
-  // the row loads run one step ahead, as in table_kernel
-  const long long step = static_cast<long long>(gridDim.x) * TNT;
-  long long nk = 0;
-  double na = 0.0, nb = 0.0, nc = 0.0;
-  bool nin = false;
-  auto load_row = [&](long long row) {
-    nk = 0; na = 0.0; nb = 0.0; nc = 0.0;
-    nin = row < n;
-    if (nin && mask) nin = (__ldg(mask + (row >> 6)) >> (row & 63)) & 1ull;
-    if (nin) {
-      nk = load_key<true>(keys, row);
-      na = load_val<F32>(col_a, row);
-      if (need_b) nb = load_val<F32>(a.cols.b, row);
-      if (need_c) nc = load_val<F32>(a.cols.c, row);
+  // Each thread takes a pair of adjacent rows per step (one 16-byte load per column when the
+  // columns are 16-byte aligned); the loads run one step ahead, as in table_kernel.
+  constexpr int QR = 2;
+  const long long step = static_cast<long long>(gridDim.x) * TNT * QR;
+  // (a row mask keeps the per-row loads: the columns of rows it drops are not read)
+  const bool vec = !F32 && mask == nullptr && ((reinterpret_cast<uintptr_t>(keys) | reinterpret_cast<uintptr_t>(col_a) |
+                             reinterpret_cast<uintptr_t>(need_b ? a.cols.b : nullptr) |
+                             reinterpret_cast<uintptr_t>(need_c ? a.cols.c : nullptr)) & 15u) == 0;
+  long long nk[QR];
+  double na[QR], nb[QR], nc[QR];
+  bool nin[QR];
+  auto load_rows = [&](long long r0) {  // rows r0, r0 + 1
+#pragma unroll
+    for (int r = 0; r < QR; ++r) {
+      nk[r] = 0; na[r] = 0.0; nb[r] = 0.0; nc[r] = 0.0;
+      nin[r] = r0 + r < n;
+    }
+    if (vec && r0 + 1 < n) {
+      const longlong2 k2 = __ldcs(reinterpret_cast<const longlong2*>(keys) + (r0 >> 1));
+      const double2 a2 = __ldcs(reinterpret_cast<const double2*>(col_a) + (r0 >> 1));
+      nk[0] = k2.x; nk[1] = k2.y; na[0] = a2.x; na[1] = a2.y;
+      if (need_b) {
+        const double2 b2 = __ldcs(reinterpret_cast<const double2*>(a.cols.b) + (r0 >> 1));
+        nb[0] = b2.x; nb[1] = b2.y;
+      }
+      if (need_c) {
+        const double2 c2 = __ldcs(reinterpret_cast<const double2*>(a.cols.c) + (r0 >> 1));
+        nc[0] = c2.x; nc[1] = c2.y;
+      }
+    } else {
+#pragma unroll
+      for (int r = 0; r < QR; ++r) {
+        if (nin[r] && mask) nin[r] = (__ldg(mask + ((r0 + r) >> 6)) >> ((r0 + r) & 63)) & 1ull;
+        if (nin[r]) {
+          nk[r] = load_key<true>(keys, r0 + r);
+          na[r] = load_val<F32>(col_a, r0 + r);
+          if (need_b) nb[r] = load_val<F32>(a.cols.b, r0 + r);
+          if (need_c) nc[r] = load_val<F32>(a.cols.c, r0 + r);
+        }
+      }
     }
   };
-  load_row(static_cast<long long>(blockIdx.x) * TNT + tid);
-  for (long long base = static_cast<long long>(blockIdx.x) * TNT; base < n; base += step) {
-    const long long k = nk;
-    const double va = na, vb = nb, vc = nc;
-    const bool in = nin;
-    load_row(base + step + tid);
-    const bool live = in && eval_pred(pred, va, thr);
-    push(lk, lv, lhead, live, static_cast<unsigned long long>(k), eval_expr(expr, va, vb, vc));
-    if (lhead - ltail >= 32u) local_batch(32u);
+  load_rows(static_cast<long long>(blockIdx.x) * TNT * QR + 2 * tid);
+  for (long long base = static_cast<long long>(blockIdx.x) * TNT * QR; base < n; base += step) {
+    long long k[QR];
+    double va[QR], vb[QR], vc[QR];
+    bool in[QR];
+#pragma unroll
+    for (int r = 0; r < QR; ++r) {
+      k[r] = nk[r]; va[r] = na[r]; vb[r] = nb[r]; vc[r] = nc[r]; in[r] = nin[r];
+    }
+    load_rows(base + step + 2 * tid);
+#pragma unroll
+    for (int r = 0; r < QR; ++r) {
+      const bool live = in[r] && eval_pred(pred, va[r], thr);
+      push(lk, lv, lhead, live, static_cast<unsigned long long>(k[r]), eval_expr(expr, va[r], vb[r], vc[r]));
+      if (lhead - ltail >= 32u) local_batch(32u);
+    }
   }
   if (lhead != ltail) local_batch(lhead - ltail);
   while (ghead != gtail) global_batch(ghead - gtail < 32u ? ghead - gtail : 32u);
 
   __syncthreads();
-  for (int s = tid; s < LocalTable<FULL>::LS; s += TNT) {
+  for (int s = tid; s < LT::LS; s += TNT) {
     const unsigned long long k = lt.key[s];
     if (k == kEmptyKey) continue;
     const unsigned long long h = fmix64(k) & hmask;
@@ -728,12 +826,12 @@ __device__ __forceinline__ void row_gk(SlotArrays<true>& t, int s, unsigned long
 // GK merge of slot s into global slot p: the sums already share its K.
 __device__ __forceinline__ void flush_gk(const SlotArrays<true>& t, int s, unsigned long long* p, bool m34,
                                          bool extrema) {
-  const unsigned long long n_nn = t.cnt[s] & 0xFFFFFFFFull, n_f = n_nn - (t.cnt[s] >> 32);
+  const unsigned long long n_nn = t.cnt[s] & 0xFFFFFFFFull, n_inf = t.cnt[s] >> 32, n_f = n_nn - n_inf;
   if (n_nn) atomicAdd(p + FL_NN, n_nn);
+  if (n_inf) atomicAdd(p + FL_NI, n_inf);
   if (n_f) {
     atomicAdd(reinterpret_cast<double*>(p + FL_S1), t.s1[s]);
     atomicAdd(reinterpret_cast<double*>(p + FL_S2), t.s2[s]);
-    atomicAdd(p + FL_NF, n_f);
     if (m34) {
       atomicAdd(reinterpret_cast<double*>(p + FL_S3), t.s3[s]);
       atomicAdd(reinterpret_cast<double*>(p + FL_S4), t.s4[s]);
@@ -879,7 +977,7 @@ __global__ void table_init_kernel(unsigned long long* T, unsigned long long nslo
     for (unsigned long long s = i0; s < nslots; s += stride) {
       ulonglong2* p = reinterpret_cast<ulonglong2*>(T + s * FL_WORDS);
       p[0] = make_ulonglong2(kEmptyKey, K_UNSET);  // KEY, K
-      p[1] = make_ulonglong2(0ull, 0ull);          // NN, NF
+      p[1] = make_ulonglong2(0ull, 0ull);          // NN, NI
       p[2] = make_ulonglong2(0ull, 0ull);          // S1, S2 (+0.0)
       p[3] = make_ulonglong2(mn0, mx0);            // MN, MX
       p[4] = make_ulonglong2(kNoId, ~0ull);        // ID, ZF
@@ -899,7 +997,7 @@ __global__ void table_init_kernel(unsigned long long* T, unsigned long long nslo
 __device__ __forceinline__ GState slot_state(const unsigned long long* p) {
   GState s = gstate_empty();
   s.nn = static_cast<double>(p[FL_NN]);
-  const unsigned long long nf = p[FL_NF];
+  const unsigned long long nf = p[FL_NN] - p[FL_NI];
   if (nf > 0) {
     s.nf = static_cast<double>(nf);
     s.K = bitsd(p[FL_K]);
@@ -1061,7 +1159,7 @@ template <bool F32, bool FULL>
 cudaError_t launch_queue(const TablePlan& P, const TableArgs& a, cudaStream_t s) {
   const bool m34 = FULL && a.m34;
   auto k = m34 ? table_queue_kernel<F32, FULL, true> : table_queue_kernel<F32, FULL, false>;
-  const size_t smem = queue_table_bytes<FULL>(m34) + 16 + kQueueRingBytes;
+  const size_t smem = (m34 ? queue_table_bytes<FULL, true>() : queue_table_bytes<FULL, false>()) + 16 + kQueueRingBytes;
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e != cudaSuccess) return e;
   k<<<P.grid, TNT, smem, s>>>(a);

@@ -18,7 +18,9 @@ namespace tbgb {
 //   ID   output row of the group (hash mode)     ZF  first zero row code (row << 1 | sign)
 //   S3/S4 sum((v - K)^3), sum((v - K)^4) over finite rows, when m3 / m4 are requested
 // SUMCOUNT slot, 32 bytes (one sector): KEY, NN, SUM (finite values), ID.
-enum { FL_KEY = 0, FL_K, FL_NN, FL_NF, FL_S1, FL_S2, FL_MN, FL_MX, FL_ID, FL_ZF, FL_S3, FL_S4, FL_WORDS };
+// FULL slot words.  FL_NN: non-NaN rows; FL_NI: the +-inf ones among them (finite rows =
+// FL_NN - FL_NI: a finite row, the common case, costs one counter update, not two).
+enum { FL_KEY = 0, FL_K, FL_NN, FL_NI, FL_S1, FL_S2, FL_MN, FL_MX, FL_ID, FL_ZF, FL_S3, FL_S4, FL_WORDS };
 enum { SC_KEY = 0, SC_NN, SC_SUM, SC_ID, SC_WORDS };
 
 constexpr unsigned long long kEmptyKey = 0x8000000000000000ull;  // INT64_MIN marks a free slot
