@@ -97,7 +97,7 @@ def parse():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-check", action="store_true", help="skip the parity check after the timed region")
     ap.add_argument("--ids", type=int, default=None, help="override the distinct-id count of a hash workload")
-    ap.add_argument("--table-mode", default="auto", choices=["auto", "local", "direct", "bucket", "range"],
+    ap.add_argument("--table-mode", default="auto", choices=["auto", "local", "direct", "bucket", "range", "sweep"],
                     help="global-table kernel: shared-memory pre-aggregation or direct atomics")
     ap.add_argument("--exchange", default="pull", choices=["pull", "nccl"],
                     help="multi-GPU high-cardinality exchange: owners read the senders' routed rows in place over "
@@ -535,7 +535,14 @@ def dense_kernel_name(G: int, mode: str) -> str:
     """Main kernel of a plain dense groupby (count/sum/min/max/mean/var) under a table mode."""
     if G <= 512 or (mode != "auto" and G <= 1024):
         return "dense_moments_kernel"
-    if mode in ("auto", "range") and -(-G // (225 * 1024 // 56)) <= 8:
+    if mode == "auto" and (227 * 1024 // G - 60) // 8 >= 4:  # rank and sweep: one range, four columns
+        return "sweep_table_kernel"
+    if mode == "sweep":  # up to 8 ranges with two value columns a group
+        for r in range(1, 9):
+            gr = -(-G // r)
+            if (227 * 1024 // gr - 60) // 8 >= 2:
+                return "sweep_table_kernel"
+    if mode in ("auto", "range", "sweep") and -(-G // (225 * 1024 // 56)) <= 8:
         return "range_table_kernel"
     return "table_kernel"
 

@@ -425,8 +425,14 @@ tbgb_status tbgb_radix_fallback(tbgb_ctx* ctx, uint32_t* bits);
  * rows (falls back to mode 2 beyond 8 ranges; int64 keys as mode 0); 5 = int64 keys with
  * count / sum / mean outputs only and max_groups <= 2^28: radix partitioning (two streaming
  * passes by hash bits, then a shared-memory table per bucket; mode 0 chooses it for at least
- * 2^24 rows and 2^22 <= max_groups <= 2^28), other calls as mode 0.  Modes 1, 2 and 4 never
- * bucket. */
+ * 2^24 rows and 2^22 <= max_groups <= 2^28), other calls as mode 0; 6 = dense keys with the
+ * full moments: rank and sweep (the groups split into as few ranges as keep at least two
+ * value columns per group in one CTA's shared memory, up to 8 ranges, about 29,000 groups; each
+ * tile's rows ranked into per-group columns with one shared u32 atomic, then one thread per
+ * group folds its columns into the group's shared-memory state without atomics; one column
+ * without expression and 16-byte aligned keys, else as mode 4), int64 keys as mode 0.  Mode 0
+ * takes mode 6 for dense keys with the full moments where one range holds every group with at
+ * least four columns (up to about 2,500 groups).  Modes 1, 2, 4 and 6 never bucket. */
 tbgb_status tbgb_set_table_mode(tbgb_ctx* ctx, int mode);
 
 /* Waits for `stream` and returns the first deferred device error of the calls

@@ -59,7 +59,7 @@ def test_column_kernel_default_skips_higher_moments(ctx):
         assert np.array_equal(a[f], b[f])
 
 
-@pytest.mark.parametrize("mode", ["local", "direct", "range"])
+@pytest.mark.parametrize("mode", ["local", "direct", "range", "sweep"])
 def test_table_dense(ctx, mode):
     n, G = 1_000_000, 5000
     keys = oracle.gen_keys_uniform(n, G, 5)

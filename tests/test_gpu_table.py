@@ -9,7 +9,7 @@ from parity import SUM_TOL, abs_sums, bits, check, to_host
 pytestmark = pytest.mark.gpu
 
 SALT = 0x5EED5EED12345678
-MODES = ("local", "direct", "bucket", "range")
+MODES = ("local", "direct", "bucket", "range", "sweep")
 
 
 def dev(x):

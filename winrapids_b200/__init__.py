@@ -122,9 +122,9 @@ class Context:
     def set_table_mode(self, mode: str | int):
         """'auto' (0), 'local' (1: per-CTA shared-memory pre-aggregation), 'direct' (2),
         'bucket' (3: partition first), 'range' (4: dense keys, group ranges held whole in
-        shared memory) or 'radix' (5: int64 keys, count / sum / mean by radix partitioning);
-        see tbgb_set_table_mode."""
-        m = {"auto": 0, "local": 1, "direct": 2, "bucket": 3, "range": 4, "radix": 5}.get(mode, mode)
+        shared memory), 'radix' (5: int64 keys, count / sum / mean by radix partitioning) or
+        'sweep' (6: dense keys, full moments, rank and sweep); see tbgb_set_table_mode."""
+        m = {"auto": 0, "local": 1, "direct": 2, "bucket": 3, "range": 4, "radix": 5, "sweep": 6}.get(mode, mode)
         self._check(self._L.tbgb_set_table_mode(self._h, int(m)))
 
     @staticmethod

@@ -283,7 +283,8 @@ tbgb_status table_common(tbgb_ctx* ctx, bool hash, const void* keys, const tbgb_
   DeviceGuard dg(ctx->device);
   if (!dg.ok) return fail(ctx, TBGB_ERR_BACKEND, "cudaSetDevice failed");
   if (hash && !full && groups <= tbgb::kRadixMaxGroups &&
-      (ctx->table_mode == 5 || (ctx->table_mode == 0 && tbgb::radix_eligible(*cols, out, n, groups))))
+      (ctx->table_mode == 5 ||
+       ((ctx->table_mode == 0 || ctx->table_mode == 6) && tbgb::radix_eligible(*cols, out, n, groups))))
     return radix_hash(ctx, static_cast<const int64_t*>(keys), cols, mask, n, groups, out_keys, out, d_n_groups,
                       stream);
   const int B = hash ? hash_buckets(ctx, full, groups) : 1;
@@ -541,7 +542,7 @@ size_t tbgb_workspace_bytes(const tbgb_ctx* ctx, int64_t n, int32_t n_groups) {
 
 tbgb_status tbgb_set_table_mode(tbgb_ctx* ctx, int mode) {
   if (!ctx) return TBGB_ERR_INVALID_ARGUMENT;
-  if (mode < 0 || mode > 5) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "table mode must be 0 to 5");
+  if (mode < 0 || mode > 6) return fail(ctx, TBGB_ERR_INVALID_ARGUMENT, "table mode must be 0 to 6");
   ctx->table_mode = mode;
   return TBGB_OK;
 }

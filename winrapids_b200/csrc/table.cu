@@ -1155,6 +1155,248 @@ __global__ void __launch_bounds__(FIN_NT) table_compact_kernel(const unsigned lo
   }
 }
 
+// ---- dense keys beyond the column kernel: rank and sweep with the state in shared memory ----
+// For G > 512 dense groups (count / sum / mean / m2 / variances / extrema, optionally m3 / m4) of
+// one column with an optional predicate.  The groups are split into R ranges of Gr groups whose
+// state (packed counts, shift K, power sums, ordered min / max, first-zero code) lives in shared
+// memory, structure of arrays; CTA b owns range b % R and walks 8192-row tiles b / R,
+// b / R + P, ... (the R CTAs reading a tile run side by side: the keys cross HBM once).  Per tile:
+//   rank   every row of the range takes its rank inside its group with one shared u32 atomic
+//          and stores its value into column `rank` of a [C][Gr] buffer; rows ranked >= C, zeros
+//          (the first-zero code needs the row) and +-inf rows update the state directly with
+//          shared atomics (no owner runs meanwhile);
+//   sweep  thread t owns groups t, t + 1024, ...: it folds the group's column entries into the
+//          group's state with plain loads and stores, no atomics, and clears the rank counter.
+// Two CTA barriers a tile.  The next tile's keys are loaded at the start of the rank phase and
+// its values at its end, so both are in flight across the barriers and the sweep.  At the end
+// the CTA merges its state into the global table (SlotArrays::flush).
+constexpr int SW_TILE = 8192;             // rows per tile
+constexpr int SW_RPT = SW_TILE / TNT;     // rows per thread per tile (two 16-byte key loads)
+constexpr int SW_MAXC = 32;               // column depth cap
+constexpr int SW_AHEAD = 3;               // tiles ahead of the current one prefetched into L2
+constexpr size_t kSweepSmemBytes = 227 * 1024;
+
+__host__ __device__ constexpr int sweep_state_bytes(bool m34) { return m34 ? 72 : 56; }
+
+struct SweepPlan {
+  int R;      // ranges
+  int Gr;     // groups per range
+  int C;      // column depth
+  size_t smem;
+};
+
+// R ranges with at least two columns each (0 ranges: the shapes this kernel does not take).
+// max_ranges 1 (the automatic choice): every CTA of a range reads all the keys of its tiles, so
+// beyond one range the group-range table kernel, which reads fewer of them per row, measured
+// faster (3,000 groups: 1.76 against 1.62 ms; 10,000: 4.04 against 2.75 ms), while one range with
+// at least four columns beat it (1,000 groups: 1.08 against 2.03 ms; 2,000: 1.28 against 1.63).
+SweepPlan sweep_plan(long long G, bool m34, int num_sms, int max_ranges, int min_cols) {
+  SweepPlan S{};
+  for (int R = 1; R <= max_ranges && R <= num_sms; ++R) {
+    const long long Gr = (G + R - 1) / R;
+    const long long per = static_cast<long long>(kSweepSmemBytes) / Gr - sweep_state_bytes(m34) - 4;
+    const long long C = per / 8;
+    if (C >= min_cols) {
+      S.R = static_cast<int>((G + Gr - 1) / Gr);
+      S.Gr = static_cast<int>(Gr);
+      S.C = static_cast<int>(C < SW_MAXC ? C : SW_MAXC);
+      S.smem = static_cast<size_t>(Gr) * (sweep_state_bytes(m34) + 4 + 8 * S.C) + 64;
+      return S;
+    }
+  }
+  return S;
+}
+
+template <bool F32, bool M34>
+__global__ void __launch_bounds__(TNT, 1) sweep_table_kernel(TableArgs a, int R, int Gr, int C, int every) {
+  extern __shared__ __align__(16) unsigned char sm[];
+  if (a.gate && *a.gate == 0u) return;
+  constexpr int W = slot_words<true>();
+  const int tid = threadIdx.x;
+  const int range = static_cast<int>(blockIdx.x) % R;
+  const int P = static_cast<int>(gridDim.x) / R;
+  const long long G = static_cast<long long>(a.slots);
+  const long long g0 = static_cast<long long>(range) * Gr;
+  const int Gq = static_cast<int>(G - g0 < Gr ? G - g0 : Gr);  // groups of this range
+  // shared memory: state arrays, rank counters, columns
+  SlotArrays<true> st{};
+  unsigned char* q = sm;
+  st.cnt = reinterpret_cast<unsigned long long*>(q); q += static_cast<size_t>(Gr) * 8;
+  st.K = reinterpret_cast<unsigned long long*>(q); q += static_cast<size_t>(Gr) * 8;
+  st.s1 = reinterpret_cast<double*>(q); q += static_cast<size_t>(Gr) * 8;
+  st.s2 = reinterpret_cast<double*>(q); q += static_cast<size_t>(Gr) * 8;
+  st.mn = reinterpret_cast<unsigned long long*>(q); q += static_cast<size_t>(Gr) * 8;
+  st.mx = reinterpret_cast<unsigned long long*>(q); q += static_cast<size_t>(Gr) * 8;
+  st.zf = reinterpret_cast<unsigned long long*>(q); q += static_cast<size_t>(Gr) * 8;
+  st.s3 = st.s4 = nullptr;
+  if constexpr (M34) {
+    st.s3 = reinterpret_cast<double*>(q); q += static_cast<size_t>(Gr) * 8;
+    st.s4 = reinterpret_cast<double*>(q); q += static_cast<size_t>(Gr) * 8;
+  }
+  double* col = reinterpret_cast<double*>(q); q += static_cast<size_t>(C) * Gr * 8;
+  unsigned int* rk = reinterpret_cast<unsigned int*>(q);
+  for (int j = tid; j < Gr; j += TNT) {
+    st.clear(j);
+    rk[j] = 0u;
+  }
+  __syncthreads();
+
+  const long long n = a.n;
+  const int* keys = static_cast<const int*>(a.keys);
+  const uint64_t* mask = a.mask;
+  const int pred = a.cols.pred;
+  const double thr = a.cols.threshold;
+  const long long ntiles = (n + SW_TILE - 1) / SW_TILE;
+  const int ig0 = static_cast<int>(g0);
+  const unsigned uGq = static_cast<unsigned>(Gq), uG = static_cast<unsigned>(G);
+  // this thread's e-th row of a tile: two 4-row chunks 4096 rows apart (tile-relative, 32-bit)
+  auto lrow = [&](int e) { return (e >> 2) * (TNT * 4) + 4 * tid + (e & 3); };
+  auto tile_rows = [&](long long t) {
+    return t < ntiles ? static_cast<int>(n - t * SW_TILE < SW_TILE ? n - t * SW_TILE : SW_TILE) : 0;
+  };
+  auto selected = [&](long long row) { return !mask || ((__ldg(mask + (row >> 6)) >> (row & 63)) & 1ull); };
+  int ck[SW_RPT], nk[SW_RPT];
+  double cv[SW_RPT], nv[SW_RPT];
+  auto load_keys = [&](long long t, int* kk) {
+    const int rows = tile_rows(t);
+    const int* kt = keys + t * SW_TILE;
+#pragma unroll
+    for (int h = 0; h < SW_RPT / 4; ++h) {
+      const int l0 = lrow(4 * h);
+      if (l0 + 3 < rows) {
+        const int4 k4 = __ldcs(reinterpret_cast<const int4*>(kt + l0));
+        kk[4 * h] = k4.x; kk[4 * h + 1] = k4.y; kk[4 * h + 2] = k4.z; kk[4 * h + 3] = k4.w;
+      } else {
+#pragma unroll
+        for (int e = 0; e < 4; ++e) kk[4 * h + e] = l0 + e < rows ? __ldcs(kt + l0 + e) : ig0 - 1;
+      }
+    }
+  };
+  // values of this range's rows (rows past the end carry key g0 - 1: outside every range's test)
+  auto load_vals = [&](long long t, const int* kk, double* vv) {
+#pragma unroll
+    for (int e = 0; e < SW_RPT; ++e) {
+      vv[e] = 0.0;
+      if (static_cast<unsigned>(kk[e] - ig0) < uGq) {
+        const long long row = t * SW_TILE + lrow(e);
+        if (selected(row)) vv[e] = load_val<F32>(a.cols.a, row);
+      }
+    }
+  };
+  // bulk L2 prefetch of a later tile's keys and values (one thread; sizes rounded down to 16 bytes)
+  const int vsz = F32 ? 4 : 8;
+  const bool valign = (reinterpret_cast<uintptr_t>(a.cols.a) & 15u) == 0;
+  auto prefetch = [&](long long t2) {
+    if (tid == 0 && t2 < ntiles) {
+      const long long r0 = t2 * SW_TILE;
+      const long long rows = tile_rows(t2);
+      const uint32_t kbytes = static_cast<uint32_t>((rows * 4) & ~15ll);
+      if (kbytes) bulk_prefetch_l2(keys + r0, kbytes);
+      const uint32_t vbytes = static_cast<uint32_t>((rows * vsz) & ~15ll);
+      if (valign && vbytes) bulk_prefetch_l2(static_cast<const char*>(a.cols.a) + r0 * vsz, vbytes);
+    }
+  };
+  long long tile = blockIdx.x / R;
+  prefetch(tile + P);
+  load_keys(tile, ck);
+  load_vals(tile, ck, cv);
+  int since = 0;  // tiles ranked since the last sweep
+  for (; tile < ntiles; tile += P) {
+    prefetch(tile + SW_AHEAD * P);
+    load_keys(tile + P, nk);
+    // ---- rank
+#pragma unroll
+    for (int e = 0; e < SW_RPT; ++e) {
+      const unsigned j = static_cast<unsigned>(ck[e] - ig0);
+      if (j >= uGq) {
+        // a key outside [0, G) (range 0 checks): an error when the row is selected
+        if (range == 0 && static_cast<unsigned>(ck[e]) >= uG && lrow(e) < tile_rows(tile)) {
+          const long long row = tile * SW_TILE + lrow(e);
+          if (selected(row) && eval_pred(pred, load_val<F32>(a.cols.a, row), thr)) atomicOr(a.err, KERR_KEY_RANGE);
+        }
+        continue;
+      }
+      const double v = cv[e];
+      if (!eval_pred(pred, v, thr) || is_nan(v)) continue;
+      if (mask && !selected(tile * SW_TILE + lrow(e))) continue;
+      if (is_finite(v) && v != 0.0) {
+        const unsigned r = atomicAdd(rk + j, 1u);
+        if (r < static_cast<unsigned>(C)) {
+          col[r * static_cast<unsigned>(Gr) + j] = v;
+          continue;
+        }
+      }
+      // overflow, zero or +-inf: straight into the state
+      st.row(static_cast<int>(j), v, a.row_offset + tile * SW_TILE + lrow(e), M34, true);
+    }
+    load_vals(tile + P, nk, nv);
+#pragma unroll
+    for (int e = 0; e < SW_RPT; ++e) {
+      ck[e] = nk[e];
+      cv[e] = nv[e];
+    }
+    if (++since < every && tile + P < ntiles) continue;  // columns still have room: rank another tile first
+    since = 0;
+    __syncthreads();
+    // ---- sweep
+    for (int j = tid; j < Gq; j += TNT) {
+      const unsigned cnt = rk[j];
+      if (cnt == 0u) continue;
+      rk[j] = 0u;
+      const int m = cnt < static_cast<unsigned>(C) ? static_cast<int>(cnt) : C;
+      unsigned long long kb = st.K[j];
+      double s1 = st.s1[j], s2 = st.s2[j], s3 = 0.0, s4 = 0.0;
+      if constexpr (M34) {
+        s3 = st.s3[j];
+        s4 = st.s4[j];
+      }
+      double mn = o2f(st.mn[j]), mx = o2f(st.mx[j]);
+      if (kb == K_UNSET) kb = dbits(col[j]);
+      const double K = bitsd(kb);
+      for (int r = 0; r < m; ++r) {
+        const double v = col[static_cast<size_t>(r) * Gr + j];
+        const double d = v - K, dd = d * d;
+        s1 += d;
+        s2 += dd;
+        if constexpr (M34) {
+          s3 += dd * d;
+          s4 += dd * dd;
+        }
+        mn = v < mn ? v : mn;  // finite, non-zero values: the numeric order is the ordered-bits order
+        mx = v > mx ? v : mx;
+      }
+      st.K[j] = kb;
+      st.s1[j] = s1;
+      st.s2[j] = s2;
+      if constexpr (M34) {
+        st.s3[j] = s3;
+        st.s4[j] = s4;
+      }
+      st.mn[j] = f2o(mn);
+      st.mx[j] = f2o(mx);
+      st.cnt[j] += static_cast<unsigned long long>(m);  // non-NaN rows, low word
+    }
+    __syncthreads();
+  }
+  // merge into the global table
+  unsigned long long* T = a.table;
+  for (int j = tid; j < Gq; j += TNT) st.flush(j, T + static_cast<unsigned long long>(g0 + j) * W, M34, true);
+}
+
+template <bool F32>
+cudaError_t launch_sweep(const TablePlan& P, const TableArgs& a, cudaStream_t s) {
+  auto k = a.m34 ? sweep_table_kernel<F32, true> : sweep_table_kernel<F32, false>;
+  cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(P.smem));
+  if (e != cudaSuccess) return e;
+  // tiles ranked between sweeps: the columns about half full on average for uniform keys
+  // (rows ranked past the columns take the shared atomics instead)
+  const long long G = static_cast<long long>(a.slots);
+  long long every = static_cast<long long>(P.sweep_cols) * G / (2ll * SW_TILE);
+  every = every < 1 ? 1 : (every > 8 ? 8 : every);
+  k<<<P.grid, TNT, P.smem, s>>>(a, P.ranges, P.range_groups, P.sweep_cols, static_cast<int>(every));
+  return cudaGetLastError();
+}
+
 template <bool F32, bool FULL>
 cudaError_t launch_queue(const TablePlan& P, const TableArgs& a, cudaStream_t s) {
   const bool m34 = FULL && a.m34;
@@ -1237,8 +1479,22 @@ TablePlan table_plan(bool hash, bool full, int mode, long long groups, int num_s
       static_cast<unsigned long long>(P.buckets) * (P.slots + (hash ? 1 : 0)) * table_slot_words(full) + 1;
   P.table_bytes = (words * 8 + 255) / 256 * 256;
   P.grid = num_sms;
+  P.num_sms = num_sms;
   P.block = TNT;
   P.smem = P.local ? (full ? LocalTable<true>::bytes() : LocalTable<false>::bytes()) : 0;
+  // dense keys, full moments: rank and sweep (mode 6, and the default where it fits)
+  if (!hash && full && (mode == 0 || mode == 6)) {
+    const SweepPlan S = mode == 6 ? sweep_plan(groups, m34, num_sms, kMaxRanges, 2) : sweep_plan(groups, m34, num_sms, 1, 4);
+    if (S.R > 0) {
+      P.local = false;
+      P.ranges = S.R;
+      P.range_groups = S.Gr;
+      P.sweep_cols = S.C;
+      P.grid = num_sms / S.R * S.R;
+      P.smem = S.smem;
+      return P;
+    }
+  }
   // dense keys: group ranges in shared memory (mode 4, and the default while R stays small)
   if (!hash && (mode == 0 || mode == 4)) {
     long long per = full ? range_slot_bytes<true>(m34) : range_slot_bytes<false>(m34);
@@ -1294,6 +1550,21 @@ cudaError_t table_accumulate(const TablePlan& P, const TableArgs& a, cudaStream_
   const bool f32 = a.cols.dtype == TBGB_F32;
   if (ev0) cudaEventRecord(ev0, s);
   cudaError_t e;
+  if (P.sweep_cols > 0) {
+    // rank and sweep: one column without expression, 16-byte aligned keys, packed 32-bit counts
+    // per CTA that cannot wrap; other calls take the group-range kernel planned for them
+    const bool ok = !a.dev_count && a.cols.expr == TBGB_EXPR_A && (reinterpret_cast<uintptr_t>(a.keys) & 15u) == 0 &&
+                    a.n / (P.grid / P.ranges) + SW_TILE < (1ll << 32);
+    if (ok) {
+      e = f32 ? launch_sweep<true>(P, a, s) : launch_sweep<false>(P, a, s);
+      if (e != cudaSuccess) return e;
+      if (ev1) cudaEventRecord(ev1, s);
+      (*launches)++;
+      return cudaSuccess;
+    }
+    const TablePlan Q = table_plan(false, true, 4, static_cast<long long>(a.slots), P.num_sms, 1, a.m34 != 0);
+    return table_accumulate(Q, a, s, launches, nullptr, ev1);
+  }
   // group ranges: a CTA's packed 32-bit row counts must not wrap
   const bool range = P.ranges > 0 && !a.dev_count &&
                      a.n / (P.grid / P.ranges) + RTILE < (1ll << 32);

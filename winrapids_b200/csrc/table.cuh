@@ -52,6 +52,8 @@ struct TablePlan {
   int ranges;      // dense keys: group ranges held whole in shared memory (range_table_kernel), 0 = none
   int range_groups;  // groups per range
   bool range_gk;   // FULL group ranges: shift and first-zero code in the global slot (fewer ranges)
+  int sweep_cols;  // dense FULL keys by rank and sweep (sweep_table_kernel): column depth, 0 = not used
+  int num_sms;
   int buckets;     // hash: sub-tables (rows bucketed by their key's high hash bits first), 1 = one table
   unsigned long long slots;       // dense: n_groups; hash: slots of each sub-table (a power of two)
   size_t table_bytes;  // including the sentinel slot and the counter word
