@@ -175,7 +175,44 @@ def test_dense_range_ragged_unaligned(ctx, G, f32):
         ctx.set_table_mode("auto")
 
 
-def test_dense_range_key_out_of_range_only_when_selected(ctx):
+@pytest.mark.parametrize("G", [1500, 9000])
+@pytest.mark.parametrize("f32", [False, True])
+def test_dense_sweep_ragged_masked(ctx, G, f32):
+    """Rank and sweep (mode 6): a row count that is not a multiple of four, a row mask, a predicate,
+    NaN / +-inf / +-0 values, keys 16-byte aligned (offsets 0 and 4) and not (offset 1: the call
+    takes the group-range kernel instead); one range at 1,500 groups, three at 9,000."""
+    import torch
+
+    n, seed = 1_000_003, 53
+    keys = oracle.gen_keys_uniform(n + 4, G, seed)
+    a = oracle.gen_values_normal(n + 4, 0.0, 1.0, seed + 1)
+    a[::777] = np.nan
+    a[3::1201] = np.inf
+    a[5::1301] = -np.inf
+    a[7::901] = 0.0
+    a[9::1103] = -0.0
+    if f32:
+        a = a.astype(np.float32)
+    user = host_mask(n)
+    user[::5] = np.uint64(0x0F0F0F0F0F0F0F0F)
+    dk = torch.as_tensor(keys).cuda()
+    da = torch.as_tensor(a).cuda()
+    ctx.set_table_mode("sweep")
+    try:
+        for off in (0, 1, 4):
+            got = to_host(ctx.groupby_dense_columns(dk[off:off + n], da[off:off + n], G, pred=">=", threshold=-1.0,
+                                                    mask=dev_mask(user)))
+            ha = a[off:off + n].astype(np.float64)
+            m = host_mask(n, ha, ">=", -1.0, user)
+            k = keys[off:off + n]
+            want = oracle.moments_grouped_mt(ha, k, G, threads=8, mask=m)
+            check(got, want, abs_sums(k, ha, G, rows_of(m, n)), f"sweep G={G} f32={f32} off={off}")
+    finally:
+        ctx.set_table_mode("auto")
+
+
+@pytest.mark.parametrize("mode", ["range", "sweep"])
+def test_dense_range_key_out_of_range_only_when_selected(ctx, mode):
     """Keys outside [0, G) raise only on rows that the mask and the predicate select."""
     import winrapids_b200 as wb
 
@@ -187,7 +224,7 @@ def test_dense_range_key_out_of_range_only_when_selected(ctx):
     user = host_mask(n)
     for r in (100, n - 1):
         user[r // 64] &= ~np.uint64(1 << (r % 64))
-    ctx.set_table_mode("range")
+    ctx.set_table_mode(mode)
     try:
         got = to_host(ctx.groupby_dense_columns(dev(keys), dev(vals), G, pred=">", threshold=0.0,
                                                 mask=dev_mask(user)))
@@ -200,7 +237,7 @@ def test_dense_range_key_out_of_range_only_when_selected(ctx):
     m = host_mask(n, vals, ">", 0.0, user)
     k = np.where((keys >= 0) & (keys < G), keys, 0).astype(np.int32)
     want = oracle.moments_grouped_mt(vals, k, G, threads=8, mask=m)
-    check(got, want, abs_sums(k, vals, G, rows_of(m, n)), "range oor masked")
+    check(got, want, abs_sums(k, vals, G, rows_of(m, n)), f"{mode} oor masked")
     for f in ("count", "min", "max"):
         assert np.array_equal(bits(got[f]), bits(again[f])), f
 
