@@ -107,7 +107,7 @@ def test_stress_without_inf_variance_is_tight(ctx):
     assert rel.max() < 1e-9
 
 
-@pytest.mark.parametrize("G", [1, 2, 3, 31, 32, 33, 255, 256, 257, 511, 512, 513, 777, 1023, 1024])
+@pytest.mark.parametrize("G", [1, 2, 3, 31, 32, 33, 127, 128, 129, 255, 256, 257, 511, 512, 513, 777, 1023, 1024])
 def test_group_counts_sweep(ctx, G):
     n = 123_457
     keys = oracle.gen_keys_uniform(n, G, G)
@@ -198,6 +198,34 @@ def test_row_mask(ctx):
     want = oracle.moments_grouped_masked(vals, keys, mask, G)
     sel = np.unpackbits(mask.view(np.uint8), bitorder="little")[:n].astype(bool)
     check(got, want, abs_sums(keys, vals, G, sel), "mask")
+
+
+@pytest.mark.parametrize("masked", [False, True])
+@pytest.mark.parametrize("G", [128, 256, 512])
+def test_compile_time_group_counts(ctx, G, masked):
+    """128, 256 and 512 groups run their own kernel instantiations: zeros of both signs,
+    +-inf, NaN, column overflow from a skewed key and a mask over many tiles all reach them."""
+    n = 4096 * 300 + 77
+    keys = oracle.gen_keys_uniform(n, G, 40 + G)
+    keys[: 4096 * 3: 2] = 7  # one group overflows its column
+    vals = oracle.gen_values_normal(n, 0.0, 1.0, 40 + G)
+    vals[::1009] = np.nan
+    vals[3::7919] = np.inf
+    vals[5::8191] = -np.inf
+    vals[11::5003] = 0.0
+    vals[13::6007] = -0.0
+    if masked:
+        a = oracle.gen_values_normal(n, 0.0, 1.0, 41 + G)
+        a[4096 * 20: 4096 * 60] = -1.0  # whole tiles without a selected row
+        mask = oracle.filter_mask("gt", -0.3, a)
+        got = run_gpu(ctx, keys, vals, G, mask=mask)
+        want = oracle.moments_grouped_masked(vals, keys, mask, G)
+        sel = np.unpackbits(mask.view(np.uint8), bitorder="little")[:n].astype(bool)
+        check(got, want, abs_sums(keys, vals, G, sel), f"G={G} masked")
+    else:
+        got = run_gpu(ctx, keys, vals, G)
+        want = oracle.moments_grouped_mt(vals, keys, G, threads=8)
+        check(got, want, abs_sums(keys, vals, G), f"G={G}")
 
 
 def test_unaligned_inputs_take_the_plain_load_path(ctx):

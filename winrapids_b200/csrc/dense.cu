@@ -160,18 +160,21 @@ size_t dense_smem_bytes(int G, int C) {
          2 * gp * 4 + 2 * SPL * 4 + 16 + (2 * STAGES + 4) * 8 + 16;
 }
 
+// Column capacity (rows per group in one column buffer) and owners per group for G groups.
+__host__ __device__ constexpr int dense_cols(int G) {
+  return (kDenseColBudget / 2) / G > TILE ? TILE : ((kDenseColBudget / 2) / G < 1 ? 1 : (kDenseColBudget / 2) / G);
+}
+__host__ __device__ constexpr int dense_opg(int G) { return G >= NOW ? 1 : NOW / G; }
+
 DenseLaunch dense_plan(int G, int num_sms) {
   DenseLaunch L{};
   L.grid = num_sms;
-  int C = (kDenseColBudget / 2) / G;
-  if (C > TILE) C = TILE;
-  if (C < 1) C = 1;
-  L.C = C;
-  L.opg = G >= NOW ? 1 : NOW / G;
+  L.C = dense_cols(G);
+  L.opg = dense_opg(G);
   L.slots = G * L.opg;
   const int ms = (L.slots + NOW - 1) / NOW;
   L.maxslots = ms <= 1 ? 1 : (ms <= 2 ? 2 : 4);
-  L.smem = dense_smem_bytes(G, C);
+  L.smem = dense_smem_bytes(G, L.C);
   L.part_doubles = static_cast<size_t>(ST_COUNT) * L.grid * TEAMS * L.slots;
   L.spill_words = static_cast<size_t>(SP_COUNT) * L.grid * G;
   return L;
@@ -376,11 +379,16 @@ struct OwnerAcc4 {
 template <int NCH, bool M34>
 using OwnerAccT = typename std::conditional<M34, OwnerAcc4<NCH>, OwnerAcc<NCH>>::type;
 
-template <int MAXSLOTS, bool MASKED, bool TMA, bool M34>
+// GC > 0: an instantiation for exactly GC groups.  With the group count (and so the column
+// capacity and the owners per group) known at compile time, the column address rank * G + key
+// and the owners' column strides fold into shifts and immediate offsets: 10^9 rows over 256
+// groups took 2.55 ms against 2.75 ms with the counts read from the arguments.
+template <int MAXSLOTS, bool MASKED, bool TMA, bool M34, int GC = 0>
 __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int tid = threadIdx.x;
-  const int G = a.G, C = a.C;
+  const int G = GC ? GC : a.G, C = GC ? dense_cols(GC) : a.C;
+  const int opg = GC ? dense_opg(GC) : a.opg;
   const int gp = (G + 3) & ~3;
   double* col0 = reinterpret_cast<double*>(smem + STAGES * STAGE_BYTES);
   double* col1 = col0 + static_cast<size_t>(C) * G;
@@ -717,7 +725,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
     // With one owner per group (n_groups >= owner threads) each count has a single
     // reader and the owner warps run independently; otherwise the sub-owners of a
     // group meet at a named barrier before its count is reset.
-    const bool shared_counts = a.opg > 1;
+    const bool shared_counts = opg > 1;
     for (long long k = team; k < nbatch; k += TEAMS) {
       const int bs = static_cast<int>(k & 1);
       const double* col = bs ? col1 : col0;
@@ -748,7 +756,7 @@ __global__ void __launch_bounds__(NT, 1) dense_moments_kernel(DenseArgs a) {
         if (og[q] >= 0 && osub[q] == 0) cnt[og[q]] = 0;
 #pragma unroll
       for (int q = 0; q < MAXSLOTS; ++q)
-        if (og[q] >= 0) acc[q].sweep(col + og[q], c[q], osub[q], a.opg, G);
+        if (og[q] >= 0) acc[q].sweep(col + og[q], c[q], osub[q], opg, G);
       for (int e = 0; e < nspill; ++e) {  // rows that overflowed their column (rare)
         const int key = splk[e];
 #pragma unroll
@@ -929,22 +937,34 @@ __global__ void __launch_bounds__(256) merge_states_kernel(const double* __restr
 // host launchers
 // ---------------------------------------------------------------------------
 
-template <int MAXSLOTS, bool MASKED, bool TMA, bool M34>
+template <int MAXSLOTS, bool MASKED, bool TMA, bool M34, int GC = 0>
 static cudaError_t launch_main(const DenseLaunch& L, const DenseArgs& a, cudaStream_t stream) {
-  auto kern = dense_moments_kernel<MAXSLOTS, MASKED, TMA, M34>;
+  auto kern = dense_moments_kernel<MAXSLOTS, MASKED, TMA, M34, GC>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(L.smem));
   if (e != cudaSuccess) return e;
   kern<<<L.grid, NT, L.smem, stream>>>(a);
   return cudaGetLastError();
 }
 
+// Staged (TMA) launches of the common group counts run an instantiation for that count.
+template <int MAXSLOTS, bool MASKED, bool M34>
+static cudaError_t launch_staged(const DenseLaunch& L, const DenseArgs& a, cudaStream_t stream) {
+  if constexpr (MAXSLOTS == 1) {
+    if (a.G == 256) return launch_main<1, MASKED, true, M34, 256>(L, a, stream);
+    if (a.G == 128) return launch_main<1, MASKED, true, M34, 128>(L, a, stream);
+  } else if constexpr (MAXSLOTS == 2) {
+    if (a.G == 512) return launch_main<2, MASKED, true, M34, 512>(L, a, stream);
+  }
+  return launch_main<MAXSLOTS, MASKED, true, M34>(L, a, stream);
+}
+
 template <int MAXSLOTS, bool M34>
 static cudaError_t launch_slots(const DenseLaunch& L, const DenseArgs& a, bool masked, bool aligned,
                                 cudaStream_t stream) {
   if (masked)
-    return aligned ? launch_main<MAXSLOTS, true, true, M34>(L, a, stream)
+    return aligned ? launch_staged<MAXSLOTS, true, M34>(L, a, stream)
                    : launch_main<MAXSLOTS, true, false, M34>(L, a, stream);
-  return aligned ? launch_main<MAXSLOTS, false, true, M34>(L, a, stream)
+  return aligned ? launch_staged<MAXSLOTS, false, M34>(L, a, stream)
                  : launch_main<MAXSLOTS, false, false, M34>(L, a, stream);
 }
 
