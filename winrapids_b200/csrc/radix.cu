@@ -125,11 +125,37 @@ struct RxScatter {
   const unsigned long long* out_base;  // nullable: first row of each destination bucket
   const unsigned long long* out_cap;   // with out_base: rows of each destination bucket
   uint32_t* fallback;
+  int stage;                   // 1: full, 16-byte aligned tiles arrive by TMA bulk copy (local sources)
 };
 
-template <bool VF32>
-constexpr size_t scatter_smem() {
-  return static_cast<size_t>(RX_TILE) * 16;  // one 16-byte (hash, value) entry a row
+// Plain sources (SRC 0, 2) stage whole tiles into shared memory with a bulk copy issued one tile
+// ahead: the copy of a CTA's next tile runs while the current tile is ranked, reordered and
+// written, so the row loads leave the tile's critical path.
+template <int SRC>
+__host__ __device__ constexpr bool scatter_staged() { return SRC != 1; }
+
+// The reordered tile (hashes and values as two arrays), and for staged sources the tile being
+// copied in (keys or hashes, values).
+template <int SRC, bool VF32>
+__host__ __device__ constexpr size_t scatter_smem() {
+  constexpr size_t vb = VF32 ? 4 : 8;
+  return static_cast<size_t>(RX_TILE) * (8 + vb) * (scatter_staged<SRC>() ? 2 : 1) + 16;
+}
+
+__device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+// Bounded wait on a stage's bulk copy (about 2 s; a copy that never lands sends the call to the
+// fallback instead of hanging the CTA).
+__device__ __forceinline__ bool stage_wait(uint64_t* bar, uint32_t parity, uint32_t* fallback) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (;;) {
+    if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
+    if (globaltimer_ns() - t0 > 2000000000ull) {
+      atomicOr(fallback, 4u);
+      return false;
+    }
+  }
 }
 
 // SRC: 0 = the caller's key and value columns as they are, 1 = the caller's columns with mask /
@@ -138,12 +164,19 @@ constexpr size_t scatter_smem() {
 template <int SRC, bool VF32, bool F32IN, int DBITS>
 __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
   using VT = typename std::conditional<VF32, float, double>::type;
+  using ST = typename std::conditional<SRC == 0, int64_t, unsigned long long>::type;  // staged key / hash
   constexpr int ND = 1 << DBITS;  // destination digits of this pass
+  constexpr bool STAGED = scatter_staged<SRC>();
   static_assert(ND <= RX_NT, "one thread per digit in phase B");
   extern __shared__ __align__(16) unsigned char rx_sm[];
-  // the tile reordered by bucket: one 16-byte entry a row (hash, value), written and read with one
-  // vector access each; the bucket is recomputed from the hash when the runs are written out
-  uint4* sh_row = reinterpret_cast<uint4*>(rx_sm);
+  // the tile reordered by bucket (hashes, values); the bucket is recomputed from the hash when the
+  // runs are written out
+  unsigned long long* sh_h = reinterpret_cast<unsigned long long*>(rx_sm);
+  VT* sh_v = reinterpret_cast<VT*>(rx_sm + RX_TILE * 8);
+  // staged sources: the tile in flight (keys or hashes, values) and its mbarrier
+  ST* st_k = reinterpret_cast<ST*>(rx_sm + RX_TILE * (8 + sizeof(VT)));
+  VT* st_v = reinterpret_cast<VT*>(rx_sm + RX_TILE * (16 + sizeof(VT)));
+  uint64_t* st_bar = reinterpret_cast<uint64_t*>(rx_sm + RX_TILE * (16 + 2 * sizeof(VT)));
   __shared__ unsigned int hist[ND];
   __shared__ unsigned int lstart[ND];
   __shared__ unsigned int wlim[ND];
@@ -159,6 +192,37 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
   const long long ntiles = SRC == 2 ? a.seg_tiles[a.n_seg] : (a.n + RX_TILE - 1) / RX_TILE;
   VT* dst_v = static_cast<VT*>(a.dst_v);
   int seg = 0;
+  // Source addresses of tile t when it is a full, 16-byte aligned tile of a staged source (every
+  // thread decides the same way); `sg` walks the segments forward like the tile loop does.
+  auto stage_src = [&](long long t, int& sg, const ST*& sk, const VT*& sv) -> bool {
+    if (!STAGED || !a.stage || t >= ntiles) return false;
+    if constexpr (SRC == 2) {
+      while (__ldg(a.seg_tiles + sg + 1) <= t) ++sg;
+      const long long r0 = (t - __ldg(a.seg_tiles + sg)) * RX_TILE;
+      if (__ldg(a.seg_count + sg) - r0 < RX_TILE) return false;
+      sk = reinterpret_cast<const ST*>(__ldg(a.seg_h + sg)) + r0;
+      sv = reinterpret_cast<const VT*>(__ldg(a.seg_v + sg)) + r0;
+    } else {
+      const long long r0 = t * RX_TILE;
+      if (a.n - r0 < RX_TILE) return false;
+      sk = reinterpret_cast<const ST*>(a.keys) + r0;
+      sv = static_cast<const VT*>(a.cols.a) + r0;
+    }
+    return aligned16(sk) && aligned16(sv);
+  };
+  uint32_t st_phase = 0;
+  int sg_next = 0;  // segment cursor of the copies issued ahead
+  if (STAGED && tid == 0) {
+    mbar_init(st_bar, 1);
+    mbar_fence_init();
+    const ST* sk = nullptr;
+    const VT* sv = nullptr;
+    if (stage_src(blockIdx.x, sg_next, sk, sv)) {
+      mbar_arrive_expect_tx(st_bar, RX_TILE * (8 + sizeof(VT)));
+      bulk_g2s(st_k, sk, RX_TILE * 8, st_bar);
+      bulk_g2s(st_v, sv, RX_TILE * sizeof(VT), st_bar);
+    }
+  }
   __syncthreads();
   for (long long t = blockIdx.x; t < ntiles; t += gridDim.x) {
     long long row0, rows;
@@ -183,13 +247,32 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
     unsigned long long hv[RX_PER];
     VT vv[RX_PER];
     unsigned int rk[RX_PER];  // bit 31 valid, bits 16-24 digit, bits 0-15 rank
+    bool staged = false;
+    if constexpr (STAGED) {
+      int sg_t = seg;
+      const ST* sk = nullptr;
+      const VT* sv = nullptr;
+      staged = stage_src(t, sg_t, sk, sv);
+      if (staged) {
+        if (!stage_wait(st_bar, st_phase, a.fallback)) staged = false;  // rows then come from global memory
+        st_phase ^= 1u;
+      }
+    }
     if constexpr (SRC == 2) {
+      if (staged) {
 #pragma unroll
-      for (int j = 0; j < RX_PER; ++j) {
-        const int li = j * RX_NT + tid;
-        if (li < rows) {
-          hv[j] = __ldcs(src_h + row0 + li);
-          vv[j] = __ldcs(src_v + row0 + li);
+        for (int j = 0; j < RX_PER; ++j) {
+          hv[j] = st_k[j * RX_NT + tid];
+          vv[j] = st_v[j * RX_NT + tid];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < RX_PER; ++j) {
+          const int li = j * RX_NT + tid;
+          if (li < rows) {
+            hv[j] = __ldcs(src_h + row0 + li);
+            vv[j] = __ldcs(src_v + row0 + li);
+          }
         }
       }
 #pragma unroll
@@ -202,12 +285,20 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
         }
       }
     } else if constexpr (SRC == 0) {
+      if (staged) {
 #pragma unroll
-      for (int j = 0; j < RX_PER; ++j) {
-        const int li = j * RX_NT + tid;
-        if (li < rows) {
-          hv[j] = static_cast<unsigned long long>(__ldcs(a.keys + row0 + li));
-          vv[j] = __ldcs(static_cast<const VT*>(a.cols.a) + row0 + li);
+        for (int j = 0; j < RX_PER; ++j) {
+          hv[j] = static_cast<unsigned long long>(st_k[j * RX_NT + tid]);
+          vv[j] = st_v[j * RX_NT + tid];
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < RX_PER; ++j) {
+          const int li = j * RX_NT + tid;
+          if (li < rows) {
+            hv[j] = static_cast<unsigned long long>(__ldcs(a.keys + row0 + li));
+            vv[j] = __ldcs(static_cast<const VT*>(a.cols.a) + row0 + li);
+          }
         }
       }
 #pragma unroll
@@ -244,6 +335,17 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
       }
     }
     __syncthreads();
+    // every thread has read the stage: copy the CTA's next tile into it
+    if (STAGED && tid == 0) {
+      const ST* sk = nullptr;
+      const VT* sv = nullptr;
+      if (stage_src(t + gridDim.x, sg_next, sk, sv)) {
+        fence_proxy_async_smem();
+        mbar_arrive_expect_tx(st_bar, RX_TILE * (8 + sizeof(VT)));
+        bulk_g2s(st_k, sk, RX_TILE * 8, st_bar);
+        bulk_g2s(st_v, sv, RX_TILE * sizeof(VT), st_bar);
+      }
+    }
 
     // ---- phase B: claim a run per bucket, offsets of the buckets inside the tile
     unsigned int c = 0, inc = 0;
@@ -285,18 +387,8 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
       if (rk[j] >> 31) {
         const unsigned d = (rk[j] >> 16) & DMASK;
         const unsigned p = lstart[d] + (rk[j] & 0xFFFFu);
-        uint4 e;
-        e.x = static_cast<unsigned>(hv[j]);
-        e.y = static_cast<unsigned>(hv[j] >> 32);
-        if constexpr (VF32) {
-          e.z = __float_as_uint(vv[j]);
-          e.w = 0u;
-        } else {
-          const unsigned long long vb = static_cast<unsigned long long>(__double_as_longlong(vv[j]));
-          e.z = static_cast<unsigned>(vb);
-          e.w = static_cast<unsigned>(vb >> 32);
-        }
-        sh_row[p] = e;
+        sh_h[p] = hv[j];
+        sh_v[p] = vv[j];
       }
     }
     __syncthreads();
@@ -304,15 +396,13 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
     // ---- phase D: write each bucket's run (consecutive threads, consecutive addresses)
     const unsigned int tot = tile_total;
     for (unsigned int p = tid; p < tot; p += RX_NT) {
-      const uint4 e = sh_row[p];
-      const unsigned long long h = (static_cast<unsigned long long>(e.y) << 32) | e.x;
+      const unsigned long long h = sh_h[p];
       const unsigned d = SRC == 2 ? static_cast<unsigned>(h >> a.shift) & DMASK : static_cast<unsigned>(h >> (64 - DBITS));
       const unsigned i = p - lstart[d];
       if (i < wlim[d]) {
         const unsigned long long dst = gdst[d] + i;
         a.dst_h[dst] = h;
-        if constexpr (VF32) dst_v[dst] = __uint_as_float(e.z);
-        else dst_v[dst] = __longlong_as_double(static_cast<long long>((static_cast<unsigned long long>(e.w) << 32) | e.z));
+        dst_v[dst] = sh_v[p];
       }
     }
     // the next tile's first barrier orders these reads before lstart / gdst / sh_* change
@@ -562,7 +652,7 @@ unsigned long long bucket_cap(unsigned long long e, unsigned long long margin) {
 template <int SRC, bool VF32, bool F32IN>
 cudaError_t launch_scatter(const RxScatter& s, int grid, cudaStream_t st) {
   auto k = rx_scatter_kernel<SRC, VF32, F32IN, SRC == 2 ? D2_BITS : D1_BITS>;
-  constexpr size_t smem = scatter_smem<VF32>();
+  constexpr size_t smem = scatter_smem<SRC, VF32>();
   cudaError_t e = cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem));
   if (e == cudaSuccess) e = cudaFuncSetAttribute(k, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
   if (e != cudaSuccess) return e;
@@ -601,7 +691,7 @@ int scatter_blocks_per_sm(bool vf32) {
   int& c = cached[vf32 ? 1 : 0];
   if (c == 0) {
     int v = 0;
-    const size_t smem = vf32 ? scatter_smem<true>() : scatter_smem<false>();
+    const size_t smem = vf32 ? scatter_smem<2, true>() : scatter_smem<2, false>();
     cudaError_t e = vf32 ? cudaFuncSetAttribute(rx_scatter_kernel<2, true, true, D2_BITS>,
                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, static_cast<int>(smem))
                          : cudaFuncSetAttribute(rx_scatter_kernel<2, false, false, D2_BITS>,
@@ -668,6 +758,7 @@ cudaError_t radix_groupby(const RadixPlan& P, const RadixArgs& a, void* ws, uint
   p1.cursor = x->cur1;
   p1.cap = P.cap1;
   p1.fallback = &x->fallback;
+  p1.stage = 1;  // local sources: full tiles arrive by bulk copy
   const bool plain = a.mask == nullptr && a.cols.pred == TBGB_PRED_NONE && a.cols.expr == TBGB_EXPR_A;
   const bool f32in = a.cols.dtype == TBGB_F32;
   if (a.n > 0) {
@@ -697,6 +788,7 @@ cudaError_t radix_groupby(const RadixPlan& P, const RadixArgs& a, void* ws, uint
   p2.cursor = x->cur2;
   p2.cap = P.cap2;
   p2.fallback = &x->fallback;
+  p2.stage = 1;  // local sources: full tiles arrive by bulk copy
   if (a.n > 0) {
     e = P.vf32 ? launch_scatter<2, true, true>(p2, P.grid_scatter, s)
                : launch_scatter<2, false, false>(p2, P.grid_scatter, s);
@@ -748,6 +840,7 @@ cudaError_t radix_route(const RadixArgs& a, unsigned long long* out_h, void* out
   p1.out_base = x->route_base;
   p1.out_cap = x->route_cap;
   p1.fallback = &x->fallback;
+  p1.stage = 1;  // local sources: full tiles arrive by bulk copy
   const bool plain = a.mask == nullptr && a.cols.pred == TBGB_PRED_NONE && a.cols.expr == TBGB_EXPR_A;
   const bool f32in = a.cols.dtype == TBGB_F32;
   const bool vf32 = radix_value_f32(a.cols);
@@ -828,6 +921,7 @@ cudaError_t radix_groupby_routed(const RadixPlan& P, const RoutedArgs& r, void* 
   p2.cursor = x->cur2;
   p2.cap = P.cap2;
   p2.fallback = &x->fallback;
+  p2.stage = 0;  // peers' buffers are read with plain loads over NVLink
   if (r.n_rows > 0) {
     e = P.vf32 ? launch_scatter<2, true, true>(p2, P.grid_scatter, s)
                : launch_scatter<2, false, false>(p2, P.grid_scatter, s);
