@@ -85,6 +85,28 @@ def test_f32_values_plain(ctx):
     compare(gk, got, keys, vals.astype(np.float64), np.ones(n, bool), "f32")
 
 
+def test_f32_values_across_the_fixed_point_range(ctx):
+    """f32 sums are exact 64-bit fixed point for magnitudes in [2^-13, 2^E) and f64 atomics
+    outside it: groups that mix tiny, huge, negative, zero, subnormal and non-finite values, with
+    a group's positive and negative values cancelling, take both parts and their sum."""
+    rng = np.random.default_rng(11)
+    n, ids = 4_000_003, 1 << 20
+    keys = oracle.gen_keys_ids(n, ids, SALT, 5)
+    mag = np.float32(2.0) ** rng.integers(-40, 40, n).astype(np.float32)
+    vals = (rng.uniform(1.0, 2.0, n).astype(np.float32) * mag).astype(np.float32)
+    vals[rng.random(n) < 0.5] *= np.float32(-1.0)
+    vals[rng.random(n) < 0.01] = np.float32(0.0)
+    vals[rng.random(n) < 0.01] = np.float32(1e-42)  # subnormal
+    vals[rng.random(n) < 0.01] = np.float32(3e38)
+    vals[rng.random(n) < 0.01] = np.float32(np.nan)
+    vals[rng.random(n) < 0.005] = np.float32(np.inf)
+    edge = np.float32(2.0) ** np.float32(-13)
+    vals[rng.random(n) < 0.01] = edge  # the smallest magnitude on the fixed-point side
+    vals[rng.random(n) < 0.01] = np.nextafter(edge, np.float32(0.0))  # the largest below it
+    gk, got = run(ctx, keys, vals, ids)
+    compare(gk, got, keys, vals.astype(np.float64), np.ones(n, bool), "f32 range")
+
+
 def test_f64_values_plain_with_nonfinite_and_edge_keys(ctx):
     rng = np.random.default_rng(7)
     n = 3_000_000
