@@ -144,14 +144,14 @@ __host__ __device__ constexpr size_t scatter_smem() {
 
 __device__ __forceinline__ bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
-// Bounded wait on a stage's bulk copy (about 2 s; a copy that never lands sends the call to the
+// Bounded wait on a stage's bulk copy (limit_ns; a copy that never lands sends the call to the
 // fallback instead of hanging the CTA).
-__device__ __forceinline__ bool stage_wait(uint64_t* bar, uint32_t parity, uint32_t* fallback) {
+__device__ __forceinline__ bool stage_wait(uint64_t* bar, uint32_t parity, uint32_t* fallback, uint64_t limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = globaltimer_ns();
   for (;;) {
     if (mbar_try_wait_sleep(bar, parity, 20000u)) return true;
-    if (globaltimer_ns() - t0 > 2000000000ull) {
+    if (globaltimer_ns() - t0 > limit_ns) {
       atomicOr(fallback, 4u);
       return false;
     }
@@ -210,8 +210,17 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
     }
     return aligned16(sk) && aligned16(sv);
   };
+  // st_tile: the tile whose copy the stage holds or receives (-1: none); st_off: a copy did not land
+  // in time, so this CTA issues no more (the call already falls back) and loads rows directly
+  __shared__ long long st_tile;
+  __shared__ int st_off;
   uint32_t st_phase = 0;
-  int sg_next = 0;  // segment cursor of the copies issued ahead
+  int sg_next = 0;        // segment cursor of the copies issued ahead (thread 0)
+  int st_pending = -1;    // thread 0: parity of a copy whose wait gave up, still to be waited out
+  if (tid == 0) {
+    st_tile = -1;
+    st_off = 0;
+  }
   if (STAGED && tid == 0) {
     mbar_init(st_bar, 1);
     mbar_fence_init();
@@ -221,6 +230,7 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
       mbar_arrive_expect_tx(st_bar, RX_TILE * (8 + sizeof(VT)));
       bulk_g2s(st_k, sk, RX_TILE * 8, st_bar);
       bulk_g2s(st_v, sv, RX_TILE * sizeof(VT), st_bar);
+      st_tile = blockIdx.x;
     }
   }
   __syncthreads();
@@ -249,12 +259,13 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
     unsigned int rk[RX_PER];  // bit 31 valid, bits 16-24 digit, bits 0-15 rank
     bool staged = false;
     if constexpr (STAGED) {
-      int sg_t = seg;
-      const ST* sk = nullptr;
-      const VT* sv = nullptr;
-      staged = stage_src(t, sg_t, sk, sv);
+      staged = st_tile == t;  // the same in every thread: written by thread 0 between barriers
       if (staged) {
-        if (!stage_wait(st_bar, st_phase, a.fallback)) staged = false;  // rows then come from global memory
+        if (!stage_wait(st_bar, st_phase, a.fallback, 2000000000ull)) {
+          staged = false;  // this thread's rows then come from global memory
+          st_off = 1;
+          if (tid == 0) st_pending = static_cast<int>(st_phase);
+        }
         st_phase ^= 1u;
       }
     }
@@ -337,13 +348,15 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
     __syncthreads();
     // every thread has read the stage: copy the CTA's next tile into it
     if (STAGED && tid == 0) {
+      st_tile = -1;
       const ST* sk = nullptr;
       const VT* sv = nullptr;
-      if (stage_src(t + gridDim.x, sg_next, sk, sv)) {
+      if (!st_off && stage_src(t + gridDim.x, sg_next, sk, sv)) {
         fence_proxy_async_smem();
         mbar_arrive_expect_tx(st_bar, RX_TILE * (8 + sizeof(VT)));
         bulk_g2s(st_k, sk, RX_TILE * 8, st_bar);
         bulk_g2s(st_v, sv, RX_TILE * sizeof(VT), st_bar);
+        st_tile = t + gridDim.x;
       }
     }
 
@@ -407,6 +420,9 @@ __global__ void __launch_bounds__(RX_NT, 2) rx_scatter_kernel(RxScatter a) {
     }
     // the next tile's first barrier orders these reads before lstart / gdst / sh_* change
   }
+  // a copy whose wait gave up may still be in flight into this CTA's shared memory: wait once
+  // more (bounded) before the CTA exits
+  if (STAGED && tid == 0 && st_pending >= 0) stage_wait(st_bar, static_cast<uint32_t>(st_pending), a.fallback, 500000000ull);
 }
 
 // Segments of pass 2 (one per first-pass bucket): addresses, rows written, tiles.
