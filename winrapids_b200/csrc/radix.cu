@@ -9,9 +9,9 @@
 //   pass 2  each of those -> 512 buckets by the next 9 bits            (262,144 buckets)
 //   pass 3  one CTA per bucket: a shared-memory table of 2,048 slots keyed by the low 46 bits of
 //           h (the top 18 are the bucket) takes the bucket's rows, then writes its groups.  A
-//           slot is the key (claimed by a 64-bit compare-and-swap), a u32 count and an f64 sum:
-//           a row costs one probe read, one 32-bit add and one f64 add; 40 KB a table lets four
-//           CTAs share an SM.
+//           slot is the key (claimed by a 64-bit compare-and-swap), a u32 count and the sum: for
+//           f32 values an exact 64-bit fixed-point sum in two u32 words (below), for f64 values
+//           an f64 sum.  An f32 row costs one probe read and three 32-bit adds.
 // fmix64 (MurmurHash3's finaliser) is a bijection, so the rows carry h instead of the key and
 // pass 3 recovers each group's key by inverting it.  A row is (h, value): 12 bytes for an f32
 // column without an expression, 16 otherwise.
